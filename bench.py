@@ -1,0 +1,461 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 INT4 MoE expert-FFN path (one JSON line on rank 0).
+
+Workload: one Qwen3-30B-A3B-shape MoE layer — hidden
+2048, 128 routed experts, top-8, expert intermediate 768, SwiGLU, softmax
+router (bf16 weights N(0, 0.02)), expert weights N(0, 0.02) quantized INT4
+AWQ-symmetric, group 128, bf16-valued scales; hidden states N(0,1) bf16.
+A step is one layer forward over T tokens (default T=64, the largest
+decode-size batch); the line also carries a sweep over T in {1, 8, 64, 512}.
+All data is synthetic, generated on the device from fixed seeds.
+
+L2 (126 MB): the timed loop rotates over R distinct copies of the layer
+(different random weights), sized so the weights the steps touch exceed
+3x L2, so weights stream from HBM every step.
+
+Arms:
+  (default)          this library through its C ABI (libllmoc_b200.so)
+  --impl reference   the reference's own CPU implementation of the path
+                     (oracle/_ref: its src/hal AVX2/OpenMP operators, per-token
+                     moe_ffn_token loop) on the host cores, bounded samples.
+Multi-GPU (torchrun, --gpus N): N independent replicas of the step, one per
+GPU (weak scaling); time = max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "llm-on-cpu_b200"))
+
+CONFIGS = {
+    "qwen3_30b_a3b": dict(H=2048, I=768, E=128, topk=8, gs=128, router=0, scaling=1.0, shared=False),
+    "glm45_air": dict(H=4096, I=1408, E=128, topk=8, gs=128, router=1, scaling=1.0, shared=True),
+    "kimi_k2": dict(H=7168, I=2048, E=384, topk=8, gs=32, router=1, scaling=2.827, shared=True),
+}
+L2_BYTES = 126 * 1024 * 1024
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="llmoc", choices=["llmoc", "reference"])
+    ap.add_argument("--config", default="qwen3_30b_a3b", choices=list(CONFIGS))
+    ap.add_argument("--tokens", type=int, default=64)
+    ap.add_argument("--sweep", default="1,8,64,512", help="extra T values ('' = none)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------- helpers
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(
+        os.environ.get("LOCAL_RANK", 0))
+
+
+def expected_touched(E, k, T):
+    return E * (1.0 - (1.0 - k / E) ** T)
+
+
+def layer_bytes(cfg):
+    """(gate+up bytes, down bytes) one expert streams: packed q + fp16 scales."""
+    H, I, gs = cfg["H"], cfg["I"], cfg["gs"]
+    gu = 2 * (I * H // 2 + I * (H // gs) * 2)
+    dn = H * I // 2 + H * (I // gs) * 2
+    return gu, dn
+
+
+class Clocks:
+    """nvidia-smi samples every 200 ms while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.idx)], stdout=subprocess.PIPE,
+                stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in out.strip().splitlines():
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_peak():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def ncu_traffic(config: str, T: int):
+    """dram bytes per launch of the dominant kernel from a committed ncu summary."""
+    p = os.path.join(REPO, "profiles", "traffic.json")
+    if not os.path.exists(p):
+        return None
+    d = json.load(open(p))
+    return d.get(f"{config}:T{T}")
+
+
+# ------------------------------------------------------- device workload
+
+def build_layers(torch, L, cfg, R, seed, keep_host=False, device=0):
+    """R distinct layers generated and quantized in HBM (llmoc_quantize_awq_sym),
+    then repacked by llmoc_moe_layer_create_device.  keep_host returns the
+    first layer's QLWC tensors on the host for the CPU baseline."""
+    H, I, E, gs = cfg["H"], cfg["I"], cfg["E"], cfg["gs"]
+    n_exp = E + (1 if cfg["shared"] else 0)
+    g = torch.Generator(device="cuda")
+    layers, host = [], None
+    stream = torch.cuda.current_stream()
+    for r in range(R):
+        g.manual_seed(seed + 1000 * r)
+        raw = {}
+        for name, (M, K) in (("gate", (I, H)), ("up", (I, H)), ("down", (H, I))):
+            q = torch.empty((n_exp * M, K // 2), dtype=torch.uint8, device="cuda")
+            s = torch.empty((n_exp * M, K // gs), dtype=torch.int16, device="cuda")
+            per = max(1, int(2 ** 28 // (M * K)))  # experts per generation chunk (<= 1 GiB fp32)
+            for e0 in range(0, n_exp, per):
+                e1 = min(n_exp, e0 + per)
+                W = (torch.randn(((e1 - e0) * M, K), generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+                L.quantize_awq_sym(W, (e1 - e0) * M, K, gs, True, q[e0 * M:e1 * M], s[e0 * M:e1 * M], stream)
+                del W
+            raw[name] = (q, s, M, K)
+        rw = (torch.randn((E, H), generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+        bias = (torch.randn((E,), generator=g, device="cuda") * 0.1).float() if cfg["router"] == 1 else None
+        views = []
+        for e in range(n_exp):
+            for name in ("gate", "up", "down"):
+                q, s, M, K = raw[name]
+                views.append(L.view(q.data_ptr() + e * M * (K // 2), s.data_ptr() + e * M * (K // gs) * 2,
+                                    None, M, K, gs))
+        desc = L.LayerDesc(H, I, E, cfg["topk"], gs, L.SCHEME_AWQ_SYM, 7, cfg["router"], cfg["scaling"],
+                           1 if cfg["shared"] else 0, 1.0)
+        torch.cuda.synchronize()
+        layer = L.MoeLayer.create(desc, rw, bias, views[:3 * E], views[3 * E:] if cfg["shared"] else None,
+                                  device=device, on_device=True)
+        layers.append(layer)
+        if keep_host and r == 0:
+            host = {k: (v[0].cpu().numpy(), v[1].cpu().numpy().view(np.uint16), v[2], v[3]) for k, v in raw.items()}
+            host["router_w"] = rw.view(torch.int16).cpu().numpy().view(np.uint16)
+            host["bias"] = bias.cpu().numpy() if bias is not None else None
+        del raw
+    torch.cuda.synchronize()
+    return layers, host
+
+
+def host_layer(cfg, host):
+    """The kept layer as oracle objects (for the reference CPU path)."""
+    import orc
+
+    H, I, E, gs = cfg["H"], cfg["I"], cfg["E"], cfg["gs"]
+    n_exp = E + (1 if cfg["shared"] else 0)
+    ex = []
+    for e in range(n_exp):
+        ws = []
+        for name in ("gate", "up", "down"):
+            q, s, M, K = host[name]
+            ws.append(orc.Int4Weight(q[e * M:(e + 1) * M], s[e * M:(e + 1) * M], None, M, K, gs,
+                                     orc.SCHEME_AWQ_SYM, 7))
+        ex.append(orc.Expert(*ws))
+    return orc.MoeLayer(H, I, E, cfg["topk"], host["router_w"], ex[:E], cfg["router"], host["bias"],
+                        cfg["scaling"], ex[E] if cfg["shared"] else None, 1.0)
+
+
+def reference_cpu(cfg, layer_obj, T_total, budget_s=4.0, min_tokens=4):
+    """Time the reference's CPU path (oracle/_ref) on a bounded token sample."""
+    import orc
+
+    R = orc.Reference()
+    rng = np.random.default_rng(7)
+    Xs = orc.make_tokens(rng, max(min_tokens, 64), cfg["H"])
+    done, t0 = 0, time.perf_counter()
+    R.moe_layer_forward(layer_obj, Xs[:1])  # warm
+    t0 = time.perf_counter()
+    while True:
+        n = min(len(Xs), max(1, min_tokens))
+        R.moe_layer_forward(layer_obj, Xs[:n])
+        done += n
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": done / dt, "unit": "tokens/s", "cores": R.max_threads(), "kind": "reference",
+            "sample": f"{done} tokens of the {cfg['H']}-hidden layer through the reference's per-token "
+                      f"moe_ffn_token CPU path (src/hal AVX2/OpenMP, {R.max_threads()} OpenMP threads), "
+                      f"{dt:.1f} s"}
+
+
+# ------------------------------------------------------------------- arms
+
+def run_llmoc(args):
+    import torch
+    import llmoc_b200 as L
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    cfg = CONFIGS[args.config]
+    H, E, k = cfg["H"], cfg["E"], cfg["topk"]
+    Ts = sorted({args.tokens} | ({int(x) for x in args.sweep.split(",") if x} if args.sweep else set()))
+    gu_b, dn_b = layer_bytes(cfg)
+    exp_b = gu_b + dn_b
+    touched_min = min(expected_touched(E, k, T) for T in Ts) + (1 if cfg["shared"] else 0)
+    R = int(max(2, min(24, np.ceil(3 * L2_BYTES / (touched_min * exp_b)))))
+    layers, host = build_layers(torch, L, cfg, R, seed=1234 + rank, keep_host=(rank == 0 and not args.no_cpu_baseline))
+    Tmax = max(Ts)
+    ws_bytes = layers[0].workspace_bytes(Tmax)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(99 + rank)
+    Xpool = [(torch.randn((Tmax, H), generator=g, device="cuda")).to(torch.bfloat16) for _ in range(R)]
+    Y = torch.empty((Tmax, H), dtype=torch.bfloat16, device="cuda")
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+
+    def step(i, T):
+        layers[i % R].forward(Xpool[i % R], T, Y, ws, ws_bytes, sp)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if dist is None:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed(T, K, fn):
+        barrier()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for i in range(K):
+            fn(i, T)
+        b.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        return max_over_ranks(a.elapsed_time(b))
+
+    results = {}
+    clocks = Clocks(int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local])
+                    if os.environ.get("CUDA_VISIBLE_DEVICES") else local)
+    for T in Ts:
+        for i in range(args.warmup):
+            step(i, T)
+        torch.cuda.synchronize()
+        if T == args.tokens:
+            clocks.start()
+            n0 = L.launch_count()
+        ms = timed(T, args.steps, step)
+        if T == args.tokens:
+            launches = L.launch_count() - n0
+            clk = clocks.stop()
+        # stage timing pass (separate; events around each stage)
+        for lay in layers:
+            lay.set_stage_timing(True)
+        for i in range(args.steps):
+            step(i, T)
+        torch.cuda.synchronize()
+        stage = {s: 0.0 for s in L.MoeLayer.STAGES}
+        calls = 0
+        touched = []
+        for lay in layers:
+            st, n = lay.stage_times()
+            for s_, v in st.items():
+                stage[s_] += v
+            calls += n
+            lay.set_stage_timing(False)
+        for j in range(R):  # experts touched per layer copy with its own input
+            step(j, T)
+            v = layers[j % R].route_views(T, ws, ws_bytes)
+            torch.cuda.synchronize()
+            off = ws[v.offsets - ws.data_ptr(): v.offsets - ws.data_ptr() + 4 * (layers[0].n_exp + 1)]
+            cnt = np.diff(off.cpu().numpy().view(np.int32))
+            touched.append(int(np.count_nonzero(cnt)))
+        results[T] = dict(ms=ms, stage={s_: v / max(calls, 1) for s_, v in stage.items()},
+                          touched=float(np.mean(touched)))
+
+    # e2e through the public API with host buffers (pinned), copies inside the timed region
+    T = args.tokens
+    Xh = torch.empty((T, H), dtype=torch.bfloat16, pin_memory=True)
+    Xh.copy_(Xpool[0][:T].cpu())
+    Yh = torch.empty((T, H), dtype=torch.bfloat16, pin_memory=True)
+    Xd = torch.empty((T, H), dtype=torch.bfloat16, device="cuda")
+
+    def e2e_step(i, T):
+        Xd.copy_(Xh, non_blocking=True)
+        layers[i % R].forward(Xd, T, Y, ws, ws_bytes, sp)
+        Yh.copy_(Y[:T], non_blocking=True)
+
+    for i in range(args.warmup):
+        e2e_step(i, T)
+    ms_e2e = timed(T, args.steps, e2e_step)
+
+    out = None
+    if rank == 0:
+        world_tokens = world * T * args.steps
+        r = results[T]
+        peak, peak_kind = measured_peak()
+        # dominant kernel: grouped gate/up (+SiLU*mul) — its algorithmic bytes per launch
+        gu_ms = r["stage"]["gate_up"]
+        touched = r["touched"]
+        alg_bytes = touched * gu_b + T * H * 2 + T * (k + (1 if cfg["shared"] else 0)) * cfg["I"] * 2
+        achieved = alg_bytes / (gu_ms * 1e-3) / 1e9 if gu_ms > 0 else None
+        step_bytes = touched * exp_b + E * H * 2 + 2 * T * H * 2
+        sweep = {}
+        for t_, rr in results.items():
+            per_step = rr["ms"] / args.steps
+            b = rr["touched"] * exp_b + E * H * 2 + 2 * t_ * H * 2
+            sweep[str(t_)] = {"tokens_per_s": world * t_ * args.steps / (rr["ms"] * 1e-3),
+                              "ms_per_step": per_step, "touched_experts": rr["touched"],
+                              "layer_GBps": b / (per_step * 1e-3) / 1e9,
+                              "layer_hbm_frac": b / (per_step * 1e-3) / 1e9 / peak,
+                              "stage_ms": {s_: round(v, 5) for s_, v in rr["stage"].items()}}
+        cpu = None
+        if host is not None:
+            try:
+                cpu = reference_cpu(cfg, host_layer(cfg, host), T)
+            except Exception as ex:  # the baseline is reported, not required
+                cpu = {"value": None, "unit": "tokens/s", "cores": None, "kind": "reference",
+                       "sample": f"unavailable: {ex}"}
+        out = {
+            "metric": "INT4 MoE FFN tokens/s (decode, T=%d)" % T,
+            "value": world_tokens / (r["ms"] * 1e-3),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": r["ms"] / args.steps,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "int4 weights x bf16 activations, fp32 accumulate",
+            "data": "synthetic (seeded device RNG; BASELINE shapes and distributions)",
+            "config": {"workload": f"{args.config} MoE layer (BASELINE config 2)" if args.config == "qwen3_30b_a3b"
+                       else f"{args.config} MoE layer", "tokens": T, "hidden": H, "experts": E,
+                       "topk": k, "inter": cfg["I"], "group_size": cfg["gs"],
+                       "parallelism": "replicas" if world > 1 else "single GPU",
+                       "l2": f"rotating {R} distinct layer copies (touched weights >= 3x the 126 MB L2)"},
+            "e2e": {"value": world * T * args.steps / (ms_e2e * 1e-3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 2},
+            "roofline": {"bound": "hbm", "kernel": "k_int4_mma<GATE_UP> (grouped gate/up + SiLU*mul)",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak if achieved else None,
+                         "peak_kind": peak_kind, "traffic": ncu_traffic(args.config, T),
+                         "alg_bytes_per_launch": alg_bytes, "launch_ms": gu_ms},
+            "layer_roofline": {"achieved_GBps": step_bytes / (r["ms"] / args.steps * 1e-3) / 1e9,
+                               "frac": step_bytes / (r["ms"] / args.steps * 1e-3) / 1e9 / peak,
+                               "bytes_per_step": step_bytes},
+            "sweep": sweep,
+            "cpu_baseline": cpu,
+            "clocks": clk,
+            "gpu_launches": int(launches),
+        }
+        print(json.dumps(out), flush=True)
+    for lay in layers:
+        lay.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return out
+
+
+def run_reference(args):
+    """The reference's own CPU implementation of the path on the host cores."""
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return None
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import orc
+
+    if not orc.ref_available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libllmoc_ref.so was not built"}))
+        return None
+    cfg = CONFIGS[args.config]
+    rng = np.random.default_rng(1234)
+    O = orc.Oracle()
+    layer = orc.make_layer(O, rng, H=cfg["H"], I=cfg["I"], E=cfg["E"], topk=cfg["topk"], gs=cfg["gs"],
+                           router=cfg["router"], routed_scaling=cfg["scaling"], shared=cfg["shared"],
+                           n_real=16)
+    R = orc.Reference()
+    T = args.tokens
+    X = orc.make_tokens(rng, T, cfg["H"])
+    per_step = max(1, min(T, 8))  # bounded sample of each step's tokens
+    for i in range(args.warmup):
+        R.moe_layer_forward(layer, X[:per_step])
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        R.moe_layer_forward(layer, X[(i * per_step) % T:][:per_step])
+    dt = time.perf_counter() - t0
+    v = per_step * args.steps / dt
+    line = {"impl": "reference", "metric": "INT4 MoE FFN tokens/s (decode, T=%d)" % T, "value": v,
+            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int4 weights x fp32 activations (AVX2 fp32)",
+            "data": "synthetic", "config": {"workload": f"{args.config} MoE layer", "tokens": T},
+            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": R.max_threads(), "kind": "reference",
+                             "sample": f"{per_step} of the {T} tokens per step through the reference's "
+                                       f"per-token moe_ffn_token CPU path"},
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return line
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_llmoc(args)
+
+
+if __name__ == "__main__":
+    main()

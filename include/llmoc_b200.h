@@ -1,0 +1,238 @@
+/*
+ * llmoc_b200.h — C ABI of the B200 (sm_100a) INT4 weight-only MoE expert-FFN
+ * library that replaces llm-on-cpu's hal::cuda INT4 / MoE entry points.
+ *
+ * Every entry point below names the reference interface it stands in for
+ * (paths inside appolloqin/llm-on-cpu).  The plain structs are layout-
+ * identical to the reference's C++ types, so the reference can pass its own
+ * objects through a reinterpret_cast.
+ *
+ * Conventions
+ *  - llmoc_try_* keep the reference's bool contract: 1 = done, 0 = not done
+ *    (the caller may then run its own CPU path).  The reason for a 0 is in
+ *    llmoc_last_error().  They take host fp32 pointers and are synchronous,
+ *    like the reference (cuda_backend.cpp:2692-2728).
+ *  - llmoc_moe_* (the batched device API) return llmoc_status; pointers are
+ *    device pointers; work is enqueued on the given stream (cudaStream_t
+ *    passed as void*, NULL = the legacy default stream) and is asynchronous.
+ *  - INT4 layout: qweight [M, ceil(K/2)] bytes, low nibble = even k;
+ *    scales/zeros [M, ceil(K/group_size)] fp16 bits, row-major
+ *    (src/weights/qlwc_format.h:34-46).  Scheme 2 (AWQ sym): w = (q - zp) * s;
+ *    scheme 1 (GPTQ asym): w = q * s + z (src/hal/int4_ops.cpp:640-662).
+ */
+#ifndef LLMOC_B200_H
+#define LLMOC_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define LLMOC_API __attribute__((visibility("default")))
+#else
+#define LLMOC_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- types */
+
+typedef enum llmoc_status {
+  LLMOC_OK = 0,
+  LLMOC_ERR_INVALID = 1,     /* bad argument or shape */
+  LLMOC_ERR_NO_DEVICE = 2,   /* no CUDA device / not sm_100 */
+  LLMOC_ERR_CUDA = 3,        /* a CUDA call failed */
+  LLMOC_ERR_NO_MEMORY = 4,   /* allocation failed or VRAM budget exhausted */
+  LLMOC_ERR_NOT_ENABLED = 5, /* llmoc_cuda_enable() not called */
+  LLMOC_ERR_UNSUPPORTED = 6, /* shape or scheme this build does not handle */
+  LLMOC_ERR_WORKSPACE = 7,   /* workspace too small */
+  LLMOC_ERR_TIMEOUT = 8      /* a bounded device-side wait gave up */
+} llmoc_status;
+
+enum { LLMOC_SCHEME_GPTQ_ASYM = 1, LLMOC_SCHEME_AWQ_SYM = 2 };
+enum { LLMOC_ROUTER_SOFTMAX = 0, LLMOC_ROUTER_SIGMOID_BIAS = 1 };
+
+/* Layout-identical to qlwc::Int4View (src/weights/qlwc_store.h:17-27). */
+typedef struct llmoc_int4_view {
+  const uint8_t* qweight;
+  const uint16_t* scales;
+  const uint16_t* zeros;
+  const float* scales_f32; /* ignored */
+  int32_t M, K;
+  int32_t group_size;
+  uint32_t scheme; /* LLMOC_SCHEME_* (qlwc::Scheme) */
+  int32_t awq_zp;  /* <= 0 means 7 */
+} llmoc_int4_view;
+
+/* Layout-identical to hal::cuda::MoeExpertInt4 (src/hal/cuda_backend.h:180-185). */
+typedef struct llmoc_moe_expert_int4 {
+  const llmoc_int4_view* gate;
+  const llmoc_int4_view* up;
+  const llmoc_int4_view* down;
+  float weight;
+} llmoc_moe_expert_int4;
+
+/* ------------------------------------------------------------ lifecycle */
+
+/* hal::cuda::probe_available (src/hal/cuda_backend.h:14; .cpp:733) */
+LLMOC_API int llmoc_cuda_probe_available(void);
+/* hal::cuda::enabled (cuda_backend.h:15) */
+LLMOC_API int llmoc_cuda_enabled(void);
+/* hal::cuda::status (cuda_backend.h:16) — also the last error text */
+LLMOC_API const char* llmoc_cuda_status(void);
+/* hal::cuda::device_count (cuda_backend.h:17) */
+LLMOC_API int llmoc_cuda_device_count(void);
+/* hal::cuda::enable (cuda_backend.h:21; .cpp:917).  Budget caps the resident
+ * INT4 weight cache of the llmoc_try_* entry points (0 = unlimited). */
+LLMOC_API int llmoc_cuda_enable(size_t vram_budget_bytes);
+/* hal::cuda::disable (cuda_backend.h:22; .cpp:947): frees the weight cache. */
+LLMOC_API void llmoc_cuda_disable(void);
+/* hal::cuda::vram_used / vram_budget / set_vram_budget (cuda_backend.h:24-27) */
+LLMOC_API size_t llmoc_cuda_vram_used(void);
+LLMOC_API size_t llmoc_cuda_vram_budget(void);
+LLMOC_API void llmoc_cuda_set_vram_budget(size_t bytes);
+/* hal::cuda::device_mem_info (cuda_backend.h:29) */
+LLMOC_API int llmoc_cuda_device_mem_info(size_t* free_bytes, size_t* total_bytes);
+/* hal::cuda::host_register / host_unregister (cuda_backend.h:32-33) */
+LLMOC_API int llmoc_cuda_host_register(void* ptr, size_t bytes);
+LLMOC_API int llmoc_cuda_host_unregister(void* ptr);
+/* Text of the last failure on the calling thread ("" if none). */
+LLMOC_API const char* llmoc_last_error(void);
+
+/* ------------------------------------------------- INT4 GEMM (host fp32) */
+
+/* hal::cuda::try_gemm_int4 (cuda_backend.h:165; .cpp:2692): y[M] = W . x */
+LLMOC_API int llmoc_try_gemm_int4(const float* x, const llmoc_int4_view* W, float* y);
+/* hal::cuda::try_gemm_int4_batch (cuda_backend.h:166; .cpp:2858): Y[n,M] = X[n,K] . W^T */
+LLMOC_API int llmoc_try_gemm_int4_batch(const float* X, int n, const llmoc_int4_view* W, float* Y);
+/* hal::cuda::try_gemm_int4_multi (cuda_backend.h:172; .cpp:3048): 2..4 weights sharing x */
+LLMOC_API int llmoc_try_gemm_int4_multi(const float* x, const llmoc_int4_view* const* Ws, float* const* ys,
+                              int n);
+/* hal::cuda::try_gemm_int4_batch_multi (cuda_backend.h:170-171) */
+LLMOC_API int llmoc_try_gemm_int4_batch_multi(const float* X, int n, const llmoc_int4_view* const* Ws,
+                                    float* const* Ys, int nW);
+/* hal::cuda::prefetch_int4_weight / pin_int4_weight (cuda_backend.h:173-175; .cpp:5199-5215):
+ * upload (repacked) into the resident cache keyed by W->qweight; pin exempts it from LRU. */
+LLMOC_API int llmoc_prefetch_int4_weight(const llmoc_int4_view* W);
+LLMOC_API int llmoc_pin_int4_weight(const llmoc_int4_view* W);
+/* hal::dequant_int4_matrix (src/hal/int4_ops.h:27; int4_ops.cpp:664-668) run on
+ * the GPU from the resident repacked copy: out[M*K] fp32 host, bit-exact. */
+LLMOC_API int llmoc_try_dequant_int4_matrix(const llmoc_int4_view* W, float* out);
+
+/* ---------------------------------------------------- fused MoE (1 token) */
+
+/* hal::cuda::try_moe_ffn_int4 (src/hal/cuda_backend.h:186-188; .cpp:5217-5317):
+ * y[H] = sum_i experts[i].weight * down_i(silu(gate_i x) * up_i x)
+ *        + shared_scale * shared(x); y is overwritten; n_experts <= 64;
+ * experts with |weight| < 1e-12 are skipped. */
+LLMOC_API int llmoc_try_moe_ffn_int4(const float* x, int H, int I, const llmoc_moe_expert_int4* experts,
+                           int n_experts, const llmoc_int4_view* shared_gate,
+                           const llmoc_int4_view* shared_up, const llmoc_int4_view* shared_down,
+                           float shared_scale, float* y);
+
+/* ------------------------------------------- batched device-resident layer */
+
+/* One MoE layer uploaded once into HBM in the kernels' repacked layout: the
+ * replacement for the per-token moe_ffn_token loop
+ * (src/model/qwen3_6_moe_int4_model.cpp:377-404, called per token from
+ * src/model/qwen3_5_int4_model.cpp:1204-1208) and for the expert slot cache
+ * (src/moe/offload_cache.h:24-91, src/moe/host_banks.h:54-111). */
+typedef struct llmoc_moe_layer llmoc_moe_layer;
+
+typedef struct llmoc_moe_layer_desc {
+  int32_t hidden;         /* H */
+  int32_t inter;          /* I (routed and shared experts) */
+  int32_t n_experts;      /* E routed experts */
+  int32_t topk;           /* k <= 64 (qwen3_6_moe_int4_model.cpp:384) */
+  int32_t group_size;     /* INT4 group along K */
+  int32_t scheme;         /* LLMOC_SCHEME_* (all experts) */
+  int32_t awq_zp;         /* <= 0 means 7 */
+  int32_t router;         /* LLMOC_ROUTER_* */
+  float routed_scaling;   /* sigmoid router: weight multiplier */
+  int32_t has_shared;     /* 1: one always-on shared expert */
+  float shared_scale;     /* its combine weight */
+} llmoc_moe_layer_desc;
+
+/* Create from host QLWC views: router_w [E,H] bf16, bias [E] fp32 (sigmoid
+ * router, else NULL), experts[3*E] = (gate, up, down) per expert, shared[3]
+ * or NULL.  Uploads and repacks on `device`.  The host buffers are not kept. */
+LLMOC_API llmoc_status llmoc_moe_layer_create(const llmoc_moe_layer_desc* desc, const uint16_t* router_w,
+                                    const float* bias, const llmoc_int4_view* experts,
+                                    const llmoc_int4_view* shared, int device,
+                                    llmoc_moe_layer** out);
+/* Same, but every pointer (router_w, bias, and the views' qweight/scales/zeros)
+ * is a device pointer on `device` (no host staging; used to build large layers
+ * directly in HBM). */
+LLMOC_API llmoc_status llmoc_moe_layer_create_device(const llmoc_moe_layer_desc* desc,
+                                           const uint16_t* router_w, const float* bias,
+                                           const llmoc_int4_view* experts,
+                                           const llmoc_int4_view* shared, int device,
+                                           llmoc_moe_layer** out);
+LLMOC_API void llmoc_moe_layer_destroy(llmoc_moe_layer* layer);
+/* Bytes of resident expert weights (packed q + fp16 scales/zeros), router excluded. */
+LLMOC_API size_t llmoc_moe_layer_weight_bytes(const llmoc_moe_layer* layer);
+/* Bytes one expert streams per forward (src/moe/qlwc_expert_bytes.h:43-60). */
+LLMOC_API size_t llmoc_expert_storage_bytes(int H, int I, int group_size, int has_zeros);
+
+/* Workspace (device memory the caller provides) for up to max_tokens tokens. */
+LLMOC_API size_t llmoc_moe_workspace_bytes(const llmoc_moe_layer* layer, int max_tokens);
+
+/* Y[T,H] bf16 = MoE(X[T,H] bf16): router GEMV (fp32, the reference's
+ * summation order), softmax or sigmoid+bias top-k, renormalise, canonical
+ * permutation, grouped INT4 gate/up + SiLU*mul, down, weighted combine (+ the
+ * shared expert).  T may be 0 (no work).  Asynchronous on `stream`. */
+LLMOC_API llmoc_status llmoc_moe_forward(const llmoc_moe_layer* layer, const uint16_t* X, int T, uint16_t* Y,
+                               void* workspace, size_t workspace_bytes, void* stream);
+
+/* Routing results inside a workspace after llmoc_moe_forward / llmoc_moe_route
+ * (device pointers; kk = topk + has_shared slots per token):
+ *   logits [T,E] fp32; ids [T,kk] int32; weights [T,kk] fp32;
+ *   offsets [E+has_shared+1] int32; sorted [T*kk] int32 (= t*kk + j);
+ *   inverse [T*kk] int32; n_active: number of experts with >= 1 pair. */
+typedef struct llmoc_route_views {
+  float* logits;
+  int32_t* ids;
+  float* weights;
+  int32_t* offsets;
+  int32_t* sorted;
+  int32_t* inverse;
+  int32_t* n_active;
+} llmoc_route_views;
+LLMOC_API llmoc_status llmoc_moe_route_views(const llmoc_moe_layer* layer, int T, void* workspace,
+                                   size_t workspace_bytes, llmoc_route_views* out);
+/* Routing and permutation only (no expert FFN). */
+LLMOC_API llmoc_status llmoc_moe_route(const llmoc_moe_layer* layer, const uint16_t* X, int T,
+                             void* workspace, size_t workspace_bytes, void* stream);
+
+/* Dequantise one resident projection (proj 0 gate, 1 up, 2 down; expert ==
+ * n_experts selects the shared expert) from the repacked layout into
+ * out[M*K] fp32 (device), bit-exact with hal::dequant_int4_matrix. */
+LLMOC_API llmoc_status llmoc_moe_dequant(const llmoc_moe_layer* layer, int expert, int proj, float* out,
+                               void* stream);
+
+/* Per-stage CUDA-event timing of llmoc_moe_forward (the reference only keeps
+ * wall-clock accumulators, src/hal/cuda_backend.cpp:285-288, :5347-5357).
+ * While enabled, every forward records events around its six stages on its
+ * stream: 0 router GEMV, 1 top-k, 2 permutation, 3 gate/up + SiLU*mul,
+ * 4 down, 5 combine.  llmoc_moe_stage_times synchronizes on the recorded
+ * events, writes the summed milliseconds per stage into ms[6] and the number
+ * of timed calls into *calls, and clears the record.  Disabling also clears. */
+LLMOC_API llmoc_status llmoc_moe_set_stage_timing(llmoc_moe_layer* layer, int enable);
+LLMOC_API llmoc_status llmoc_moe_stage_times(llmoc_moe_layer* layer, float* ms, int* calls);
+
+/* ------------------------------------------------------------ utilities */
+
+/* quant_awq_sym (tools/quantize_int4.py:150-166) on the device: W [M,K] bf16
+ * -> q [M,K/2], scales [M,K/gs] fp16.  bf16_scale rounds each scale to bf16
+ * first.  Requires K % gs == 0.  Used to build synthetic layers in HBM. */
+LLMOC_API llmoc_status llmoc_quantize_awq_sym(const uint16_t* W, int M, int K, int group_size,
+                                    int bf16_scale, uint8_t* q, uint16_t* scales, void* stream);
+
+/* Number of this library's kernels launched since load (all devices). */
+LLMOC_API uint64_t llmoc_kernel_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LLMOC_B200_H */

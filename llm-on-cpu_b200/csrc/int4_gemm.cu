@@ -1,0 +1,573 @@
+// int4_gemm.cu — INT4 weight-only grouped GEMM kernels and their helpers.
+//
+//  k_repack            QLWC layout (src/weights/qlwc_format.h) -> fragment order
+//  k_dequant           fragment order -> fp32 W[M,K] (bit-exact with
+//                      hal::dequant_int4_row, src/hal/int4_ops.cpp:640-662)
+//  k_int4_mma          tensor-core grouped dequant-GEMM for AWQ-sym weights
+//                      and bf16 activations (decode and small groups)
+//  k_int4_cc           CUDA-core fp32 grouped GEMV for any scheme and fp32 or
+//                      bf16 activations (GPTQ-asym, the host-fp32 API)
+//  k_combine           y[t] = sum_j w[t,j] * d[t,j] (+ shared), fixed j order
+//  k_quant_awq_sym     tools/quantize_int4.py:150-166 on the device
+//
+// Both GEMM kernels walk a device-built work list (expert, first row of the
+// expert-sorted pair list, <= 32 rows) and read one weight row-tile per warp,
+// so every selected expert's weights stream from HBM once per 32 of its
+// tokens.  The per-group structure of the reference (dot of x with (q - zp)
+// per group, times the group scale, accumulated in fp32; int4_ops.cpp:228)
+// is kept: the tensor core multiplies exact bf16 integers (q - zp) by bf16
+// activations, and the fp32 group partials are scaled on the accumulator.
+#include "kernels.cuh"
+
+namespace llmoc {
+
+// ------------------------------------------------------------------ repack
+
+__device__ __forceinline__ uint32_t src_nib(const RepackArgs& a, int r, int k) {
+  if (r >= a.M || k >= a.K) return 0u;
+  const uint8_t b = a.q[(size_t)r * ((a.K + 1) / 2) + (k >> 1)];
+  return (k & 1) ? (b >> 4) : (b & 0xFu);
+}
+
+__global__ void k_repack(RepackArgs a) {
+  const int Mt = (a.M + 15) / 16;
+  const size_t n_words = (size_t)Mt * a.Kc * 128;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n_words;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const int wd = (int)(i & 3);
+    const int lane = (int)((i >> 2) & 31);
+    const size_t tc = i >> 7;  // rt * Kc + c
+    const int c = (int)(tc % a.Kc);
+    const int rt = (int)(tc / a.Kc);
+    const int g = lane >> 2, t = lane & 3, kb = wd >> 1, kt = wd & 1;
+    const int r0 = rt * 16 + g, r1 = r0 + 8;
+    const int k = c * 64 + kb * 32 + t * 8 + kt * 4;
+    // nibble slot = (i&1)*4 + (i>>1)*2 + (row g+8 ? 1 : 0)
+    uint32_t w = 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int slot = (e & 1) * 4 + (e >> 1) * 2;
+      w |= src_nib(a, r0, k + e) << (4 * slot);
+      w |= src_nib(a, r1, k + e) << (4 * (slot + 1));
+    }
+    a.qo[i] = w;
+  }
+  const size_t n_sc = (size_t)Mt * a.ng * 16;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n_sc;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const int r = (int)(i & 15);
+    const size_t tg = i >> 4;
+    const int grp = (int)(tg % a.ng);
+    const int rt = (int)(tg / a.ng);
+    const int row = rt * 16 + r;
+    const bool ok = row < a.M;
+    a.so[i] = ok ? a.s[(size_t)row * a.ng + grp] : (uint16_t)0;
+    if (a.zo) a.zo[i] = (ok && a.z) ? a.z[(size_t)row * a.ng + grp] : (uint16_t)0;
+  }
+}
+
+// ----------------------------------------------------------------- dequant
+
+// out[M,K] fp32 = (q - zp) * s (AWQ) or q * s + z (GPTQ), read from the
+// fragment-order copy (proves the repack and the kernels' indexing).
+__global__ void k_dequant(ProjDev P, int M, int K, int gs, int ng, int Kc, int awq, int zp,
+                          float* __restrict__ out) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < (size_t)M * K;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const int m = (int)(i / K), k = (int)(i % K);
+    const int rt = m >> 4, r = m & 15, g = r & 7, hi = r >> 3;
+    const int c = k >> 6, kb = (k >> 5) & 1, t = (k >> 3) & 3, kt = (k >> 2) & 1, e = k & 3;
+    const int lane = g * 4 + t;
+    const uint32_t* q32 = reinterpret_cast<const uint32_t*>(P.q);
+    const uint32_t w = q32[(((size_t)rt * Kc + c) * 32 + lane) * 4 + kb * 2 + kt];
+    const int slot = (e & 1) * 4 + (e >> 1) * 2 + hi;
+    const int q = (w >> (4 * slot)) & 0xF;
+    const int grp = k / gs;
+    const float s = __half2float(P.s[((size_t)rt * ng + grp) * 16 + r]);
+    if (awq) {
+      out[i] = __fmul_rn((float)(q - zp), s);
+    } else {
+      const float z = P.z ? __half2float(P.z[((size_t)rt * ng + grp) * 16 + r]) : 0.f;
+      out[i] = __fmaf_rn((float)q, s, z);  // q*s is exact, so this equals q*s + z
+    }
+  }
+}
+
+// ---------------------------------------------------- tensor-core grouped GEMM
+
+__device__ __forceinline__ const ProjDev& pick(const ExpertDev& e, int p) {
+  return p == 0 ? e.gate : (p == 1 ? e.up : e.down);
+}
+
+__device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t bf16x2_sub(uint32_t a, uint32_t b) {
+  __nv_bfloat162 x = *reinterpret_cast<__nv_bfloat162*>(&a);
+  const __nv_bfloat162 y = *reinterpret_cast<__nv_bfloat162*>(&b);
+  x = __hsub2(x, y);
+  return *reinterpret_cast<uint32_t*>(&x);
+}
+
+// One 32-bit fragment word -> the four A registers (bf16 pairs of q - zp).
+__device__ __forceinline__ void dequant_word(uint32_t w, uint32_t zp2, uint32_t a[4]) {
+  a[0] = bf16x2_sub(lop3_and_or(w, 0x000F000Fu, 0x43004300u), zp2);
+  a[1] = bf16x2_sub(lop3_and_or(w >> 4, 0x000F000Fu, 0x43004300u), zp2);
+  a[2] = bf16x2_sub(lop3_and_or(w >> 8, 0x000F000Fu, 0x43004300u), zp2);
+  a[3] = bf16x2_sub(lop3_and_or(w >> 12, 0x000F000Fu, 0x43004300u), zp2);
+}
+
+__device__ __forceinline__ void mma_bf16(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint4 ldg_nc(const uint4* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ float silu_mul(float g, float u) { return (g / (1.f + expf(-g))) * u; }
+
+// grid.x = ceil(Mt / 4) (one 16-row tile per warp), grid.y = work-list bound.
+// NP = 2 computes gate and up of the same rows (GATE_UP), NP = 1 one projection.
+template <int MODE, int NT>
+__global__ void __launch_bounds__(128) k_int4_mma(GemmArgs a) {
+  constexpr int NP = MODE == MODE_GATE_UP ? 2 : 1;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int rt = blockIdx.x * 4 + warp;
+  if (rt * 16 >= a.M) return;
+  if ((int)blockIdx.y >= *a.n_work) return;
+  const WorkItem it = a.work[blockIdx.y];
+  const ExpertDev& ex = a.experts[it.expert];
+  const ProjDev* P[2];
+  P[0] = MODE == MODE_GATE_UP ? &ex.gate : &pick(ex, a.proj);
+  P[1] = &ex.up;
+  const int ntc = (it.nrows + 7) >> 3;
+
+  const __nv_bfloat16* brow[NT];
+  bool bval[NT];
+#pragma unroll
+  for (int n = 0; n < NT; ++n) {
+    const int r = 8 * n + g;
+    bval[n] = r < it.nrows;
+    const int pos = it.row0 + (bval[n] ? r : 0);
+    const int row = a.gather ? a.gather[pos] / a.kk : pos;
+    brow[n] = reinterpret_cast<const __nv_bfloat16*>(a.B) + (size_t)row * a.ldb + 8 * t;
+  }
+  const uint32_t zp2 = (uint32_t)(0x4300 + a.zp) * 0x10001u;  // bf16 (128+zp) twice
+  // bf16 128+zp is exact for zp < 128: 0x4300 encodes 128, mantissa step 1
+
+  float acc[NP][NT][4], tmp[NP][NT][4];
+#pragma unroll
+  for (int p = 0; p < NP; ++p)
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) acc[p][n][r] = tmp[p][n][r] = 0.f;
+
+  const uint4* qp[NP];
+#pragma unroll
+  for (int p = 0; p < NP; ++p) qp[p] = P[p]->q + (size_t)rt * a.Kc * 32 + lane;
+
+  for (int c = 0; c < a.Kc; ++c) {
+    uint4 qw[NP];
+#pragma unroll
+    for (int p = 0; p < NP; ++p) qw[p] = ldg_nc(qp[p] + (size_t)c * 32);
+#pragma unroll
+    for (int kb = 0; kb < 2; ++kb) {
+      const int k32 = c * 64 + kb * 32;
+      if (k32 >= a.K) break;
+      uint4 bv[NT];
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        bv[n] = make_uint4(0, 0, 0, 0);
+        if (n < ntc && bval[n]) bv[n] = *reinterpret_cast<const uint4*>(brow[n] + k32);
+      }
+#pragma unroll
+      for (int kt = 0; kt < 2; ++kt) {
+#pragma unroll
+        for (int p = 0; p < NP; ++p) {
+          const uint32_t wd = (kb * 2 + kt == 0)   ? qw[p].x
+                              : (kb * 2 + kt == 1) ? qw[p].y
+                              : (kb * 2 + kt == 2) ? qw[p].z
+                                                   : qw[p].w;
+          uint32_t af[4];
+          dequant_word(wd, zp2, af);
+#pragma unroll
+          for (int n = 0; n < NT; ++n) {
+            if (n < ntc) {
+              const uint32_t b0 = kt ? bv[n].z : bv[n].x;
+              const uint32_t b1 = kt ? bv[n].w : bv[n].y;
+              mma_bf16(tmp[p][n], af, b0, b1);
+            }
+          }
+        }
+      }
+      if (((k32 + 32) % a.gs) == 0 || k32 + 32 >= a.K) {
+        const int grp = k32 / a.gs;
+#pragma unroll
+        for (int p = 0; p < NP; ++p) {
+          const __half* sp = P[p]->s + ((size_t)rt * a.ng + grp) * 16;
+          const float s0 = __half2float(sp[g]), s1 = __half2float(sp[g + 8]);
+#pragma unroll
+          for (int n = 0; n < NT; ++n) {
+            acc[p][n][0] = __fmaf_rn(tmp[p][n][0], s0, acc[p][n][0]);
+            acc[p][n][1] = __fmaf_rn(tmp[p][n][1], s0, acc[p][n][1]);
+            acc[p][n][2] = __fmaf_rn(tmp[p][n][2], s1, acc[p][n][2]);
+            acc[p][n][3] = __fmaf_rn(tmp[p][n][3], s1, acc[p][n][3]);
+            tmp[p][n][0] = tmp[p][n][1] = tmp[p][n][2] = tmp[p][n][3] = 0.f;
+          }
+        }
+      }
+    }
+  }
+
+  // epilogue: C fragment (row g / g+8, col 2t / 2t+1) of each N-tile
+  const int m0 = rt * 16 + g, m1 = m0 + 8;
+#pragma unroll
+  for (int n = 0; n < NT; ++n) {
+    if (n >= ntc) continue;
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int col = 8 * n + 2 * t + (r & 1);
+      const int m = (r < 2) ? m0 : m1;
+      if (col >= it.nrows || m >= a.M) continue;
+      const size_t o = (size_t)(it.row0 + col) * a.ldo + m;
+      float v = acc[0][n][r];
+      if (!isfinite(v)) v = 0.f;  // non-finite -> 0, as every reference GEMV does
+      if (MODE == MODE_GATE_UP) {
+        float u = acc[NP - 1][n][r];
+        if (!isfinite(u)) u = 0.f;
+        reinterpret_cast<__nv_bfloat16*>(a.out)[o] = __float2bfloat16_rn(silu_mul(v, u));
+      } else {
+        reinterpret_cast<float*>(a.out)[o] = v;
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------ CUDA-core fp32 GEMV
+
+template <typename BT>
+__device__ __forceinline__ void load8(const BT* p, float v[8]);
+template <>
+__device__ __forceinline__ void load8<float>(const float* p, float v[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p);
+  const float4 b = *reinterpret_cast<const float4*>(p + 4);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+template <>
+__device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* p, float v[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = __uint_as_float(w[i] << 16);
+    v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+// Same work decomposition as k_int4_mma: one 16-row tile per warp; lane
+// (g, t) owns rows g and g+8 at the 16 k positions of its fragment words.
+// Per group it forms sum x*(q - zp) (AWQ) or sum x*q and sum x (GPTQ) in
+// fp32 and accumulates them times the group scale (and zero).  Handles the
+// item's rows TOK at a time.
+template <int MODE, typename BT, int TOK>
+__global__ void __launch_bounds__(128) k_int4_cc(GemmArgs a, int awq) {
+  constexpr int NP = MODE == MODE_GATE_UP ? 2 : 1;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int rt = blockIdx.x * 4 + warp;
+  if (rt * 16 >= a.M) return;
+  if ((int)blockIdx.y >= *a.n_work) return;
+  const WorkItem it = a.work[blockIdx.y];
+  const ExpertDev& ex = a.experts[it.expert];
+  const ProjDev* P[2];
+  P[0] = MODE == MODE_GATE_UP ? &ex.gate : &pick(ex, a.proj);
+  P[1] = &ex.up;
+  const float zp = (float)a.zp;
+
+  for (int r0 = 0; r0 < it.nrows; r0 += TOK) {
+    const BT* brow[TOK];
+    bool bv[TOK];
+#pragma unroll
+    for (int j = 0; j < TOK; ++j) {
+      bv[j] = r0 + j < it.nrows;
+      const int pos = it.row0 + (bv[j] ? r0 + j : 0);
+      const int row = a.gather ? a.gather[pos] / a.kk : pos;
+      brow[j] = reinterpret_cast<const BT*>(a.B) + (size_t)row * a.ldb + 8 * t;
+    }
+    float acc[NP][2][TOK];
+    float pq[NP][2][TOK], px[TOK];
+#pragma unroll
+    for (int p = 0; p < NP; ++p)
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int j = 0; j < TOK; ++j) acc[p][h][j] = pq[p][h][j] = 0.f;
+#pragma unroll
+    for (int j = 0; j < TOK; ++j) px[j] = 0.f;
+
+    for (int c = 0; c < a.Kc; ++c) {
+      uint4 qw[NP];
+#pragma unroll
+      for (int p = 0; p < NP; ++p) qw[p] = ldg_nc(P[p]->q + ((size_t)rt * a.Kc + c) * 32 + lane);
+#pragma unroll
+      for (int kb = 0; kb < 2; ++kb) {
+        const int k32 = c * 64 + kb * 32;
+        if (k32 >= a.K) break;
+        float xv[TOK][8];
+#pragma unroll
+        for (int j = 0; j < TOK; ++j) {
+          if (bv[j]) {
+            load8<BT>(brow[j] + k32, xv[j]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) xv[j][e] = 0.f;
+          }
+        }
+#pragma unroll
+        for (int p = 0; p < NP; ++p) {
+          const uint32_t w0 = kb ? qw[p].z : qw[p].x;
+          const uint32_t w1 = kb ? qw[p].w : qw[p].y;
+          // element e (0..7) of the lane's 8 k values: kt = e>>2, i = e&3
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const uint32_t w = (e >> 2) ? w1 : w0;
+            const int i = e & 3;
+            const int slot = (i & 1) * 4 + (i >> 1) * 2;
+            const float q0 = (float)((w >> (4 * slot)) & 0xF);
+            const float q1 = (float)((w >> (4 * (slot + 1))) & 0xF);
+            const float d0 = awq ? q0 - zp : q0;
+            const float d1 = awq ? q1 - zp : q1;
+#pragma unroll
+            for (int j = 0; j < TOK; ++j) {
+              pq[p][0][j] = __fmaf_rn(xv[j][e], d0, pq[p][0][j]);
+              pq[p][1][j] = __fmaf_rn(xv[j][e], d1, pq[p][1][j]);
+            }
+          }
+        }
+        if (!awq) {
+#pragma unroll
+          for (int j = 0; j < TOK; ++j)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) px[j] += xv[j][e];
+        }
+        if (((k32 + 32) % a.gs) == 0 || k32 + 32 >= a.K) {
+          const int grp = k32 / a.gs;
+#pragma unroll
+          for (int p = 0; p < NP; ++p) {
+            const size_t so = ((size_t)rt * a.ng + grp) * 16;
+            const float s0 = __half2float(P[p]->s[so + g]), s1 = __half2float(P[p]->s[so + g + 8]);
+            float z0 = 0.f, z1 = 0.f;
+            if (!awq && P[p]->z) {
+              z0 = __half2float(P[p]->z[so + g]);
+              z1 = __half2float(P[p]->z[so + g + 8]);
+            }
+#pragma unroll
+            for (int j = 0; j < TOK; ++j) {
+              acc[p][0][j] = __fmaf_rn(pq[p][0][j], s0, acc[p][0][j]);
+              acc[p][1][j] = __fmaf_rn(pq[p][1][j], s1, acc[p][1][j]);
+              if (!awq) {
+                acc[p][0][j] = __fmaf_rn(px[j], z0, acc[p][0][j]);
+                acc[p][1][j] = __fmaf_rn(px[j], z1, acc[p][1][j]);
+              }
+              pq[p][0][j] = pq[p][1][j] = 0.f;
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < TOK; ++j) px[j] = 0.f;
+        }
+      }
+    }
+    // reduce over the 4 lanes t of row group g
+#pragma unroll
+    for (int p = 0; p < NP; ++p)
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int j = 0; j < TOK; ++j) {
+          float v = acc[p][h][j];
+          v += __shfl_xor_sync(0xffffffffu, v, 1);
+          v += __shfl_xor_sync(0xffffffffu, v, 2);
+          acc[p][h][j] = v;
+        }
+    if (t == 0) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int m = rt * 16 + g + 8 * h;
+        if (m >= a.M) continue;
+#pragma unroll
+        for (int j = 0; j < TOK; ++j) {
+          if (!bv[j]) continue;
+          const size_t o = (size_t)(it.row0 + r0 + j) * a.ldo + m;
+          float v = acc[0][h][j];
+          if (!isfinite(v)) v = 0.f;
+          if (MODE == MODE_GATE_UP) {
+            float u = acc[NP - 1][h][j];
+            if (!isfinite(u)) u = 0.f;
+            const float mid = silu_mul(v, u);
+            if (a.out_bf16)
+              reinterpret_cast<__nv_bfloat16*>(a.out)[o] = __float2bfloat16_rn(mid);
+            else
+              reinterpret_cast<float*>(a.out)[o] = mid;
+          } else {
+            reinterpret_cast<float*>(a.out)[o] = v;
+          }
+        }
+      }
+    }
+  }
+}
+
+// ----------------------------------------------------------------- combine
+
+// y[t,h] = sum_{j<kk} w[t,j] * d[inverse[t*kk+j], h] in j order (fma), the
+// order of the reference's combine (qwen3_6_moe_int4_model.cpp:213, :372).
+template <typename OT>
+__global__ void k_combine(const float* __restrict__ d, const int* __restrict__ inverse,
+                          const float* __restrict__ w, int T, int kk, int H, OT* __restrict__ y,
+                          int skip_tiny) {
+  const int t = blockIdx.y;
+  const int h = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  if (t >= T || h >= H) return;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int j = 0; j < kk; ++j) {
+    const float wj = w[(size_t)t * kk + j];
+    if (skip_tiny && fabsf(wj) < 1e-12f) continue;
+    const float* row = d + (size_t)inverse[(size_t)t * kk + j] * H;
+    if (h + 3 < H) {
+      const float4 v = *reinterpret_cast<const float4*>(row + h);
+      acc.x = __fmaf_rn(wj, v.x, acc.x);
+      acc.y = __fmaf_rn(wj, v.y, acc.y);
+      acc.z = __fmaf_rn(wj, v.z, acc.z);
+      acc.w = __fmaf_rn(wj, v.w, acc.w);
+    } else {
+      float* ap = &acc.x;
+      for (int i = 0; h + i < H; ++i) ap[i] = __fmaf_rn(wj, row[h + i], ap[i]);
+    }
+  }
+  const float* ap = &acc.x;
+  for (int i = 0; i < 4 && h + i < H; ++i) {
+    if constexpr (sizeof(OT) == 2)
+      y[(size_t)t * H + h + i] = __float2bfloat16_rn(ap[i]);
+    else
+      y[(size_t)t * H + h + i] = ap[i];
+  }
+}
+
+// ---------------------------------------------------------------- quantize
+
+// quant_awq_sym: scale = max(absmax / 7, 1e-8); optionally rounded to bf16;
+// stored as fp16 (round-to-nearest-even); q = clip(rint(w / scale) + 7, 0, 15).
+__global__ void k_quant_awq_sym(const __nv_bfloat16* __restrict__ W, int M, int K, int gs,
+                                int bf16_scale, uint8_t* __restrict__ q, __half* __restrict__ sc) {
+  const int ng = K / gs;
+  const size_t n = (size_t)M * ng;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const int m = (int)(i / ng), grp = (int)(i % ng);
+    const __nv_bfloat16* row = W + (size_t)m * K + (size_t)grp * gs;
+    float amax = 0.f;
+    for (int k = 0; k < gs; ++k) amax = fmaxf(amax, fabsf(__bfloat162float(row[k])));
+    float s = __fdiv_rn(amax, 7.0f);
+    if (!(s > 1e-8f)) s = 1e-8f;
+    if (bf16_scale) s = __bfloat162float(__float2bfloat16_rn(s));
+    sc[i] = __float2half_rn(s);
+    uint8_t* qo = q + (size_t)m * (K / 2) + (size_t)grp * gs / 2;
+    for (int k = 0; k < gs; k += 2) {
+      float q0 = rintf(__fdiv_rn(__bfloat162float(row[k]), s)) + 7.f;
+      float q1 = rintf(__fdiv_rn(__bfloat162float(row[k + 1]), s)) + 7.f;
+      q0 = fminf(fmaxf(q0, 0.f), 15.f);
+      q1 = fminf(fmaxf(q1, 0.f), 15.f);
+      qo[k / 2] = (uint8_t)((uint32_t)q0 | ((uint32_t)q1 << 4));
+    }
+  }
+}
+
+// -------------------------------------------------------------- launchers
+
+static int grid_for(size_t n, int threads) {
+  size_t b = (n + threads - 1) / threads;
+  if (b > 148u * 64u) b = 148u * 64u;
+  return (int)(b ? b : 1);
+}
+
+cudaError_t launch_repack(const RepackArgs& a, cudaStream_t st) {
+  const int Mt = (a.M + 15) / 16;
+  const size_t n = (size_t)Mt * a.Kc * 128;
+  k_repack<<<grid_for(n, 256), 256, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_dequant(const ProjDev& P, int M, int K, int gs, int awq, int zp, float* out,
+                           cudaStream_t st) {
+  const int ng = (K + gs - 1) / gs, Kc = (K + 63) / 64;
+  k_dequant<<<grid_for((size_t)M * K, 256), 256, 0, st>>>(P, M, K, gs, ng, Kc, awq, zp, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemm(int mode, int path, const GemmArgs& a, int max_work, int awq,
+                        int ntiles, cudaStream_t st) {
+  if (max_work <= 0) return cudaSuccess;
+  const int Mt = (a.M + 15) / 16;
+  dim3 grid((Mt + 3) / 4, max_work);
+  if (path == 0) {
+    if (mode == MODE_GATE_UP) {
+      if (ntiles <= 1)
+        k_int4_mma<MODE_GATE_UP, 1><<<grid, 128, 0, st>>>(a);
+      else
+        k_int4_mma<MODE_GATE_UP, 4><<<grid, 128, 0, st>>>(a);
+    } else {
+      if (ntiles <= 1)
+        k_int4_mma<MODE_PLAIN_F32, 1><<<grid, 128, 0, st>>>(a);
+      else
+        k_int4_mma<MODE_PLAIN_F32, 4><<<grid, 128, 0, st>>>(a);
+    }
+  } else if (path == 1) {
+    if (mode == MODE_GATE_UP)
+      k_int4_cc<MODE_GATE_UP, float, 4><<<grid, 128, 0, st>>>(a, awq);
+    else
+      k_int4_cc<MODE_PLAIN_F32, float, 4><<<grid, 128, 0, st>>>(a, awq);
+  } else {
+    if (mode == MODE_GATE_UP)
+      k_int4_cc<MODE_GATE_UP, __nv_bfloat16, 4><<<grid, 128, 0, st>>>(a, awq);
+    else
+      k_int4_cc<MODE_PLAIN_F32, __nv_bfloat16, 4><<<grid, 128, 0, st>>>(a, awq);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_combine(const float* d, const int* inverse, const float* w, int T, int kk, int H,
+                           void* y, int y_bf16, int skip_tiny, cudaStream_t st) {
+  if (T <= 0) return cudaSuccess;
+  const int threads = 128;
+  dim3 grid(((H + 3) / 4 + threads - 1) / threads, T);
+  if (y_bf16)
+    k_combine<__nv_bfloat16><<<grid, threads, 0, st>>>(d, inverse, w, T, kk, H,
+                                                      (__nv_bfloat16*)y, skip_tiny);
+  else
+    k_combine<float><<<grid, threads, 0, st>>>(d, inverse, w, T, kk, H, (float*)y, skip_tiny);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quant_awq_sym(const __nv_bfloat16* W, int M, int K, int gs, int bf16_scale,
+                                 uint8_t* q, __half* sc, cudaStream_t st) {
+  const size_t n = (size_t)M * (K / gs);
+  k_quant_awq_sym<<<grid_for(n, 128), 128, 0, st>>>(W, M, K, gs, bf16_scale, q, sc);
+  return cudaGetLastError();
+}
+
+}  // namespace llmoc

@@ -1,0 +1,82 @@
+// kernels.cuh — argument structs and launchers shared by the kernel files
+// (route.cu, int4_gemm.cu) and the host runtime (runtime.cu).
+#pragma once
+#include "common.cuh"
+
+namespace llmoc {
+
+// ---- route.cu
+struct TopkArgs {
+  const float* logits;   // [T,E]
+  const float* bias;     // [E] (sigmoid router)
+  int T, E, k, kk;       // kk = k + has_shared
+  int router;            // 0 softmax, 1 sigmoid+bias
+  float routed_scaling;
+  float shared_scale;
+  int has_shared;
+  int* ids;              // [T,kk]
+  float* weights;        // [T,kk]
+};
+
+struct PermArgs {
+  const int* ids;   // [n] expert id per pair, n = T*kk, pair p = t*kk + j
+  int n;
+  int n_exp;        // experts incl. the shared one
+  int* offsets;     // [n_exp+1]
+  int* sorted;      // [n]
+  int* inverse;     // [n]
+  WorkItem* work;   // [max_work]
+  int* n_work;
+  int* n_active;
+};
+
+constexpr int kPermThreads = 1024;
+constexpr int kPermWarps = kPermThreads / 32;
+constexpr int kMaxExpPerm = 512;  // experts (incl. shared) the permutation CTA handles
+
+cudaError_t launch_router_logits(const void* X, bool x_is_f32, const uint16_t* Wr, int T, int E,
+                                 int H, float* logits, cudaStream_t st);
+cudaError_t launch_topk(const TopkArgs& a, cudaStream_t st);
+cudaError_t launch_permute(const PermArgs& a, cudaStream_t st);
+
+// ---- int4_gemm.cu
+struct RepackArgs {
+  const uint8_t* q;      // QLWC [M, ceil(K/2)]
+  const uint16_t* s;     // [M, ng] fp16
+  const uint16_t* z;     // [M, ng] fp16 or nullptr
+  int M, K, gs, ng, Kc;  // Kc = ceil(K/64)
+  uint32_t* qo;          // [Mt][Kc][32][4] words
+  uint16_t* so;          // [Mt][ng][16]
+  uint16_t* zo;          // [Mt][ng][16] or nullptr
+};
+
+enum { MODE_GATE_UP = 0, MODE_PLAIN_F32 = 1 };
+
+struct GemmArgs {
+  const ExpertDev* experts;
+  int proj;               // MODE_PLAIN_F32: 0 gate, 1 up, 2 down
+  int M, K, Kc, gs, ng;
+  int zp;                 // AWQ zero point
+  const void* B;          // activations (bf16 for mma; bf16 or fp32 for cc)
+  int ldb;
+  const int* gather;      // B row of sorted pos p = gather[p] / kk (nullptr: row p)
+  int kk;
+  const WorkItem* work;
+  const int* n_work;
+  void* out;              // GATE_UP: mid [pos][ldo]; PLAIN: fp32 [pos][ldo]
+  int ldo;
+  int out_bf16;           // GATE_UP output type (cc kernel): 1 bf16, 0 fp32
+};
+
+cudaError_t launch_repack(const RepackArgs& a, cudaStream_t st);
+cudaError_t launch_dequant(const ProjDev& P, int M, int K, int gs, int awq, int zp, float* out,
+                           cudaStream_t st);
+// path: 0 tensor-core (AWQ, bf16 B), 1 CUDA-core fp32 B, 2 CUDA-core bf16 B
+cudaError_t launch_gemm(int mode, int path, const GemmArgs& a, int max_work, int awq, int ntiles,
+                        cudaStream_t st);
+cudaError_t launch_combine(const float* d, const int* inverse, const float* w, int T, int kk, int H,
+                           void* y, int y_bf16, int skip_tiny, cudaStream_t st);
+cudaError_t launch_quant_awq_sym(const __nv_bfloat16* W, int M, int K, int gs, int bf16_scale,
+                                 uint8_t* q, __half* sc, cudaStream_t st);
+
+}  // namespace llmoc

@@ -1,0 +1,380 @@
+// route.cu — router GEMV, top-k selection and token->expert permutation.
+//
+// Router GEMV: logits[t,e] = W_r[e,:] . x[t,:] in exactly the fp32 order of
+// the reference's AVX2 hal::gemm_bias_free (src/hal/cpu_ops.cpp:57-86): 32
+// independent FMA chains, chain c covering k = c (mod 32) in increasing k,
+// folded as a[i] = (c[i]+c[8+i]) + (c[16+i]+c[24+i]); b[i] = a[i]+a[4+i];
+// r = (b0+b1) + (b2+b3); a K % 32 tail is added unfused; non-finite -> 0.
+// Products of bf16 weights with bf16/fp32 activations are formed by fmaf,
+// so the logits are bitwise equal to the reference's and the top-k ids are
+// too.  Layout: 8 lanes own the 32 chains of one (token, expert) dot (4
+// chains per lane, fed by 8-byte/16-byte vector loads); a warp holds 4 such
+// groups; register blocking over TW tokens x EW experts per group.
+//
+// Top-k: one warp per token, k rounds of a warp argmax (largest key, ties
+// to the smaller expert id).  Softmax weights follow
+// src/model/qwen3_6_moe_int4_model.cpp:388-402 (exp of l - max rounded to
+// fp32, probabilities normalised by a double sum in index order, weights
+// renormalised by a double sum in selection order).  Sigmoid+bias: s =
+// 1/(1+exp(-l)) in double rounded to fp32, selection on s + bias,
+// weights s / sum(s_sel) * routed_scaling.
+//
+// Permutation: one CTA, deterministic: pairs p = t*kk + j sorted stably by
+// expert (canonical order: expert, then t, then j), with per-expert offsets,
+// the inverse map, and the list of work items (<= 32 pairs of one expert).
+#include <cfloat>
+
+#include "kernels.cuh"
+
+namespace llmoc {
+
+// ------------------------------------------------------------ router GEMV
+
+template <typename XT>
+struct XLoad4;
+template <>
+struct XLoad4<__nv_bfloat16> {
+  __device__ __forceinline__ static void load(const __nv_bfloat16* p, float v[4]) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    v[0] = __uint_as_float(u.x << 16);
+    v[1] = __uint_as_float(u.x & 0xFFFF0000u);
+    v[2] = __uint_as_float(u.y << 16);
+    v[3] = __uint_as_float(u.y & 0xFFFF0000u);
+  }
+};
+template <>
+struct XLoad4<float> {
+  __device__ __forceinline__ static void load(const float* p, float v[4]) {
+    const float4 u = *reinterpret_cast<const float4*>(p);
+    v[0] = u.x;
+    v[1] = u.y;
+    v[2] = u.z;
+    v[3] = u.w;
+  }
+};
+
+// grid.x covers groups of (TW tokens x EW experts); 8 lanes per group.
+template <typename XT, int TW, int EW>
+__global__ void __launch_bounds__(256) k_router_logits(const XT* __restrict__ X,
+                                                       const uint16_t* __restrict__ Wr, int T,
+                                                       int E, int H, float* __restrict__ logits) {
+  const int lane = threadIdx.x & 31;
+  const int sub = lane & 7;  // owns chains 4*sub .. 4*sub+3
+  const int group = (blockIdx.x * blockDim.x + threadIdx.x) >> 3;
+  const int n_et = (E + EW - 1) / EW;
+  const int et = group % n_et;
+  const int tt = group / n_et;
+  const int t0 = tt * TW, e0 = et * EW;
+  const bool live = t0 < T;  // whole 8-lane group agrees
+
+  float acc[TW][EW][4];
+#pragma unroll
+  for (int a = 0; a < TW; ++a)
+#pragma unroll
+    for (int b = 0; b < EW; ++b)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc[a][b][c] = 0.f;
+
+  const XT* xr[TW];
+  const uint16_t* wr[EW];
+#pragma unroll
+  for (int a = 0; a < TW; ++a) xr[a] = X + (size_t)min(t0 + a, T - 1) * H;
+#pragma unroll
+  for (int b = 0; b < EW; ++b) wr[b] = Wr + (size_t)min(e0 + b, E - 1) * H;
+
+  const int K32 = live ? (H & ~31) : 0;
+#pragma unroll 2
+  for (int k = 4 * sub; k < K32; k += 32) {
+    float xv[TW][4];
+#pragma unroll
+    for (int a = 0; a < TW; ++a) XLoad4<XT>::load(xr[a] + k, xv[a]);
+#pragma unroll
+    for (int b = 0; b < EW; ++b) {
+      const uint2 u = *reinterpret_cast<const uint2*>(wr[b] + k);
+      float wv[4];
+      wv[0] = __uint_as_float(u.x << 16);
+      wv[1] = __uint_as_float(u.x & 0xFFFF0000u);
+      wv[2] = __uint_as_float(u.y << 16);
+      wv[3] = __uint_as_float(u.y & 0xFFFF0000u);
+#pragma unroll
+      for (int a = 0; a < TW; ++a)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[a][b][c] = __fmaf_rn(xv[a][c], wv[c], acc[a][b][c]);
+    }
+  }
+
+  // Fold: chain index ch = 4*sub + c.  a[i] = (c[i]+c[8+i]) + (c[16+i]+c[24+i])
+  // chain i lives in lane sub = i/4 register i%4; chain 8+i in sub+2; 16+i in
+  // sub+4; 24+i in sub+6.
+#pragma unroll
+  for (int a = 0; a < TW; ++a)
+#pragma unroll
+    for (int b = 0; b < EW; ++b) {
+      float v[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const float c8 = __shfl_down_sync(0xffffffffu, acc[a][b][c], 2, 8);
+        const float c16 = __shfl_down_sync(0xffffffffu, acc[a][b][c], 4, 8);
+        const float c24 = __shfl_down_sync(0xffffffffu, acc[a][b][c], 6, 8);
+        v[c] = (acc[a][b][c] + c8) + (c16 + c24);  // valid in sub 0,1: a[4*sub + c]
+      }
+      // b[i] = a[i] + a[4+i]: a[i] in sub 0 reg i, a[4+i] in sub 1 reg i
+      float bb[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) bb[c] = v[c] + __shfl_down_sync(0xffffffffu, v[c], 1, 8);
+      float r = (bb[0] + bb[1]) + (bb[2] + bb[3]);
+      if (sub == 0 && live && t0 + a < T && e0 + b < E) {
+        const int t = t0 + a, e = e0 + b;
+        for (int kk = K32; kk < H; ++kk) {
+          const float prod =
+              __fmul_rn(to_f32(X[(size_t)t * H + kk]), bf16_bits_to_f32(Wr[(size_t)e * H + kk]));
+          r = __fadd_rn(r, prod);  // the reference leaves this tail unfused
+        }
+        logits[(size_t)t * E + e] = isfinite(r) ? r : 0.f;
+      }
+    }
+}
+
+// --------------------------------------------------------------- top-k
+
+
+// One warp per token.  Dynamic smem: 8 warps x E floats (keys) + E floats (probs/scores).
+__global__ void __launch_bounds__(256) k_topk(TopkArgs a) {
+  extern __shared__ float sm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + warp;
+  if (t >= a.T) return;
+  float* key = sm + (size_t)warp * 2 * a.E;
+  float* val = key + a.E;  // softmax: p (float); sigmoid: s
+  const float* lg = a.logits + (size_t)t * a.E;
+
+  if (a.router == 0) {
+    float m = -INFINITY;
+    for (int e = lane; e < a.E; e += 32) {
+      const float l = lg[e];
+      key[e] = l;
+      m = fmaxf(m, l);
+    }
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    for (int e = lane; e < a.E; e += 32) {
+      // exp of the fp32 difference, correctly rounded to fp32 via double
+      val[e] = (float)exp((double)(lg[e] - m));
+    }
+  } else {
+    for (int e = lane; e < a.E; e += 32) {
+      const float s = (float)(1.0 / (1.0 + exp(-(double)lg[e])));
+      val[e] = s;
+      const float kv = s + a.bias[e];
+      key[e] = kv == kv ? kv : -FLT_MAX;  // a NaN bias must still leave a valid id
+    }
+  }
+  __syncwarp();
+
+  // k rounds of argmax over keys (ties -> smaller id); selected keys -> -inf.
+  int* ids = a.ids + (size_t)t * a.kk;
+  float* w = a.weights + (size_t)t * a.kk;
+  for (int j = 0; j < a.k; ++j) {
+    float bk = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int e = lane; e < a.E; e += 32) {
+      const float v = key[e];
+      if (v > bk || (v == bk && e < bi)) {
+        bk = v;
+        bi = e;
+      }
+    }
+    for (int o = 16; o; o >>= 1) {
+      const float ok = __shfl_xor_sync(0xffffffffu, bk, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ok > bk || (ok == bk && oi < bi)) {
+        bk = ok;
+        bi = oi;
+      }
+    }
+    // keys are never NaN (non-finite logits were zeroed, NaN sums mapped to
+    // -FLT_MAX), so a taken key set to -inf is never chosen again while k <= E
+    if (lane == 0) {
+      ids[j] = bi;
+      key[bi] = -INFINITY;
+    }
+    __syncwarp();
+  }
+
+  if (lane == 0) {
+    if (a.router == 0) {
+      double s = 0.0;
+      for (int e = 0; e < a.E; ++e) s += (double)val[e];
+      double wsum = 0.0;
+      for (int j = 0; j < a.k; ++j) wsum += (double)(float)((double)val[ids[j]] / s);
+      if (wsum < 1e-12) wsum = 1.0;
+      for (int j = 0; j < a.k; ++j) {
+        const float p = (float)((double)val[ids[j]] / s);
+        w[j] = (float)((double)p / wsum);
+      }
+    } else {
+      double wsum = 0.0;
+      for (int j = 0; j < a.k; ++j) wsum += (double)val[ids[j]];
+      if (wsum < 1e-20) wsum = 1.0;
+      for (int j = 0; j < a.k; ++j)
+        w[j] = __fmul_rn((float)((double)val[ids[j]] / wsum), a.routed_scaling);
+    }
+    if (a.has_shared) {
+      ids[a.k] = a.E;
+      w[a.k] = a.shared_scale;
+    }
+  }
+}
+
+// ----------------------------------------------------------- permutation
+
+// Single CTA.  smem: cnt[kPermWarps][n_exp] ints.
+__global__ void __launch_bounds__(kPermThreads) k_permute(PermArgs a) {
+  extern __shared__ int psm[];
+  int* cnt = psm;  // [warps][n_exp]: counts, then running positions
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < kPermWarps * a.n_exp; i += kPermThreads) cnt[i] = 0;
+  __syncthreads();
+
+  const int per = (a.n + kPermWarps - 1) / kPermWarps;
+  const int lo = min(a.n, warp * per), hi = min(a.n, lo + per);
+  for (int i = lo + lane; i < hi; i += 32) atomicAdd(&cnt[warp * a.n_exp + a.ids[i]], 1);
+  __syncthreads();
+
+  // per expert totals -> exclusive scans (pairs and work chunks); thread e
+  // handles expert e (n_exp <= 512 < 1024 threads).
+  const int e = threadIdx.x;
+  int tot = 0;
+  if (e < a.n_exp)
+    for (int w = 0; w < kPermWarps; ++w) tot += cnt[w * a.n_exp + e];
+  const int chunks = (tot + kChunkRows - 1) / kChunkRows;
+  // block exclusive scan of (tot, chunks, active) packed: do two scans
+  int v1 = tot, v2 = chunks, v3 = tot > 0;
+  for (int o = 1; o < 32; o <<= 1) {
+    const int a1 = __shfl_up_sync(0xffffffffu, v1, o);
+    const int a2 = __shfl_up_sync(0xffffffffu, v2, o);
+    const int a3 = __shfl_up_sync(0xffffffffu, v3, o);
+    if (lane >= o) {
+      v1 += a1;
+      v2 += a2;
+      v3 += a3;
+    }
+  }
+  __shared__ int w1[kPermWarps], w2[kPermWarps], w3[kPermWarps];
+  if (lane == 31) {
+    w1[warp] = v1;
+    w2[warp] = v2;
+    w3[warp] = v3;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    int x1 = w1[lane], x2 = w2[lane], x3 = w3[lane];
+    for (int o = 1; o < 32; o <<= 1) {
+      const int a1 = __shfl_up_sync(0xffffffffu, x1, o);
+      const int a2 = __shfl_up_sync(0xffffffffu, x2, o);
+      const int a3 = __shfl_up_sync(0xffffffffu, x3, o);
+      if (lane >= o) {
+        x1 += a1;
+        x2 += a2;
+        x3 += a3;
+      }
+    }
+    w1[lane] = x1;
+    w2[lane] = x2;
+    w3[lane] = x3;
+  }
+  __syncthreads();
+  const int base1 = (warp ? w1[warp - 1] : 0) + v1 - tot;     // exclusive pair offset
+  const int base2 = (warp ? w2[warp - 1] : 0) + v2 - chunks;  // exclusive chunk offset
+  if (e < a.n_exp) {
+    a.offsets[e] = base1;
+    int run = base1;
+    for (int w = 0; w < kPermWarps; ++w) {
+      const int c = cnt[w * a.n_exp + e];
+      cnt[w * a.n_exp + e] = run;
+      run += c;
+    }
+    for (int c = 0; c < chunks; ++c) {
+      WorkItem it;
+      it.expert = e;
+      it.row0 = base1 + c * kChunkRows;
+      it.nrows = min(kChunkRows, tot - c * kChunkRows);
+      it.pad = 0;
+      a.work[base2 + c] = it;
+    }
+  }
+  if (threadIdx.x == kPermThreads - 1) {
+    a.offsets[a.n_exp] = w1[kPermWarps - 1];
+    *a.n_work = w2[kPermWarps - 1];
+    *a.n_active = w3[kPermWarps - 1];
+  }
+  __syncthreads();
+
+  // placement: each warp walks its own range in order, 32 pairs at a time.
+  for (int b = lo; b < hi; b += 32) {
+    const int i = b + lane;
+    const bool ok = i < hi;
+    const unsigned act = __ballot_sync(0xffffffffu, ok);
+    if (ok) {
+      const int ex = a.ids[i];
+      const unsigned peers = __match_any_sync(act, ex);
+      const int rank = __popc(peers & lanemask_lt());
+      const int pos = cnt[warp * a.n_exp + ex] + rank;
+      a.sorted[pos] = i;
+      a.inverse[i] = pos;
+      __syncwarp(act);
+      if (rank == 0) cnt[warp * a.n_exp + ex] += __popc(peers);
+    }
+    __syncwarp();
+  }
+}
+
+// ---------------------------------------------------------------- launch
+
+cudaError_t launch_router_logits(const void* X, bool x_is_f32, const uint16_t* Wr, int T, int E,
+                                 int H, float* logits, cudaStream_t st) {
+  if (T <= 0) return cudaSuccess;
+  const int threads = 256;
+  if (T <= 8) {
+    const long groups = (long)T * E;
+    const int blocks = (int)((groups * 8 + threads - 1) / threads);
+    if (x_is_f32)
+      k_router_logits<float, 1, 1><<<blocks, threads, 0, st>>>((const float*)X, Wr, T, E, H, logits);
+    else
+      k_router_logits<__nv_bfloat16, 1, 1>
+          <<<blocks, threads, 0, st>>>((const __nv_bfloat16*)X, Wr, T, E, H, logits);
+  } else {
+    constexpr int TW = 4, EW = 4;
+    const long groups = (long)((T + TW - 1) / TW) * ((E + EW - 1) / EW);
+    const int blocks = (int)((groups * 8 + threads - 1) / threads);
+    if (x_is_f32)
+      k_router_logits<float, TW, EW>
+          <<<blocks, threads, 0, st>>>((const float*)X, Wr, T, E, H, logits);
+    else
+      k_router_logits<__nv_bfloat16, TW, EW>
+          <<<blocks, threads, 0, st>>>((const __nv_bfloat16*)X, Wr, T, E, H, logits);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_topk(const TopkArgs& a, cudaStream_t st) {
+  if (a.T <= 0) return cudaSuccess;
+  const size_t smem = (size_t)8 * 2 * a.E * sizeof(float);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(k_topk, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  k_topk<<<(a.T + 7) / 8, 256, smem, st>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_permute(const PermArgs& a, cudaStream_t st) {
+  const size_t smem = (size_t)kPermWarps * a.n_exp * sizeof(int);
+  cudaError_t e = cudaFuncSetAttribute(k_permute, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+  if (e != cudaSuccess) return e;
+  k_permute<<<1, kPermThreads, smem, st>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace llmoc

@@ -1,0 +1,1042 @@
+// runtime.cu — host side of the C ABI (include/llmoc_b200.h).
+//
+// Mirrors the reference's hal::cuda process-global backend
+// (src/hal/cuda_backend.cpp:155 mutex, :604-688 INT4 residency keyed by the
+// host qweight pointer with an LRU under a VRAM budget, :2692 try_gemm_int4,
+// :5217 try_moe_ffn_int4) on top of this library's kernels, and adds the
+// device-resident batched MoE layer (llmoc_moe_*).  No CPU fallback exists:
+// when the GPU path cannot run, the try_* calls return 0 and the batched
+// calls return an error status.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <array>
+#include <cmath>
+#include <atomic>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/llmoc_b200.h"
+#include "kernels.cuh"
+
+
+using namespace llmoc;
+
+namespace {
+
+// ------------------------------------------------------------------ state
+
+std::atomic<uint64_t> g_launches{0};
+thread_local std::string t_err;
+std::mutex g_mu;  // serialises the process-global backend, like the reference's g_mu
+bool g_probed = false, g_available = false, g_enabled = false;
+int g_ndev = 0;
+std::string g_status = "not probed";
+size_t g_budget = 0, g_used = 0;
+uint64_t g_tick = 0;
+cudaStream_t g_stream = nullptr;
+
+constexpr int kMaxExperts = kMaxExpPerm - 1;  // routed experts per layer (+1 shared) in the permutation CTA
+constexpr int kMaxTopk = 64;      // qwen3_6_moe_int4_model.cpp:384
+
+int fail(const std::string& msg) {
+  t_err = msg;
+  return 0;
+}
+llmoc_status fails(llmoc_status s, const std::string& msg) {
+  t_err = msg;
+  return s;
+}
+bool cuda_ok(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return true;
+  t_err = std::string(what) + ": " + cudaGetErrorString(e);
+  return false;
+}
+void count_launch(int n = 1) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
+
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+// Geometry of one repacked projection.
+struct Geo {
+  int M = 0, K = 0, gs = 0, ng = 0, Kc = 0, Mt = 0;
+  size_t qbytes = 0, sbytes = 0, zbytes = 0;
+  size_t total() const { return align256(qbytes) + align256(sbytes) + align256(zbytes); }
+};
+Geo make_geo(int M, int K, int gs, bool zeros) {
+  Geo g;
+  g.M = M;
+  g.K = K;
+  g.gs = gs;
+  g.ng = (K + gs - 1) / gs;
+  g.Kc = (K + 63) / 64;
+  g.Mt = (M + 15) / 16;
+  g.qbytes = (size_t)g.Mt * g.Kc * 512;
+  g.sbytes = (size_t)g.Mt * g.ng * 16 * 2;
+  g.zbytes = zeros ? g.sbytes : 0;
+  return g;
+}
+
+// Shapes the kernels accept: K a multiple of 32, group size a multiple of 32.
+bool shape_ok(int M, int K, int gs, std::string* why) {
+  if (M <= 0 || K <= 0 || gs <= 0) {
+    *why = "non-positive M/K/group_size";
+    return false;
+  }
+  if (K % 32 != 0 || gs % 32 != 0) {
+    *why = "K and group_size must be multiples of 32";
+    return false;
+  }
+  return true;
+}
+
+// Upload a QLWC projection (host or device source) into `dst` (repacked).
+bool repack_into(const llmoc_int4_view& W, bool src_on_device, const Geo& g, char* dst,
+                 cudaStream_t st, ProjDev* out) {
+  const bool awq = W.scheme == LLMOC_SCHEME_AWQ_SYM;
+  const size_t rb = (size_t)((W.K + 1) / 2);
+  const size_t qsrc = rb * W.M, ssrc = (size_t)W.M * g.ng * 2;
+  const uint8_t* q = W.qweight;
+  const uint16_t* s = W.scales;
+  const uint16_t* z = (!awq && W.zeros) ? W.zeros : nullptr;
+  void* staging = nullptr;
+  if (!src_on_device) {
+    const size_t need = align256(qsrc) + align256(ssrc) + (z ? align256(ssrc) : 0);
+    if (!cuda_ok(cudaMallocAsync(&staging, need, st), "cudaMallocAsync(staging)")) return false;
+    char* p = (char*)staging;
+    if (!cuda_ok(cudaMemcpyAsync(p, q, qsrc, cudaMemcpyHostToDevice, st), "H2D qweight")) return false;
+    q = (const uint8_t*)p;
+    p += align256(qsrc);
+    if (!cuda_ok(cudaMemcpyAsync(p, s, ssrc, cudaMemcpyHostToDevice, st), "H2D scales")) return false;
+    s = (const uint16_t*)p;
+    p += align256(ssrc);
+    if (z) {
+      if (!cuda_ok(cudaMemcpyAsync(p, z, ssrc, cudaMemcpyHostToDevice, st), "H2D zeros")) return false;
+      z = (const uint16_t*)p;
+    }
+  }
+  RepackArgs ra;
+  ra.q = q;
+  ra.s = s;
+  ra.z = z;
+  ra.M = W.M;
+  ra.K = W.K;
+  ra.gs = g.gs;
+  ra.ng = g.ng;
+  ra.Kc = g.Kc;
+  ra.qo = (uint32_t*)dst;
+  ra.so = (uint16_t*)(dst + align256(g.qbytes));
+  ra.zo = g.zbytes ? (uint16_t*)(dst + align256(g.qbytes) + align256(g.sbytes)) : nullptr;
+  const bool ok = cuda_ok(launch_repack(ra, st), "repack");
+  count_launch();
+  if (staging) cudaFreeAsync(staging, st);
+  out->q = (const uint4*)ra.qo;
+  out->s = (const __half*)ra.so;
+  out->z = (const __half*)ra.zo;
+  return ok;
+}
+
+// --------------------------------------------------- resident weight cache
+
+struct Resident {
+  char* buf = nullptr;
+  Geo geo;
+  ProjDev dev{};
+  ExpertDev* table = nullptr;  // 1-entry device table with gate = dev (dense GEMM)
+  int scheme = LLMOC_SCHEME_AWQ_SYM;
+  int zp = 7;
+  size_t bytes = 0;
+  bool pinned = false;
+  uint64_t last_use = 0;
+};
+std::unordered_map<const void*, Resident> g_cache;
+
+void free_resident(Resident& r) {
+  if (r.buf) cudaFree(r.buf);
+  if (r.table) cudaFree(r.table);
+  r.buf = nullptr;
+  r.table = nullptr;
+}
+
+int view_zp(const llmoc_int4_view& W) { return W.awq_zp > 0 ? W.awq_zp : 7; }
+
+// ensure_int4_resident (cuda_backend.cpp:604-688), caller holds g_mu.
+Resident* ensure_resident(const llmoc_int4_view* Wp) {
+  if (!g_enabled) {
+    t_err = "CUDA backend not enabled";
+    return nullptr;
+  }
+  if (!Wp || !Wp->qweight || !Wp->scales) {
+    t_err = "null INT4 view";
+    return nullptr;
+  }
+  const llmoc_int4_view& W = *Wp;
+  std::string why;
+  const int gs = W.group_size > 0 ? W.group_size : 128;
+  if (!shape_ok(W.M, W.K, gs, &why)) {
+    t_err = why;
+    return nullptr;
+  }
+  auto it = g_cache.find(W.qweight);
+  if (it != g_cache.end()) {
+    if (it->second.geo.M != W.M || it->second.geo.K != W.K) {
+      t_err = "resident weight shape mismatch for the same qweight pointer";
+      return nullptr;
+    }
+    it->second.last_use = ++g_tick;
+    return &it->second;
+  }
+  const bool awq = W.scheme == LLMOC_SCHEME_AWQ_SYM;
+  const Geo g = make_geo(W.M, W.K, gs, !awq && W.zeros);
+  const size_t total = g.total() + sizeof(ExpertDev);
+  if (g_budget > 0 && g_used + total > g_budget) {
+    std::vector<std::pair<uint64_t, const void*>> items;
+    for (auto& kv : g_cache)
+      if (!kv.second.pinned) items.push_back({kv.second.last_use, kv.first});
+    std::sort(items.begin(), items.end());
+    for (auto& p : items) {
+      if (g_used + total <= g_budget) break;
+      auto e = g_cache.find(p.second);
+      g_used -= e->second.bytes;
+      free_resident(e->second);
+      g_cache.erase(e);
+    }
+    if (g_used + total > g_budget) {
+      t_err = "VRAM budget exhausted";
+      return nullptr;
+    }
+  }
+  Resident r;
+  r.geo = g;
+  r.scheme = awq ? LLMOC_SCHEME_AWQ_SYM : LLMOC_SCHEME_GPTQ_ASYM;
+  r.zp = view_zp(W);
+  r.bytes = total;
+  if (!cuda_ok(cudaMalloc(&r.buf, g.total()), "cudaMalloc(weights)")) return nullptr;
+  if (!cuda_ok(cudaMalloc(&r.table, sizeof(ExpertDev)), "cudaMalloc(table)")) {
+    free_resident(r);
+    return nullptr;
+  }
+  if (!repack_into(W, false, g, r.buf, g_stream, &r.dev)) {
+    cudaStreamSynchronize(g_stream);
+    free_resident(r);
+    return nullptr;
+  }
+  ExpertDev ed;
+  ed.gate = ed.up = ed.down = r.dev;
+  if (!cuda_ok(cudaMemcpyAsync(r.table, &ed, sizeof ed, cudaMemcpyHostToDevice, g_stream),
+               "H2D table") ||
+      !cuda_ok(cudaStreamSynchronize(g_stream), "upload")) {
+    free_resident(r);
+    return nullptr;
+  }
+  r.last_use = ++g_tick;
+  g_used += total;
+  auto res = g_cache.emplace(W.qweight, r);
+  return &res.first->second;
+}
+
+// Growable device scratch for the host-pointer entry points.
+struct Scratch {
+  char* p = nullptr;
+  size_t cap = 0;
+  bool ensure(size_t n) {
+    if (n <= cap) return true;
+    if (p) cudaFree(p);
+    p = nullptr;
+    cap = 0;
+    if (!cuda_ok(cudaMalloc(&p, n), "cudaMalloc(scratch)")) return false;
+    cap = n;
+    return true;
+  }
+  void release() {
+    if (p) cudaFree(p);
+    p = nullptr;
+    cap = 0;
+  }
+} g_scratch;
+
+// Dense Y[n,M] = X[n,K] . W^T through the CUDA-core fp32 kernel; X, Y host.
+int dense_gemm_host(const float* X, int n, const llmoc_int4_view* W, float* Y) {
+  if (!X || !Y || n <= 0) return fail("bad arguments");
+  Resident* r = ensure_resident(W);
+  if (!r) return 0;
+  const Geo& g = r->geo;
+  const int nwork = (n + kChunkRows - 1) / kChunkRows;
+  const size_t xb = align256((size_t)n * g.K * 4), yb = align256((size_t)n * g.M * 4);
+  const size_t wb = align256((size_t)nwork * sizeof(WorkItem) + 16);
+  if (!g_scratch.ensure(xb + yb + wb)) return 0;
+  char* p = g_scratch.p;
+  float* dX = (float*)p;
+  float* dY = (float*)(p + xb);
+  WorkItem* dW = (WorkItem*)(p + xb + yb);
+  int* dN = (int*)(dW + nwork);
+  std::vector<WorkItem> work(nwork);
+  for (int i = 0; i < nwork; ++i) work[i] = WorkItem{0, i * kChunkRows, std::min(kChunkRows, n - i * kChunkRows), 0};
+  cudaStream_t st = g_stream;
+  if (!cuda_ok(cudaMemcpyAsync(dX, X, (size_t)n * g.K * 4, cudaMemcpyHostToDevice, st), "H2D x") ||
+      !cuda_ok(cudaMemcpyAsync(dW, work.data(), nwork * sizeof(WorkItem), cudaMemcpyHostToDevice, st), "H2D work") ||
+      !cuda_ok(cudaMemcpyAsync(dN, &nwork, sizeof(int), cudaMemcpyHostToDevice, st), "H2D n"))
+    return 0;
+  GemmArgs a{};
+  a.experts = r->table;
+  a.proj = 0;
+  a.M = g.M;
+  a.K = g.K;
+  a.Kc = g.Kc;
+  a.gs = g.gs;
+  a.ng = g.ng;
+  a.zp = r->zp;
+  a.B = dX;
+  a.ldb = g.K;
+  a.gather = nullptr;
+  a.kk = 1;
+  a.work = dW;
+  a.n_work = dN;
+  a.out = dY;
+  a.ldo = g.M;
+  if (!cuda_ok(launch_gemm(MODE_PLAIN_F32, 1, a, nwork, r->scheme == LLMOC_SCHEME_AWQ_SYM, 1, st),
+               "gemm launch"))
+    return 0;
+  count_launch();
+  if (!cuda_ok(cudaMemcpyAsync(Y, dY, (size_t)n * g.M * 4, cudaMemcpyDeviceToHost, st), "D2H y") ||
+      !cuda_ok(cudaStreamSynchronize(st), "gemm"))
+    return 0;
+  return 1;
+}
+
+}  // namespace
+
+// =================================================================== layer
+
+struct llmoc_moe_layer {
+  llmoc_moe_layer_desc d{};
+  int device = 0;
+  int n_exp = 0;  // routed + shared
+  int kk = 0;     // slots per token
+  Geo gu, dn;     // gate/up [I,H] and down [H,I] geometry
+  char* arena = nullptr;
+  size_t weight_bytes = 0;    // packed q + scales (+zeros), as streamed
+  ExpertDev* table = nullptr; // device [n_exp]
+  std::vector<ExpertDev> htable;
+  uint16_t* router_w = nullptr;
+  float* bias = nullptr;
+  // stage timing (llmoc_moe_set_stage_timing): 7 events per timed call
+  bool timing = false;
+  std::vector<cudaEvent_t> ev_pool;
+  std::vector<std::array<cudaEvent_t, 7>> ev_calls;
+};
+
+namespace {
+
+struct WsLayout {
+  size_t logits, ids, weights, offsets, sorted, inverse, work, n_work, n_active, mid, partial, total;
+  int max_work;
+};
+
+WsLayout ws_layout(const llmoc_moe_layer* L, int T) {
+  WsLayout w{};
+  const size_t n = (size_t)T * L->kk;
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = o;
+    o += align256(bytes);
+    return at;
+  };
+  w.max_work = (int)(std::min<size_t>((size_t)L->n_exp, n) + (n + kChunkRows - 1) / kChunkRows);
+  w.logits = take((size_t)T * L->d.n_experts * 4);
+  w.ids = take(n * 4);
+  w.weights = take(n * 4);
+  w.offsets = take((size_t)(L->n_exp + 1) * 4);
+  w.sorted = take(n * 4);
+  w.inverse = take(n * 4);
+  w.work = take((size_t)std::max(1, w.max_work) * sizeof(WorkItem));
+  w.n_work = take(4);
+  w.n_active = take(4);
+  w.mid = take(n * L->d.inter * 2);
+  w.partial = take(n * L->d.hidden * 4);
+  w.total = o;
+  return w;
+}
+
+llmoc_status validate_desc(const llmoc_moe_layer_desc* d) {
+  if (!d) return fails(LLMOC_ERR_INVALID, "null layer desc");
+  if (d->hidden <= 0 || d->inter <= 0 || d->n_experts <= 0 || d->topk <= 0)
+    return fails(LLMOC_ERR_INVALID, "non-positive layer dimension");
+  if (d->topk > kMaxTopk || d->topk > d->n_experts)
+    return fails(LLMOC_ERR_INVALID, "topk must be <= 64 and <= n_experts");
+  if (d->n_experts > kMaxExperts)
+    return fails(LLMOC_ERR_UNSUPPORTED, "more than 511 routed experts per layer");
+  if (d->router != LLMOC_ROUTER_SOFTMAX && d->router != LLMOC_ROUTER_SIGMOID_BIAS)
+    return fails(LLMOC_ERR_INVALID, "unknown router");
+  if (d->scheme != LLMOC_SCHEME_AWQ_SYM && d->scheme != LLMOC_SCHEME_GPTQ_ASYM)
+    return fails(LLMOC_ERR_INVALID, "unknown INT4 scheme");
+  std::string why;
+  if (!shape_ok(d->inter, d->hidden, d->group_size, &why) ||
+      !shape_ok(d->hidden, d->inter, d->group_size, &why))
+    return fails(LLMOC_ERR_UNSUPPORTED, why);
+  if (d->hidden % 8 != 0) return fails(LLMOC_ERR_UNSUPPORTED, "hidden must be a multiple of 8");
+  return LLMOC_OK;
+}
+
+bool view_matches(const llmoc_int4_view& v, int M, int K, const llmoc_moe_layer_desc* d) {
+  const int gs = v.group_size > 0 ? v.group_size : 128;
+  const int scheme = v.scheme == LLMOC_SCHEME_AWQ_SYM ? LLMOC_SCHEME_AWQ_SYM : LLMOC_SCHEME_GPTQ_ASYM;
+  return v.qweight && v.scales && v.M == M && v.K == K && gs == d->group_size && scheme == d->scheme &&
+         (scheme == LLMOC_SCHEME_AWQ_SYM || v.zeros);
+}
+
+llmoc_status layer_create(const llmoc_moe_layer_desc* d, const uint16_t* router_w, const float* bias,
+                          const llmoc_int4_view* experts, const llmoc_int4_view* shared, int device,
+                          bool on_device, llmoc_moe_layer** out) {
+  if (!out) return fails(LLMOC_ERR_INVALID, "null out");
+  *out = nullptr;
+  llmoc_status s = validate_desc(d);
+  if (s != LLMOC_OK) return s;
+  if (!router_w || !experts) return fails(LLMOC_ERR_INVALID, "null router or experts");
+  if (d->router == LLMOC_ROUTER_SIGMOID_BIAS && !bias)
+    return fails(LLMOC_ERR_INVALID, "sigmoid router needs a bias");
+  if (d->has_shared && !shared) return fails(LLMOC_ERR_INVALID, "has_shared without shared views");
+  const int E = d->n_experts, H = d->hidden, I = d->inter;
+  const int n_exp = E + (d->has_shared ? 1 : 0);
+  for (int e = 0; e < n_exp; ++e) {
+    const llmoc_int4_view* v = e < E ? experts + 3 * e : shared;
+    if (!view_matches(v[0], I, H, d) || !view_matches(v[1], I, H, d) || !view_matches(v[2], H, I, d))
+      return fails(LLMOC_ERR_INVALID, "expert " + std::to_string(e) + " view does not match the layer");
+  }
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev)
+    return fails(LLMOC_ERR_NO_DEVICE, "no such CUDA device");
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(device);
+  auto* L = new llmoc_moe_layer();
+  L->d = *d;
+  if (L->d.awq_zp <= 0) L->d.awq_zp = 7;
+  L->device = device;
+  L->n_exp = n_exp;
+  L->kk = d->topk + (d->has_shared ? 1 : 0);
+  const bool z = d->scheme == LLMOC_SCHEME_GPTQ_ASYM;
+  L->gu = make_geo(I, H, d->group_size, z);
+  L->dn = make_geo(H, I, d->group_size, z);
+  const size_t per_exp = 2 * L->gu.total() + L->dn.total();
+  L->weight_bytes = (size_t)n_exp * (2 * (L->gu.qbytes + L->gu.sbytes + L->gu.zbytes) +
+                                     (L->dn.qbytes + L->dn.sbytes + L->dn.zbytes));
+  cudaStream_t st = nullptr;
+  llmoc_status rc = LLMOC_OK;
+  auto bail = [&](llmoc_status code, const std::string& msg) {
+    rc = fails(code, msg);
+    return rc;
+  };
+  do {
+    if (cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) != cudaSuccess) {
+      bail(LLMOC_ERR_CUDA, "stream create");
+      break;
+    }
+    if (cudaMalloc(&L->arena, per_exp * n_exp) != cudaSuccess) {
+      bail(LLMOC_ERR_NO_MEMORY, "cudaMalloc(expert arena) failed");
+      break;
+    }
+    if (cudaMalloc(&L->table, sizeof(ExpertDev) * n_exp) != cudaSuccess ||
+        cudaMalloc(&L->router_w, (size_t)E * H * 2) != cudaSuccess) {
+      bail(LLMOC_ERR_NO_MEMORY, "cudaMalloc(router/table) failed");
+      break;
+    }
+    if (bias && cudaMalloc(&L->bias, (size_t)E * 4) != cudaSuccess) {
+      bail(LLMOC_ERR_NO_MEMORY, "cudaMalloc(bias) failed");
+      break;
+    }
+    const cudaMemcpyKind kind = on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+    if (cudaMemcpyAsync(L->router_w, router_w, (size_t)E * H * 2, kind, st) != cudaSuccess ||
+        (bias && cudaMemcpyAsync(L->bias, bias, (size_t)E * 4, kind, st) != cudaSuccess)) {
+      bail(LLMOC_ERR_CUDA, "router upload failed");
+      break;
+    }
+    L->htable.resize(n_exp);
+    char* p = L->arena;
+    for (int e = 0; e < n_exp && rc == LLMOC_OK; ++e) {
+      const llmoc_int4_view* v = e < E ? experts + 3 * e : shared;
+      ExpertDev& ed = L->htable[e];
+      if (!repack_into(v[0], on_device, L->gu, p, st, &ed.gate)) bail(LLMOC_ERR_CUDA, t_err);
+      p += L->gu.total();
+      if (rc == LLMOC_OK && !repack_into(v[1], on_device, L->gu, p, st, &ed.up)) bail(LLMOC_ERR_CUDA, t_err);
+      p += L->gu.total();
+      if (rc == LLMOC_OK && !repack_into(v[2], on_device, L->dn, p, st, &ed.down)) bail(LLMOC_ERR_CUDA, t_err);
+      p += L->dn.total();
+    }
+    if (rc != LLMOC_OK) break;
+    if (cudaMemcpyAsync(L->table, L->htable.data(), sizeof(ExpertDev) * n_exp,
+                        cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess) {
+      bail(LLMOC_ERR_CUDA, std::string("layer upload: ") + cudaGetErrorString(cudaGetLastError()));
+      break;
+    }
+  } while (false);
+  if (st) {
+    cudaStreamSynchronize(st);
+    cudaStreamDestroy(st);
+  }
+  cudaSetDevice(prev);
+  if (rc != LLMOC_OK) {
+    llmoc_moe_layer_destroy(L);
+    return rc;
+  }
+  *out = L;
+  return LLMOC_OK;
+}
+
+struct DevGuard {
+  int prev = -1;
+  explicit DevGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+    else prev = -1;
+  }
+  ~DevGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+// Event recorder for one timed forward (no-op when timing is off).
+struct StageEvents {
+  llmoc_moe_layer* L = nullptr;
+  std::array<cudaEvent_t, 7> ev{};
+  int next = 0;
+  StageEvents(const llmoc_moe_layer* layer) {
+    if (!layer->timing) return;
+    L = const_cast<llmoc_moe_layer*>(layer);
+    for (auto& e : ev) {
+      if (!L->ev_pool.empty()) {
+        e = L->ev_pool.back();
+        L->ev_pool.pop_back();
+      } else if (cudaEventCreate(&e) != cudaSuccess) {
+        e = nullptr;
+      }
+    }
+  }
+  void mark(cudaStream_t st) {
+    if (L && next < 7 && ev[next]) cudaEventRecord(ev[next], st);
+    ++next;
+  }
+  void commit() {
+    if (L && next == 7) {
+      L->ev_calls.push_back(ev);
+      L = nullptr;
+    }
+  }
+  ~StageEvents() {
+    if (L)
+      for (auto e : ev)
+        if (e) L->ev_pool.push_back(e);
+  }
+};
+
+llmoc_status run_route(const llmoc_moe_layer* L, const uint16_t* X, int T, const WsLayout& w,
+                       char* ws, cudaStream_t st, StageEvents* se = nullptr) {
+  const int E = L->d.n_experts, H = L->d.hidden;
+  float* logits = (float*)(ws + w.logits);
+  if (se) se->mark(st);
+  if (!cuda_ok(launch_router_logits(X, false, L->router_w, T, E, H, logits, st), "router"))
+    return LLMOC_ERR_CUDA;
+  if (se) se->mark(st);
+  TopkArgs ta{};
+  ta.logits = logits;
+  ta.bias = L->bias;
+  ta.T = T;
+  ta.E = E;
+  ta.k = L->d.topk;
+  ta.kk = L->kk;
+  ta.router = L->d.router;
+  ta.routed_scaling = L->d.routed_scaling;
+  ta.shared_scale = L->d.shared_scale;
+  ta.has_shared = L->d.has_shared;
+  ta.ids = (int*)(ws + w.ids);
+  ta.weights = (float*)(ws + w.weights);
+  if (!cuda_ok(launch_topk(ta, st), "topk")) return LLMOC_ERR_CUDA;
+  if (se) se->mark(st);
+  PermArgs pa{};
+  pa.ids = ta.ids;
+  pa.n = T * L->kk;
+  pa.n_exp = L->n_exp;
+  pa.offsets = (int*)(ws + w.offsets);
+  pa.sorted = (int*)(ws + w.sorted);
+  pa.inverse = (int*)(ws + w.inverse);
+  pa.work = (WorkItem*)(ws + w.work);
+  pa.n_work = (int*)(ws + w.n_work);
+  pa.n_active = (int*)(ws + w.n_active);
+  if (!cuda_ok(launch_permute(pa, st), "permute")) return LLMOC_ERR_CUDA;
+  if (se) se->mark(st);
+  count_launch(3);
+  return LLMOC_OK;
+}
+
+}  // namespace
+
+// ===================================================================== ABI
+
+extern "C" {
+
+int llmoc_cuda_probe_available(void) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_probed) return g_available;
+  g_probed = true;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    g_status = "no CUDA device";
+    return 0;
+  }
+  cudaDeviceProp p{};
+  if (cudaGetDeviceProperties(&p, 0) != cudaSuccess || p.major != 10) {
+    g_status = "device 0 is not sm_100 (B200)";
+    return 0;
+  }
+  g_ndev = n;
+  g_available = true;
+  g_status = std::string("available: ") + p.name;
+  return 1;
+}
+
+int llmoc_cuda_enabled(void) { return g_enabled ? 1 : 0; }
+const char* llmoc_cuda_status(void) { return g_status.c_str(); }
+int llmoc_cuda_device_count(void) {
+  llmoc_cuda_probe_available();
+  return g_ndev;
+}
+
+int llmoc_cuda_enable(size_t vram_budget_bytes) {
+  if (!llmoc_cuda_probe_available()) return fail(g_status);
+  std::lock_guard<std::mutex> lk(g_mu);
+  g_budget = vram_budget_bytes;
+  if (g_enabled) return 1;
+  if (!cuda_ok(cudaStreamCreateWithFlags(&g_stream, cudaStreamNonBlocking), "stream create"))
+    return 0;
+  g_enabled = true;
+  g_status = "enabled";
+  return 1;
+}
+
+void llmoc_cuda_disable(void) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_enabled) return;
+  cudaStreamSynchronize(g_stream);
+  for (auto& kv : g_cache) free_resident(kv.second);
+  g_cache.clear();
+  g_used = 0;
+  g_scratch.release();
+  cudaStreamDestroy(g_stream);
+  g_stream = nullptr;
+  g_enabled = false;
+  g_status = "disabled";
+}
+
+size_t llmoc_cuda_vram_used(void) { return g_used; }
+size_t llmoc_cuda_vram_budget(void) { return g_budget; }
+void llmoc_cuda_set_vram_budget(size_t bytes) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  g_budget = bytes;
+}
+int llmoc_cuda_device_mem_info(size_t* free_bytes, size_t* total_bytes) {
+  size_t f = 0, t = 0;
+  if (cudaMemGetInfo(&f, &t) != cudaSuccess) {
+    cudaGetLastError();
+    return fail("cudaMemGetInfo failed");
+  }
+  if (free_bytes) *free_bytes = f;
+  if (total_bytes) *total_bytes = t;
+  return 1;
+}
+int llmoc_cuda_host_register(void* ptr, size_t bytes) {
+  if (!ptr || !bytes) return fail("bad arguments");
+  return cuda_ok(cudaHostRegister(ptr, bytes, cudaHostRegisterPortable), "cudaHostRegister") ? 1 : 0;
+}
+int llmoc_cuda_host_unregister(void* ptr) {
+  if (!ptr) return fail("bad arguments");
+  return cuda_ok(cudaHostUnregister(ptr), "cudaHostUnregister") ? 1 : 0;
+}
+const char* llmoc_last_error(void) { return t_err.c_str(); }
+
+int llmoc_try_gemm_int4(const float* x, const llmoc_int4_view* W, float* y) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  return dense_gemm_host(x, 1, W, y);
+}
+
+int llmoc_try_gemm_int4_batch(const float* X, int n, const llmoc_int4_view* W, float* Y) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  return dense_gemm_host(X, n, W, Y);
+}
+
+int llmoc_try_gemm_int4_multi(const float* x, const llmoc_int4_view* const* Ws, float* const* ys,
+                              int n) {
+  if (!Ws || !ys || n < 1 || n > 4) return fail("try_gemm_int4_multi takes 1..4 weights");
+  std::lock_guard<std::mutex> lk(g_mu);
+  for (int i = 0; i < n; ++i)
+    if (!Ws[i] || Ws[i]->K != Ws[0]->K) return fail("weights must share K");
+  for (int i = 0; i < n; ++i)
+    if (!dense_gemm_host(x, 1, Ws[i], ys[i])) return 0;
+  return 1;
+}
+
+int llmoc_try_gemm_int4_batch_multi(const float* X, int n, const llmoc_int4_view* const* Ws,
+                                    float* const* Ys, int nW) {
+  if (!Ws || !Ys || nW < 1 || nW > 4) return fail("try_gemm_int4_batch_multi takes 1..4 weights");
+  std::lock_guard<std::mutex> lk(g_mu);
+  for (int i = 0; i < nW; ++i)
+    if (!dense_gemm_host(X, n, Ws[i], Ys[i])) return 0;
+  return 1;
+}
+
+int llmoc_prefetch_int4_weight(const llmoc_int4_view* W) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  return ensure_resident(W) ? 1 : 0;
+}
+
+int llmoc_pin_int4_weight(const llmoc_int4_view* W) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  Resident* r = ensure_resident(W);
+  if (!r) return 0;
+  r->pinned = true;
+  return 1;
+}
+
+int llmoc_try_dequant_int4_matrix(const llmoc_int4_view* W, float* out) {
+  if (!out) return fail("null out");
+  std::lock_guard<std::mutex> lk(g_mu);
+  Resident* r = ensure_resident(W);
+  if (!r) return 0;
+  const size_t bytes = (size_t)r->geo.M * r->geo.K * 4;
+  if (!g_scratch.ensure(bytes)) return 0;
+  if (!cuda_ok(launch_dequant(r->dev, r->geo.M, r->geo.K, r->geo.gs,
+                              r->scheme == LLMOC_SCHEME_AWQ_SYM, r->zp, (float*)g_scratch.p, g_stream),
+               "dequant"))
+    return 0;
+  count_launch();
+  if (!cuda_ok(cudaMemcpyAsync(out, g_scratch.p, bytes, cudaMemcpyDeviceToHost, g_stream), "D2H") ||
+      !cuda_ok(cudaStreamSynchronize(g_stream), "dequant"))
+    return 0;
+  return 1;
+}
+
+int llmoc_try_moe_ffn_int4(const float* x, int H, int I, const llmoc_moe_expert_int4* experts,
+                           int n_experts, const llmoc_int4_view* shared_gate,
+                           const llmoc_int4_view* shared_up, const llmoc_int4_view* shared_down,
+                           float shared_scale, float* y) {
+  if (!x || !y || !experts || n_experts <= 0 || H <= 0 || I <= 0) return fail("bad arguments");
+  if (n_experts > 64) return fail("n_experts > 64");
+  const bool has_shared = shared_gate && shared_up && shared_down && shared_gate->qweight &&
+                          shared_up->qweight && shared_down->qweight && std::fabs(shared_scale) > 0.f;
+  auto dims_ok = [&](const llmoc_int4_view* g, const llmoc_int4_view* u, const llmoc_int4_view* d) {
+    return g && u && d && g->qweight && u->qweight && d->qweight && g->M == I && u->M == I &&
+           d->M == H && g->K == H && u->K == H && d->K == I;
+  };
+  if (has_shared && !dims_ok(shared_gate, shared_up, shared_down))
+    return fail("shared expert dims must be (I, H)");
+  for (int i = 0; i < n_experts; ++i)
+    if (!dims_ok(experts[i].gate, experts[i].up, experts[i].down)) return fail("expert dims mismatch");
+
+  std::lock_guard<std::mutex> lk(g_mu);
+  // pairs: experts with |w| >= 1e-12 (cuda_backend.cpp:5284), then the shared one
+  std::vector<ExpertDev> tab;
+  std::vector<float> wts;
+  int scheme = -1, zp = 7, gs = 0;
+  auto add = [&](const llmoc_int4_view* g, const llmoc_int4_view* u, const llmoc_int4_view* d,
+                 float w) -> bool {
+    Resident* rg = ensure_resident(g);
+    Resident* ru = rg ? ensure_resident(u) : nullptr;
+    Resident* rd = ru ? ensure_resident(d) : nullptr;
+    if (!rd) return false;
+    for (Resident* r : {rg, ru, rd}) {
+      if (scheme < 0) {
+        scheme = r->scheme;
+        zp = r->zp;
+        gs = r->geo.gs;
+      } else if (r->scheme != scheme || r->zp != zp || r->geo.gs != gs) {
+        t_err = "experts must share scheme, zero point and group size";
+        return false;
+      }
+    }
+    tab.push_back(ExpertDev{rg->dev, ru->dev, rd->dev});
+    wts.push_back(w);
+    return true;
+  };
+  for (int i = 0; i < n_experts; ++i) {
+    if (std::fabs(experts[i].weight) < 1e-12f) continue;
+    if (!add(experts[i].gate, experts[i].up, experts[i].down, experts[i].weight)) return 0;
+  }
+  if (has_shared && !add(shared_gate, shared_up, shared_down, shared_scale)) return 0;
+  const int n = (int)tab.size();
+  if (n == 0) {
+    std::fill(y, y + H, 0.f);
+    return 1;
+  }
+  const Geo gu = make_geo(I, H, gs, false), dn = make_geo(H, I, gs, false);
+  // scratch: table | work | n_work | zeros(gather) | x | weights | inverse | mid | partial | y
+  size_t o = 0;
+  auto take = [&](size_t b) {
+    size_t at = o;
+    o += align256(b);
+    return at;
+  };
+  const size_t o_tab = take(sizeof(ExpertDev) * n), o_work = take(sizeof(WorkItem) * n),
+               o_nw = take(4), o_gat = take(4 * n), o_x = take((size_t)H * 4), o_w = take(4 * n),
+               o_inv = take(4 * n), o_mid = take((size_t)n * I * 4), o_part = take((size_t)n * H * 4),
+               o_y = take((size_t)H * 4);
+  if (!g_scratch.ensure(o)) return 0;
+  char* s = g_scratch.p;
+  // host staging of the small tables in one pageable block, copied in order
+  std::vector<char> host(o_x);
+  memcpy(host.data() + o_tab, tab.data(), sizeof(ExpertDev) * n);
+  WorkItem* wk = (WorkItem*)(host.data() + o_work);
+  int* gat = (int*)(host.data() + o_gat);
+  for (int i = 0; i < n; ++i) {
+    wk[i] = WorkItem{i, i, 1, 0};
+    gat[i] = 0;
+  }
+  memcpy(host.data() + o_nw, &n, 4);
+  std::vector<int> inv(n);
+  for (int i = 0; i < n; ++i) inv[i] = i;
+  cudaStream_t st = g_stream;
+  if (!cuda_ok(cudaMemcpyAsync(s, host.data(), o_x, cudaMemcpyHostToDevice, st), "H2D tables") ||
+      !cuda_ok(cudaMemcpyAsync(s + o_x, x, (size_t)H * 4, cudaMemcpyHostToDevice, st), "H2D x") ||
+      !cuda_ok(cudaMemcpyAsync(s + o_w, wts.data(), 4 * n, cudaMemcpyHostToDevice, st), "H2D w") ||
+      !cuda_ok(cudaMemcpyAsync(s + o_inv, inv.data(), 4 * n, cudaMemcpyHostToDevice, st), "H2D inv"))
+    return 0;
+  GemmArgs a{};
+  a.experts = (const ExpertDev*)(s + o_tab);
+  a.M = I;
+  a.K = H;
+  a.Kc = gu.Kc;
+  a.gs = gs;
+  a.ng = gu.ng;
+  a.zp = zp;
+  a.B = s + o_x;
+  a.ldb = H;
+  a.gather = (const int*)(s + o_gat);
+  a.kk = 1;
+  a.work = (const WorkItem*)(s + o_work);
+  a.n_work = (const int*)(s + o_nw);
+  a.out = s + o_mid;
+  a.ldo = I;
+  a.out_bf16 = 0;
+  const int awq = scheme == LLMOC_SCHEME_AWQ_SYM;
+  if (!cuda_ok(launch_gemm(MODE_GATE_UP, 1, a, n, awq, 1, st), "gate/up")) return 0;
+  GemmArgs b = a;
+  b.proj = 2;
+  b.M = H;
+  b.K = I;
+  b.Kc = dn.Kc;
+  b.ng = dn.ng;
+  b.B = s + o_mid;
+  b.ldb = I;
+  b.gather = nullptr;
+  b.out = s + o_part;
+  b.ldo = H;
+  if (!cuda_ok(launch_gemm(MODE_PLAIN_F32, 1, b, n, awq, 1, st), "down")) return 0;
+  if (!cuda_ok(launch_combine((const float*)(s + o_part), (const int*)(s + o_inv),
+                              (const float*)(s + o_w), 1, n, H, s + o_y, 0, 0, st),
+               "combine"))
+    return 0;
+  count_launch(3);
+  if (!cuda_ok(cudaMemcpyAsync(y, s + o_y, (size_t)H * 4, cudaMemcpyDeviceToHost, st), "D2H y") ||
+      !cuda_ok(cudaStreamSynchronize(st), "moe ffn"))
+    return 0;
+  return 1;
+}
+
+// ------------------------------------------------------------- layer API
+
+llmoc_status llmoc_moe_layer_create(const llmoc_moe_layer_desc* desc, const uint16_t* router_w,
+                                    const float* bias, const llmoc_int4_view* experts,
+                                    const llmoc_int4_view* shared, int device,
+                                    llmoc_moe_layer** out) {
+  return layer_create(desc, router_w, bias, experts, shared, device, false, out);
+}
+
+llmoc_status llmoc_moe_layer_create_device(const llmoc_moe_layer_desc* desc,
+                                           const uint16_t* router_w, const float* bias,
+                                           const llmoc_int4_view* experts,
+                                           const llmoc_int4_view* shared, int device,
+                                           llmoc_moe_layer** out) {
+  return layer_create(desc, router_w, bias, experts, shared, device, true, out);
+}
+
+void llmoc_moe_layer_destroy(llmoc_moe_layer* L) {
+  if (!L) return;
+  DevGuard dg(L->device);
+  llmoc_moe_set_stage_timing(L, 0);
+  for (auto e : L->ev_pool) cudaEventDestroy(e);
+  if (L->arena) cudaFree(L->arena);
+  if (L->table) cudaFree(L->table);
+  if (L->router_w) cudaFree(L->router_w);
+  if (L->bias) cudaFree(L->bias);
+  delete L;
+}
+
+size_t llmoc_moe_layer_weight_bytes(const llmoc_moe_layer* L) { return L ? L->weight_bytes : 0; }
+
+size_t llmoc_expert_storage_bytes(int H, int I, int group_size, int has_zeros) {
+  // qlwc_expert_bytes.h:43-48: gate[IxH] + up[IxH] + down[HxI], q + fp16 scales (+zeros)
+  auto proj = [&](size_t M, size_t K) {
+    const size_t gs = group_size > 0 ? (size_t)group_size : 128;
+    const size_t ng = (K + gs - 1) / gs;
+    return M * ((K + 1) / 2) + M * ng * 2 * (has_zeros ? 2 : 1);
+  };
+  return 2 * proj((size_t)I, (size_t)H) + proj((size_t)H, (size_t)I);
+}
+
+size_t llmoc_moe_workspace_bytes(const llmoc_moe_layer* L, int max_tokens) {
+  if (!L || max_tokens < 0) return 0;
+  return ws_layout(L, max_tokens).total;
+}
+
+llmoc_status llmoc_moe_route_views(const llmoc_moe_layer* L, int T, void* workspace,
+                                   size_t workspace_bytes, llmoc_route_views* out) {
+  if (!L || !out || T < 0) return fails(LLMOC_ERR_INVALID, "bad arguments");
+  const WsLayout w = ws_layout(L, T);
+  if (!workspace || workspace_bytes < w.total) return fails(LLMOC_ERR_WORKSPACE, "workspace too small");
+  char* ws = (char*)workspace;
+  out->logits = (float*)(ws + w.logits);
+  out->ids = (int32_t*)(ws + w.ids);
+  out->weights = (float*)(ws + w.weights);
+  out->offsets = (int32_t*)(ws + w.offsets);
+  out->sorted = (int32_t*)(ws + w.sorted);
+  out->inverse = (int32_t*)(ws + w.inverse);
+  out->n_active = (int32_t*)(ws + w.n_active);
+  return LLMOC_OK;
+}
+
+llmoc_status llmoc_moe_route(const llmoc_moe_layer* L, const uint16_t* X, int T, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+  if (!L || T < 0 || (T > 0 && !X)) return fails(LLMOC_ERR_INVALID, "bad arguments");
+  if (T == 0) return LLMOC_OK;
+  const WsLayout w = ws_layout(L, T);
+  if (!workspace || workspace_bytes < w.total) return fails(LLMOC_ERR_WORKSPACE, "workspace too small");
+  DevGuard dg(L->device);
+  return run_route(L, X, T, w, (char*)workspace, (cudaStream_t)stream);
+}
+
+llmoc_status llmoc_moe_forward(const llmoc_moe_layer* L, const uint16_t* X, int T, uint16_t* Y,
+                               void* workspace, size_t workspace_bytes, void* stream) {
+  if (!L || T < 0 || (T > 0 && (!X || !Y))) return fails(LLMOC_ERR_INVALID, "bad arguments");
+  if (T == 0) return LLMOC_OK;
+  const WsLayout w = ws_layout(L, T);
+  if (!workspace || workspace_bytes < w.total) return fails(LLMOC_ERR_WORKSPACE, "workspace too small");
+  DevGuard dg(L->device);
+  cudaStream_t st = (cudaStream_t)stream;
+  char* ws = (char*)workspace;
+  StageEvents se(L);
+  llmoc_status rc = run_route(L, X, T, w, ws, st, &se);
+  if (rc != LLMOC_OK) return rc;
+  const int H = L->d.hidden, I = L->d.inter;
+  const bool awq = L->d.scheme == LLMOC_SCHEME_AWQ_SYM;
+  const int path = awq ? 0 : 2;
+  const int ntiles = T <= 8 ? 1 : 4;
+  GemmArgs a{};
+  a.experts = L->table;
+  a.M = I;
+  a.K = H;
+  a.Kc = L->gu.Kc;
+  a.gs = L->d.group_size;
+  a.ng = L->gu.ng;
+  a.zp = L->d.awq_zp;
+  a.B = X;
+  a.ldb = H;
+  a.gather = (const int*)(ws + w.sorted);
+  a.kk = L->kk;
+  a.work = (const WorkItem*)(ws + w.work);
+  a.n_work = (const int*)(ws + w.n_work);
+  a.out = ws + w.mid;
+  a.ldo = I;
+  a.out_bf16 = 1;
+  if (!cuda_ok(launch_gemm(MODE_GATE_UP, path, a, w.max_work, awq, ntiles, st), "gate/up"))
+    return LLMOC_ERR_CUDA;
+  se.mark(st);
+  GemmArgs b = a;
+  b.proj = 2;
+  b.M = H;
+  b.K = I;
+  b.Kc = L->dn.Kc;
+  b.ng = L->dn.ng;
+  b.B = ws + w.mid;
+  b.ldb = I;
+  b.gather = nullptr;
+  b.out = ws + w.partial;
+  b.ldo = H;
+  if (!cuda_ok(launch_gemm(MODE_PLAIN_F32, path, b, w.max_work, awq, ntiles, st), "down"))
+    return LLMOC_ERR_CUDA;
+  se.mark(st);
+  if (!cuda_ok(launch_combine((const float*)(ws + w.partial), (const int*)(ws + w.inverse),
+                              (const float*)(ws + w.weights), T, L->kk, H, Y, 1, 0, st),
+               "combine"))
+    return LLMOC_ERR_CUDA;
+  se.mark(st);
+  se.commit();
+  count_launch(3);
+  return LLMOC_OK;
+}
+
+llmoc_status llmoc_moe_dequant(const llmoc_moe_layer* L, int expert, int proj, float* out,
+                               void* stream) {
+  if (!L || !out || expert < 0 || expert >= L->n_exp || proj < 0 || proj > 2)
+    return fails(LLMOC_ERR_INVALID, "bad arguments");
+  DevGuard dg(L->device);
+  const ExpertDev& e = L->htable[expert];
+  const ProjDev& P = proj == 0 ? e.gate : (proj == 1 ? e.up : e.down);
+  const Geo& g = proj == 2 ? L->dn : L->gu;
+  if (!cuda_ok(launch_dequant(P, g.M, g.K, g.gs, L->d.scheme == LLMOC_SCHEME_AWQ_SYM, L->d.awq_zp,
+                              out, (cudaStream_t)stream),
+               "dequant"))
+    return LLMOC_ERR_CUDA;
+  count_launch();
+  return LLMOC_OK;
+}
+
+llmoc_status llmoc_quantize_awq_sym(const uint16_t* W, int M, int K, int group_size, int bf16_scale,
+                                    uint8_t* q, uint16_t* scales, void* stream) {
+  if (!W || !q || !scales || M <= 0 || K <= 0 || group_size <= 0 || K % group_size || group_size % 2)
+    return fails(LLMOC_ERR_INVALID, "bad arguments (K % group_size must be 0)");
+  if (!cuda_ok(launch_quant_awq_sym((const __nv_bfloat16*)W, M, K, group_size, bf16_scale, q,
+                                    (__half*)scales, (cudaStream_t)stream),
+               "quantize"))
+    return LLMOC_ERR_CUDA;
+  count_launch();
+  return LLMOC_OK;
+}
+
+llmoc_status llmoc_moe_set_stage_timing(llmoc_moe_layer* L, int enable) {
+  if (!L) return fails(LLMOC_ERR_INVALID, "null layer");
+  DevGuard dg(L->device);
+  for (auto& call : L->ev_calls) {
+    cudaEventSynchronize(call[6]);
+    for (auto e : call) L->ev_pool.push_back(e);
+  }
+  L->ev_calls.clear();
+  L->timing = enable != 0;
+  return LLMOC_OK;
+}
+
+llmoc_status llmoc_moe_stage_times(llmoc_moe_layer* L, float* ms, int* calls) {
+  if (!L || !ms) return fails(LLMOC_ERR_INVALID, "bad arguments");
+  DevGuard dg(L->device);
+  for (int i = 0; i < 6; ++i) ms[i] = 0.f;
+  for (auto& call : L->ev_calls) {
+    if (!cuda_ok(cudaEventSynchronize(call[6]), "stage events")) return LLMOC_ERR_CUDA;
+    for (int i = 0; i < 6; ++i) {
+      float t = 0.f;
+      if (!cuda_ok(cudaEventElapsedTime(&t, call[i], call[i + 1]), "stage elapsed"))
+        return LLMOC_ERR_CUDA;
+      ms[i] += t;
+    }
+  }
+  if (calls) *calls = (int)L->ev_calls.size();
+  for (auto& call : L->ev_calls)
+    for (auto e : call) L->ev_pool.push_back(e);
+  L->ev_calls.clear();
+  return LLMOC_OK;
+}
+
+uint64_t llmoc_kernel_launch_count(void) { return g_launches.load(); }
+
+}  // extern "C"

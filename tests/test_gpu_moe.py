@@ -1,0 +1,289 @@
+"""GPU parity: the CUDA path through the C ABI against the CPU oracle.
+
+Bars (north star): expert ids, permutation and dequantised weights bit-exact;
+router logits bit-exact (the ids depend on them); bf16 layer outputs within
+normwise max relative error 1e-2 and cosine >= 0.9999 of the fp32 oracle.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import llmoc_b200 as L
+import moe_gpu as G
+import orc
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module", autouse=True)
+def cuda_ready():
+    assert torch.cuda.is_available(), "gpu tests need a CUDA device"
+    assert L.lib.llmoc_cuda_probe_available() == 1, L.lib.llmoc_cuda_status()
+    assert L.lib.llmoc_cuda_enable(0) == 1
+    yield
+
+
+SMALL = {
+    "qwen_like": dict(H=512, I=256, E=32, topk=8, gs=128),
+    "glm_like_shared_sigmoid": dict(H=512, I=128, E=32, topk=8, gs=128, router=1, shared=True),
+    "kimi_like_gs32": dict(H=448, I=128, E=48, topk=8, gs=32, router=1, routed_scaling=2.827,
+                           shared=True),
+    "gptq_shared": dict(H=256, I=128, E=16, topk=4, gs=64, scheme=1, shared=True, shared_scale=0.75),
+    "odd_k_chunks": dict(H=288, I=96, E=12, topk=3, gs=32),
+}
+
+
+def build(oracle, name, seed, max_tokens):
+    rng = np.random.default_rng(seed)
+    layer = orc.make_layer(oracle, rng, **SMALL[name])
+    return G.DevLayer(layer, max_tokens), rng
+
+
+@pytest.mark.parametrize("name", list(SMALL))
+def test_dequant_bit_exact(oracle, name):
+    dl, _ = build(oracle, name, 1, 1)
+    h = dl.host
+    for e in (0, h.E - 1) + ((h.E,) if h.shared is not None else ()):
+        ex = h.experts[e] if e < h.E else h.shared
+        for p, w in enumerate((ex.gate, ex.up, ex.down)):
+            out = torch.empty((w.M, w.K), dtype=torch.float32, device="cuda")
+            dl.dev.dequant(e, p, out)
+            torch.cuda.synchronize()
+            got = out.cpu().numpy()
+            ref = oracle.dequant_matrix(w)
+            assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), (e, p)
+    dl.close()
+
+
+@pytest.mark.parametrize("gs,bf16_scale", [(32, True), (128, True), (128, False)])
+def test_device_quantizer_matches_reference_quantizer(oracle, gs, bf16_scale):
+    rng = np.random.default_rng(gs)
+    M, K = 96, 1024
+    W = orc.bf16_round(rng.standard_normal((M, K), dtype=np.float32) * np.float32(0.02))
+    W[3, :gs] = 0.0  # an all-zero group takes the 1e-8 floor
+    ref = oracle.quant_awq_sym(W, gs, bf16_scale)
+    q = torch.empty((M, K // 2), dtype=torch.uint8, device="cuda")
+    s = torch.empty((M, K // gs), dtype=torch.int16, device="cuda")
+    L.quantize_awq_sym(G.bf16_dev(W), M, K, gs, bf16_scale, q, s)
+    torch.cuda.synchronize()
+    assert np.array_equal(q.cpu().numpy(), ref.q)
+    assert np.array_equal(s.cpu().numpy().view(np.uint16), ref.scales)
+
+
+def check_routing(oracle, dl, X, v, sample=None):
+    """Logits, ids and weights of the tokens in `sample` (default: all) against
+    the oracle; the permutation of all tokens against the canonical order."""
+    h = dl.host
+    T = X.shape[0]
+    sample = range(T) if sample is None else sample
+    for t in sample:
+        ref_logits = oracle.gemm_bias_free(X[t], h.router_w)
+        assert np.array_equal(v["logits"][t].view(np.uint32), ref_logits.view(np.uint32)), t
+        if h.router == orc.ROUTER_SOFTMAX:
+            ids, w, _ = oracle.route_softmax(ref_logits, h.topk)
+        else:
+            ids, w = oracle.route_sigmoid_bias(ref_logits, h.bias, h.topk, h.routed_scaling)
+        assert np.array_equal(v["ids"][t, :h.topk], ids), t
+        np.testing.assert_allclose(v["weights"][t, :h.topk], w, rtol=2e-6, atol=0)
+        if h.shared is not None:
+            assert v["ids"][t, h.topk] == h.E
+            assert v["weights"][t, h.topk] == np.float32(h.shared_scale)
+    off, srt, inv = oracle.permute(v["ids"], dl.dev.n_exp)
+    assert np.array_equal(v["offsets"], off)
+    assert np.array_equal(v["sorted"], srt)
+    assert np.array_equal(v["inverse"], inv)
+    assert v["n_active"] == int(np.count_nonzero(np.diff(off)))
+
+
+@pytest.mark.parametrize("name", list(SMALL))
+@pytest.mark.parametrize("T", [1, 7, 64, 133])
+def test_routing_bit_exact(oracle, name, T):
+    dl, rng = build(oracle, name, 2, T)
+    X = orc.make_tokens(rng, T, dl.host.H)
+    v = dl.route(X)
+    check_routing(oracle, dl, X, v)
+    dl.close()
+
+
+@pytest.mark.parametrize("name", list(SMALL))
+@pytest.mark.parametrize("T", [1, 5, 40, 129])
+def test_layer_matches_oracle(oracle, name, T):
+    dl, rng = build(oracle, name, 3, T)
+    X = orc.make_tokens(rng, T, dl.host.H)
+    Y, ws_bytes = dl.forward(X)
+    Yref, ids, w, _ = oracle.moe_layer_forward(dl.host, X)
+    v = dl.views(T, ws_bytes)
+    assert np.array_equal(v["ids"][:, :dl.host.topk], ids)
+    mre, cos = G.quality(G.bf16_to_f32(Y), Yref)
+    assert mre <= G.MAX_REL and cos >= G.MIN_COS, (mre, cos)
+    for t in range(T):  # every token on its own, too
+        mre_t, cos_t = G.quality(G.bf16_to_f32(Y[t]), Yref[t])
+        assert mre_t <= 2 * G.MAX_REL and cos_t >= 0.999, (t, mre_t, cos_t)
+    dl.close()
+
+
+def test_zero_tokens_is_a_no_op(oracle):
+    dl, _ = build(oracle, "qwen_like", 4, 4)
+    assert L.lib.llmoc_moe_forward(dl.dev.handle, None, 0, None, None, 0, None) == 0
+    dl.close()
+
+
+def test_workspace_too_small_is_rejected(oracle):
+    dl, rng = build(oracle, "qwen_like", 5, 8)
+    X = G.bf16_dev(orc.make_tokens(rng, 8, dl.host.H))
+    Y = torch.empty((8, dl.host.H), dtype=torch.bfloat16, device="cuda")
+    st = L.lib.llmoc_moe_forward(dl.dev.handle, X.data_ptr(), 8, Y.data_ptr(), dl.ws.data_ptr(),
+                                 dl.dev.workspace_bytes(8) - 1, None)
+    assert st == 7
+    dl.close()
+
+
+def test_skewed_routing_hot_expert(oracle):
+    """Every token prefers the same few experts (one expert gets all T pairs):
+    exercises multi-chunk work items of one expert and empty experts."""
+    rng = np.random.default_rng(6)
+    layer = orc.make_layer(oracle, rng, H=512, I=256, E=32, topk=4, gs=128)
+    rw = orc.bits_to_f32(layer.router_w)
+    rw[:4] += 0.5  # a strong shared component towards experts 0..3
+    layer.router_w = orc.bf16_bits(rw)
+    T = 200
+    X = np.abs(orc.make_tokens(rng, T, 512))
+    dl = G.DevLayer(layer, T)
+    Y, ws_bytes = dl.forward(X)
+    v = dl.views(T, ws_bytes)
+    counts = np.diff(v["offsets"])
+    assert counts.max() == T and (counts == 0).sum() > 0
+    Yref, ids, _, _ = oracle.moe_layer_forward(layer, X)
+    assert np.array_equal(v["ids"], ids)
+    mre, cos = G.quality(G.bf16_to_f32(Y), Yref)
+    assert mre <= G.MAX_REL and cos >= G.MIN_COS, (mre, cos)
+    dl.close()
+
+
+def test_zero_weights_give_zero_output(oracle):
+    rng = np.random.default_rng(7)
+    layer = orc.make_layer(oracle, rng, H=256, I=128, E=8, topk=2, gs=64, wstd=0.0)
+    dl = G.DevLayer(layer, 3)
+    Y, _ = dl.forward(orc.make_tokens(rng, 3, 256))
+    assert float(Y.float().abs().max()) == 0.0
+    dl.close()
+
+
+# ------------------------------------------------------------- full sizes
+
+FULL = {
+    # Qwen3-30B-A3B layer
+    "qwen3_30b_a3b": dict(H=2048, I=768, E=128, topk=8, gs=128, n_real=16),
+    # GLM-4.5-Air layer (sigmoid + bias, shared expert)
+    "glm45_air": dict(H=4096, I=1408, E=128, topk=8, gs=128, router=1, shared=True, n_real=8),
+    # Kimi-K2 layer (gs 32, 384 experts, scaling 2.827, shared)
+    "kimi_k2": dict(H=7168, I=2048, E=384, topk=8, gs=32, router=1, routed_scaling=2.827,
+                    shared=True, n_real=4),
+}
+
+
+@pytest.mark.parametrize("name,T", [("qwen3_30b_a3b", 1), ("qwen3_30b_a3b", 8), ("qwen3_30b_a3b", 64),
+                                    ("qwen3_30b_a3b", 512), ("glm45_air", 64), ("kimi_k2", 64)])
+def test_full_size_layer(oracle, name, T):
+    """Full BASELINE shapes: routing bit-exact for every token; outputs checked
+    against the oracle on a sample of tokens (each token's output depends on
+    that token alone)."""
+    rng = np.random.default_rng(100 + T)
+    layer = orc.make_layer(oracle, rng, **FULL[name])
+    X = orc.make_tokens(rng, T, layer.H)
+    dl = G.DevLayer(layer, T)
+    Y, ws_bytes = dl.forward(X)
+    v = dl.views(T, ws_bytes)
+    sample = np.unique(np.linspace(0, T - 1, min(T, 8)).astype(int))
+    check_routing(oracle, dl, X, v, sample)
+    Yref, ids, _, _ = oracle.moe_layer_forward(layer, X[sample])
+    assert np.array_equal(v["ids"][sample, :layer.topk], ids)
+    mre, cos = G.quality(G.bf16_to_f32(Y[torch.as_tensor(sample, device="cuda")]), Yref)
+    assert mre <= G.MAX_REL and cos >= G.MIN_COS, (mre, cos)
+    dl.close()
+
+
+# ------------------------------------------- the reference's host-fp32 API
+
+def unit_case(name):
+    import make_golden as mg
+
+    g = np.load(f"{mg.HERE}/unit_cases.npz")
+    d = {k.split("/")[1]: g[k] for k in g.files if k.startswith(name + "/")}
+    sc = int(d["scheme"])
+    W = orc.Int4Weight(d["q"], d["s"], d.get("z"), int(d["M"]), int(d["K"]), int(d["gs"]), sc,
+                       7 if sc == 2 else 0)
+    return d, W
+
+
+@pytest.mark.parametrize("case", ["awq_scalar", "awq_gemv", "gptq_gemv"])
+def test_try_gemm_int4_reference_cases(case):
+    """GpuGemmMatchesCpuIfCuda / AwqGemvJitMatchesCpu / GptqGemvJitMatchesCpu
+    (tests/unit/test_int4_gemm.cpp:151-198, test_gpu_quant_gemm.cpp:130-245):
+    GPU vs the reference CPU result, rel 1e-3."""
+    d, W = unit_case(case)
+    y = np.full(W.M, -1e9, np.float32)
+    v = L.view_of(W)
+    assert L.lib.llmoc_try_gemm_int4(L.ptr(d["x"]), C.byref(v), L.ptr(y)) == 1, L.last_error()
+    assert np.all(np.abs(y - d["y"]) < 1e-3 * (1 + np.abs(d["y"])))
+    dq = np.empty((W.M, W.K), np.float32)
+    assert L.lib.llmoc_try_dequant_int4_matrix(C.byref(v), L.ptr(dq)) == 1
+    assert np.array_equal(dq.view(np.uint32), d["dq"].view(np.uint32))
+
+
+@pytest.mark.parametrize("case", ["awq_batch", "gptq_batch"])
+def test_try_gemm_int4_batch_reference_cases(case):
+    d, W = unit_case(case)
+    X = np.ascontiguousarray(d["X"])
+    Y = np.empty((X.shape[0], W.M), np.float32)
+    v = L.view_of(W)
+    assert L.lib.llmoc_try_gemm_int4_batch(L.ptr(X), X.shape[0], C.byref(v), L.ptr(Y)) == 1
+    assert np.all(np.abs(Y - d["Y"]) < 1e-3 * (1 + np.abs(d["Y"])))
+
+
+@pytest.mark.parametrize("M,K,gs,n,scheme", [(4096, 4096, 128, 1, 2), (11008, 4096, 128, 8, 2),
+                                             (768, 2048, 128, 64, 1), (2048, 7168, 32, 3, 2)])
+def test_try_gemm_int4_config1_shapes(oracle, M, K, gs, n, scheme):
+    rng = np.random.default_rng(M + n)
+    Wf = orc.bf16_round(rng.standard_normal((M, K), dtype=np.float32) * np.float32(0.02))
+    W = oracle.quant_awq_sym(Wf, gs, True) if scheme == 2 else oracle.quant_gptq_asym(Wf, gs)
+    X = rng.standard_normal((n, K), dtype=np.float32)
+    Y = np.empty((n, M), np.float32)
+    v = L.view_of(W)
+    assert L.lib.llmoc_try_gemm_int4_batch(L.ptr(X), n, C.byref(v), L.ptr(Y)) == 1, L.last_error()
+    ref = oracle.gemm_int4_batch(X, W)
+    assert np.all(np.abs(Y - ref) < 1e-3 * (1 + np.abs(ref)))
+    ys = [np.empty(M, np.float32) for _ in range(2)]
+    Ws = (C.POINTER(L.Int4View) * 2)(C.pointer(v), C.pointer(v))
+    yp = (C.c_void_p * 2)(*[L.ptr(a) for a in ys])
+    assert L.lib.llmoc_try_gemm_int4_multi(L.ptr(X[0]), Ws, yp, 2) == 1
+    assert np.array_equal(ys[0], Y[0]) and np.array_equal(ys[1], Y[0])
+
+
+@pytest.mark.parametrize("shared", [False, True])
+def test_try_moe_ffn_int4(oracle, shared):
+    """hal::cuda::try_moe_ffn_int4 contract: one token, given experts and weights."""
+    rng = np.random.default_rng(11)
+    layer = orc.make_layer(oracle, rng, H=1024, I=384, E=12, topk=6, gs=128, shared=shared)
+    x = orc.make_tokens(rng, 1, 1024)[0]
+    w = np.array([0.3, 0.2, 1e-13, 0.25, 0.15, 0.1], np.float32)
+    sel = [5, 1, 7, 0, 11, 3]
+    views = []
+    exps = (L.MoeExpertInt4 * 6)()
+    for i, e in enumerate(sel):
+        ex = layer.experts[e]
+        trio = [L.view_of(ex.gate), L.view_of(ex.up), L.view_of(ex.down)]
+        views.append(trio)
+        exps[i] = L.MoeExpertInt4(C.pointer(trio[0]), C.pointer(trio[1]), C.pointer(trio[2]), float(w[i]))
+    sh = [L.view_of(layer.shared.gate), L.view_of(layer.shared.up), L.view_of(layer.shared.down)] \
+        if shared else [None, None, None]
+    shp = [C.pointer(s) if s is not None else None for s in sh]
+    y = np.empty(1024, np.float32)
+    ok = L.lib.llmoc_try_moe_ffn_int4(L.ptr(x), 1024, 384, exps, 6, shp[0], shp[1], shp[2], 0.5, L.ptr(y))
+    assert ok == 1, L.last_error()
+    ref = oracle.moe_ffn_routed(x, 1024, 384, [layer.experts[e] for e in sel], w,
+                                layer.shared if shared else None, 0.5)
+    mre, cos = G.quality(y, ref)
+    assert mre <= 1e-3 and cos >= 0.99999, (mre, cos)
