@@ -55,6 +55,9 @@ def parse():
     ap.add_argument("--tokens", type=int, default=64)
     ap.add_argument("--sweep", default="1,8,64,512", help="extra T values ('' = none)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--copies", type=int, default=0,
+                    help="distinct layer copies to rotate (0 = enough to defeat L2); small values "
+                         "make ncu captures cheap")
     return ap.parse_args()
 
 
@@ -100,12 +103,12 @@ class Clocks:
     def stop(self):
         if not self.proc:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        time.sleep(0.25)
         self.proc.terminate()
         out, _ = self.proc.communicate(timeout=10)
         sm, mx, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in out.strip().splitlines():
+        lines = out.strip().splitlines()[2:]  # the first samples can predate the load
+        for ln in lines:
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
@@ -187,6 +190,7 @@ def build_layers(torch, L, cfg, R, seed, keep_host=False, device=0):
 
 def host_layer(cfg, host):
     """The kept layer as oracle objects (for the reference CPU path)."""
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
     import orc
 
     H, I, E, gs = cfg["H"], cfg["I"], cfg["E"], cfg["gs"]
@@ -205,6 +209,7 @@ def host_layer(cfg, host):
 
 def reference_cpu(cfg, layer_obj, T_total, budget_s=4.0, min_tokens=4):
     """Time the reference's CPU path (oracle/_ref) on a bounded token sample."""
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
     import orc
 
     R = orc.Reference()
@@ -248,6 +253,8 @@ def run_llmoc(args):
     exp_b = gu_b + dn_b
     touched_min = min(expected_touched(E, k, T) for T in Ts) + (1 if cfg["shared"] else 0)
     R = int(max(2, min(24, np.ceil(3 * L2_BYTES / (touched_min * exp_b)))))
+    if args.copies > 0:
+        R = args.copies
     layers, host = build_layers(torch, L, cfg, R, seed=1234 + rank, keep_host=(rank == 0 and not args.no_cpu_baseline))
     Tmax = max(Ts)
     ws_bytes = layers[0].workspace_bytes(Tmax)
@@ -292,7 +299,16 @@ def run_llmoc(args):
             step(i, T)
         torch.cuda.synchronize()
         if T == args.tokens:
+            # back-to-back untimed steps so the clock samples (200 ms apart)
+            # see the GPU under this load; the timed region follows directly
             clocks.start()
+            t_end = time.perf_counter() + 1.5
+            i = 0
+            while time.perf_counter() < t_end:
+                for _ in range(50):
+                    step(i, T)
+                    i += 1
+                torch.cuda.synchronize()
             n0 = L.launch_count()
         ms = timed(T, args.steps, step)
         if T == args.tokens:

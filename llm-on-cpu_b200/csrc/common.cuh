@@ -48,7 +48,7 @@ struct WorkItem {
   int pad;
 };
 
-constexpr int kChunkRows = 32;  // pairs per work item (tensor-core N = 4 x 8)
+constexpr int kChunkRows = 32;  // largest work item (tensor-core N = 4 x 8 rows)
 
 __device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) {
   return __uint_as_float(static_cast<uint32_t>(b) << 16);

@@ -138,15 +138,22 @@ __device__ __forceinline__ uint4 ldg_nc(const uint4* p) {
 
 __device__ __forceinline__ float silu_mul(float g, float u) { return (g / (1.f + expf(-g))) * u; }
 
-// grid.x = ceil(Mt / 4) (one 16-row tile per warp), grid.y = work-list bound.
+// One CTA = one 16-row tile of one work item; its KS warps split K into
+// contiguous slices (group-aligned where the group spans whole chunks) and
+// keep a DEPTH-deep ring of 128-bit weight loads in flight each.  Partial
+// accumulators meet in shared memory and are summed in warp order (fixed,
+// so results do not depend on scheduling).  grid.x = Mt, grid.y = work bound.
 // NP = 2 computes gate and up of the same rows (GATE_UP), NP = 1 one projection.
+constexpr int kKS = 4;     // warps per CTA (K slices)
+constexpr int kDepth = 4;  // weight chunks in flight per warp and projection
+
 template <int MODE, int NT>
-__global__ void __launch_bounds__(128) k_int4_mma(GemmArgs a) {
+__global__ void __launch_bounds__(kKS * 32) k_int4_mma(GemmArgs a) {
   constexpr int NP = MODE == MODE_GATE_UP ? 2 : 1;
+  __shared__ float red[kKS][NP][NT][4][32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
-  const int rt = blockIdx.x * 4 + warp;
-  if (rt * 16 >= a.M) return;
+  const int rt = blockIdx.x;
   if ((int)blockIdx.y >= *a.n_work) return;
   const WorkItem it = a.work[blockIdx.y];
   const ExpertDev& ex = a.experts[it.expert];
@@ -154,6 +161,13 @@ __global__ void __launch_bounds__(128) k_int4_mma(GemmArgs a) {
   P[0] = MODE == MODE_GATE_UP ? &ex.gate : &pick(ex, a.proj);
   P[1] = &ex.up;
   const int ntc = (it.nrows + 7) >> 3;
+
+  // this warp's chunk range [c0, c1)
+  const int align = a.gs >= 64 ? a.gs / 64 : 1;
+  int per = (a.Kc + kKS - 1) / kKS;
+  per = (per + align - 1) / align * align;
+  const int c0 = min(a.Kc, warp * per), c1 = min(a.Kc, c0 + per);
+  const int kend = min(a.K, c1 * 64);
 
   const __nv_bfloat16* brow[NT];
   bool bval[NT];
@@ -165,8 +179,8 @@ __global__ void __launch_bounds__(128) k_int4_mma(GemmArgs a) {
     const int row = a.gather ? a.gather[pos] / a.kk : pos;
     brow[n] = reinterpret_cast<const __nv_bfloat16*>(a.B) + (size_t)row * a.ldb + 8 * t;
   }
-  const uint32_t zp2 = (uint32_t)(0x4300 + a.zp) * 0x10001u;  // bf16 (128+zp) twice
-  // bf16 128+zp is exact for zp < 128: 0x4300 encodes 128, mantissa step 1
+  // bf16 (128 + zp) in both halves; exact for zp < 128 (0x4300 encodes 128, step 1)
+  const uint32_t zp2 = (uint32_t)(0x4300 + a.zp) * 0x10001u;
 
   float acc[NP][NT][4], tmp[NP][NT][4];
 #pragma unroll
@@ -180,60 +194,89 @@ __global__ void __launch_bounds__(128) k_int4_mma(GemmArgs a) {
 #pragma unroll
   for (int p = 0; p < NP; ++p) qp[p] = P[p]->q + (size_t)rt * a.Kc * 32 + lane;
 
-  for (int c = 0; c < a.Kc; ++c) {
-    uint4 qw[NP];
+  uint4 ring[NP][kDepth];
 #pragma unroll
-    for (int p = 0; p < NP; ++p) qw[p] = ldg_nc(qp[p] + (size_t)c * 32);
+  for (int d = 0; d < kDepth; ++d)
 #pragma unroll
-    for (int kb = 0; kb < 2; ++kb) {
-      const int k32 = c * 64 + kb * 32;
-      if (k32 >= a.K) break;
-      uint4 bv[NT];
+    for (int p = 0; p < NP; ++p)
+      if (c0 + d < c1) ring[p][d] = ldg_nc(qp[p] + (size_t)(c0 + d) * 32);
+
+  for (int cb = c0; cb < c1; cb += kDepth) {
 #pragma unroll
-      for (int n = 0; n < NT; ++n) {
-        bv[n] = make_uint4(0, 0, 0, 0);
-        if (n < ntc && bval[n]) bv[n] = *reinterpret_cast<const uint4*>(brow[n] + k32);
+    for (int d = 0; d < kDepth; ++d) {
+      const int c = cb + d;
+      if (c >= c1) break;
+      uint4 qw[NP];
+#pragma unroll
+      for (int p = 0; p < NP; ++p) {
+        qw[p] = ring[p][d];
+        if (c + kDepth < c1) ring[p][d] = ldg_nc(qp[p] + (size_t)(c + kDepth) * 32);
       }
 #pragma unroll
-      for (int kt = 0; kt < 2; ++kt) {
+      for (int kb = 0; kb < 2; ++kb) {
+        const int k32 = c * 64 + kb * 32;
+        if (k32 >= a.K) break;
+        uint4 bv[NT];
 #pragma unroll
-        for (int p = 0; p < NP; ++p) {
-          const uint32_t wd = (kb * 2 + kt == 0)   ? qw[p].x
-                              : (kb * 2 + kt == 1) ? qw[p].y
-                              : (kb * 2 + kt == 2) ? qw[p].z
-                                                   : qw[p].w;
-          uint32_t af[4];
-          dequant_word(wd, zp2, af);
+        for (int n = 0; n < NT; ++n) {
+          bv[n] = make_uint4(0, 0, 0, 0);
+          if (n < ntc && bval[n]) bv[n] = *reinterpret_cast<const uint4*>(brow[n] + k32);
+        }
 #pragma unroll
-          for (int n = 0; n < NT; ++n) {
-            if (n < ntc) {
-              const uint32_t b0 = kt ? bv[n].z : bv[n].x;
-              const uint32_t b1 = kt ? bv[n].w : bv[n].y;
-              mma_bf16(tmp[p][n], af, b0, b1);
-            }
+        for (int kt = 0; kt < 2; ++kt) {
+#pragma unroll
+          for (int p = 0; p < NP; ++p) {
+            const int wi = kb * 2 + kt;
+            const uint32_t wd = wi == 0 ? qw[p].x : wi == 1 ? qw[p].y : wi == 2 ? qw[p].z : qw[p].w;
+            uint32_t af[4];
+            dequant_word(wd, zp2, af);
+#pragma unroll
+            for (int n = 0; n < NT; ++n)
+              if (n < ntc) mma_bf16(tmp[p][n], af, kt ? bv[n].z : bv[n].x, kt ? bv[n].w : bv[n].y);
           }
         }
-      }
-      if (((k32 + 32) % a.gs) == 0 || k32 + 32 >= a.K) {
-        const int grp = k32 / a.gs;
+        if (((k32 + 32) % a.gs) == 0 || k32 + 32 >= kend) {
+          const int grp = k32 / a.gs;
 #pragma unroll
-        for (int p = 0; p < NP; ++p) {
-          const __half* sp = P[p]->s + ((size_t)rt * a.ng + grp) * 16;
-          const float s0 = __half2float(sp[g]), s1 = __half2float(sp[g + 8]);
+          for (int p = 0; p < NP; ++p) {
+            const __half* sp = P[p]->s + ((size_t)rt * a.ng + grp) * 16;
+            const float s0 = __half2float(sp[g]), s1 = __half2float(sp[g + 8]);
 #pragma unroll
-          for (int n = 0; n < NT; ++n) {
-            acc[p][n][0] = __fmaf_rn(tmp[p][n][0], s0, acc[p][n][0]);
-            acc[p][n][1] = __fmaf_rn(tmp[p][n][1], s0, acc[p][n][1]);
-            acc[p][n][2] = __fmaf_rn(tmp[p][n][2], s1, acc[p][n][2]);
-            acc[p][n][3] = __fmaf_rn(tmp[p][n][3], s1, acc[p][n][3]);
-            tmp[p][n][0] = tmp[p][n][1] = tmp[p][n][2] = tmp[p][n][3] = 0.f;
+            for (int n = 0; n < NT; ++n) {
+              acc[p][n][0] = __fmaf_rn(tmp[p][n][0], s0, acc[p][n][0]);
+              acc[p][n][1] = __fmaf_rn(tmp[p][n][1], s0, acc[p][n][1]);
+              acc[p][n][2] = __fmaf_rn(tmp[p][n][2], s1, acc[p][n][2]);
+              acc[p][n][3] = __fmaf_rn(tmp[p][n][3], s1, acc[p][n][3]);
+              tmp[p][n][0] = tmp[p][n][1] = tmp[p][n][2] = tmp[p][n][3] = 0.f;
+            }
           }
         }
       }
     }
   }
 
-  // epilogue: C fragment (row g / g+8, col 2t / 2t+1) of each N-tile
+  // K-slice reduction in warp order, then the epilogue on warp 0
+#pragma unroll
+  for (int p = 0; p < NP; ++p)
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) red[warp][p][n][r][lane] = acc[p][n][r];
+  __syncthreads();
+  if (warp != 0) return;
+#pragma unroll
+  for (int p = 0; p < NP; ++p)
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        float v = red[0][p][n][r][lane];
+#pragma unroll
+        for (int w = 1; w < kKS; ++w) v += red[w][p][n][r][lane];
+        acc[p][n][r] = v;
+      }
+
+  // C fragment (row g / g+8, col 2t / 2t+1) of each N-tile
   const int m0 = rt * 16 + g, m1 = m0 + 8;
 #pragma unroll
   for (int n = 0; n < NT; ++n) {
@@ -525,16 +568,21 @@ cudaError_t launch_gemm(int mode, int path, const GemmArgs& a, int max_work, int
   const int Mt = (a.M + 15) / 16;
   dim3 grid((Mt + 3) / 4, max_work);
   if (path == 0) {
+    const dim3 gm(Mt, max_work);
     if (mode == MODE_GATE_UP) {
       if (ntiles <= 1)
-        k_int4_mma<MODE_GATE_UP, 1><<<grid, 128, 0, st>>>(a);
+        k_int4_mma<MODE_GATE_UP, 1><<<gm, kKS * 32, 0, st>>>(a);
+      else if (ntiles == 2)
+        k_int4_mma<MODE_GATE_UP, 2><<<gm, kKS * 32, 0, st>>>(a);
       else
-        k_int4_mma<MODE_GATE_UP, 4><<<grid, 128, 0, st>>>(a);
+        k_int4_mma<MODE_GATE_UP, 4><<<gm, kKS * 32, 0, st>>>(a);
     } else {
       if (ntiles <= 1)
-        k_int4_mma<MODE_PLAIN_F32, 1><<<grid, 128, 0, st>>>(a);
+        k_int4_mma<MODE_PLAIN_F32, 1><<<gm, kKS * 32, 0, st>>>(a);
+      else if (ntiles == 2)
+        k_int4_mma<MODE_PLAIN_F32, 2><<<gm, kKS * 32, 0, st>>>(a);
       else
-        k_int4_mma<MODE_PLAIN_F32, 4><<<grid, 128, 0, st>>>(a);
+        k_int4_mma<MODE_PLAIN_F32, 4><<<gm, kKS * 32, 0, st>>>(a);
     }
   } else if (path == 1) {
     if (mode == MODE_GATE_UP)

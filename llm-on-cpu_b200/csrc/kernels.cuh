@@ -28,6 +28,7 @@ struct PermArgs {
   WorkItem* work;   // [max_work]
   int* n_work;
   int* n_active;
+  int chunk;        // rows per work item (8, 16 or 32)
 };
 
 constexpr int kPermThreads = 1024;

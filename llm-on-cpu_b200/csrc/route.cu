@@ -83,7 +83,7 @@ __global__ void __launch_bounds__(256) k_router_logits(const XT* __restrict__ X,
   for (int b = 0; b < EW; ++b) wr[b] = Wr + (size_t)min(e0 + b, E - 1) * H;
 
   const int K32 = live ? (H & ~31) : 0;
-#pragma unroll 2
+#pragma unroll 4
   for (int k = 4 * sub; k < K32; k += 32) {
     float xv[TW][4];
 #pragma unroll
@@ -246,7 +246,7 @@ __global__ void __launch_bounds__(kPermThreads) k_permute(PermArgs a) {
   int tot = 0;
   if (e < a.n_exp)
     for (int w = 0; w < kPermWarps; ++w) tot += cnt[w * a.n_exp + e];
-  const int chunks = (tot + kChunkRows - 1) / kChunkRows;
+  const int chunks = (tot + a.chunk - 1) / a.chunk;
   // block exclusive scan of (tot, chunks, active) packed: do two scans
   int v1 = tot, v2 = chunks, v3 = tot > 0;
   for (int o = 1; o < 32; o <<= 1) {
@@ -296,8 +296,8 @@ __global__ void __launch_bounds__(kPermThreads) k_permute(PermArgs a) {
     for (int c = 0; c < chunks; ++c) {
       WorkItem it;
       it.expert = e;
-      it.row0 = base1 + c * kChunkRows;
-      it.nrows = min(kChunkRows, tot - c * kChunkRows);
+      it.row0 = base1 + c * a.chunk;
+      it.nrows = min(a.chunk, tot - c * a.chunk);
       it.pad = 0;
       a.work[base2 + c] = it;
     }
@@ -341,6 +341,16 @@ cudaError_t launch_router_logits(const void* X, bool x_is_f32, const uint16_t* W
       k_router_logits<float, 1, 1><<<blocks, threads, 0, st>>>((const float*)X, Wr, T, E, H, logits);
     else
       k_router_logits<__nv_bfloat16, 1, 1>
+          <<<blocks, threads, 0, st>>>((const __nv_bfloat16*)X, Wr, T, E, H, logits);
+  } else if (T <= 256) {
+    constexpr int TW = 2, EW = 2;
+    const long groups = (long)((T + TW - 1) / TW) * ((E + EW - 1) / EW);
+    const int blocks = (int)((groups * 8 + threads - 1) / threads);
+    if (x_is_f32)
+      k_router_logits<float, TW, EW>
+          <<<blocks, threads, 0, st>>>((const float*)X, Wr, T, E, H, logits);
+    else
+      k_router_logits<__nv_bfloat16, TW, EW>
           <<<blocks, threads, 0, st>>>((const __nv_bfloat16*)X, Wr, T, E, H, logits);
   } else {
     constexpr int TW = 4, EW = 4;

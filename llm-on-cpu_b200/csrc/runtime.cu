@@ -331,6 +331,10 @@ struct llmoc_moe_layer {
 
 namespace {
 
+// Rows per work item (tensor-core N tiles of 8): small batches use narrower
+// items so the kernel variant carries fewer accumulators.
+int chunk_rows(int T) { return T <= 8 ? 8 : (T <= 128 ? 16 : kChunkRows); }
+
 struct WsLayout {
   size_t logits, ids, weights, offsets, sorted, inverse, work, n_work, n_active, mid, partial, total;
   int max_work;
@@ -345,7 +349,8 @@ WsLayout ws_layout(const llmoc_moe_layer* L, int T) {
     o += align256(bytes);
     return at;
   };
-  w.max_work = (int)(std::min<size_t>((size_t)L->n_exp, n) + (n + kChunkRows - 1) / kChunkRows);
+  const int chunk = chunk_rows(T);
+  w.max_work = (int)(std::min<size_t>((size_t)L->n_exp, n) + (n + chunk - 1) / chunk);
   w.logits = take((size_t)T * L->d.n_experts * 4);
   w.ids = take(n * 4);
   w.weights = take(n * 4);
@@ -566,6 +571,7 @@ llmoc_status run_route(const llmoc_moe_layer* L, const uint16_t* X, int T, const
   pa.work = (WorkItem*)(ws + w.work);
   pa.n_work = (int*)(ws + w.n_work);
   pa.n_active = (int*)(ws + w.n_active);
+  pa.chunk = chunk_rows(T);
   if (!cuda_ok(launch_permute(pa, st), "permute")) return LLMOC_ERR_CUDA;
   if (se) se->mark(st);
   count_launch(3);
@@ -932,7 +938,7 @@ llmoc_status llmoc_moe_forward(const llmoc_moe_layer* L, const uint16_t* X, int 
   const int H = L->d.hidden, I = L->d.inter;
   const bool awq = L->d.scheme == LLMOC_SCHEME_AWQ_SYM;
   const int path = awq ? 0 : 2;
-  const int ntiles = T <= 8 ? 1 : 4;
+  const int ntiles = chunk_rows(T) / 8;
   GemmArgs a{};
   a.experts = L->table;
   a.M = I;

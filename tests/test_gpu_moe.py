@@ -207,6 +207,18 @@ def test_full_size_layer(oracle, name, T):
 
 # ------------------------------------------- the reference's host-fp32 API
 
+@pytest.fixture
+def fresh_cache():
+    """The host-pointer API caches weights keyed by the host qweight address
+    (src/hal/cuda_backend.cpp:607); numpy reuses freed addresses between tests,
+    so each test starts from an empty cache (disable() frees it)."""
+    L.lib.llmoc_cuda_disable()
+    assert L.lib.llmoc_cuda_enable(0) == 1
+    yield
+    L.lib.llmoc_cuda_disable()
+    assert L.lib.llmoc_cuda_enable(0) == 1
+
+
 def unit_case(name):
     import make_golden as mg
 
@@ -219,7 +231,7 @@ def unit_case(name):
 
 
 @pytest.mark.parametrize("case", ["awq_scalar", "awq_gemv", "gptq_gemv"])
-def test_try_gemm_int4_reference_cases(case):
+def test_try_gemm_int4_reference_cases(case, fresh_cache):
     """GpuGemmMatchesCpuIfCuda / AwqGemvJitMatchesCpu / GptqGemvJitMatchesCpu
     (tests/unit/test_int4_gemm.cpp:151-198, test_gpu_quant_gemm.cpp:130-245):
     GPU vs the reference CPU result, rel 1e-3."""
@@ -234,7 +246,7 @@ def test_try_gemm_int4_reference_cases(case):
 
 
 @pytest.mark.parametrize("case", ["awq_batch", "gptq_batch"])
-def test_try_gemm_int4_batch_reference_cases(case):
+def test_try_gemm_int4_batch_reference_cases(case, fresh_cache):
     d, W = unit_case(case)
     X = np.ascontiguousarray(d["X"])
     Y = np.empty((X.shape[0], W.M), np.float32)
@@ -245,7 +257,7 @@ def test_try_gemm_int4_batch_reference_cases(case):
 
 @pytest.mark.parametrize("M,K,gs,n,scheme", [(4096, 4096, 128, 1, 2), (11008, 4096, 128, 8, 2),
                                              (768, 2048, 128, 64, 1), (2048, 7168, 32, 3, 2)])
-def test_try_gemm_int4_config1_shapes(oracle, M, K, gs, n, scheme):
+def test_try_gemm_int4_config1_shapes(oracle, M, K, gs, n, scheme, fresh_cache):
     rng = np.random.default_rng(M + n)
     Wf = orc.bf16_round(rng.standard_normal((M, K), dtype=np.float32) * np.float32(0.02))
     W = oracle.quant_awq_sym(Wf, gs, True) if scheme == 2 else oracle.quant_gptq_asym(Wf, gs)
@@ -263,7 +275,7 @@ def test_try_gemm_int4_config1_shapes(oracle, M, K, gs, n, scheme):
 
 
 @pytest.mark.parametrize("shared", [False, True])
-def test_try_moe_ffn_int4(oracle, shared):
+def test_try_moe_ffn_int4(oracle, shared, fresh_cache):
     """hal::cuda::try_moe_ffn_int4 contract: one token, given experts and weights."""
     rng = np.random.default_rng(11)
     layer = orc.make_layer(oracle, rng, H=1024, I=384, E=12, topk=6, gs=128, shared=shared)
@@ -287,3 +299,29 @@ def test_try_moe_ffn_int4(oracle, shared):
                                 layer.shared if shared else None, 0.5)
     mre, cos = G.quality(y, ref)
     assert mre <= 1e-3 and cos >= 0.99999, (mre, cos)
+
+
+def test_resident_cache_budget_and_pinning(oracle, fresh_cache):
+    """LRU eviction under the VRAM budget skips pinned weights
+    (cuda_backend.cpp:618-639); a shape change at a cached address is refused."""
+    rng = np.random.default_rng(12)
+    ws = [oracle.quant_awq_sym(orc.bf16_round(rng.standard_normal((256, 1024), dtype=np.float32) * 0.02), 128)
+          for _ in range(4)]
+    vs = [L.view_of(w) for w in ws]
+    assert L.lib.llmoc_pin_int4_weight(C.byref(vs[0])) == 1
+    one = L.lib.llmoc_cuda_vram_used()
+    L.lib.llmoc_cuda_set_vram_budget(int(one * 2.5))
+    for v in vs[1:]:
+        assert L.lib.llmoc_prefetch_int4_weight(C.byref(v)) == 1
+    assert L.lib.llmoc_cuda_vram_used() <= int(one * 2.5)
+    x = rng.standard_normal(1024, dtype=np.float32)
+    for w, v in zip(ws, vs):  # evicted weights re-upload transparently
+        y = np.empty(256, np.float32)
+        assert L.lib.llmoc_try_gemm_int4(L.ptr(x), C.byref(v), L.ptr(y)) == 1
+        ref = oracle.gemm_int4(x, w)
+        assert np.all(np.abs(y - ref) < 1e-3 * (1 + np.abs(ref)))
+    L.lib.llmoc_cuda_set_vram_budget(0)
+    bad = L.view(ws[0].q, ws[0].scales, None, 128, 1024, 128)
+    y = np.empty(128, np.float32)
+    assert L.lib.llmoc_try_gemm_int4(L.ptr(x), C.byref(bad), L.ptr(y)) == 0
+    assert "mismatch" in L.last_error()
