@@ -138,23 +138,28 @@ __device__ __forceinline__ uint4 ldg_nc(const uint4* p) {
 
 __device__ __forceinline__ float silu_mul(float g, float u) { return (g / (1.f + expf(-g))) * u; }
 
-// One CTA = one 16-row tile of one work item; its KS warps split K into
-// contiguous slices (group-aligned where the group spans whole chunks) and
-// keep a DEPTH-deep ring of 128-bit weight loads in flight each.  Partial
-// accumulators meet in shared memory and are summed in warp order (fixed,
-// so results do not depend on scheduling).  grid.x = Mt, grid.y = work bound.
+// A CTA of 4 warps covers 4/KS row tiles (16 rows each) of one work item;
+// the KS warps of a tile split K into contiguous group-aligned slices.  Each
+// warp keeps a kDepth-deep ring of 128-bit weight loads in flight.  GSB is
+// the group size in 32-wide k blocks (1, 2 or 4; 0 = any multiple of 32, kept
+// with a running counter).  Slices meet in shared memory and are summed in
+// warp order (fixed, so results do not depend on scheduling).
+// grid.x = ceil(Mt * KS / 4), grid.y = work-list bound.
 // NP = 2 computes gate and up of the same rows (GATE_UP), NP = 1 one projection.
-constexpr int kKS = 4;     // warps per CTA (K slices)
+constexpr int kWarps = 4;  // warps per CTA
 constexpr int kDepth = 4;  // weight chunks in flight per warp and projection
 
-template <int MODE, int NT>
-__global__ void __launch_bounds__(kKS * 32) k_int4_mma(GemmArgs a) {
+template <int MODE, int NT, int GSB>
+__global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
   constexpr int NP = MODE == MODE_GATE_UP ? 2 : 1;
-  __shared__ float red[kKS][NP][NT][4][32];
+  __shared__ float red[kWarps][NP][NT][4][32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
-  const int rt = blockIdx.x;
+  const int slice = warp % ks;
+  const int rt = blockIdx.x * (kWarps / ks) + warp / ks;
   if ((int)blockIdx.y >= *a.n_work) return;
+  const int Mt = (a.M + 15) >> 4;
+  const bool live = rt < Mt;
   const WorkItem it = a.work[blockIdx.y];
   const ExpertDev& ex = a.experts[it.expert];
   const ProjDev* P[2];
@@ -162,12 +167,14 @@ __global__ void __launch_bounds__(kKS * 32) k_int4_mma(GemmArgs a) {
   P[1] = &ex.up;
   const int ntc = (it.nrows + 7) >> 3;
 
-  // this warp's chunk range [c0, c1)
-  const int align = a.gs >= 64 ? a.gs / 64 : 1;
-  int per = (a.Kc + kKS - 1) / kKS;
+  // this warp's chunk range [c0, c1), aligned to whole groups when possible
+  const int gsb = GSB ? GSB : (a.gs >> 5);
+  const int align = gsb >= 2 ? gsb >> 1 : 1;  // chunks per group (>= 1)
+  int per = (a.Kc + ks - 1) / ks;
   per = (per + align - 1) / align * align;
-  const int c0 = min(a.Kc, warp * per), c1 = min(a.Kc, c0 + per);
-  const int kend = min(a.K, c1 * 64);
+  const int c0 = live ? min(a.Kc, slice * per) : 0;
+  const int c1 = live ? min(a.Kc, c0 + per) : 0;
+  const int kb_last = (a.K >> 5) - 1;  // index of the last valid 32-wide block
 
   const __nv_bfloat16* brow[NT];
   bool bval[NT];
@@ -191,8 +198,12 @@ __global__ void __launch_bounds__(kKS * 32) k_int4_mma(GemmArgs a) {
       for (int r = 0; r < 4; ++r) acc[p][n][r] = tmp[p][n][r] = 0.f;
 
   const uint4* qp[NP];
+  const __half* sp[NP];
 #pragma unroll
-  for (int p = 0; p < NP; ++p) qp[p] = P[p]->q + (size_t)rt * a.Kc * 32 + lane;
+  for (int p = 0; p < NP; ++p) {
+    qp[p] = P[p]->q + (size_t)(live ? rt : 0) * a.Kc * 32 + lane;
+    sp[p] = P[p]->s + (size_t)(live ? rt : 0) * a.ng * 16 + g;
+  }
 
   uint4 ring[NP][kDepth];
 #pragma unroll
@@ -201,6 +212,8 @@ __global__ void __launch_bounds__(kKS * 32) k_int4_mma(GemmArgs a) {
     for (int p = 0; p < NP; ++p)
       if (c0 + d < c1) ring[p][d] = ldg_nc(qp[p] + (size_t)(c0 + d) * 32);
 
+  int grp = (c0 * 2) / gsb;                  // group of the first block
+  int left = gsb - ((c0 * 2) % gsb);         // blocks left in that group (GSB == 0 only)
   for (int cb = c0; cb < c1; cb += kDepth) {
 #pragma unroll
     for (int d = 0; d < kDepth; ++d) {
@@ -214,8 +227,9 @@ __global__ void __launch_bounds__(kKS * 32) k_int4_mma(GemmArgs a) {
       }
 #pragma unroll
       for (int kb = 0; kb < 2; ++kb) {
-        const int k32 = c * 64 + kb * 32;
-        if (k32 >= a.K) break;
+        const int blk = 2 * c + kb;
+        if (blk > kb_last) break;
+        const int k32 = blk * 32;
         uint4 bv[NT];
 #pragma unroll
         for (int n = 0; n < NT; ++n) {
@@ -235,12 +249,16 @@ __global__ void __launch_bounds__(kKS * 32) k_int4_mma(GemmArgs a) {
               if (n < ntc) mma_bf16(tmp[p][n], af, kt ? bv[n].z : bv[n].x, kt ? bv[n].w : bv[n].y);
           }
         }
-        if (((k32 + 32) % a.gs) == 0 || k32 + 32 >= kend) {
-          const int grp = k32 / a.gs;
+        // end of a group (or of the warp's slice / of K): scale into acc
+        bool gend;
+        if (GSB == 1) gend = true;
+        else if (GSB == 2) gend = kb == 1 || blk == kb_last;
+        else if (GSB == 4) gend = (kb == 1 && (c & 1)) || blk == kb_last || (kb == 1 && c + 1 == c1);
+        else gend = (--left == 0) || blk == kb_last || (kb == 1 && c + 1 == c1);
+        if (gend) {
 #pragma unroll
           for (int p = 0; p < NP; ++p) {
-            const __half* sp = P[p]->s + ((size_t)rt * a.ng + grp) * 16;
-            const float s0 = __half2float(sp[g]), s1 = __half2float(sp[g + 8]);
+            const float s0 = __half2float(sp[p][grp * 16]), s1 = __half2float(sp[p][grp * 16 + 8]);
 #pragma unroll
             for (int n = 0; n < NT; ++n) {
               acc[p][n][0] = __fmaf_rn(tmp[p][n][0], s0, acc[p][n][0]);
@@ -250,31 +268,34 @@ __global__ void __launch_bounds__(kKS * 32) k_int4_mma(GemmArgs a) {
               tmp[p][n][0] = tmp[p][n][1] = tmp[p][n][2] = tmp[p][n][3] = 0.f;
             }
           }
+          ++grp;
+          if (GSB == 0) left = gsb;
         }
       }
     }
   }
 
-  // K-slice reduction in warp order, then the epilogue on warp 0
+  if (ks > 1) {  // K-slice reduction in warp order
 #pragma unroll
-  for (int p = 0; p < NP; ++p)
+    for (int p = 0; p < NP; ++p)
 #pragma unroll
-    for (int n = 0; n < NT; ++n)
+      for (int n = 0; n < NT; ++n)
 #pragma unroll
-      for (int r = 0; r < 4; ++r) red[warp][p][n][r][lane] = acc[p][n][r];
-  __syncthreads();
-  if (warp != 0) return;
+        for (int r = 0; r < 4; ++r) red[warp][p][n][r][lane] = acc[p][n][r];
+    __syncthreads();
+    if (slice != 0) return;
 #pragma unroll
-  for (int p = 0; p < NP; ++p)
+    for (int p = 0; p < NP; ++p)
 #pragma unroll
-    for (int n = 0; n < NT; ++n)
+      for (int n = 0; n < NT; ++n)
 #pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        float v = red[0][p][n][r][lane];
-#pragma unroll
-        for (int w = 1; w < kKS; ++w) v += red[w][p][n][r][lane];
-        acc[p][n][r] = v;
-      }
+        for (int r = 0; r < 4; ++r) {
+          float v = red[warp][p][n][r][lane];
+          for (int w = 1; w < ks; ++w) v += red[warp + w][p][n][r][lane];
+          acc[p][n][r] = v;
+        }
+  }
+  if (!live) return;
 
   // C fragment (row g / g+8, col 2t / 2t+1) of each N-tile
   const int m0 = rt * 16 + g, m1 = m0 + 8;
@@ -298,6 +319,25 @@ __global__ void __launch_bounds__(kKS * 32) k_int4_mma(GemmArgs a) {
       }
     }
   }
+}
+
+template <int MODE, int NT>
+static void launch_mma_gs(const GemmArgs& a, int max_work, int ks, cudaStream_t st) {
+  const int Mt = (a.M + 15) / 16;
+  const dim3 grid((Mt * ks + kWarps - 1) / kWarps, max_work);
+  switch (a.gs) {
+    case 32: k_int4_mma<MODE, NT, 1><<<grid, kWarps * 32, 0, st>>>(a, ks); break;
+    case 64: k_int4_mma<MODE, NT, 2><<<grid, kWarps * 32, 0, st>>>(a, ks); break;
+    case 128: k_int4_mma<MODE, NT, 4><<<grid, kWarps * 32, 0, st>>>(a, ks); break;
+    default: k_int4_mma<MODE, NT, 0><<<grid, kWarps * 32, 0, st>>>(a, ks); break;
+  }
+}
+
+template <int MODE>
+static void launch_mma(const GemmArgs& a, int max_work, int ntiles, int ks, cudaStream_t st) {
+  if (ntiles <= 1) launch_mma_gs<MODE, 1>(a, max_work, ks, st);
+  else if (ntiles == 2) launch_mma_gs<MODE, 2>(a, max_work, ks, st);
+  else launch_mma_gs<MODE, 4>(a, max_work, ks, st);
 }
 
 // ------------------------------------------------------ CUDA-core fp32 GEMV
@@ -487,19 +527,33 @@ __global__ void k_combine(const float* __restrict__ d, const int* __restrict__ i
   const int h = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
   if (t >= T || h >= H) return;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int j = 0; j < kk; ++j) {
-    const float wj = w[(size_t)t * kk + j];
-    if (skip_tiny && fabsf(wj) < 1e-12f) continue;
-    const float* row = d + (size_t)inverse[(size_t)t * kk + j] * H;
-    if (h + 3 < H) {
-      const float4 v = *reinterpret_cast<const float4*>(row + h);
-      acc.x = __fmaf_rn(wj, v.x, acc.x);
-      acc.y = __fmaf_rn(wj, v.y, acc.y);
-      acc.z = __fmaf_rn(wj, v.z, acc.z);
-      acc.w = __fmaf_rn(wj, v.w, acc.w);
-    } else {
-      float* ap = &acc.x;
-      for (int i = 0; h + i < H; ++i) ap[i] = __fmaf_rn(wj, row[h + i], ap[i]);
+  // issue the slot loads in groups of 8 before the ordered FMAs
+  for (int j0 = 0; j0 < kk; j0 += 8) {
+    float wj[8];
+    float4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int j = j0 + u;
+      wj[u] = 0.f;
+      v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (j < kk) {
+        wj[u] = w[(size_t)t * kk + j];
+        const float* row = d + (size_t)inverse[(size_t)t * kk + j] * H;
+        if (h + 3 < H) {
+          v[u] = *reinterpret_cast<const float4*>(row + h);
+        } else {
+          float* vp = &v[u].x;
+          for (int i = 0; h + i < H; ++i) vp[i] = row[h + i];
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      if (j0 + u >= kk || (skip_tiny && fabsf(wj[u]) < 1e-12f)) continue;
+      acc.x = __fmaf_rn(wj[u], v[u].x, acc.x);
+      acc.y = __fmaf_rn(wj[u], v[u].y, acc.y);
+      acc.z = __fmaf_rn(wj[u], v[u].z, acc.z);
+      acc.w = __fmaf_rn(wj[u], v[u].w, acc.w);
     }
   }
   const float* ap = &acc.x;
@@ -568,22 +622,13 @@ cudaError_t launch_gemm(int mode, int path, const GemmArgs& a, int max_work, int
   const int Mt = (a.M + 15) / 16;
   dim3 grid((Mt + 3) / 4, max_work);
   if (path == 0) {
-    const dim3 gm(Mt, max_work);
-    if (mode == MODE_GATE_UP) {
-      if (ntiles <= 1)
-        k_int4_mma<MODE_GATE_UP, 1><<<gm, kKS * 32, 0, st>>>(a);
-      else if (ntiles == 2)
-        k_int4_mma<MODE_GATE_UP, 2><<<gm, kKS * 32, 0, st>>>(a);
-      else
-        k_int4_mma<MODE_GATE_UP, 4><<<gm, kKS * 32, 0, st>>>(a);
-    } else {
-      if (ntiles <= 1)
-        k_int4_mma<MODE_PLAIN_F32, 1><<<gm, kKS * 32, 0, st>>>(a);
-      else if (ntiles == 2)
-        k_int4_mma<MODE_PLAIN_F32, 2><<<gm, kKS * 32, 0, st>>>(a);
-      else
-        k_int4_mma<MODE_PLAIN_F32, 4><<<gm, kKS * 32, 0, st>>>(a);
-    }
+    // K split: enough CTAs to cover the SMs when the expected work is small
+    const long tiles = (long)Mt * max_work;
+    const int ks = a.Kc >= 16 && tiles < 148 * 16 ? 4 : (a.Kc >= 16 ? 2 : 1);
+    if (mode == MODE_GATE_UP)
+      launch_mma<MODE_GATE_UP>(a, max_work, ntiles, ks, st);
+    else
+      launch_mma<MODE_PLAIN_F32>(a, max_work, ntiles, ks, st);
   } else if (path == 1) {
     if (mode == MODE_GATE_UP)
       k_int4_cc<MODE_GATE_UP, float, 4><<<grid, 128, 0, st>>>(a, awq);

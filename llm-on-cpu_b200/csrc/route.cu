@@ -200,28 +200,43 @@ __global__ void __launch_bounds__(256) k_topk(TopkArgs a) {
     __syncwarp();
   }
 
-  if (lane == 0) {
-    if (a.router == 0) {
-      double s = 0.0;
-      for (int e = 0; e < a.E; ++e) s += (double)val[e];
-      double wsum = 0.0;
-      for (int j = 0; j < a.k; ++j) wsum += (double)(float)((double)val[ids[j]] / s);
-      if (wsum < 1e-12) wsum = 1.0;
-      for (int j = 0; j < a.k; ++j) {
-        const float p = (float)((double)val[ids[j]] / s);
-        w[j] = (float)((double)p / wsum);
-      }
-    } else {
-      double wsum = 0.0;
-      for (int j = 0; j < a.k; ++j) wsum += (double)val[ids[j]];
-      if (wsum < 1e-20) wsum = 1.0;
-      for (int j = 0; j < a.k; ++j)
-        w[j] = __fmul_rn((float)((double)val[ids[j]] / wsum), a.routed_scaling);
+  // weights: lane l computes w[j] for j = l, l+32 (k <= 64); sums are warp
+  // reductions in double (the reference sums sequentially in double; the two
+  // agree except for double roundings far below fp32 resolution)
+  if (a.router == 0) {
+    double s = 0.0;
+    for (int e = lane; e < a.E; e += 32) s += (double)val[e];
+    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    float p[2];
+    double ws = 0.0;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int j = lane + 32 * h;
+      p[h] = j < a.k ? (float)((double)val[ids[j]] / s) : 0.f;  // the reference's fp32 prob
+      ws += (double)p[h];
     }
-    if (a.has_shared) {
-      ids[a.k] = a.E;
-      w[a.k] = a.shared_scale;
+    for (int o = 16; o; o >>= 1) ws += __shfl_xor_sync(0xffffffffu, ws, o);
+    if (ws < 1e-12) ws = 1.0;
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+      if (lane + 32 * h < a.k) w[lane + 32 * h] = (float)((double)p[h] / ws);
+  } else {
+    double sv[2], ws = 0.0;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int j = lane + 32 * h;
+      sv[h] = j < a.k ? (double)val[ids[j]] : 0.0;
+      ws += sv[h];
     }
+    for (int o = 16; o; o >>= 1) ws += __shfl_xor_sync(0xffffffffu, ws, o);
+    if (ws < 1e-20) ws = 1.0;
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+      if (lane + 32 * h < a.k) w[lane + 32 * h] = __fmul_rn((float)(sv[h] / ws), a.routed_scaling);
+  }
+  if (lane == 0 && a.has_shared) {
+    ids[a.k] = a.E;
+    w[a.k] = a.shared_scale;
   }
 }
 
@@ -334,7 +349,7 @@ cudaError_t launch_router_logits(const void* X, bool x_is_f32, const uint16_t* W
                                  int H, float* logits, cudaStream_t st) {
   if (T <= 0) return cudaSuccess;
   const int threads = 256;
-  if (T <= 8) {
+  if (T <= 64) {
     const long groups = (long)T * E;
     const int blocks = (int)((groups * 8 + threads - 1) / threads);
     if (x_is_f32)
