@@ -105,21 +105,6 @@ __device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t
   return d;
 }
 
-__device__ __forceinline__ uint32_t bf16x2_sub(uint32_t a, uint32_t b) {
-  __nv_bfloat162 x = *reinterpret_cast<__nv_bfloat162*>(&a);
-  const __nv_bfloat162 y = *reinterpret_cast<__nv_bfloat162*>(&b);
-  x = __hsub2(x, y);
-  return *reinterpret_cast<uint32_t*>(&x);
-}
-
-// One 32-bit fragment word -> the four A registers (bf16 pairs of q - zp).
-__device__ __forceinline__ void dequant_word(uint32_t w, uint32_t zp2, uint32_t a[4]) {
-  a[0] = bf16x2_sub(lop3_and_or(w, 0x000F000Fu, 0x43004300u), zp2);
-  a[1] = bf16x2_sub(lop3_and_or(w >> 4, 0x000F000Fu, 0x43004300u), zp2);
-  a[2] = bf16x2_sub(lop3_and_or(w >> 8, 0x000F000Fu, 0x43004300u), zp2);
-  a[3] = bf16x2_sub(lop3_and_or(w >> 12, 0x000F000Fu, 0x43004300u), zp2);
-}
-
 __device__ __forceinline__ void mma_bf16(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
   asm volatile(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
@@ -138,28 +123,40 @@ __device__ __forceinline__ uint4 ldg_nc(const uint4* p) {
 
 __device__ __forceinline__ float silu_mul(float g, float u) { return (g / (1.f + expf(-g))) * u; }
 
-// A CTA of 4 warps covers 4/KS row tiles (16 rows each) of one work item;
-// the KS warps of a tile split K into contiguous group-aligned slices.  Each
-// warp keeps a kDepth-deep ring of 128-bit weight loads in flight.  GSB is
-// the group size in 32-wide k blocks (1, 2 or 4; 0 = any multiple of 32, kept
-// with a running counter).  Slices meet in shared memory and are summed in
-// warp order (fixed, so results do not depend on scheduling).
-// grid.x = ceil(Mt * KS / 4), grid.y = work-list bound.
-// NP = 2 computes gate and up of the same rows (GATE_UP), NP = 1 one projection.
-constexpr int kWarps = 4;  // warps per CTA
-constexpr int kDepth = 4;  // weight chunks in flight per warp and projection
+// Raw fragment word -> four A registers holding bf16 (128 + q) pairs: one
+// lop3 per register (the zero point is removed after the MMA, below).
+__device__ __forceinline__ void raw_word(uint32_t w, uint32_t a[4]) {
+  a[0] = lop3_and_or(w, 0x000F000Fu, 0x43004300u);
+  a[1] = lop3_and_or(w >> 4, 0x000F000Fu, 0x43004300u);
+  a[2] = lop3_and_or(w >> 8, 0x000F000Fu, 0x43004300u);
+  a[3] = lop3_and_or(w >> 12, 0x000F000Fu, 0x43004300u);
+}
 
-template <int MODE, int NT, int GSB>
-__global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
+// Grouped INT4 GEMM on the tensor cores.  A warp owns kRT (1 or 2) consecutive
+// 16-row tiles (both projections when NP = 2) of one work item; the ks warps
+// of a CTA that share those tiles split K into contiguous group-aligned
+// slices.  Weights stream as 128-bit fragment words through a kDepth-deep
+// register ring.  The MMA consumes the biased integers (128 + q), which are
+// exact in bf16, and one extra MMA per k-step against an all-ones A fragment
+// gives xs = sum_k x (per token, shared by every row and projection).  Per
+// group the fp32 partials become
+//     AWQ:  s * (P - (128 + zp) * xs)        GPTQ: s * (P - 128 * xs) + z * xs
+// i.e. the reference's  sum_k x * (q - zp) * s  and  sum_k x * (q * s + z).
+// K slices meet in shared memory and are summed in warp order.
+// grid.x = ceil(ceil(Mt/2) * ks / 4), grid.y = work-list bound.
+constexpr int kWarps = 4;  // warps per CTA
+constexpr int kDepth = 2;  // weight chunks in flight per (warp, projection, tile)
+template <int MODE, int NT, int GSB, int kRT>
+__global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks, int awq) {
   constexpr int NP = MODE == MODE_GATE_UP ? 2 : 1;
-  __shared__ float red[kWarps][NP][NT][4][32];
+  __shared__ float red[kWarps][NP][kRT][NT][4][32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int slice = warp % ks;
-  const int rt = blockIdx.x * (kWarps / ks) + warp / ks;
+  const int u = blockIdx.x * (kWarps / ks) + warp / ks;  // tile group index
   if ((int)blockIdx.y >= *a.n_work) return;
   const int Mt = (a.M + 15) >> 4;
-  const bool live = rt < Mt;
+  const bool live = kRT * u < Mt;
   const WorkItem it = a.work[blockIdx.y];
   const ExpertDev& ex = a.experts[it.expert];
   const ProjDev* P[2];
@@ -181,50 +178,68 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
 #pragma unroll
   for (int n = 0; n < NT; ++n) {
     const int r = 8 * n + g;
-    bval[n] = r < it.nrows;
-    const int pos = it.row0 + (bval[n] ? r : 0);
+    bval[n] = r < it.nrows && n < ntc;
+    const int pos = it.row0 + (r < it.nrows ? r : 0);
     const int row = a.gather ? a.gather[pos] / a.kk : pos;
     brow[n] = reinterpret_cast<const __nv_bfloat16*>(a.B) + (size_t)row * a.ldb + 8 * t;
   }
-  // bf16 (128 + zp) in both halves; exact for zp < 128 (0x4300 encodes 128, step 1)
-  const uint32_t zp2 = (uint32_t)(0x4300 + a.zp) * 0x10001u;
+  const uint32_t ones[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};
+  const float bias = awq ? (float)(128 + a.zp) : 128.f;
 
-  float acc[NP][NT][4], tmp[NP][NT][4];
+  float acc[NP][kRT][NT][4], tmp[NP][kRT][NT][4], xs[NT][4];
 #pragma unroll
   for (int p = 0; p < NP; ++p)
 #pragma unroll
-    for (int n = 0; n < NT; ++n)
+    for (int h = 0; h < kRT; ++h)
 #pragma unroll
-      for (int r = 0; r < 4; ++r) acc[p][n][r] = tmp[p][n][r] = 0.f;
-
-  const uint4* qp[NP];
-  const __half* sp[NP];
+      for (int n = 0; n < NT; ++n)
 #pragma unroll
-  for (int p = 0; p < NP; ++p) {
-    qp[p] = P[p]->q + (size_t)(live ? rt : 0) * a.Kc * 32 + lane;
-    sp[p] = P[p]->s + (size_t)(live ? rt : 0) * a.ng * 16 + g;
-  }
+        for (int r = 0; r < 4; ++r) acc[p][h][n][r] = tmp[p][h][n][r] = 0.f;
+#pragma unroll
+  for (int n = 0; n < NT; ++n)
+#pragma unroll
+    for (int r = 0; r < 4; ++r) xs[n][r] = 0.f;
 
-  uint4 ring[NP][kDepth];
+  // tile h of the group: rt = kRT*u + h (may fall past Mt: clamp reads)
+  const int rt0 = live ? kRT * u : 0;
+  const int rt1 = live ? min(kRT * u + kRT - 1, Mt - 1) : 0;
+  const uint4* qp[NP][kRT];
+  const __half* sp[NP][kRT];
+  const __half* zp_[NP][kRT];
+#pragma unroll
+  for (int p = 0; p < NP; ++p)
+#pragma unroll
+    for (int h = 0; h < kRT; ++h) {
+      const int rt = h ? rt1 : rt0;
+      qp[p][h] = P[p]->q + (size_t)rt * a.Kc * 32 + lane;
+      sp[p][h] = P[p]->s + (size_t)rt * a.ng * 16 + g;
+      zp_[p][h] = P[p]->z ? P[p]->z + (size_t)rt * a.ng * 16 + g : nullptr;
+    }
+
+  uint4 ring[NP][kRT][kDepth];
 #pragma unroll
   for (int d = 0; d < kDepth; ++d)
 #pragma unroll
     for (int p = 0; p < NP; ++p)
-      if (c0 + d < c1) ring[p][d] = ldg_nc(qp[p] + (size_t)(c0 + d) * 32);
+#pragma unroll
+      for (int h = 0; h < kRT; ++h)
+        if (c0 + d < c1) ring[p][h][d] = ldg_nc(qp[p][h] + (size_t)(c0 + d) * 32);
 
-  int grp = (c0 * 2) / gsb;                  // group of the first block
-  int left = gsb - ((c0 * 2) % gsb);         // blocks left in that group (GSB == 0 only)
+  int grp = (c0 * 2) / gsb;           // group of the first block
+  int left = gsb - ((c0 * 2) % gsb);  // blocks left in that group (GSB == 0 only)
   for (int cb = c0; cb < c1; cb += kDepth) {
 #pragma unroll
     for (int d = 0; d < kDepth; ++d) {
       const int c = cb + d;
       if (c >= c1) break;
-      uint4 qw[NP];
+      uint4 qw[NP][kRT];
 #pragma unroll
-      for (int p = 0; p < NP; ++p) {
-        qw[p] = ring[p][d];
-        if (c + kDepth < c1) ring[p][d] = ldg_nc(qp[p] + (size_t)(c + kDepth) * 32);
-      }
+      for (int p = 0; p < NP; ++p)
+#pragma unroll
+        for (int h = 0; h < kRT; ++h) {
+          qw[p][h] = ring[p][h][d];
+          if (c + kDepth < c1) ring[p][h][d] = ldg_nc(qp[p][h] + (size_t)(c + kDepth) * 32);
+        }
 #pragma unroll
       for (int kb = 0; kb < 2; ++kb) {
         const int blk = 2 * c + kb;
@@ -234,22 +249,29 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
 #pragma unroll
         for (int n = 0; n < NT; ++n) {
           bv[n] = make_uint4(0, 0, 0, 0);
-          if (n < ntc && bval[n]) bv[n] = *reinterpret_cast<const uint4*>(brow[n] + k32);
+          if (bval[n]) bv[n] = *reinterpret_cast<const uint4*>(brow[n] + k32);
         }
 #pragma unroll
         for (int kt = 0; kt < 2; ++kt) {
 #pragma unroll
-          for (int p = 0; p < NP; ++p) {
-            const int wi = kb * 2 + kt;
-            const uint32_t wd = wi == 0 ? qw[p].x : wi == 1 ? qw[p].y : wi == 2 ? qw[p].z : qw[p].w;
-            uint32_t af[4];
-            dequant_word(wd, zp2, af);
+          for (int n = 0; n < NT; ++n)
+            if (n < ntc) mma_bf16(xs[n], ones, kt ? bv[n].z : bv[n].x, kt ? bv[n].w : bv[n].y);
 #pragma unroll
-            for (int n = 0; n < NT; ++n)
-              if (n < ntc) mma_bf16(tmp[p][n], af, kt ? bv[n].z : bv[n].x, kt ? bv[n].w : bv[n].y);
-          }
+          for (int p = 0; p < NP; ++p)
+#pragma unroll
+            for (int h = 0; h < kRT; ++h) {
+              const int wi = kb * 2 + kt;
+              const uint4& q4 = qw[p][h];
+              const uint32_t wd = wi == 0 ? q4.x : wi == 1 ? q4.y : wi == 2 ? q4.z : q4.w;
+              uint32_t af[4];
+              raw_word(wd, af);
+#pragma unroll
+              for (int n = 0; n < NT; ++n)
+                if (n < ntc)
+                  mma_bf16(tmp[p][h][n], af, kt ? bv[n].z : bv[n].x, kt ? bv[n].w : bv[n].y);
+            }
         }
-        // end of a group (or of the warp's slice / of K): scale into acc
+        // end of a group (or of the warp's slice / of K): fold into acc
         bool gend;
         if (GSB == 1) gend = true;
         else if (GSB == 2) gend = kb == 1 || blk == kb_last;
@@ -257,17 +279,31 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
         else gend = (--left == 0) || blk == kb_last || (kb == 1 && c + 1 == c1);
         if (gend) {
 #pragma unroll
-          for (int p = 0; p < NP; ++p) {
-            const float s0 = __half2float(sp[p][grp * 16]), s1 = __half2float(sp[p][grp * 16 + 8]);
+          for (int p = 0; p < NP; ++p)
 #pragma unroll
-            for (int n = 0; n < NT; ++n) {
-              acc[p][n][0] = __fmaf_rn(tmp[p][n][0], s0, acc[p][n][0]);
-              acc[p][n][1] = __fmaf_rn(tmp[p][n][1], s0, acc[p][n][1]);
-              acc[p][n][2] = __fmaf_rn(tmp[p][n][2], s1, acc[p][n][2]);
-              acc[p][n][3] = __fmaf_rn(tmp[p][n][3], s1, acc[p][n][3]);
-              tmp[p][n][0] = tmp[p][n][1] = tmp[p][n][2] = tmp[p][n][3] = 0.f;
+            for (int h = 0; h < kRT; ++h) {
+              const float s0 = __half2float(sp[p][h][grp * 16]);
+              const float s1 = __half2float(sp[p][h][grp * 16 + 8]);
+              float z0 = 0.f, z1 = 0.f;
+              if (!awq && zp_[p][h]) {
+                z0 = __half2float(zp_[p][h][grp * 16]);
+                z1 = __half2float(zp_[p][h][grp * 16 + 8]);
+              }
+#pragma unroll
+              for (int n = 0; n < NT; ++n)
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                  const float sc = r < 2 ? s0 : s1;
+                  const float v = __fmaf_rn(-bias, xs[n][r], tmp[p][h][n][r]);  // sum x*(q - zp)
+                  acc[p][h][n][r] = __fmaf_rn(v, sc, acc[p][h][n][r]);
+                  if (!awq) acc[p][h][n][r] = __fmaf_rn(r < 2 ? z0 : z1, xs[n][r], acc[p][h][n][r]);
+                  tmp[p][h][n][r] = 0.f;
+                }
             }
-          }
+#pragma unroll
+          for (int n = 0; n < NT; ++n)
+#pragma unroll
+            for (int r = 0; r < 4; ++r) xs[n][r] = 0.f;
           ++grp;
           if (GSB == 0) left = gsb;
         }
@@ -279,65 +315,76 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
 #pragma unroll
     for (int p = 0; p < NP; ++p)
 #pragma unroll
-      for (int n = 0; n < NT; ++n)
+      for (int h = 0; h < kRT; ++h)
 #pragma unroll
-        for (int r = 0; r < 4; ++r) red[warp][p][n][r][lane] = acc[p][n][r];
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+          for (int r = 0; r < 4; ++r) red[warp][p][h][n][r][lane] = acc[p][h][n][r];
     __syncthreads();
     if (slice != 0) return;
 #pragma unroll
     for (int p = 0; p < NP; ++p)
 #pragma unroll
-      for (int n = 0; n < NT; ++n)
+      for (int h = 0; h < kRT; ++h)
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
-          float v = red[warp][p][n][r][lane];
-          for (int w = 1; w < ks; ++w) v += red[warp + w][p][n][r][lane];
-          acc[p][n][r] = v;
-        }
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            float v = red[warp][p][h][n][r][lane];
+            for (int w = 1; w < ks; ++w) v += red[warp + w][p][h][n][r][lane];
+            acc[p][h][n][r] = v;
+          }
   }
   if (!live) return;
 
-  // C fragment (row g / g+8, col 2t / 2t+1) of each N-tile
-  const int m0 = rt * 16 + g, m1 = m0 + 8;
+  // C fragment (row g / g+8, col 2t / 2t+1) of each N-tile of each tile
 #pragma unroll
-  for (int n = 0; n < NT; ++n) {
-    if (n >= ntc) continue;
+  for (int h = 0; h < kRT; ++h) {
+    const int rt = kRT * u + h;
+    if (rt >= Mt) continue;
+    const int m0 = rt * 16 + g, m1 = m0 + 8;
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const int col = 8 * n + 2 * t + (r & 1);
-      const int m = (r < 2) ? m0 : m1;
-      if (col >= it.nrows || m >= a.M) continue;
-      const size_t o = (size_t)(it.row0 + col) * a.ldo + m;
-      float v = acc[0][n][r];
-      if (!isfinite(v)) v = 0.f;  // non-finite -> 0, as every reference GEMV does
-      if (MODE == MODE_GATE_UP) {
-        float u = acc[NP - 1][n][r];
-        if (!isfinite(u)) u = 0.f;
-        reinterpret_cast<__nv_bfloat16*>(a.out)[o] = __float2bfloat16_rn(silu_mul(v, u));
-      } else {
-        reinterpret_cast<float*>(a.out)[o] = v;
+    for (int n = 0; n < NT; ++n) {
+      if (n >= ntc) continue;
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int col = 8 * n + 2 * t + (r & 1);
+        const int m = (r < 2) ? m0 : m1;
+        if (col >= it.nrows || m >= a.M) continue;
+        const size_t o = (size_t)(it.row0 + col) * a.ldo + m;
+        float v = acc[0][h][n][r];
+        if (!isfinite(v)) v = 0.f;  // non-finite -> 0, as every reference GEMV does
+        if (MODE == MODE_GATE_UP) {
+          float uu = acc[NP - 1][h][n][r];
+          if (!isfinite(uu)) uu = 0.f;
+          reinterpret_cast<__nv_bfloat16*>(a.out)[o] = __float2bfloat16_rn(silu_mul(v, uu));
+        } else {
+          reinterpret_cast<float*>(a.out)[o] = v;
+        }
       }
     }
   }
 }
 
 template <int MODE, int NT>
-static void launch_mma_gs(const GemmArgs& a, int max_work, int ks, cudaStream_t st) {
+static void launch_mma_gs(const GemmArgs& a, int max_work, int ks, int awq, cudaStream_t st) {
+  constexpr int RT = NT >= 4 ? 1 : 2;
   const int Mt = (a.M + 15) / 16;
-  const dim3 grid((Mt * ks + kWarps - 1) / kWarps, max_work);
+  const int groups = (Mt + RT - 1) / RT;
+  const dim3 grid((groups * ks + kWarps - 1) / kWarps, max_work);
   switch (a.gs) {
-    case 32: k_int4_mma<MODE, NT, 1><<<grid, kWarps * 32, 0, st>>>(a, ks); break;
-    case 64: k_int4_mma<MODE, NT, 2><<<grid, kWarps * 32, 0, st>>>(a, ks); break;
-    case 128: k_int4_mma<MODE, NT, 4><<<grid, kWarps * 32, 0, st>>>(a, ks); break;
-    default: k_int4_mma<MODE, NT, 0><<<grid, kWarps * 32, 0, st>>>(a, ks); break;
+    case 32: k_int4_mma<MODE, NT, 1, RT><<<grid, kWarps * 32, 0, st>>>(a, ks, awq); break;
+    case 64: k_int4_mma<MODE, NT, 2, RT><<<grid, kWarps * 32, 0, st>>>(a, ks, awq); break;
+    case 128: k_int4_mma<MODE, NT, 4, RT><<<grid, kWarps * 32, 0, st>>>(a, ks, awq); break;
+    default: k_int4_mma<MODE, NT, 0, RT><<<grid, kWarps * 32, 0, st>>>(a, ks, awq); break;
   }
 }
 
 template <int MODE>
-static void launch_mma(const GemmArgs& a, int max_work, int ntiles, int ks, cudaStream_t st) {
-  if (ntiles <= 1) launch_mma_gs<MODE, 1>(a, max_work, ks, st);
-  else if (ntiles == 2) launch_mma_gs<MODE, 2>(a, max_work, ks, st);
-  else launch_mma_gs<MODE, 4>(a, max_work, ks, st);
+static void launch_mma(const GemmArgs& a, int max_work, int ntiles, int ks, int awq, cudaStream_t st) {
+  if (ntiles <= 1) launch_mma_gs<MODE, 1>(a, max_work, ks, awq, st);
+  else if (ntiles == 2) launch_mma_gs<MODE, 2>(a, max_work, ks, awq, st);
+  else launch_mma_gs<MODE, 4>(a, max_work, ks, awq, st);
 }
 
 // ------------------------------------------------------ CUDA-core fp32 GEMV
@@ -622,13 +669,13 @@ cudaError_t launch_gemm(int mode, int path, const GemmArgs& a, int max_work, int
   const int Mt = (a.M + 15) / 16;
   dim3 grid((Mt + 3) / 4, max_work);
   if (path == 0) {
-    // K split: enough CTAs to cover the SMs when the expected work is small
-    const long tiles = (long)Mt * max_work;
-    const int ks = a.Kc >= 16 && tiles < 148 * 16 ? 4 : (a.Kc >= 16 ? 2 : 1);
+    // K split: enough warps to cover the SMs when the expected work is small
+    const long units = (long)((Mt + 1) / 2) * max_work;
+    const int ks = a.Kc >= 16 && units < 148 * 32 ? 4 : (a.Kc >= 16 ? 2 : 1);
     if (mode == MODE_GATE_UP)
-      launch_mma<MODE_GATE_UP>(a, max_work, ntiles, ks, st);
+      launch_mma<MODE_GATE_UP>(a, max_work, ntiles, ks, awq, st);
     else
-      launch_mma<MODE_PLAIN_F32>(a, max_work, ntiles, ks, st);
+      launch_mma<MODE_PLAIN_F32>(a, max_work, ntiles, ks, awq, st);
   } else if (path == 1) {
     if (mode == MODE_GATE_UP)
       k_int4_cc<MODE_GATE_UP, float, 4><<<grid, 128, 0, st>>>(a, awq);

@@ -937,7 +937,7 @@ llmoc_status llmoc_moe_forward(const llmoc_moe_layer* L, const uint16_t* X, int 
   if (rc != LLMOC_OK) return rc;
   const int H = L->d.hidden, I = L->d.inter;
   const bool awq = L->d.scheme == LLMOC_SCHEME_AWQ_SYM;
-  const int path = awq ? 0 : 2;
+  const int path = 0;  // tensor cores for both schemes (GPTQ zeros use the per-token sums)
   const int ntiles = chunk_rows(T) / 8;
   GemmArgs a{};
   a.experts = L->table;
