@@ -145,7 +145,7 @@ __device__ __forceinline__ void raw_word(uint32_t w, uint32_t a[4]) {
 // K slices meet in shared memory and are summed in warp order.
 // grid.x = ceil(ceil(Mt/2) * ks / 4), grid.y = work-list bound.
 constexpr int kWarps = 4;  // warps per CTA
-constexpr int kDepth = 2;  // weight chunks in flight per (warp, projection, tile)
+constexpr int kDepth = 4;  // weight chunks in flight per (warp, projection, tile)
 template <int MODE, int NT, int GSB, int kRT>
 __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks, int awq) {
   constexpr int NP = MODE == MODE_GATE_UP ? 2 : 1;
@@ -255,7 +255,7 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks, in
         for (int kt = 0; kt < 2; ++kt) {
 #pragma unroll
           for (int n = 0; n < NT; ++n)
-            if (n < ntc) mma_bf16(xs[n], ones, kt ? bv[n].z : bv[n].x, kt ? bv[n].w : bv[n].y);
+            if (NT == 1 || n < ntc) mma_bf16(xs[n], ones, kt ? bv[n].z : bv[n].x, kt ? bv[n].w : bv[n].y);
 #pragma unroll
           for (int p = 0; p < NP; ++p)
 #pragma unroll
@@ -267,7 +267,7 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks, in
               raw_word(wd, af);
 #pragma unroll
               for (int n = 0; n < NT; ++n)
-                if (n < ntc)
+                if (NT == 1 || n < ntc)
                   mma_bf16(tmp[p][h][n], af, kt ? bv[n].z : bv[n].x, kt ? bv[n].w : bv[n].y);
             }
         }
@@ -368,7 +368,7 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks, in
 
 template <int MODE, int NT>
 static void launch_mma_gs(const GemmArgs& a, int max_work, int ks, int awq, cudaStream_t st) {
-  constexpr int RT = NT >= 4 ? 1 : 2;
+  constexpr int RT = 1;
   const int Mt = (a.M + 15) / 16;
   const int groups = (Mt + RT - 1) / RT;
   const dim3 grid((groups * ks + kWarps - 1) / kWarps, max_work);

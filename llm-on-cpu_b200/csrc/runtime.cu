@@ -331,9 +331,9 @@ struct llmoc_moe_layer {
 
 namespace {
 
-// Rows per work item (tensor-core N tiles of 8): small batches use narrower
-// items so the kernel variant carries fewer accumulators.
-int chunk_rows(int T) { return T <= 8 ? 8 : (T <= 128 ? 16 : kChunkRows); }
+// Rows per work item (tensor-core N tiles of 8): decode-size batches use
+// one N tile per item, so the kernel variant has no per-tile branches.
+int chunk_rows(int T) { return T <= 128 ? 8 : kChunkRows; }
 
 struct WsLayout {
   size_t logits, ids, weights, offsets, sorted, inverse, work, n_work, n_active, mid, partial, total;
