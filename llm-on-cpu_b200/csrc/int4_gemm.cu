@@ -123,6 +123,8 @@ __device__ __forceinline__ uint4 ldg_nc(const uint4* p) {
 
 __device__ __forceinline__ float silu_mul(float g, float u) { return (g / (1.f + expf(-g))) * u; }
 
+constexpr int kWarps = 4;  // warps per CTA of the grouped GEMM kernels
+
 // Raw fragment word -> four A registers holding bf16 (128 + q) pairs: one
 // lop3 per register (the zero point is removed after the MMA, below).
 __device__ __forceinline__ void raw_word(uint32_t w, uint32_t a[4]) {
@@ -132,31 +134,32 @@ __device__ __forceinline__ void raw_word(uint32_t w, uint32_t a[4]) {
   a[3] = lop3_and_or(w >> 12, 0x000F000Fu, 0x43004300u);
 }
 
-// Grouped INT4 GEMM on the tensor cores.  A warp owns kRT (1 or 2) consecutive
-// 16-row tiles (both projections when NP = 2) of one work item; the ks warps
-// of a CTA that share those tiles split K into contiguous group-aligned
-// slices.  Weights stream as 128-bit fragment words through a kDepth-deep
-// register ring.  The MMA consumes the biased integers (128 + q), which are
-// exact in bf16, and one extra MMA per k-step against an all-ones A fragment
-// gives xs = sum_k x (per token, shared by every row and projection).  Per
-// group the fp32 partials become
+// Grouped INT4 GEMM on the tensor cores.  A warp owns one 16-row tile (both
+// projections when NP = 2) of one work item; the ks warps of a CTA that
+// share the tile split K into contiguous slices of 128-wide steps (K % 128 ==
+// 0, group size 32/64/128, so every group end sits at a fixed place of a
+// step).  Weights stream as 128-bit fragment words through a kRing-step
+// register ring.  The MMA consumes the biased integers (128 + q), exact in
+// bf16, and one extra MMA per k16 against an all-ones A fragment gives
+// xs = sum_k x per token (shared by both projections).  Per group the fp32
+// partials become
 //     AWQ:  s * (P - (128 + zp) * xs)        GPTQ: s * (P - 128 * xs) + z * xs
 // i.e. the reference's  sum_k x * (q - zp) * s  and  sum_k x * (q * s + z).
 // K slices meet in shared memory and are summed in warp order.
-// grid.x = ceil(ceil(Mt/2) * ks / 4), grid.y = work-list bound.
-constexpr int kWarps = 4;  // warps per CTA
-constexpr int kDepth = 4;  // weight chunks in flight per (warp, projection, tile)
-template <int MODE, int NT, int GSB, int kRT>
-__global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks, int awq) {
+// grid.x = ceil(Mt * ks / 4), grid.y = work-list bound.
+constexpr int kRing = 2;  // 128-wide K steps of weights in flight per warp
+
+template <int MODE, int NT, int GSB, bool AWQ>
+__global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
   constexpr int NP = MODE == MODE_GATE_UP ? 2 : 1;
-  __shared__ float red[kWarps][NP][kRT][NT][4][32];
+  __shared__ float red[kWarps][NP][NT][4][32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int slice = warp % ks;
-  const int u = blockIdx.x * (kWarps / ks) + warp / ks;  // tile group index
+  const int rt = blockIdx.x * (kWarps / ks) + warp / ks;
   if ((int)blockIdx.y >= *a.n_work) return;
   const int Mt = (a.M + 15) >> 4;
-  const bool live = kRT * u < Mt;
+  const bool live = rt < Mt;
   const WorkItem it = a.work[blockIdx.y];
   const ExpertDev& ex = a.experts[it.expert];
   const ProjDev* P[2];
@@ -164,16 +167,12 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks, in
   P[1] = &ex.up;
   const int ntc = (it.nrows + 7) >> 3;
 
-  // this warp's chunk range [c0, c1), aligned to whole groups when possible
-  const int gsb = GSB ? GSB : (a.gs >> 5);
-  const int align = gsb >= 2 ? gsb >> 1 : 1;  // chunks per group (>= 1)
-  int per = (a.Kc + ks - 1) / ks;
-  per = (per + align - 1) / align * align;
-  const int c0 = live ? min(a.Kc, slice * per) : 0;
-  const int c1 = live ? min(a.Kc, c0 + per) : 0;
-  const int kb_last = (a.K >> 5) - 1;  // index of the last valid 32-wide block
+  const int nsteps = a.K >> 7;
+  const int per = (nsteps + ks - 1) / ks;
+  const int s0 = live ? min(nsteps, slice * per) : 0;
+  const int s1 = live ? min(nsteps, s0 + per) : 0;
 
-  const __nv_bfloat16* brow[NT];
+  const uint4* bq[NT];  // activation pointer of this lane (row 8n+g, k offset 8t)
   bool bval[NT];
 #pragma unroll
   for (int n = 0; n < NT; ++n) {
@@ -181,132 +180,126 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks, in
     bval[n] = r < it.nrows && n < ntc;
     const int pos = it.row0 + (r < it.nrows ? r : 0);
     const int row = a.gather ? a.gather[pos] / a.kk : pos;
-    brow[n] = reinterpret_cast<const __nv_bfloat16*>(a.B) + (size_t)row * a.ldb + 8 * t;
+    bq[n] = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.B) +
+                                           (size_t)row * a.ldb + 8 * t + s0 * 128);
   }
   const uint32_t ones[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};
-  const float bias = awq ? (float)(128 + a.zp) : 128.f;
+  const float bias = AWQ ? (float)(128 + a.zp) : 128.f;
 
-  float acc[NP][kRT][NT][4], tmp[NP][kRT][NT][4], xs[NT][4];
+  float acc[NP][NT][4], tmp[NP][NT][4], xs[NT][4];
 #pragma unroll
   for (int p = 0; p < NP; ++p)
 #pragma unroll
-    for (int h = 0; h < kRT; ++h)
+    for (int n = 0; n < NT; ++n)
 #pragma unroll
-      for (int n = 0; n < NT; ++n)
-#pragma unroll
-        for (int r = 0; r < 4; ++r) acc[p][h][n][r] = tmp[p][h][n][r] = 0.f;
+      for (int r = 0; r < 4; ++r) acc[p][n][r] = tmp[p][n][r] = 0.f;
 #pragma unroll
   for (int n = 0; n < NT; ++n)
 #pragma unroll
     for (int r = 0; r < 4; ++r) xs[n][r] = 0.f;
 
-  // tile h of the group: rt = kRT*u + h (may fall past Mt: clamp reads)
-  const int rt0 = live ? kRT * u : 0;
-  const int rt1 = live ? min(kRT * u + kRT - 1, Mt - 1) : 0;
-  const uint4* qp[NP][kRT];
-  const __half* sp[NP][kRT];
-  const __half* zp_[NP][kRT];
+  const int rtc = live ? rt : 0;
+  const uint4* wq[NP];   // next step to load (two 512-B chunks per step)
+  const __half* sq[NP];  // scales of this tile, first group of the slice
+  const __half* zq[NP];
 #pragma unroll
-  for (int p = 0; p < NP; ++p)
+  for (int p = 0; p < NP; ++p) {
+    wq[p] = P[p]->q + ((size_t)rtc * a.Kc + 2 * s0) * 32 + lane;
+    sq[p] = P[p]->s + ((size_t)rtc * a.ng + (s0 * 4) / GSB) * 16 + g;
+    zq[p] = AWQ ? nullptr : P[p]->z + ((size_t)rtc * a.ng + (s0 * 4) / GSB) * 16 + g;
+  }
+  const int nst = s1 - s0;
+  uint4 ring[NP][kRing][2];
 #pragma unroll
-    for (int h = 0; h < kRT; ++h) {
-      const int rt = h ? rt1 : rt0;
-      qp[p][h] = P[p]->q + (size_t)rt * a.Kc * 32 + lane;
-      sp[p][h] = P[p]->s + (size_t)rt * a.ng * 16 + g;
-      zp_[p][h] = P[p]->z ? P[p]->z + (size_t)rt * a.ng * 16 + g : nullptr;
-    }
-
-  uint4 ring[NP][kRT][kDepth];
-#pragma unroll
-  for (int d = 0; d < kDepth; ++d)
+  for (int d = 0; d < kRing; ++d)
 #pragma unroll
     for (int p = 0; p < NP; ++p)
-#pragma unroll
-      for (int h = 0; h < kRT; ++h)
-        if (c0 + d < c1) ring[p][h][d] = ldg_nc(qp[p][h] + (size_t)(c0 + d) * 32);
+      if (d < nst) {
+        ring[p][d][0] = ldg_nc(wq[p]);
+        ring[p][d][1] = ldg_nc(wq[p] + 32);
+        wq[p] += 64;
+      }
 
-  int grp = (c0 * 2) / gsb;           // group of the first block
-  int left = gsb - ((c0 * 2) % gsb);  // blocks left in that group (GSB == 0 only)
-  for (int cb = c0; cb < c1; cb += kDepth) {
+  for (int i0 = 0; i0 < nst; i0 += kRing) {
 #pragma unroll
-    for (int d = 0; d < kDepth; ++d) {
-      const int c = cb + d;
-      if (c >= c1) break;
-      uint4 qw[NP][kRT];
+    for (int d = 0; d < kRing; ++d) {
+      if (i0 + d >= nst) break;
+      // activations of this 128-wide step: 4 blocks of 8 bf16 per lane
+      uint4 bv[NT][4];
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+#pragma unroll
+        for (int b = 0; b < 4; ++b) bv[n][b] = bval[n] ? bq[n][b * 4] : make_uint4(0, 0, 0, 0);
+        bq[n] += 16;
+      }
+      // scales (and zeros) of the groups in this step
+      constexpr int NG = GSB == 4 ? 1 : (GSB == 2 ? 2 : 4);  // groups per step
+      float sc[NP][NG][2], zz[NP][NG][2];
 #pragma unroll
       for (int p = 0; p < NP; ++p)
 #pragma unroll
-        for (int h = 0; h < kRT; ++h) {
-          qw[p][h] = ring[p][h][d];
-          if (c + kDepth < c1) ring[p][h][d] = ldg_nc(qp[p][h] + (size_t)(c + kDepth) * 32);
+        for (int q = 0; q < NG; ++q) {
+          sc[p][q][0] = __half2float(sq[p][q * 16]);
+          sc[p][q][1] = __half2float(sq[p][q * 16 + 8]);
+          if (!AWQ) {
+            zz[p][q][0] = __half2float(zq[p][q * 16]);
+            zz[p][q][1] = __half2float(zq[p][q * 16 + 8]);
+          }
         }
 #pragma unroll
-      for (int kb = 0; kb < 2; ++kb) {
-        const int blk = 2 * c + kb;
-        if (blk > kb_last) break;
-        const int k32 = blk * 32;
-        uint4 bv[NT];
+      for (int p = 0; p < NP; ++p) {
+        sq[p] += NG * 16;
+        if (!AWQ) zq[p] += NG * 16;
+      }
 #pragma unroll
-        for (int n = 0; n < NT; ++n) {
-          bv[n] = make_uint4(0, 0, 0, 0);
-          if (bval[n]) bv[n] = *reinterpret_cast<const uint4*>(brow[n] + k32);
-        }
+      for (int b = 0; b < 4; ++b) {  // 32-wide block b of the step
 #pragma unroll
         for (int kt = 0; kt < 2; ++kt) {
 #pragma unroll
           for (int n = 0; n < NT; ++n)
-            if (NT == 1 || n < ntc) mma_bf16(xs[n], ones, kt ? bv[n].z : bv[n].x, kt ? bv[n].w : bv[n].y);
+            if (NT == 1 || n < ntc)
+              mma_bf16(xs[n], ones, kt ? bv[n][b].z : bv[n][b].x, kt ? bv[n][b].w : bv[n][b].y);
 #pragma unroll
-          for (int p = 0; p < NP; ++p)
+          for (int p = 0; p < NP; ++p) {
+            const uint4& q4 = ring[p][d][b >> 1];
+            const int wi = (b & 1) * 2 + kt;
+            const uint32_t wd = wi == 0 ? q4.x : wi == 1 ? q4.y : wi == 2 ? q4.z : q4.w;
+            uint32_t af[4];
+            raw_word(wd, af);
 #pragma unroll
-            for (int h = 0; h < kRT; ++h) {
-              const int wi = kb * 2 + kt;
-              const uint4& q4 = qw[p][h];
-              const uint32_t wd = wi == 0 ? q4.x : wi == 1 ? q4.y : wi == 2 ? q4.z : q4.w;
-              uint32_t af[4];
-              raw_word(wd, af);
-#pragma unroll
-              for (int n = 0; n < NT; ++n)
-                if (NT == 1 || n < ntc)
-                  mma_bf16(tmp[p][h][n], af, kt ? bv[n].z : bv[n].x, kt ? bv[n].w : bv[n].y);
-            }
+            for (int n = 0; n < NT; ++n)
+              if (NT == 1 || n < ntc)
+                mma_bf16(tmp[p][n], af, kt ? bv[n][b].z : bv[n][b].x, kt ? bv[n][b].w : bv[n][b].y);
+          }
         }
-        // end of a group (or of the warp's slice / of K): fold into acc
-        bool gend;
-        if (GSB == 1) gend = true;
-        else if (GSB == 2) gend = kb == 1 || blk == kb_last;
-        else if (GSB == 4) gend = (kb == 1 && (c & 1)) || blk == kb_last || (kb == 1 && c + 1 == c1);
-        else gend = (--left == 0) || blk == kb_last || (kb == 1 && c + 1 == c1);
-        if (gend) {
+        if ((b + 1) % GSB == 0) {  // group end
+          const int q = b / GSB;
 #pragma unroll
           for (int p = 0; p < NP; ++p)
 #pragma unroll
-            for (int h = 0; h < kRT; ++h) {
-              const float s0 = __half2float(sp[p][h][grp * 16]);
-              const float s1 = __half2float(sp[p][h][grp * 16 + 8]);
-              float z0 = 0.f, z1 = 0.f;
-              if (!awq && zp_[p][h]) {
-                z0 = __half2float(zp_[p][h][grp * 16]);
-                z1 = __half2float(zp_[p][h][grp * 16 + 8]);
+            for (int n = 0; n < NT; ++n)
+#pragma unroll
+              for (int r = 0; r < 4; ++r) {
+                const float v = __fmaf_rn(-bias, xs[n][r], tmp[p][n][r]);  // sum x*(q - zp)
+                acc[p][n][r] = __fmaf_rn(v, sc[p][q][r >> 1], acc[p][n][r]);
+                if (!AWQ) acc[p][n][r] = __fmaf_rn(zz[p][q][r >> 1], xs[n][r], acc[p][n][r]);
+                tmp[p][n][r] = 0.f;
               }
-#pragma unroll
-              for (int n = 0; n < NT; ++n)
-#pragma unroll
-                for (int r = 0; r < 4; ++r) {
-                  const float sc = r < 2 ? s0 : s1;
-                  const float v = __fmaf_rn(-bias, xs[n][r], tmp[p][h][n][r]);  // sum x*(q - zp)
-                  acc[p][h][n][r] = __fmaf_rn(v, sc, acc[p][h][n][r]);
-                  if (!awq) acc[p][h][n][r] = __fmaf_rn(r < 2 ? z0 : z1, xs[n][r], acc[p][h][n][r]);
-                  tmp[p][h][n][r] = 0.f;
-                }
-            }
 #pragma unroll
           for (int n = 0; n < NT; ++n)
 #pragma unroll
             for (int r = 0; r < 4; ++r) xs[n][r] = 0.f;
-          ++grp;
-          if (GSB == 0) left = gsb;
         }
+      }
+      // refill this ring slot with the step kRing ahead (clamped: a harmless
+      // re-load of the last step when none is left)
+      const bool more = i0 + d + kRing < nst;
+#pragma unroll
+      for (int p = 0; p < NP; ++p) {
+        const uint4* src = more ? wq[p] : wq[p] - 64;
+        ring[p][d][0] = ldg_nc(src);
+        ring[p][d][1] = ldg_nc(src + 32);
+        if (more) wq[p] += 64;
       }
     }
   }
@@ -315,76 +308,68 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks, in
 #pragma unroll
     for (int p = 0; p < NP; ++p)
 #pragma unroll
-      for (int h = 0; h < kRT; ++h)
+      for (int n = 0; n < NT; ++n)
 #pragma unroll
-        for (int n = 0; n < NT; ++n)
-#pragma unroll
-          for (int r = 0; r < 4; ++r) red[warp][p][h][n][r][lane] = acc[p][h][n][r];
+        for (int r = 0; r < 4; ++r) red[warp][p][n][r][lane] = acc[p][n][r];
     __syncthreads();
     if (slice != 0) return;
 #pragma unroll
     for (int p = 0; p < NP; ++p)
 #pragma unroll
-      for (int h = 0; h < kRT; ++h)
+      for (int n = 0; n < NT; ++n)
 #pragma unroll
-        for (int n = 0; n < NT; ++n)
-#pragma unroll
-          for (int r = 0; r < 4; ++r) {
-            float v = red[warp][p][h][n][r][lane];
-            for (int w = 1; w < ks; ++w) v += red[warp + w][p][h][n][r][lane];
-            acc[p][h][n][r] = v;
-          }
+        for (int r = 0; r < 4; ++r) {
+          float v = red[warp][p][n][r][lane];
+          for (int w = 1; w < ks; ++w) v += red[warp + w][p][n][r][lane];
+          acc[p][n][r] = v;
+        }
   }
   if (!live) return;
 
-  // C fragment (row g / g+8, col 2t / 2t+1) of each N-tile of each tile
+  // C fragment (row g / g+8, col 2t / 2t+1) of each N-tile
+  const int m0 = rt * 16 + g, m1 = m0 + 8;
 #pragma unroll
-  for (int h = 0; h < kRT; ++h) {
-    const int rt = kRT * u + h;
-    if (rt >= Mt) continue;
-    const int m0 = rt * 16 + g, m1 = m0 + 8;
+  for (int n = 0; n < NT; ++n) {
+    if (n >= ntc) continue;
 #pragma unroll
-    for (int n = 0; n < NT; ++n) {
-      if (n >= ntc) continue;
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const int col = 8 * n + 2 * t + (r & 1);
-        const int m = (r < 2) ? m0 : m1;
-        if (col >= it.nrows || m >= a.M) continue;
-        const size_t o = (size_t)(it.row0 + col) * a.ldo + m;
-        float v = acc[0][h][n][r];
-        if (!isfinite(v)) v = 0.f;  // non-finite -> 0, as every reference GEMV does
-        if (MODE == MODE_GATE_UP) {
-          float uu = acc[NP - 1][h][n][r];
-          if (!isfinite(uu)) uu = 0.f;
-          reinterpret_cast<__nv_bfloat16*>(a.out)[o] = __float2bfloat16_rn(silu_mul(v, uu));
-        } else {
-          reinterpret_cast<float*>(a.out)[o] = v;
-        }
+    for (int r = 0; r < 4; ++r) {
+      const int col = 8 * n + 2 * t + (r & 1);
+      const int m = (r < 2) ? m0 : m1;
+      if (col >= it.nrows || m >= a.M) continue;
+      const size_t o = (size_t)(it.row0 + col) * a.ldo + m;
+      float v = acc[0][n][r];
+      if (!isfinite(v)) v = 0.f;  // non-finite -> 0, as every reference GEMV does
+      if (MODE == MODE_GATE_UP) {
+        float uu = acc[NP - 1][n][r];
+        if (!isfinite(uu)) uu = 0.f;
+        reinterpret_cast<__nv_bfloat16*>(a.out)[o] = __float2bfloat16_rn(silu_mul(v, uu));
+      } else {
+        reinterpret_cast<float*>(a.out)[o] = v;
       }
     }
   }
 }
 
-template <int MODE, int NT>
-static void launch_mma_gs(const GemmArgs& a, int max_work, int ks, int awq, cudaStream_t st) {
-  constexpr int RT = 1;
+template <int MODE, int NT, bool AWQ>
+static void launch_mma_gs(const GemmArgs& a, int max_work, int ks, cudaStream_t st) {
   const int Mt = (a.M + 15) / 16;
-  const int groups = (Mt + RT - 1) / RT;
-  const dim3 grid((groups * ks + kWarps - 1) / kWarps, max_work);
+  const dim3 grid((Mt * ks + kWarps - 1) / kWarps, max_work);
   switch (a.gs) {
-    case 32: k_int4_mma<MODE, NT, 1, RT><<<grid, kWarps * 32, 0, st>>>(a, ks, awq); break;
-    case 64: k_int4_mma<MODE, NT, 2, RT><<<grid, kWarps * 32, 0, st>>>(a, ks, awq); break;
-    case 128: k_int4_mma<MODE, NT, 4, RT><<<grid, kWarps * 32, 0, st>>>(a, ks, awq); break;
-    default: k_int4_mma<MODE, NT, 0, RT><<<grid, kWarps * 32, 0, st>>>(a, ks, awq); break;
+    case 32: k_int4_mma<MODE, NT, 1, AWQ><<<grid, kWarps * 32, 0, st>>>(a, ks); break;
+    case 64: k_int4_mma<MODE, NT, 2, AWQ><<<grid, kWarps * 32, 0, st>>>(a, ks); break;
+    default: k_int4_mma<MODE, NT, 4, AWQ><<<grid, kWarps * 32, 0, st>>>(a, ks); break;
   }
 }
 
 template <int MODE>
 static void launch_mma(const GemmArgs& a, int max_work, int ntiles, int ks, int awq, cudaStream_t st) {
-  if (ntiles <= 1) launch_mma_gs<MODE, 1>(a, max_work, ks, awq, st);
-  else if (ntiles == 2) launch_mma_gs<MODE, 2>(a, max_work, ks, awq, st);
-  else launch_mma_gs<MODE, 4>(a, max_work, ks, awq, st);
+  if (awq) {
+    if (ntiles <= 1) launch_mma_gs<MODE, 1, true>(a, max_work, ks, st);
+    else launch_mma_gs<MODE, 4, true>(a, max_work, ks, st);
+  } else {
+    if (ntiles <= 1) launch_mma_gs<MODE, 1, false>(a, max_work, ks, st);
+    else launch_mma_gs<MODE, 4, false>(a, max_work, ks, st);
+  }
 }
 
 // ------------------------------------------------------ CUDA-core fp32 GEMV
@@ -670,8 +655,9 @@ cudaError_t launch_gemm(int mode, int path, const GemmArgs& a, int max_work, int
   dim3 grid((Mt + 3) / 4, max_work);
   if (path == 0) {
     // K split: enough warps to cover the SMs when the expected work is small
-    const long units = (long)((Mt + 1) / 2) * max_work;
-    const int ks = a.Kc >= 16 && units < 148 * 32 ? 4 : (a.Kc >= 16 ? 2 : 1);
+    const long units = (long)Mt * max_work;
+    const int nsteps = a.K / 128;
+    const int ks = nsteps >= 8 && units < 148 * 16 ? 4 : (nsteps >= 8 ? 2 : 1);
     if (mode == MODE_GATE_UP)
       launch_mma<MODE_GATE_UP>(a, max_work, ntiles, ks, awq, st);
     else

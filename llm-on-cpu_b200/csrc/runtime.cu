@@ -937,7 +937,11 @@ llmoc_status llmoc_moe_forward(const llmoc_moe_layer* L, const uint16_t* X, int 
   if (rc != LLMOC_OK) return rc;
   const int H = L->d.hidden, I = L->d.inter;
   const bool awq = L->d.scheme == LLMOC_SCHEME_AWQ_SYM;
-  const int path = 0;  // tensor cores for both schemes (GPTQ zeros use the per-token sums)
+  // tensor cores when K of both GEMMs is a multiple of 128 and the group is
+  // 32/64/128 wide (every BASELINE shape); the CUDA-core kernel otherwise
+  const int gs = L->d.group_size;
+  const bool tc = H % 128 == 0 && I % 128 == 0 && (gs == 32 || gs == 64 || gs == 128);
+  const int path = tc ? 0 : 2;
   const int ntiles = chunk_rows(T) / 8;
   GemmArgs a{};
   a.experts = L->table;
