@@ -189,7 +189,9 @@ LLMOC_API llmoc_status llmoc_moe_forward(const llmoc_moe_layer* layer, const uin
  * (device pointers; kk = topk + has_shared slots per token):
  *   logits [T,E] fp32; ids [T,kk] int32; weights [T,kk] fp32;
  *   offsets [E+has_shared+1] int32; sorted [T*kk] int32 (= t*kk + j);
- *   inverse [T*kk] int32; n_active: number of experts with >= 1 pair. */
+ *   inverse [T*kk] int32; n_active: number of experts with >= 1 pair;
+ *   error_flag: 0, or bit 0 set when a bounded device-side wait gave up
+ *   (the outputs of that forward are then not valid). */
 typedef struct llmoc_route_views {
   float* logits;
   int32_t* ids;
@@ -198,6 +200,7 @@ typedef struct llmoc_route_views {
   int32_t* sorted;
   int32_t* inverse;
   int32_t* n_active;
+  int32_t* error_flag;
 } llmoc_route_views;
 LLMOC_API llmoc_status llmoc_moe_route_views(const llmoc_moe_layer* layer, int T, void* workspace,
                                    size_t workspace_bytes, llmoc_route_views* out);

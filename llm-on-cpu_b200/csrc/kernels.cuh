@@ -28,6 +28,7 @@ struct PermArgs {
   WorkItem* work;   // [max_work]
   int* n_work;
   int* n_active;
+  int* err;         // device error word, cleared here for the kernels that follow
   int chunk;        // rows per work item (8, 16 or 32)
 };
 
@@ -67,6 +68,7 @@ struct GemmArgs {
   void* out;              // GATE_UP: mid [pos][ldo]; PLAIN: fp32 [pos][ldo]
   int ldo;
   int out_bf16;           // GATE_UP output type (cc kernel): 1 bf16, 0 fp32
+  int* err;               // device error word: bit 0 = a bounded wait gave up (may be null)
 };
 
 cudaError_t launch_repack(const RepackArgs& a, cudaStream_t st);
@@ -75,6 +77,9 @@ cudaError_t launch_dequant(const ProjDev& P, int M, int K, int gs, int awq, int 
 // path: 0 tensor-core (AWQ, bf16 B), 1 CUDA-core fp32 B, 2 CUDA-core bf16 B
 cudaError_t launch_gemm(int mode, int path, const GemmArgs& a, int max_work, int awq, int ntiles,
                         cudaStream_t st);
+// int4_tma.cu: the same grouped GEMM fed by cp.async.bulk through a shared-
+// memory stage ring (decode-size items, K % 128 == 0, gs in {32, 64, 128}).
+cudaError_t launch_gemm_tma(int mode, const GemmArgs& a, int max_work, int awq, cudaStream_t st);
 cudaError_t launch_combine(const float* d, const int* inverse, const float* w, int T, int kk, int H,
                            void* y, int y_bf16, int skip_tiny, cudaStream_t st);
 cudaError_t launch_quant_awq_sym(const __nv_bfloat16* W, int M, int K, int gs, int bf16_scale,

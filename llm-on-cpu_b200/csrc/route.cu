@@ -318,6 +318,7 @@ __global__ void __launch_bounds__(kPermThreads) k_permute(PermArgs a) {
     }
   }
   if (threadIdx.x == kPermThreads - 1) {
+    if (a.err) *a.err = 0;
     a.offsets[a.n_exp] = w1[kPermWarps - 1];
     *a.n_work = w2[kPermWarps - 1];
     *a.n_active = w3[kPermWarps - 1];

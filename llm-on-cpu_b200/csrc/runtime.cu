@@ -14,6 +14,7 @@
 #include <cmath>
 #include <atomic>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -331,12 +332,27 @@ struct llmoc_moe_layer {
 
 namespace {
 
+// Grouped-GEMM implementation override for measurement (environment
+// LLMOC_GEMM_PATH = tma | mma | cuda_core; default: tma for decode-size
+// items, mma otherwise).  0 default, 1 mma, 2 cuda-core.
+int gemm_path_pref() {
+  static const int pref = [] {
+    const char* v = getenv("LLMOC_GEMM_PATH");
+    if (!v) return 0;
+    if (!strcmp(v, "mma")) return 1;
+    if (!strcmp(v, "cuda_core")) return 2;
+    return 0;
+  }();
+  return pref;
+}
+
 // Rows per work item (tensor-core N tiles of 8): decode-size batches use
 // one N tile per item, so the kernel variant has no per-tile branches.
 int chunk_rows(int T) { return T <= 128 ? 8 : kChunkRows; }
 
 struct WsLayout {
-  size_t logits, ids, weights, offsets, sorted, inverse, work, n_work, n_active, mid, partial, total;
+  size_t logits, ids, weights, offsets, sorted, inverse, work, n_work, n_active, err, mid, partial,
+      total;
   int max_work;
 };
 
@@ -360,6 +376,7 @@ WsLayout ws_layout(const llmoc_moe_layer* L, int T) {
   w.work = take((size_t)std::max(1, w.max_work) * sizeof(WorkItem));
   w.n_work = take(4);
   w.n_active = take(4);
+  w.err = take(4);
   w.mid = take(n * L->d.inter * 2);
   w.partial = take(n * L->d.hidden * 4);
   w.total = o;
@@ -571,6 +588,7 @@ llmoc_status run_route(const llmoc_moe_layer* L, const uint16_t* X, int T, const
   pa.work = (WorkItem*)(ws + w.work);
   pa.n_work = (int*)(ws + w.n_work);
   pa.n_active = (int*)(ws + w.n_active);
+  pa.err = (int*)(ws + w.err);
   pa.chunk = chunk_rows(T);
   if (!cuda_ok(launch_permute(pa, st), "permute")) return LLMOC_ERR_CUDA;
   if (se) se->mark(st);
@@ -910,6 +928,7 @@ llmoc_status llmoc_moe_route_views(const llmoc_moe_layer* L, int T, void* worksp
   out->sorted = (int32_t*)(ws + w.sorted);
   out->inverse = (int32_t*)(ws + w.inverse);
   out->n_active = (int32_t*)(ws + w.n_active);
+  out->error_flag = (int32_t*)(ws + w.err);
   return LLMOC_OK;
 }
 
@@ -941,7 +960,9 @@ llmoc_status llmoc_moe_forward(const llmoc_moe_layer* L, const uint16_t* X, int 
   // 32/64/128 wide (every BASELINE shape); the CUDA-core kernel otherwise
   const int gs = L->d.group_size;
   const bool tc = H % 128 == 0 && I % 128 == 0 && (gs == 32 || gs == 64 || gs == 128);
-  const int path = tc ? 0 : 2;
+  int path = tc ? 0 : 2;
+  const bool tma = tc && chunk_rows(T) == 8 && gemm_path_pref() != 1;
+  if (tc && gemm_path_pref() == 2) path = 2;
   const int ntiles = chunk_rows(T) / 8;
   GemmArgs a{};
   a.experts = L->table;
@@ -960,7 +981,10 @@ llmoc_status llmoc_moe_forward(const llmoc_moe_layer* L, const uint16_t* X, int 
   a.out = ws + w.mid;
   a.ldo = I;
   a.out_bf16 = 1;
-  if (!cuda_ok(launch_gemm(MODE_GATE_UP, path, a, w.max_work, awq, ntiles, st), "gate/up"))
+  a.err = (int*)(ws + w.err);
+  if (!cuda_ok(tma && path == 0 ? launch_gemm_tma(MODE_GATE_UP, a, w.max_work, awq, st)
+                                : launch_gemm(MODE_GATE_UP, path, a, w.max_work, awq, ntiles, st),
+               "gate/up"))
     return LLMOC_ERR_CUDA;
   se.mark(st);
   GemmArgs b = a;
@@ -974,7 +998,9 @@ llmoc_status llmoc_moe_forward(const llmoc_moe_layer* L, const uint16_t* X, int 
   b.gather = nullptr;
   b.out = ws + w.partial;
   b.ldo = H;
-  if (!cuda_ok(launch_gemm(MODE_PLAIN_F32, path, b, w.max_work, awq, ntiles, st), "down"))
+  if (!cuda_ok(tma && path == 0 ? launch_gemm_tma(MODE_PLAIN_F32, b, w.max_work, awq, st)
+                                : launch_gemm(MODE_PLAIN_F32, path, b, w.max_work, awq, ntiles, st),
+               "down"))
     return LLMOC_ERR_CUDA;
   se.mark(st);
   if (!cuda_ok(launch_combine((const float*)(ws + w.partial), (const int*)(ws + w.inverse),

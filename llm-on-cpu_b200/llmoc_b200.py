@@ -51,7 +51,7 @@ class LayerDesc(C.Structure):
 class RouteViews(C.Structure):
     _fields_ = [("logits", C.c_void_p), ("ids", C.c_void_p), ("weights", C.c_void_p),
                 ("offsets", C.c_void_p), ("sorted", C.c_void_p), ("inverse", C.c_void_p),
-                ("n_active", C.c_void_p)]
+                ("n_active", C.c_void_p), ("error_flag", C.c_void_p)]
 
 
 _vp, _i, _sz, _f = C.c_void_p, C.c_int, C.c_size_t, C.c_float

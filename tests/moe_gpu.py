@@ -96,6 +96,7 @@ class DevLayer:
             sorted=grab(v.sorted, T * kk, np.int32),
             inverse=grab(v.inverse, T * kk, np.int32),
             n_active=int(grab(v.n_active, 1, np.int32)[0]),
+            error_flag=int(grab(v.error_flag, 1, np.int32)[0]),
         )
 
     def close(self):

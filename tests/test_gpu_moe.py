@@ -115,6 +115,7 @@ def test_layer_matches_oracle(oracle, name, T):
     Y, ws_bytes = dl.forward(X)
     Yref, ids, w, _ = oracle.moe_layer_forward(dl.host, X)
     v = dl.views(T, ws_bytes)
+    assert v["error_flag"] == 0
     assert np.array_equal(v["ids"][:, :dl.host.topk], ids)
     mre, cos = G.quality(G.bf16_to_f32(Y), Yref)
     assert mre <= G.MAX_REL and cos >= G.MIN_COS, (mre, cos)
@@ -196,6 +197,7 @@ def test_full_size_layer(oracle, name, T):
     dl = G.DevLayer(layer, T)
     Y, ws_bytes = dl.forward(X)
     v = dl.views(T, ws_bytes)
+    assert v["error_flag"] == 0
     sample = np.unique(np.linspace(0, T - 1, min(T, 8)).astype(int))
     check_routing(oracle, dl, X, v, sample)
     Yref, ids, _, _ = oracle.moe_layer_forward(layer, X[sample])
