@@ -6,25 +6,31 @@
 // the reference's sum_k x * (q - zp) * s (AWQ) or sum_k x * (q * s + z)
 // (GPTQ), accumulated in fp32.
 //
-// Memory side: each of the 4 consumer warps owns one 16-row tile (or one K
-// slice of it) of one work item.  Lane w of a fifth, producer warp streams
-// that warp's 128-wide K steps into a kStages-deep shared-memory ring with
-// cp.async.bulk (the 1-D TMA; no multicast): per step the fragment words of
-// each projection (1 KB, contiguous in the repacked layout), its group scales
-// (and zeros), and the step's slice of the item's activation rows (gathered,
-// 256 B per row).  Completion is tracked with mbarrier transaction counts;
-// the consumer releases a stage with an mbarrier arrive.  Every wait is
-// bounded: on timeout the kernel sets bit 0 of *err and stops waiting.
+// Memory side: a CTA covers 4 consecutive 16-row tiles of one work item, one
+// per consumer warp; all four walk the same 128-wide K steps with the same
+// tokens.  A fifth, producer warp streams each step into a kStages-deep
+// shared-memory ring with cp.async.bulk (the 1-D TMA; no multicast), one copy
+// per lane in a single SIMT instruction: the fragment words of every (tile,
+// projection) (1 KB each, contiguous in the repacked layout), their group
+// scales (and zeros), and the step's slice of the item's activation rows
+// (gathered, 256 B per row, shared by the four tiles).  Completion is tracked
+// with mbarrier transaction counts; each consumer warp releases a stage with
+// an mbarrier arrive.  Every wait is bounded (~1 s of %globaltimer): on
+// timeout the kernel sets bit 0 of *err and stops waiting.
 #include "kernels.cuh"
 
 namespace llmoc {
 
 namespace {
 
-constexpr int kStages = 3;
-constexpr int kCWarps = 4;                      // consumer warps
+constexpr int kStages = 4;
+constexpr int kCWarps = 4;                      // consumer warps = row tiles per CTA
 constexpr int kBRow = 256 + 16;                 // padded activation row in smem (bytes)
-constexpr int kStageBytes = 2 * 1024 + 2 * 4 * 32 * 2 + 8 * kBRow;  // w, s+z, B
+// stage: weights [tile][proj] 1 KB | scales [tile][proj] 128 B | zeros | 8 activation rows
+constexpr int kOffS = kCWarps * 2 * 1024;
+constexpr int kOffZ = kOffS + kCWarps * 2 * 128;
+constexpr int kOffB = kOffZ + kCWarps * 2 * 128;
+constexpr int kStageBytes = kOffB + 8 * kBRow;
 constexpr uint64_t kWaitNs = 1000000000ull;     // a bounded wait gives up after ~1 s
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -97,79 +103,92 @@ __device__ __forceinline__ const ProjDev& pick(const ExpertDev& e, int p) {
 
 }  // namespace
 
-// grid.x = ceil(Mt * ks / 4), grid.y = work-list bound; block = 5 warps.
+// grid.x = ceil(Mt / 4), grid.y = work-list bound; block = 5 warps.
 template <int MODE, int GSB, bool AWQ>
-__global__ void __launch_bounds__((kCWarps + 1) * 32) k_int4_tma(GemmArgs a, int ks) {
+__global__ void __launch_bounds__((kCWarps + 1) * 32) k_int4_tma(GemmArgs a) {
   constexpr int NP = MODE == MODE_GATE_UP ? 2 : 1;
   constexpr int NG = GSB == 4 ? 1 : (GSB == 2 ? 2 : 4);  // groups per 128-wide step
   extern __shared__ __align__(128) unsigned char smem[];
-  __shared__ __align__(8) uint64_t full[kCWarps][kStages], empty[kCWarps][kStages];
-  __shared__ float red[kCWarps][NP][4][32];
+  __shared__ __align__(8) uint64_t full[kStages], empty[kStages];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if ((int)blockIdx.y >= *a.n_work) return;  // uniform over the CTA
   const WorkItem it = a.work[blockIdx.y];
   const ExpertDev& ex = a.experts[it.expert];
   const int Mt = (a.M + 15) >> 4;
+  const int rt0 = blockIdx.x * kCWarps;
+  const int ntiles = min(kCWarps, Mt - rt0);
   const int nsteps = a.K >> 7;
-  const int per = (nsteps + ks - 1) / ks;
 
   if (threadIdx.x == 0) {
-    for (int w = 0; w < kCWarps; ++w)
-      for (int s = 0; s < kStages; ++s) {
-        mbar_init(&full[w][s], 1);
-        mbar_init(&empty[w][s], 1);
-      }
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kCWarps);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
 
   if (warp == kCWarps) {
-    // ---------------- producer: lane w feeds consumer warp w ----------------
-    if (lane >= kCWarps) return;
-    const int w = lane;
-    const int rt = blockIdx.x * (kCWarps / ks) + w / ks;
-    const int slice = w % ks;
-    if (rt >= Mt) return;
-    const int s0 = min(nsteps, slice * per), s1 = min(nsteps, s0 + per);
+    // ----------------------------- producer warp -----------------------------
+    // lane roles: [0, 4*NP) weights of (tile, proj); [8, 8+4*NP) scales;
+    // [16, 16+4*NP) zeros (GPTQ); [24, 32) activation rows
     const ProjDev* P[2] = {MODE == MODE_GATE_UP ? &ex.gate : &pick(ex, a.proj), &ex.up};
-    const unsigned char* brow[8];
-    int nb = 0;
-    for (int r = 0; r < 8 && r < it.nrows; ++r) {
-      const int pos = it.row0 + r;
-      const int row = a.gather ? a.gather[pos] / a.kk : pos;
-      brow[r] = reinterpret_cast<const unsigned char*>(a.B) + ((size_t)row * a.ldb) * 2;
-      nb = r + 1;
-    }
-    const uint32_t bytes = NP * 1024u + NP * NG * 32u * (AWQ ? 1u : 2u) + (uint32_t)nb * 256u;
-    unsigned char* base = smem + (size_t)w * kStages * kStageBytes;
-    for (int j = s0; j < s1; ++j) {
-      const int i = j - s0, st = i % kStages;
-      if (i >= kStages && !mbar_wait(&empty[w][st], ((i / kStages) - 1) & 1)) {
-        if (a.err) atomicOr(a.err, 1);
-        break;
+    const int nb = min(8, it.nrows);
+    const int role = lane >> 3, idx = lane & 7;
+    const int tile = idx / NP, proj = idx % NP;
+    bool act = false;
+    const unsigned char* src = nullptr;
+    uint32_t dst_off = 0, size = 0;
+    size_t step_stride = 0;  // bytes the source advances per step
+    if (role < 3) {
+      act = idx < kCWarps * NP && tile < ntiles && (role != 2 || !AWQ);
+      if (act) {
+        const int rt = rt0 + tile;
+        if (role == 0) {
+          src = reinterpret_cast<const unsigned char*>(P[proj]->q + (size_t)rt * a.Kc * 32);
+          dst_off = (tile * 2 + proj) * 1024;
+          size = 1024;
+          step_stride = 1024;
+        } else {
+          const __half* base = role == 1 ? P[proj]->s : P[proj]->z;
+          src = reinterpret_cast<const unsigned char*>(base + (size_t)rt * a.ng * 16);
+          dst_off = (role == 1 ? kOffS : kOffZ) + (tile * 2 + proj) * 128;
+          size = NG * 32;
+          step_stride = (size_t)NG * 32;
+        }
       }
-      unsigned char* sb = base + st * kStageBytes;
-      mbar_expect_tx(&full[w][st], bytes);
-      for (int p = 0; p < NP; ++p) {
-        bulk_g2s(sb + p * 1024, P[p]->q + ((size_t)rt * a.Kc + 2 * j) * 32, 1024, &full[w][st]);
-        const size_t go = ((size_t)rt * a.ng + (size_t)j * 4 / GSB) * 16;
-        bulk_g2s(sb + 2048 + p * 256, P[p]->s + go, NG * 32, &full[w][st]);
-        if (!AWQ) bulk_g2s(sb + 2048 + p * 256 + 128, P[p]->z + go, NG * 32, &full[w][st]);
+    } else {
+      act = idx < nb;
+      if (act) {
+        const int pos = it.row0 + idx;
+        const int row = a.gather ? a.gather[pos] / a.kk : pos;
+        src = reinterpret_cast<const unsigned char*>(a.B) + (size_t)row * a.ldb * 2;
+        dst_off = kOffB + idx * kBRow;
+        size = 256;
+        step_stride = 256;
       }
-      for (int r = 0; r < nb; ++r)
-        bulk_g2s(sb + 2560 + r * kBRow, brow[r] + (size_t)j * 256, 256, &full[w][st]);
     }
+    const uint32_t bytes = (uint32_t)ntiles * NP * (1024u + NG * 32u * (AWQ ? 1u : 2u)) + nb * 256u;
+    bool ok = true;
+    for (int j = 0; j < nsteps; ++j) {
+      const int st = j % kStages;
+      if (lane == 0) {
+        if (j >= kStages && !mbar_wait(&empty[st], ((j / kStages) - 1) & 1)) ok = false;
+        if (ok) mbar_expect_tx(&full[st], bytes);
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      if (act) bulk_g2s(smem + st * kStageBytes + dst_off, src + (size_t)j * step_stride, size, &full[st]);
+    }
+    if (!ok && lane == 0 && a.err) atomicOr(a.err, 1);
     return;
   }
 
-  // ---------------------------- consumers ----------------------------------
+  // ------------------------------ consumers --------------------------------
   const int g = lane >> 2, t = lane & 3;
-  const int rt = blockIdx.x * (kCWarps / ks) + warp / ks;
-  const int slice = warp % ks;
-  const bool live = rt < Mt;
-  const int s0 = live ? min(nsteps, slice * per) : 0;
-  const int s1 = live ? min(nsteps, s0 + per) : 0;
+  const int rt = rt0 + warp;
+  const bool live = warp < ntiles;
   const float bias = AWQ ? (float)(128 + a.zp) : 128.f;
   const uint32_t ones[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};
 
@@ -181,41 +200,43 @@ __global__ void __launch_bounds__((kCWarps + 1) * 32) k_int4_tma(GemmArgs a, int
 #pragma unroll
   for (int r = 0; r < 4; ++r) xs[r] = 0.f;
 
-  const unsigned char* base = smem + (size_t)warp * kStages * kStageBytes;
   bool ok = true;
-  for (int j = s0; j < s1; ++j) {
-    const int i = j - s0, st = i % kStages;
-    if (!mbar_wait(&full[warp][st], (i / kStages) & 1)) {
+  for (int j = 0; j < nsteps; ++j) {
+    const int st = j % kStages;
+    if (!mbar_wait(&full[st], (j / kStages) & 1)) {
       ok = false;
       break;
     }
-    const unsigned char* sb = base + st * kStageBytes;
-    uint4 wq[NP][2];
-#pragma unroll
-    for (int p = 0; p < NP; ++p) {
-      wq[p][0] = *reinterpret_cast<const uint4*>(sb + p * 1024 + lane * 16);
-      wq[p][1] = *reinterpret_cast<const uint4*>(sb + p * 1024 + 512 + lane * 16);
-    }
-    uint4 bv[4];
-#pragma unroll
-    for (int b = 0; b < 4; ++b)
-      bv[b] = *reinterpret_cast<const uint4*>(sb + 2560 + g * kBRow + b * 64 + t * 16);
+    const unsigned char* sb = smem + st * kStageBytes;
+    uint4 wq[NP][2], bv[4];
     float sc[NP][NG][2], zz[NP][NG][2];
+    if (live) {
 #pragma unroll
-    for (int p = 0; p < NP; ++p)
-#pragma unroll
-      for (int q = 0; q < NG; ++q) {
-        const __half* sp = reinterpret_cast<const __half*>(sb + 2048 + p * 256) + q * 16;
-        sc[p][q][0] = __half2float(sp[g]);
-        sc[p][q][1] = __half2float(sp[g + 8]);
-        if (!AWQ) {
-          const __half* zp = reinterpret_cast<const __half*>(sb + 2048 + p * 256 + 128) + q * 16;
-          zz[p][q][0] = __half2float(zp[g]);
-          zz[p][q][1] = __half2float(zp[g + 8]);
-        }
+      for (int p = 0; p < NP; ++p) {
+        const unsigned char* wp = sb + (warp * 2 + p) * 1024 + lane * 16;
+        wq[p][0] = *reinterpret_cast<const uint4*>(wp);
+        wq[p][1] = *reinterpret_cast<const uint4*>(wp + 512);
       }
+#pragma unroll
+      for (int b = 0; b < 4; ++b)
+        bv[b] = *reinterpret_cast<const uint4*>(sb + kOffB + g * kBRow + b * 64 + t * 16);
+#pragma unroll
+      for (int p = 0; p < NP; ++p)
+#pragma unroll
+        for (int q = 0; q < NG; ++q) {
+          const __half* sp = reinterpret_cast<const __half*>(sb + kOffS + (warp * 2 + p) * 128) + q * 16;
+          sc[p][q][0] = __half2float(sp[g]);
+          sc[p][q][1] = __half2float(sp[g + 8]);
+          if (!AWQ) {
+            const __half* zp = reinterpret_cast<const __half*>(sb + kOffZ + (warp * 2 + p) * 128) + q * 16;
+            zz[p][q][0] = __half2float(zp[g]);
+            zz[p][q][1] = __half2float(zp[g + 8]);
+          }
+        }
+    }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[warp][st]);  // operands are in registers now
+    if (lane == 0) mbar_arrive(&empty[st]);  // operands are in registers now
+    if (!live) continue;
 
 #pragma unroll
     for (int b = 0; b < 4; ++b) {
@@ -250,25 +271,7 @@ __global__ void __launch_bounds__((kCWarps + 1) * 32) k_int4_tma(GemmArgs a, int
     }
   }
   if (!ok && lane == 0 && a.err) atomicOr(a.err, 1);
-
-  if (ks > 1) {
-    // the K slices of a tile are the ks consecutive warps: sum in warp order
-#pragma unroll
-    for (int p = 0; p < NP; ++p)
-#pragma unroll
-      for (int r = 0; r < 4; ++r) red[warp][p][r][lane] = acc[p][r];
-    asm volatile("bar.sync 1, %0;" ::"r"(kCWarps * 32));  // consumers only
-    if (slice != 0) return;
-#pragma unroll
-    for (int p = 0; p < NP; ++p)
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        float v = red[warp][p][r][lane];
-        for (int w = 1; w < ks; ++w) v += red[warp + w][p][r][lane];
-        acc[p][r] = v;
-      }
-  }
-  if (!live) return;
+  if (!live || !ok) return;
   const int m0 = rt * 16 + g, m1 = m0 + 8;
 #pragma unroll
   for (int r = 0; r < 4; ++r) {
@@ -289,24 +292,24 @@ __global__ void __launch_bounds__((kCWarps + 1) * 32) k_int4_tma(GemmArgs a, int
 }
 
 template <int MODE, bool AWQ>
-static cudaError_t launch_t(const GemmArgs& a, int max_work, int ks, cudaStream_t st) {
+static cudaError_t launch_t(const GemmArgs& a, int max_work, cudaStream_t st) {
   const int Mt = (a.M + 15) / 16;
-  const dim3 grid((Mt * ks + kCWarps - 1) / kCWarps, max_work);
-  const size_t smem = (size_t)kCWarps * kStages * kStageBytes;
+  const dim3 grid((Mt + kCWarps - 1) / kCWarps, max_work);
+  const size_t smem = (size_t)kStages * kStageBytes;
   const int threads = (kCWarps + 1) * 32;
   cudaError_t e = cudaSuccess;
   switch (a.gs) {
     case 32:
       e = cudaFuncSetAttribute(k_int4_tma<MODE, 1, AWQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e == cudaSuccess) k_int4_tma<MODE, 1, AWQ><<<grid, threads, smem, st>>>(a, ks);
+      if (e == cudaSuccess) k_int4_tma<MODE, 1, AWQ><<<grid, threads, smem, st>>>(a);
       break;
     case 64:
       e = cudaFuncSetAttribute(k_int4_tma<MODE, 2, AWQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e == cudaSuccess) k_int4_tma<MODE, 2, AWQ><<<grid, threads, smem, st>>>(a, ks);
+      if (e == cudaSuccess) k_int4_tma<MODE, 2, AWQ><<<grid, threads, smem, st>>>(a);
       break;
     default:
       e = cudaFuncSetAttribute(k_int4_tma<MODE, 4, AWQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e == cudaSuccess) k_int4_tma<MODE, 4, AWQ><<<grid, threads, smem, st>>>(a, ks);
+      if (e == cudaSuccess) k_int4_tma<MODE, 4, AWQ><<<grid, threads, smem, st>>>(a);
       break;
   }
   return e != cudaSuccess ? e : cudaGetLastError();
@@ -314,15 +317,10 @@ static cudaError_t launch_t(const GemmArgs& a, int max_work, int ks, cudaStream_
 
 cudaError_t launch_gemm_tma(int mode, const GemmArgs& a, int max_work, int awq, cudaStream_t st) {
   if (max_work <= 0) return cudaSuccess;
-  const int Mt = (a.M + 15) / 16;
-  const int nsteps = a.K / 128;
-  const long units = (long)Mt * max_work;
-  const int ks = nsteps >= 8 && units < 148 * 16 ? 4 : (nsteps >= 8 ? 2 : 1);
   if (mode == MODE_GATE_UP)
-    return awq ? launch_t<MODE_GATE_UP, true>(a, max_work, ks, st)
-               : launch_t<MODE_GATE_UP, false>(a, max_work, ks, st);
-  return awq ? launch_t<MODE_PLAIN_F32, true>(a, max_work, ks, st)
-             : launch_t<MODE_PLAIN_F32, false>(a, max_work, ks, st);
+    return awq ? launch_t<MODE_GATE_UP, true>(a, max_work, st) : launch_t<MODE_GATE_UP, false>(a, max_work, st);
+  return awq ? launch_t<MODE_PLAIN_F32, true>(a, max_work, st)
+             : launch_t<MODE_PLAIN_F32, false>(a, max_work, st);
 }
 
 }  // namespace llmoc
