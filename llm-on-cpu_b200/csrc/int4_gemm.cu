@@ -220,16 +220,28 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
         wq[p] += 64;
       }
 
+  // activations: this step's fragments, and the next step's in flight
+  uint4 bnext[NT][4];
+#pragma unroll
+  for (int n = 0; n < NT; ++n)
+#pragma unroll
+    for (int b = 0; b < 4; ++b)
+      bnext[n][b] = (bval[n] && nst > 0) ? bq[n][b * 4] : make_uint4(0, 0, 0, 0);
+
   for (int i0 = 0; i0 < nst; i0 += kRing) {
 #pragma unroll
     for (int d = 0; d < kRing; ++d) {
       if (i0 + d >= nst) break;
       // activations of this 128-wide step: 4 blocks of 8 bf16 per lane
       uint4 bv[NT][4];
+      const bool bmore = i0 + d + 1 < nst;
 #pragma unroll
       for (int n = 0; n < NT; ++n) {
 #pragma unroll
-        for (int b = 0; b < 4; ++b) bv[n][b] = bval[n] ? bq[n][b * 4] : make_uint4(0, 0, 0, 0);
+        for (int b = 0; b < 4; ++b) {
+          bv[n][b] = bnext[n][b];
+          if (bval[n] && bmore) bnext[n][b] = bq[n][16 + b * 4];
+        }
         bq[n] += 16;
       }
       // scales (and zeros) of the groups in this step

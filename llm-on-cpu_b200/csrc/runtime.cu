@@ -333,14 +333,16 @@ struct llmoc_moe_layer {
 namespace {
 
 // Grouped-GEMM implementation override for measurement (environment
-// LLMOC_GEMM_PATH = tma | mma | cuda_core; default: tma for decode-size
-// items, mma otherwise).  0 default, 1 mma, 2 cuda-core.
+// LLMOC_GEMM_PATH = mma | tma | cuda_core).  Default (0): the register-fed
+// tensor-core kernel.  1 mma, 2 cuda-core, 3 the TMA-fed kernel for
+// decode-size items.
 int gemm_path_pref() {
   static const int pref = [] {
     const char* v = getenv("LLMOC_GEMM_PATH");
     if (!v) return 0;
     if (!strcmp(v, "mma")) return 1;
     if (!strcmp(v, "cuda_core")) return 2;
+    if (!strcmp(v, "tma")) return 3;
     return 0;
   }();
   return pref;
@@ -961,7 +963,7 @@ llmoc_status llmoc_moe_forward(const llmoc_moe_layer* L, const uint16_t* X, int 
   const int gs = L->d.group_size;
   const bool tc = H % 128 == 0 && I % 128 == 0 && (gs == 32 || gs == 64 || gs == 128);
   int path = tc ? 0 : 2;
-  const bool tma = tc && chunk_rows(T) == 8 && gemm_path_pref() != 1;
+  const bool tma = tc && chunk_rows(T) == 8 && gemm_path_pref() == 3;
   if (tc && gemm_path_pref() == 2) path = 2;
   const int ntiles = chunk_rows(T) / 8;
   GemmArgs a{};
