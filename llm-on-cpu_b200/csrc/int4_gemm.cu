@@ -138,21 +138,50 @@ __device__ __forceinline__ void raw_word(uint32_t w, uint32_t a[4]) {
 // projections when NP = 2) of one work item; the ks warps of a CTA that
 // share the tile split K into contiguous slices of 128-wide steps (K % 128 ==
 // 0, group size 32/64/128, so every group end sits at a fixed place of a
-// step).  Weights stream as 128-bit fragment words through a kRing-step
-// register ring.  The MMA consumes the biased integers (128 + q), exact in
-// bf16, and one extra MMA per k16 against an all-ones A fragment gives
-// xs = sum_k x per token (shared by both projections).  Per group the fp32
-// partials become
+// step).  Memory: each lane runs a private kStagesW-deep pipeline in shared
+// memory — cp.async (16 B, L1 bypass) of its own fragment words and its own
+// activation bytes for step i + kStagesW - 1 while it computes step i — so
+// the bytes in flight do not cost registers and no barrier is needed (a lane
+// only reads what it copied; the group scales, shared by the warp, are the
+// one item read across lanes, after a __syncwarp).
+// The MMA consumes the biased integers (128 + q), exact in bf16, and one
+// extra MMA per k16 against an all-ones A fragment gives xs = sum_k x per
+// token (shared by both projections).  Per group the fp32 partials become
 //     AWQ:  s * (P - (128 + zp) * xs)        GPTQ: s * (P - 128 * xs) + z * xs
 // i.e. the reference's  sum_k x * (q - zp) * s  and  sum_k x * (q * s + z).
 // K slices meet in shared memory and are summed in warp order.
 // grid.x = ceil(Mt * ks / 4), grid.y = work-list bound.
-constexpr int kRing = 2;  // 128-wide K steps of weights in flight per warp
+constexpr int kStagesW = 4;
+
+template <int NP, int NT, bool AWQ>
+struct WStage {  // bytes of one stage of one warp
+  static constexpr int kW = NP * 1024;         // 2 chunks x 512 B per projection
+  static constexpr int kS = NP * 128;          // scales of the step's groups (<= 4 x 32 B)
+  static constexpr int kZ = AWQ ? 0 : NP * 128;  // zeros (GPTQ)
+  static constexpr int kB = NT * 4 * 512;      // 4 blocks x 16 B per lane per N-tile
+  static constexpr int kBytes = kW + kS + kZ + kB;
+  // the K-slice reduction reuses the warp's own stages once they are drained
+  static_assert(kStagesW * kBytes >= NP * NT * 4 * 32 * 4, "reduction slot");
+};
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+               "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
 
 template <int MODE, int NT, int GSB, bool AWQ>
 __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
   constexpr int NP = MODE == MODE_GATE_UP ? 2 : 1;
-  __shared__ float red[kWarps][NP][NT][4][32];
+  constexpr int NG = GSB == 4 ? 1 : (GSB == 2 ? 2 : 4);  // groups per step
+  using SG = WStage<NP, NT, AWQ>;
+  extern __shared__ __align__(128) unsigned char wsm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int slice = warp % ks;
@@ -171,8 +200,10 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
   const int per = (nsteps + ks - 1) / ks;
   const int s0 = live ? min(nsteps, slice * per) : 0;
   const int s1 = live ? min(nsteps, s0 + per) : 0;
+  const int nst = s1 - s0;
 
-  const uint4* bq[NT];  // activation pointer of this lane (row 8n+g, k offset 8t)
+  // sources advanced one step per issue
+  const unsigned char* bsrc[NT];
   bool bval[NT];
 #pragma unroll
   for (int n = 0; n < NT; ++n) {
@@ -180,12 +211,53 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
     bval[n] = r < it.nrows && n < ntc;
     const int pos = it.row0 + (r < it.nrows ? r : 0);
     const int row = a.gather ? a.gather[pos] / a.kk : pos;
-    bq[n] = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.B) +
-                                           (size_t)row * a.ldb + 8 * t + s0 * 128);
+    bsrc[n] = reinterpret_cast<const unsigned char*>(a.B) + ((size_t)row * a.ldb + 8 * t + s0 * 128) * 2;
   }
+  const int rtc = live ? rt : 0;
+  const unsigned char* wsrc[NP];
+  const unsigned char* ssrc[NP];
+  const unsigned char* zsrc[NP];
+#pragma unroll
+  for (int p = 0; p < NP; ++p) {
+    wsrc[p] = reinterpret_cast<const unsigned char*>(P[p]->q + ((size_t)rtc * a.Kc + 2 * s0) * 32 + lane);
+    ssrc[p] = reinterpret_cast<const unsigned char*>(P[p]->s + ((size_t)rtc * a.ng + (size_t)s0 * NG) * 16);
+    zsrc[p] = AWQ ? nullptr
+                  : reinterpret_cast<const unsigned char*>(P[p]->z + ((size_t)rtc * a.ng + (size_t)s0 * NG) * 16);
+  }
+  unsigned char* wbase = wsm + (size_t)warp * kStagesW * SG::kBytes;
+
+  // issue the copies of one step into a stage (every lane its own 16 B pieces)
+  auto issue = [&](int stage) {
+    unsigned char* sb = wbase + stage * SG::kBytes;
+#pragma unroll
+    for (int p = 0; p < NP; ++p) {
+      cp_async16(sb + p * 1024 + lane * 16, wsrc[p]);
+      cp_async16(sb + p * 1024 + 512 + lane * 16, wsrc[p] + 512);
+      wsrc[p] += 1024;
+      if (lane < NG * 2) cp_async16(sb + SG::kW + p * 128 + lane * 16, ssrc[p] + lane * 16);
+      if (!AWQ && lane < NG * 2) cp_async16(sb + SG::kW + SG::kS + p * 128 + lane * 16, zsrc[p] + lane * 16);
+      ssrc[p] += NG * 32;
+      if (!AWQ) zsrc[p] += NG * 32;
+    }
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      if (bval[n]) {
+#pragma unroll
+        for (int b = 0; b < 4; ++b)
+          cp_async16(sb + SG::kW + SG::kS + SG::kZ + (n * 4 + b) * 512 + lane * 16, bsrc[n] + b * 64);
+      }
+      bsrc[n] += 256;
+    }
+  };
+
+#pragma unroll
+  for (int d = 0; d < kStagesW - 1; ++d) {
+    if (d < nst) issue(d);
+    cp_async_commit();
+  }
+
   const uint32_t ones[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};
   const float bias = AWQ ? (float)(128 + a.zp) : 128.f;
-
   float acc[NP][NT][4], tmp[NP][NT][4], xs[NT][4];
 #pragma unroll
   for (int p = 0; p < NP; ++p)
@@ -198,131 +270,89 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
 #pragma unroll
     for (int r = 0; r < 4; ++r) xs[n][r] = 0.f;
 
-  const int rtc = live ? rt : 0;
-  const uint4* wq[NP];   // next step to load (two 512-B chunks per step)
-  const __half* sq[NP];  // scales of this tile, first group of the slice
-  const __half* zq[NP];
+  for (int i = 0; i < nst; ++i) {
+    if (i + kStagesW - 1 < nst) issue((i + kStagesW - 1) % kStagesW);
+    cp_async_commit();
+    cp_async_wait<kStagesW - 1>();
+    __syncwarp();  // the scales are copied by lanes 0..2*NG-1 and read by all
+    const unsigned char* sb = wbase + (i % kStagesW) * SG::kBytes;
+    uint4 wq[NP][2], bv[NT][4];
+    float sc[NP][NG][2], zz[NP][NG][2];
 #pragma unroll
-  for (int p = 0; p < NP; ++p) {
-    wq[p] = P[p]->q + ((size_t)rtc * a.Kc + 2 * s0) * 32 + lane;
-    sq[p] = P[p]->s + ((size_t)rtc * a.ng + (s0 * 4) / GSB) * 16 + g;
-    zq[p] = AWQ ? nullptr : P[p]->z + ((size_t)rtc * a.ng + (s0 * 4) / GSB) * 16 + g;
-  }
-  const int nst = s1 - s0;
-  uint4 ring[NP][kRing][2];
+    for (int p = 0; p < NP; ++p) {
+      wq[p][0] = *reinterpret_cast<const uint4*>(sb + p * 1024 + lane * 16);
+      wq[p][1] = *reinterpret_cast<const uint4*>(sb + p * 1024 + 512 + lane * 16);
 #pragma unroll
-  for (int d = 0; d < kRing; ++d)
-#pragma unroll
-    for (int p = 0; p < NP; ++p)
-      if (d < nst) {
-        ring[p][d][0] = ldg_nc(wq[p]);
-        ring[p][d][1] = ldg_nc(wq[p] + 32);
-        wq[p] += 64;
-      }
-
-  // activations: this step's fragments, and the next step's in flight
-  uint4 bnext[NT][4];
-#pragma unroll
-  for (int n = 0; n < NT; ++n)
-#pragma unroll
-    for (int b = 0; b < 4; ++b)
-      bnext[n][b] = (bval[n] && nst > 0) ? bq[n][b * 4] : make_uint4(0, 0, 0, 0);
-
-  for (int i0 = 0; i0 < nst; i0 += kRing) {
-#pragma unroll
-    for (int d = 0; d < kRing; ++d) {
-      if (i0 + d >= nst) break;
-      // activations of this 128-wide step: 4 blocks of 8 bf16 per lane
-      uint4 bv[NT][4];
-      const bool bmore = i0 + d + 1 < nst;
-#pragma unroll
-      for (int n = 0; n < NT; ++n) {
-#pragma unroll
-        for (int b = 0; b < 4; ++b) {
-          bv[n][b] = bnext[n][b];
-          if (bval[n] && bmore) bnext[n][b] = bq[n][16 + b * 4];
+      for (int q = 0; q < NG; ++q) {
+        const __half* sp = reinterpret_cast<const __half*>(sb + SG::kW + p * 128) + q * 16;
+        sc[p][q][0] = __half2float(sp[g]);
+        sc[p][q][1] = __half2float(sp[g + 8]);
+        if (!AWQ) {
+          const __half* zp = reinterpret_cast<const __half*>(sb + SG::kW + SG::kS + p * 128) + q * 16;
+          zz[p][q][0] = __half2float(zp[g]);
+          zz[p][q][1] = __half2float(zp[g + 8]);
         }
-        bq[n] += 16;
       }
-      // scales (and zeros) of the groups in this step
-      constexpr int NG = GSB == 4 ? 1 : (GSB == 2 ? 2 : 4);  // groups per step
-      float sc[NP][NG][2], zz[NP][NG][2];
+    }
 #pragma unroll
-      for (int p = 0; p < NP; ++p)
+    for (int n = 0; n < NT; ++n)
 #pragma unroll
-        for (int q = 0; q < NG; ++q) {
-          sc[p][q][0] = __half2float(sq[p][q * 16]);
-          sc[p][q][1] = __half2float(sq[p][q * 16 + 8]);
-          if (!AWQ) {
-            zz[p][q][0] = __half2float(zq[p][q * 16]);
-            zz[p][q][1] = __half2float(zq[p][q * 16 + 8]);
-          }
-        }
+      for (int b = 0; b < 4; ++b)
+        bv[n][b] = bval[n] ? *reinterpret_cast<const uint4*>(sb + SG::kW + SG::kS + SG::kZ + (n * 4 + b) * 512 + lane * 16)
+                           : make_uint4(0, 0, 0, 0);
+    __syncwarp();  // every lane holds its operands before any lane refills this stage
+
 #pragma unroll
-      for (int p = 0; p < NP; ++p) {
-        sq[p] += NG * 16;
-        if (!AWQ) zq[p] += NG * 16;
-      }
+    for (int b = 0; b < 4; ++b) {  // 32-wide block b of the step
 #pragma unroll
-      for (int b = 0; b < 4; ++b) {  // 32-wide block b of the step
+      for (int kt = 0; kt < 2; ++kt) {
 #pragma unroll
-        for (int kt = 0; kt < 2; ++kt) {
+        for (int n = 0; n < NT; ++n)
+          if (NT == 1 || n < ntc)
+            mma_bf16(xs[n], ones, kt ? bv[n][b].z : bv[n][b].x, kt ? bv[n][b].w : bv[n][b].y);
+#pragma unroll
+        for (int p = 0; p < NP; ++p) {
+          const uint4& q4 = wq[p][b >> 1];
+          const int wi = (b & 1) * 2 + kt;
+          const uint32_t wd = wi == 0 ? q4.x : wi == 1 ? q4.y : wi == 2 ? q4.z : q4.w;
+          uint32_t af[4];
+          raw_word(wd, af);
 #pragma unroll
           for (int n = 0; n < NT; ++n)
             if (NT == 1 || n < ntc)
-              mma_bf16(xs[n], ones, kt ? bv[n][b].z : bv[n][b].x, kt ? bv[n][b].w : bv[n][b].y);
-#pragma unroll
-          for (int p = 0; p < NP; ++p) {
-            const uint4& q4 = ring[p][d][b >> 1];
-            const int wi = (b & 1) * 2 + kt;
-            const uint32_t wd = wi == 0 ? q4.x : wi == 1 ? q4.y : wi == 2 ? q4.z : q4.w;
-            uint32_t af[4];
-            raw_word(wd, af);
-#pragma unroll
-            for (int n = 0; n < NT; ++n)
-              if (NT == 1 || n < ntc)
-                mma_bf16(tmp[p][n], af, kt ? bv[n][b].z : bv[n][b].x, kt ? bv[n][b].w : bv[n][b].y);
-          }
+              mma_bf16(tmp[p][n], af, kt ? bv[n][b].z : bv[n][b].x, kt ? bv[n][b].w : bv[n][b].y);
         }
-        if ((b + 1) % GSB == 0) {  // group end
-          const int q = b / GSB;
+      }
+      if ((b + 1) % GSB == 0) {  // group end
+        const int q = b / GSB;
 #pragma unroll
-          for (int p = 0; p < NP; ++p)
-#pragma unroll
-            for (int n = 0; n < NT; ++n)
-#pragma unroll
-              for (int r = 0; r < 4; ++r) {
-                const float v = __fmaf_rn(-bias, xs[n][r], tmp[p][n][r]);  // sum x*(q - zp)
-                acc[p][n][r] = __fmaf_rn(v, sc[p][q][r >> 1], acc[p][n][r]);
-                if (!AWQ) acc[p][n][r] = __fmaf_rn(zz[p][q][r >> 1], xs[n][r], acc[p][n][r]);
-                tmp[p][n][r] = 0.f;
-              }
+        for (int p = 0; p < NP; ++p)
 #pragma unroll
           for (int n = 0; n < NT; ++n)
 #pragma unroll
-            for (int r = 0; r < 4; ++r) xs[n][r] = 0.f;
-        }
-      }
-      // refill this ring slot with the step kRing ahead (clamped: a harmless
-      // re-load of the last step when none is left)
-      const bool more = i0 + d + kRing < nst;
+            for (int r = 0; r < 4; ++r) {
+              const float v = __fmaf_rn(-bias, xs[n][r], tmp[p][n][r]);  // sum x*(q - zp)
+              acc[p][n][r] = __fmaf_rn(v, sc[p][q][r >> 1], acc[p][n][r]);
+              if (!AWQ) acc[p][n][r] = __fmaf_rn(zz[p][q][r >> 1], xs[n][r], acc[p][n][r]);
+              tmp[p][n][r] = 0.f;
+            }
 #pragma unroll
-      for (int p = 0; p < NP; ++p) {
-        const uint4* src = more ? wq[p] : wq[p] - 64;
-        ring[p][d][0] = ldg_nc(src);
-        ring[p][d][1] = ldg_nc(src + 32);
-        if (more) wq[p] += 64;
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+          for (int r = 0; r < 4; ++r) xs[n][r] = 0.f;
       }
     }
   }
+  cp_async_wait<0>();
 
-  if (ks > 1) {  // K-slice reduction in warp order
+  if (ks > 1) {  // K-slice reduction in warp order, in each warp's drained stages
+    float* slot = reinterpret_cast<float*>(wbase);
 #pragma unroll
     for (int p = 0; p < NP; ++p)
 #pragma unroll
       for (int n = 0; n < NT; ++n)
 #pragma unroll
-        for (int r = 0; r < 4; ++r) red[warp][p][n][r][lane] = acc[p][n][r];
+        for (int r = 0; r < 4; ++r) slot[((p * NT + n) * 4 + r) * 32 + lane] = acc[p][n][r];
     __syncthreads();
     if (slice != 0) return;
 #pragma unroll
@@ -331,8 +361,11 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
       for (int n = 0; n < NT; ++n)
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
-          float v = red[warp][p][n][r][lane];
-          for (int w = 1; w < ks; ++w) v += red[warp + w][p][n][r][lane];
+          float v = acc[p][n][r];
+          for (int w = 1; w < ks; ++w) {
+            const float* o = reinterpret_cast<const float*>(wsm + (size_t)(warp + w) * kStagesW * SG::kBytes);
+            v += o[((p * NT + n) * 4 + r) * 32 + lane];
+          }
           acc[p][n][r] = v;
         }
   }
@@ -362,14 +395,27 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
   }
 }
 
+template <int MODE, int NT, int GSB, bool AWQ>
+static void launch_mma_k(const GemmArgs& a, dim3 grid, int ks, cudaStream_t st) {
+  constexpr int NP = MODE == MODE_GATE_UP ? 2 : 1;
+  const size_t smem = (size_t)kWarps * kStagesW * WStage<NP, NT, AWQ>::kBytes;
+  static bool attr = false;  // per template instance
+  if (!attr) {
+    cudaFuncSetAttribute(k_int4_mma<MODE, NT, GSB, AWQ>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem);
+    attr = true;
+  }
+  k_int4_mma<MODE, NT, GSB, AWQ><<<grid, kWarps * 32, smem, st>>>(a, ks);
+}
+
 template <int MODE, int NT, bool AWQ>
 static void launch_mma_gs(const GemmArgs& a, int max_work, int ks, cudaStream_t st) {
   const int Mt = (a.M + 15) / 16;
   const dim3 grid((Mt * ks + kWarps - 1) / kWarps, max_work);
   switch (a.gs) {
-    case 32: k_int4_mma<MODE, NT, 1, AWQ><<<grid, kWarps * 32, 0, st>>>(a, ks); break;
-    case 64: k_int4_mma<MODE, NT, 2, AWQ><<<grid, kWarps * 32, 0, st>>>(a, ks); break;
-    default: k_int4_mma<MODE, NT, 4, AWQ><<<grid, kWarps * 32, 0, st>>>(a, ks); break;
+    case 32: launch_mma_k<MODE, NT, 1, AWQ>(a, grid, ks, st); break;
+    case 64: launch_mma_k<MODE, NT, 2, AWQ>(a, grid, ks, st); break;
+    default: launch_mma_k<MODE, NT, 4, AWQ>(a, grid, ks, st); break;
   }
 }
 
