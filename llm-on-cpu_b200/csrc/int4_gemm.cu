@@ -151,7 +151,7 @@ __device__ __forceinline__ void raw_word(uint32_t w, uint32_t a[4]) {
 // i.e. the reference's  sum_k x * (q - zp) * s  and  sum_k x * (q * s + z).
 // K slices meet in shared memory and are summed in warp order.
 // grid.x = ceil(Mt * ks / 4), grid.y = work-list bound.
-constexpr int kStagesW = 4;
+constexpr int kStagesW = 3;
 
 template <int NP, int NT, bool AWQ>
 struct WStage {  // bytes of one stage of one warp
