@@ -126,14 +126,12 @@ __device__ __forceinline__ float silu_mul(float g, float u) { return (g / (1.f +
 constexpr int kWarps = 4;  // warps per CTA of the grouped GEMM kernels
 
 // Raw fragment word -> four A registers holding bf16 (128 + q) pairs: one
-// lop3 per register (the zero point is removed after the MMA, below).  The
-// right shifts are done as high-half multiplies (w >> n == umulhi(w, 2^(32-n)))
-// so they run on the FMA pipe, leaving the ALU pipe to the lop3s.
+// lop3 per register (the zero point is removed after the MMA, below).
 __device__ __forceinline__ void raw_word(uint32_t w, uint32_t a[4]) {
   a[0] = lop3_and_or(w, 0x000F000Fu, 0x43004300u);
-  a[1] = lop3_and_or(__umulhi(w, 1u << 28), 0x000F000Fu, 0x43004300u);
-  a[2] = lop3_and_or(__umulhi(w, 1u << 24), 0x000F000Fu, 0x43004300u);
-  a[3] = lop3_and_or(__umulhi(w, 1u << 20), 0x000F000Fu, 0x43004300u);
+  a[1] = lop3_and_or(w >> 4, 0x000F000Fu, 0x43004300u);
+  a[2] = lop3_and_or(w >> 8, 0x000F000Fu, 0x43004300u);
+  a[3] = lop3_and_or(w >> 12, 0x000F000Fu, 0x43004300u);
 }
 
 // Grouped INT4 GEMM on the tensor cores.  A warp owns one 16-row tile (both
@@ -272,15 +270,12 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
 #pragma unroll
     for (int r = 0; r < 4; ++r) xs[n][r] = 0.f;
 
-  int st_rd = 0, st_wr = kStagesW - 1;  // ring positions (no modulo in the loop)
   for (int i = 0; i < nst; ++i) {
-    if (i + kStagesW - 1 < nst) issue(st_wr);
-    st_wr = st_wr == kStagesW - 1 ? 0 : st_wr + 1;
+    if (i + kStagesW - 1 < nst) issue((i + kStagesW - 1) % kStagesW);
     cp_async_commit();
     cp_async_wait<kStagesW - 1>();
     __syncwarp();  // the scales are copied by lanes 0..2*NG-1 and read by all
-    const unsigned char* sb = wbase + st_rd * SG::kBytes;
-    st_rd = st_rd == kStagesW - 1 ? 0 : st_rd + 1;
+    const unsigned char* sb = wbase + (i % kStagesW) * SG::kBytes;
     uint4 wq[NP][2], bv[NT][4];
     float sc[NP][NG][2], zz[NP][NG][2];
 #pragma unroll
