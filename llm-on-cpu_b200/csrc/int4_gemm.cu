@@ -258,17 +258,19 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
 
   const uint32_t ones[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};
   const float bias = AWQ ? (float)(128 + a.zp) : 128.f;
-  float acc[NP][NT][4], tmp[NP][NT][4], xs[NT][4];
+  // two partial accumulators per chain (k16 halves kt = 0 / 1) halve the
+  // dependent MMA chains; they are added at each group end
+  float acc[NP][NT][4], tmp[NP][NT][2][4], xs[NT][2][4];
 #pragma unroll
   for (int p = 0; p < NP; ++p)
 #pragma unroll
     for (int n = 0; n < NT; ++n)
 #pragma unroll
-      for (int r = 0; r < 4; ++r) acc[p][n][r] = tmp[p][n][r] = 0.f;
+      for (int r = 0; r < 4; ++r) acc[p][n][r] = tmp[p][n][0][r] = tmp[p][n][1][r] = 0.f;
 #pragma unroll
   for (int n = 0; n < NT; ++n)
 #pragma unroll
-    for (int r = 0; r < 4; ++r) xs[n][r] = 0.f;
+    for (int r = 0; r < 4; ++r) xs[n][0][r] = xs[n][1][r] = 0.f;
 
   for (int i = 0; i < nst; ++i) {
     if (i + kStagesW - 1 < nst) issue((i + kStagesW - 1) % kStagesW);
@@ -309,7 +311,7 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
 #pragma unroll
         for (int n = 0; n < NT; ++n)
           if (NT == 1 || n < ntc)
-            mma_bf16(xs[n], ones, kt ? bv[n][b].z : bv[n][b].x, kt ? bv[n][b].w : bv[n][b].y);
+            mma_bf16(xs[n][kt], ones, kt ? bv[n][b].z : bv[n][b].x, kt ? bv[n][b].w : bv[n][b].y);
 #pragma unroll
         for (int p = 0; p < NP; ++p) {
           const uint4& q4 = wq[p][b >> 1];
@@ -320,26 +322,31 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
 #pragma unroll
           for (int n = 0; n < NT; ++n)
             if (NT == 1 || n < ntc)
-              mma_bf16(tmp[p][n], af, kt ? bv[n][b].z : bv[n][b].x, kt ? bv[n][b].w : bv[n][b].y);
+              mma_bf16(tmp[p][n][kt], af, kt ? bv[n][b].z : bv[n][b].x, kt ? bv[n][b].w : bv[n][b].y);
         }
       }
       if ((b + 1) % GSB == 0) {  // group end
         const int q = b / GSB;
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+          for (int r = 0; r < 4; ++r) xs[n][0][r] += xs[n][1][r];
 #pragma unroll
         for (int p = 0; p < NP; ++p)
 #pragma unroll
           for (int n = 0; n < NT; ++n)
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
-              const float v = __fmaf_rn(-bias, xs[n][r], tmp[p][n][r]);  // sum x*(q - zp)
+              const float pr = tmp[p][n][0][r] + tmp[p][n][1][r];
+              const float v = __fmaf_rn(-bias, xs[n][0][r], pr);  // sum x*(q - zp)
               acc[p][n][r] = __fmaf_rn(v, sc[p][q][r >> 1], acc[p][n][r]);
-              if (!AWQ) acc[p][n][r] = __fmaf_rn(zz[p][q][r >> 1], xs[n][r], acc[p][n][r]);
-              tmp[p][n][r] = 0.f;
+              if (!AWQ) acc[p][n][r] = __fmaf_rn(zz[p][q][r >> 1], xs[n][0][r], acc[p][n][r]);
+              tmp[p][n][0][r] = tmp[p][n][1][r] = 0.f;
             }
 #pragma unroll
         for (int n = 0; n < NT; ++n)
 #pragma unroll
-          for (int r = 0; r < 4; ++r) xs[n][r] = 0.f;
+          for (int r = 0; r < 4; ++r) xs[n][0][r] = xs[n][1][r] = 0.f;
       }
     }
   }
