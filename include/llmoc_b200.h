@@ -224,6 +224,23 @@ LLMOC_API llmoc_status llmoc_moe_dequant(const llmoc_moe_layer* layer, int exper
 LLMOC_API llmoc_status llmoc_moe_set_stage_timing(llmoc_moe_layer* layer, int enable);
 LLMOC_API llmoc_status llmoc_moe_stage_times(llmoc_moe_layer* layer, float* ms, int* calls);
 
+/* Allocation-free forward (no counterpart in the reference).  For callers
+ * that cannot provide device memory for a workspace — their device memory is
+ * owned by another allocator, or their serving loop must not call
+ * cudaMalloc/cudaFree (which synchronize the device), or they reach this
+ * library through an FFI without a device allocator — this runs
+ * llmoc_moe_forward with its workspace in a fixed file-scope device array of
+ * llmoc_moe_noalloc_capacity() bytes (8 MiB) that every GPU loading the
+ * library holds until the process exits.  It allocates nothing.  The first
+ * call on a device looks up the array's device address; make that first call
+ * before any stream capture on the device.  Returns LLMOC_ERR_WORKSPACE when
+ * llmoc_moe_workspace_bytes(layer, T) exceeds the capacity.  All calls on a
+ * device share the array: calls whose work overlaps on the GPU race and must
+ * be serialized by the caller. */
+LLMOC_API llmoc_status llmoc_moe_forward_noalloc(const llmoc_moe_layer* layer, const uint16_t* X,
+                                                 int T, uint16_t* Y, void* stream);
+LLMOC_API size_t llmoc_moe_noalloc_capacity(void);
+
 /* ------------------------------------------------------------ utilities */
 
 /* quant_awq_sym (tools/quantize_int4.py:150-166) on the device: W [M,K] bf16

@@ -1078,3 +1078,13 @@ llmoc_status llmoc_moe_stage_times(llmoc_moe_layer* L, float* ms, int* calls) {
 uint64_t llmoc_kernel_launch_count(void) { return g_launches.load(); }
 
 }  // extern "C"
+
+namespace llmoc {
+// Device a layer lives on (used by the allocation-free entry point in no_alloc.cu).
+int layer_device(const llmoc_moe_layer* L) { return L ? L->device : -1; }
+}  // namespace llmoc
+
+namespace llmoc {
+// Sets the text llmoc_last_error() returns on this thread.
+void set_last_error(const std::string& msg) { t_err = msg; }
+}  // namespace llmoc

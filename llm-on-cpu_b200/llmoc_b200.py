@@ -94,6 +94,8 @@ _SIGS = {
     "llmoc_quantize_awq_sym": (_i, [_vp, _i, _i, _i, _i, _vp, _vp, _vp]),
     "llmoc_kernel_launch_count": (C.c_uint64, []),
     "llmoc_moe_set_stage_timing": (_i, [_vp, _i]),
+    "llmoc_moe_forward_noalloc": (_i, [_vp, _vp, _i, _vp, _vp]),
+    "llmoc_moe_noalloc_capacity": (_sz, []),
     "llmoc_moe_stage_times": (_i, [_vp, C.POINTER(C.c_float), C.POINTER(_i)]),
 }
 for _name, (_res, _args) in _SIGS.items():
