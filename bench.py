@@ -137,8 +137,8 @@ def ncu_traffic(config: str, T: int):
     p = os.path.join(REPO, "profiles", "traffic.json")
     if not os.path.exists(p):
         return None
-    d = json.load(open(p))
-    return d.get(f"{config}:T{T}")
+    d = json.load(open(p)).get(f"{config}:T{T}")
+    return d["dram_bytes_per_launch"] if d else None
 
 
 # ------------------------------------------------------- device workload
