@@ -80,6 +80,9 @@ cudaError_t launch_gemm(int mode, int path, const GemmArgs& a, int max_work, int
 // int4_tma.cu: the same grouped GEMM fed by cp.async.bulk through a shared-
 // memory stage ring (decode-size items, K % 128 == 0, gs in {32, 64, 128}).
 cudaError_t launch_gemm_tma(int mode, const GemmArgs& a, int max_work, int awq, cudaStream_t st);
+// int4_umma.cu: tcgen05.mma (TMEM accumulator) grouped GEMM for work items of
+// up to 128 rows (prefill-size groups); same K / group-size conditions.
+cudaError_t launch_gemm_umma(int mode, const GemmArgs& a, int max_work, int awq, cudaStream_t st);
 cudaError_t launch_combine(const float* d, const int* inverse, const float* w, int T, int kk, int H,
                            void* y, int y_bf16, int skip_tiny, cudaStream_t st);
 cudaError_t launch_quant_awq_sym(const __nv_bfloat16* W, int M, int K, int gs, int bf16_scale,

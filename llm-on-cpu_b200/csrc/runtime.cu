@@ -348,9 +348,10 @@ int gemm_path_pref() {
   return pref;
 }
 
-// Rows per work item (tensor-core N tiles of 8): decode-size batches use
-// one N tile per item, so the kernel variant has no per-tile branches.
-int chunk_rows(int T) { return T <= 128 ? 8 : kChunkRows; }
+// Rows per work item: decode-size batches use one mma N tile (8 rows), so
+// that kernel variant has no per-tile branches; prefill-size batches use
+// 128-row items for the tcgen05 kernel (32 when the mma path is forced).
+int chunk_rows(int T) { return T <= 128 ? 8 : (gemm_path_pref() == 1 ? kChunkRows : 128); }
 
 struct WsLayout {
   size_t logits, ids, weights, offsets, sorted, inverse, work, n_work, n_active, err, mid, partial,
@@ -964,8 +965,9 @@ llmoc_status llmoc_moe_forward(const llmoc_moe_layer* L, const uint16_t* X, int 
   const bool tc = H % 128 == 0 && I % 128 == 0 && (gs == 32 || gs == 64 || gs == 128);
   int path = tc ? 0 : 2;
   const bool tma = tc && chunk_rows(T) == 8 && gemm_path_pref() == 3;
+  const bool umma = tc && chunk_rows(T) == 128;
   if (tc && gemm_path_pref() == 2) path = 2;
-  const int ntiles = chunk_rows(T) / 8;
+  const int ntiles = std::min(4, chunk_rows(T) / 8);
   GemmArgs a{};
   a.experts = L->table;
   a.M = I;
@@ -984,8 +986,9 @@ llmoc_status llmoc_moe_forward(const llmoc_moe_layer* L, const uint16_t* X, int 
   a.ldo = I;
   a.out_bf16 = 1;
   a.err = (int*)(ws + w.err);
-  if (!cuda_ok(tma && path == 0 ? launch_gemm_tma(MODE_GATE_UP, a, w.max_work, awq, st)
-                                : launch_gemm(MODE_GATE_UP, path, a, w.max_work, awq, ntiles, st),
+  if (!cuda_ok(umma && path == 0 ? launch_gemm_umma(MODE_GATE_UP, a, w.max_work, awq, st)
+               : tma && path == 0 ? launch_gemm_tma(MODE_GATE_UP, a, w.max_work, awq, st)
+                                  : launch_gemm(MODE_GATE_UP, path, a, w.max_work, awq, ntiles, st),
                "gate/up"))
     return LLMOC_ERR_CUDA;
   se.mark(st);
@@ -1000,8 +1003,9 @@ llmoc_status llmoc_moe_forward(const llmoc_moe_layer* L, const uint16_t* X, int 
   b.gather = nullptr;
   b.out = ws + w.partial;
   b.ldo = H;
-  if (!cuda_ok(tma && path == 0 ? launch_gemm_tma(MODE_PLAIN_F32, b, w.max_work, awq, st)
-                                : launch_gemm(MODE_PLAIN_F32, path, b, w.max_work, awq, ntiles, st),
+  if (!cuda_ok(umma && path == 0 ? launch_gemm_umma(MODE_PLAIN_F32, b, w.max_work, awq, st)
+               : tma && path == 0 ? launch_gemm_tma(MODE_PLAIN_F32, b, w.max_work, awq, st)
+                                  : launch_gemm(MODE_PLAIN_F32, path, b, w.max_work, awq, ntiles, st),
                "down"))
     return LLMOC_ERR_CUDA;
   se.mark(st);
