@@ -6,15 +6,19 @@
 //     D[m, n] = sum_k W[m, k] * X[n, k]
 // with K walked in 64-wide blocks through a kStages-deep shared-memory ring.
 //
-//   warps 1..4  producers: dequantise the INT4 fragment words of the block
-//               (w = (q - zp) * s, or q * s + z, rounded once to bf16) straight
-//               into the 128-byte-swizzled K-major layout the MMA reads, and
-//               cp.async-gather the block of the item's activation rows into
-//               the same layout; then fence.proxy.async and arrive on full[s].
-//   warp 0      allocates TMEM; lane 0 waits full[s], issues the four K=16
+//   warps 1..4  producers.  A kLoad-deep load ring receives, by cp.async, the
+//               raw INT4 fragment words (each lane copies exactly the words it
+//               will dequantise), their group scales (and zeros), and the
+//               block's slice of the item's activation rows, gathered into the
+//               128-byte-swizzled K-major layout the MMA reads; loads run
+//               kLoad - 1 blocks ahead.  Each block's words are then
+//               dequantised (w = (q - zp) * s, or q * s + z, rounded once to
+//               bf16) into a 2-slot A ring in the same swizzled layout; then
+//               fence.proxy.async and arrive on full[a].
+//   warp 0      allocates TMEM; lane 0 waits full[a], issues the four K=16
 //               tcgen05.mma per projection (M = 128, N = rows rounded up to 16),
-//               and tcgen05.commit's the stage back to empty[s]; a final
-//               commit signals `done`.
+//               and tcgen05.commit's both the A slot (emptyA) and the load slot
+//               (emptyL) back to the producers; a final commit signals `done`.
 //   warps 1..4  epilogue: tcgen05.ld the accumulators (warp w reads TMEM
 //               lanes 32*(w%4)..+31 = rows), SiLU*mul (gate/up) or fp32 (down),
 //               store to the expert-sorted output rows.
@@ -28,11 +32,14 @@ namespace llmoc {
 
 namespace {
 
-constexpr int kUStages = 3;
+constexpr int kLoad = 4;                   // load-ring depth (raw words, scales, activations)
+constexpr int kASlots = 2;                 // dequantised-A ring depth
 constexpr int kUProd = 4;                  // producer / epilogue warps
 constexpr int kUThreads = (1 + kUProd) * 32;
 constexpr int kTileA = 128 * 128;          // 128 rows x 64 bf16 (one swizzle atom wide)
 constexpr int kTileB = 128 * 128;          // up to 128 token rows x 64 bf16
+constexpr int kRawQ = 128 * 32;            // 128 rows x 64 nibbles (fragment order)
+constexpr int kRawS = 8 * 128;             // scales: 8 sub-tiles x up to 4 groups x 32 B
 constexpr uint64_t kUWaitNs = 1000000000ull;
 
 __device__ __forceinline__ uint32_t su32(const void* p) {
@@ -151,13 +158,27 @@ __device__ __forceinline__ uint32_t swz(int row, int k) {
 
 }  // namespace
 
+// Shared-memory plan (bytes), per projection count NP:
+//   A ring   kASlots x NP x kTileA        dequantised weights (swizzled)
+//   load     kLoad x [B kTileB | raw q NP x kRawQ | scales NP x kRawS | zeros NP x kRawS]
+template <int NP, bool AWQ>
+struct USmem {
+  static constexpr int kA = kASlots * NP * kTileA;
+  static constexpr int kOffQ = kTileB;
+  static constexpr int kOffS = kOffQ + NP * kRawQ;
+  static constexpr int kOffZ = kOffS + NP * kRawS;
+  static constexpr int kLoadSlot = kOffZ + (AWQ ? 0 : NP * kRawS);  // multiple of 1024
+  static constexpr int kBytes = kA + kLoad * kLoadSlot;
+};
+
 // grid.x = ceil(M / 128), grid.y = work-list bound.  Work items hold <= 128 rows.
 template <int MODE, int GSB, bool AWQ>
 __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a) {
   constexpr int NP = MODE == MODE_GATE_UP ? 2 : 1;
-  constexpr int kStage = NP * kTileA + kTileB;
+  constexpr int NG = GSB == 4 ? 1 : (GSB == 2 ? 1 : 2);  // groups per 64-wide block
+  using SM = USmem<NP, AWQ>;
   extern __shared__ __align__(1024) unsigned char usm[];
-  __shared__ __align__(8) uint64_t full[kUStages], empty[kUStages], done;
+  __shared__ __align__(8) uint64_t fullA[kASlots], emptyA[kASlots], emptyL[kLoad], done;
   __shared__ uint32_t tmem_base;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -167,14 +188,17 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a) {
   const int m0 = blockIdx.x * 128;
   const int nb = a.K >> 6;                       // 64-wide K blocks
   const int N = (it.nrows + 15) & ~15;           // MMA N (multiple of 16 for M = 128)
-  // 1024-byte aligned ring (the swizzle pattern is tied to absolute address bits)
-  unsigned char* ring = usm + ((1024 - (su32(usm) & 1023)) & 1023);
+  // 1024-byte aligned base (the swizzle pattern is tied to absolute address bits)
+  unsigned char* base = usm + ((1024 - (su32(usm) & 1023)) & 1023);
+  unsigned char* ringA = base;
+  unsigned char* ringL = base + SM::kA;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kUStages; ++s) {
-      mb_init(&full[s], kUProd);
-      mb_init(&empty[s], 1);
+    for (int s = 0; s < kASlots; ++s) {
+      mb_init(&fullA[s], kUProd);
+      mb_init(&emptyA[s], 1);
     }
+    for (int s = 0; s < kLoad; ++s) mb_init(&emptyL[s], 1);
     mb_init(&done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -194,21 +218,23 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a) {
     if (lane == 0) {
       const uint32_t idesc = instr_desc(128, N);
       for (int kb = 0; kb < nb; ++kb) {
-        const int s = kb % kUStages;
-        if (!mb_wait(&full[s], (kb / kUStages) & 1)) {
+        const int sa = kb % kASlots, sl = kb % kLoad;
+        if (!mb_wait(&fullA[sa], (kb / kASlots) & 1)) {
           ok = false;
           break;
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t sb = su32(ring + s * kStage);
+        const uint32_t ab = su32(ringA + sa * NP * kTileA);
+        const uint32_t bb = su32(ringL + sl * SM::kLoadSlot);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
-          const uint64_t db = smem_desc(sb + NP * kTileA + kk * 32);
+          const uint64_t db = smem_desc(bb + kk * 32);
 #pragma unroll
           for (int p = 0; p < NP; ++p)
-            umma(tmem + p * 128, smem_desc(sb + p * kTileA + kk * 32), db, idesc, (kb | kk) != 0);
+            umma(tmem + p * 128, smem_desc(ab + p * kTileA + kk * 32), db, idesc, (kb | kk) != 0);
         }
-        umma_commit(&empty[s]);
+        umma_commit(&emptyA[sa]);
+        umma_commit(&emptyL[sl]);
       }
       umma_commit(&done);  // fires when every MMA issued above has completed
     }
@@ -228,13 +254,13 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a) {
       rv[h] = rt < Mt;
       rts[h] = rv[h] ? rt : 0;
     }
-    // activation row sources of this thread's cp.async pieces (8 pieces per block)
+    // activation pieces of this thread (8 per block): row n = piece / 8, chunk c = piece % 8
     const unsigned char* bsrc[8];
     uint32_t bdst[8];
     bool bok[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const int piece = ptid + 128 * i;  // 0..1023: row n = piece / 8, 16-byte chunk c = piece % 8
+      const int piece = ptid + 128 * i;
       const int n = piece >> 3, c = piece & 7;
       bok[i] = n < it.nrows;
       const int pos = it.row0 + (bok[i] ? n : 0);
@@ -242,55 +268,85 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a) {
       bsrc[i] = reinterpret_cast<const unsigned char*>(a.B) + ((size_t)row * a.ldb + c * 8) * 2;
       bdst[i] = (uint32_t)((n >> 3) * 1024 + (n & 7) * 128 + ((c ^ (n & 7)) << 4));
     }
+    // scale pieces of this warp's two sub-tiles: per (p, h) NG groups x 32 B = 2*NG pieces
     const float zpf = AWQ ? (float)(128 + a.zp) : 128.f;
     const uint32_t zp2 = bf16x2_of(zpf);
 
-    auto issue_b = [&](int kb) {
-      const uint32_t base = su32(ring + (kb % kUStages) * kStage + NP * kTileA);
+    auto issue = [&](int kb) {  // block kb's loads into load slot kb % kLoad
+      unsigned char* sl = ringL + (kb % kLoad) * SM::kLoadSlot;
+      const uint32_t slu = su32(sl);
 #pragma unroll
       for (int i = 0; i < 8; ++i)
-        if (bok[i]) cp16(base + bdst[i], bsrc[i] + (size_t)kb * 128);
+        if (bok[i]) cp16(slu + bdst[i], bsrc[i] + (size_t)kb * 128);
+#pragma unroll
+      for (int p = 0; p < NP; ++p)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          if (rv[h]) cp16(slu + SM::kOffQ + p * kRawQ + ((2 * pw + h) * 32 + lane) * 16,
+                          P[p]->q + ((size_t)rts[h] * a.Kc + kb) * 32 + lane);
+          // scales (and zeros) of the block's group(s): lanes 0 .. 2*NG-1
+          const int grp0 = GSB == 4 ? (kb >> 1) : (GSB == 2 ? kb : kb * 2);
+          if (rv[h] && lane < 2 * NG) {
+            const size_t go = ((size_t)rts[h] * a.ng + grp0) * 16;
+            const int so = p * kRawS + (2 * pw + h) * 128 + lane * 16;
+            cp16(slu + SM::kOffS + so, reinterpret_cast<const unsigned char*>(P[p]->s + go) + lane * 16);
+            if (!AWQ) cp16(slu + SM::kOffZ + so, reinterpret_cast<const unsigned char*>(P[p]->z + go) + lane * 16);
+          }
+        }
       asm volatile("cp.async.commit_group;" ::: "memory");
     };
 
-    // prologue: B of block 0 (stage 0 is fresh)
-    if (nb > 0) issue_b(0);
+    // prologue: blocks 0 .. kLoad-2 (their slots are fresh)
+#pragma unroll
+    for (int d = 0; d < kLoad - 1; ++d) {
+      if (d < nb) issue(d);
+      else asm volatile("cp.async.commit_group;" ::: "memory");
+    }
     for (int kb = 0; kb < nb && ok; ++kb) {
-      const int s = kb % kUStages;
-      // (a) the next block's activations into its stage, once the MMA released it
-      if (kb + 1 < nb) {
-        const int kn = kb + 1;
-        if (kn >= kUStages && !mb_wait(&empty[kn % kUStages], ((kn / kUStages) - 1) & 1)) {
+      // (1) loads for block kb + kLoad - 1, once the MMA released its slot (block kb - 1)
+      const int kn = kb + kLoad - 1;
+      if (kn < nb) {
+        if (kn >= kLoad && !mb_wait(&emptyL[kn % kLoad], ((kn / kLoad) - 1) & 1)) {
           ok = false;
           break;
         }
-        issue_b(kn);
+        issue(kn);
       } else {
-        asm volatile("cp.async.commit_group;" ::: "memory");  // keep the group count uniform
+        asm volatile("cp.async.commit_group;" ::: "memory");
       }
-      // (b) dequantise this block's weights into stage s (its B was issued earlier;
-      // stage s itself was released before that issue)
-      unsigned char* sa = ring + s * kStage;
+      // (2) block kb's own pieces have landed (this lane's words, scales, activations)
+      asm volatile("cp.async.wait_group %0;" ::"n"(kLoad - 1) : "memory");
+      __syncwarp();  // scale pieces were copied by other lanes of this warp
+      // (3) dequantise into A slot kb % kASlots once the MMA of block kb - kASlots is done
+      const int sa = kb % kASlots;
+      if (kb >= kASlots && !mb_wait(&emptyA[sa], ((kb / kASlots) - 1) & 1)) {
+        ok = false;
+        break;
+      }
+      const unsigned char* sl = ringL + (kb % kLoad) * SM::kLoadSlot;
+      unsigned char* sA = ringA + sa * NP * kTileA;
 #pragma unroll
       for (int p = 0; p < NP; ++p) {
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          const int rt = rts[h];
-          const uint4 q4 = rv[h] ? *reinterpret_cast<const uint4*>(P[p]->q + ((size_t)rt * a.Kc + kb) * 32 + lane)
-                                 : make_uint4(0, 0, 0, 0);
+          const uint4 q4 = *reinterpret_cast<const uint4*>(sl + SM::kOffQ + p * kRawQ + ((2 * pw + h) * 32 + lane) * 16);
+          const __half* sp = reinterpret_cast<const __half*>(sl + SM::kOffS + p * kRawS + (2 * pw + h) * 128);
+          const __half* zq = reinterpret_cast<const __half*>(sl + SM::kOffZ + p * kRawS + (2 * pw + h) * 128);
+          uint32_t sc[NG][2], zc[NG][2];
+#pragma unroll
+          for (int q = 0; q < NG; ++q) {
+            sc[q][0] = bf16x2_of(__half2float(sp[q * 16 + g]));
+            sc[q][1] = bf16x2_of(__half2float(sp[q * 16 + g + 8]));
+            if (!AWQ) {
+              zc[q][0] = bf16x2_of(__half2float(zq[q * 16 + g]));
+              zc[q][1] = bf16x2_of(__half2float(zq[q * 16 + g + 8]));
+            }
+          }
           const uint32_t wds[4] = {q4.x, q4.y, q4.z, q4.w};
 #pragma unroll
           for (int wi = 0; wi < 4; ++wi) {
             const int kbb = wi >> 1, kt = wi & 1;  // 32-wide half of the block, k16 step
-            const int grp = GSB == 4 ? (kb >> 1) : (GSB == 2 ? kb : kb * 2 + kbb);
-            const __half* sp = P[p]->s + ((size_t)rt * a.ng + grp) * 16;
-            const uint32_t s0 = bf16x2_of(__half2float(sp[g])), s1 = bf16x2_of(__half2float(sp[g + 8]));
-            uint32_t z0 = 0, z1 = 0;
-            if (!AWQ) {
-              const __half* zq = P[p]->z + ((size_t)rt * a.ng + grp) * 16;
-              z0 = bf16x2_of(__half2float(zq[g]));
-              z1 = bf16x2_of(__half2float(zq[g + 8]));
-            }
+            const int q = NG == 2 ? kbb : 0;
             const uint32_t w = wds[wi];
             uint32_t r[4];
             r[0] = lop3_and_or(w, 0x000F000Fu, 0x43004300u);        // row g,   k+0, k+1
@@ -300,21 +356,19 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a) {
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               const uint32_t qd = h2sub(r[j], zp2);  // exact: q - zp (or q)
-              r[j] = AWQ ? h2mul(qd, (j & 1) ? s1 : s0) : h2fma(qd, (j & 1) ? s1 : s0, (j & 1) ? z1 : z0);
+              r[j] = AWQ ? h2mul(qd, sc[q][j & 1]) : h2fma(qd, sc[q][j & 1], zc[q][j & 1]);
             }
             const int row = (2 * pw + h) * 16 + g;  // row in the 128-row tile
             const int k = kbb * 32 + 8 * t + 4 * kt;
-            uint2 v0 = make_uint2(r[0], r[2]), v1 = make_uint2(r[1], r[3]);
-            *reinterpret_cast<uint2*>(sa + p * kTileA + swz(row, k)) = v0;
-            *reinterpret_cast<uint2*>(sa + p * kTileA + swz(row + 8, k)) = v1;
+            *reinterpret_cast<uint2*>(sA + p * kTileA + swz(row, k)) = make_uint2(r[0], r[2]);
+            *reinterpret_cast<uint2*>(sA + p * kTileA + swz(row + 8, k)) = make_uint2(r[1], r[3]);
           }
         }
       }
-      // (c) this block's activations have landed; publish the stage to the MMA proxy
-      asm volatile("cp.async.wait_group 1;" ::: "memory");
+      // (4) publish A (generic writes) and B (cp.async writes) to the MMA proxy
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
-      if (lane == 0) mb_arrive(&full[s]);
+      if (lane == 0) mb_arrive(&fullA[sa]);
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
     if (!ok && lane == 0 && a.err) atomicOr(a.err, 1);
@@ -364,7 +418,7 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a) {
 template <int MODE, int GSB, bool AWQ>
 static cudaError_t launch_u(const GemmArgs& a, int max_work, cudaStream_t st) {
   constexpr int NP = MODE == MODE_GATE_UP ? 2 : 1;
-  const size_t smem = (size_t)kUStages * (NP * kTileA + kTileB) + 1024;
+  const size_t smem = (size_t)USmem<NP, AWQ>::kBytes + 1024;
   cudaError_t e = cudaFuncSetAttribute(k_int4_umma<MODE, GSB, AWQ>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
