@@ -11,10 +11,12 @@
 //               will dequantise), their group scales (and zeros), and the
 //               block's slice of the item's activation rows, gathered into the
 //               128-byte-swizzled K-major layout the MMA reads; loads run
-//               kLoad - 1 blocks ahead.  Each block's words are then
-//               dequantised (w = (q - zp) * s, or q * s + z, rounded once to
-//               bf16) into a 2-slot A ring in the same swizzled layout; then
-//               fence.proxy.async and arrive on full[a].
+//               kAhead blocks ahead and reuse the slot of block kb - 2, so a
+//               producer never waits for the MMA it has just fed.  Each
+//               block's words are then dequantised (w = (q - zp) * s, or
+//               q * s + z, rounded once to bf16) into a kASlots-deep A ring in
+//               the same swizzled layout; then fence.proxy.async and arrive on
+//               full[a].
 //   warp 0      allocates TMEM; lane 0 waits full[a], issues the four K=16
 //               tcgen05.mma per projection (M = 128, N = rows rounded up to 16),
 //               and tcgen05.commit's both the A slot (emptyA) and the load slot
@@ -33,7 +35,8 @@ namespace llmoc {
 namespace {
 
 constexpr int kLoad = 4;                   // load-ring depth (raw words, scales, activations)
-constexpr int kASlots = 2;                 // dequantised-A ring depth
+constexpr int kAhead = kLoad - 2;          // blocks the loads run ahead (one MMA of slack)
+constexpr int kASlots = 3;                 // dequantised-A ring depth
 constexpr int kUProd = 4;                  // producer / epilogue warps
 constexpr int kUThreads = (1 + kUProd) * 32;
 constexpr int kTileA = 128 * 128;          // 128 rows x 64 bf16 (one swizzle atom wide)
@@ -296,15 +299,15 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a) {
       asm volatile("cp.async.commit_group;" ::: "memory");
     };
 
-    // prologue: blocks 0 .. kLoad-2 (their slots are fresh)
+    // prologue: blocks 0 .. kAhead-1 (their slots are fresh)
 #pragma unroll
-    for (int d = 0; d < kLoad - 1; ++d) {
+    for (int d = 0; d < kAhead; ++d) {
       if (d < nb) issue(d);
       else asm volatile("cp.async.commit_group;" ::: "memory");
     }
     for (int kb = 0; kb < nb && ok; ++kb) {
-      // (1) loads for block kb + kLoad - 1, once the MMA released its slot (block kb - 1)
-      const int kn = kb + kLoad - 1;
+      // (1) loads for block kb + kAhead, once the MMA released its slot (block kb + kAhead - kLoad)
+      const int kn = kb + kAhead;
       if (kn < nb) {
         if (kn >= kLoad && !mb_wait(&emptyL[kn % kLoad], ((kn / kLoad) - 1) & 1)) {
           ok = false;
@@ -315,7 +318,7 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a) {
         asm volatile("cp.async.commit_group;" ::: "memory");
       }
       // (2) block kb's own pieces have landed (this lane's words, scales, activations)
-      asm volatile("cp.async.wait_group %0;" ::"n"(kLoad - 1) : "memory");
+      asm volatile("cp.async.wait_group %0;" ::"n"(kAhead) : "memory");
       __syncwarp();  // scale pieces were copied by other lanes of this warp
       // (3) dequantise into A slot kb % kASlots once the MMA of block kb - kASlots is done
       const int sa = kb % kASlots;
