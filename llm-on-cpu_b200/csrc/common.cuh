@@ -24,6 +24,11 @@ namespace llmoc {
 // so lop3(w >> 4j, 0x000F000F, 0x43004300) yields A register j as a bf16
 // pair (128+q_lo, 128+q_hi).  The matching B (activation) elements of lane t
 // are 8 consecutive values x[kb*32 + 8t .. +7], one 16-byte load.
+// Lane L's 16 bytes are STORED at slot piece_slot(L) = L ^ ((L >> 3) & 3) of
+// the chunk (an involution): a warp still moves the whole 512-byte chunk, and
+// a reader that gives each thread one weight row (threads g = 0..7 reading
+// the pieces (g, t) of one t) touches eight different shared-memory bank
+// quads when the chunk is copied verbatim into shared memory.
 // Scales (and GPTQ zeros) are fp16, [M/16][ng][16] (tile, group, row).
 // M is padded to a multiple of 16, K to a multiple of 64 (pad nibbles
 // encode q = zp, i.e. weight 0, and pad scales are 0).
@@ -47,6 +52,8 @@ struct WorkItem {
   int nrows;
   int pad;
 };
+
+__host__ __device__ __forceinline__ int piece_slot(int lane) { return lane ^ ((lane >> 3) & 3); }
 
 constexpr int kChunkRows = 32;  // largest work item (tensor-core N = 4 x 8 rows)
 

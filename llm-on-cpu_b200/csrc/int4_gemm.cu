@@ -35,7 +35,7 @@ __global__ void k_repack(RepackArgs a) {
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n_words;
        i += (size_t)gridDim.x * blockDim.x) {
     const int wd = (int)(i & 3);
-    const int lane = (int)((i >> 2) & 31);
+    const int lane = piece_slot((int)((i >> 2) & 31));  // lane whose piece is stored here
     const size_t tc = i >> 7;  // rt * Kc + c
     const int c = (int)(tc % a.Kc);
     const int rt = (int)(tc / a.Kc);
@@ -77,9 +77,9 @@ __global__ void k_dequant(ProjDev P, int M, int K, int gs, int ng, int Kc, int a
     const int m = (int)(i / K), k = (int)(i % K);
     const int rt = m >> 4, r = m & 15, g = r & 7, hi = r >> 3;
     const int c = k >> 6, kb = (k >> 5) & 1, t = (k >> 3) & 3, kt = (k >> 2) & 1, e = k & 3;
-    const int lane = g * 4 + t;
+    const int slot32 = piece_slot(g * 4 + t);
     const uint32_t* q32 = reinterpret_cast<const uint32_t*>(P.q);
-    const uint32_t w = q32[(((size_t)rt * Kc + c) * 32 + lane) * 4 + kb * 2 + kt];
+    const uint32_t w = q32[(((size_t)rt * Kc + c) * 32 + slot32) * 4 + kb * 2 + kt];
     const int slot = (e & 1) * 4 + (e >> 1) * 2 + hi;
     const int q = (w >> (4 * slot)) & 0xF;
     const int grp = k / gs;
@@ -219,7 +219,7 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
   const unsigned char* zsrc[NP];
 #pragma unroll
   for (int p = 0; p < NP; ++p) {
-    wsrc[p] = reinterpret_cast<const unsigned char*>(P[p]->q + ((size_t)rtc * a.Kc + 2 * s0) * 32 + lane);
+    wsrc[p] = reinterpret_cast<const unsigned char*>(P[p]->q + ((size_t)rtc * a.Kc + 2 * s0) * 32 + piece_slot(lane));
     ssrc[p] = reinterpret_cast<const unsigned char*>(P[p]->s + ((size_t)rtc * a.ng + (size_t)s0 * NG) * 16);
     zsrc[p] = AWQ ? nullptr
                   : reinterpret_cast<const unsigned char*>(P[p]->z + ((size_t)rtc * a.ng + (size_t)s0 * NG) * 16);
@@ -503,7 +503,7 @@ __global__ void __launch_bounds__(128) k_int4_cc(GemmArgs a, int awq) {
     for (int c = 0; c < a.Kc; ++c) {
       uint4 qw[NP];
 #pragma unroll
-      for (int p = 0; p < NP; ++p) qw[p] = ldg_nc(P[p]->q + ((size_t)rt * a.Kc + c) * 32 + lane);
+      for (int p = 0; p < NP; ++p) qw[p] = ldg_nc(P[p]->q + ((size_t)rt * a.Kc + c) * 32 + piece_slot(lane));
 #pragma unroll
       for (int kb = 0; kb < 2; ++kb) {
         const int k32 = c * 64 + kb * 32;

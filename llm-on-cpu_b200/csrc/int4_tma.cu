@@ -213,7 +213,7 @@ __global__ void __launch_bounds__((kCWarps + 1) * 32) k_int4_tma(GemmArgs a) {
     if (live) {
 #pragma unroll
       for (int p = 0; p < NP; ++p) {
-        const unsigned char* wp = sb + (warp * 2 + p) * 1024 + lane * 16;
+        const unsigned char* wp = sb + (warp * 2 + p) * 1024 + piece_slot(lane) * 16;
         wq[p][0] = *reinterpret_cast<const uint4*>(wp);
         wq[p][1] = *reinterpret_cast<const uint4*>(wp + 512);
       }

@@ -11,53 +11,87 @@
 // The dequantised weights are the A operand and live in TENSOR MEMORY, not in
 // shared memory: each dequantising thread owns one weight row (= one TMEM
 // lane) and writes its bf16 values with tcgen05.st, so the only shared-memory
-// traffic of the MMA is the activation tile (B).  Accumulators are double-
+// operand of the MMA is the activation tile (B).  Accumulators are double-
 // buffered in TMEM so the epilogue of tile i overlaps the main loop of i+1.
 //
 //   TMEM (512 columns x 128 lanes, fp32 words)
 //     [0,128) [128,256)   accumulator buffers (N <= 128 columns each)
 //     [256 + 32 s, +32)   A slot s (s < kASlots): 128 rows x 64 k, bf16 pairs
 //
-//   warp 0      TMEM alloc; lane 0 issues tcgen05.mma (A from TMEM, B from a
-//               128B-swizzled K-major smem tile) and tcgen05.commit's the A
-//               slot, the load slot and, per tile, the accumulator buffer.
-//   warp 1      weight loader: cp.async of the block's raw INT4 words (8 x 512
-//               B fragment-order sub-tiles, stored XOR-swizzled so the row-per-
-//               thread reads below are bank-conflict free) and group scales
-//               (and GPTQ zeros); completion via cp.async.mbarrier.arrive.
-//   warp 14     activation loader: cp.async gather of the item's token rows
-//               (64 bf16 per row per block) into the swizzled B tile.
-//   warps 2..9  dequantisers: two per TMEM lane quadrant, alternating blocks;
-//               thread = one weight row: 16 words -> 64 bf16 w = (q - zp) * s
-//               (or q * s + z), one tcgen05.st.32x32b.x32 per block.
-//   warps 10..13 epilogue: tcgen05.ld the accumulator, SiLU*mul (gate/up,
-//               bf16 out) or fp32 (down), store to the expert-sorted rows.
+//   shared memory: a B ring (kBS slots of 128 token rows x 128 B, 128-byte
+//   swizzled K-major, one 64-wide K block each) and a weight ring (kWS slots of
+//   kSlotBlocks K blocks: raw INT4 words + group scales (+ GPTQ zeros)).
+//
+//   warp 0       TMEM alloc; lane 0 issues tcgen05.mma (A from TMEM, B from
+//                smem) and tcgen05.commit's the A slot, the B slot and, per
+//                tile, the accumulator buffer.
+//   warps 1..2   weight loaders (alternate slot uses): one instruction per
+//                slot whose lanes issue the 3-D TMA boxes of the raw words
+//                (fragment-order 512-byte chunks, whose piece order makes the
+//                row-per-thread reads below bank-conflict free), the scales
+//                and the zeros, from per-expert tensor maps built at layer
+//                creation.
+//   warps 3..6   activation loaders (alternate blocks): TMA 2-D boxes (32
+//                token rows x 64 bf16, 128-byte swizzle, 4 KB aligned) of the
+//                item's rows, which are contiguous: the down GEMM reads the
+//                expert-sorted gate/up output, and the gate/up GEMM a copy of
+//                the tokens gathered into expert-sorted order (k_gather_rows).
+//   warps 7..14  dequantisers: two per TMEM lane quadrant, alternating blocks;
+//                thread = one weight row: 16 words -> 64 bf16 w = (q - zp) * s
+//                (or q * s + z), one tcgen05.st.32x32b.x32 per block.  A
+//                weight slot is released as soon as its words are in registers.
+//   warps 15..18 epilogue: tcgen05.ld the accumulator, SiLU*mul (gate/up,
+//                bf16 out) or fp32 (down), store to the expert-sorted rows.
 //
 // Every wait is bounded (about 2^31 SM clocks, ~1 s); a wait that gives up
 // sets a CTA-wide abort flag, bit 0 of *err, and every role drains and exits.
 // TMEM is always freed.  No TMA multicast is used anywhere.
+#include <cstring>
+#include <cuda.h>  // CUtensorMap and its encode enums (the encoder is reached through cudart)
+
 #include "kernels.cuh"
 
 namespace llmoc {
 
 namespace {
 
-constexpr int kLoad = 8;                   // load-ring depth
 constexpr int kASlots = 4;                 // A slots in TMEM
 constexpr int kDeqWarps = 8;
 constexpr int kEpiWarps = 4;
-constexpr int kWarps = 3 + kDeqWarps + kEpiWarps;  // MMA, W loader, B loader
-constexpr int kUThreads = kWarps * 32;             // 480
-constexpr int kBLoaderWarp = 2 + kDeqWarps + kEpiWarps;  // 14
+// Warp roles.  A warp's TMA copies proceed about one issue round at a time
+// (measured: throughput per loader warp ~ bytes per instruction / ~0.45 us,
+// and it scales with the number of issuing warps), so the copies are spread
+// over several loader warps and each instruction carries several boxes.
+constexpr int kWLoaders = 2;               // warps 1, 2: weight slots u % 2
+constexpr int kBLoaders = 4;               // warps 3..6: B blocks j % 4
+constexpr int kWLoader0 = 1;
+constexpr int kBLoader0 = kWLoader0 + kWLoaders;          // 3
+constexpr int kDeq0 = kBLoader0 + kBLoaders;              // 7: warps 7..14 (lane quadrants 3,0,1,2 twice)
+constexpr int kEpi0 = kDeq0 + kDeqWarps;                  // 15: warps 15..18
+constexpr int kWarps = kEpi0 + kEpiWarps;                 // 19
+constexpr int kUThreads = kWarps * 32;                    // 608
 constexpr int kTmemCols = 512;
 constexpr int kAccCol = 0;                 // + 128 * buffer
 constexpr int kACol = 256;                 // + 32 * slot
-// load slot: B tile (<= 128 token rows x 128 B) | raw words 8 x 512 B | scales | zeros
-constexpr int kOffQ = 128 * 128;
-constexpr int kOffS = kOffQ + 8 * 512;
-constexpr int kOffZ = kOffS + 8 * 2 * 32;
-constexpr int kSlot = kOffZ + 8 * 2 * 32;  // 21504, a multiple of 1024
-constexpr int kUSmem = kLoad * kSlot + 1024;
+constexpr int kBS = 7;                     // B ring depth (one 64-wide K block per slot)
+constexpr int kBSlot = 128 * 128;          // <= 128 token rows x 64 bf16
+constexpr int kBBoxRows = 32;              // token rows per B TMA box (4 KB)
+// A weight slot holds kSlotBlocks 64-wide K blocks of the tile's 128 rows:
+//   raw words  [op][tile][block][512 B]  (2 ops x 4 tiles for gate/up, 1 x 8 for down)
+//   scales     [op][tile][group][32 B]   (groups of the slot's 256 k), then zeros (GPTQ)
+// Each part arrives in ONE TMA box per op: few, large copies keep enough bytes
+// in flight per SM (the copy engine's cost is per operation, not per byte).
+constexpr int kSlotBlocks = 4;
+constexpr int kWRaw = 8 * kSlotBlocks * 512;              // 16 KB
+constexpr int kWSc = 8 * 8 * 32;                          // up to 8 groups per slot (gs 32)
+constexpr int kWOffS = kWRaw;
+constexpr int kWOffZ = kWRaw + kWSc;
+template <bool AWQ>
+struct WRing {
+  static constexpr int kSlot = kWRaw + kWSc * (AWQ ? 1 : 2);  // 18 / 20 KB
+  static constexpr int kDepth = 5;                              // 20 blocks in flight
+  static constexpr int kSmem = kBS * kBSlot + kDepth * kSlot + 1024;  // + alignment slack
+};
 constexpr long long kWaitCycles = 1ll << 31;
 
 __device__ __forceinline__ uint32_t su32(const void* p) {
@@ -79,12 +113,26 @@ __device__ __forceinline__ bool mb_try(uint64_t* b, uint32_t par) {
       : "memory");
   return ok != 0;
 }
+// As mb_try, but a waiting thread is suspended (not spinning, so it takes no
+// issue slots from the working warps) until the phase completes or about
+// kSuspendNs have passed.
+constexpr uint32_t kSuspendNs = 1000000;
+__device__ __forceinline__ bool mb_try_sleep(uint64_t* b, uint32_t par) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      " selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(su32(b)), "r"(par), "r"(kSuspendNs)
+      : "memory");
+  return ok != 0;
+}
 // Wait for phase parity `par`.  Gives up when the CTA's abort flag is set or
 // after kWaitCycles (then sets the flag so every other role stops too).
 __device__ __forceinline__ bool mb_wait(uint64_t* b, uint32_t par, volatile int* abort) {
   if (mb_try(b, par)) return true;
   const long long t0 = clock64();
-  while (!mb_try(b, par)) {
+  while (!mb_try_sleep(b, par)) {
     if (*abort) return false;
     if (clock64() - t0 > kWaitCycles) {
       *abort = 1;
@@ -93,11 +141,53 @@ __device__ __forceinline__ bool mb_wait(uint64_t* b, uint32_t par, volatile int*
   }
   return true;
 }
-__device__ __forceinline__ void cp16(uint32_t dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+__device__ __forceinline__ void mb_expect(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes) : "memory");
 }
-__device__ __forceinline__ void cp_arrive(uint64_t* b) {
-  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(su32(b)) : "memory");
+// global -> shared bulk copy on the TMA engine (no multicast); 16-byte aligned,
+// size a multiple of 16; completes `bytes` of the barrier's transaction count
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(su32(bar))
+               : "memory");
+}
+// Before a loader exits: wait (bounded, whatever the abort flag says) until the
+// copies it issued into the last `depth` uses of a ring have landed, so no
+// asynchronous write reaches shared memory after the CTA is gone.
+__device__ __forceinline__ void drain_ring(uint64_t* full, int depth, uint32_t issued, uint32_t first,
+                                           uint32_t step) {
+  // uses first, first + step, ... < issued; only the last `depth` can be in flight
+  for (uint32_t u = first; u < issued; u += step) {
+    if (u + depth < issued) continue;
+    const long long t0 = clock64();
+    while (!mb_try(&full[u % depth], (u / depth) & 1))
+      if (clock64() - t0 > kWaitCycles) return;
+  }
+}
+// TMA 2-D tile load (no multicast) of box (x, y) into a 1024-byte aligned
+// destination; completes the box's bytes on the barrier
+// L2 policy for data read exactly once (the weights): evicted first, so the
+// streamed weights do not push the activation tiles (re-read by every M tile
+// of an item) out of L2
+__device__ __forceinline__ uint64_t l2_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* map, int x, int y, int z, uint64_t* bar,
+                                            uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, "
+      "{%2, %3, %4}], [%5], %6;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(su32(bar)), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(su32(bar))
+      : "memory");
 }
 
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
@@ -205,11 +295,15 @@ __device__ __forceinline__ int sub_rt(int mt, int st) {
 }  // namespace
 
 template <int MODE, int GSB, bool AWQ>
-__global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a) {
+__global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a, const __grid_constant__ CUtensorMap tmB) {
   constexpr int NG = GSB == 1 ? 2 : 1;  // scale groups per 64-wide block
   constexpr int kRowsTile = MODE == MODE_GATE_UP ? 64 : 128;
+  constexpr int kWS = WRing<AWQ>::kDepth;
+  constexpr int kWSlot = WRing<AWQ>::kSlot;
   extern __shared__ __align__(1024) unsigned char usm[];
-  __shared__ __align__(8) uint64_t fullL[kLoad], emptyL[kLoad], fullA[kASlots], emptyA[kASlots];
+  __shared__ __align__(8) uint64_t fullW[kWS], emptyW[kWS];
+  __shared__ __align__(8) uint64_t fullB[kBS], emptyB[kBS];
+  __shared__ __align__(8) uint64_t fullA[kASlots], emptyA[kASlots];
   __shared__ __align__(8) uint64_t accFull[2], accEmpty[2], done;
   __shared__ uint32_t tmem_base;
   __shared__ volatile int abort_flag;
@@ -219,15 +313,27 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a) {
   const int ntiles = *a.n_work * nmt;
   if ((int)blockIdx.x >= ntiles) return;  // uniform over the CTA
   const int nb = a.K >> 6;                // 64-wide K blocks per tile
-  unsigned char* ring = usm + ((1024 - (su32(usm) & 1023)) & 1023);  // 1024-aligned (SW128)
+  const int G = gridDim.x;
+  const uint32_t my_tiles = (uint32_t)((ntiles - (int)blockIdx.x + G - 1) / G);
+  const uint32_t my_blocks = my_tiles * (uint32_t)nb;
+  const int nsl = (nb + kSlotBlocks - 1) / kSlotBlocks;  // weight-slot uses per tile (nb is even)
+  constexpr int kGps = 4 * 64 / (GSB * 32);                // scale groups per weight slot
+  constexpr int kOps = MODE == MODE_GATE_UP ? 2 : 1;     // TMA boxes per part (gate, up)
+  constexpr int kTilesOp = 8 / kOps;                     // 16-row tiles per box
+  unsigned char* ringB = usm + ((1024 - (su32(usm) & 1023)) & 1023);  // 1024-aligned (SW128)
+  unsigned char* ringW = ringB + kBS * kBSlot;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kLoad; ++s) {
-      mb_init(&fullL[s], 64);  // 32 lanes of each loader warp (cp.async arrive)
-      mb_init(&emptyL[s], 1);
+    for (int s = 0; s < kWS; ++s) {
+      mb_init(&fullW[s], 1);   // weight loader's expect_tx (+ the bulk copies' bytes)
+      mb_init(&emptyW[s], kDeqWarps);  // every dequantising warp, after its last block of the slot
+    }
+    for (int s = 0; s < kBS; ++s) {
+      mb_init(&fullB[s], 1);   // B loader's expect_tx (+ the TMA boxes' bytes)
+      mb_init(&emptyB[s], 1);  // MMA commit
     }
     for (int s = 0; s < kASlots; ++s) {
-      mb_init(&fullA[s], 4);   // the four dequantising warps of the block
+      mb_init(&fullA[s], 4);
       mb_init(&emptyA[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -253,9 +359,10 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a) {
     // ------------------------------- MMA issuer -------------------------------
     if (lane == 0) {
       uint32_t j = 0, i = 0;
-      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++i) {
-        const WorkItem it = a.work[tile / nmt];
-        const uint32_t idesc = instr_desc(128, (it.nrows + 15) & ~15);
+      int nrows = a.work[blockIdx.x / nmt].nrows;
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += G, ++i) {
+        const int nxt = tile + G < ntiles ? a.work[(tile + G) / nmt].nrows : 0;  // prefetch
+        const uint32_t idesc = instr_desc(128, (nrows + 15) & ~15);
         const uint32_t b = i & 1;
         if (i >= 2 && !mb_wait(&accEmpty[b], ((i >> 1) - 1) & 1, &abort_flag)) {
           ok = false;
@@ -264,22 +371,22 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a) {
         tc_fence_after();
         const uint32_t dcol = tmem + kAccCol + 128 * b;
         for (int kb = 0; kb < nb; ++kb, ++j) {
-          const uint32_t sa = j % kASlots, sl = j % kLoad;
+          const uint32_t sa = j % kASlots, sb = j % kBS;
           if (!mb_wait(&fullA[sa], (j / kASlots) & 1, &abort_flag) ||
-              !mb_wait(&fullL[sl], (j / kLoad) & 1, &abort_flag)) {
+              !mb_wait(&fullB[sb], (j / kBS) & 1, &abort_flag)) {
             ok = false;
             break;
           }
-          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // cp.async data -> MMA
           tc_fence_after();
-          const uint32_t bb = su32(ring + sl * kSlot);
+          const uint32_t bb = su32(ringB + sb * kBSlot);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
             umma_ts(dcol, tmem + kACol + 32 * sa + 8 * kk, smem_desc(bb + kk * 32), idesc, (kb | kk) != 0);
           umma_commit(&emptyA[sa]);
-          umma_commit(&emptyL[sl]);
+          umma_commit(&emptyB[sb]);
         }
         if (ok) umma_commit(&accFull[b]);
+        nrows = nxt;
       }
       // every MMA issued above has completed once `done` fires
       umma_commit(&done);
@@ -291,111 +398,110 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a) {
         }
     }
     __syncwarp();
-  } else if (warp == 1) {
-    // --------------------------- weight loader -----------------------------------
-    const int g = lane >> 2, t = lane & 3;
-    const uint32_t qdst = kOffQ + g * 64 + (((t ^ (g >> 1)) & 3) << 4);
-    const bool shas = lane < 16 * NG;         // lanes carrying one 16 B scale piece
-    const int s_st = lane / (2 * NG), s_w = lane % (2 * NG);
-    const uint32_t sdst = (s_st * NG + (s_w >> 1)) * 32 + (s_w & 1) * 16;
-    uint32_t j = 0;
-    for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
-      const int mt = tile % nmt;
-      const ExpertDev& ex = a.experts[a.work[tile / nmt].expert];
-      const uint4* qb[8];
-#pragma unroll
-      for (int st = 0; st < 8; ++st)
-        qb[st] = sub_proj<MODE>(ex, a.proj, st).q + (size_t)sub_rt<MODE>(mt, st) * a.Kc * 32 + lane;
-      const ProjDev& sp = sub_proj<MODE>(ex, a.proj, s_st);
-      const size_t so = ((size_t)sub_rt<MODE>(mt, s_st) * a.ng + (s_w >> 1)) * 16 + (s_w & 1) * 8;
-      const __half* sb = sp.s + so;
-      const __half* zb = AWQ ? nullptr : sp.z + so;
-      for (int kb = 0; kb < nb; ++kb, ++j) {
-        const uint32_t sl = j % kLoad;
-        if (j >= kLoad && !mb_wait(&emptyL[sl], ((j / kLoad) - 1) & 1, &abort_flag)) {
+  } else if (warp >= kWLoader0 && warp < kWLoader0 + kWLoaders) {
+    // --------------------------- weight loaders -----------------------------------
+    // warp kWLoader0 + w fills weight-slot uses u = w, w + kWLoaders, ...; per use
+    // ONE instruction in which lane i < kOps * (AWQ ? 2 : 3) issues one 3-D TMA
+    // box: raw words {128 words, kSlotBlocks chunks, kTilesOp tiles} of op
+    // (gate/up), then its scales {16 rows, kGps groups, kTilesOp tiles}, then
+    // its zeros
+    constexpr uint32_t kWBytes = kWRaw + 256 * kGps * (AWQ ? 1 : 2);
+    const uint32_t wl = warp - kWLoader0;
+    const int part = lane / kOps, op = lane % kOps;  // part 0 raw, 1 scales, 2 zeros
+    const bool active = part == 0 || part == 1 || (!AWQ && part == 2);
+    const int proj = MODE == MODE_GATE_UP ? op : a.proj;  // gate, up / a.proj (down)
+    const uint32_t dst_off = part == 0 ? op * (kWRaw / kOps)
+                                       : (part == 1 ? kWOffS : kWOffZ) + op * (kTilesOp * kGps * 32);
+    const int ystep = part == 0 ? kSlotBlocks : kGps;
+    const CUtensorMap* maps = reinterpret_cast<const CUtensorMap*>(a.wmaps);
+    const uint64_t pol = l2_evict_first();
+    uint32_t u = 0;
+    int e_cur = a.work[blockIdx.x / nmt].expert;
+    for (int tile = blockIdx.x; tile < ntiles && ok; tile += G) {
+      const int e_nxt = tile + G < ntiles ? a.work[(tile + G) / nmt].expert : 0;  // prefetch
+      const int t0 = (tile % nmt) * kTilesOp;
+      const CUtensorMap* map = maps + (size_t)e_cur * kMapsPerExpert + (active ? part : 0) * 3 + proj;
+      for (int sidx = 0; sidx < nsl; ++sidx, ++u) {
+        if (u % kWLoaders != wl) continue;
+        const uint32_t sw = u % kWS;
+        if (u >= (uint32_t)kWS && !mb_wait(&emptyW[sw], ((u / kWS) - 1) & 1, &abort_flag)) {
           ok = false;
           break;
         }
-        const uint32_t base = su32(ring + sl * kSlot);
-#pragma unroll
-        for (int st = 0; st < 8; ++st) cp16(base + qdst + st * 512, qb[st] + (size_t)kb * 32);
-        if (shas) {
-          const int grp0 = GSB == 4 ? (kb >> 1) : (GSB == 2 ? kb : kb * 2);
-          cp16(base + kOffS + sdst, sb + (size_t)grp0 * 16);
-          if (!AWQ) cp16(base + kOffZ + sdst, zb + (size_t)grp0 * 16);
-        }
-        cp_arrive(&fullL[sl]);
+        if (lane == 0) mb_expect(&fullW[sw], kWBytes);
+        __syncwarp();
+        if (active) tma_load_3d(su32(ringW + sw * kWSlot) + dst_off, map, 0, sidx * ystep, t0, &fullW[sw], pol);
       }
+      e_cur = e_nxt;
     }
-    asm volatile("cp.async.wait_all;" ::: "memory");
-  } else if (warp == kBLoaderWarp) {
+    if (lane == 0) drain_ring(fullW, kWS, u, wl, kWLoaders);
+  } else if (warp >= kBLoader0 && warp < kBLoader0 + kBLoaders) {
     // --------------------------- activation loader -------------------------------
-    // lane: 16-byte chunk c of rows n0 + 4 i (i < 32) of the item
-    const int c = lane & 7, n0 = lane >> 3;
-    const uint32_t bd0 = n0 * 128 + ((c ^ n0) << 4);
-    const uint32_t bd1 = (n0 + 4) * 128 + ((c ^ (n0 + 4)) << 4);
-    const __nv_bfloat16* Bp = reinterpret_cast<const __nv_bfloat16*>(a.B);
+    // warp kBLoader0 + b loads blocks j = b, b + kBLoaders, ... (one instruction
+    // each): lane i < ceil(nrows / 32): box of token rows row0 + 32 i .. +31 (rows past the
+    // item belong to the next item or are out of bounds (zero-filled); their
+    // accumulator columns are never stored)
     uint32_t j = 0;
-    for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
-      const WorkItem it = a.work[tile / nmt];
-      uint32_t boff[32];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int n = n0 + 4 * i;
-        const int pos = it.row0 + (n < it.nrows ? n : 0);
-        const int row = a.gather ? a.gather[pos] / a.kk : pos;
-        boff[i] = (uint32_t)row * (uint32_t)a.ldb + c * 8;
-      }
+    WorkItem it = a.work[blockIdx.x / nmt];
+    for (int tile = blockIdx.x; tile < ntiles && ok; tile += G) {
+      const WorkItem nit = tile + G < ntiles ? a.work[(tile + G) / nmt] : it;  // prefetch
+      const int nbox = (it.nrows + kBBoxRows - 1) / kBBoxRows;
       for (int kb = 0; kb < nb; ++kb, ++j) {
-        const uint32_t sl = j % kLoad;
-        if (j >= kLoad && !mb_wait(&emptyL[sl], ((j / kLoad) - 1) & 1, &abort_flag)) {
+        if (j % kBLoaders != (uint32_t)(warp - kBLoader0)) continue;
+        const uint32_t sb = j % kBS;
+        if (j >= (uint32_t)kBS && !mb_wait(&emptyB[sb], ((j / kBS) - 1) & 1, &abort_flag)) {
           ok = false;
           break;
         }
-        const uint32_t base = su32(ring + sl * kSlot);
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (n0 + 4 * i < it.nrows)
-            cp16(base + (i >> 1) * 1024 + ((i & 1) ? bd1 : bd0), Bp + boff[i] + (size_t)kb * 64);
-        cp_arrive(&fullL[sl]);
+        if (lane == 0) mb_expect(&fullB[sb], (uint32_t)nbox * kBBoxRows * 128u);
+        __syncwarp();
+        if (lane < nbox)
+          tma_load_2d(su32(ringB + sb * kBSlot) + lane * kBBoxRows * 128, &tmB, kb * 64, it.row0 + kBBoxRows * lane,
+                      &fullB[sb]);
       }
+      it = nit;
     }
-    asm volatile("cp.async.wait_all;" ::: "memory");
-  } else if (warp < 2 + kDeqWarps) {
+    if (lane == 0) drain_ring(fullB, kBS, j, warp - kBLoader0, kBLoaders);
+  } else if (warp >= kDeq0 && warp < kDeq0 + kDeqWarps) {
     // ------------------------------- dequantisers -------------------------------
     const int quad = warp & 3;                  // TMEM lanes 32 quad .. +31
-    const uint32_t h = (warp - 2) >> 2;         // blocks j with j % 2 == h
-    const int st = 2 * quad + (lane >> 4);      // sub-tile of this thread's row
+    const int h = (warp - kDeq0) >> 2;          // blocks kb with kb % 2 == h
     const int r16 = lane & 15, g = r16 & 7, hi = r16 >> 3;
+    // this thread's row: box op and tile within the box
+    const int op = MODE == MODE_GATE_UP ? (lane >> 4) : 0;
+    const int tt = MODE == MODE_GATE_UP ? quad : 2 * quad + (lane >> 4);
     const uint32_t shift = 4 * hi;              // nibbles of row g+8 sit 4 bits higher
     uint32_t qsrc[4];
 #pragma unroll
-    for (int t = 0; t < 4; ++t) qsrc[t] = kOffQ + st * 512 + g * 64 + (((t ^ (g >> 1)) & 3) << 4);
-    const uint32_t ssrc = kOffS + st * NG * 32 + r16 * 2;
+    for (int t = 0; t < 4; ++t)
+      qsrc[t] = op * (kWRaw / kOps) + tt * kSlotBlocks * 512 + g * 64 + (((t ^ (g >> 1)) & 3) << 4);
+    const uint32_t ssrc = kWOffS + op * (kTilesOp * kGps * 32) + tt * kGps * 32 + r16 * 2;
     const float zpf = AWQ ? (float)(128 + a.zp) : 128.f;
     const uint32_t zp2 = bf16x2_of(zpf);
     const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16) + kACol;
-    uint32_t j = 0;
-    for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
-      for (int kb = 0; kb < nb; ++kb, ++j) {
-        if ((j & 1) != h) continue;
-        const uint32_t sl = j % kLoad, sa = j % kASlots;
-        if (!mb_wait(&fullL[sl], (j / kLoad) & 1, &abort_flag) ||
-            (j >= kASlots && !mb_wait(&emptyA[sa], ((j / kASlots) - 1) & 1, &abort_flag))) {
+    uint32_t j = 0;  // block counter (A slots)
+    for (uint32_t ti = 0; ti < my_tiles && ok; ++ti) {
+      for (int kb = h; kb < nb; kb += 2) {
+        const uint32_t jb = j + kb;
+        const uint32_t u = ti * nsl + kb / kSlotBlocks, sw = u % kWS, sa = jb % kASlots;
+        const int c = kb % kSlotBlocks;
+        if (!mb_wait(&fullW[sw], (u / kWS) & 1, &abort_flag)) {
           ok = false;
           break;
         }
-        tc_fence_after();
-        const unsigned char* sb = ring + sl * kSlot;
+        const unsigned char* wsl = ringW + sw * kWSlot;
         uint4 q4[4];
 #pragma unroll
-        for (int t = 0; t < 4; ++t) q4[t] = *reinterpret_cast<const uint4*>(sb + qsrc[t]);
+        for (int t = 0; t < 4; ++t) q4[t] = *reinterpret_cast<const uint4*>(wsl + qsrc[t] + c * 512);
+        // groups of this block within the slot: gs 128 -> c/2, gs 64 -> c, gs 32 -> 2c, 2c+1
+        const int gq = GSB == 4 ? (c >> 1) : (GSB == 2 ? c : 2 * c);
         uint32_t sc[NG], zc[NG];
 #pragma unroll
         for (int q = 0; q < NG; ++q) {
-          sc[q] = bf16x2_of(__half2float(*reinterpret_cast<const __half*>(sb + ssrc + q * 32)));
+          sc[q] = bf16x2_of(__half2float(*reinterpret_cast<const __half*>(wsl + ssrc + (gq + q) * 32)));
           if (!AWQ)
-            zc[q] = bf16x2_of(__half2float(*reinterpret_cast<const __half*>(sb + ssrc + q * 32 + kOffZ - kOffS)));
+            zc[q] = bf16x2_of(
+                __half2float(*reinterpret_cast<const __half*>(wsl + ssrc + (gq + q) * 32 + kWOffZ - kWOffS)));
         }
         uint32_t r[32];
 #pragma unroll
@@ -422,27 +528,36 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a) {
             r[col + 1] = p1;
           }
         }
+        // the slot's words are in registers: release it after this warp's last block in it
+        __syncwarp();
+        if (lane == 0 && (c + 2 >= kSlotBlocks || kb + 2 >= nb)) mb_arrive(&emptyW[sw]);
+        if (jb >= (uint32_t)kASlots && !mb_wait(&emptyA[sa], ((jb / kASlots) - 1) & 1, &abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
         tmem_st32(tl + 32 * sa, r);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mb_arrive(&fullA[sa]);
       }
+      j += nb;
     }
   } else {
     // --------------------------------- epilogue ---------------------------------
     const int quad = warp & 3;
     const uint32_t tq = tmem + ((uint32_t)(quad * 32) << 16) + kAccCol;
     uint32_t i = 0;
-    for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++i) {
-      const WorkItem it = a.work[tile / nmt];
+    for (int tile = blockIdx.x; tile < ntiles && ok; tile += G, ++i) {
+      const WorkItem it = a.work[tile / nmt];  // loads while the accumulator fills
       const int mt = tile % nmt;
-      const int N = (it.nrows + 15) & ~15;
       const uint32_t b = i & 1;
       if (!mb_wait(&accFull[b], (i >> 1) & 1, &abort_flag)) {
         ok = false;
         break;
       }
       tc_fence_after();
+      const int N = (it.nrows + 15) & ~15;
       const uint32_t ta = tq + 128 * b;
       for (int c0 = 0; c0 < N; c0 += 16) {
         float v[16];
@@ -493,6 +608,95 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a) {
   }
 }
 
+// Rows of the gate/up activations in expert-sorted order: Xs[p] = X[sorted[p] / kk]
+// (one warp per row, 16-byte pieces), so every work item's rows are contiguous
+// and its B tiles are plain TMA boxes.
+__global__ void __launch_bounds__(256) k_gather_rows(const uint4* __restrict__ X, int H8,
+                                                     const int* __restrict__ sorted, int kk, int n,
+                                                     uint4* __restrict__ Xs) {
+  const int p = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (p >= n) return;
+  const uint4* src = X + (size_t)(sorted[p] / kk) * H8;
+  uint4* dst = Xs + (size_t)p * H8;
+  for (int c = threadIdx.x & 31; c < H8; c += 32) dst[c] = __ldg(src + c);
+}
+
+cudaError_t launch_gather_rows(const void* X, int H, const int* sorted, int kk, int n, void* Xs,
+                               cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  k_gather_rows<<<(n + 7) / 8, 256, 0, st>>>(reinterpret_cast<const uint4*>(X), H / 8, sorted, kk, n,
+                                             reinterpret_cast<uint4*>(Xs));
+  return cudaGetLastError();
+}
+
+namespace {
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiled tensor_map_encoder() {
+  static const EncodeTiled fn = []() -> EncodeTiled {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<EncodeTiled>(p);
+  }();
+  return fn;
+}
+// B operand: `rows` x K bf16, row stride ld elements; boxes of kBBoxRows rows x
+// 64 elements (128 B, the 128-byte swizzle span); out-of-bounds rows read zero.
+bool b_tensor_map(CUtensorMap* m, const void* base, int K, int rows, int ld) {
+  const EncodeTiled enc = tensor_map_encoder();
+  if (!enc || rows <= 0 || K <= 0 || (reinterpret_cast<uintptr_t>(base) & 15) || (ld * 2) % 16) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  const cuuint32_t box[2] = {64, (cuuint32_t)kBBoxRows};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+}  // namespace
+
+bool build_umma_weight_maps(const ExpertDev* h, int n_exp, int inter, int hidden, int gs, bool gptq,
+                            void* host_out) {
+  static_assert(sizeof(CUtensorMap) == kTensorMapBytes, "tensor map size");
+  const EncodeTiled enc = tensor_map_encoder();
+  if (!enc || gs <= 0 || 256 % gs) return false;
+  CUtensorMap* out = static_cast<CUtensorMap*>(host_out);
+  memset(host_out, 0, (size_t)n_exp * kMapsPerExpert * sizeof(CUtensorMap));
+  for (int e = 0; e < n_exp; ++e)
+    for (int proj = 0; proj < 3; ++proj) {
+      const ProjDev& P = proj == 0 ? h[e].gate : (proj == 1 ? h[e].up : h[e].down);
+      const int M = proj < 2 ? inter : hidden, K = proj < 2 ? hidden : inter;
+      const cuuint64_t Kc = (cuuint64_t)(K / 64), Mt = (cuuint64_t)(M / 16), ng = (cuuint64_t)(K / gs);
+      const cuuint32_t tiles = proj < 2 ? 4 : 8;  // 16-row tiles per box (64 or 128 weight rows)
+      const cuuint32_t estr[3] = {1, 1, 1};
+      {  // raw words: {128 words of a 512-byte chunk, chunk, tile}
+        const cuuint64_t dims[3] = {128, Kc, Mt};
+        const cuuint64_t strides[2] = {512, Kc * 512};
+        const cuuint32_t box[3] = {128, (cuuint32_t)kSlotBlocks, tiles};
+        if (enc(out + e * kMapsPerExpert + proj, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<uint4*>(P.q), dims,
+                strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+          return false;
+      }
+      for (int part = 1; part <= (gptq ? 2 : 1); ++part) {  // scales / zeros: {16 rows, group, tile}
+        const cuuint64_t dims[3] = {16, ng, Mt};
+        const cuuint64_t strides[2] = {32, ng * 32};
+        const cuuint32_t box[3] = {16, (cuuint32_t)(256 / gs), tiles};
+        const __half* base = part == 1 ? P.s : P.z;
+        if (!base || enc(out + e * kMapsPerExpert + part * 3 + proj, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3,
+                         const_cast<__half*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+          return false;
+      }
+    }
+  return true;
+}
+
 namespace {
 int sm_count() {
   static int n[64] = {0};
@@ -509,35 +713,39 @@ int sm_count() {
 }  // namespace
 
 template <int MODE, int GSB, bool AWQ>
-static cudaError_t launch_u(const GemmArgs& a, int max_work, cudaStream_t st) {
+static cudaError_t launch_u(const GemmArgs& a, int max_work, int b_rows, cudaStream_t st) {
+  CUtensorMap tmB;
+  if (!b_tensor_map(&tmB, a.B, a.K, b_rows, a.ldb)) return cudaErrorInvalidValue;
+  constexpr int smem = WRing<AWQ>::kSmem;
   cudaError_t e = cudaFuncSetAttribute(k_int4_umma<MODE, GSB, AWQ>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kUSmem);
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   const int nmt = a.M / (MODE == MODE_GATE_UP ? 64 : 128);
   const long long tiles = (long long)max_work * nmt;
   const int grid = (int)std::min<long long>(tiles, sm_count());
-  k_int4_umma<MODE, GSB, AWQ><<<grid, kUThreads, kUSmem, st>>>(a);
+  k_int4_umma<MODE, GSB, AWQ><<<grid, kUThreads, smem, st>>>(a, tmB);
   return cudaGetLastError();
 }
 
 template <int MODE, bool AWQ>
-static cudaError_t launch_u_gs(const GemmArgs& a, int max_work, cudaStream_t st) {
+static cudaError_t launch_u_gs(const GemmArgs& a, int max_work, int b_rows, cudaStream_t st) {
   switch (a.gs) {
-    case 32: return launch_u<MODE, 1, AWQ>(a, max_work, st);
-    case 64: return launch_u<MODE, 2, AWQ>(a, max_work, st);
-    default: return launch_u<MODE, 4, AWQ>(a, max_work, st);
+    case 32: return launch_u<MODE, 1, AWQ>(a, max_work, b_rows, st);
+    case 64: return launch_u<MODE, 2, AWQ>(a, max_work, b_rows, st);
+    default: return launch_u<MODE, 4, AWQ>(a, max_work, b_rows, st);
   }
 }
 
 // Requires M % 64 (gate/up) or M % 128 (down) == 0, K % 128 == 0, items of
-// at most 128 rows, gs in {32, 64, 128}.
-cudaError_t launch_gemm_umma(int mode, const GemmArgs& a, int max_work, int awq, cudaStream_t st) {
+// at most 128 rows, gs in {32, 64, 128}, and B = b_rows contiguous expert-
+// sorted rows (a.gather is not used).
+cudaError_t launch_gemm_umma(int mode, const GemmArgs& a, int max_work, int awq, int b_rows, cudaStream_t st) {
   if (max_work <= 0) return cudaSuccess;
   if (mode == MODE_GATE_UP)
-    return awq ? launch_u_gs<MODE_GATE_UP, true>(a, max_work, st)
-               : launch_u_gs<MODE_GATE_UP, false>(a, max_work, st);
-  return awq ? launch_u_gs<MODE_PLAIN_F32, true>(a, max_work, st)
-             : launch_u_gs<MODE_PLAIN_F32, false>(a, max_work, st);
+    return awq ? launch_u_gs<MODE_GATE_UP, true>(a, max_work, b_rows, st)
+               : launch_u_gs<MODE_GATE_UP, false>(a, max_work, b_rows, st);
+  return awq ? launch_u_gs<MODE_PLAIN_F32, true>(a, max_work, b_rows, st)
+             : launch_u_gs<MODE_PLAIN_F32, false>(a, max_work, b_rows, st);
 }
 
 }  // namespace llmoc

@@ -69,6 +69,7 @@ struct GemmArgs {
   int ldo;
   int out_bf16;           // GATE_UP output type (cc kernel): 1 bf16, 0 fp32
   int* err;               // device error word: bit 0 = a bounded wait gave up (may be null)
+  const void* wmaps;      // tcgen05 path: per-expert TMA maps of the weights (build_umma_weight_maps)
 };
 
 cudaError_t launch_repack(const RepackArgs& a, cudaStream_t st);
@@ -81,8 +82,20 @@ cudaError_t launch_gemm(int mode, int path, const GemmArgs& a, int max_work, int
 // memory stage ring (decode-size items, K % 128 == 0, gs in {32, 64, 128}).
 cudaError_t launch_gemm_tma(int mode, const GemmArgs& a, int max_work, int awq, cudaStream_t st);
 // int4_umma.cu: tcgen05.mma (TMEM accumulator) grouped GEMM for work items of
-// up to 128 rows (prefill-size groups); same K / group-size conditions.
-cudaError_t launch_gemm_umma(int mode, const GemmArgs& a, int max_work, int awq, cudaStream_t st);
+// up to 128 rows (prefill-size groups); same K / group-size conditions.  B is
+// b_rows contiguous expert-sorted rows read by TMA (a.gather unused).
+cudaError_t launch_gemm_umma(int mode, const GemmArgs& a, int max_work, int awq, int b_rows, cudaStream_t st);
+// TMA tensor maps (128 bytes each) of every expert's repacked weights for the
+// tcgen05 kernel, kMapsPerExpert per expert: [part * 3 + proj], part 0 raw
+// words, 1 scales, 2 zeros (GPTQ); proj 0 gate, 1 up, 2 down.  Built once per
+// layer on the host (host_out: n_exp * kMapsPerExpert * 128 bytes).
+constexpr int kMapsPerExpert = 9;
+constexpr int kTensorMapBytes = 128;
+bool build_umma_weight_maps(const ExpertDev* host_table, int n_exp, int inter, int hidden, int gs, bool gptq,
+                            void* host_out);
+// Xs[p, :] = X[sorted[p] / kk, :] for p < n (bf16 rows of H elements, H % 8 == 0).
+cudaError_t launch_gather_rows(const void* X, int H, const int* sorted, int kk, int n, void* Xs,
+                               cudaStream_t st);
 cudaError_t launch_combine(const float* d, const int* inverse, const float* w, int T, int kk, int H,
                            void* y, int y_bf16, int skip_tiny, cudaStream_t st);
 cudaError_t launch_quant_awq_sym(const __nv_bfloat16* W, int M, int K, int gs, int bf16_scale,

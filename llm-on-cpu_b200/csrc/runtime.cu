@@ -321,6 +321,7 @@ struct llmoc_moe_layer {
   char* arena = nullptr;
   size_t weight_bytes = 0;    // packed q + scales (+zeros), as streamed
   ExpertDev* table = nullptr; // device [n_exp]
+  void* wmaps = nullptr;      // device TMA maps of the weights (tcgen05 path), or null
   std::vector<ExpertDev> htable;
   uint16_t* router_w = nullptr;
   float* bias = nullptr;
@@ -355,9 +356,19 @@ int chunk_rows(int T) { return T <= 128 ? 8 : (gemm_path_pref() == 1 ? kChunkRow
 
 struct WsLayout {
   size_t logits, ids, weights, offsets, sorted, inverse, work, n_work, n_active, err, mid, partial,
-      total;
+      xs, total;
   int max_work;
 };
+
+// The tcgen05 prefill GEMMs run when K of both GEMMs is a multiple of 128, the
+// group is 32/64/128 wide (every BASELINE shape) and the items are 128 rows.
+bool tc_shapes(const llmoc_moe_layer* L) {
+  const int gs = L->d.group_size;
+  return L->d.hidden % 128 == 0 && L->d.inter % 128 == 0 && (gs == 32 || gs == 64 || gs == 128);
+}
+bool use_umma(const llmoc_moe_layer* L, int T) {
+  return tc_shapes(L) && L->wmaps && chunk_rows(T) == 128 && gemm_path_pref() != 2;
+}
 
 WsLayout ws_layout(const llmoc_moe_layer* L, int T) {
   WsLayout w{};
@@ -382,6 +393,7 @@ WsLayout ws_layout(const llmoc_moe_layer* L, int T) {
   w.err = take(4);
   w.mid = take(n * L->d.inter * 2);
   w.partial = take(n * L->d.hidden * 4);
+  w.xs = use_umma(L, T) ? take(n * L->d.hidden * 2) : 0;  // tokens in expert-sorted order
   w.total = o;
   return w;
 }
@@ -497,6 +509,16 @@ llmoc_status layer_create(const llmoc_moe_layer_desc* d, const uint16_t* router_
         cudaStreamSynchronize(st) != cudaSuccess) {
       bail(LLMOC_ERR_CUDA, std::string("layer upload: ") + cudaGetErrorString(cudaGetLastError()));
       break;
+    }
+    if (tc_shapes(L)) {  // TMA maps of the resident weights for the tcgen05 prefill GEMMs
+      std::vector<unsigned char> maps((size_t)n_exp * kMapsPerExpert * kTensorMapBytes);
+      if (build_umma_weight_maps(L->htable.data(), n_exp, I, H, d->group_size, z, maps.data())) {
+        if (cudaMalloc(&L->wmaps, maps.size()) != cudaSuccess ||
+            cudaMemcpy(L->wmaps, maps.data(), maps.size(), cudaMemcpyHostToDevice) != cudaSuccess) {
+          bail(LLMOC_ERR_NO_MEMORY, "weight tensor maps");
+          break;
+        }
+      }
     }
   } while (false);
   if (st) {
@@ -896,6 +918,7 @@ void llmoc_moe_layer_destroy(llmoc_moe_layer* L) {
   for (auto e : L->ev_pool) cudaEventDestroy(e);
   if (L->arena) cudaFree(L->arena);
   if (L->table) cudaFree(L->table);
+  if (L->wmaps) cudaFree(L->wmaps);
   if (L->router_w) cudaFree(L->router_w);
   if (L->bias) cudaFree(L->bias);
   delete L;
@@ -961,12 +984,18 @@ llmoc_status llmoc_moe_forward(const llmoc_moe_layer* L, const uint16_t* X, int 
   const bool awq = L->d.scheme == LLMOC_SCHEME_AWQ_SYM;
   // tensor cores when K of both GEMMs is a multiple of 128 and the group is
   // 32/64/128 wide (every BASELINE shape); the CUDA-core kernel otherwise
-  const int gs = L->d.group_size;
-  const bool tc = H % 128 == 0 && I % 128 == 0 && (gs == 32 || gs == 64 || gs == 128);
+  const bool tc = tc_shapes(L);
   int path = tc ? 0 : 2;
   const bool tma = tc && chunk_rows(T) == 8 && gemm_path_pref() == 3;
-  const bool umma = tc && chunk_rows(T) == 128;
+  const bool umma = use_umma(L, T);
   if (tc && gemm_path_pref() == 2) path = 2;
+  const int n_pairs = T * L->kk;
+  if (umma) {
+    if (!cuda_ok(launch_gather_rows(X, H, (const int*)(ws + w.sorted), L->kk, n_pairs, ws + w.xs, st),
+                 "gather"))
+      return LLMOC_ERR_CUDA;
+    count_launch(1);
+  }
   const int ntiles = std::min(4, chunk_rows(T) / 8);
   GemmArgs a{};
   a.experts = L->table;
@@ -986,7 +1015,12 @@ llmoc_status llmoc_moe_forward(const llmoc_moe_layer* L, const uint16_t* X, int 
   a.ldo = I;
   a.out_bf16 = 1;
   a.err = (int*)(ws + w.err);
-  if (!cuda_ok(umma && path == 0 ? launch_gemm_umma(MODE_GATE_UP, a, w.max_work, awq, st)
+  a.wmaps = L->wmaps;
+  if (umma) {  // B = the gathered rows, read by TMA
+    a.B = ws + w.xs;
+    a.gather = nullptr;
+  }
+  if (!cuda_ok(umma ? launch_gemm_umma(MODE_GATE_UP, a, w.max_work, awq, n_pairs, st)
                : tma && path == 0 ? launch_gemm_tma(MODE_GATE_UP, a, w.max_work, awq, st)
                                   : launch_gemm(MODE_GATE_UP, path, a, w.max_work, awq, ntiles, st),
                "gate/up"))
@@ -1003,7 +1037,7 @@ llmoc_status llmoc_moe_forward(const llmoc_moe_layer* L, const uint16_t* X, int 
   b.gather = nullptr;
   b.out = ws + w.partial;
   b.ldo = H;
-  if (!cuda_ok(umma && path == 0 ? launch_gemm_umma(MODE_PLAIN_F32, b, w.max_work, awq, st)
+  if (!cuda_ok(umma ? launch_gemm_umma(MODE_PLAIN_F32, b, w.max_work, awq, n_pairs, st)
                : tma && path == 0 ? launch_gemm_tma(MODE_PLAIN_F32, b, w.max_work, awq, st)
                                   : launch_gemm(MODE_PLAIN_F32, path, b, w.max_work, awq, ntiles, st),
                "down"))
