@@ -241,6 +241,46 @@ LLMOC_API llmoc_status llmoc_moe_forward_noalloc(const llmoc_moe_layer* layer, c
                                                  int T, uint16_t* Y, void* stream);
 LLMOC_API size_t llmoc_moe_noalloc_capacity(void);
 
+/* ------------------------------------------------- expert parallelism (EP)
+ * The reference gives only the contracts: expert e is owned by rank
+ * e % world (DeviceMesh::owner_rank with EpShard::kMod,
+ * src/contracts/device_mesh.h:63-72) and the transport is an all-to-all
+ * (ICollective::alltoall, src/contracts/collective.h:13).  A layer shard
+ * created with llmoc_moe_layer_create_ep holds the routed experts e with
+ * e % world == rank (owner-local id e / world), the replicated router and the
+ * shared expert.  One forward of T tokens on every rank is:
+ *   1. llmoc_moe_ep_dispatch: route the rank's T tokens over all n_experts,
+ *      order the T*topk routed pairs by (owner rank, owner-local expert,
+ *      token, slot), write their bf16 rows to send_rows [T*topk][hidden], the
+ *      owner-local expert ids to send_expert, and per-rank pair counts to
+ *      send_counts [world] (all device memory);
+ *   2. the caller exchanges counts, rows and expert ids with an all-to-all;
+ *   3. llmoc_moe_ep_experts on the received rows (any order; expert ids
+ *      owner-local) writes each row's expert output (bf16) to out_rows in the
+ *      same order;
+ *   4. the caller returns out_rows with the inverse all-to-all, so the source
+ *      gets its rows back in send order (ret_rows);
+ *   5. llmoc_moe_ep_combine (same workspace as step 1): the routed weights
+ *      times ret_rows, in slot order, plus the shared expert run locally,
+ *      into Y [T][hidden] (bf16).
+ * n_experts % world == 0.  llmoc_moe_forward / llmoc_moe_route refuse a shard
+ * with world > 1. */
+LLMOC_API llmoc_status llmoc_moe_layer_create_ep(const llmoc_moe_layer_desc* desc, const uint16_t* router_w,
+                                                 const float* bias, const llmoc_int4_view* experts,
+                                                 const llmoc_int4_view* shared, int device, int rank,
+                                                 int world, int on_device, llmoc_moe_layer** out);
+LLMOC_API size_t llmoc_moe_ep_source_workspace_bytes(const llmoc_moe_layer* layer, int max_tokens);
+LLMOC_API size_t llmoc_moe_ep_owner_workspace_bytes(const llmoc_moe_layer* layer, int max_rows);
+LLMOC_API llmoc_status llmoc_moe_ep_dispatch(const llmoc_moe_layer* layer, const uint16_t* X, int T,
+                                             void* workspace, size_t workspace_bytes, uint16_t* send_rows,
+                                             int32_t* send_expert, int32_t* send_counts, void* stream);
+LLMOC_API llmoc_status llmoc_moe_ep_experts(const llmoc_moe_layer* layer, const uint16_t* rows,
+                                            const int32_t* expert, int n, uint16_t* out_rows, void* workspace,
+                                            size_t workspace_bytes, void* stream);
+LLMOC_API llmoc_status llmoc_moe_ep_combine(const llmoc_moe_layer* layer, const uint16_t* X, int T,
+                                            const uint16_t* ret_rows, uint16_t* Y, void* workspace,
+                                            size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------ utilities */
 
 /* quant_awq_sym (tools/quantize_int4.py:150-166) on the device: W [M,K] bf16

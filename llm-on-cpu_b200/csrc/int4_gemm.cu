@@ -634,7 +634,7 @@ __global__ void k_combine(const float* __restrict__ d, const int* __restrict__ i
       wj[u] = 0.f;
       v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
       if (j < kk) {
-        wj[u] = w[(size_t)t * kk + j];
+        wj[u] = w ? w[(size_t)t * kk + j] : 1.f;
         const float* row = d + (size_t)inverse[(size_t)t * kk + j] * H;
         if (h + 3 < H) {
           v[u] = *reinterpret_cast<const float4*>(row + h);
@@ -738,6 +738,39 @@ cudaError_t launch_gemm(int mode, int path, const GemmArgs& a, int max_work, int
     else
       k_int4_cc<MODE_PLAIN_F32, __nv_bfloat16, 4><<<grid, 128, 0, st>>>(a, awq);
   }
+  return cudaGetLastError();
+}
+
+// Expert-parallel combine at the token's source rank: the routed slots' rows
+// come back from their owners as bf16 in the dispatch order (ret[inverse[t *
+// topk + j]]), the shared expert's fp32 row is computed locally (sh[sh_inv[t]]);
+// the same fmaf order as k_combine (routed j = 0..topk-1, then the shared slot).
+__global__ void k_combine_ep(const __nv_bfloat16* __restrict__ ret, const int* __restrict__ inverse,
+                             const float* __restrict__ w, int T, int topk, int H, const float* __restrict__ sh,
+                             const int* __restrict__ sh_inv, float sh_scale, __nv_bfloat16* __restrict__ y) {
+  const int t = blockIdx.y;
+  const int h = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  if (t >= T || h >= H) return;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int j = 0; j < topk; ++j) {
+    const float wj = w[(size_t)t * topk + j];
+    const __nv_bfloat16* row = ret + (size_t)inverse[(size_t)t * topk + j] * H;
+    for (int i = 0; i < 4 && h + i < H; ++i) acc[i] = __fmaf_rn(wj, __bfloat162float(row[h + i]), acc[i]);
+  }
+  if (sh) {
+    const float* row = sh + (size_t)sh_inv[t] * H;
+    for (int i = 0; i < 4 && h + i < H; ++i) acc[i] = __fmaf_rn(sh_scale, row[h + i], acc[i]);
+  }
+  for (int i = 0; i < 4 && h + i < H; ++i) y[(size_t)t * H + h + i] = __float2bfloat16_rn(acc[i]);
+}
+
+cudaError_t launch_combine_ep(const void* ret, const int* inverse, const float* w, int T, int topk, int H,
+                              const float* sh, const int* sh_inv, float sh_scale, void* y, cudaStream_t st) {
+  if (T <= 0) return cudaSuccess;
+  const int threads = 128;
+  dim3 grid(((H + 3) / 4 + threads - 1) / threads, T);
+  k_combine_ep<<<grid, threads, 0, st>>>((const __nv_bfloat16*)ret, inverse, w, T, topk, H, sh, sh_inv, sh_scale,
+                                         (__nv_bfloat16*)y);
   return cudaGetLastError();
 }
 

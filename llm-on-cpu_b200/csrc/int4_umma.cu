@@ -265,12 +265,11 @@ __device__ __forceinline__ uint32_t h2mul(uint32_t a, uint32_t b) {
   x = __hmul2(x, y);
   return *reinterpret_cast<uint32_t*>(&x);
 }
-__device__ __forceinline__ uint32_t h2fma(uint32_t a, uint32_t b, uint32_t c) {
-  __nv_bfloat162 x = *reinterpret_cast<__nv_bfloat162*>(&a);
-  const __nv_bfloat162 y = *reinterpret_cast<__nv_bfloat162*>(&b);
-  const __nv_bfloat162 z = *reinterpret_cast<__nv_bfloat162*>(&c);
-  x = __hfma2(x, y, z);
-  return *reinterpret_cast<uint32_t*>(&x);
+// (128 + q_lo, 128 + q_hi) as a bf16 pair -> bf16 pair of q * s + z
+__device__ __forceinline__ uint32_t gptq_pair(uint32_t v, float s, float z) {
+  const float lo = __uint_as_float(v << 16) - 128.f, hi = __uint_as_float(v & 0xFFFF0000u) - 128.f;
+  const __nv_bfloat162 r = __floats2bfloat162_rn(__fmaf_rn(lo, s, z), __fmaf_rn(hi, s, z));
+  return *reinterpret_cast<const uint32_t*>(&r);
 }
 __device__ __forceinline__ uint32_t bf16x2_of(float f) {
   const __nv_bfloat16 h = __float2bfloat16_rn(f);
@@ -495,13 +494,17 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a, const __
         for (int t = 0; t < 4; ++t) q4[t] = *reinterpret_cast<const uint4*>(wsl + qsrc[t] + c * 512);
         // groups of this block within the slot: gs 128 -> c/2, gs 64 -> c, gs 32 -> 2c, 2c+1
         const int gq = GSB == 4 ? (c >> 1) : (GSB == 2 ? c : 2 * c);
-        uint32_t sc[NG], zc[NG];
+        uint32_t sc[NG];  // AWQ: the scale as a bf16 pair
+        float sf[NG], zf[NG];  // GPTQ: scale and zero in fp32 (exact fp16 values)
 #pragma unroll
         for (int q = 0; q < NG; ++q) {
-          sc[q] = bf16x2_of(__half2float(*reinterpret_cast<const __half*>(wsl + ssrc + (gq + q) * 32)));
-          if (!AWQ)
-            zc[q] = bf16x2_of(
-                __half2float(*reinterpret_cast<const __half*>(wsl + ssrc + (gq + q) * 32 + kWOffZ - kWOffS)));
+          const float s16 = __half2float(*reinterpret_cast<const __half*>(wsl + ssrc + (gq + q) * 32));
+          if (AWQ) {
+            sc[q] = bf16x2_of(s16);
+          } else {
+            sf[q] = s16;
+            zf[q] = __half2float(*reinterpret_cast<const __half*>(wsl + ssrc + (gq + q) * 32 + kWOffZ - kWOffS));
+          }
         }
         uint32_t r[32];
 #pragma unroll
@@ -514,14 +517,12 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a, const __
             const uint32_t v = wds[wi] >> shift;
             uint32_t p0 = lop3_and_or(v, 0x000F000Fu, 0x43004300u);       // k+0, k+1
             uint32_t p1 = lop3_and_or(v >> 8, 0x000F000Fu, 0x43004300u);  // k+2, k+3
-            p0 = h2sub(p0, zp2);                                           // exact: q - zp (or q)
-            p1 = h2sub(p1, zp2);
-            if (AWQ) {
-              p0 = h2mul(p0, sc[q]);
-              p1 = h2mul(p1, sc[q]);
-            } else {
-              p0 = h2fma(p0, sc[q], zc[q]);
-              p1 = h2fma(p1, sc[q], zc[q]);
+            if (AWQ) {  // (q - zp) * s: an exact integer times the scale, rounded once
+              p0 = h2mul(h2sub(p0, zp2), sc[q]);
+              p1 = h2mul(h2sub(p1, zp2), sc[q]);
+            } else {  // q * s + z in fp32 (q * s exact), rounded once to bf16
+              p0 = gptq_pair(p0, sf[q], zf[q]);
+              p1 = gptq_pair(p1, sf[q], zf[q]);
             }
             const int col = kb2 * 16 + 4 * t + 2 * kt;  // TMEM column = k / 2
             r[col] = p0;

@@ -40,6 +40,13 @@ cudaError_t launch_router_logits(const void* X, bool x_is_f32, const uint16_t* W
                                  int H, float* logits, cudaStream_t st);
 cudaError_t launch_topk(const TopkArgs& a, cudaStream_t st);
 cudaError_t launch_permute(const PermArgs& a, cudaStream_t st);
+// expert parallelism (owner of expert e = rank e % world, local id e / world)
+cudaError_t launch_ep_keys(const int* ids, int n, int world, int e_loc, int* key, cudaStream_t st);
+cudaError_t launch_ep_meta(const int* offsets, const int* sorted, const int* key, int n, int world, int e_loc,
+                           int* counts, int* send_expert, cudaStream_t st);
+cudaError_t launch_fill_i32(int* p, int n, int v, cudaStream_t st);
+cudaError_t launch_combine_ep(const void* ret, const int* inverse, const float* w, int T, int topk, int H,
+                              const float* sh, const int* sh_inv, float sh_scale, void* y, cudaStream_t st);
 
 // ---- int4_gemm.cu
 struct RepackArgs {

@@ -24,6 +24,8 @@
 // the inverse map, and the list of work items (<= 32 pairs of one expert).
 #include <cfloat>
 
+#include <algorithm>
+
 #include "kernels.cuh"
 
 namespace llmoc {
@@ -400,6 +402,51 @@ cudaError_t launch_permute(const PermArgs& a, cudaStream_t st) {
                                        (int)smem);
   if (e != cudaSuccess) return e;
   k_permute<<<1, kPermThreads, smem, st>>>(a);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------ expert parallelism
+// Expert e is owned by rank e % world and is local expert e / world there (the
+// reference's DeviceMesh::owner_rank with EpShard::kMod).  Sorting the routed
+// pairs by key = owner * e_loc + local id groups them by destination rank, in
+// the owner's local expert order.
+
+__global__ void k_ep_keys(const int* __restrict__ ids, int n, int world, int e_loc, int* __restrict__ key) {
+  for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < n; p += gridDim.x * blockDim.x) {
+    const int e = ids[p];
+    key[p] = (e % world) * e_loc + e / world;
+  }
+}
+
+// counts[r] = pairs sent to rank r; send_expert[q] = owner-local expert of the
+// q-th pair in key order
+__global__ void k_ep_meta(const int* __restrict__ offsets, const int* __restrict__ sorted,
+                          const int* __restrict__ key, int n, int world, int e_loc, int* __restrict__ counts,
+                          int* __restrict__ send_expert) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < world) counts[i] = offsets[(i + 1) * e_loc] - offsets[i * e_loc];
+  for (int q = i; q < n; q += gridDim.x * blockDim.x) send_expert[q] = key[sorted[q]] % e_loc;
+}
+
+__global__ void k_fill_i32(int* __restrict__ p, int n, int v) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) p[i] = v;
+}
+
+cudaError_t launch_ep_keys(const int* ids, int n, int world, int e_loc, int* key, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  k_ep_keys<<<std::min((n + 255) / 256, 1184), 256, 0, st>>>(ids, n, world, e_loc, key);
+  return cudaGetLastError();
+}
+cudaError_t launch_ep_meta(const int* offsets, const int* sorted, const int* key, int n, int world, int e_loc,
+                           int* counts, int* send_expert, cudaStream_t st) {
+  const int m = std::max(n, world);
+  k_ep_meta<<<std::min((m + 255) / 256, 1184), 256, 0, st>>>(offsets, sorted, key, n, world, e_loc, counts,
+                                                            send_expert);
+  return cudaGetLastError();
+}
+cudaError_t launch_fill_i32(int* p, int n, int v, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  k_fill_i32<<<std::min((n + 255) / 256, 1184), 256, 0, st>>>(p, n, v);
   return cudaGetLastError();
 }
 

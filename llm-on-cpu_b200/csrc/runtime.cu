@@ -315,8 +315,10 @@ int dense_gemm_host(const float* X, int n, const llmoc_int4_view* W, float* Y) {
 struct llmoc_moe_layer {
   llmoc_moe_layer_desc d{};
   int device = 0;
-  int n_exp = 0;  // routed + shared
+  int n_exp = 0;  // routed + shared experts held by this layer object
   int kk = 0;     // slots per token
+  int ep_rank = 0, ep_world = 1;  // expert parallelism: this rank holds experts e % ep_world == ep_rank
+  int e_loc = 0;                  // routed experts held (n_experts / ep_world), as local ids e / ep_world
   Geo gu, dn;     // gate/up [I,H] and down [H,I] geometry
   char* arena = nullptr;
   size_t weight_bytes = 0;    // packed q + scales (+zeros), as streamed
@@ -366,25 +368,32 @@ bool tc_shapes(const llmoc_moe_layer* L) {
   const int gs = L->d.group_size;
   return L->d.hidden % 128 == 0 && L->d.inter % 128 == 0 && (gs == 32 || gs == 64 || gs == 128);
 }
-bool use_umma(const llmoc_moe_layer* L, int T) {
-  return tc_shapes(L) && L->wmaps && chunk_rows(T) == 128 && gemm_path_pref() != 2;
+
+// Items hold at most `chunk` rows: 8 for decode-size groups (register-fed
+// tensor-core kernel), 128 for the tcgen05 kernel.
+int chunk_for_rows(int pairs, int groups) {
+  return pairs <= 8 * std::max(1, groups) + groups / 2 ? 8 : (gemm_path_pref() == 1 ? kChunkRows : 128);
+}
+bool use_umma_c(const llmoc_moe_layer* L, int chunk) {
+  return tc_shapes(L) && L->wmaps && chunk == 128 && gemm_path_pref() != 2;
 }
 
-WsLayout ws_layout(const llmoc_moe_layer* L, int T) {
+// Workspace of one grouped run over T rows with kk slots each, permuted over
+// n_perm groups; `logits` adds the router's [T, n_experts] logits.
+WsLayout ws_layout_g(const llmoc_moe_layer* L, int T, int kk, int n_perm, int chunk, bool logits) {
   WsLayout w{};
-  const size_t n = (size_t)T * L->kk;
+  const size_t n = (size_t)T * kk;
   size_t o = 0;
   auto take = [&](size_t bytes) {
     const size_t at = o;
     o += align256(bytes);
     return at;
   };
-  const int chunk = chunk_rows(T);
-  w.max_work = (int)(std::min<size_t>((size_t)L->n_exp, n) + (n + chunk - 1) / chunk);
-  w.logits = take((size_t)T * L->d.n_experts * 4);
+  w.max_work = (int)(std::min<size_t>((size_t)n_perm, n) + (n + chunk - 1) / chunk);
+  w.logits = logits ? take((size_t)T * L->d.n_experts * 4) : 0;
   w.ids = take(n * 4);
   w.weights = take(n * 4);
-  w.offsets = take((size_t)(L->n_exp + 1) * 4);
+  w.offsets = take((size_t)(n_perm + 1) * 4);
   w.sorted = take(n * 4);
   w.inverse = take(n * 4);
   w.work = take((size_t)std::max(1, w.max_work) * sizeof(WorkItem));
@@ -393,9 +402,13 @@ WsLayout ws_layout(const llmoc_moe_layer* L, int T) {
   w.err = take(4);
   w.mid = take(n * L->d.inter * 2);
   w.partial = take(n * L->d.hidden * 4);
-  w.xs = use_umma(L, T) ? take(n * L->d.hidden * 2) : 0;  // tokens in expert-sorted order
+  w.xs = use_umma_c(L, chunk) ? take(n * L->d.hidden * 2) : 0;  // rows in expert-sorted order
   w.total = o;
   return w;
+}
+
+WsLayout ws_layout(const llmoc_moe_layer* L, int T) {
+  return ws_layout_g(L, T, L->kk, L->n_exp, chunk_rows(T), true);
 }
 
 llmoc_status validate_desc(const llmoc_moe_layer_desc* d) {
@@ -425,9 +438,11 @@ bool view_matches(const llmoc_int4_view& v, int M, int K, const llmoc_moe_layer_
          (scheme == LLMOC_SCHEME_AWQ_SYM || v.zeros);
 }
 
+// world > 1: an expert-parallel shard holding the routed experts e with
+// e % world == rank (local id e / world), the router and the shared expert.
 llmoc_status layer_create(const llmoc_moe_layer_desc* d, const uint16_t* router_w, const float* bias,
                           const llmoc_int4_view* experts, const llmoc_int4_view* shared, int device,
-                          bool on_device, llmoc_moe_layer** out) {
+                          bool on_device, llmoc_moe_layer** out, int rank = 0, int world = 1) {
   if (!out) return fails(LLMOC_ERR_INVALID, "null out");
   *out = nullptr;
   llmoc_status s = validate_desc(d);
@@ -437,9 +452,13 @@ llmoc_status layer_create(const llmoc_moe_layer_desc* d, const uint16_t* router_
     return fails(LLMOC_ERR_INVALID, "sigmoid router needs a bias");
   if (d->has_shared && !shared) return fails(LLMOC_ERR_INVALID, "has_shared without shared views");
   const int E = d->n_experts, H = d->hidden, I = d->inter;
-  const int n_exp = E + (d->has_shared ? 1 : 0);
+  if (world < 1 || rank < 0 || rank >= world || E % world != 0)
+    return fails(LLMOC_ERR_INVALID, "expert parallelism needs 0 <= rank < world and n_experts % world == 0");
+  const int e_loc = E / world;
+  const int n_exp = e_loc + (d->has_shared ? 1 : 0);
+  auto view_of = [&](int e) { return e < e_loc ? experts + 3 * ((size_t)e * world + rank) : shared; };
   for (int e = 0; e < n_exp; ++e) {
-    const llmoc_int4_view* v = e < E ? experts + 3 * e : shared;
+    const llmoc_int4_view* v = view_of(e);
     if (!view_matches(v[0], I, H, d) || !view_matches(v[1], I, H, d) || !view_matches(v[2], H, I, d))
       return fails(LLMOC_ERR_INVALID, "expert " + std::to_string(e) + " view does not match the layer");
   }
@@ -455,6 +474,9 @@ llmoc_status layer_create(const llmoc_moe_layer_desc* d, const uint16_t* router_
   L->device = device;
   L->n_exp = n_exp;
   L->kk = d->topk + (d->has_shared ? 1 : 0);
+  L->ep_rank = rank;
+  L->ep_world = world;
+  L->e_loc = e_loc;
   const bool z = d->scheme == LLMOC_SCHEME_GPTQ_ASYM;
   L->gu = make_geo(I, H, d->group_size, z);
   L->dn = make_geo(H, I, d->group_size, z);
@@ -494,7 +516,7 @@ llmoc_status layer_create(const llmoc_moe_layer_desc* d, const uint16_t* router_
     L->htable.resize(n_exp);
     char* p = L->arena;
     for (int e = 0; e < n_exp && rc == LLMOC_OK; ++e) {
-      const llmoc_int4_view* v = e < E ? experts + 3 * e : shared;
+      const llmoc_int4_view* v = view_of(e);
       ExpertDev& ed = L->htable[e];
       if (!repack_into(v[0], on_device, L->gu, p, st, &ed.gate)) bail(LLMOC_ERR_CUDA, t_err);
       p += L->gu.total();
@@ -580,6 +602,25 @@ struct StageEvents {
   }
 };
 
+llmoc_status run_permute(const int* ids, int n, int n_perm, int chunk, const WsLayout& w, char* ws,
+                         cudaStream_t st) {
+  PermArgs pa{};
+  pa.ids = ids;
+  pa.n = n;
+  pa.n_exp = n_perm;
+  pa.offsets = (int*)(ws + w.offsets);
+  pa.sorted = (int*)(ws + w.sorted);
+  pa.inverse = (int*)(ws + w.inverse);
+  pa.work = (WorkItem*)(ws + w.work);
+  pa.n_work = (int*)(ws + w.n_work);
+  pa.n_active = (int*)(ws + w.n_active);
+  pa.err = (int*)(ws + w.err);
+  pa.chunk = chunk;
+  if (!cuda_ok(launch_permute(pa, st), "permute")) return LLMOC_ERR_CUDA;
+  count_launch(1);
+  return LLMOC_OK;
+}
+
 llmoc_status run_route(const llmoc_moe_layer* L, const uint16_t* X, int T, const WsLayout& w,
                        char* ws, cudaStream_t st, StageEvents* se = nullptr) {
   const int E = L->d.n_experts, H = L->d.hidden;
@@ -603,22 +644,138 @@ llmoc_status run_route(const llmoc_moe_layer* L, const uint16_t* X, int T, const
   ta.weights = (float*)(ws + w.weights);
   if (!cuda_ok(launch_topk(ta, st), "topk")) return LLMOC_ERR_CUDA;
   if (se) se->mark(st);
-  PermArgs pa{};
-  pa.ids = ta.ids;
-  pa.n = T * L->kk;
-  pa.n_exp = L->n_exp;
-  pa.offsets = (int*)(ws + w.offsets);
-  pa.sorted = (int*)(ws + w.sorted);
-  pa.inverse = (int*)(ws + w.inverse);
-  pa.work = (WorkItem*)(ws + w.work);
-  pa.n_work = (int*)(ws + w.n_work);
-  pa.n_active = (int*)(ws + w.n_active);
-  pa.err = (int*)(ws + w.err);
-  pa.chunk = chunk_rows(T);
-  if (!cuda_ok(launch_permute(pa, st), "permute")) return LLMOC_ERR_CUDA;
+  count_launch(2);
+  llmoc_status rc = run_permute(ta.ids, T * L->kk, L->n_exp, chunk_rows(T), w, ws, st);
   if (se) se->mark(st);
-  count_launch(3);
+  return rc;
+}
+
+// Grouped expert FFN over R rows of X (kk slots per row, expert ids and weights
+// in the workspace, already permuted): gather (tcgen05 path), gate/up +
+// SiLU*mul, down; then, when Y is given, the weighted sum of each row's kk
+// slots into Y (bf16; `weights` null = 1).
+llmoc_status run_ffn(const llmoc_moe_layer* L, const uint16_t* X, int R, int kk, int chunk, const WsLayout& w,
+                     char* ws, uint16_t* Y, const float* weights, cudaStream_t st, StageEvents* se = nullptr) {
+  const int H = L->d.hidden, I = L->d.inter;
+  const bool awq = L->d.scheme == LLMOC_SCHEME_AWQ_SYM;
+  // tensor cores when K of both GEMMs is a multiple of 128 and the group is
+  // 32/64/128 wide (every BASELINE shape); the CUDA-core kernel otherwise
+  const bool tc = tc_shapes(L);
+  int path = tc ? 0 : 2;
+  const bool tma = tc && chunk == 8 && gemm_path_pref() == 3;
+  const bool umma = use_umma_c(L, chunk);
+  if (tc && gemm_path_pref() == 2) path = 2;
+  const int n_pairs = R * kk;
+  if (umma) {
+    if (!cuda_ok(launch_gather_rows(X, H, (const int*)(ws + w.sorted), kk, n_pairs, ws + w.xs, st), "gather"))
+      return LLMOC_ERR_CUDA;
+    count_launch(1);
+  }
+  const int ntiles = std::min(4, chunk / 8);
+  GemmArgs a{};
+  a.experts = L->table;
+  a.M = I;
+  a.K = H;
+  a.Kc = L->gu.Kc;
+  a.gs = L->d.group_size;
+  a.ng = L->gu.ng;
+  a.zp = L->d.awq_zp;
+  a.B = X;
+  a.ldb = H;
+  a.gather = (const int*)(ws + w.sorted);
+  a.kk = kk;
+  a.work = (const WorkItem*)(ws + w.work);
+  a.n_work = (const int*)(ws + w.n_work);
+  a.out = ws + w.mid;
+  a.ldo = I;
+  a.out_bf16 = 1;
+  a.err = (int*)(ws + w.err);
+  a.wmaps = L->wmaps;
+  if (umma) {  // B = the gathered rows, read by TMA
+    a.B = ws + w.xs;
+    a.gather = nullptr;
+  }
+  if (!cuda_ok(umma ? launch_gemm_umma(MODE_GATE_UP, a, w.max_work, awq, n_pairs, st)
+               : tma && path == 0 ? launch_gemm_tma(MODE_GATE_UP, a, w.max_work, awq, st)
+                                  : launch_gemm(MODE_GATE_UP, path, a, w.max_work, awq, ntiles, st),
+               "gate/up"))
+    return LLMOC_ERR_CUDA;
+  if (se) se->mark(st);
+  GemmArgs b = a;
+  b.proj = 2;
+  b.M = H;
+  b.K = I;
+  b.Kc = L->dn.Kc;
+  b.ng = L->dn.ng;
+  b.B = ws + w.mid;
+  b.ldb = I;
+  b.gather = nullptr;
+  b.out = ws + w.partial;
+  b.ldo = H;
+  if (!cuda_ok(umma ? launch_gemm_umma(MODE_PLAIN_F32, b, w.max_work, awq, n_pairs, st)
+               : tma && path == 0 ? launch_gemm_tma(MODE_PLAIN_F32, b, w.max_work, awq, st)
+                                  : launch_gemm(MODE_PLAIN_F32, path, b, w.max_work, awq, ntiles, st),
+               "down"))
+    return LLMOC_ERR_CUDA;
+  if (se) se->mark(st);
+  count_launch(2);
+  if (Y) {
+    if (!cuda_ok(launch_combine((const float*)(ws + w.partial), (const int*)(ws + w.inverse), weights, R, kk, H, Y,
+                                1, 0, st),
+                 "combine"))
+      return LLMOC_ERR_CUDA;
+    count_launch(1);
+  }
+  if (se) se->mark(st);
   return LLMOC_OK;
+}
+
+// Expert-parallel source-rank workspace (llmoc_moe_ep_dispatch, then
+// llmoc_moe_ep_combine with the same workspace): routing of the T tokens over
+// all n_experts (topk routed slots, no shared slot), the pairs ordered by
+// (owner rank, owner-local expert, token, slot); then the shared expert's run
+// over the T tokens.
+struct EpSrcLayout {
+  size_t logits, ids, weights, key, offsets, sorted, inverse, work, n_work, n_active, err;
+  size_t sh = 0;     // shared-expert grouped run (ws_layout_g with kk = 1)
+  WsLayout shl{};
+  int sh_chunk = 8;
+  size_t total;
+};
+EpSrcLayout ep_src_layout(const llmoc_moe_layer* L, int T) {
+  EpSrcLayout w{};
+  const size_t n = (size_t)T * L->d.topk;
+  const int E = L->d.n_experts;
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = o;
+    o += align256(bytes);
+    return at;
+  };
+  const int max_work = (int)(std::min<size_t>((size_t)E, n) + (n + 7) / 8);
+  w.logits = take((size_t)T * E * 4);
+  w.ids = take(n * 4);
+  w.weights = take(n * 4);
+  w.key = take(n * 4);
+  w.offsets = take((size_t)(E + 1) * 4);
+  w.sorted = take(n * 4);
+  w.inverse = take(n * 4);
+  w.work = take((size_t)std::max(1, max_work) * sizeof(WorkItem));
+  w.n_work = take(4);
+  w.n_active = take(4);
+  w.err = take(4);
+  if (L->d.has_shared) {
+    w.sh_chunk = chunk_for_rows(T, 1);
+    w.shl = ws_layout_g(L, T, 1, L->n_exp, w.sh_chunk, false);
+    w.sh = take(w.shl.total);
+  }
+  w.total = o;
+  return w;
+}
+// owner-rank workspace for `rows` received rows (the larger of the two item sizes)
+size_t ep_owner_bytes(const llmoc_moe_layer* L, int rows) {
+  return std::max(ws_layout_g(L, rows, 1, L->n_exp, 8, false).total,
+                  ws_layout_g(L, rows, 1, L->n_exp, gemm_path_pref() == 1 ? kChunkRows : 128, false).total);
 }
 
 }  // namespace
@@ -911,6 +1068,13 @@ llmoc_status llmoc_moe_layer_create_device(const llmoc_moe_layer_desc* desc,
   return layer_create(desc, router_w, bias, experts, shared, device, true, out);
 }
 
+llmoc_status llmoc_moe_layer_create_ep(const llmoc_moe_layer_desc* desc, const uint16_t* router_w,
+                                       const float* bias, const llmoc_int4_view* experts,
+                                       const llmoc_int4_view* shared, int device, int rank, int world,
+                                       int on_device, llmoc_moe_layer** out) {
+  return layer_create(desc, router_w, bias, experts, shared, device, on_device != 0, out, rank, world);
+}
+
 void llmoc_moe_layer_destroy(llmoc_moe_layer* L) {
   if (!L) return;
   DevGuard dg(L->device);
@@ -961,6 +1125,7 @@ llmoc_status llmoc_moe_route_views(const llmoc_moe_layer* L, int T, void* worksp
 llmoc_status llmoc_moe_route(const llmoc_moe_layer* L, const uint16_t* X, int T, void* workspace,
                              size_t workspace_bytes, void* stream) {
   if (!L || T < 0 || (T > 0 && !X)) return fails(LLMOC_ERR_INVALID, "bad arguments");
+  if (L->ep_world > 1) return fails(LLMOC_ERR_INVALID, "expert-parallel layer: use llmoc_moe_ep_*");
   if (T == 0) return LLMOC_OK;
   const WsLayout w = ws_layout(L, T);
   if (!workspace || workspace_bytes < w.total) return fails(LLMOC_ERR_WORKSPACE, "workspace too small");
@@ -971,6 +1136,7 @@ llmoc_status llmoc_moe_route(const llmoc_moe_layer* L, const uint16_t* X, int T,
 llmoc_status llmoc_moe_forward(const llmoc_moe_layer* L, const uint16_t* X, int T, uint16_t* Y,
                                void* workspace, size_t workspace_bytes, void* stream) {
   if (!L || T < 0 || (T > 0 && (!X || !Y))) return fails(LLMOC_ERR_INVALID, "bad arguments");
+  if (L->ep_world > 1) return fails(LLMOC_ERR_INVALID, "expert-parallel layer: use llmoc_moe_ep_*");
   if (T == 0) return LLMOC_OK;
   const WsLayout w = ws_layout(L, T);
   if (!workspace || workspace_bytes < w.total) return fails(LLMOC_ERR_WORKSPACE, "workspace too small");
@@ -980,76 +1146,9 @@ llmoc_status llmoc_moe_forward(const llmoc_moe_layer* L, const uint16_t* X, int 
   StageEvents se(L);
   llmoc_status rc = run_route(L, X, T, w, ws, st, &se);
   if (rc != LLMOC_OK) return rc;
-  const int H = L->d.hidden, I = L->d.inter;
-  const bool awq = L->d.scheme == LLMOC_SCHEME_AWQ_SYM;
-  // tensor cores when K of both GEMMs is a multiple of 128 and the group is
-  // 32/64/128 wide (every BASELINE shape); the CUDA-core kernel otherwise
-  const bool tc = tc_shapes(L);
-  int path = tc ? 0 : 2;
-  const bool tma = tc && chunk_rows(T) == 8 && gemm_path_pref() == 3;
-  const bool umma = use_umma(L, T);
-  if (tc && gemm_path_pref() == 2) path = 2;
-  const int n_pairs = T * L->kk;
-  if (umma) {
-    if (!cuda_ok(launch_gather_rows(X, H, (const int*)(ws + w.sorted), L->kk, n_pairs, ws + w.xs, st),
-                 "gather"))
-      return LLMOC_ERR_CUDA;
-    count_launch(1);
-  }
-  const int ntiles = std::min(4, chunk_rows(T) / 8);
-  GemmArgs a{};
-  a.experts = L->table;
-  a.M = I;
-  a.K = H;
-  a.Kc = L->gu.Kc;
-  a.gs = L->d.group_size;
-  a.ng = L->gu.ng;
-  a.zp = L->d.awq_zp;
-  a.B = X;
-  a.ldb = H;
-  a.gather = (const int*)(ws + w.sorted);
-  a.kk = L->kk;
-  a.work = (const WorkItem*)(ws + w.work);
-  a.n_work = (const int*)(ws + w.n_work);
-  a.out = ws + w.mid;
-  a.ldo = I;
-  a.out_bf16 = 1;
-  a.err = (int*)(ws + w.err);
-  a.wmaps = L->wmaps;
-  if (umma) {  // B = the gathered rows, read by TMA
-    a.B = ws + w.xs;
-    a.gather = nullptr;
-  }
-  if (!cuda_ok(umma ? launch_gemm_umma(MODE_GATE_UP, a, w.max_work, awq, n_pairs, st)
-               : tma && path == 0 ? launch_gemm_tma(MODE_GATE_UP, a, w.max_work, awq, st)
-                                  : launch_gemm(MODE_GATE_UP, path, a, w.max_work, awq, ntiles, st),
-               "gate/up"))
-    return LLMOC_ERR_CUDA;
-  se.mark(st);
-  GemmArgs b = a;
-  b.proj = 2;
-  b.M = H;
-  b.K = I;
-  b.Kc = L->dn.Kc;
-  b.ng = L->dn.ng;
-  b.B = ws + w.mid;
-  b.ldb = I;
-  b.gather = nullptr;
-  b.out = ws + w.partial;
-  b.ldo = H;
-  if (!cuda_ok(umma ? launch_gemm_umma(MODE_PLAIN_F32, b, w.max_work, awq, n_pairs, st)
-               : tma && path == 0 ? launch_gemm_tma(MODE_PLAIN_F32, b, w.max_work, awq, st)
-                                  : launch_gemm(MODE_PLAIN_F32, path, b, w.max_work, awq, ntiles, st),
-               "down"))
-    return LLMOC_ERR_CUDA;
-  se.mark(st);
-  if (!cuda_ok(launch_combine((const float*)(ws + w.partial), (const int*)(ws + w.inverse),
-                              (const float*)(ws + w.weights), T, L->kk, H, Y, 1, 0, st),
-               "combine"))
-    return LLMOC_ERR_CUDA;
-  se.mark(st);
+  rc = run_ffn(L, X, T, L->kk, chunk_rows(T), w, ws, Y, (const float*)(ws + w.weights), st, &se);
+  if (rc != LLMOC_OK) return rc;
   se.commit();
-  count_launch(3);
   return LLMOC_OK;
 }
 
@@ -1114,6 +1213,118 @@ llmoc_status llmoc_moe_stage_times(llmoc_moe_layer* L, float* ms, int* calls) {
 }
 
 uint64_t llmoc_kernel_launch_count(void) { return g_launches.load(); }
+
+// ------------------------------------------------------ expert parallelism
+
+size_t llmoc_moe_ep_source_workspace_bytes(const llmoc_moe_layer* L, int max_tokens) {
+  if (!L || max_tokens < 0) return 0;
+  return ep_src_layout(L, max_tokens).total;
+}
+
+size_t llmoc_moe_ep_owner_workspace_bytes(const llmoc_moe_layer* L, int max_rows) {
+  if (!L || max_rows < 0) return 0;
+  return ep_owner_bytes(L, max_rows);
+}
+
+llmoc_status llmoc_moe_ep_dispatch(const llmoc_moe_layer* L, const uint16_t* X, int T, void* workspace,
+                                   size_t workspace_bytes, uint16_t* send_rows, int32_t* send_expert,
+                                   int32_t* send_counts, void* stream) {
+  if (!L || T < 0 || (T > 0 && (!X || !send_rows || !send_expert)) || !send_counts)
+    return fails(LLMOC_ERR_INVALID, "bad arguments");
+  const EpSrcLayout w = ep_src_layout(L, T);
+  if (!workspace || workspace_bytes < w.total) return fails(LLMOC_ERR_WORKSPACE, "workspace too small");
+  DevGuard dg(L->device);
+  cudaStream_t st = (cudaStream_t)stream;
+  char* ws = (char*)workspace;
+  const int E = L->d.n_experts, H = L->d.hidden, k = L->d.topk, n = T * k;
+  if (T == 0) {
+    if (!cuda_ok(cudaMemsetAsync(send_counts, 0, sizeof(int32_t) * L->ep_world, st), "counts"))
+      return LLMOC_ERR_CUDA;
+    return LLMOC_OK;
+  }
+  float* logits = (float*)(ws + w.logits);
+  if (!cuda_ok(launch_router_logits(X, false, L->router_w, T, E, H, logits, st), "router")) return LLMOC_ERR_CUDA;
+  TopkArgs ta{};
+  ta.logits = logits;
+  ta.bias = L->bias;
+  ta.T = T;
+  ta.E = E;
+  ta.k = k;
+  ta.kk = k;  // routed slots only: the shared expert runs on the source rank
+  ta.router = L->d.router;
+  ta.routed_scaling = L->d.routed_scaling;
+  ta.shared_scale = L->d.shared_scale;
+  ta.has_shared = 0;
+  ta.ids = (int*)(ws + w.ids);
+  ta.weights = (float*)(ws + w.weights);
+  if (!cuda_ok(launch_topk(ta, st), "topk")) return LLMOC_ERR_CUDA;
+  int* key = (int*)(ws + w.key);
+  if (!cuda_ok(launch_ep_keys(ta.ids, n, L->ep_world, L->e_loc, key, st), "ep keys")) return LLMOC_ERR_CUDA;
+  PermArgs pa{};
+  pa.ids = key;
+  pa.n = n;
+  pa.n_exp = E;
+  pa.offsets = (int*)(ws + w.offsets);
+  pa.sorted = (int*)(ws + w.sorted);
+  pa.inverse = (int*)(ws + w.inverse);
+  pa.work = (WorkItem*)(ws + w.work);
+  pa.n_work = (int*)(ws + w.n_work);
+  pa.n_active = (int*)(ws + w.n_active);
+  pa.err = (int*)(ws + w.err);
+  pa.chunk = 8;
+  if (!cuda_ok(launch_permute(pa, st), "permute")) return LLMOC_ERR_CUDA;
+  if (!cuda_ok(launch_ep_meta(pa.offsets, pa.sorted, key, n, L->ep_world, L->e_loc, send_counts, send_expert, st),
+               "ep meta") ||
+      !cuda_ok(launch_gather_rows(X, H, pa.sorted, k, n, send_rows, st), "gather"))
+    return LLMOC_ERR_CUDA;
+  count_launch(6);
+  return LLMOC_OK;
+}
+
+llmoc_status llmoc_moe_ep_experts(const llmoc_moe_layer* L, const uint16_t* rows, const int32_t* expert, int n,
+                                  uint16_t* out_rows, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!L || n < 0 || (n > 0 && (!rows || !expert || !out_rows))) return fails(LLMOC_ERR_INVALID, "bad arguments");
+  if (n == 0) return LLMOC_OK;
+  const int chunk = chunk_for_rows(n, L->e_loc);
+  const WsLayout w = ws_layout_g(L, n, 1, L->n_exp, chunk, false);
+  if (!workspace || workspace_bytes < w.total) return fails(LLMOC_ERR_WORKSPACE, "workspace too small");
+  DevGuard dg(L->device);
+  cudaStream_t st = (cudaStream_t)stream;
+  char* ws = (char*)workspace;
+  llmoc_status rc = run_permute(expert, n, L->n_exp, chunk, w, ws, st);
+  if (rc != LLMOC_OK) return rc;
+  return run_ffn(L, rows, n, 1, chunk, w, ws, out_rows, nullptr, st);
+}
+
+llmoc_status llmoc_moe_ep_combine(const llmoc_moe_layer* L, const uint16_t* X, int T, const uint16_t* ret_rows,
+                                  uint16_t* Y, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!L || T < 0 || (T > 0 && (!X || !ret_rows || !Y))) return fails(LLMOC_ERR_INVALID, "bad arguments");
+  if (T == 0) return LLMOC_OK;
+  const EpSrcLayout w = ep_src_layout(L, T);
+  if (!workspace || workspace_bytes < w.total) return fails(LLMOC_ERR_WORKSPACE, "workspace too small");
+  DevGuard dg(L->device);
+  cudaStream_t st = (cudaStream_t)stream;
+  char* ws = (char*)workspace;
+  const float* sh = nullptr;
+  const int* sh_inv = nullptr;
+  if (L->d.has_shared) {  // the shared expert over this rank's own tokens
+    char* s2 = ws + w.sh;
+    int* ids = (int*)(s2 + w.shl.ids);
+    if (!cuda_ok(launch_fill_i32(ids, T, L->e_loc, st), "fill")) return LLMOC_ERR_CUDA;
+    count_launch(1);
+    llmoc_status rc = run_permute(ids, T, L->n_exp, w.sh_chunk, w.shl, s2, st);
+    if (rc == LLMOC_OK) rc = run_ffn(L, X, T, 1, w.sh_chunk, w.shl, s2, nullptr, nullptr, st);
+    if (rc != LLMOC_OK) return rc;
+    sh = (const float*)(s2 + w.shl.partial);
+    sh_inv = (const int*)(s2 + w.shl.inverse);
+  }
+  if (!cuda_ok(launch_combine_ep(ret_rows, (const int*)(ws + w.inverse), (const float*)(ws + w.weights), T,
+                                 L->d.topk, L->d.hidden, sh, sh_inv, L->d.shared_scale, Y, st),
+               "combine"))
+    return LLMOC_ERR_CUDA;
+  count_launch(1);
+  return LLMOC_OK;
+}
 
 }  // extern "C"
 

@@ -1,0 +1,154 @@
+"""Expert-parallel MoE layer forward: one process per GPU, token dispatch and
+combine as all-to-alls over torch.distributed (NCCL over NVLink on the GPU
+box, gloo in the CPU tests).
+
+The partition is the reference's: expert e lives on rank e % world
+(DeviceMesh::owner_rank with EpShard::kMod, src/contracts/device_mesh.h:63-72),
+as owner-local expert e // world; the router and the shared expert are
+replicated; the transport is an all-to-all (ICollective::alltoall,
+src/contracts/collective.h:13).  Every rank routes its own T tokens.  One
+layer step:
+
+    1. backend.dispatch   route, order the T*topk routed pairs by (owner,
+                          owner-local expert, token, slot), gather their rows
+    2. all-to-all         per-peer pair counts, then rows + owner-local ids
+    3. backend.experts    grouped expert FFN over the received rows
+    4. all-to-all         expert outputs back to the source, in send order
+    5. backend.combine    routed weights x returned rows (slot order) + shared
+
+`DeviceBackend` runs 1, 3 and 5 through the C ABI (llmoc_moe_ep_*); any
+object with the same three methods can stand in (the CPU tests use one built
+on the oracle).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+
+def owner_rank(expert: int, world: int) -> int:
+    """Rank that holds routed expert `expert` (the reference's kMod shard)."""
+    return expert % world
+
+
+def local_expert(expert: int, world: int) -> int:
+    return expert // world
+
+
+@dataclass
+class EpTimes:
+    """Device milliseconds of one step: local compute and the all-to-alls."""
+    dispatch_ms: float = 0.0
+    a2a_ms: float = 0.0
+    experts_ms: float = 0.0
+    combine_ms: float = 0.0
+    sent_rows: int = 0
+    recv_rows: int = 0
+
+
+class _Marks:
+    def __init__(self, enabled: bool):
+        self.ev = [] if enabled else None
+        self.on = enabled
+
+    def mark(self):
+        if self.on:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            self.ev.append(e)
+
+
+def ep_forward(backend, X: torch.Tensor, T: int, group=None, times: Optional[EpTimes] = None) -> torch.Tensor:
+    """Y [T, H] (bf16) of this rank's T tokens; collective over `group`."""
+    H = X.shape[1]
+    dev = X.device
+    timed = times is not None and dev.type == "cuda"
+    mk = _Marks(timed)
+    mk.mark()
+    send_rows, send_expert, send_counts = backend.dispatch(X, T)
+    mk.mark()
+    recv_counts = torch.empty_like(send_counts)
+    dist.all_to_all_single(recv_counts, send_counts, group=group)
+    counts = torch.stack([send_counts, recv_counts]).cpu()  # host split sizes
+    s_split = [int(v) for v in counts[0]]
+    r_split = [int(v) for v in counts[1]]
+    n_recv = sum(r_split)
+    recv_rows = torch.empty((n_recv, H), dtype=send_rows.dtype, device=dev)
+    recv_expert = torch.empty((n_recv,), dtype=send_expert.dtype, device=dev)
+    dist.all_to_all_single(recv_rows, send_rows, r_split, s_split, group=group)
+    dist.all_to_all_single(recv_expert, send_expert, r_split, s_split, group=group)
+    mk.mark()
+    out_rows = backend.experts(recv_rows, recv_expert, n_recv)
+    mk.mark()
+    ret_rows = torch.empty_like(send_rows)
+    dist.all_to_all_single(ret_rows, out_rows, s_split, r_split, group=group)
+    mk.mark()
+    Y = backend.combine(X, T, ret_rows)
+    mk.mark()
+    if times is not None:
+        times.sent_rows, times.recv_rows = sum(s_split), n_recv
+        if timed:
+            torch.cuda.current_stream().synchronize()
+            e = mk.ev
+            times.dispatch_ms = e[0].elapsed_time(e[1])
+            times.a2a_ms = e[1].elapsed_time(e[2]) + e[3].elapsed_time(e[4])
+            times.experts_ms = e[2].elapsed_time(e[3])
+            times.combine_ms = e[4].elapsed_time(e[5])
+    return Y
+
+
+@dataclass
+class DeviceBackend:
+    """The three local phases on this rank's GPU through the C ABI.
+
+    `shard` is an llmoc_b200.EpLayerShard; buffers grow on demand (torch
+    allocations outside the timed kernels)."""
+    shard: object
+    H: int
+    topk: int
+    stream: Optional[torch.cuda.Stream] = None
+    _src: dict = field(default_factory=dict)
+    _own: dict = field(default_factory=dict)
+
+    def _buf(self, cache: dict, name: str, shape, dtype, dev):
+        n = 1
+        for d in shape:
+            n *= d
+        t = cache.get(name)
+        if t is None or t.numel() < n or t.dtype != dtype:
+            t = torch.empty(max(n, 1), dtype=dtype, device=dev)
+            cache[name] = t
+        return t[:n].view(*shape)
+
+    def _stream(self):
+        return self.stream if self.stream is not None else torch.cuda.current_stream()
+
+    def dispatch(self, X, T):
+        dev = X.device
+        n = T * self.topk
+        wsb = self.shard.source_workspace_bytes(T)
+        self._src["wsb"] = wsb
+        ws = self._buf(self._src, "ws", (wsb,), torch.uint8, dev)
+        rows = self._buf(self._src, "rows", (n, self.H), torch.bfloat16, dev)
+        eid = self._buf(self._src, "eid", (n,), torch.int32, dev)
+        cnt = self._buf(self._src, "cnt", (self.shard.world,), torch.int32, dev)
+        self.shard.dispatch(X, T, ws, wsb, rows, eid, cnt, self._stream())
+        return rows, eid, cnt
+
+    def experts(self, rows, expert, n):
+        dev = rows.device
+        out = self._buf(self._own, "out", (n, self.H), torch.bfloat16, dev)
+        if n == 0:
+            return out
+        wsb = self.shard.owner_workspace_bytes(n)
+        ws = self._buf(self._own, "ws", (wsb,), torch.uint8, dev)
+        self.shard.experts(rows, expert, n, out, ws, wsb, self._stream())
+        return out
+
+    def combine(self, X, T, ret_rows):
+        Y = torch.empty((T, self.H), dtype=torch.bfloat16, device=X.device)
+        self.shard.combine(X, T, ret_rows, Y, self._src["ws"], self._src["wsb"], self._stream())
+        return Y

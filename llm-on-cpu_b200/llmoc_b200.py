@@ -97,6 +97,13 @@ _SIGS = {
     "llmoc_moe_forward_noalloc": (_i, [_vp, _vp, _i, _vp, _vp]),
     "llmoc_moe_noalloc_capacity": (_sz, []),
     "llmoc_moe_stage_times": (_i, [_vp, C.POINTER(C.c_float), C.POINTER(_i)]),
+    "llmoc_moe_layer_create_ep": (_i, [C.POINTER(LayerDesc), _vp, _vp, C.POINTER(Int4View),
+                                       C.POINTER(Int4View), _i, _i, _i, _i, C.POINTER(_vp)]),
+    "llmoc_moe_ep_source_workspace_bytes": (_sz, [_vp, _i]),
+    "llmoc_moe_ep_owner_workspace_bytes": (_sz, [_vp, _i]),
+    "llmoc_moe_ep_dispatch": (_i, [_vp, _vp, _i, _vp, _sz, _vp, _vp, _vp, _vp]),
+    "llmoc_moe_ep_experts": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _sz, _vp]),
+    "llmoc_moe_ep_combine": (_i, [_vp, _vp, _i, _vp, _vp, _vp, _sz, _vp]),
 }
 for _name, (_res, _args) in _SIGS.items():
     _fn = getattr(lib, _name)
@@ -251,3 +258,60 @@ def quantize_awq_sym(W, M: int, K: int, gs: int, bf16_scale: bool, q, scales, st
 
 def launch_count() -> int:
     return int(lib.llmoc_kernel_launch_count())
+
+
+class EpLayerShard(MoeLayer):
+    """One rank's shard of an expert-parallel layer (llmoc_moe_layer_create_ep):
+    routed experts e with e % world == rank, plus the router and shared expert."""
+
+    def __init__(self, handle: int, desc: LayerDesc, rank: int, world: int):
+        super().__init__(handle, desc)
+        self.rank, self.world = rank, world
+
+    @classmethod
+    def create_ep(cls, desc: LayerDesc, router_w, bias, experts: Sequence[Int4View],
+                  shared: Optional[Sequence[Int4View]], rank: int, world: int, device: int = 0,
+                  on_device: bool = False):
+        n = len(experts)
+        arr = (Int4View * n)(*experts)
+        sh = (Int4View * 3)(*shared) if shared is not None else None
+        h = C.c_void_p()
+        check(lib.llmoc_moe_layer_create_ep(C.byref(desc), ptr(router_w), ptr(bias), arr, sh, device, rank, world,
+                                            1 if on_device else 0, C.byref(h)), "llmoc_moe_layer_create_ep")
+        return cls(h.value, desc, rank, world)
+
+    @classmethod
+    def from_host_ep(cls, layer, rank: int, world: int, device: int = 0) -> "EpLayerShard":
+        e0 = layer.experts[0].gate
+        desc = LayerDesc(layer.H, layer.I, layer.E, layer.topk, e0.group_size, e0.scheme,
+                         e0.awq_zp if e0.awq_zp > 0 else 7, layer.router, layer.routed_scaling,
+                         1 if layer.shared is not None else 0, layer.shared_scale)
+        views = []
+        for ex in layer.experts:
+            views += [view_of(ex.gate), view_of(ex.up), view_of(ex.down)]
+        sh = None
+        if layer.shared is not None:
+            sh = [view_of(layer.shared.gate), view_of(layer.shared.up), view_of(layer.shared.down)]
+        return cls.create_ep(desc, layer.router_w, layer.bias, views, sh, rank, world, device)
+
+    @property
+    def e_loc(self) -> int:
+        return self.desc.n_experts // self.world
+
+    def source_workspace_bytes(self, T: int) -> int:
+        return int(lib.llmoc_moe_ep_source_workspace_bytes(self.handle, T))
+
+    def owner_workspace_bytes(self, rows: int) -> int:
+        return int(lib.llmoc_moe_ep_owner_workspace_bytes(self.handle, rows))
+
+    def dispatch(self, X, T, ws, ws_bytes, send_rows, send_expert, send_counts, stream=None) -> None:
+        check(lib.llmoc_moe_ep_dispatch(self.handle, ptr(X), T, ptr(ws), ws_bytes, ptr(send_rows), ptr(send_expert),
+                                        ptr(send_counts), stream_ptr(stream)), "llmoc_moe_ep_dispatch")
+
+    def experts(self, rows, expert, n, out_rows, ws, ws_bytes, stream=None) -> None:
+        check(lib.llmoc_moe_ep_experts(self.handle, ptr(rows), ptr(expert), n, ptr(out_rows), ptr(ws), ws_bytes,
+                                       stream_ptr(stream)), "llmoc_moe_ep_experts")
+
+    def combine(self, X, T, ret_rows, Y, ws, ws_bytes, stream=None) -> None:
+        check(lib.llmoc_moe_ep_combine(self.handle, ptr(X), T, ptr(ret_rows), ptr(Y), ptr(ws), ws_bytes,
+                                       stream_ptr(stream)), "llmoc_moe_ep_combine")

@@ -1,0 +1,167 @@
+"""Expert parallelism on the GPU: the llmoc_moe_ep_* phases through the C ABI.
+
+Two shards of one layer on one GPU with the all-to-all done by hand (the
+kernels of world = 2 without a second GPU), world = 1 against the plain
+forward, and, where the box has two GPUs, two NCCL ranks running
+ep.ep_forward.  Each rank's output is checked against the fp32 oracle of the
+whole layer on that rank's tokens (bf16 output bar: normwise max relative
+error 1e-2, cosine 0.9999)."""
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+
+import llmoc_b200 as L
+import moe_gpu as G
+import orc
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+import ep  # noqa: E402
+
+CFGS = {
+    "qwen_like": dict(H=512, I=256, E=32, topk=8, gs=128),
+    "glm_like_shared_sigmoid": dict(H=512, I=128, E=32, topk=8, gs=128, router=1, shared=True),
+    "kimi_like_gs32": dict(H=448, I=128, E=48, topk=8, gs=32, router=1, routed_scaling=2.827, shared=True),
+    "gptq_shared": dict(H=256, I=128, E=16, topk=4, gs=64, scheme=1, shared=True, shared_scale=0.75),
+}
+
+
+@pytest.fixture(scope="module", autouse=True)
+def cuda_ready():
+    assert torch.cuda.is_available()
+    assert L.lib.llmoc_cuda_probe_available() == 1, L.lib.llmoc_cuda_status()
+    yield
+
+
+def _check(Y, Yref, what):
+    mre, cos = G.quality(G.bf16_to_f32(Y), Yref)
+    assert mre <= G.MAX_REL and cos >= G.MIN_COS, (what, mre, cos)
+
+
+def _backends(layer, world):
+    shards = [L.EpLayerShard.from_host_ep(layer, r, world) for r in range(world)]
+    return shards, [ep.DeviceBackend(s, layer.H, layer.topk) for s in shards]
+
+
+def _emulated_forward(backends, Xs):
+    """ep_forward for every rank in one process: the all-to-alls as copies."""
+    world = len(backends)
+    sends = [b.dispatch(X, X.shape[0]) for b, X in zip(backends, Xs)]
+    counts = [s[2].cpu().numpy().astype(int) for s in sends]
+    bounds = [np.concatenate([[0], np.cumsum(c)]) for c in counts]
+    outs = []
+    for r in range(world):  # rows and ids from every source, source order
+        rows = torch.cat([sends[s][0][bounds[s][r]:bounds[s][r + 1]] for s in range(world)])
+        eid = torch.cat([sends[s][1][bounds[s][r]:bounds[s][r + 1]] for s in range(world)])
+        outs.append((backends[r].experts(rows.contiguous(), eid.contiguous(), rows.shape[0]).clone(),
+                     [counts[s][r] for s in range(world)]))
+    Ys = []
+    for s in range(world):  # back to the source, in its send order (by owner rank)
+        parts = []
+        for r in range(world):
+            out, per_src = outs[r]
+            o = int(sum(per_src[:s]))
+            parts.append(out[o:o + per_src[s]])
+        Ys.append(backends[s].combine(Xs[s], Xs[s].shape[0], torch.cat(parts).contiguous()))
+    torch.cuda.synchronize()
+    return Ys, counts
+
+
+@pytest.mark.parametrize("name", list(CFGS))
+@pytest.mark.parametrize("T", [5, 40, 200])
+def test_two_shards_on_one_gpu(oracle, name, T):
+    layer = orc.make_layer(oracle, np.random.default_rng(3), **CFGS[name])
+    shards, bks = _backends(layer, 2)
+    Xh = [orc.make_tokens(np.random.default_rng(50 + r), T + 3 * r, layer.H) for r in range(2)]
+    Ys, counts = _emulated_forward(bks, [G.bf16_dev(X) for X in Xh])
+    for r in range(2):
+        Yref, ids, _, _ = oracle.moe_layer_forward(layer, Xh[r])
+        _check(Ys[r], Yref, (name, T, r))
+        # per-owner counts equal the oracle's routing
+        want = np.bincount((ids % 2).reshape(-1), minlength=2)
+        assert np.array_equal(counts[r], want)
+    for s in shards:
+        s.close()
+
+
+@pytest.mark.parametrize("name", ["qwen_like", "glm_like_shared_sigmoid"])
+def test_world_one_matches_plain_forward(oracle, name):
+    layer = orc.make_layer(oracle, np.random.default_rng(4), **CFGS[name])
+    shards, bks = _backends(layer, 1)
+    X = orc.make_tokens(np.random.default_rng(9), 64, layer.H)
+    Ys, _ = _emulated_forward(bks, [G.bf16_dev(X)])
+    dl = G.DevLayer(layer, 64)
+    Y, _ = dl.forward(X)
+    mre, cos = G.quality(G.bf16_to_f32(Ys[0]), G.bf16_to_f32(Y))
+    assert mre <= G.MAX_REL and cos >= G.MIN_COS
+    _check(Ys[0], oracle.moe_layer_forward(layer, X)[0], name)
+    dl.close()
+    shards[0].close()
+
+
+def test_shard_refuses_the_single_gpu_forward(oracle):
+    layer = orc.make_layer(oracle, np.random.default_rng(5), **CFGS["qwen_like"])
+    s = L.EpLayerShard.from_host_ep(layer, 0, 2)
+    ws = torch.empty(s.workspace_bytes(4) + 1024, dtype=torch.uint8, device="cuda")
+    X = G.bf16_dev(orc.make_tokens(np.random.default_rng(1), 4, layer.H))
+    Y = torch.empty((4, layer.H), dtype=torch.bfloat16, device="cuda")
+    rc = L.lib.llmoc_moe_forward(s.handle, X.data_ptr(), 4, Y.data_ptr(), ws.data_ptr(), ws.numel(), None)
+    assert rc == 1 and b"expert-parallel" in L.lib.llmoc_last_error()
+    with pytest.raises(L.LlmocError):  # world must divide n_experts
+        L.EpLayerShard.from_host_ep(layer, 0, 3)
+    s.close()
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _nccl_worker(rank, world, port, name, T, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        torch.cuda.set_device(rank)
+        dist = torch.distributed
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", rank))
+        oracle = orc.Oracle()
+        layer = orc.make_layer(oracle, np.random.default_rng(3), **CFGS[name])
+        shard = L.EpLayerShard.from_host_ep(layer, rank, world, device=rank)
+        bk = ep.DeviceBackend(shard, layer.H, layer.topk)
+        Xh = orc.make_tokens(np.random.default_rng(70 + rank), T + rank, layer.H)
+        X = G.bf16_dev(Xh).to(f"cuda:{rank}")
+        Y = ep.ep_forward(bk, X, X.shape[0])
+        torch.cuda.synchronize()
+        mre, cos = G.quality(G.bf16_to_f32(Y), oracle.moe_layer_forward(layer, Xh)[0])
+        q.put((rank, mre, cos))
+        dist.barrier()
+        dist.destroy_process_group()
+        shard.close()
+    except Exception as e:
+        q.put((rank, repr(e), None))
+
+
+@pytest.mark.parametrize("name", ["qwen_like", "kimi_like_gs32"])
+def test_two_nccl_ranks(name):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_nccl_worker, args=(r, 2, port, name, 33, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = [q.get(timeout=300) for _ in range(2)]
+    for p in ps:
+        p.join(timeout=60)
+    for rank, mre, cos in res:
+        assert cos is not None, (rank, mre)
+        assert mre <= G.MAX_REL and cos >= G.MIN_COS, (rank, mre, cos)
