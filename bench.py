@@ -18,8 +18,12 @@ Arms:
   --impl reference   the reference's own CPU implementation of the path
                      (oracle/_ref: its src/hal AVX2/OpenMP operators, per-token
                      moe_ffn_token loop) on the host cores, bounded samples.
-Multi-GPU (torchrun, --gpus N): N independent replicas of the step, one per
-GPU (weak scaling); time = max over ranks.
+Multi-GPU (torchrun, --gpus N): expert parallelism — GPU r holds the experts
+e with e % N == r of every layer copy (router and shared expert replicated),
+routes its own T tokens, and the routed token rows go to their experts' GPUs
+and back by NCCL all-to-alls (ep.py).  Weak scaling: T tokens per GPU; value
+= N * T / step time, the time the max over ranks; the all-to-all time is
+reported beside the local compute.
 """
 from __future__ import annotations
 
@@ -143,9 +147,10 @@ def ncu_traffic(config: str, T: int):
 
 # ------------------------------------------------------- device workload
 
-def build_layers(torch, L, cfg, R, seed, keep_host=False, device=0):
+def build_layers(torch, L, cfg, R, seed, keep_host=False, device=0, ep=None):
     """R distinct layers generated and quantized in HBM (llmoc_quantize_awq_sym),
-    then repacked by llmoc_moe_layer_create_device.  keep_host returns the
+    then repacked by llmoc_moe_layer_create_device (or, with ep = (rank,
+    world), this rank's expert-parallel shard of each).  keep_host returns the
     first layer's QLWC tensors on the host for the CPU baseline."""
     H, I, E, gs = cfg["H"], cfg["I"], cfg["E"], cfg["gs"]
     n_exp = E + (1 if cfg["shared"] else 0)
@@ -176,8 +181,12 @@ def build_layers(torch, L, cfg, R, seed, keep_host=False, device=0):
         desc = L.LayerDesc(H, I, E, cfg["topk"], gs, L.SCHEME_AWQ_SYM, 7, cfg["router"], cfg["scaling"],
                            1 if cfg["shared"] else 0, 1.0)
         torch.cuda.synchronize()
-        layer = L.MoeLayer.create(desc, rw, bias, views[:3 * E], views[3 * E:] if cfg["shared"] else None,
-                                  device=device, on_device=True)
+        if ep is not None:
+            layer = L.EpLayerShard.create_ep(desc, rw, bias, views[:3 * E], views[3 * E:] if cfg["shared"] else None,
+                                             ep[0], ep[1], device=device, on_device=True)
+        else:
+            layer = L.MoeLayer.create(desc, rw, bias, views[:3 * E], views[3 * E:] if cfg["shared"] else None,
+                                      device=device, on_device=True)
         layers.append(layer)
         if keep_host and r == 0:
             host = {k: (v[0].cpu().numpy(), v[1].cpu().numpy().view(np.uint16), v[2], v[3]) for k, v in raw.items()}
@@ -465,10 +474,172 @@ def run_reference(args):
     return line
 
 
+def run_ep(args):
+    """--gpus N > 1: the expert-parallel layer step across N ranks (NCCL)."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import ep as EP
+    import llmoc_b200 as L
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    cfg = CONFIGS[args.config]
+    H, E, k, I = cfg["H"], cfg["E"], cfg["topk"], cfg["I"]
+    Ts = sorted({args.tokens} | ({int(x) for x in args.sweep.split(",") if x} if args.sweep else set()))
+    gu_b, dn_b = layer_bytes(cfg)
+    exp_b = gu_b + dn_b
+
+    def touched_local(T):  # expected routed experts of this shard that the world's tokens touch
+        return expected_touched(E, k, world * T) / world
+
+    touched_min = min(touched_local(T) for T in Ts) + (1 if cfg["shared"] else 0)
+    R = int(max(2, min(24, np.ceil(3 * L2_BYTES / (touched_min * exp_b)))))
+    if args.copies > 0:
+        R = args.copies
+    shards, _ = build_layers(torch, L, cfg, R, seed=1234, device=local, ep=(rank, world))
+    backends = [EP.DeviceBackend(s, H, k) for s in shards]
+    Tmax = max(Ts)
+    g = torch.Generator(device="cuda").manual_seed(99 + rank)
+    Xpool = [(torch.randn((Tmax, H), generator=g, device="cuda")).to(torch.bfloat16) for _ in range(R)]
+    stream = torch.cuda.current_stream()
+
+    def step(i, T):
+        EP.ep_forward(backends[i % R], Xpool[i % R][:T], T)
+
+    def max_over_ranks(v):
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed(T, K, fn):
+        dist.barrier()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for i in range(K):
+            fn(i, T)
+        b.record(stream)
+        torch.cuda.synchronize()
+        dist.barrier()
+        return max_over_ranks(a.elapsed_time(b))
+
+    results = {}
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    clocks = Clocks(int(vis.split(",")[local]) if vis else local)
+    clk, launches = None, 0
+    for T in Ts:
+        for i in range(max(3, args.warmup)):
+            step(i, T)
+        torch.cuda.synchronize()
+        if T == args.tokens:
+            clocks.start()
+            t_end = time.perf_counter() + 1.5
+            i = 0
+            while time.perf_counter() < t_end:
+                for _ in range(10):
+                    step(i, T)
+                    i += 1
+                torch.cuda.synchronize()
+            n0 = L.launch_count()
+        ms = timed(T, args.steps, step)
+        if T == args.tokens:
+            launches = L.launch_count() - n0
+            clk = clocks.stop()
+        # phase times (a separate pass: events around each phase)
+        acc = {"dispatch_ms": 0.0, "a2a_ms": 0.0, "experts_ms": 0.0, "combine_ms": 0.0}
+        rows = [0, 0]
+        for i in range(args.steps):
+            tm = EP.EpTimes()
+            EP.ep_forward(backends[i % R], Xpool[i % R][:T], T, times=tm)
+            for key in acc:
+                acc[key] += getattr(tm, key) / args.steps
+            rows[0] += tm.sent_rows
+            rows[1] += tm.recv_rows
+        phases = {key: max_over_ranks(v) for key, v in acc.items()}
+        recv_max = max_over_ranks(rows[1] / args.steps)
+        results[T] = dict(ms=ms, phases=phases, recv_rows_max=recv_max)
+
+    # e2e: host tokens in, host outputs out, every step on every rank
+    T = args.tokens
+    Xh = torch.empty((T, H), dtype=torch.bfloat16, pin_memory=True)
+    Xh.copy_(Xpool[0][:T].cpu())
+    Yh = torch.empty((T, H), dtype=torch.bfloat16, pin_memory=True)
+    Xd = torch.empty((T, H), dtype=torch.bfloat16, device="cuda")
+
+    def e2e_step(i, T):
+        Xd.copy_(Xh, non_blocking=True)
+        Y = EP.ep_forward(backends[i % R], Xd, T)
+        Yh.copy_(Y, non_blocking=True)
+
+    for i in range(max(3, args.warmup)):
+        e2e_step(i, T)
+    ms_e2e = timed(T, args.steps, e2e_step)
+
+    out = None
+    if rank == 0:
+        r = results[T]
+        peak, peak_kind = measured_peak()
+        ph = r["phases"]
+        per_step = r["ms"] / args.steps
+        tl = touched_local(T) + (1 if cfg["shared"] else 0)
+        # the local expert phase streams the shard's touched experts and reads/writes the received rows
+        alg = tl * exp_b + r["recv_rows_max"] * H * 2 * 2
+        achieved = alg / (ph["experts_ms"] * 1e-3) / 1e9 if ph["experts_ms"] > 0 else None
+        sweep = {}
+        for t_, rr in results.items():
+            ps = rr["ms"] / args.steps
+            sweep[str(t_)] = {"tokens_per_s": world * t_ * args.steps / (rr["ms"] * 1e-3), "ms_per_step": ps,
+                              "phases_ms": {a: round(b, 5) for a, b in rr["phases"].items()}}
+        a2a_bytes = T * k * H * 2 * 2 + T * k * 4  # rows out and back (bf16) + expert ids, per GPU
+        out = {
+            "metric": "INT4 MoE FFN tokens/s (decode, T=%d per GPU)" % T,
+            "value": world * T * args.steps / (r["ms"] * 1e-3),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": max(3, args.warmup),
+            "ms_per_step": per_step,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "int4 weights x bf16 activations, fp32 accumulate",
+            "data": "synthetic (seeded device RNG; BASELINE shapes and distributions)",
+            "config": {"workload": f"{args.config} MoE layer, expert-parallel", "tokens_per_gpu": T, "hidden": H,
+                       "experts": E, "experts_per_gpu": E // world, "topk": k, "inter": I,
+                       "group_size": cfg["gs"], "parallelism": f"ep{world}",
+                       "l2": f"rotating {R} distinct layer copies (touched weights >= 3x the 126 MB L2)"},
+            "ep": {"phases_ms": ph, "a2a_bytes_per_gpu_per_step": a2a_bytes,
+                   "a2a_GBps_per_gpu": a2a_bytes / (ph["a2a_ms"] * 1e-3) / 1e9 if ph["a2a_ms"] > 0 else None,
+                   "transport": "NCCL all_to_all_single over NVLink (torch.distributed)"},
+            "e2e": {"value": world * T * args.steps / (ms_e2e * 1e-3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 2},
+            "roofline": {"bound": "hbm", "kernel": "local expert phase (grouped gate/up + down on the shard)",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak if achieved else None, "peak_kind": peak_kind, "traffic": None,
+                         "alg_bytes_per_launch": alg, "launch_ms": ph["experts_ms"]},
+            "sweep": sweep,
+            "cpu_baseline": None,
+            "clocks": clk,
+            "gpu_launches": int(launches),
+        }
+        print(json.dumps(out), flush=True)
+    dist.barrier()
+    for s in shards:
+        s.close()
+    dist.destroy_process_group()
+    return out
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif dist_env()[1] > 1:
+        run_ep(args)
     else:
         run_llmoc(args)
 
