@@ -2,7 +2,7 @@
 // (tcgen05.mma) for prefill-size work items.
 //
 // One CTA per SM, persistent over a list of tiles.  A tile is 128 weight rows
-// of one expert against one work item (up to 128 of that expert's tokens):
+// of one expert against one work item (up to 256 of that expert's tokens):
 //     D[m, n] = sum_k W[m, k] * X[n, k]
 // MODE_GATE_UP tiles hold 64 gate rows and the same 64 up rows (interleaved
 // by 16 so a gate row and its up row sit 16 TMEM lanes apart and meet with one
@@ -11,37 +11,44 @@
 // The dequantised weights are the A operand and live in TENSOR MEMORY, not in
 // shared memory: each dequantising thread owns one weight row (= one TMEM
 // lane) and writes its bf16 values with tcgen05.st, so the only shared-memory
-// operand of the MMA is the activation tile (B).  Accumulators are double-
-// buffered in TMEM so the epilogue of tile i overlaps the main loop of i+1.
+// operand of the MMA is the activation tile (B).
+//
+// Issue cost sets the shape.  One thread issues the MMAs, and an M = 128, K =
+// 16 MMA of N = 128 columns runs for only ~64 SM cycles, about what a barrier
+// wait plus a commit cost the issuing thread.  So an item holds up to 256
+// tokens (N = 256: ~128 cycles per MMA), and each 64-wide K block costs one
+// wait and one commit: the A slot and the B slot of a block form one STAGE
+// with one "full" barrier (the four dequantising warps and the B loader arrive
+// on it) and one "empty" barrier (the MMA commit).
 //
 //   TMEM (512 columns x 128 lanes, fp32 words)
-//     [0,128) [128,256)   accumulator buffers (N <= 128 columns each)
-//     [256 + 32 s, +32)   A slot s (s < kASlots): 128 rows x 64 k, bf16 pairs
+//     [0,256)             accumulator (N <= 256 columns), single-buffered
+//     [256 + 32 s, +32)   A slot of stage s (s < kStages): 128 rows x 64 k, bf16 pairs
 //
-//   shared memory: a B ring (kBS slots of 128 token rows x 128 B, 128-byte
+//   shared memory: the B slots (kStages x 256 token rows x 128 B, 128-byte
 //   swizzled K-major, one 64-wide K block each) and a weight ring (kWS slots of
 //   kSlotBlocks K blocks: raw INT4 words + group scales (+ GPTQ zeros)).
 //
 //   warp 0       TMEM alloc; lane 0 issues tcgen05.mma (A from TMEM, B from
-//                smem) and tcgen05.commit's the A slot, the B slot and, per
-//                tile, the accumulator buffer.
+//                smem), commits each stage and, per tile, the accumulator.
 //   warps 1..2   weight loaders (alternate slot uses): one instruction per
 //                slot whose lanes issue the 3-D TMA boxes of the raw words
 //                (fragment-order 512-byte chunks, whose piece order makes the
 //                row-per-thread reads below bank-conflict free), the scales
 //                and the zeros, from per-expert tensor maps built at layer
 //                creation.
-//   warps 3..6   activation loaders (alternate blocks): TMA 2-D boxes (32
-//                token rows x 64 bf16, 128-byte swizzle, 4 KB aligned) of the
-//                item's rows, which are contiguous: the down GEMM reads the
+//   warps 3..4   activation loaders (alternate blocks): one TMA 2-D box (64 bf16
+//                x 32/64/128/256 token rows, 128-byte swizzle) of the item's
+//                rows, which are contiguous: the down GEMM reads the
 //                expert-sorted gate/up output, and the gate/up GEMM a copy of
 //                the tokens gathered into expert-sorted order (k_gather_rows).
-//   warps 7..14  dequantisers: two per TMEM lane quadrant, alternating blocks;
+//   warps 5..12  dequantisers: two per TMEM lane quadrant, alternating blocks;
 //                thread = one weight row: 16 words -> 64 bf16 w = (q - zp) * s
 //                (or q * s + z), one tcgen05.st.32x32b.x32 per block.  A
 //                weight slot is released as soon as its words are in registers.
-//   warps 15..18 epilogue: tcgen05.ld the accumulator, SiLU*mul (gate/up,
-//                bf16 out) or fp32 (down), store to the expert-sorted rows.
+//   warps 13..20 epilogue, two per lane quadrant (half of the columns each):
+//                tcgen05.ld the accumulator, SiLU*mul (gate/up, bf16 out) or
+//                fp32 (down), store to the expert-sorted rows.
 //
 // Every wait is bounded (about 2^31 SM clocks, ~1 s); a wait that gives up
 // sets a CTA-wide abort flag, bit 0 of *err, and every role drains and exits.
@@ -55,32 +62,28 @@ namespace llmoc {
 
 namespace {
 
-constexpr int kASlots = 4;                 // A slots in TMEM
+constexpr int kStages = 5;                 // stage ring: A slot (TMEM) + B slot (smem) per K block
 constexpr int kDeqWarps = 8;
-constexpr int kEpiWarps = 4;
-// Warp roles.  A warp's TMA copies proceed about one issue round at a time
-// (measured: throughput per loader warp ~ bytes per instruction / ~0.45 us,
-// and it scales with the number of issuing warps), so the copies are spread
-// over several loader warps and each instruction carries several boxes.
+constexpr int kEpiWarps = 8;
+// Warp roles.  TMA copies are latency-bound (~2.5k cycles from L2 whatever
+// their size), so each instruction carries a large box and the rings are deep.
 constexpr int kWLoaders = 2;               // warps 1, 2: weight slots u % 2
-constexpr int kBLoaders = 4;               // warps 3..6: B blocks j % 4
+constexpr int kBLoaders = 2;               // warps 3, 4: B blocks j % 2
 constexpr int kWLoader0 = 1;
 constexpr int kBLoader0 = kWLoader0 + kWLoaders;          // 3
-constexpr int kDeq0 = kBLoader0 + kBLoaders;              // 7: warps 7..14 (lane quadrants 3,0,1,2 twice)
-constexpr int kEpi0 = kDeq0 + kDeqWarps;                  // 15: warps 15..18
-constexpr int kWarps = kEpi0 + kEpiWarps;                 // 19
-constexpr int kUThreads = kWarps * 32;                    // 608
+constexpr int kDeq0 = kBLoader0 + kBLoaders;              // 5: warps 5..12 (lane quadrants 1,2,3,0 twice)
+constexpr int kEpi0 = kDeq0 + kDeqWarps;                  // 13: warps 13..20
+constexpr int kWarps = kEpi0 + kEpiWarps;                 // 21
+constexpr int kUThreads = kWarps * 32;                    // 672
 constexpr int kTmemCols = 512;
-constexpr int kAccCol = 0;                 // + 128 * buffer
-constexpr int kACol = 256;                 // + 32 * slot
-constexpr int kBS = 7;                     // B ring depth (one 64-wide K block per slot)
-constexpr int kBSlot = 128 * 128;          // <= 128 token rows x 64 bf16
-constexpr int kBBoxRows = 32;              // token rows per B TMA box (4 KB)
+constexpr int kAccCol = 0;                 // N <= 256 columns
+constexpr int kACol = 256;                 // + 32 * stage
+constexpr int kBSlot = kUmmaRows * 128;    // <= 256 token rows x 64 bf16 (32 KB)
+constexpr int kBBoxKinds = 4;              // B boxes of 32, 64, 128, 256 rows
 // A weight slot holds kSlotBlocks 64-wide K blocks of the tile's 128 rows:
 //   raw words  [op][tile][block][512 B]  (2 ops x 4 tiles for gate/up, 1 x 8 for down)
 //   scales     [op][tile][group][32 B]   (groups of the slot's 256 k), then zeros (GPTQ)
-// Each part arrives in ONE TMA box per op: few, large copies keep enough bytes
-// in flight per SM (the copy engine's cost is per operation, not per byte).
+// Each part arrives in ONE TMA box per op.
 constexpr int kSlotBlocks = 4;
 constexpr int kWRaw = 8 * kSlotBlocks * 512;              // 16 KB
 constexpr int kWSc = 8 * 8 * 32;                          // up to 8 groups per slot (gs 32)
@@ -89,9 +92,11 @@ constexpr int kWOffZ = kWRaw + kWSc;
 template <bool AWQ>
 struct WRing {
   static constexpr int kSlot = kWRaw + kWSc * (AWQ ? 1 : 2);  // 18 / 20 KB
-  static constexpr int kDepth = 5;                              // 20 blocks in flight
-  static constexpr int kSmem = kBS * kBSlot + kDepth * kSlot + 1024;  // + alignment slack
+  static constexpr int kDepth = 3;                              // 12 blocks in flight
+  static constexpr int kSmem = kStages * kBSlot + kDepth * kSlot + 1024;  // + alignment slack
 };
+static_assert(kACol + 32 * kStages <= kTmemCols, "TMEM columns");
+static_assert(WRing<false>::kSmem <= 227 * 1024, "shared memory");
 constexpr long long kWaitCycles = 1ll << 31;
 
 __device__ __forceinline__ uint32_t su32(const void* p) {
@@ -205,13 +210,23 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
 __device__ __forceinline__ uint32_t instr_desc(int M, int N) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
-// D[tmem] (+)= A[tmem] * B[smem]^T, M = 128, K = 16
-__device__ __forceinline__ void umma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t idesc,
-                                        uint32_t accumulate) {
+// D[tmem] (+)= A[tmem] * B[smem]^T over one 64-wide K block: four M = 128,
+// K = 16 MMAs in one asm statement.  A: columns ta, ta + 8, ta + 16, ta + 24
+// (bf16 pairs); B: the descriptor db of the block's first 16 k, the next ones
+// 32 bytes further (descriptor start address + 2).  `accumulate` = 0 starts a
+// new sum with the first MMA.  The descriptor is built once per kernel and
+// only offset here: rebuilding it per MMA costs more issue time than an
+// M = 128, N = 128 MMA takes to run.
+__device__ __forceinline__ void umma_ts_k64(uint32_t tmem_d, uint32_t ta, uint64_t db, uint32_t idesc,
+                                            uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(tmem_d),
-      "r"(tmem_a), "l"(db), "r"(idesc), "r"(accumulate));
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%5], %6, %3, 1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%7], %8, %3, 1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%9], %10, %3, 1;\n\t}\n" ::"r"(tmem_d),
+      "r"(ta), "l"(db), "r"(idesc), "r"(accumulate), "r"(ta + 8), "l"(db + 2), "r"(ta + 16), "l"(db + 4),
+      "r"(ta + 24), "l"(db + 6));
 }
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -293,17 +308,22 @@ __device__ __forceinline__ int sub_rt(int mt, int st) {
 
 }  // namespace
 
+// B operand tensor maps: boxes of 64 bf16 x {32, 64, 128, 256} token rows
+// (128-byte swizzle); an item reads the smallest box that covers its rows.
+struct BMaps {
+  CUtensorMap m[kBBoxKinds];
+};
+
 template <int MODE, int GSB, bool AWQ>
-__global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a, const __grid_constant__ CUtensorMap tmB) {
+__global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a, const __grid_constant__ BMaps tmB) {
   constexpr int NG = GSB == 1 ? 2 : 1;  // scale groups per 64-wide block
   constexpr int kRowsTile = MODE == MODE_GATE_UP ? 64 : 128;
   constexpr int kWS = WRing<AWQ>::kDepth;
   constexpr int kWSlot = WRing<AWQ>::kSlot;
   extern __shared__ __align__(1024) unsigned char usm[];
   __shared__ __align__(8) uint64_t fullW[kWS], emptyW[kWS];
-  __shared__ __align__(8) uint64_t fullB[kBS], emptyB[kBS];
-  __shared__ __align__(8) uint64_t fullA[kASlots], emptyA[kASlots];
-  __shared__ __align__(8) uint64_t accFull[2], accEmpty[2], done;
+  __shared__ __align__(8) uint64_t full[kStages], empty[kStages];
+  __shared__ __align__(8) uint64_t accFull, accEmpty, done;
   __shared__ uint32_t tmem_base;
   __shared__ volatile int abort_flag;
 
@@ -311,34 +331,27 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a, const __
   const int nmt = a.M / kRowsTile;
   const int ntiles = *a.n_work * nmt;
   if ((int)blockIdx.x >= ntiles) return;  // uniform over the CTA
-  const int nb = a.K >> 6;                // 64-wide K blocks per tile
+  const int nb = a.K >> 6;                // 64-wide K blocks per tile (even: K % 128 == 0)
   const int G = gridDim.x;
   const uint32_t my_tiles = (uint32_t)((ntiles - (int)blockIdx.x + G - 1) / G);
-  const uint32_t my_blocks = my_tiles * (uint32_t)nb;
-  const int nsl = (nb + kSlotBlocks - 1) / kSlotBlocks;  // weight-slot uses per tile (nb is even)
+  const int nsl = (nb + kSlotBlocks - 1) / kSlotBlocks;  // weight-slot uses per tile
   constexpr int kGps = 4 * 64 / (GSB * 32);                // scale groups per weight slot
   constexpr int kOps = MODE == MODE_GATE_UP ? 2 : 1;     // TMA boxes per part (gate, up)
   constexpr int kTilesOp = 8 / kOps;                     // 16-row tiles per box
   unsigned char* ringB = usm + ((1024 - (su32(usm) & 1023)) & 1023);  // 1024-aligned (SW128)
-  unsigned char* ringW = ringB + kBS * kBSlot;
+  unsigned char* ringW = ringB + kStages * kBSlot;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kWS; ++s) {
-      mb_init(&fullW[s], 1);   // weight loader's expect_tx (+ the bulk copies' bytes)
+      mb_init(&fullW[s], 1);           // weight loader's expect_tx (+ the bulk copies' bytes)
       mb_init(&emptyW[s], kDeqWarps);  // every dequantising warp, after its last block of the slot
     }
-    for (int s = 0; s < kBS; ++s) {
-      mb_init(&fullB[s], 1);   // B loader's expect_tx (+ the TMA boxes' bytes)
-      mb_init(&emptyB[s], 1);  // MMA commit
+    for (int s = 0; s < kStages; ++s) {
+      mb_init(&full[s], 5);   // 4 dequantising warps (one per lane quadrant) + the B loader's expect_tx
+      mb_init(&empty[s], 1);  // MMA commit
     }
-    for (int s = 0; s < kASlots; ++s) {
-      mb_init(&fullA[s], 4);
-      mb_init(&emptyA[s], 1);
-    }
-    for (int b = 0; b < 2; ++b) {
-      mb_init(&accFull[b], 1);
-      mb_init(&accEmpty[b], kEpiWarps);
-    }
+    mb_init(&accFull, 1);
+    mb_init(&accEmpty, kEpiWarps);
     mb_init(&done, 1);
     abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -356,35 +369,35 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a, const __
 
   if (warp == 0) {
     // ------------------------------- MMA issuer -------------------------------
+    // Per 64-wide K block: one wait (A slot dequantised and B box landed), four
+    // M = 128 MMAs of N = the item's rows rounded up to 16 (<= 256), one commit
+    // that frees the stage.  The accumulator is single-buffered: tile i starts
+    // once the epilogue has drained tile i - 1 (the loaders and dequantisers
+    // keep filling the stage ring meanwhile).
     if (lane == 0) {
-      uint32_t j = 0, i = 0;
+      uint32_t s = 0, ph = 0;
+      const uint64_t dB0 = smem_desc(su32(ringB));
       int nrows = a.work[blockIdx.x / nmt].nrows;
+      uint32_t i = 0;
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += G, ++i) {
         const int nxt = tile + G < ntiles ? a.work[(tile + G) / nmt].nrows : 0;  // prefetch
         const uint32_t idesc = instr_desc(128, (nrows + 15) & ~15);
-        const uint32_t b = i & 1;
-        if (i >= 2 && !mb_wait(&accEmpty[b], ((i >> 1) - 1) & 1, &abort_flag)) {
+        if (i >= 1 && !mb_wait(&accEmpty, (i - 1) & 1, &abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t dcol = tmem + kAccCol + 128 * b;
-        for (int kb = 0; kb < nb; ++kb, ++j) {
-          const uint32_t sa = j % kASlots, sb = j % kBS;
-          if (!mb_wait(&fullA[sa], (j / kASlots) & 1, &abort_flag) ||
-              !mb_wait(&fullB[sb], (j / kBS) & 1, &abort_flag)) {
+        for (int kb = 0; kb < nb; ++kb) {
+          if (!mb_wait(&full[s], ph, &abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t bb = su32(ringB + sb * kBSlot);
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            umma_ts(dcol, tmem + kACol + 32 * sa + 8 * kk, smem_desc(bb + kk * 32), idesc, (kb | kk) != 0);
-          umma_commit(&emptyA[sa]);
-          umma_commit(&emptyB[sb]);
+          umma_ts_k64(tmem + kAccCol, tmem + kACol + 32 * s, dB0 + ((s * kBSlot) >> 4), idesc, kb != 0);
+          umma_commit(&empty[s]);
+          if (++s == kStages) s = 0, ph ^= 1;
         }
-        if (ok) umma_commit(&accFull[b]);
+        if (ok) umma_commit(&accFull);
         nrows = nxt;
       }
       // every MMA issued above has completed once `done` fires
@@ -435,32 +448,39 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a, const __
     }
     if (lane == 0) drain_ring(fullW, kWS, u, wl, kWLoaders);
   } else if (warp >= kBLoader0 && warp < kBLoader0 + kBLoaders) {
-    // --------------------------- activation loader -------------------------------
-    // warp kBLoader0 + b loads blocks j = b, b + kBLoaders, ... (one instruction
-    // each): lane i < ceil(nrows / 32): box of token rows row0 + 32 i .. +31 (rows past the
-    // item belong to the next item or are out of bounds (zero-filled); their
-    // accumulator columns are never stored)
+    // --------------------------- activation loaders -----------------------------
+    // warp kBLoader0 + b loads blocks j = b, b + kBLoaders, ... of the stage
+    // ring: one TMA box of the item's rows (the smallest of 32/64/128/256 rows
+    // that covers them; rows past the item belong to the next item or are out
+    // of bounds and zero-filled, and their accumulator columns are never stored).
     uint32_t j = 0;
     WorkItem it = a.work[blockIdx.x / nmt];
     for (int tile = blockIdx.x; tile < ntiles && ok; tile += G) {
       const WorkItem nit = tile + G < ntiles ? a.work[(tile + G) / nmt] : it;  // prefetch
-      const int nbox = (it.nrows + kBBoxRows - 1) / kBBoxRows;
+      const int kind = it.nrows <= 32 ? 0 : (it.nrows <= 64 ? 1 : (it.nrows <= 128 ? 2 : 3));
+      const uint32_t bytes = (32u << kind) * 128u;
       for (int kb = 0; kb < nb; ++kb, ++j) {
         if (j % kBLoaders != (uint32_t)(warp - kBLoader0)) continue;
-        const uint32_t sb = j % kBS;
-        if (j >= (uint32_t)kBS && !mb_wait(&emptyB[sb], ((j / kBS) - 1) & 1, &abort_flag)) {
+        const uint32_t s = j % kStages;
+        if (j >= (uint32_t)kStages && !mb_wait(&empty[s], ((j / kStages) - 1) & 1, &abort_flag)) {
           ok = false;
           break;
         }
-        if (lane == 0) mb_expect(&fullB[sb], (uint32_t)nbox * kBBoxRows * 128u);
+        if (lane == 0) {
+          mb_expect(&full[s], bytes);
+          tma_load_2d(su32(ringB + s * kBSlot), &tmB.m[kind], kb * 64, it.row0, &full[s]);
+        }
         __syncwarp();
-        if (lane < nbox)
-          tma_load_2d(su32(ringB + sb * kBSlot) + lane * kBBoxRows * 128, &tmB, kb * 64, it.row0 + kBBoxRows * lane,
-                      &fullB[sb]);
       }
       it = nit;
     }
-    if (lane == 0) drain_ring(fullB, kBS, j, warp - kBLoader0, kBLoaders);
+    // the stage barriers also count the dequantisers' arrivals, so after an
+    // abort they may never complete: give the boxes in flight time to land
+    if (!ok && lane == 0) {
+      const long long t0 = clock64();
+      while (clock64() - t0 < (1ll << 22)) {
+      }
+    }
   } else if (warp >= kDeq0 && warp < kDeq0 + kDeqWarps) {
     // ------------------------------- dequantisers -------------------------------
     const int quad = warp & 3;                  // TMEM lanes 32 quad .. +31
@@ -478,11 +498,11 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a, const __
     const float zpf = AWQ ? (float)(128 + a.zp) : 128.f;
     const uint32_t zp2 = bf16x2_of(zpf);
     const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16) + kACol;
-    uint32_t j = 0;  // block counter (A slots)
+    uint32_t j = 0;  // block counter (stage ring)
     for (uint32_t ti = 0; ti < my_tiles && ok; ++ti) {
       for (int kb = h; kb < nb; kb += 2) {
         const uint32_t jb = j + kb;
-        const uint32_t u = ti * nsl + kb / kSlotBlocks, sw = u % kWS, sa = jb % kASlots;
+        const uint32_t u = ti * nsl + kb / kSlotBlocks, sw = u % kWS, sa = jb % kStages;
         const int c = kb % kSlotBlocks;
         if (!mb_wait(&fullW[sw], (u / kWS) & 1, &abort_flag)) {
           ok = false;
@@ -532,7 +552,7 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a, const __
         // the slot's words are in registers: release it after this warp's last block in it
         __syncwarp();
         if (lane == 0 && (c + 2 >= kSlotBlocks || kb + 2 >= nb)) mb_arrive(&emptyW[sw]);
-        if (jb >= (uint32_t)kASlots && !mb_wait(&emptyA[sa], ((jb / kASlots) - 1) & 1, &abort_flag)) {
+        if (jb >= (uint32_t)kStages && !mb_wait(&empty[sa], ((jb / kStages) - 1) & 1, &abort_flag)) {
           ok = false;
           break;
         }
@@ -540,29 +560,30 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a, const __
         tmem_st32(tl + 32 * sa, r);
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mb_arrive(&fullA[sa]);
+        if (lane == 0) mb_arrive(&full[sa]);
       }
       j += nb;
     }
   } else {
     // --------------------------------- epilogue ---------------------------------
+    // two warps per TMEM lane quadrant, each draining half of the N columns
     const int quad = warp & 3;
+    const int half = (warp - kEpi0) >> 2;
     const uint32_t tq = tmem + ((uint32_t)(quad * 32) << 16) + kAccCol;
     uint32_t i = 0;
     for (int tile = blockIdx.x; tile < ntiles && ok; tile += G, ++i) {
       const WorkItem it = a.work[tile / nmt];  // loads while the accumulator fills
       const int mt = tile % nmt;
-      const uint32_t b = i & 1;
-      if (!mb_wait(&accFull[b], (i >> 1) & 1, &abort_flag)) {
+      if (!mb_wait(&accFull, i & 1, &abort_flag)) {
         ok = false;
         break;
       }
       tc_fence_after();
       const int N = (it.nrows + 15) & ~15;
-      const uint32_t ta = tq + 128 * b;
-      for (int c0 = 0; c0 < N; c0 += 16) {
+      const int cbeg = half * 128, cend = min(N, cbeg + 128);
+      for (int c0 = cbeg; c0 < cend; c0 += 16) {
         float v[16];
-        tmem_ld16(ta + c0, v);
+        tmem_ld16(tq + c0, v);
         if (MODE == MODE_GATE_UP) {
           // lanes 0..15: gate rows, lanes 16..31: the same up rows; the pair
           // (c, c+1) is split: gate lane -> column c, up lane -> column c+1
@@ -595,7 +616,7 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a, const __
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mb_arrive(&accEmpty[b]);
+      if (lane == 0) mb_arrive(&accEmpty);
     }
   }
 
@@ -645,14 +666,14 @@ EncodeTiled tensor_map_encoder() {
   }();
   return fn;
 }
-// B operand: `rows` x K bf16, row stride ld elements; boxes of kBBoxRows rows x
-// 64 elements (128 B, the 128-byte swizzle span); out-of-bounds rows read zero.
-bool b_tensor_map(CUtensorMap* m, const void* base, int K, int rows, int ld) {
+// B operand: `rows` x K bf16, row stride ld elements; boxes of 64 elements
+// (128 B, the 128-byte swizzle span) x box_rows rows; out-of-bounds rows read zero.
+bool b_tensor_map(CUtensorMap* m, const void* base, int K, int rows, int ld, int box_rows) {
   const EncodeTiled enc = tensor_map_encoder();
   if (!enc || rows <= 0 || K <= 0 || (reinterpret_cast<uintptr_t>(base) & 15) || (ld * 2) % 16) return false;
   const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
-  const cuuint32_t box[2] = {64, (cuuint32_t)kBBoxRows};
+  const cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
   const cuuint32_t estr[2] = {1, 1};
   return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
@@ -715,8 +736,9 @@ int sm_count() {
 
 template <int MODE, int GSB, bool AWQ>
 static cudaError_t launch_u(const GemmArgs& a, int max_work, int b_rows, cudaStream_t st) {
-  CUtensorMap tmB;
-  if (!b_tensor_map(&tmB, a.B, a.K, b_rows, a.ldb)) return cudaErrorInvalidValue;
+  BMaps tmB;
+  for (int k = 0; k < kBBoxKinds; ++k)
+    if (!b_tensor_map(&tmB.m[k], a.B, a.K, b_rows, a.ldb, 32 << k)) return cudaErrorInvalidValue;
   constexpr int smem = WRing<AWQ>::kSmem;
   cudaError_t e = cudaFuncSetAttribute(k_int4_umma<MODE, GSB, AWQ>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -738,7 +760,7 @@ static cudaError_t launch_u_gs(const GemmArgs& a, int max_work, int b_rows, cuda
 }
 
 // Requires M % 64 (gate/up) or M % 128 (down) == 0, K % 128 == 0, items of
-// at most 128 rows, gs in {32, 64, 128}, and B = b_rows contiguous expert-
+// at most kUmmaRows (256) rows, gs in {32, 64, 128}, and B = b_rows contiguous expert-
 // sorted rows (a.gather is not used).
 cudaError_t launch_gemm_umma(int mode, const GemmArgs& a, int max_work, int awq, int b_rows, cudaStream_t st) {
   if (max_work <= 0) return cudaSuccess;

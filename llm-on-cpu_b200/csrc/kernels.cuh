@@ -89,8 +89,9 @@ cudaError_t launch_gemm(int mode, int path, const GemmArgs& a, int max_work, int
 // memory stage ring (decode-size items, K % 128 == 0, gs in {32, 64, 128}).
 cudaError_t launch_gemm_tma(int mode, const GemmArgs& a, int max_work, int awq, cudaStream_t st);
 // int4_umma.cu: tcgen05.mma (TMEM accumulator) grouped GEMM for work items of
-// up to 128 rows (prefill-size groups); same K / group-size conditions.  B is
+// up to kUmmaRows rows (prefill-size groups); same K / group-size conditions.  B is
 // b_rows contiguous expert-sorted rows read by TMA (a.gather unused).
+constexpr int kUmmaRows = 256;
 cudaError_t launch_gemm_umma(int mode, const GemmArgs& a, int max_work, int awq, int b_rows, cudaStream_t st);
 // TMA tensor maps (128 bytes each) of every expert's repacked weights for the
 // tcgen05 kernel, kMapsPerExpert per expert: [part * 3 + proj], part 0 raw

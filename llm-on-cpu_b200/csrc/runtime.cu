@@ -353,8 +353,8 @@ int gemm_path_pref() {
 
 // Rows per work item: decode-size batches use one mma N tile (8 rows), so
 // that kernel variant has no per-tile branches; prefill-size batches use
-// 128-row items for the tcgen05 kernel (32 when the mma path is forced).
-int chunk_rows(int T) { return T <= 128 ? 8 : (gemm_path_pref() == 1 ? kChunkRows : 128); }
+// kUmmaRows-row items for the tcgen05 kernel (32 when the mma path is forced).
+int chunk_rows(int T) { return T <= 128 ? 8 : (gemm_path_pref() == 1 ? kChunkRows : kUmmaRows); }
 
 struct WsLayout {
   size_t logits, ids, weights, offsets, sorted, inverse, work, n_work, n_active, err, mid, partial,
@@ -363,19 +363,19 @@ struct WsLayout {
 };
 
 // The tcgen05 prefill GEMMs run when K of both GEMMs is a multiple of 128, the
-// group is 32/64/128 wide (every BASELINE shape) and the items are 128 rows.
+// group is 32/64/128 wide (every BASELINE shape) and the items are kUmmaRows rows.
 bool tc_shapes(const llmoc_moe_layer* L) {
   const int gs = L->d.group_size;
   return L->d.hidden % 128 == 0 && L->d.inter % 128 == 0 && (gs == 32 || gs == 64 || gs == 128);
 }
 
 // Items hold at most `chunk` rows: 8 for decode-size groups (register-fed
-// tensor-core kernel), 128 for the tcgen05 kernel.
+// tensor-core kernel), kUmmaRows for the tcgen05 kernel.
 int chunk_for_rows(int pairs, int groups) {
-  return pairs <= 8 * std::max(1, groups) + groups / 2 ? 8 : (gemm_path_pref() == 1 ? kChunkRows : 128);
+  return pairs <= 8 * std::max(1, groups) + groups / 2 ? 8 : (gemm_path_pref() == 1 ? kChunkRows : kUmmaRows);
 }
 bool use_umma_c(const llmoc_moe_layer* L, int chunk) {
-  return tc_shapes(L) && L->wmaps && chunk == 128 && gemm_path_pref() != 2;
+  return tc_shapes(L) && L->wmaps && chunk == kUmmaRows && gemm_path_pref() != 2;
 }
 
 // Workspace of one grouped run over T rows with kk slots each, permuted over
@@ -775,7 +775,7 @@ EpSrcLayout ep_src_layout(const llmoc_moe_layer* L, int T) {
 // owner-rank workspace for `rows` received rows (the larger of the two item sizes)
 size_t ep_owner_bytes(const llmoc_moe_layer* L, int rows) {
   return std::max(ws_layout_g(L, rows, 1, L->n_exp, 8, false).total,
-                  ws_layout_g(L, rows, 1, L->n_exp, gemm_path_pref() == 1 ? kChunkRows : 128, false).total);
+                  ws_layout_g(L, rows, 1, L->n_exp, gemm_path_pref() == 1 ? kChunkRows : kUmmaRows, false).total);
 }
 
 }  // namespace

@@ -141,15 +141,16 @@ def test_workspace_too_small_is_rejected(oracle):
     dl.close()
 
 
-def test_skewed_routing_hot_expert(oracle):
+@pytest.mark.parametrize("T", [200, 600])
+def test_skewed_routing_hot_expert(oracle, T):
     """Every token prefers the same few experts (one expert gets all T pairs):
-    exercises multi-chunk work items of one expert and empty experts."""
+    exercises multi-chunk work items of one expert (T = 600: items of 256,
+    256 and 88 rows on the tcgen05 path) and empty experts."""
     rng = np.random.default_rng(6)
     layer = orc.make_layer(oracle, rng, H=512, I=256, E=32, topk=4, gs=128)
     rw = orc.bits_to_f32(layer.router_w)
     rw[:4] += 0.5  # a strong shared component towards experts 0..3
     layer.router_w = orc.bf16_bits(rw)
-    T = 200
     X = np.abs(orc.make_tokens(rng, T, 512))
     dl = G.DevLayer(layer, T)
     Y, ws_bytes = dl.forward(X)
@@ -186,7 +187,8 @@ FULL = {
 
 
 @pytest.mark.parametrize("name,T", [("qwen3_30b_a3b", 1), ("qwen3_30b_a3b", 8), ("qwen3_30b_a3b", 64),
-                                    ("qwen3_30b_a3b", 512), ("glm45_air", 64), ("kimi_k2", 64)])
+                                    ("qwen3_30b_a3b", 512), ("glm45_air", 64), ("glm45_air", 1024),
+                                    ("kimi_k2", 64), ("kimi_k2", 1024)])
 def test_full_size_layer(oracle, name, T):
     """Full BASELINE shapes: routing bit-exact for every token; outputs checked
     against the oracle on a sample of tokens (each token's output depends on
