@@ -23,6 +23,8 @@
 // expert (canonical order: expert, then t, then j), with per-expert offsets,
 // the inverse map, and the list of work items (<= 32 pairs of one expert).
 #include <cfloat>
+#include <cstdlib>
+#include <cstring>
 
 #include <algorithm>
 
@@ -135,6 +137,146 @@ __global__ void __launch_bounds__(256) k_router_logits(const XT* __restrict__ X,
         logits[(size_t)t * E + e] = isfinite(r) ? r : 0.f;
       }
     }
+}
+
+// ----------------------------------------------- router GEMV, tiled (bf16 X)
+//
+// The same arithmetic as k_router_logits, laid out as an SGEMM whose 32 lanes
+// are the 32 chains: lane c of a warp accumulates chain c (k = c mod 32, k
+// ascending) of TT tokens x EE experts in registers, one fmaf per k and
+// output, from fp32 copies of X and W_r staged through shared memory in
+// 256-wide K chunks (double-buffered; the next chunk's global loads are in
+// flight while the current one is multiplied).  After the K loop every lane
+// writes its chain values to shared memory and each thread folds whole
+// outputs in the reference's tree order.  A CTA of WT x WE warps covers
+// TT*WT tokens x EE*WE experts.  Requires H % 256 == 0.
+constexpr int kRouterKC = 256;
+
+template <int TT, int EE, int WT, int WE>
+struct RouterTile {
+  static constexpr int kThreads = 32 * WT * WE;
+  static constexpr int kRowsX = TT * WT, kRowsW = EE * WE, kRows = kRowsX + kRowsW;
+  static constexpr int kChunks = kRows * (kRouterKC / 8);            // 8-element pieces per stage
+  static constexpr int kPer = (kChunks + kThreads - 1) / kThreads;   // per thread
+  static constexpr int kStage = kRows * kRouterKC;                   // floats per stage
+  static constexpr int kOut = kRowsX * kRowsW;
+  static constexpr size_t kSmem =
+      (size_t)4 * (2 * kStage > kOut * 33 ? 2 * kStage : kOut * 33);  // stages, reused for the fold
+};
+
+template <int TT, int EE, int WT, int WE>
+__global__ void __launch_bounds__(RouterTile<TT, EE, WT, WE>::kThreads, 1)
+    k_router_tiled(const __nv_bfloat16* __restrict__ X, const uint16_t* __restrict__ Wr, int T, int E, int H,
+                   float* __restrict__ logits) {
+  using RT = RouterTile<TT, EE, WT, WE>;
+  extern __shared__ float rsm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tg = warp % WT, eg = warp / WT;
+  const int t0 = blockIdx.y * RT::kRowsX, e0 = blockIdx.x * RT::kRowsW;
+
+  // staging piece q: row q / 32 (X rows first, then W_r rows), k offset 8 (q % 32)
+  const uint4* src[RT::kPer];
+  bool live[RT::kPer];
+#pragma unroll
+  for (int p = 0; p < RT::kPer; ++p) {
+    const int q = threadIdx.x + p * RT::kThreads;
+    live[p] = q < RT::kChunks;
+    const int row = live[p] ? q / 32 : 0, k8 = q % 32;
+    const uint16_t* base = row < RT::kRowsX
+                               ? reinterpret_cast<const uint16_t*>(X) + (size_t)min(t0 + row, T - 1) * H
+                               : Wr + (size_t)min(e0 + row - RT::kRowsX, E - 1) * H;
+    src[p] = reinterpret_cast<const uint4*>(base + 8 * k8);
+  }
+  uint4 stg[RT::kPer];
+  auto fetch = [&](int kc) {
+#pragma unroll
+    for (int p = 0; p < RT::kPer; ++p)
+      if (live[p]) stg[p] = __ldg(src[p] + kc / 8);
+  };
+  auto park = [&](int s) {  // staged bf16 -> fp32 in stage s
+#pragma unroll
+    for (int p = 0; p < RT::kPer; ++p) {
+      if (!live[p]) continue;
+      const int q = threadIdx.x + p * RT::kThreads;
+      float4* d = reinterpret_cast<float4*>(rsm + (size_t)s * RT::kStage + (q / 32) * kRouterKC + 8 * (q % 32));
+      const uint4 u = stg[p];
+      d[0] = make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u),
+                         __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xFFFF0000u));
+      d[1] = make_float4(__uint_as_float(u.z << 16), __uint_as_float(u.z & 0xFFFF0000u),
+                         __uint_as_float(u.w << 16), __uint_as_float(u.w & 0xFFFF0000u));
+    }
+  };
+
+  float acc[TT][EE];
+#pragma unroll
+  for (int a = 0; a < TT; ++a)
+#pragma unroll
+    for (int b = 0; b < EE; ++b) acc[a][b] = 0.f;
+
+  fetch(0);
+  park(0);
+  __syncthreads();
+  const int nk = H / kRouterKC;
+  for (int c = 0; c < nk; ++c) {
+    const int s = c & 1;
+    if (c + 1 < nk) fetch((c + 1) * kRouterKC);
+    const float* xs = rsm + (size_t)s * RT::kStage + (tg * TT) * kRouterKC + lane;
+    const float* ws = rsm + (size_t)s * RT::kStage + (RT::kRowsX + eg * EE) * kRouterKC + lane;
+#pragma unroll 2
+    for (int i = 0; i < kRouterKC / 32; ++i) {
+      float xv[TT], wv[EE];
+#pragma unroll
+      for (int a = 0; a < TT; ++a) xv[a] = xs[a * kRouterKC + 32 * i];
+#pragma unroll
+      for (int b = 0; b < EE; ++b) wv[b] = ws[b * kRouterKC + 32 * i];
+#pragma unroll
+      for (int a = 0; a < TT; ++a)
+#pragma unroll
+        for (int b = 0; b < EE; ++b) acc[a][b] = __fmaf_rn(xv[a], wv[b], acc[a][b]);
+    }
+    if (c + 1 < nk) park(s ^ 1);
+    __syncthreads();
+  }
+
+  // chain values -> shared memory [output][chain] (33-float rows), then fold
+  // one output per thread: a[i] = (c[i]+c[8+i]) + (c[16+i]+c[24+i]);
+  // b[i] = a[i] + a[4+i]; r = (b0+b1) + (b2+b3)
+#pragma unroll
+  for (int a = 0; a < TT; ++a)
+#pragma unroll
+    for (int b = 0; b < EE; ++b) {
+      const int o = (tg * TT + a) * RT::kRowsW + eg * EE + b;
+      rsm[o * 33 + lane] = acc[a][b];
+    }
+  __syncthreads();
+  for (int o = threadIdx.x; o < RT::kOut; o += RT::kThreads) {
+    const int t = t0 + o / RT::kRowsW, e = e0 + o % RT::kRowsW;
+    if (t >= T || e >= E) continue;
+    const float* ch = rsm + o * 33;
+    float av[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) av[i] = (ch[i] + ch[8 + i]) + (ch[16 + i] + ch[24 + i]);
+    float bv[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) bv[i] = av[i] + av[4 + i];
+    const float r = (bv[0] + bv[1]) + (bv[2] + bv[3]);
+    logits[(size_t)t * E + e] = isfinite(r) ? r : 0.f;
+  }
+}
+
+template <int TT, int EE, int WT, int WE>
+static cudaError_t launch_router_tiled(const __nv_bfloat16* X, const uint16_t* Wr, int T, int E, int H,
+                                       float* logits, cudaStream_t st) {
+  using RT = RouterTile<TT, EE, WT, WE>;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(k_router_tiled<TT, EE, WT, WE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)RT::kSmem);
+    attr = true;
+  }
+  const dim3 grid((E + RT::kRowsW - 1) / RT::kRowsW, (T + RT::kRowsX - 1) / RT::kRowsX);
+  k_router_tiled<TT, EE, WT, WE><<<grid, RT::kThreads, RT::kSmem, st>>>(X, Wr, T, E, H, logits);
+  return cudaGetLastError();
 }
 
 // --------------------------------------------------------------- top-k
@@ -351,6 +493,19 @@ __global__ void __launch_bounds__(kPermThreads) k_permute(PermArgs a) {
 cudaError_t launch_router_logits(const void* X, bool x_is_f32, const uint16_t* Wr, int T, int E,
                                  int H, float* logits, cudaStream_t st) {
   if (T <= 0) return cudaSuccess;
+  // bf16 activations with H % 256 == 0 (every BASELINE shape): the tiled
+  // kernel, its tile chosen by T; LLMOC_ROUTER_PATH=lanes keeps the
+  // lane-group kernel below (same arithmetic) for comparison
+  static const bool lanes_only = [] {
+    const char* v = getenv("LLMOC_ROUTER_PATH");
+    return v && !strcmp(v, "lanes");
+  }();
+  if (!x_is_f32 && H % kRouterKC == 0 && !lanes_only) {
+    const auto* Xb = static_cast<const __nv_bfloat16*>(X);
+    if (T <= 8) return launch_router_tiled<8, 1, 1, 8>(Xb, Wr, T, E, H, logits, st);    // 8 t x 8 e
+    if (T < 128) return launch_router_tiled<8, 2, 1, 8>(Xb, Wr, T, E, H, logits, st);   // 8 t x 16 e
+    return launch_router_tiled<8, 16, 4, 2>(Xb, Wr, T, E, H, logits, st);               // 32 t x 32 e
+  }
   const int threads = 256;
   if (T <= 64) {
     const long groups = (long)T * E;

@@ -107,6 +107,26 @@ def test_routing_bit_exact(oracle, name, T):
     dl.close()
 
 
+@pytest.mark.parametrize("T", [3, 77, 150])
+def test_router_tiles_bit_exact(oracle, T):
+    """Router logits of every token bitwise equal to the reference's AVX2 order
+    on each tile shape of the tiled router (T <= 8, 8 < T < 128, T >= 128),
+    with partial token and expert tiles (E = 40, T not a multiple of 32) and a
+    non-finite activation (that token's logits become 0, as in the reference)."""
+    rng = np.random.default_rng(40 + T)
+    layer = orc.make_layer(oracle, rng, H=768, I=128, E=40, topk=4, gs=128)
+    X = orc.make_tokens(rng, T, 768)
+    X[T // 2, 5] = np.inf
+    dl = G.DevLayer(layer, T)
+    _, ws_bytes = dl.forward(X)
+    v = dl.views(T, ws_bytes)
+    for t in range(T):
+        ref = oracle.gemm_bias_free(X[t], layer.router_w)
+        assert np.array_equal(v["logits"][t].view(np.uint32), ref.view(np.uint32)), t
+    assert np.all(v["logits"][T // 2] == 0)
+    dl.close()
+
+
 @pytest.mark.parametrize("name", list(SMALL))
 @pytest.mark.parametrize("T", [1, 5, 40, 129])
 def test_layer_matches_oracle(oracle, name, T):
