@@ -46,6 +46,9 @@ CONFIGS = {
     "glm45_air": dict(H=4096, I=1408, E=128, topk=8, gs=128, router=1, scaling=1.0, shared=True),
     "kimi_k2": dict(H=7168, I=2048, E=384, topk=8, gs=32, router=1, scaling=2.827, shared=True),
 }
+# 48 Qwen3-30B-A3B-shape MoE layers (router + FFN, residual
+# add between layers), decode T in {1, 4, 16}, expert popularity Zipf(s=1.1)
+STACKS = {"qwen3_30b_a3b_stack48": dict(base="qwen3_30b_a3b", layers=48, zipf=1.1, mu=64.0, x_std=4.0)}
 L2_BYTES = 126 * 1024 * 1024
 
 
@@ -55,7 +58,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="llmoc", choices=["llmoc", "reference"])
-    ap.add_argument("--config", default="qwen3_30b_a3b", choices=list(CONFIGS))
+    ap.add_argument("--config", default="qwen3_30b_a3b", choices=list(CONFIGS) + list(STACKS))
     ap.add_argument("--tokens", type=int, default=64)
     ap.add_argument("--sweep", default="1,8,64,512", help="extra T values ('' = none)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -147,11 +150,13 @@ def ncu_traffic(config: str, T: int):
 
 # ------------------------------------------------------- device workload
 
-def build_layers(torch, L, cfg, R, seed, keep_host=False, device=0, ep=None):
+def build_layers(torch, L, cfg, R, seed, keep_host=False, device=0, ep=None, rw_add=None):
     """R distinct layers generated and quantized in HBM (llmoc_quantize_awq_sym),
     then repacked by llmoc_moe_layer_create_device (or, with ep = (rank,
     world), this rank's expert-parallel shard of each).  keep_host returns the
-    first layer's QLWC tensors on the host for the CPU baseline."""
+    first layer's QLWC tensors on the host for the CPU baseline.  rw_add(r)
+    returns an [E, H] fp32 tensor added to copy r's router weights before
+    they are rounded to bf16 (the Zipf-skewed stack)."""
     H, I, E, gs = cfg["H"], cfg["I"], cfg["E"], cfg["gs"]
     n_exp = E + (1 if cfg["shared"] else 0)
     g = torch.Generator(device="cuda")
@@ -170,7 +175,10 @@ def build_layers(torch, L, cfg, R, seed, keep_host=False, device=0, ep=None):
                 L.quantize_awq_sym(W, (e1 - e0) * M, K, gs, True, q[e0 * M:e1 * M], s[e0 * M:e1 * M], stream)
                 del W
             raw[name] = (q, s, M, K)
-        rw = (torch.randn((E, H), generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+        rw = torch.randn((E, H), generator=g, device="cuda") * 0.02
+        if rw_add is not None:
+            rw = rw + rw_add(r)
+        rw = rw.to(torch.bfloat16)
         bias = (torch.randn((E,), generator=g, device="cuda") * 0.1).float() if cfg["router"] == 1 else None
         views = []
         for e in range(n_exp):
@@ -433,6 +441,183 @@ def run_llmoc(args):
     return out
 
 
+def zipf_targets(E, k, s):
+    """Per-expert selection frequencies f_r = min(1, c r^-s), sum k (a token
+    picks an expert at most once, so the most popular ones saturate at 1)."""
+    r = np.arange(1, E + 1, dtype=np.float64)
+    lo, hi = 0.0, 1e6
+    for _ in range(200):
+        c = 0.5 * (lo + hi)
+        if np.minimum(1.0, c * r ** -s).sum() > k:
+            hi = c
+        else:
+            lo = c
+    return np.minimum(1.0, lo * r ** -s)
+
+
+def calibrate_boosts(E, k, sigma, target, seed, iters=80, n=16384):
+    """Logit offsets b (mean 0) so that top-k of N(0, sigma^2) noise + b picks
+    expert r with frequency target[r]."""
+    rng = np.random.default_rng(seed)
+    noise = rng.standard_normal((n, E)) * sigma
+    b = np.zeros(E)
+    f = None
+    for _ in range(iters):
+        top = np.argpartition(-(noise + b), k, axis=1)[:, :k]
+        f = np.bincount(top.ravel(), minlength=E) / n
+        b += 0.5 * (np.log(target + 1e-4) - np.log(f + 1e-4))
+        b -= b.mean()
+    return b, f
+
+
+def run_stack(args):
+    """a step is one decode pass of T tokens through 48 MoE
+    layers (router + expert FFN, in-place residual add fused into the combine:
+    llmoc_moe_forward_residual), T in {1, 4, 16}.  Expert popularity follows
+    Zipf(1.1): every router row gets c_e * v and every hidden state mu * v for
+    a fixed unit vector v, with c_e calibrated on the host against truncated
+    Zipf targets (each layer its own random expert order); the measured
+    selection histogram is reported beside the target's."""
+    import torch
+    import llmoc_b200 as L
+
+    st = STACKS[args.config]
+    cfg = CONFIGS[st["base"]]
+    H, E, k, NL = cfg["H"], cfg["E"], cfg["topk"], st["layers"]
+    torch.cuda.set_device(0)
+    Ts = sorted({args.tokens if args.tokens <= 16 else 16} | ({1, 4, 16} if args.sweep else set()))
+    target = zipf_targets(E, k, st["zipf"])
+    # hidden states N(0, x_std^2) + mu v: x_std well above the size of one layer's
+    # output keeps the logits' noise (and so the skew) nearly constant through the
+    # 48 residual adds
+    sigma = 0.02 * np.sqrt(H) * st["x_std"]  # std of a logit from N(0, 0.02^2) rows
+    boosts, f_model = calibrate_boosts(E, k, sigma, target, seed=5)
+    g = torch.Generator(device="cuda").manual_seed(77)
+    v = torch.randn((H,), generator=g, device="cuda")
+    v = v / v.norm()
+    perms = [np.random.default_rng(100 + l).permutation(E) for l in range(NL)]
+    mu = st["mu"]
+
+    def rw_add(l):
+        c = torch.tensor(boosts[np.argsort(perms[l])] / mu, dtype=torch.float32, device="cuda")  # expert e -> rank
+        return c[:, None] * v[None, :]
+
+    layers = []
+    for l in range(NL):  # one distinct layer each (15 GB of experts: no reuse through L2 across layers)
+        lay, _ = build_layers(torch, L, cfg, 1, seed=4321 + 7 * l, rw_add=lambda r, l=l: rw_add(l))
+        layers += lay
+    Tmax = max(Ts)
+    ws_bytes = layers[0].workspace_bytes(Tmax)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+    X0 = (torch.randn((Tmax, H), generator=g, device="cuda") * st["x_std"] + mu * v[None, :]).to(torch.bfloat16)
+    X = torch.empty_like(X0)
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    gu_b, dn_b = layer_bytes(cfg)
+    exp_b = gu_b + dn_b
+
+    def step(T):
+        for lay in layers:
+            lay.forward_residual(X, T, X, X, ws, ws_bytes, sp)
+
+    results = {}
+    clocks = Clocks(0)
+    clk, launches = None, 0
+    for T in Ts:
+        X.copy_(X0)
+        for _ in range(max(3, args.warmup)):
+            step(T)
+        # selection histogram and touched experts of one step, layer by layer
+        X.copy_(X0)
+        hist = np.zeros(E)
+        touched = 0
+        for l, lay in enumerate(layers):
+            lay.forward_residual(X, T, X, X, ws, ws_bytes, sp)
+            vw = lay.route_views(T, ws, ws_bytes)
+            off = ws[vw.offsets - ws.data_ptr(): vw.offsets - ws.data_ptr() + 4 * (E + 1)].cpu().numpy().view(np.int32)
+            cnt = np.diff(off)
+            touched += int(np.count_nonzero(cnt))
+            hist += cnt[perms[l]]  # by popularity rank
+        torch.cuda.synchronize()
+        if T == max(Ts):
+            clocks.start()
+            t_end = time.perf_counter() + 1.5
+            while time.perf_counter() < t_end:
+                step(T)
+                torch.cuda.synchronize()
+            n0 = L.launch_count()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(args.steps):
+            step(T)
+        b.record(stream)
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b)
+        if T == max(Ts):
+            launches = L.launch_count() - n0
+            clk = clocks.stop()
+        results[T] = dict(ms=ms, touched=touched, hist=hist)
+
+    T = max(Ts)
+    Xh = torch.empty((T, H), dtype=torch.bfloat16, pin_memory=True)
+    Xh.copy_(X0[:T].cpu())
+    Yh = torch.empty((T, H), dtype=torch.bfloat16, pin_memory=True)
+
+    def e2e_step():
+        X[:T].copy_(Xh, non_blocking=True)
+        step(T)
+        Yh.copy_(X[:T], non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms_e2e = a.elapsed_time(b)
+
+    peak, peak_kind = measured_peak()
+    sweep = {}
+    for t_, rr in results.items():
+        per = rr["ms"] / args.steps
+        byts = rr["touched"] * exp_b + NL * (E * H * 2 + 2 * t_ * H * 2)
+        h = rr["hist"] / rr["hist"].sum()
+        sweep[str(t_)] = {"tokens_per_s": t_ * args.steps / (rr["ms"] * 1e-3), "ms_per_step": per,
+                          "touched_experts_per_layer": rr["touched"] / NL, "GBps": byts / (per * 1e-3) / 1e9,
+                          "hbm_frac": byts / (per * 1e-3) / 1e9 / peak,
+                          "pair_share_by_rank": {"top1": round(float(h[0]), 4), "top8": round(float(h[:8].sum()), 4),
+                                                 "top32": round(float(h[:32].sum()), 4)}}
+    r = results[T]
+    per = r["ms"] / args.steps
+    byts = r["touched"] * exp_b + NL * (E * H * 2 + 2 * T * H * 2)
+    tgt = target / target.sum()
+    out = {
+        "metric": "INT4 MoE 48-layer stack tokens/s (decode, T=%d)" % T,
+        "value": T * args.steps / (r["ms"] * 1e-3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": max(3, args.warmup), "ms_per_step": per, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int4 weights x bf16 activations, fp32 accumulate",
+        "data": "synthetic (seeded device RNG; BASELINE config 3 shapes, Zipf-skewed router)",
+        "config": {"workload": "qwen3_30b_a3b x 48 layers (BASELINE config 3)", "tokens": T, "layers": NL,
+                   "zipf_s": st["zipf"], "l2": "48 distinct layers (15 GB of experts)",
+                   "zipf_target_share": {"top1": round(float(tgt[0]), 4), "top8": round(float(tgt[:8].sum()), 4),
+                                         "top32": round(float(tgt[:32].sum()), 4)}},
+        "e2e": {"value": T * args.steps / (ms_e2e * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2,
+                "d2h_bytes_per_step": T * H * 2},
+        "roofline": {"bound": "hbm", "kernel": "whole 48-layer step", "achieved": byts / (per * 1e-3) / 1e9,
+                     "peak": peak, "unit": "GB/s", "frac": byts / (per * 1e-3) / 1e9 / peak, "peak_kind": peak_kind,
+                     "traffic": None, "alg_bytes_per_launch": byts, "launch_ms": per},
+        "sweep": sweep, "cpu_baseline": None, "clocks": clk, "gpu_launches": int(launches),
+    }
+    print(json.dumps(out), flush=True)
+    for lay in layers:
+        lay.close()
+    return out
+
+
 def run_reference(args):
     """The reference's own CPU implementation of the path on the host cores."""
     rank, world, _ = dist_env()
@@ -638,6 +823,8 @@ def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.config in STACKS:
+        run_stack(args)
     elif dist_env()[1] > 1:
         run_ep(args)
     else:

@@ -185,6 +185,15 @@ LLMOC_API size_t llmoc_moe_workspace_bytes(const llmoc_moe_layer* layer, int max
 LLMOC_API llmoc_status llmoc_moe_forward(const llmoc_moe_layer* layer, const uint16_t* X, int T, uint16_t* Y,
                                void* workspace, size_t workspace_bytes, void* stream);
 
+/* Y = R + MoE(X): the forward above with the decoder's residual add fused
+ * into the weighted combine (y = bf16(float(r) + sum), one rounding), so the
+ * residual stream stays on the device.  Replaces the per-token
+ * `down_acc` + caller-side add of src/model/qwen3_5_int4_model.cpp:1204-1208
+ * for a batch.  R may alias Y (in-place residual) and both may alias X. */
+LLMOC_API llmoc_status llmoc_moe_forward_residual(const llmoc_moe_layer* layer, const uint16_t* X, int T,
+                                                  const uint16_t* R, uint16_t* Y, void* workspace,
+                                                  size_t workspace_bytes, void* stream);
+
 /* Routing results inside a workspace after llmoc_moe_forward / llmoc_moe_route
  * (device pointers; kk = topk + has_shared slots per token):
  *   logits [T,E] fp32; ids [T,kk] int32; weights [T,kk] fp32;

@@ -70,4 +70,33 @@ __device__ __forceinline__ uint32_t lanemask_lt() {
   return m;
 }
 
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch.  The kernels of one forward are launched with
+// launch_pdl, so a kernel's CTAs may start while its predecessor in the stream
+// is still running.  Every such kernel calls grid_dep_wait() before it reads
+// anything its predecessor wrote (the wait returns once the predecessor has
+// completed and its memory is visible; it is a no-op for a normal launch),
+// then grid_dep_release() to let its own successor launch.  A kernel may do
+// independent work (e.g. fetch static weights of a work list that an earlier,
+// already waited-for kernel produced) before waiting.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_release() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 }  // namespace llmoc

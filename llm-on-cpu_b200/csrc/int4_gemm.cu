@@ -17,6 +17,8 @@
 // per group, times the group scale, accumulated in fp32; int4_ops.cpp:228)
 // is kept: the tensor core multiplies exact bf16 integers (q - zp) by bf16
 // activations, and the fp32 group partials are scaled on the accumulator.
+#include <algorithm>
+
 #include "kernels.cuh"
 
 namespace llmoc {
@@ -186,6 +188,15 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
   const int g = lane >> 2, t = lane & 3;
   const int slice = warp % ks;
   const int rt = blockIdx.x * (kWarps / ks) + warp / ks;
+  // launched with programmatic dependent launch: gate/up waits for its
+  // predecessor before reading the work list; the down GEMM (whose
+  // predecessor, gate/up, only released it after waiting for the kernel that
+  // built the work list) reads the work list and starts its weight copies
+  // first, and waits before touching the activations (gate/up's output)
+  if (MODE == MODE_GATE_UP) {
+    grid_dep_wait();
+    grid_dep_release();
+  }
   if ((int)blockIdx.y >= *a.n_work) return;
   const int Mt = (a.M + 15) >> 4;
   const bool live = rt < Mt;
@@ -226,8 +237,9 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
   }
   unsigned char* wbase = wsm + (size_t)warp * kStagesW * SG::kBytes;
 
-  // issue the copies of one step into a stage (every lane its own 16 B pieces)
-  auto issue = [&](int stage) {
+  // issue the copies of one step into a stage (every lane its own 16 B
+  // pieces): the weights (and scales, zeros), then the activations
+  auto issue_w = [&](int stage) {
     unsigned char* sb = wbase + stage * SG::kBytes;
 #pragma unroll
     for (int p = 0; p < NP; ++p) {
@@ -239,6 +251,9 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
       ssrc[p] += NG * 32;
       if (!AWQ) zsrc[p] += NG * 32;
     }
+  };
+  auto issue_b = [&](int stage) {
+    unsigned char* sb = wbase + stage * SG::kBytes;
 #pragma unroll
     for (int n = 0; n < NT; ++n) {
       if (bval[n]) {
@@ -249,10 +264,21 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
       bsrc[n] += 256;
     }
   };
+  auto issue = [&](int stage) {
+    issue_w(stage);
+    issue_b(stage);
+  };
 
 #pragma unroll
+  for (int d = 0; d < kStagesW - 1; ++d)
+    if (d < nst) issue_w(d);
+  if (MODE != MODE_GATE_UP) {
+    grid_dep_wait();
+    grid_dep_release();
+  }
+#pragma unroll
   for (int d = 0; d < kStagesW - 1; ++d) {
-    if (d < nst) issue(d);
+    if (d < nst) issue_b(d);
     cp_async_commit();
   }
 
@@ -402,6 +428,252 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
   }
 }
 
+// Persistent form of k_int4_mma for decode-size items (NT = 1: at most 8 rows
+// per item; no K split).  The grid stays resident; each warp takes units
+// (work item, 16-row tile) from a device counter (a.ctr, zeroed by the
+// permutation kernel) and runs their 128-wide K steps back to back through its
+// cp.async ring, which never drains between units: while the last steps of a
+// unit are multiplied, the first steps of the next one are in flight.  The
+// next unit's work item, activation row and weight pointers are fetched when
+// the copies enter the current one, so they are in registers when needed.
+// Same arithmetic, per unit, as k_int4_mma with ks = 1.
+template <int MODE, int GSB, bool AWQ>
+__global__ void __launch_bounds__(kWarps * 32) k_int4_mma_p(GemmArgs a) {
+  constexpr int NP = MODE == MODE_GATE_UP ? 2 : 1;
+  constexpr int NG = GSB == 4 ? 1 : (GSB == 2 ? 2 : 4);  // groups per step
+  using SG = WStage<NP, 1, AWQ>;
+  extern __shared__ __align__(128) unsigned char wsm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  unsigned char* wbase = wsm + (size_t)warp * kStagesW * SG::kBytes;
+  // programmatic dependent launch: as k_int4_mma (the down GEMM starts its
+  // first weight copies before it waits for gate/up's output)
+  if (MODE == MODE_GATE_UP) {
+    grid_dep_wait();
+    grid_dep_release();
+  }
+  const int Mt = (a.M + 15) >> 4;
+  const int nunits = *a.n_work * Mt;
+  const int nsteps = a.K >> 7;
+
+  // the next unit the copies will enter
+  int pu = 0, prow = 0;
+  WorkItem pit{};
+  const uint4* pq[NP];
+  const __half* ps[NP];
+  const __half* pz[NP];
+  auto prefetch = [&]() {
+    int u = 0;
+    if (lane == 0) u = atomicAdd(a.ctr, 1);
+    pu = __shfl_sync(0xffffffffu, u, 0);
+    if (pu < nunits) {
+      pit = a.work[pu / Mt];
+      const int pos = pit.row0 + (g < pit.nrows ? g : 0);
+      prow = a.gather ? a.gather[pos] / a.kk : pos;
+      const ExpertDev& ex = a.experts[pit.expert];
+      const ProjDev& P0 = MODE == MODE_GATE_UP ? ex.gate : pick(ex, a.proj);
+      pq[0] = P0.q;
+      ps[0] = P0.s;
+      pz[0] = P0.z;
+      if (NP == 2) {
+        pq[NP - 1] = ex.up.q;
+        ps[NP - 1] = ex.up.s;
+        pz[NP - 1] = ex.up.z;
+      }
+    }
+  };
+
+  // copy side: the unit being copied and its sources, advanced one step per issue
+  const unsigned char* wsrc[NP];
+  const unsigned char* ssrc[NP];
+  const unsigned char* zsrc[NP];
+  const unsigned char* bsrc = nullptr;
+  bool bval = false;
+  int is = 0, entered = 0;
+  int n_row0 = 0, n_nrows = 0, n_rt = 0;  // the unit last entered
+  auto enter = [&]() {
+    const int rt = pu % Mt;
+#pragma unroll
+    for (int p = 0; p < NP; ++p) {
+      wsrc[p] = reinterpret_cast<const unsigned char*>(pq[p] + (size_t)rt * a.Kc * 32 + piece_slot(lane));
+      ssrc[p] = reinterpret_cast<const unsigned char*>(ps[p] + (size_t)rt * a.ng * 16);
+      zsrc[p] = AWQ ? nullptr : reinterpret_cast<const unsigned char*>(pz[p] + (size_t)rt * a.ng * 16);
+    }
+    bval = g < pit.nrows;
+    bsrc = reinterpret_cast<const unsigned char*>(a.B) + ((size_t)prow * a.ldb + 8 * t) * 2;
+    n_row0 = pit.row0;
+    n_nrows = pit.nrows;
+    n_rt = rt;
+    is = 0;
+    ++entered;
+  };
+  auto issue_w = [&](int stage) {
+    unsigned char* sb = wbase + stage * SG::kBytes;
+#pragma unroll
+    for (int p = 0; p < NP; ++p) {
+      cp_async16(sb + p * 1024 + lane * 16, wsrc[p]);
+      cp_async16(sb + p * 1024 + 512 + lane * 16, wsrc[p] + 512);
+      wsrc[p] += 1024;
+      if (lane < NG * 2) cp_async16(sb + SG::kW + p * 128 + lane * 16, ssrc[p] + lane * 16);
+      if (!AWQ && lane < NG * 2) cp_async16(sb + SG::kW + SG::kS + p * 128 + lane * 16, zsrc[p] + lane * 16);
+      ssrc[p] += NG * 32;
+      if (!AWQ) zsrc[p] += NG * 32;
+    }
+  };
+  auto issue_b = [&](int stage) {
+    unsigned char* sb = wbase + stage * SG::kBytes;
+    if (bval) {
+#pragma unroll
+      for (int b = 0; b < 4; ++b)
+        cp_async16(sb + SG::kW + SG::kS + SG::kZ + b * 512 + lane * 16, bsrc + b * 64);
+    }
+    bsrc += 256;
+  };
+  bool copying = true;
+  // one step of copies; enters the prefetched unit when the current one is done
+  auto issue_step = [&](int stage) {
+    if (!copying) return;
+    if (is == nsteps) {
+      if (pu >= nunits) {
+        copying = false;
+        return;
+      }
+      enter();
+      prefetch();
+    }
+    issue_w(stage);
+    issue_b(stage);
+    ++is;
+  };
+
+  prefetch();
+  if (pu >= nunits) return;  // no unit for this warp (whole warp)
+  enter();
+  prefetch();
+#pragma unroll
+  for (int d = 0; d < kStagesW - 1; ++d) issue_w(d);  // nsteps >= kStagesW - 1 (K >= 256)
+  if (MODE != MODE_GATE_UP) {
+    grid_dep_wait();
+    grid_dep_release();
+  }
+#pragma unroll
+  for (int d = 0; d < kStagesW - 1; ++d) {
+    issue_b(d);
+    ++is;
+    cp_async_commit();
+  }
+
+  const uint32_t ones[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};
+  const float bias = AWQ ? (float)(128 + a.zp) : 128.f;
+  float acc[NP][4], tmp[NP][2][4], xs[2][4];
+#pragma unroll
+  for (int p = 0; p < NP; ++p)
+#pragma unroll
+    for (int r = 0; r < 4; ++r) acc[p][r] = tmp[p][0][r] = tmp[p][1][r] = 0.f;
+#pragma unroll
+  for (int r = 0; r < 4; ++r) xs[0][r] = xs[1][r] = 0.f;
+
+  int c_row0 = n_row0, c_nrows = n_nrows, c_rt = n_rt, done = 0, cs = 0;
+  for (int i = 0;; ++i) {
+    issue_step((i + kStagesW - 1) % kStagesW);
+    cp_async_commit();
+    cp_async_wait<kStagesW - 1>();
+    __syncwarp();  // the scales are copied by lanes 0..2*NG-1 and read by all
+    const unsigned char* sb = wbase + (i % kStagesW) * SG::kBytes;
+    uint4 wq[NP][2], bv[4];
+    float sc[NP][NG][2], zz[NP][NG][2];
+#pragma unroll
+    for (int p = 0; p < NP; ++p) {
+      wq[p][0] = *reinterpret_cast<const uint4*>(sb + p * 1024 + lane * 16);
+      wq[p][1] = *reinterpret_cast<const uint4*>(sb + p * 1024 + 512 + lane * 16);
+#pragma unroll
+      for (int q = 0; q < NG; ++q) {
+        const __half* sp = reinterpret_cast<const __half*>(sb + SG::kW + p * 128) + q * 16;
+        sc[p][q][0] = __half2float(sp[g]);
+        sc[p][q][1] = __half2float(sp[g + 8]);
+        if (!AWQ) {
+          const __half* zp = reinterpret_cast<const __half*>(sb + SG::kW + SG::kS + p * 128) + q * 16;
+          zz[p][q][0] = __half2float(zp[g]);
+          zz[p][q][1] = __half2float(zp[g + 8]);
+        }
+      }
+    }
+    const bool cval = g < c_nrows;
+#pragma unroll
+    for (int b = 0; b < 4; ++b)
+      bv[b] = cval ? *reinterpret_cast<const uint4*>(sb + SG::kW + SG::kS + SG::kZ + b * 512 + lane * 16)
+                   : make_uint4(0, 0, 0, 0);
+    __syncwarp();  // every lane holds its operands before any lane refills this stage
+
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {  // 32-wide block b of the step
+#pragma unroll
+      for (int kt = 0; kt < 2; ++kt) {
+        mma_bf16(xs[kt], ones, kt ? bv[b].z : bv[b].x, kt ? bv[b].w : bv[b].y);
+#pragma unroll
+        for (int p = 0; p < NP; ++p) {
+          const uint4& q4 = wq[p][b >> 1];
+          const int wi = (b & 1) * 2 + kt;
+          const uint32_t wd = wi == 0 ? q4.x : wi == 1 ? q4.y : wi == 2 ? q4.z : q4.w;
+          uint32_t af[4];
+          raw_word(wd, af);
+          mma_bf16(tmp[p][kt], af, kt ? bv[b].z : bv[b].x, kt ? bv[b].w : bv[b].y);
+        }
+      }
+      if ((b + 1) % GSB == 0) {  // group end
+        const int q = b / GSB;
+#pragma unroll
+        for (int r = 0; r < 4; ++r) xs[0][r] += xs[1][r];
+#pragma unroll
+        for (int p = 0; p < NP; ++p)
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const float pr = tmp[p][0][r] + tmp[p][1][r];
+            const float v = __fmaf_rn(-bias, xs[0][r], pr);  // sum x*(q - zp)
+            acc[p][r] = __fmaf_rn(v, sc[p][q][r >> 1], acc[p][r]);
+            if (!AWQ) acc[p][r] = __fmaf_rn(zz[p][q][r >> 1], xs[0][r], acc[p][r]);
+            tmp[p][0][r] = tmp[p][1][r] = 0.f;
+          }
+#pragma unroll
+        for (int r = 0; r < 4; ++r) xs[0][r] = xs[1][r] = 0.f;
+      }
+    }
+
+    if (++cs < nsteps) continue;
+    // unit done: C fragment (row g / g+8, col 2t / 2t+1) -> outputs
+    const int m0 = c_rt * 16 + g, m1 = m0 + 8;
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int col = 2 * t + (r & 1);
+      const int m = (r < 2) ? m0 : m1;
+      if (col < c_nrows && m < a.M) {
+        const size_t o = (size_t)(c_row0 + col) * a.ldo + m;
+        float v = acc[0][r];
+        if (!isfinite(v)) v = 0.f;  // non-finite -> 0, as every reference GEMV does
+        if (MODE == MODE_GATE_UP) {
+          float uu = acc[NP - 1][r];
+          if (!isfinite(uu)) uu = 0.f;
+          reinterpret_cast<__nv_bfloat16*>(a.out)[o] = __float2bfloat16_rn(silu_mul(v, uu));
+        } else {
+          reinterpret_cast<float*>(a.out)[o] = v;
+        }
+      }
+    }
+#pragma unroll
+    for (int p = 0; p < NP; ++p)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) acc[p][r] = 0.f;
+    cs = 0;
+    // the copies run kStagesW - 1 steps ahead and units have >= kStagesW - 1
+    // steps, so the next unit (if any) has been entered by now
+    if (++done == entered) break;
+    c_row0 = n_row0;
+    c_nrows = n_nrows;
+    c_rt = n_rt;
+  }
+  cp_async_wait<0>();
+}
+
 template <int MODE, int NT, int GSB, bool AWQ>
 static void launch_mma_k(const GemmArgs& a, dim3 grid, int ks, cudaStream_t st) {
   constexpr int NP = MODE == MODE_GATE_UP ? 2 : 1;
@@ -412,7 +684,58 @@ static void launch_mma_k(const GemmArgs& a, dim3 grid, int ks, cudaStream_t st) 
                          (int)smem);
     attr = true;
   }
-  k_int4_mma<MODE, NT, GSB, AWQ><<<grid, kWarps * 32, smem, st>>>(a, ks);
+  launch_pdl(k_int4_mma<MODE, NT, GSB, AWQ>, grid, dim3(kWarps * 32), smem, st, a, ks);
+}
+
+// Persistent grid: as many 4-warp CTAs as fit on the SMs at once.
+template <int MODE, int GSB, bool AWQ>
+static int mma_p_grid() {
+  constexpr int NP = MODE == MODE_GATE_UP ? 2 : 1;
+  const size_t smem = (size_t)kWarps * kStagesW * WStage<NP, 1, AWQ>::kBytes;
+  static int grid = 0;  // per template instance (one device per process in practice)
+  if (!grid) {
+    cudaFuncSetAttribute(k_int4_mma_p<MODE, GSB, AWQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    int per_sm = 0, dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_int4_mma_p<MODE, GSB, AWQ>, kWarps * 32, smem);
+    grid = std::max(1, per_sm) * std::max(1, sms);
+  }
+  return grid;
+}
+
+template <int MODE, int GSB, bool AWQ>
+static void launch_mma_pk(const GemmArgs& a, cudaStream_t st) {
+  constexpr int NP = MODE == MODE_GATE_UP ? 2 : 1;
+  const size_t smem = (size_t)kWarps * kStagesW * WStage<NP, 1, AWQ>::kBytes;
+  launch_pdl(k_int4_mma_p<MODE, GSB, AWQ>, dim3(mma_p_grid<MODE, GSB, AWQ>()), dim3(kWarps * 32), smem, st, a);
+}
+
+template <int MODE, bool AWQ>
+static int mma_p_grid_gs(int gs) {
+  return gs == 32 ? mma_p_grid<MODE, 1, AWQ>() : (gs == 64 ? mma_p_grid<MODE, 2, AWQ>() : mma_p_grid<MODE, 4, AWQ>());
+}
+static long mma_p_resident_warps(bool gate_up, int gs, int awq) {
+  const int grid = gate_up ? (awq ? mma_p_grid_gs<MODE_GATE_UP, true>(gs) : mma_p_grid_gs<MODE_GATE_UP, false>(gs))
+                           : (awq ? mma_p_grid_gs<MODE_PLAIN_F32, true>(gs) : mma_p_grid_gs<MODE_PLAIN_F32, false>(gs));
+  return (long)grid * kWarps;
+}
+
+template <int MODE>
+static void launch_mma_p(const GemmArgs& a, int awq, cudaStream_t st) {
+  if (awq) {
+    switch (a.gs) {
+      case 32: launch_mma_pk<MODE, 1, true>(a, st); break;
+      case 64: launch_mma_pk<MODE, 2, true>(a, st); break;
+      default: launch_mma_pk<MODE, 4, true>(a, st); break;
+    }
+  } else {
+    switch (a.gs) {
+      case 32: launch_mma_pk<MODE, 1, false>(a, st); break;
+      case 64: launch_mma_pk<MODE, 2, false>(a, st); break;
+      default: launch_mma_pk<MODE, 4, false>(a, st); break;
+    }
+  }
 }
 
 template <int MODE, int NT, bool AWQ>
@@ -618,8 +941,10 @@ __global__ void __launch_bounds__(128) k_int4_cc(GemmArgs a, int awq) {
 // order of the reference's combine (qwen3_6_moe_int4_model.cpp:213, :372).
 template <typename OT>
 __global__ void k_combine(const float* __restrict__ d, const int* __restrict__ inverse,
-                          const float* __restrict__ w, int T, int kk, int H, OT* __restrict__ y,
-                          int skip_tiny) {
+                          const float* __restrict__ w, int T, int kk, int H, OT* y, int skip_tiny,
+                          const __nv_bfloat16* res) {
+  grid_dep_wait();
+  grid_dep_release();
   const int t = blockIdx.y;
   const int h = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
   if (t >= T || h >= H) return;
@@ -653,7 +978,9 @@ __global__ void k_combine(const float* __restrict__ d, const int* __restrict__ i
       acc.w = __fmaf_rn(wj[u], v[u].w, acc.w);
     }
   }
-  const float* ap = &acc.x;
+  float* ap = &acc.x;
+  if (res)  // residual stream: y = r + sum (one fp32 add; res may alias y, read before written)
+    for (int i = 0; i < 4 && h + i < H; ++i) ap[i] = __fadd_rn(__bfloat162float(res[(size_t)t * H + h + i]), ap[i]);
   for (int i = 0; i < 4 && h + i < H; ++i) {
     if constexpr (sizeof(OT) == 2)
       y[(size_t)t * H + h + i] = __float2bfloat16_rn(ap[i]);
@@ -714,19 +1041,30 @@ cudaError_t launch_dequant(const ProjDev& P, int M, int K, int gs, int awq, int 
 }
 
 cudaError_t launch_gemm(int mode, int path, const GemmArgs& a, int max_work, int awq,
-                        int ntiles, cudaStream_t st) {
+                        int ntiles, cudaStream_t st, int n_groups) {
   if (max_work <= 0) return cudaSuccess;
   const int Mt = (a.M + 15) / 16;
   dim3 grid((Mt + 3) / 4, max_work);
   if (path == 0) {
     // K split: enough warps to cover the SMs when the expected work is small
     const long units = (long)Mt * max_work;
+    const long units_est = (long)Mt * std::min(max_work, n_groups > 0 ? n_groups : max_work);
     const int nsteps = a.K / 128;
     const int ks = nsteps >= 8 && units < 148 * 16 ? 4 : (nsteps >= 8 ? 2 : 1);
-    if (mode == MODE_GATE_UP)
+    // decode-size items: the persistent kernel when the expected units (items ~
+    // min(max_work, distinct experts) x row tiles) keep 1.5x its resident warps
+    // busy; below that the K-split launch has more warps in flight
+    if (ntiles <= 1 && a.ctr && nsteps >= kStagesW - 1 &&
+        2L * units_est >= 3L * mma_p_resident_warps(mode == MODE_GATE_UP, a.gs, awq)) {
+      if (mode == MODE_GATE_UP)
+        launch_mma_p<MODE_GATE_UP>(a, awq, st);
+      else
+        launch_mma_p<MODE_PLAIN_F32>(a, awq, st);
+    } else if (mode == MODE_GATE_UP) {
       launch_mma<MODE_GATE_UP>(a, max_work, ntiles, ks, awq, st);
-    else
+    } else {
       launch_mma<MODE_PLAIN_F32>(a, max_work, ntiles, ks, awq, st);
+    }
   } else if (path == 1) {
     if (mode == MODE_GATE_UP)
       k_int4_cc<MODE_GATE_UP, float, 4><<<grid, 128, 0, st>>>(a, awq);
@@ -775,16 +1113,15 @@ cudaError_t launch_combine_ep(const void* ret, const int* inverse, const float* 
 }
 
 cudaError_t launch_combine(const float* d, const int* inverse, const float* w, int T, int kk, int H,
-                           void* y, int y_bf16, int skip_tiny, cudaStream_t st) {
+                           void* y, int y_bf16, int skip_tiny, cudaStream_t st, const void* res) {
   if (T <= 0) return cudaSuccess;
   const int threads = 128;
   dim3 grid(((H + 3) / 4 + threads - 1) / threads, T);
   if (y_bf16)
-    k_combine<__nv_bfloat16><<<grid, threads, 0, st>>>(d, inverse, w, T, kk, H,
-                                                      (__nv_bfloat16*)y, skip_tiny);
-  else
-    k_combine<float><<<grid, threads, 0, st>>>(d, inverse, w, T, kk, H, (float*)y, skip_tiny);
-  return cudaGetLastError();
+    return launch_pdl(k_combine<__nv_bfloat16>, grid, dim3(threads), 0, st, d, inverse, w, T, kk, H,
+                      (__nv_bfloat16*)y, skip_tiny, (const __nv_bfloat16*)res);
+  return launch_pdl(k_combine<float>, grid, dim3(threads), 0, st, d, inverse, w, T, kk, H, (float*)y, skip_tiny,
+                    (const __nv_bfloat16*)res);
 }
 
 cudaError_t launch_quant_awq_sym(const __nv_bfloat16* W, int M, int K, int gs, int bf16_scale,

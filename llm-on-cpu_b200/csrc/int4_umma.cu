@@ -328,6 +328,8 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a, const __
   __shared__ volatile int abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  grid_dep_wait();
+  grid_dep_release();
   const int nmt = a.M / kRowsTile;
   const int ntiles = *a.n_work * nmt;
   if ((int)blockIdx.x >= ntiles) return;  // uniform over the CTA
@@ -636,6 +638,8 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a, const __
 __global__ void __launch_bounds__(256) k_gather_rows(const uint4* __restrict__ X, int H8,
                                                      const int* __restrict__ sorted, int kk, int n,
                                                      uint4* __restrict__ Xs) {
+  grid_dep_wait();
+  grid_dep_release();
   const int p = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (p >= n) return;
   const uint4* src = X + (size_t)(sorted[p] / kk) * H8;
@@ -646,9 +650,8 @@ __global__ void __launch_bounds__(256) k_gather_rows(const uint4* __restrict__ X
 cudaError_t launch_gather_rows(const void* X, int H, const int* sorted, int kk, int n, void* Xs,
                                cudaStream_t st) {
   if (n <= 0) return cudaSuccess;
-  k_gather_rows<<<(n + 7) / 8, 256, 0, st>>>(reinterpret_cast<const uint4*>(X), H / 8, sorted, kk, n,
-                                             reinterpret_cast<uint4*>(Xs));
-  return cudaGetLastError();
+  return launch_pdl(k_gather_rows, dim3((n + 7) / 8), dim3(256), 0, st, reinterpret_cast<const uint4*>(X), H / 8,
+                    sorted, kk, n, reinterpret_cast<uint4*>(Xs));
 }
 
 namespace {
@@ -746,8 +749,7 @@ static cudaError_t launch_u(const GemmArgs& a, int max_work, int b_rows, cudaStr
   const int nmt = a.M / (MODE == MODE_GATE_UP ? 64 : 128);
   const long long tiles = (long long)max_work * nmt;
   const int grid = (int)std::min<long long>(tiles, sm_count());
-  k_int4_umma<MODE, GSB, AWQ><<<grid, kUThreads, smem, st>>>(a, tmB);
-  return cudaGetLastError();
+  return launch_pdl(k_int4_umma<MODE, GSB, AWQ>, dim3(grid), dim3(kUThreads), (size_t)smem, st, a, tmB);
 }
 
 template <int MODE, bool AWQ>

@@ -28,10 +28,11 @@ struct PermArgs {
   WorkItem* work;   // [max_work]
   int* n_work;
   int* n_active;
-  int* err;         // device error word, cleared here for the kernels that follow
+  int* err;         // device error word + kGemmCounters unit counters, all cleared here for the kernels that follow
   int chunk;        // rows per work item (8, 16 or 32)
 };
 
+constexpr int kGemmCounters = 2;  // err[1], err[2]: unit counters of the gate/up and down GEMMs
 constexpr int kPermThreads = 1024;
 constexpr int kPermWarps = kPermThreads / 32;
 constexpr int kMaxExpPerm = 512;  // experts (incl. shared) the permutation CTA handles
@@ -40,6 +41,9 @@ cudaError_t launch_router_logits(const void* X, bool x_is_f32, const uint16_t* W
                                  int H, float* logits, cudaStream_t st);
 cudaError_t launch_topk(const TopkArgs& a, cudaStream_t st);
 cudaError_t launch_permute(const PermArgs& a, cudaStream_t st);
+// top-k and permutation in one CTA (decode-size T; pa.ids must be ta.ids)
+constexpr int kFusedRouteMaxT = 16;
+cudaError_t launch_topk_permute(const TopkArgs& ta, const PermArgs& pa, cudaStream_t st);
 // expert parallelism (owner of expert e = rank e % world, local id e / world)
 cudaError_t launch_ep_keys(const int* ids, int n, int world, int e_loc, int* key, cudaStream_t st);
 cudaError_t launch_ep_meta(const int* offsets, const int* sorted, const int* key, int n, int world, int e_loc,
@@ -77,14 +81,16 @@ struct GemmArgs {
   int out_bf16;           // GATE_UP output type (cc kernel): 1 bf16, 0 fp32
   int* err;               // device error word: bit 0 = a bounded wait gave up (may be null)
   const void* wmaps;      // tcgen05 path: per-expert TMA maps of the weights (build_umma_weight_maps)
+  int* ctr;               // persistent decode kernel: unit counter, zeroed by the permutation (or null)
 };
 
 cudaError_t launch_repack(const RepackArgs& a, cudaStream_t st);
 cudaError_t launch_dequant(const ProjDev& P, int M, int K, int gs, int awq, int zp, float* out,
                            cudaStream_t st);
 // path: 0 tensor-core (AWQ, bf16 B), 1 CUDA-core fp32 B, 2 CUDA-core bf16 B
+// n_groups: experts (groups) the rows can reach, for the decode kernel choice (0: unknown)
 cudaError_t launch_gemm(int mode, int path, const GemmArgs& a, int max_work, int awq, int ntiles,
-                        cudaStream_t st);
+                        cudaStream_t st, int n_groups = 0);
 // int4_tma.cu: the same grouped GEMM fed by cp.async.bulk through a shared-
 // memory stage ring (decode-size items, K % 128 == 0, gs in {32, 64, 128}).
 cudaError_t launch_gemm_tma(int mode, const GemmArgs& a, int max_work, int awq, cudaStream_t st);
@@ -104,8 +110,10 @@ bool build_umma_weight_maps(const ExpertDev* host_table, int n_exp, int inter, i
 // Xs[p, :] = X[sorted[p] / kk, :] for p < n (bf16 rows of H elements, H % 8 == 0).
 cudaError_t launch_gather_rows(const void* X, int H, const int* sorted, int kk, int n, void* Xs,
                                cudaStream_t st);
+// y[t] (+)= sum_j w[t,j] * d[inverse[t*kk+j]]; res (bf16 [T,H], may alias y):
+// y = res + sum, the residual stream of the caller's decoder layer.
 cudaError_t launch_combine(const float* d, const int* inverse, const float* w, int T, int kk, int H,
-                           void* y, int y_bf16, int skip_tiny, cudaStream_t st);
+                           void* y, int y_bf16, int skip_tiny, cudaStream_t st, const void* res = nullptr);
 cudaError_t launch_quant_awq_sym(const __nv_bfloat16* W, int M, int K, int gs, int bf16_scale,
                                  uint8_t* q, __half* sc, cudaStream_t st);
 

@@ -62,6 +62,8 @@ template <typename XT, int TW, int EW>
 __global__ void __launch_bounds__(256) k_router_logits(const XT* __restrict__ X,
                                                        const uint16_t* __restrict__ Wr, int T,
                                                        int E, int H, float* __restrict__ logits) {
+  grid_dep_wait();
+  grid_dep_release();
   const int lane = threadIdx.x & 31;
   const int sub = lane & 7;  // owns chains 4*sub .. 4*sub+3
   const int group = (blockIdx.x * blockDim.x + threadIdx.x) >> 3;
@@ -170,6 +172,8 @@ __global__ void __launch_bounds__(RouterTile<TT, EE, WT, WE>::kThreads, 1)
                    float* __restrict__ logits) {
   using RT = RouterTile<TT, EE, WT, WE>;
   extern __shared__ float rsm[];
+  grid_dep_wait();
+  grid_dep_release();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tg = warp % WT, eg = warp / WT;
   const int t0 = blockIdx.y * RT::kRowsX, e0 = blockIdx.x * RT::kRowsW;
@@ -275,88 +279,122 @@ static cudaError_t launch_router_tiled(const __nv_bfloat16* X, const uint16_t* W
     attr = true;
   }
   const dim3 grid((E + RT::kRowsW - 1) / RT::kRowsW, (T + RT::kRowsX - 1) / RT::kRowsX);
-  k_router_tiled<TT, EE, WT, WE><<<grid, RT::kThreads, RT::kSmem, st>>>(X, Wr, T, E, H, logits);
-  return cudaGetLastError();
+  return launch_pdl(k_router_tiled<TT, EE, WT, WE>, grid, dim3(RT::kThreads), RT::kSmem, st, X, Wr, T, E, H, logits);
 }
 
 // --------------------------------------------------------------- top-k
 
 
-// One warp per token.  Dynamic smem: 8 warps x E floats (keys) + E floats (probs/scores).
-__global__ void __launch_bounds__(256) k_topk(TopkArgs a) {
-  extern __shared__ float sm[];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t = blockIdx.x * 8 + warp;
-  if (t >= a.T) return;
-  float* key = sm + (size_t)warp * 2 * a.E;
-  float* val = key + a.E;  // softmax: p (float); sigmoid: s
-  const float* lg = a.logits + (size_t)t * a.E;
+// Order-preserving map of a non-NaN float key to uint32 (larger key ->
+// larger code; -0 is folded into +0 first, so equal keys get equal codes).
+__device__ __forceinline__ uint32_t key_code(float v) {
+  const uint32_t u = __float_as_uint(v + 0.f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
 
+// Top-k of one token by one warp (E <= 32 * kTopkSlots).  Lane l holds the
+// keys and values of experts l, l + 32, ... in registers; a round takes the
+// warp's largest key (smaller id on ties) with two warp reductions, and the
+// chosen ids and values stay in registers until the weights are written.
+constexpr int kTopkSlots = 16;  // E <= 512
+template <int Q>  // slots per lane: E <= 32 * Q
+__device__ __forceinline__ void topk_token_q(const TopkArgs& a, int t, int lane) {
+  const float* lg = a.logits + (size_t)t * a.E;
+  float key[Q], val[Q];
   if (a.router == 0) {
+    // keys = logits; probabilities exp(l - max) (their rounding only reaches
+    // the weights, which are compared with a tolerance, never the ids)
     float m = -INFINITY;
-    for (int e = lane; e < a.E; e += 32) {
-      const float l = lg[e];
-      key[e] = l;
-      m = fmaxf(m, l);
+#pragma unroll
+    for (int q = 0; q < Q; ++q) {
+      const int e = lane + 32 * q;
+      key[q] = e < a.E ? lg[e] : -INFINITY;
+      m = fmaxf(m, key[q]);
     }
-    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    for (int e = lane; e < a.E; e += 32) {
-      // exp of the fp32 difference, correctly rounded to fp32 via double
-      val[e] = (float)exp((double)(lg[e] - m));
-    }
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 8));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+#pragma unroll
+    for (int q = 0; q < Q; ++q) val[q] = lane + 32 * q < a.E ? expf(key[q] - m) : 0.f;
   } else {
-    for (int e = lane; e < a.E; e += 32) {
-      const float s = (float)(1.0 / (1.0 + exp(-(double)lg[e])));
-      val[e] = s;
-      const float kv = s + a.bias[e];
-      key[e] = kv == kv ? kv : -FLT_MAX;  // a NaN bias must still leave a valid id
+    // s = sigmoid(l) in double rounded to fp32 (part of the selection key)
+#pragma unroll
+    for (int q = 0; q < Q; ++q) {
+      const int e = lane + 32 * q;
+      if (e < a.E) {
+        const float sg = (float)(1.0 / (1.0 + exp(-(double)lg[e])));
+        val[q] = sg;
+        const float kv = sg + a.bias[e];
+        key[q] = kv == kv ? kv : -FLT_MAX;  // a NaN bias must still leave a valid id
+      } else {
+        val[q] = 0.f;
+        key[q] = -INFINITY;
+      }
     }
   }
-  __syncwarp();
 
   // k rounds of argmax over keys (ties -> smaller id); selected keys -> -inf.
-  int* ids = a.ids + (size_t)t * a.kk;
-  float* w = a.weights + (size_t)t * a.kk;
+  // Padding slots (e >= E) hold -inf with ids above every real id, so a tie at
+  // -inf still resolves to a real expert.
+  int my_id = 0;
+  float my_val = 0.f;
   for (int j = 0; j < a.k; ++j) {
-    float bk = -INFINITY;
-    int bi = 0x7fffffff;
-    for (int e = lane; e < a.E; e += 32) {
-      const float v = key[e];
-      if (v > bk || (v == bk && e < bi)) {
-        bk = v;
-        bi = e;
+    uint32_t bc = key_code(key[0]);
+    int bq = 0;
+#pragma unroll
+    for (int q = 1; q < Q; ++q) {
+      const uint32_t c = key_code(key[q]);
+      if (c > bc) {
+        bc = c;
+        bq = q;
       }
     }
-    for (int o = 16; o; o >>= 1) {
-      const float ok = __shfl_xor_sync(0xffffffffu, bk, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ok > bk || (ok == bk && oi < bi)) {
-        bk = ok;
-        bi = oi;
+    const uint32_t mc = __reduce_max_sync(0xffffffffu, bc);
+    const int bi = (int)__reduce_min_sync(0xffffffffu, bc == mc ? (uint32_t)(lane + 32 * bq) : 0x7fffffffu);
+    const int oq = bi >> 5, ol = bi & 31;
+    float v = 0.f;
+#pragma unroll
+    for (int q = 0; q < Q; ++q)
+      if (q == oq) {
+        v = val[q];
+        if (lane == ol) key[q] = -INFINITY;
+      }
+    v = __shfl_sync(0xffffffffu, v, ol);
+    if (lane == (j & 31)) {
+      if (j < 32) {
+        my_id = bi;
+        my_val = v;
       }
     }
-    // keys are never NaN (non-finite logits were zeroed, NaN sums mapped to
-    // -FLT_MAX), so a taken key set to -inf is never chosen again while k <= E
-    if (lane == 0) {
-      ids[j] = bi;
-      key[bi] = -INFINITY;
+    if (j >= 32 && lane == (j & 31)) {  // k > 32: slots 32..63 go out now
+      a.ids[(size_t)t * a.kk + j] = bi;
+      a.weights[(size_t)t * a.kk + j] = v;  // finished below
     }
-    __syncwarp();
   }
 
   // weights: lane l computes w[j] for j = l, l+32 (k <= 64); sums are warp
   // reductions in double (the reference sums sequentially in double; the two
   // agree except for double roundings far below fp32 resolution)
+  int* ids = a.ids + (size_t)t * a.kk;
+  float* w = a.weights + (size_t)t * a.kk;
+  float sel[2];
+  sel[0] = my_val;
+  sel[1] = lane + 32 < a.k ? w[lane + 32] : 0.f;
+  __syncwarp();
+  if (lane < a.k) ids[lane] = my_id;
   if (a.router == 0) {
     double s = 0.0;
-    for (int e = lane; e < a.E; e += 32) s += (double)val[e];
+#pragma unroll
+    for (int q = 0; q < Q; ++q) s += (double)val[q];
     for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     float p[2];
     double ws = 0.0;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int j = lane + 32 * h;
-      p[h] = j < a.k ? (float)((double)val[ids[j]] / s) : 0.f;  // the reference's fp32 prob
+      p[h] = j < a.k ? (float)((double)sel[h] / s) : 0.f;  // the reference's fp32 prob
       ws += (double)p[h];
     }
     for (int o = 16; o; o >>= 1) ws += __shfl_xor_sync(0xffffffffu, ws, o);
@@ -369,7 +407,7 @@ __global__ void __launch_bounds__(256) k_topk(TopkArgs a) {
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int j = lane + 32 * h;
-      sv[h] = j < a.k ? (double)val[ids[j]] : 0.0;
+      sv[h] = j < a.k ? (double)sel[h] : 0.0;
       ws += sv[h];
     }
     for (int o = 16; o; o >>= 1) ws += __shfl_xor_sync(0xffffffffu, ws, o);
@@ -384,12 +422,28 @@ __global__ void __launch_bounds__(256) k_topk(TopkArgs a) {
   }
 }
 
+__device__ __forceinline__ void topk_token(const TopkArgs& a, int t, int lane) {
+  if (a.E <= 128) topk_token_q<4>(a, t, lane);
+  else if (a.E <= 256) topk_token_q<8>(a, t, lane);
+  else if (a.E <= 384) topk_token_q<12>(a, t, lane);
+  else topk_token_q<16>(a, t, lane);
+}
+
+// One warp per token.
+__global__ void __launch_bounds__(256) k_topk(TopkArgs a) {
+  grid_dep_wait();
+  grid_dep_release();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + warp;
+  if (t >= a.T) return;
+  topk_token(a, t, lane);
+}
+
 // ----------------------------------------------------------- permutation
 
-// Single CTA.  smem: cnt[kPermWarps][n_exp] ints.
-__global__ void __launch_bounds__(kPermThreads) k_permute(PermArgs a) {
-  extern __shared__ int psm[];
-  int* cnt = psm;  // [warps][n_exp]: counts, then running positions
+// One CTA of kPermThreads threads.  cnt: kPermWarps x n_exp ints of shared
+// memory (counts, then running positions).
+__device__ __forceinline__ void permute_block(const PermArgs& a, int* cnt) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int i = threadIdx.x; i < kPermWarps * a.n_exp; i += kPermThreads) cnt[i] = 0;
   __syncthreads();
@@ -462,7 +516,8 @@ __global__ void __launch_bounds__(kPermThreads) k_permute(PermArgs a) {
     }
   }
   if (threadIdx.x == kPermThreads - 1) {
-    if (a.err) *a.err = 0;
+    if (a.err)
+      for (int i = 0; i <= kGemmCounters; ++i) a.err[i] = 0;
     a.offsets[a.n_exp] = w1[kPermWarps - 1];
     *a.n_work = w2[kPermWarps - 1];
     *a.n_active = w3[kPermWarps - 1];
@@ -488,6 +543,26 @@ __global__ void __launch_bounds__(kPermThreads) k_permute(PermArgs a) {
   }
 }
 
+__global__ void __launch_bounds__(kPermThreads) k_permute(PermArgs a) {
+  extern __shared__ int psm[];
+  grid_dep_wait();
+  grid_dep_release();
+  permute_block(a, psm);
+}
+
+// Decode-size batches: top-k of every token (warp w takes tokens w, w + 32,
+// ...) and the permutation in one CTA, saving a launch and a pass over the
+// ids.  Shared memory: kPermWarps x n_exp ints (the permutation's counts).
+__global__ void __launch_bounds__(kPermThreads) k_topk_permute(TopkArgs ta, PermArgs pa) {
+  extern __shared__ int fsm[];
+  grid_dep_wait();
+  grid_dep_release();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int t = warp; t < ta.T; t += kPermWarps) topk_token(ta, t, lane);
+  __syncthreads();  // the ids written above are visible to the whole CTA
+  permute_block(pa, fsm);
+}
+
 // ---------------------------------------------------------------- launch
 
 cudaError_t launch_router_logits(const void* X, bool x_is_f32, const uint16_t* Wr, int T, int E,
@@ -511,44 +586,41 @@ cudaError_t launch_router_logits(const void* X, bool x_is_f32, const uint16_t* W
     const long groups = (long)T * E;
     const int blocks = (int)((groups * 8 + threads - 1) / threads);
     if (x_is_f32)
-      k_router_logits<float, 1, 1><<<blocks, threads, 0, st>>>((const float*)X, Wr, T, E, H, logits);
+      return launch_pdl(k_router_logits<float, 1, 1>, dim3(blocks), dim3(threads), 0, st, (const float*)X, Wr, T, E, H, logits);
     else
-      k_router_logits<__nv_bfloat16, 1, 1>
-          <<<blocks, threads, 0, st>>>((const __nv_bfloat16*)X, Wr, T, E, H, logits);
+      return launch_pdl(k_router_logits<__nv_bfloat16, 1, 1>, dim3(blocks), dim3(threads), 0, st, (const __nv_bfloat16*)X, Wr, T, E, H, logits);
   } else if (T <= 256) {
     constexpr int TW = 2, EW = 2;
     const long groups = (long)((T + TW - 1) / TW) * ((E + EW - 1) / EW);
     const int blocks = (int)((groups * 8 + threads - 1) / threads);
     if (x_is_f32)
-      k_router_logits<float, TW, EW>
-          <<<blocks, threads, 0, st>>>((const float*)X, Wr, T, E, H, logits);
+      return launch_pdl(k_router_logits<float, TW, EW>, dim3(blocks), dim3(threads), 0, st, (const float*)X, Wr, T, E, H, logits);
     else
-      k_router_logits<__nv_bfloat16, TW, EW>
-          <<<blocks, threads, 0, st>>>((const __nv_bfloat16*)X, Wr, T, E, H, logits);
+      return launch_pdl(k_router_logits<__nv_bfloat16, TW, EW>, dim3(blocks), dim3(threads), 0, st, (const __nv_bfloat16*)X, Wr, T, E, H, logits);
   } else {
     constexpr int TW = 4, EW = 4;
     const long groups = (long)((T + TW - 1) / TW) * ((E + EW - 1) / EW);
     const int blocks = (int)((groups * 8 + threads - 1) / threads);
     if (x_is_f32)
-      k_router_logits<float, TW, EW>
-          <<<blocks, threads, 0, st>>>((const float*)X, Wr, T, E, H, logits);
+      return launch_pdl(k_router_logits<float, TW, EW>, dim3(blocks), dim3(threads), 0, st, (const float*)X, Wr, T, E, H, logits);
     else
-      k_router_logits<__nv_bfloat16, TW, EW>
-          <<<blocks, threads, 0, st>>>((const __nv_bfloat16*)X, Wr, T, E, H, logits);
+      return launch_pdl(k_router_logits<__nv_bfloat16, TW, EW>, dim3(blocks), dim3(threads), 0, st, (const __nv_bfloat16*)X, Wr, T, E, H, logits);
   }
   return cudaGetLastError();
 }
 
 cudaError_t launch_topk(const TopkArgs& a, cudaStream_t st) {
   if (a.T <= 0) return cudaSuccess;
-  const size_t smem = (size_t)8 * 2 * a.E * sizeof(float);
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(k_topk, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
-    if (e != cudaSuccess) return e;
-  }
-  k_topk<<<(a.T + 7) / 8, 256, smem, st>>>(a);
-  return cudaGetLastError();
+  if (a.E > 32 * kTopkSlots || a.k > 64) return cudaErrorInvalidValue;
+  return launch_pdl(k_topk, dim3((a.T + 7) / 8), dim3(256), 0, st, a);
+}
+
+cudaError_t launch_topk_permute(const TopkArgs& ta, const PermArgs& pa, cudaStream_t st) {
+  if (ta.E > 32 * kTopkSlots || ta.k > 64) return cudaErrorInvalidValue;
+  const size_t smem = (size_t)kPermWarps * pa.n_exp * sizeof(int);
+  cudaError_t e = cudaFuncSetAttribute(k_topk_permute, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(k_topk_permute, dim3(1), dim3(kPermThreads), smem, st, ta, pa);
 }
 
 cudaError_t launch_permute(const PermArgs& a, cudaStream_t st) {
@@ -556,8 +628,7 @@ cudaError_t launch_permute(const PermArgs& a, cudaStream_t st) {
   cudaError_t e = cudaFuncSetAttribute(k_permute, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem);
   if (e != cudaSuccess) return e;
-  k_permute<<<1, kPermThreads, smem, st>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(k_permute, dim3(1), dim3(kPermThreads), smem, st, a);
 }
 
 // ------------------------------------------------------ expert parallelism

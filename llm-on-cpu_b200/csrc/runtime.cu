@@ -399,7 +399,7 @@ WsLayout ws_layout_g(const llmoc_moe_layer* L, int T, int kk, int n_perm, int ch
   w.work = take((size_t)std::max(1, w.max_work) * sizeof(WorkItem));
   w.n_work = take(4);
   w.n_active = take(4);
-  w.err = take(4);
+  w.err = take(4 * (1 + kGemmCounters));  // error word, then the GEMM unit counters
   w.mid = take(n * L->d.inter * 2);
   w.partial = take(n * L->d.hidden * 4);
   w.xs = use_umma_c(L, chunk) ? take(n * L->d.hidden * 2) : 0;  // rows in expert-sorted order
@@ -602,8 +602,7 @@ struct StageEvents {
   }
 };
 
-llmoc_status run_permute(const int* ids, int n, int n_perm, int chunk, const WsLayout& w, char* ws,
-                         cudaStream_t st) {
+PermArgs perm_args(const int* ids, int n, int n_perm, int chunk, const WsLayout& w, char* ws) {
   PermArgs pa{};
   pa.ids = ids;
   pa.n = n;
@@ -616,7 +615,12 @@ llmoc_status run_permute(const int* ids, int n, int n_perm, int chunk, const WsL
   pa.n_active = (int*)(ws + w.n_active);
   pa.err = (int*)(ws + w.err);
   pa.chunk = chunk;
-  if (!cuda_ok(launch_permute(pa, st), "permute")) return LLMOC_ERR_CUDA;
+  return pa;
+}
+
+llmoc_status run_permute(const int* ids, int n, int n_perm, int chunk, const WsLayout& w, char* ws,
+                         cudaStream_t st) {
+  if (!cuda_ok(launch_permute(perm_args(ids, n, n_perm, chunk, w, ws), st), "permute")) return LLMOC_ERR_CUDA;
   count_launch(1);
   return LLMOC_OK;
 }
@@ -642,9 +646,18 @@ llmoc_status run_route(const llmoc_moe_layer* L, const uint16_t* X, int T, const
   ta.has_shared = L->d.has_shared;
   ta.ids = (int*)(ws + w.ids);
   ta.weights = (float*)(ws + w.weights);
+  count_launch(1);
+  if (T <= kFusedRouteMaxT && L->n_exp <= kMaxExpPerm) {  // one CTA: top-k + permutation
+    const PermArgs pa = perm_args(ta.ids, T * L->kk, L->n_exp, chunk_rows(T), w, ws);
+    if (!cuda_ok(launch_topk_permute(ta, pa, st), "topk+permute")) return LLMOC_ERR_CUDA;
+    count_launch(1);
+    if (se) se->mark(st);
+    if (se) se->mark(st);
+    return LLMOC_OK;
+  }
   if (!cuda_ok(launch_topk(ta, st), "topk")) return LLMOC_ERR_CUDA;
   if (se) se->mark(st);
-  count_launch(2);
+  count_launch(1);
   llmoc_status rc = run_permute(ta.ids, T * L->kk, L->n_exp, chunk_rows(T), w, ws, st);
   if (se) se->mark(st);
   return rc;
@@ -655,7 +668,8 @@ llmoc_status run_route(const llmoc_moe_layer* L, const uint16_t* X, int T, const
 // SiLU*mul, down; then, when Y is given, the weighted sum of each row's kk
 // slots into Y (bf16; `weights` null = 1).
 llmoc_status run_ffn(const llmoc_moe_layer* L, const uint16_t* X, int R, int kk, int chunk, const WsLayout& w,
-                     char* ws, uint16_t* Y, const float* weights, cudaStream_t st, StageEvents* se = nullptr) {
+                     char* ws, uint16_t* Y, const float* weights, cudaStream_t st, StageEvents* se = nullptr,
+                     const uint16_t* residual = nullptr) {
   const int H = L->d.hidden, I = L->d.inter;
   const bool awq = L->d.scheme == LLMOC_SCHEME_AWQ_SYM;
   // tensor cores when K of both GEMMs is a multiple of 128 and the group is
@@ -666,6 +680,7 @@ llmoc_status run_ffn(const llmoc_moe_layer* L, const uint16_t* X, int R, int kk,
   const bool umma = use_umma_c(L, chunk);
   if (tc && gemm_path_pref() == 2) path = 2;
   const int n_pairs = R * kk;
+  const int n_groups = std::min(n_pairs, L->n_exp);  // experts (groups) the pairs can reach
   if (umma) {
     if (!cuda_ok(launch_gather_rows(X, H, (const int*)(ws + w.sorted), kk, n_pairs, ws + w.xs, st), "gather"))
       return LLMOC_ERR_CUDA;
@@ -691,13 +706,14 @@ llmoc_status run_ffn(const llmoc_moe_layer* L, const uint16_t* X, int R, int kk,
   a.out_bf16 = 1;
   a.err = (int*)(ws + w.err);
   a.wmaps = L->wmaps;
+  a.ctr = (int*)(ws + w.err) + 1;
   if (umma) {  // B = the gathered rows, read by TMA
     a.B = ws + w.xs;
     a.gather = nullptr;
   }
   if (!cuda_ok(umma ? launch_gemm_umma(MODE_GATE_UP, a, w.max_work, awq, n_pairs, st)
                : tma && path == 0 ? launch_gemm_tma(MODE_GATE_UP, a, w.max_work, awq, st)
-                                  : launch_gemm(MODE_GATE_UP, path, a, w.max_work, awq, ntiles, st),
+                                  : launch_gemm(MODE_GATE_UP, path, a, w.max_work, awq, ntiles, st, n_groups),
                "gate/up"))
     return LLMOC_ERR_CUDA;
   if (se) se->mark(st);
@@ -712,16 +728,17 @@ llmoc_status run_ffn(const llmoc_moe_layer* L, const uint16_t* X, int R, int kk,
   b.gather = nullptr;
   b.out = ws + w.partial;
   b.ldo = H;
+  b.ctr = (int*)(ws + w.err) + 2;
   if (!cuda_ok(umma ? launch_gemm_umma(MODE_PLAIN_F32, b, w.max_work, awq, n_pairs, st)
                : tma && path == 0 ? launch_gemm_tma(MODE_PLAIN_F32, b, w.max_work, awq, st)
-                                  : launch_gemm(MODE_PLAIN_F32, path, b, w.max_work, awq, ntiles, st),
+                                  : launch_gemm(MODE_PLAIN_F32, path, b, w.max_work, awq, ntiles, st, n_groups),
                "down"))
     return LLMOC_ERR_CUDA;
   if (se) se->mark(st);
   count_launch(2);
   if (Y) {
     if (!cuda_ok(launch_combine((const float*)(ws + w.partial), (const int*)(ws + w.inverse), weights, R, kk, H, Y,
-                                1, 0, st),
+                                1, 0, st, residual),
                  "combine"))
       return LLMOC_ERR_CUDA;
     count_launch(1);
@@ -763,7 +780,7 @@ EpSrcLayout ep_src_layout(const llmoc_moe_layer* L, int T) {
   w.work = take((size_t)std::max(1, max_work) * sizeof(WorkItem));
   w.n_work = take(4);
   w.n_active = take(4);
-  w.err = take(4);
+  w.err = take(4 * (1 + kGemmCounters));  // error word, then the GEMM unit counters
   if (L->d.has_shared) {
     w.sh_chunk = chunk_for_rows(T, 1);
     w.shl = ws_layout_g(L, T, 1, L->n_exp, w.sh_chunk, false);
@@ -1133,8 +1150,9 @@ llmoc_status llmoc_moe_route(const llmoc_moe_layer* L, const uint16_t* X, int T,
   return run_route(L, X, T, w, (char*)workspace, (cudaStream_t)stream);
 }
 
-llmoc_status llmoc_moe_forward(const llmoc_moe_layer* L, const uint16_t* X, int T, uint16_t* Y,
-                               void* workspace, size_t workspace_bytes, void* stream) {
+namespace {
+llmoc_status moe_forward(const llmoc_moe_layer* L, const uint16_t* X, int T, const uint16_t* R, uint16_t* Y,
+                         void* workspace, size_t workspace_bytes, void* stream) {
   if (!L || T < 0 || (T > 0 && (!X || !Y))) return fails(LLMOC_ERR_INVALID, "bad arguments");
   if (L->ep_world > 1) return fails(LLMOC_ERR_INVALID, "expert-parallel layer: use llmoc_moe_ep_*");
   if (T == 0) return LLMOC_OK;
@@ -1146,10 +1164,22 @@ llmoc_status llmoc_moe_forward(const llmoc_moe_layer* L, const uint16_t* X, int 
   StageEvents se(L);
   llmoc_status rc = run_route(L, X, T, w, ws, st, &se);
   if (rc != LLMOC_OK) return rc;
-  rc = run_ffn(L, X, T, L->kk, chunk_rows(T), w, ws, Y, (const float*)(ws + w.weights), st, &se);
+  rc = run_ffn(L, X, T, L->kk, chunk_rows(T), w, ws, Y, (const float*)(ws + w.weights), st, &se, R);
   if (rc != LLMOC_OK) return rc;
   se.commit();
   return LLMOC_OK;
+}
+}  // namespace
+
+llmoc_status llmoc_moe_forward(const llmoc_moe_layer* L, const uint16_t* X, int T, uint16_t* Y,
+                               void* workspace, size_t workspace_bytes, void* stream) {
+  return moe_forward(L, X, T, nullptr, Y, workspace, workspace_bytes, stream);
+}
+
+llmoc_status llmoc_moe_forward_residual(const llmoc_moe_layer* L, const uint16_t* X, int T, const uint16_t* R,
+                                        uint16_t* Y, void* workspace, size_t workspace_bytes, void* stream) {
+  if (T > 0 && !R) return fails(LLMOC_ERR_INVALID, "null residual");
+  return moe_forward(L, X, T, R, Y, workspace, workspace_bytes, stream);
 }
 
 llmoc_status llmoc_moe_dequant(const llmoc_moe_layer* L, int expert, int proj, float* out,

@@ -88,6 +88,7 @@ _SIGS = {
     "llmoc_expert_storage_bytes": (_sz, [_i, _i, _i, _i]),
     "llmoc_moe_workspace_bytes": (_sz, [_vp, _i]),
     "llmoc_moe_forward": (_i, [_vp, _vp, _i, _vp, _vp, _sz, _vp]),
+    "llmoc_moe_forward_residual": (_i, [_vp, _vp, _i, _vp, _vp, _vp, _sz, _vp]),
     "llmoc_moe_route_views": (_i, [_vp, _i, _vp, _sz, C.POINTER(RouteViews)]),
     "llmoc_moe_route": (_i, [_vp, _vp, _i, _vp, _sz, _vp]),
     "llmoc_moe_dequant": (_i, [_vp, _i, _i, _vp, _vp]),
@@ -223,6 +224,11 @@ class MoeLayer:
     def forward(self, X, T: int, Y, ws, ws_bytes: int, stream=None) -> None:
         check(lib.llmoc_moe_forward(self.handle, ptr(X), T, ptr(Y), ptr(ws), ws_bytes,
                                     stream_ptr(stream)), "llmoc_moe_forward")
+
+    def forward_residual(self, X, T: int, R, Y, ws, ws_bytes: int, stream=None) -> None:
+        """Y = R + MoE(X) (R may be Y, and both may be X)."""
+        check(lib.llmoc_moe_forward_residual(self.handle, ptr(X), T, ptr(R), ptr(Y), ptr(ws), ws_bytes,
+                                             stream_ptr(stream)), "llmoc_moe_forward_residual")
 
     def route(self, X, T: int, ws, ws_bytes: int, stream=None) -> None:
         check(lib.llmoc_moe_route(self.handle, ptr(X), T, ptr(ws), ws_bytes, stream_ptr(stream)),

@@ -184,6 +184,35 @@ def test_skewed_routing_hot_expert(oracle, T):
     dl.close()
 
 
+@pytest.mark.parametrize("T,in_place", [(5, False), (5, True), (150, False), (150, True)])
+def test_forward_residual(oracle, T, in_place):
+    """Y = R + MoE(X) through llmoc_moe_forward_residual: separate R, and the
+    in-place residual stream (R = Y = X, the decoder's h += moe(h)); decode and
+    prefill paths.  Compared with R + the oracle's fp32 layer output, and with
+    the plain forward's output plus R."""
+    rng = np.random.default_rng(30 + T)
+    layer = orc.make_layer(oracle, rng, H=512, I=256, E=32, topk=8, gs=128)
+    X = orc.make_tokens(rng, T, 512)
+    R = X if in_place else orc.make_tokens(rng, T, 512)
+    dl = G.DevLayer(layer, T)
+    Xd = G.bf16_dev(X)
+    Rd = Xd if in_place else G.bf16_dev(R)
+    Y = Xd if in_place else torch.empty_like(Xd)
+    ws_bytes = dl.dev.workspace_bytes(T)
+    dl.dev.forward_residual(Xd, T, Rd, Y, dl.ws, ws_bytes, torch.cuda.current_stream())
+    torch.cuda.synchronize()
+    Yref, _, _, _ = oracle.moe_layer_forward(layer, X)
+    # Y carries one bf16 rounding of R + MoE(X): judged against R + the oracle
+    mre, cos = G.quality(G.bf16_to_f32(Y), R + Yref)
+    assert mre <= G.MAX_REL and cos >= G.MIN_COS, (mre, cos)
+    # same arithmetic as the plain forward followed by an fp32 add of R
+    Y2, _ = dl.forward(X)
+    y2 = G.bf16_to_f32(Y2)
+    err = np.abs(G.bf16_to_f32(Y) - (R + y2)).max()
+    assert err <= 2.0 ** -6 * (np.abs(R).max() + np.abs(y2).max()), err
+    dl.close()
+
+
 def test_zero_weights_give_zero_output(oracle):
     rng = np.random.default_rng(7)
     layer = orc.make_layer(oracle, rng, H=256, I=128, E=8, topk=2, gs=64, wstd=0.0)
