@@ -940,52 +940,81 @@ __global__ void __launch_bounds__(128) k_int4_cc(GemmArgs a, int awq) {
 // y[t,h] = sum_{j<kk} w[t,j] * d[inverse[t*kk+j], h] in j order (fma), the
 // order of the reference's combine (qwen3_6_moe_int4_model.cpp:213, :372).
 template <typename OT>
-__global__ void k_combine(const float* __restrict__ d, const int* __restrict__ inverse,
-                          const float* __restrict__ w, int T, int kk, int H, OT* y, int skip_tiny,
-                          const __nv_bfloat16* res) {
+__device__ __forceinline__ void combine_store(OT* y, size_t o, const float (&ap)[4], int n) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (i >= n) break;
+    if constexpr (sizeof(OT) == 2)
+      y[o + i] = __float2bfloat16_rn(ap[i]);
+    else
+      y[o + i] = ap[i];
+  }
+}
+
+// A thread owns 4 consecutive h of a column and walks the tokens t =
+// blockIdx.y, blockIdx.y + gridDim.y, ... two at a time, with every slot row
+// of both tokens requested before the ordered FMAs (streaming loads: each
+// partial row is read once).
+template <typename OT>
+__global__ void __launch_bounds__(256) k_combine(const float* __restrict__ d, const int* __restrict__ inverse,
+                                                 const float* __restrict__ w, int T, int kk, int H, OT* y,
+                                                 int skip_tiny, const __nv_bfloat16* res) {
   grid_dep_wait();
   grid_dep_release();
-  const int t = blockIdx.y;
   const int h = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
-  if (t >= T || h >= H) return;
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  // issue the slot loads in groups of 8 before the ordered FMAs
-  for (int j0 = 0; j0 < kk; j0 += 8) {
-    float wj[8];
-    float4 v[8];
+  if (h >= H) return;
+  const bool full4 = h + 3 < H;
+  const int nh = full4 ? 4 : H - h;
+  for (int t0 = blockIdx.y; t0 < T; t0 += 2 * gridDim.y) {
+    const int tt[2] = {t0, t0 + (int)gridDim.y};
+    float4 acc[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+    int live[2] = {0, 0};
+    for (int j0 = 0; j0 < kk; j0 += 8) {
+      float wj[2][8];
+      float4 v[2][8];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int j = j0 + u;
-      wj[u] = 0.f;
-      v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (j < kk) {
-        wj[u] = w ? w[(size_t)t * kk + j] : 1.f;
-        const float* row = d + (size_t)inverse[(size_t)t * kk + j] * H;
-        if (h + 3 < H) {
-          v[u] = *reinterpret_cast<const float4*>(row + h);
-        } else {
-          float* vp = &v[u].x;
-          for (int i = 0; h + i < H; ++i) vp[i] = row[h + i];
+      for (int q = 0; q < 2; ++q)
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int j = j0 + u;
+          wj[q][u] = 0.f;
+          v[q][u] = make_float4(0.f, 0.f, 0.f, 0.f);
+          const int src = j < kk && tt[q] < T ? inverse[(size_t)tt[q] * kk + j] : -1;
+          if (src >= 0) {  // src < 0: an empty slot (not placed by the permutation)
+            ++live[q];
+            wj[q][u] = w ? w[(size_t)tt[q] * kk + j] : 1.f;
+            const float* row = d + (size_t)src * H + h;
+            if (full4) {
+              v[q][u] = __ldcs(reinterpret_cast<const float4*>(row));
+            } else {  // the last 1-3 columns of a row whose H is not a multiple of 4
+              v[q][u].x = row[0];
+              if (nh > 1) v[q][u].y = row[1];
+              if (nh > 2) v[q][u].z = row[2];
+            }
+          }
         }
-      }
+#pragma unroll
+      for (int q = 0; q < 2; ++q)
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          if (j0 + u >= kk || (skip_tiny && fabsf(wj[q][u]) < 1e-12f)) continue;
+          acc[q].x = __fmaf_rn(wj[q][u], v[q][u].x, acc[q].x);
+          acc[q].y = __fmaf_rn(wj[q][u], v[q][u].y, acc[q].y);
+          acc[q].z = __fmaf_rn(wj[q][u], v[q][u].z, acc[q].z);
+          acc[q].w = __fmaf_rn(wj[q][u], v[q][u].w, acc[q].w);
+        }
     }
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      if (j0 + u >= kk || (skip_tiny && fabsf(wj[u]) < 1e-12f)) continue;
-      acc.x = __fmaf_rn(wj[u], v[u].x, acc.x);
-      acc.y = __fmaf_rn(wj[u], v[u].y, acc.y);
-      acc.z = __fmaf_rn(wj[u], v[u].z, acc.z);
-      acc.w = __fmaf_rn(wj[u], v[u].w, acc.w);
+    for (int q = 0; q < 2; ++q) {
+      if (tt[q] >= T || live[q] == 0) continue;  // a row of empty slots only is left untouched
+      float ap[4] = {acc[q].x, acc[q].y, acc[q].z, acc[q].w};
+      const size_t o = (size_t)tt[q] * H + h;
+      if (res)  // residual stream: y = r + sum (one fp32 add; res may alias y, read before written)
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (i < nh) ap[i] = __fadd_rn(__bfloat162float(res[o + i]), ap[i]);
+      combine_store(y, o, ap, nh);
     }
-  }
-  float* ap = &acc.x;
-  if (res)  // residual stream: y = r + sum (one fp32 add; res may alias y, read before written)
-    for (int i = 0; i < 4 && h + i < H; ++i) ap[i] = __fadd_rn(__bfloat162float(res[(size_t)t * H + h + i]), ap[i]);
-  for (int i = 0; i < 4 && h + i < H; ++i) {
-    if constexpr (sizeof(OT) == 2)
-      y[(size_t)t * H + h + i] = __float2bfloat16_rn(ap[i]);
-    else
-      y[(size_t)t * H + h + i] = ap[i];
   }
 }
 
@@ -1115,8 +1144,11 @@ cudaError_t launch_combine_ep(const void* ret, const int* inverse, const float* 
 cudaError_t launch_combine(const float* d, const int* inverse, const float* w, int T, int kk, int H,
                            void* y, int y_bf16, int skip_tiny, cudaStream_t st, const void* res) {
   if (T <= 0) return cudaSuccess;
-  const int threads = 128;
-  dim3 grid(((H + 3) / 4 + threads - 1) / threads, T);
+  const int threads = 256;
+  const int gx = ((H + 3) / 4 + threads - 1) / threads;
+  // about 8 CTAs per SM in total; each walks its tokens two at a time
+  const int gy = std::max(1, std::min((T + 1) / 2, (148 * 8 + gx - 1) / gx));
+  const dim3 grid(gx, gy);
   if (y_bf16)
     return launch_pdl(k_combine<__nv_bfloat16>, grid, dim3(threads), 0, st, d, inverse, w, T, kk, H,
                       (__nv_bfloat16*)y, skip_tiny, (const __nv_bfloat16*)res);

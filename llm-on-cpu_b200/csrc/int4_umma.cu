@@ -633,25 +633,26 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a, const __
 }
 
 // Rows of the gate/up activations in expert-sorted order: Xs[p] = X[sorted[p] / kk]
-// (one warp per row, 16-byte pieces), so every work item's rows are contiguous
-// and its B tiles are plain TMA boxes.
+// for p < *n_valid (the placed pairs; empty slots are not placed), one warp per
+// row, 16-byte pieces, so every work item's rows are contiguous and its B
+// tiles are plain TMA boxes.
 __global__ void __launch_bounds__(256) k_gather_rows(const uint4* __restrict__ X, int H8,
                                                      const int* __restrict__ sorted, int kk, int n,
-                                                     uint4* __restrict__ Xs) {
+                                                     const int* __restrict__ n_valid, uint4* __restrict__ Xs) {
   grid_dep_wait();
   grid_dep_release();
   const int p = blockIdx.x * 8 + (threadIdx.x >> 5);
-  if (p >= n) return;
+  if (p >= n || (n_valid && p >= *n_valid)) return;
   const uint4* src = X + (size_t)(sorted[p] / kk) * H8;
   uint4* dst = Xs + (size_t)p * H8;
   for (int c = threadIdx.x & 31; c < H8; c += 32) dst[c] = __ldg(src + c);
 }
 
-cudaError_t launch_gather_rows(const void* X, int H, const int* sorted, int kk, int n, void* Xs,
-                               cudaStream_t st) {
+cudaError_t launch_gather_rows(const void* X, int H, const int* sorted, int kk, int n, const int* n_valid,
+                               void* Xs, cudaStream_t st) {
   if (n <= 0) return cudaSuccess;
   return launch_pdl(k_gather_rows, dim3((n + 7) / 8), dim3(256), 0, st, reinterpret_cast<const uint4*>(X), H / 8,
-                    sorted, kk, n, reinterpret_cast<uint4*>(Xs));
+                    sorted, kk, n, n_valid, reinterpret_cast<uint4*>(Xs));
 }
 
 namespace {

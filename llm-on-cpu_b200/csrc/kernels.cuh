@@ -107,9 +107,10 @@ constexpr int kMapsPerExpert = 9;
 constexpr int kTensorMapBytes = 128;
 bool build_umma_weight_maps(const ExpertDev* host_table, int n_exp, int inter, int hidden, int gs, bool gptq,
                             void* host_out);
-// Xs[p, :] = X[sorted[p] / kk, :] for p < n (bf16 rows of H elements, H % 8 == 0).
-cudaError_t launch_gather_rows(const void* X, int H, const int* sorted, int kk, int n, void* Xs,
-                               cudaStream_t st);
+// Xs[p, :] = X[sorted[p] / kk, :] for p < min(n, *n_valid) (bf16 rows of H
+// elements, H % 8 == 0; n_valid may be null).
+cudaError_t launch_gather_rows(const void* X, int H, const int* sorted, int kk, int n, const int* n_valid,
+                               void* Xs, cudaStream_t st);
 // y[t] (+)= sum_j w[t,j] * d[inverse[t*kk+j]]; res (bf16 [T,H], may alias y):
 // y = res + sum, the residual stream of the caller's decoder layer.
 cudaError_t launch_combine(const float* d, const int* inverse, const float* w, int T, int kk, int H,

@@ -450,7 +450,12 @@ __device__ __forceinline__ void permute_block(const PermArgs& a, int* cnt) {
 
   const int per = (a.n + kPermWarps - 1) / kPermWarps;
   const int lo = min(a.n, warp * per), hi = min(a.n, lo + per);
-  for (int i = lo + lane; i < hi; i += 32) atomicAdd(&cnt[warp * a.n_exp + a.ids[i]], 1);
+  // ids outside [0, n_exp) are empty slots (the padded receive layout of the
+  // NVLink expert-parallel transport): not counted, not placed, inverse -1
+  for (int i = lo + lane; i < hi; i += 32) {
+    const int ex = a.ids[i];
+    if ((unsigned)ex < (unsigned)a.n_exp) atomicAdd(&cnt[warp * a.n_exp + ex], 1);
+  }
   __syncthreads();
 
   // per expert totals -> exclusive scans (pairs and work chunks); thread e
@@ -527,10 +532,11 @@ __device__ __forceinline__ void permute_block(const PermArgs& a, int* cnt) {
   // placement: each warp walks its own range in order, 32 pairs at a time.
   for (int b = lo; b < hi; b += 32) {
     const int i = b + lane;
-    const bool ok = i < hi;
+    const int ex = i < hi ? a.ids[i] : -1;
+    const bool ok = (unsigned)ex < (unsigned)a.n_exp;
+    if (i < hi && !ok) a.inverse[i] = -1;
     const unsigned act = __ballot_sync(0xffffffffu, ok);
     if (ok) {
-      const int ex = a.ids[i];
       const unsigned peers = __match_any_sync(act, ex);
       const int rank = __popc(peers & lanemask_lt());
       const int pos = cnt[warp * a.n_exp + ex] + rank;

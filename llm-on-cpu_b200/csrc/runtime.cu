@@ -682,7 +682,9 @@ llmoc_status run_ffn(const llmoc_moe_layer* L, const uint16_t* X, int R, int kk,
   const int n_pairs = R * kk;
   const int n_groups = std::min(n_pairs, L->n_exp);  // experts (groups) the pairs can reach
   if (umma) {
-    if (!cuda_ok(launch_gather_rows(X, H, (const int*)(ws + w.sorted), kk, n_pairs, ws + w.xs, st), "gather"))
+    if (!cuda_ok(launch_gather_rows(X, H, (const int*)(ws + w.sorted), kk, n_pairs,
+                                    (const int*)(ws + w.offsets) + L->n_exp, ws + w.xs, st),
+                 "gather"))
       return LLMOC_ERR_CUDA;
     count_launch(1);
   }
@@ -1305,7 +1307,7 @@ llmoc_status llmoc_moe_ep_dispatch(const llmoc_moe_layer* L, const uint16_t* X, 
   if (!cuda_ok(launch_permute(pa, st), "permute")) return LLMOC_ERR_CUDA;
   if (!cuda_ok(launch_ep_meta(pa.offsets, pa.sorted, key, n, L->ep_world, L->e_loc, send_counts, send_expert, st),
                "ep meta") ||
-      !cuda_ok(launch_gather_rows(X, H, pa.sorted, k, n, send_rows, st), "gather"))
+      !cuda_ok(launch_gather_rows(X, H, pa.sorted, k, n, nullptr, send_rows, st), "gather"))
     return LLMOC_ERR_CUDA;
   count_launch(6);
   return LLMOC_OK;
