@@ -290,6 +290,48 @@ LLMOC_API llmoc_status llmoc_moe_ep_combine(const llmoc_moe_layer* layer, const 
                                             const uint16_t* ret_rows, uint16_t* Y, void* workspace,
                                             size_t workspace_bytes, void* stream);
 
+/* -------------------------- expert-parallel transport over NVLink peer memory
+ *
+ * The all-to-all of the step above (the reference only declares it:
+ * ICollective::alltoall, src/contracts/collective.h:13) done by the library's
+ * own kernels: each rank stores its routed rows straight into the owners'
+ * receive buffers (CUDA IPC peer pointers, plain stores over NVLink), raises
+ * a per-source sequence flag there, and the owners push the expert outputs
+ * back the same way.  The step needs no host synchronisation and no library
+ * collective:
+ *   llmoc_ep_p2p_send    dispatch (as llmoc_moe_ep_dispatch) + push the rows
+ *   llmoc_ep_p2p_serve   wait for every source, grouped expert FFN over the
+ *                        received rows, push the outputs back
+ *   llmoc_ep_p2p_finish  wait for every owner, combine (+ shared expert)
+ * all asynchronous on `stream`; every rank calls the three in this order with
+ * the same seq = 1, 2, 3, ... (one per layer step).  Waits are bounded
+ * (~1 s): a wait that gives up sets bit 1 of llmoc_ep_transport_error and the
+ * step's outputs are invalid.  One transport per (shard shape, max_tokens);
+ * T <= max_tokens on every call. */
+typedef struct llmoc_ep_transport llmoc_ep_transport;
+LLMOC_API size_t llmoc_ep_ipc_handle_bytes(void);
+/* Allocates this rank's buffers on `device` and writes its CUDA IPC handle
+ * (llmoc_ep_ipc_handle_bytes() bytes) to ipc_handle (may be null when every
+ * rank lives in this process: llmoc_ep_transport_connect_local). */
+LLMOC_API llmoc_status llmoc_ep_transport_create(int world, int rank, int hidden, int max_tokens, int topk,
+                                                 int device, llmoc_ep_transport** out, void* ipc_handle);
+/* handles: every rank's IPC handle in rank order (world x handle bytes). */
+LLMOC_API llmoc_status llmoc_ep_transport_connect(llmoc_ep_transport* tr, const void* handles);
+/* All ranks in this process (tests): the world's transports in rank order. */
+LLMOC_API llmoc_status llmoc_ep_transport_connect_local(llmoc_ep_transport* tr, llmoc_ep_transport* const* all);
+LLMOC_API void llmoc_ep_transport_destroy(llmoc_ep_transport* tr);
+/* Reads (synchronously) the device error word: 0, or bit 1 when a wait gave up. */
+LLMOC_API int llmoc_ep_transport_error(llmoc_ep_transport* tr);
+LLMOC_API size_t llmoc_ep_p2p_workspace_bytes(const llmoc_moe_layer* shard, const llmoc_ep_transport* tr,
+                                              int max_tokens);
+LLMOC_API llmoc_status llmoc_ep_p2p_send(const llmoc_moe_layer* shard, llmoc_ep_transport* tr, const uint16_t* X,
+                                         int T, uint32_t seq, void* workspace, size_t workspace_bytes, void* stream);
+LLMOC_API llmoc_status llmoc_ep_p2p_serve(const llmoc_moe_layer* shard, llmoc_ep_transport* tr, int T, uint32_t seq,
+                                          void* workspace, size_t workspace_bytes, void* stream);
+LLMOC_API llmoc_status llmoc_ep_p2p_finish(const llmoc_moe_layer* shard, llmoc_ep_transport* tr, const uint16_t* X,
+                                           int T, uint16_t* Y, uint32_t seq, void* workspace,
+                                           size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------ utilities */
 
 /* quant_awq_sym (tools/quantize_int4.py:150-166) on the device: W [M,K] bf16

@@ -52,6 +52,21 @@ cudaError_t launch_fill_i32(int* p, int n, int v, cudaStream_t st);
 cudaError_t launch_combine_ep(const void* ret, const int* inverse, const float* w, int T, int topk, int H,
                               const float* sh, const int* sh_inv, float sh_scale, void* y, cudaStream_t st);
 
+// ---- ep_p2p.cu: expert-parallel transport over NVLink peer memory
+constexpr int kEpMaxWorld = 64;
+constexpr int kEpPushCtas = 148;  // push grids: one CTA per SM
+// byte offsets of the regions of one rank's transport buffer
+struct EpP2PLayout {
+  int world, cap, row_bytes;  // row_bytes = hidden * 2
+  size_t flags, meta, recv_ids, recv_rows, ret_rows, total;
+};
+cudaError_t launch_ep_push_dispatch(const EpP2PLayout& L, char* const* peers, const void* send_rows,
+                                    const int* send_expert, const int* counts, int rank, uint32_t seq, int* ctr,
+                                    cudaStream_t st);
+cudaError_t launch_ep_wait(const EpP2PLayout& L, char* base, int kind, uint32_t seq, int* err, cudaStream_t st);
+cudaError_t launch_ep_push_return(const EpP2PLayout& L, char* const* peers, char* base, const void* out_rows, int rank,
+                                  uint32_t seq, int* ctr, cudaStream_t st);
+
 // ---- int4_gemm.cu
 struct RepackArgs {
   const uint8_t* q;      // QLWC [M, ceil(K/2)]

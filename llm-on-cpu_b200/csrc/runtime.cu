@@ -797,6 +797,49 @@ size_t ep_owner_bytes(const llmoc_moe_layer* L, int rows) {
                   ws_layout_g(L, rows, 1, L->n_exp, gemm_path_pref() == 1 ? kChunkRows : kUmmaRows, false).total);
 }
 
+// Workspace of one NVLink expert-parallel step on a rank: the source side
+// (routing, send rows, ids, counts) and the owner side (the grouped run over
+// the padded receive slots and its output rows), used in the same step.
+struct EpP2PWs {
+  size_t src, send_rows, send_expert, counts, own, out_rows, total;
+  EpSrcLayout sw;
+};
+EpP2PWs ep_p2p_ws(const llmoc_moe_layer* L, const llmoc_ep_transport* tr, int T);
+
+}  // namespace
+
+struct llmoc_ep_transport {
+  int world = 1, rank = 0, device = 0, hidden = 0, max_tokens = 0, topk = 0;
+  llmoc::EpP2PLayout lay{};
+  char* base = nullptr;            // this rank's buffer (exported by CUDA IPC)
+  std::vector<char*> peer;         // every rank's buffer as seen from here (own = base)
+  std::vector<bool> opened;        // opened through CUDA IPC (closed at destroy)
+  char** peers_dev = nullptr;      // device copy of `peer`
+  int* ctr = nullptr;              // device: CTA counters of the two push kernels
+  int* err = nullptr;              // device: bit 1 = a wait gave up
+  bool connected = false;
+};
+
+namespace {
+EpP2PWs ep_p2p_ws(const llmoc_moe_layer* L, const llmoc_ep_transport* tr, int T) {
+  EpP2PWs w{};
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = o;
+    o += align256(bytes);
+    return at;
+  };
+  const size_t n = (size_t)T * L->d.topk, H = (size_t)L->d.hidden, slots = (size_t)tr->world * tr->lay.cap;
+  w.sw = ep_src_layout(L, T);
+  w.src = take(w.sw.total);
+  w.send_rows = take(n * H * 2);
+  w.send_expert = take(n * 4);
+  w.counts = take((size_t)tr->world * 4);
+  w.own = take(ep_owner_bytes(L, (int)slots));
+  w.out_rows = take(slots * H * 2);
+  w.total = o;
+  return w;
+}
 }  // namespace
 
 // ===================================================================== ABI
@@ -1313,11 +1356,11 @@ llmoc_status llmoc_moe_ep_dispatch(const llmoc_moe_layer* L, const uint16_t* X, 
   return LLMOC_OK;
 }
 
-llmoc_status llmoc_moe_ep_experts(const llmoc_moe_layer* L, const uint16_t* rows, const int32_t* expert, int n,
-                                  uint16_t* out_rows, void* workspace, size_t workspace_bytes, void* stream) {
-  if (!L || n < 0 || (n > 0 && (!rows || !expert || !out_rows))) return fails(LLMOC_ERR_INVALID, "bad arguments");
-  if (n == 0) return LLMOC_OK;
-  const int chunk = chunk_for_rows(n, L->e_loc);
+namespace {
+// n rows (expert ids < 0: empty slots), about n_hint of them occupied (sets the kernel regime)
+llmoc_status ep_experts(const llmoc_moe_layer* L, const uint16_t* rows, const int32_t* expert, int n, int n_hint,
+                        uint16_t* out_rows, void* workspace, size_t workspace_bytes, void* stream) {
+  const int chunk = chunk_for_rows(n_hint, L->e_loc);
   const WsLayout w = ws_layout_g(L, n, 1, L->n_exp, chunk, false);
   if (!workspace || workspace_bytes < w.total) return fails(LLMOC_ERR_WORKSPACE, "workspace too small");
   DevGuard dg(L->device);
@@ -1326,6 +1369,14 @@ llmoc_status llmoc_moe_ep_experts(const llmoc_moe_layer* L, const uint16_t* rows
   llmoc_status rc = run_permute(expert, n, L->n_exp, chunk, w, ws, st);
   if (rc != LLMOC_OK) return rc;
   return run_ffn(L, rows, n, 1, chunk, w, ws, out_rows, nullptr, st);
+}
+}  // namespace
+
+llmoc_status llmoc_moe_ep_experts(const llmoc_moe_layer* L, const uint16_t* rows, const int32_t* expert, int n,
+                                  uint16_t* out_rows, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!L || n < 0 || (n > 0 && (!rows || !expert || !out_rows))) return fails(LLMOC_ERR_INVALID, "bad arguments");
+  if (n == 0) return LLMOC_OK;
+  return ep_experts(L, rows, expert, n, n, out_rows, workspace, workspace_bytes, stream);
 }
 
 llmoc_status llmoc_moe_ep_combine(const llmoc_moe_layer* L, const uint16_t* X, int T, const uint16_t* ret_rows,
@@ -1356,6 +1407,194 @@ llmoc_status llmoc_moe_ep_combine(const llmoc_moe_layer* L, const uint16_t* X, i
     return LLMOC_ERR_CUDA;
   count_launch(1);
   return LLMOC_OK;
+}
+
+// ------------------------------------------- NVLink expert-parallel transport
+
+size_t llmoc_ep_ipc_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }
+
+llmoc_status llmoc_ep_transport_create(int world, int rank, int hidden, int max_tokens, int topk, int device,
+                                       llmoc_ep_transport** out, void* ipc_handle) {
+  if (!out || world < 1 || world > kEpMaxWorld || rank < 0 || rank >= world || hidden <= 0 || hidden % 8 ||
+      max_tokens <= 0 || topk <= 0)
+    return fails(LLMOC_ERR_INVALID, "bad arguments");
+  *out = nullptr;
+  DevGuard dg(device);
+  auto* tr = new llmoc_ep_transport();
+  tr->world = world;
+  tr->rank = rank;
+  tr->device = device;
+  tr->hidden = hidden;
+  tr->max_tokens = max_tokens;
+  tr->topk = topk;
+  EpP2PLayout& l = tr->lay;
+  l.world = world;
+  l.cap = max_tokens * topk;  // a source sends at most this many rows (to one owner, in the worst case)
+  l.row_bytes = hidden * 2;
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = o;
+    o += align256(bytes);
+    return at;
+  };
+  l.flags = take((size_t)2 * world * 4);
+  l.meta = take((size_t)2 * world * 8);
+  l.recv_ids = take((size_t)2 * world * l.cap * 4);
+  l.recv_rows = take((size_t)2 * world * l.cap * l.row_bytes);
+  l.ret_rows = take((size_t)2 * l.cap * l.row_bytes);
+  l.total = o;
+  bool ok = cuda_ok(cudaMalloc((void**)&tr->base, l.total), "transport buffer") &&
+            cuda_ok(cudaMemset(tr->base, 0, l.total), "transport memset") &&
+            cuda_ok(cudaMalloc((void**)&tr->ctr, 64), "transport counters") &&
+            cuda_ok(cudaMemset(tr->ctr, 0, 64), "transport memset") &&
+            cuda_ok(cudaMalloc((void**)&tr->peers_dev, sizeof(char*) * world), "transport peers");
+  tr->err = tr->ctr + 8;
+  if (ok && ipc_handle) {
+    cudaIpcMemHandle_t h;
+    ok = cuda_ok(cudaIpcGetMemHandle(&h, tr->base), "ipc handle");
+    if (ok) memcpy(ipc_handle, &h, sizeof(h));
+  }
+  tr->peer.assign(world, nullptr);
+  tr->opened.assign(world, false);
+  tr->peer[rank] = tr->base;
+  if (!ok) {
+    llmoc_ep_transport_destroy(tr);
+    return LLMOC_ERR_CUDA;
+  }
+  *out = tr;
+  return LLMOC_OK;
+}
+
+namespace {
+llmoc_status upload_peers(llmoc_ep_transport* tr) {
+  if (!cuda_ok(cudaMemcpy(tr->peers_dev, tr->peer.data(), sizeof(char*) * tr->world, cudaMemcpyHostToDevice),
+               "peers"))
+    return LLMOC_ERR_CUDA;
+  tr->connected = true;
+  return LLMOC_OK;
+}
+}  // namespace
+
+llmoc_status llmoc_ep_transport_connect(llmoc_ep_transport* tr, const void* handles) {
+  if (!tr || !handles) return fails(LLMOC_ERR_INVALID, "bad arguments");
+  DevGuard dg(tr->device);
+  const char* hb = static_cast<const char*>(handles);
+  for (int r = 0; r < tr->world; ++r) {
+    if (r == tr->rank || tr->opened[r]) continue;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, hb + (size_t)r * sizeof(h), sizeof(h));
+    void* p = nullptr;
+    if (!cuda_ok(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess), "ipc open")) return LLMOC_ERR_CUDA;
+    tr->peer[r] = static_cast<char*>(p);
+    tr->opened[r] = true;
+  }
+  return upload_peers(tr);
+}
+
+llmoc_status llmoc_ep_transport_connect_local(llmoc_ep_transport* tr, llmoc_ep_transport* const* all) {
+  if (!tr || !all) return fails(LLMOC_ERR_INVALID, "bad arguments");
+  for (int r = 0; r < tr->world; ++r) {
+    if (!all[r] || all[r]->world != tr->world || all[r]->rank != r || all[r]->lay.total != tr->lay.total)
+      return fails(LLMOC_ERR_INVALID, "transports of one world, in rank order");
+    tr->peer[r] = all[r]->base;
+  }
+  DevGuard dg(tr->device);
+  return upload_peers(tr);
+}
+
+void llmoc_ep_transport_destroy(llmoc_ep_transport* tr) {
+  if (!tr) return;
+  DevGuard dg(tr->device);
+  for (int r = 0; r < tr->world; ++r)
+    if (tr->opened[r]) cudaIpcCloseMemHandle(tr->peer[r]);
+  if (tr->base) cudaFree(tr->base);
+  if (tr->ctr) cudaFree(tr->ctr);
+  if (tr->peers_dev) cudaFree(tr->peers_dev);
+  delete tr;
+}
+
+int llmoc_ep_transport_error(llmoc_ep_transport* tr) {
+  if (!tr) return -1;
+  DevGuard dg(tr->device);
+  int v = 0;
+  if (!cuda_ok(cudaMemcpy(&v, tr->err, 4, cudaMemcpyDeviceToHost), "error word")) return -1;
+  return v;
+}
+
+size_t llmoc_ep_p2p_workspace_bytes(const llmoc_moe_layer* L, const llmoc_ep_transport* tr, int max_tokens) {
+  if (!L || !tr || max_tokens < 0) return 0;
+  return ep_p2p_ws(L, tr, max_tokens).total;
+}
+
+namespace {
+llmoc_status p2p_check(const llmoc_moe_layer* L, const llmoc_ep_transport* tr, int T, uint32_t seq,
+                       size_t workspace_bytes, const void* workspace) {
+  if (!L || !tr || T < 0 || T > tr->max_tokens || seq == 0) return fails(LLMOC_ERR_INVALID, "bad arguments");
+  if (!tr->connected) return fails(LLMOC_ERR_INVALID, "transport not connected");
+  if (L->ep_world != tr->world || L->ep_rank != tr->rank || L->d.hidden != tr->hidden || L->d.topk != tr->topk ||
+      L->device != tr->device)
+    return fails(LLMOC_ERR_INVALID, "shard and transport disagree");
+  if (!workspace || workspace_bytes < ep_p2p_ws(L, tr, T).total) return fails(LLMOC_ERR_WORKSPACE, "workspace too small");
+  return LLMOC_OK;
+}
+}  // namespace
+
+llmoc_status llmoc_ep_p2p_send(const llmoc_moe_layer* L, llmoc_ep_transport* tr, const uint16_t* X, int T,
+                               uint32_t seq, void* workspace, size_t workspace_bytes, void* stream) {
+  llmoc_status rc = p2p_check(L, tr, T, seq, workspace_bytes, workspace);
+  if (rc != LLMOC_OK) return rc;
+  if (T > 0 && !X) return fails(LLMOC_ERR_INVALID, "bad arguments");
+  const EpP2PWs w = ep_p2p_ws(L, tr, T);
+  char* ws = (char*)workspace;
+  rc = llmoc_moe_ep_dispatch(L, X, T, ws + w.src, w.sw.total, (uint16_t*)(ws + w.send_rows),
+                             (int32_t*)(ws + w.send_expert), (int32_t*)(ws + w.counts), stream);
+  if (rc != LLMOC_OK) return rc;
+  DevGuard dg(L->device);
+  if (!cuda_ok(launch_ep_push_dispatch(tr->lay, tr->peers_dev, ws + w.send_rows, (const int*)(ws + w.send_expert),
+                                       (const int*)(ws + w.counts), tr->rank, seq, tr->ctr, (cudaStream_t)stream),
+               "ep push"))
+    return LLMOC_ERR_CUDA;
+  count_launch(1);
+  return LLMOC_OK;
+}
+
+llmoc_status llmoc_ep_p2p_serve(const llmoc_moe_layer* L, llmoc_ep_transport* tr, int T, uint32_t seq,
+                                void* workspace, size_t workspace_bytes, void* stream) {
+  llmoc_status rc = p2p_check(L, tr, T, seq, workspace_bytes, workspace);
+  if (rc != LLMOC_OK) return rc;
+  const EpP2PWs w = ep_p2p_ws(L, tr, T);
+  char* ws = (char*)workspace;
+  cudaStream_t st = (cudaStream_t)stream;
+  DevGuard dg(L->device);
+  if (!cuda_ok(launch_ep_wait(tr->lay, tr->base, 0, seq, tr->err, st), "ep wait")) return LLMOC_ERR_CUDA;
+  count_launch(1);
+  const int parity = seq & 1, slots = tr->world * tr->lay.cap;
+  const uint16_t* rows =
+      (const uint16_t*)(tr->base + tr->lay.recv_rows + (size_t)parity * slots * tr->lay.row_bytes);
+  const int32_t* ids = (const int32_t*)(tr->base + tr->lay.recv_ids + (size_t)parity * slots * 4);
+  rc = ep_experts(L, rows, ids, slots, std::max(1, T * L->d.topk), (uint16_t*)(ws + w.out_rows), ws + w.own,
+                  ep_owner_bytes(L, slots), stream);
+  if (rc != LLMOC_OK) return rc;
+  if (!cuda_ok(launch_ep_push_return(tr->lay, tr->peers_dev, tr->base, ws + w.out_rows, tr->rank, seq, tr->ctr + 1, st),
+               "ep push back"))
+    return LLMOC_ERR_CUDA;
+  count_launch(1);
+  return LLMOC_OK;
+}
+
+llmoc_status llmoc_ep_p2p_finish(const llmoc_moe_layer* L, llmoc_ep_transport* tr, const uint16_t* X, int T,
+                                 uint16_t* Y, uint32_t seq, void* workspace, size_t workspace_bytes, void* stream) {
+  llmoc_status rc = p2p_check(L, tr, T, seq, workspace_bytes, workspace);
+  if (rc != LLMOC_OK) return rc;
+  if (T > 0 && (!X || !Y)) return fails(LLMOC_ERR_INVALID, "bad arguments");
+  const EpP2PWs w = ep_p2p_ws(L, tr, T);
+  char* ws = (char*)workspace;
+  DevGuard dg(L->device);
+  if (!cuda_ok(launch_ep_wait(tr->lay, tr->base, 1, seq, tr->err, (cudaStream_t)stream), "ep wait back"))
+    return LLMOC_ERR_CUDA;
+  count_launch(1);
+  const uint16_t* ret = (const uint16_t*)(tr->base + tr->lay.ret_rows + (size_t)(seq & 1) * tr->lay.cap * tr->lay.row_bytes);
+  return llmoc_moe_ep_combine(L, X, T, ret, Y, ws + w.src, w.sw.total, stream);
 }
 
 }  // extern "C"

@@ -19,6 +19,12 @@ layer step:
 `DeviceBackend` runs 1, 3 and 5 through the C ABI (llmoc_moe_ep_*); any
 object with the same three methods can stand in (the CPU tests use one built
 on the oracle).
+
+`P2PStep` runs the same step with the library's own NVLink transport
+(llmoc_ep_p2p_*): rows are stored straight into the owners' receive buffers
+(CUDA IPC peer pointers) and flagged per step, so the step has no host
+synchronisation and no library collective; torch.distributed only exchanges
+the IPC handles once.
 """
 from __future__ import annotations
 
@@ -152,3 +158,75 @@ class DeviceBackend:
         Y = torch.empty((T, self.H), dtype=torch.bfloat16, device=X.device)
         self.shard.combine(X, T, ret_rows, Y, self._src["ws"], self._src["wsb"], self._stream())
         return Y
+
+
+class P2PStep:
+    """The expert-parallel layer step over the NVLink transport.
+
+    `shard` is this rank's llmoc_b200.EpLayerShard, `transport` its
+    llmoc_b200.EpTransport (connected: connect_p2p below, or
+    EpTransport.connect_local for ranks of one process).  Each call of
+    `forward` is one step (the sequence number advances); every rank calls it
+    the same number of times."""
+
+    def __init__(self, shard, transport, H: int, stream: Optional[torch.cuda.Stream] = None):
+        self.shard, self.tr, self.H = shard, transport, H
+        self.stream = stream
+        self.seq = 0
+        self.ws = None
+        self.wsb = 0
+
+    def _stream(self):
+        return self.stream if self.stream is not None else torch.cuda.current_stream()
+
+    def _ws(self, T, dev):
+        need = self.tr.workspace_bytes(self.shard, T)
+        if self.ws is None or self.ws.numel() < need:
+            self.ws = torch.empty(need, dtype=torch.uint8, device=dev)
+        self.wsb = self.ws.numel()
+
+    def send(self, X, T):
+        self.seq += 1
+        self._ws(self.tr.max_tokens, X.device)
+        self.tr.send(self.shard, X, T, self.seq, self.ws, self.wsb, self._stream())
+
+    def serve(self, T):
+        self.tr.serve(self.shard, T, self.seq, self.ws, self.wsb, self._stream())
+
+    def finish(self, X, T, Y=None):
+        if Y is None:
+            Y = torch.empty((T, self.H), dtype=torch.bfloat16, device=X.device)
+        self.tr.finish(self.shard, X, T, Y, self.seq, self.ws, self.wsb, self._stream())
+        return Y
+
+    def forward(self, X, T, times: Optional[EpTimes] = None):
+        timed = times is not None
+        mk = _Marks(timed)
+        mk.mark()
+        self.send(X, T)
+        mk.mark()
+        self.serve(T)
+        mk.mark()
+        Y = self.finish(X, T)
+        mk.mark()
+        if timed:
+            torch.cuda.current_stream().synchronize()
+            e = mk.ev
+            times.dispatch_ms = e[0].elapsed_time(e[1])   # route + dispatch + push to the owners
+            times.experts_ms = e[1].elapsed_time(e[2])    # wait for the sources + experts + push back
+            times.combine_ms = e[2].elapsed_time(e[3])    # wait for the owners + combine
+            times.a2a_ms = 0.0                            # inside the three phases (peer stores)
+        return Y
+
+
+def connect_p2p(transport, group=None) -> None:
+    """Exchange the ranks' IPC handles (one all-gather) and open the peers."""
+    import llmoc_b200 as L
+
+    nb = int(L.lib.llmoc_ep_ipc_handle_bytes())
+    dev = torch.device("cuda", torch.cuda.current_device()) if dist.get_backend(group) == "nccl" else "cpu"
+    mine = torch.frombuffer(bytearray(bytes(transport.ipc)), dtype=torch.uint8).to(dev)
+    allh = [torch.empty(nb, dtype=torch.uint8, device=dev) for _ in range(transport.world)]
+    dist.all_gather(allh, mine, group=group)
+    transport.connect(b"".join(bytes(h.cpu().numpy().tobytes()) for h in allh))
+    dist.barrier(group=group)

@@ -105,6 +105,16 @@ _SIGS = {
     "llmoc_moe_ep_dispatch": (_i, [_vp, _vp, _i, _vp, _sz, _vp, _vp, _vp, _vp]),
     "llmoc_moe_ep_experts": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _sz, _vp]),
     "llmoc_moe_ep_combine": (_i, [_vp, _vp, _i, _vp, _vp, _vp, _sz, _vp]),
+    "llmoc_ep_ipc_handle_bytes": (_sz, []),
+    "llmoc_ep_transport_create": (_i, [_i, _i, _i, _i, _i, _i, C.POINTER(_vp), _vp]),
+    "llmoc_ep_transport_connect": (_i, [_vp, _vp]),
+    "llmoc_ep_transport_connect_local": (_i, [_vp, C.POINTER(_vp)]),
+    "llmoc_ep_transport_destroy": (None, [_vp]),
+    "llmoc_ep_transport_error": (_i, [_vp]),
+    "llmoc_ep_p2p_workspace_bytes": (_sz, [_vp, _vp, _i]),
+    "llmoc_ep_p2p_send": (_i, [_vp, _vp, _vp, _i, C.c_uint32, _vp, _sz, _vp]),
+    "llmoc_ep_p2p_serve": (_i, [_vp, _vp, _i, C.c_uint32, _vp, _sz, _vp]),
+    "llmoc_ep_p2p_finish": (_i, [_vp, _vp, _vp, _i, _vp, C.c_uint32, _vp, _sz, _vp]),
 }
 for _name, (_res, _args) in _SIGS.items():
     _fn = getattr(lib, _name)
@@ -321,3 +331,55 @@ class EpLayerShard(MoeLayer):
     def combine(self, X, T, ret_rows, Y, ws, ws_bytes, stream=None) -> None:
         check(lib.llmoc_moe_ep_combine(self.handle, ptr(X), T, ptr(ret_rows), ptr(Y), ptr(ws), ws_bytes,
                                        stream_ptr(stream)), "llmoc_moe_ep_combine")
+
+
+class EpTransport:
+    """This rank's end of the NVLink expert-parallel transport
+    (llmoc_ep_transport_*): buffers for `world` ranks of a layer with `hidden`
+    and `topk`, up to max_tokens tokens per rank and step."""
+
+    def __init__(self, world: int, rank: int, hidden: int, max_tokens: int, topk: int, device: int = 0,
+                 export: bool = True):
+        self.world, self.rank, self.max_tokens = world, rank, max_tokens
+        h = C.c_void_p()
+        self.ipc = (C.c_char * int(lib.llmoc_ep_ipc_handle_bytes()))() if export else None
+        check(lib.llmoc_ep_transport_create(world, rank, hidden, max_tokens, topk, device, C.byref(h),
+                                            C.cast(self.ipc, C.c_void_p) if export else None),
+              "llmoc_ep_transport_create")
+        self.handle = h.value
+        self.seq = 0
+
+    def connect(self, handles: bytes) -> None:
+        """handles: every rank's IPC handle, in rank order."""
+        buf = C.create_string_buffer(handles, len(handles))
+        check(lib.llmoc_ep_transport_connect(self.handle, C.cast(buf, C.c_void_p)), "llmoc_ep_transport_connect")
+
+    @staticmethod
+    def connect_local(transports) -> None:
+        """Every rank of the world in this process (tests)."""
+        arr = (C.c_void_p * len(transports))(*[t.handle for t in transports])
+        for t in transports:
+            check(lib.llmoc_ep_transport_connect_local(t.handle, arr), "llmoc_ep_transport_connect_local")
+
+    def error(self) -> int:
+        return int(lib.llmoc_ep_transport_error(self.handle))
+
+    def workspace_bytes(self, shard, T: int) -> int:
+        return int(lib.llmoc_ep_p2p_workspace_bytes(shard.handle, self.handle, T))
+
+    def send(self, shard, X, T: int, seq: int, ws, ws_bytes: int, stream=None) -> None:
+        check(lib.llmoc_ep_p2p_send(shard.handle, self.handle, ptr(X), T, seq, ptr(ws), ws_bytes,
+                                    stream_ptr(stream)), "llmoc_ep_p2p_send")
+
+    def serve(self, shard, T: int, seq: int, ws, ws_bytes: int, stream=None) -> None:
+        check(lib.llmoc_ep_p2p_serve(shard.handle, self.handle, T, seq, ptr(ws), ws_bytes, stream_ptr(stream)),
+              "llmoc_ep_p2p_serve")
+
+    def finish(self, shard, X, T: int, Y, seq: int, ws, ws_bytes: int, stream=None) -> None:
+        check(lib.llmoc_ep_p2p_finish(shard.handle, self.handle, ptr(X), T, ptr(Y), seq, ptr(ws), ws_bytes,
+                                      stream_ptr(stream)), "llmoc_ep_p2p_finish")
+
+    def close(self) -> None:
+        if self.handle:
+            lib.llmoc_ep_transport_destroy(self.handle)
+            self.handle = None

@@ -2,8 +2,10 @@
 
 Two shards of one layer on one GPU with the all-to-all done by hand (the
 kernels of world = 2 without a second GPU), world = 1 against the plain
-forward, and, where the box has two GPUs, two NCCL ranks running
-ep.ep_forward.  Each rank's output is checked against the fp32 oracle of the
+forward, the NVLink transport (llmoc_ep_p2p_*) with two ranks in one process
+on one GPU (every wait already satisfied in stream order), and, where the box
+has two GPUs, two ranks running ep.ep_forward over NCCL and two running the
+NVLink transport.  Each rank's output is checked against the fp32 oracle of the
 whole layer on that rank's tokens (bf16 output bar: normwise max relative
 error 1e-2, cosine 0.9999)."""
 import datetime
@@ -115,6 +117,57 @@ def test_shard_refuses_the_single_gpu_forward(oracle):
     s.close()
 
 
+def _p2p_emulated(layer, world, Xs, steps):
+    """`steps` layer steps of every rank through the NVLink transport in one
+    process: sends, then serves, then finishes, all on one stream."""
+    shards = [L.EpLayerShard.from_host_ep(layer, r, world) for r in range(world)]
+    Tmax = max(X.shape[0] for X in Xs)
+    trs = [L.EpTransport(world, r, layer.H, Tmax, layer.topk, 0, export=False) for r in range(world)]
+    L.EpTransport.connect_local(trs)
+    st = [ep.P2PStep(shards[r], trs[r], layer.H) for r in range(world)]
+    outs = []
+    for _ in range(steps):
+        for r in range(world):
+            st[r].send(Xs[r], Xs[r].shape[0])
+        for r in range(world):
+            st[r].serve(Xs[r].shape[0])
+        Ys = [st[r].finish(Xs[r], Xs[r].shape[0]) for r in range(world)]
+        torch.cuda.synchronize()
+        outs.append(Ys)
+    errs = [t.error() for t in trs]
+    for t in trs:
+        t.close()
+    for s in shards:
+        s.close()
+    return outs, errs
+
+
+@pytest.mark.parametrize("name", list(CFGS))
+@pytest.mark.parametrize("T", [5, 40, 200])
+def test_p2p_transport_two_ranks_one_gpu(oracle, name, T):
+    """The NVLink transport's kernels for world = 2 (receive slots per source,
+    empty-slot marking, return to the send offsets, double-buffered parities):
+    three steps, each rank's output against the oracle, and every step's
+    output bitwise equal to the first (the parities alternate)."""
+    layer = orc.make_layer(oracle, np.random.default_rng(3), **CFGS[name])
+    Xh = [orc.make_tokens(np.random.default_rng(50 + r), T + 3 * r, layer.H) for r in range(2)]
+    outs, errs = _p2p_emulated(layer, 2, [G.bf16_dev(X) for X in Xh], 3)
+    assert errs == [0, 0]
+    for r in range(2):
+        _check(outs[0][r], oracle.moe_layer_forward(layer, Xh[r])[0], (name, T, r))
+        for k in (1, 2):
+            assert torch.equal(outs[k][r], outs[0][r]), (name, T, r, k)
+
+
+def test_p2p_transport_world_one(oracle):
+    """world = 1: the transport loops back to the rank itself."""
+    layer = orc.make_layer(oracle, np.random.default_rng(8), **CFGS["glm_like_shared_sigmoid"])
+    X = orc.make_tokens(np.random.default_rng(11), 24, layer.H)
+    outs, errs = _p2p_emulated(layer, 1, [G.bf16_dev(X)], 2)
+    assert errs == [0]
+    _check(outs[1][0], oracle.moe_layer_forward(layer, X)[0], "world1")
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -164,4 +217,54 @@ def test_two_nccl_ranks(name):
         p.join(timeout=60)
     for rank, mre, cos in res:
         assert cos is not None, (rank, mre)
+        assert mre <= G.MAX_REL and cos >= G.MIN_COS, (rank, mre, cos)
+
+
+def _p2p_worker(rank, world, port, name, T, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        torch.cuda.set_device(rank)
+        dist = torch.distributed
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", rank))
+        oracle = orc.Oracle()
+        layer = orc.make_layer(oracle, np.random.default_rng(3), **CFGS[name])
+        shard = L.EpLayerShard.from_host_ep(layer, rank, world, device=rank)
+        tr = L.EpTransport(world, rank, layer.H, T + world, layer.topk, rank)
+        ep.connect_p2p(tr)
+        step = ep.P2PStep(shard, tr, layer.H)
+        Xh = orc.make_tokens(np.random.default_rng(70 + rank), T + rank, layer.H)
+        X = G.bf16_dev(Xh).to(f"cuda:{rank}")
+        Ys = [step.forward(X, X.shape[0]) for _ in range(3)]
+        torch.cuda.synchronize()
+        err = tr.error()
+        same = all(torch.equal(Ys[0], y) for y in Ys[1:])
+        mre, cos = G.quality(G.bf16_to_f32(Ys[-1]), oracle.moe_layer_forward(layer, Xh)[0])
+        q.put((rank, mre, cos, err, same))
+        dist.barrier()
+        tr.close()
+        dist.destroy_process_group()
+        shard.close()
+    except Exception as e:
+        q.put((rank, repr(e), None, None, None))
+
+
+@pytest.mark.parametrize("name", ["qwen_like", "kimi_like_gs32"])
+def test_p2p_transport_two_gpus(name):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_p2p_worker, args=(r, 2, port, name, 33, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = [q.get(timeout=300) for _ in range(2)]
+    for p in ps:
+        p.join(timeout=60)
+    for rank, mre, cos, err, same in res:
+        assert cos is not None, (rank, mre)
+        assert err == 0 and same, (rank, err, same)
         assert mre <= G.MAX_REL and cos >= G.MIN_COS, (rank, mre, cos)
