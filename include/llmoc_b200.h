@@ -299,10 +299,11 @@ LLMOC_API llmoc_status llmoc_moe_ep_combine(const llmoc_moe_layer* layer, const 
  * a per-source sequence flag there, and the owners push the expert outputs
  * back the same way.  The step needs no host synchronisation and no library
  * collective:
- *   llmoc_ep_p2p_send    dispatch (as llmoc_moe_ep_dispatch) + push the rows
+ *   llmoc_ep_p2p_send    dispatch (as llmoc_moe_ep_dispatch) + push the rows,
+ *                        then the shared expert of the rank's tokens
  *   llmoc_ep_p2p_serve   wait for every source, grouped expert FFN over the
  *                        received rows, push the outputs back
- *   llmoc_ep_p2p_finish  wait for every owner, combine (+ shared expert)
+ *   llmoc_ep_p2p_finish  wait for every owner, combine (+ the shared expert's rows)
  * all asynchronous on `stream`; every rank calls the three in this order with
  * the same seq = 1, 2, 3, ... (one per layer step).  Waits are bounded
  * (~1 s): a wait that gives up sets bit 1 of llmoc_ep_transport_error and the

@@ -153,21 +153,37 @@ __global__ void __launch_bounds__(256) k_ep_wait(EpP2PLayout L, char* base, int 
   }
 }
 
-// Owner side: out rows in the padded receive order ([world][cap]) go back to
+// Owner side: the down GEMM's fp32 output rows (in expert-sorted order;
+// inverse[q] = row of receive slot q) rounded to bf16 and stored straight into
 // each source's return buffer at its send offsets; then each source's flag.
 __global__ void __launch_bounds__(256) k_ep_push_return(EpP2PLayout L, char* const* peers, char* base,
-                                                        const uint4* __restrict__ out_rows, int rank, uint32_t seq,
+                                                        const float* __restrict__ partial,
+                                                        const int* __restrict__ inverse, int rank, uint32_t seq,
                                                         int* ctr) {
   const int parity = seq & 1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  const int n16 = L.row_bytes / 16;
+  const int n16 = L.row_bytes / 16, H = L.row_bytes / 2;
   for (int q = blockIdx.x * nw + warp; q < L.world * L.cap; q += gridDim.x * nw) {
     const int s = q / L.cap, i = q % L.cap;
     const int2 m = *meta_at(base, L, parity, s);
     // a source's rows: count m.x at offset m.y of its send order (both within
     // cap unless a wait gave up; then nothing of this step is pushed outside)
     if (i >= m.x || m.x > L.cap || m.y < 0 || m.y + m.x > L.cap) continue;
-    copy_row(ret_at(peers[s], L, parity) + (size_t)(m.y + i) * n16, out_rows + (size_t)q * n16, n16, lane);
+    const int src = inverse[q];
+    if (src < 0) continue;
+    const float4* row = reinterpret_cast<const float4*>(partial + (size_t)src * H);
+    uint4* dst = ret_at(peers[s], L, parity) + (size_t)(m.y + i) * n16;
+    for (int c = lane; c < n16; c += 32) {  // 8 values per 16-byte store
+      const float4 a = row[2 * c], b = row[2 * c + 1];
+      const __nv_bfloat162 p0 = __floats2bfloat162_rn(a.x, a.y), p1 = __floats2bfloat162_rn(a.z, a.w);
+      const __nv_bfloat162 p2 = __floats2bfloat162_rn(b.x, b.y), p3 = __floats2bfloat162_rn(b.z, b.w);
+      uint4 v;
+      v.x = *reinterpret_cast<const uint32_t*>(&p0);
+      v.y = *reinterpret_cast<const uint32_t*>(&p1);
+      v.z = *reinterpret_cast<const uint32_t*>(&p2);
+      v.w = *reinterpret_cast<const uint32_t*>(&p3);
+      dst[c] = v;
+    }
   }
   if (!last_cta(ctr)) return;
   __threadfence_system();
@@ -187,10 +203,9 @@ cudaError_t launch_ep_wait(const EpP2PLayout& L, char* base, int kind, uint32_t 
   k_ep_wait<<<1, 256, 0, st>>>(L, base, kind, seq, err);
   return cudaGetLastError();
 }
-cudaError_t launch_ep_push_return(const EpP2PLayout& L, char* const* peers, char* base, const void* out_rows, int rank,
-                                  uint32_t seq, int* ctr, cudaStream_t st) {
-  k_ep_push_return<<<kEpPushCtas, 256, 0, st>>>(L, peers, base, reinterpret_cast<const uint4*>(out_rows), rank, seq,
-                                                 ctr);
+cudaError_t launch_ep_push_return(const EpP2PLayout& L, char* const* peers, char* base, const float* partial,
+                                  const int* inverse, int rank, uint32_t seq, int* ctr, cudaStream_t st) {
+  k_ep_push_return<<<kEpPushCtas, 256, 0, st>>>(L, peers, base, partial, inverse, rank, seq, ctr);
   return cudaGetLastError();
 }
 

@@ -41,9 +41,18 @@ cudaError_t launch_router_logits(const void* X, bool x_is_f32, const uint16_t* W
                                  int H, float* logits, cudaStream_t st);
 cudaError_t launch_topk(const TopkArgs& a, cudaStream_t st);
 cudaError_t launch_permute(const PermArgs& a, cudaStream_t st);
-// top-k and permutation in one CTA (decode-size T; pa.ids must be ta.ids)
+// top-k and permutation in one CTA (decode-size T; pa.ids must be ta.ids, or,
+// for the expert-parallel dispatch, ea.key: the permutation then runs over the
+// owner keys, and the per-owner counts and owner-local experts are written)
 constexpr int kFusedRouteMaxT = 16;
-cudaError_t launch_topk_permute(const TopkArgs& ta, const PermArgs& pa, cudaStream_t st);
+struct EpRouteArgs {
+  int world = 1, e_loc = 0;
+  int* key = nullptr;          // [n] owner key of each pair (null: not expert-parallel)
+  int* counts = nullptr;       // [world]
+  int* send_expert = nullptr;  // [n] owner-local expert of each pair in key order
+};
+cudaError_t launch_topk_permute(const TopkArgs& ta, const PermArgs& pa, cudaStream_t st,
+                                const EpRouteArgs& ea = EpRouteArgs{});
 // expert parallelism (owner of expert e = rank e % world, local id e / world)
 cudaError_t launch_ep_keys(const int* ids, int n, int world, int e_loc, int* key, cudaStream_t st);
 cudaError_t launch_ep_meta(const int* offsets, const int* sorted, const int* key, int n, int world, int e_loc,
@@ -64,8 +73,9 @@ cudaError_t launch_ep_push_dispatch(const EpP2PLayout& L, char* const* peers, co
                                     const int* send_expert, const int* counts, int rank, uint32_t seq, int* ctr,
                                     cudaStream_t st);
 cudaError_t launch_ep_wait(const EpP2PLayout& L, char* base, int kind, uint32_t seq, int* err, cudaStream_t st);
-cudaError_t launch_ep_push_return(const EpP2PLayout& L, char* const* peers, char* base, const void* out_rows, int rank,
-                                  uint32_t seq, int* ctr, cudaStream_t st);
+// partial: the owner's down output rows (fp32, expert-sorted), inverse: row of each receive slot
+cudaError_t launch_ep_push_return(const EpP2PLayout& L, char* const* peers, char* base, const float* partial,
+                                  const int* inverse, int rank, uint32_t seq, int* ctr, cudaStream_t st);
 
 // ---- int4_gemm.cu
 struct RepackArgs {

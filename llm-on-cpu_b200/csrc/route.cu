@@ -559,14 +559,31 @@ __global__ void __launch_bounds__(kPermThreads) k_permute(PermArgs a) {
 // Decode-size batches: top-k of every token (warp w takes tokens w, w + 32,
 // ...) and the permutation in one CTA, saving a launch and a pass over the
 // ids.  Shared memory: kPermWarps x n_exp ints (the permutation's counts).
-__global__ void __launch_bounds__(kPermThreads) k_topk_permute(TopkArgs ta, PermArgs pa) {
+// Expert-parallel dispatch (ea.key != null): the permutation runs over the
+// owner keys (e % world) * e_loc + e / world of the ids, and the per-owner
+// counts and owner-local expert of each pair in key order follow (what
+// k_ep_keys and k_ep_meta do for larger T).
+__global__ void __launch_bounds__(kPermThreads) k_topk_permute(TopkArgs ta, PermArgs pa, EpRouteArgs ea) {
   extern __shared__ int fsm[];
   grid_dep_wait();
   grid_dep_release();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int t = warp; t < ta.T; t += kPermWarps) topk_token(ta, t, lane);
   __syncthreads();  // the ids written above are visible to the whole CTA
+  if (ea.key) {
+    for (int p = threadIdx.x; p < pa.n; p += kPermThreads) {
+      const int e = ta.ids[p];
+      ea.key[p] = (e % ea.world) * ea.e_loc + e / ea.world;
+    }
+    __syncthreads();
+  }
   permute_block(pa, fsm);
+  if (ea.key) {
+    __syncthreads();  // offsets and sorted complete
+    for (int r = threadIdx.x; r < ea.world; r += kPermThreads)
+      ea.counts[r] = pa.offsets[(r + 1) * ea.e_loc] - pa.offsets[r * ea.e_loc];
+    for (int q = threadIdx.x; q < pa.n; q += kPermThreads) ea.send_expert[q] = ea.key[pa.sorted[q]] % ea.e_loc;
+  }
 }
 
 // ---------------------------------------------------------------- launch
@@ -621,12 +638,12 @@ cudaError_t launch_topk(const TopkArgs& a, cudaStream_t st) {
   return launch_pdl(k_topk, dim3((a.T + 7) / 8), dim3(256), 0, st, a);
 }
 
-cudaError_t launch_topk_permute(const TopkArgs& ta, const PermArgs& pa, cudaStream_t st) {
+cudaError_t launch_topk_permute(const TopkArgs& ta, const PermArgs& pa, cudaStream_t st, const EpRouteArgs& ea) {
   if (ta.E > 32 * kTopkSlots || ta.k > 64) return cudaErrorInvalidValue;
   const size_t smem = (size_t)kPermWarps * pa.n_exp * sizeof(int);
   cudaError_t e = cudaFuncSetAttribute(k_topk_permute, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  return launch_pdl(k_topk_permute, dim3(1), dim3(kPermThreads), smem, st, ta, pa);
+  return launch_pdl(k_topk_permute, dim3(1), dim3(kPermThreads), smem, st, ta, pa, ea);
 }
 
 cudaError_t launch_permute(const PermArgs& a, cudaStream_t st) {

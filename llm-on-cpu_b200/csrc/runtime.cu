@@ -799,9 +799,9 @@ size_t ep_owner_bytes(const llmoc_moe_layer* L, int rows) {
 
 // Workspace of one NVLink expert-parallel step on a rank: the source side
 // (routing, send rows, ids, counts) and the owner side (the grouped run over
-// the padded receive slots and its output rows), used in the same step.
+// the padded receive slots), used in the same step.
 struct EpP2PWs {
-  size_t src, send_rows, send_expert, counts, own, out_rows, total;
+  size_t src, send_rows, send_expert, counts, own, total;
   EpSrcLayout sw;
 };
 EpP2PWs ep_p2p_ws(const llmoc_moe_layer* L, const llmoc_ep_transport* tr, int T);
@@ -836,7 +836,6 @@ EpP2PWs ep_p2p_ws(const llmoc_moe_layer* L, const llmoc_ep_transport* tr, int T)
   w.send_expert = take(n * 4);
   w.counts = take((size_t)tr->world * 4);
   w.own = take(ep_owner_bytes(L, (int)slots));
-  w.out_rows = take(slots * H * 2);
   w.total = o;
   return w;
 }
@@ -1332,9 +1331,7 @@ llmoc_status llmoc_moe_ep_dispatch(const llmoc_moe_layer* L, const uint16_t* X, 
   ta.has_shared = 0;
   ta.ids = (int*)(ws + w.ids);
   ta.weights = (float*)(ws + w.weights);
-  if (!cuda_ok(launch_topk(ta, st), "topk")) return LLMOC_ERR_CUDA;
   int* key = (int*)(ws + w.key);
-  if (!cuda_ok(launch_ep_keys(ta.ids, n, L->ep_world, L->e_loc, key, st), "ep keys")) return LLMOC_ERR_CUDA;
   PermArgs pa{};
   pa.ids = key;
   pa.n = n;
@@ -1347,12 +1344,26 @@ llmoc_status llmoc_moe_ep_dispatch(const llmoc_moe_layer* L, const uint16_t* X, 
   pa.n_active = (int*)(ws + w.n_active);
   pa.err = (int*)(ws + w.err);
   pa.chunk = 8;
-  if (!cuda_ok(launch_permute(pa, st), "permute")) return LLMOC_ERR_CUDA;
-  if (!cuda_ok(launch_ep_meta(pa.offsets, pa.sorted, key, n, L->ep_world, L->e_loc, send_counts, send_expert, st),
-               "ep meta") ||
-      !cuda_ok(launch_gather_rows(X, H, pa.sorted, k, n, nullptr, send_rows, st), "gather"))
-    return LLMOC_ERR_CUDA;
-  count_launch(6);
+  if (T <= kFusedRouteMaxT && E <= kMaxExpPerm) {  // one CTA: top-k, owner keys, permutation, per-owner meta
+    EpRouteArgs ea;
+    ea.world = L->ep_world;
+    ea.e_loc = L->e_loc;
+    ea.key = key;
+    ea.counts = send_counts;
+    ea.send_expert = send_expert;
+    if (!cuda_ok(launch_topk_permute(ta, pa, st, ea), "topk+permute")) return LLMOC_ERR_CUDA;
+    count_launch(2);
+  } else {
+    if (!cuda_ok(launch_topk(ta, st), "topk") ||
+        !cuda_ok(launch_ep_keys(ta.ids, n, L->ep_world, L->e_loc, key, st), "ep keys") ||
+        !cuda_ok(launch_permute(pa, st), "permute") ||
+        !cuda_ok(launch_ep_meta(pa.offsets, pa.sorted, key, n, L->ep_world, L->e_loc, send_counts, send_expert, st),
+                 "ep meta"))
+      return LLMOC_ERR_CUDA;
+    count_launch(5);
+  }
+  if (!cuda_ok(launch_gather_rows(X, H, pa.sorted, k, n, nullptr, send_rows, st), "gather")) return LLMOC_ERR_CUDA;
+  count_launch(1);
   return LLMOC_OK;
 }
 
@@ -1379,6 +1390,38 @@ llmoc_status llmoc_moe_ep_experts(const llmoc_moe_layer* L, const uint16_t* rows
   return ep_experts(L, rows, expert, n, n, out_rows, workspace, workspace_bytes, stream);
 }
 
+namespace {
+// The shared expert over the source rank's own T tokens, into the source
+// workspace (no-op without a shared expert).
+llmoc_status ep_shared(const llmoc_moe_layer* L, const uint16_t* X, int T, const EpSrcLayout& w, char* ws,
+                       cudaStream_t st) {
+  if (!L->d.has_shared || T == 0) return LLMOC_OK;
+  char* s2 = ws + w.sh;
+  int* ids = (int*)(s2 + w.shl.ids);
+  if (!cuda_ok(launch_fill_i32(ids, T, L->e_loc, st), "fill")) return LLMOC_ERR_CUDA;
+  count_launch(1);
+  llmoc_status rc = run_permute(ids, T, L->n_exp, w.sh_chunk, w.shl, s2, st);
+  if (rc == LLMOC_OK) rc = run_ffn(L, X, T, 1, w.sh_chunk, w.shl, s2, nullptr, nullptr, st);
+  return rc;
+}
+// Y = the routed weights x the returned rows (slot order) + the shared expert's rows.
+llmoc_status ep_combine_rows(const llmoc_moe_layer* L, int T, const uint16_t* ret_rows, uint16_t* Y,
+                             const EpSrcLayout& w, char* ws, cudaStream_t st) {
+  const float* sh = nullptr;
+  const int* sh_inv = nullptr;
+  if (L->d.has_shared) {
+    sh = (const float*)(ws + w.sh + w.shl.partial);
+    sh_inv = (const int*)(ws + w.sh + w.shl.inverse);
+  }
+  if (!cuda_ok(launch_combine_ep(ret_rows, (const int*)(ws + w.inverse), (const float*)(ws + w.weights), T,
+                                 L->d.topk, L->d.hidden, sh, sh_inv, L->d.shared_scale, Y, st),
+               "combine"))
+    return LLMOC_ERR_CUDA;
+  count_launch(1);
+  return LLMOC_OK;
+}
+}  // namespace
+
 llmoc_status llmoc_moe_ep_combine(const llmoc_moe_layer* L, const uint16_t* X, int T, const uint16_t* ret_rows,
                                   uint16_t* Y, void* workspace, size_t workspace_bytes, void* stream) {
   if (!L || T < 0 || (T > 0 && (!X || !ret_rows || !Y))) return fails(LLMOC_ERR_INVALID, "bad arguments");
@@ -1388,25 +1431,9 @@ llmoc_status llmoc_moe_ep_combine(const llmoc_moe_layer* L, const uint16_t* X, i
   DevGuard dg(L->device);
   cudaStream_t st = (cudaStream_t)stream;
   char* ws = (char*)workspace;
-  const float* sh = nullptr;
-  const int* sh_inv = nullptr;
-  if (L->d.has_shared) {  // the shared expert over this rank's own tokens
-    char* s2 = ws + w.sh;
-    int* ids = (int*)(s2 + w.shl.ids);
-    if (!cuda_ok(launch_fill_i32(ids, T, L->e_loc, st), "fill")) return LLMOC_ERR_CUDA;
-    count_launch(1);
-    llmoc_status rc = run_permute(ids, T, L->n_exp, w.sh_chunk, w.shl, s2, st);
-    if (rc == LLMOC_OK) rc = run_ffn(L, X, T, 1, w.sh_chunk, w.shl, s2, nullptr, nullptr, st);
-    if (rc != LLMOC_OK) return rc;
-    sh = (const float*)(s2 + w.shl.partial);
-    sh_inv = (const int*)(s2 + w.shl.inverse);
-  }
-  if (!cuda_ok(launch_combine_ep(ret_rows, (const int*)(ws + w.inverse), (const float*)(ws + w.weights), T,
-                                 L->d.topk, L->d.hidden, sh, sh_inv, L->d.shared_scale, Y, st),
-               "combine"))
-    return LLMOC_ERR_CUDA;
-  count_launch(1);
-  return LLMOC_OK;
+  llmoc_status rc = ep_shared(L, X, T, w, ws, st);
+  if (rc != LLMOC_OK) return rc;
+  return ep_combine_rows(L, T, ret_rows, Y, w, ws, st);
 }
 
 // ------------------------------------------- NVLink expert-parallel transport
@@ -1555,7 +1582,8 @@ llmoc_status llmoc_ep_p2p_send(const llmoc_moe_layer* L, llmoc_ep_transport* tr,
                "ep push"))
     return LLMOC_ERR_CUDA;
   count_launch(1);
-  return LLMOC_OK;
+  // the shared expert of this rank's tokens while the rows travel (finish only combines)
+  return ep_shared(L, X, T, w.sw, ws + w.src, (cudaStream_t)stream);
 }
 
 llmoc_status llmoc_ep_p2p_serve(const llmoc_moe_layer* L, llmoc_ep_transport* tr, int T, uint32_t seq,
@@ -1572,10 +1600,14 @@ llmoc_status llmoc_ep_p2p_serve(const llmoc_moe_layer* L, llmoc_ep_transport* tr
   const uint16_t* rows =
       (const uint16_t*)(tr->base + tr->lay.recv_rows + (size_t)parity * slots * tr->lay.row_bytes);
   const int32_t* ids = (const int32_t*)(tr->base + tr->lay.recv_ids + (size_t)parity * slots * 4);
-  rc = ep_experts(L, rows, ids, slots, std::max(1, T * L->d.topk), (uint16_t*)(ws + w.out_rows), ws + w.own,
-                  ep_owner_bytes(L, slots), stream);
+  // the grouped FFN over the padded slots, without the output-row pass: the
+  // return push reads the down GEMM's fp32 rows through the inverse map
+  const int n_hint = std::max(1, T * L->d.topk);
+  rc = ep_experts(L, rows, ids, slots, n_hint, nullptr, ws + w.own, ep_owner_bytes(L, slots), stream);
   if (rc != LLMOC_OK) return rc;
-  if (!cuda_ok(launch_ep_push_return(tr->lay, tr->peers_dev, tr->base, ws + w.out_rows, tr->rank, seq, tr->ctr + 1, st),
+  const WsLayout wo = ws_layout_g(L, slots, 1, L->n_exp, chunk_for_rows(n_hint, L->e_loc), false);
+  if (!cuda_ok(launch_ep_push_return(tr->lay, tr->peers_dev, tr->base, (const float*)(ws + w.own + wo.partial),
+                                     (const int*)(ws + w.own + wo.inverse), tr->rank, seq, tr->ctr + 1, st),
                "ep push back"))
     return LLMOC_ERR_CUDA;
   count_launch(1);
@@ -1594,7 +1626,8 @@ llmoc_status llmoc_ep_p2p_finish(const llmoc_moe_layer* L, llmoc_ep_transport* t
     return LLMOC_ERR_CUDA;
   count_launch(1);
   const uint16_t* ret = (const uint16_t*)(tr->base + tr->lay.ret_rows + (size_t)(seq & 1) * tr->lay.cap * tr->lay.row_bytes);
-  return llmoc_moe_ep_combine(L, X, T, ret, Y, ws + w.src, w.sw.total, stream);
+  if (T == 0) return LLMOC_OK;
+  return ep_combine_rows(L, T, ret, Y, w.sw, ws + w.src, (cudaStream_t)stream);
 }
 
 }  // extern "C"
