@@ -175,6 +175,37 @@ LLMOC_API size_t llmoc_moe_layer_weight_bytes(const llmoc_moe_layer* layer);
 /* Bytes one expert streams per forward (src/moe/qlwc_expert_bytes.h:43-60). */
 LLMOC_API size_t llmoc_expert_storage_bytes(int H, int I, int group_size, int has_zeros);
 
+/* Per-token weight of the shared expert: sigmoid(gate_row . x) instead of the
+ * constant shared_scale (Qwen3.6-style shared_expert_gate, bf16 [hidden],
+ * host or device memory): the reference's `gemm_opt(normed,
+ * lp.shared_expert_gate)` + `sigmoid`
+ * (src/model/qwen3_6_moe_int4_model.cpp:365-371, :29).  The gate row joins the
+ * router GEMV (same summation order); the layer must have a shared expert.
+ * Works for single-GPU layers and expert-parallel shards. */
+LLMOC_API llmoc_status llmoc_moe_layer_set_shared_gate(llmoc_moe_layer* layer, const uint16_t* gate_row,
+                                                       int on_device);
+
+/* A layer straight from a QLWC v1 file, the reference's INT4 container
+ * (src/weights/qlwc_format.h; written by tools/quantize_int4.py): tensors
+ * `<prefix>layers.<layer>.mlp.experts.<e>.{gate,up,down}_proj.weight` (INT4),
+ * `.mlp.gate.weight` (bf16 router), optional `.mlp.shared_expert(s).*_proj`,
+ * `.mlp.shared_expert_gate.weight` and `.mlp.gate.e_score_correction_bias`
+ * (the names of src/model/qwen3_6_moe_int4_model.cpp:201 and
+ * src/model/moe_model.cpp:308-364).  Replaces the host-bank fill of
+ * QlwcExpertHostBanks::fill_from_qlwc (src/moe/host_banks.cpp:165-261): the
+ * experts are read once and uploaded to HBM, repacked. */
+typedef struct llmoc_qlwc_layer_info {
+  int32_t hidden, inter, n_experts, group_size, scheme;
+  int32_t has_router, has_shared, has_shared_gate, has_bias;
+} llmoc_qlwc_layer_info;
+LLMOC_API llmoc_status llmoc_qlwc_describe(const char* path, const char* prefix, int layer,
+                                           llmoc_qlwc_layer_info* out);
+/* desc gives what the file does not hold (topk, router kind, routed scaling,
+ * shared scale) and must agree with it on the rest (llmoc_qlwc_describe). */
+LLMOC_API llmoc_status llmoc_moe_layer_create_qlwc(const char* path, const char* prefix, int layer,
+                                                   const llmoc_moe_layer_desc* desc, int device,
+                                                   llmoc_moe_layer** out);
+
 /* Workspace (device memory the caller provides) for up to max_tokens tokens. */
 LLMOC_API size_t llmoc_moe_workspace_bytes(const llmoc_moe_layer* layer, int max_tokens);
 
@@ -196,7 +227,7 @@ LLMOC_API llmoc_status llmoc_moe_forward_residual(const llmoc_moe_layer* layer, 
 
 /* Routing results inside a workspace after llmoc_moe_forward / llmoc_moe_route
  * (device pointers; kk = topk + has_shared slots per token):
- *   logits [T,E] fp32; ids [T,kk] int32; weights [T,kk] fp32;
+ *   logits [T,E] fp32 ([T,E+1] with a shared gate: its logit last); ids [T,kk] int32; weights [T,kk] fp32;
  *   offsets [E+has_shared+1] int32; sorted [T*kk] int32 (= t*kk + j);
  *   inverse [T*kk] int32; n_active: number of experts with >= 1 pair;
  *   error_flag: 0, or bit 0 set when a bounded device-side wait gave up

@@ -107,6 +107,15 @@ __device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t
   return d;
 }
 
+// d = a * b (a fresh accumulator: no zeroing of d beforehand)
+__device__ __forceinline__ void mma_bf16_z(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+  const float z = 0.f;
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%10,%10,%10,%10};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(z));
+}
 __device__ __forceinline__ void mma_bf16(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
   asm volatile(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
@@ -565,13 +574,11 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma_p(GemmArgs a) {
 
   const uint32_t ones[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};
   const float bias = AWQ ? (float)(128 + a.zp) : 128.f;
-  float acc[NP][4], tmp[NP][2][4], xs[2][4];
+  float acc[NP][4], tmp[NP][2][4], xs[2][4];  // tmp, xs: a group's partial sums (started fresh)
 #pragma unroll
   for (int p = 0; p < NP; ++p)
 #pragma unroll
-    for (int r = 0; r < 4; ++r) acc[p][r] = tmp[p][0][r] = tmp[p][1][r] = 0.f;
-#pragma unroll
-  for (int r = 0; r < 4; ++r) xs[0][r] = xs[1][r] = 0.f;
+    for (int r = 0; r < 4; ++r) acc[p][r] = 0.f;
 
   int c_row0 = n_row0, c_nrows = n_nrows, c_rt = n_rt, done = 0, cs = 0;
   for (int i = 0;; ++i) {
@@ -607,9 +614,13 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma_p(GemmArgs a) {
 
 #pragma unroll
     for (int b = 0; b < 4; ++b) {  // 32-wide block b of the step
+      const bool fresh = b % GSB == 0;  // first block of a group: new partial sums
 #pragma unroll
       for (int kt = 0; kt < 2; ++kt) {
-        mma_bf16(xs[kt], ones, kt ? bv[b].z : bv[b].x, kt ? bv[b].w : bv[b].y);
+        if (fresh)
+          mma_bf16_z(xs[kt], ones, kt ? bv[b].z : bv[b].x, kt ? bv[b].w : bv[b].y);
+        else
+          mma_bf16(xs[kt], ones, kt ? bv[b].z : bv[b].x, kt ? bv[b].w : bv[b].y);
 #pragma unroll
         for (int p = 0; p < NP; ++p) {
           const uint4& q4 = wq[p][b >> 1];
@@ -617,7 +628,10 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma_p(GemmArgs a) {
           const uint32_t wd = wi == 0 ? q4.x : wi == 1 ? q4.y : wi == 2 ? q4.z : q4.w;
           uint32_t af[4];
           raw_word(wd, af);
-          mma_bf16(tmp[p][kt], af, kt ? bv[b].z : bv[b].x, kt ? bv[b].w : bv[b].y);
+          if (fresh)
+            mma_bf16_z(tmp[p][kt], af, kt ? bv[b].z : bv[b].x, kt ? bv[b].w : bv[b].y);
+          else
+            mma_bf16(tmp[p][kt], af, kt ? bv[b].z : bv[b].x, kt ? bv[b].w : bv[b].y);
         }
       }
       if ((b + 1) % GSB == 0) {  // group end
@@ -632,10 +646,7 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma_p(GemmArgs a) {
             const float v = __fmaf_rn(-bias, xs[0][r], pr);  // sum x*(q - zp)
             acc[p][r] = __fmaf_rn(v, sc[p][q][r >> 1], acc[p][r]);
             if (!AWQ) acc[p][r] = __fmaf_rn(zz[p][q][r >> 1], xs[0][r], acc[p][r]);
-            tmp[p][0][r] = tmp[p][1][r] = 0.f;
           }
-#pragma unroll
-        for (int r = 0; r < 4; ++r) xs[0][r] = xs[1][r] = 0.f;
       }
     }
 
@@ -1114,7 +1125,8 @@ cudaError_t launch_gemm(int mode, int path, const GemmArgs& a, int max_work, int
 // the same fmaf order as k_combine (routed j = 0..topk-1, then the shared slot).
 __global__ void k_combine_ep(const __nv_bfloat16* __restrict__ ret, const int* __restrict__ inverse,
                              const float* __restrict__ w, int T, int topk, int H, const float* __restrict__ sh,
-                             const int* __restrict__ sh_inv, float sh_scale, __nv_bfloat16* __restrict__ y) {
+                             const int* __restrict__ sh_inv, float sh_scale, const float* __restrict__ sh_w,
+                             __nv_bfloat16* __restrict__ y) {
   const int t = blockIdx.y;
   const int h = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
   if (t >= T || h >= H) return;
@@ -1124,20 +1136,22 @@ __global__ void k_combine_ep(const __nv_bfloat16* __restrict__ ret, const int* _
     const __nv_bfloat16* row = ret + (size_t)inverse[(size_t)t * topk + j] * H;
     for (int i = 0; i < 4 && h + i < H; ++i) acc[i] = __fmaf_rn(wj, __bfloat162float(row[h + i]), acc[i]);
   }
-  if (sh) {
+  if (sh) {  // sh_w: per-token weights of the shared expert (its sigmoid gate), else sh_scale
     const float* row = sh + (size_t)sh_inv[t] * H;
-    for (int i = 0; i < 4 && h + i < H; ++i) acc[i] = __fmaf_rn(sh_scale, row[h + i], acc[i]);
+    const float ss = sh_w ? sh_w[t] : sh_scale;
+    for (int i = 0; i < 4 && h + i < H; ++i) acc[i] = __fmaf_rn(ss, row[h + i], acc[i]);
   }
   for (int i = 0; i < 4 && h + i < H; ++i) y[(size_t)t * H + h + i] = __float2bfloat16_rn(acc[i]);
 }
 
 cudaError_t launch_combine_ep(const void* ret, const int* inverse, const float* w, int T, int topk, int H,
-                              const float* sh, const int* sh_inv, float sh_scale, void* y, cudaStream_t st) {
+                              const float* sh, const int* sh_inv, float sh_scale, const float* sh_w, void* y,
+                              cudaStream_t st) {
   if (T <= 0) return cudaSuccess;
   const int threads = 128;
   dim3 grid(((H + 3) / 4 + threads - 1) / threads, T);
   k_combine_ep<<<grid, threads, 0, st>>>((const __nv_bfloat16*)ret, inverse, w, T, topk, H, sh, sh_inv, sh_scale,
-                                         (__nv_bfloat16*)y);
+                                         sh_w, (__nv_bfloat16*)y);
   return cudaGetLastError();
 }
 

@@ -7,13 +7,16 @@ namespace llmoc {
 
 // ---- route.cu
 struct TopkArgs {
-  const float* logits;   // [T,E]
+  const float* logits;   // [T,ld]: E routed logits (+ the shared gate's at column E)
   const float* bias;     // [E] (sigmoid router)
   int T, E, k, kk;       // kk = k + has_shared
+  int ld = 0;            // logits row stride (0: E)
   int router;            // 0 softmax, 1 sigmoid+bias
   float routed_scaling;
   float shared_scale;
   int has_shared;
+  int shared_gate = 0;   // the shared expert's weight is sigmoid(logits[t][E]) per token
+  float* shared_w = nullptr;  // [T] per-token shared weights (expert-parallel source; may be null)
   int* ids;              // [T,kk]
   float* weights;        // [T,kk]
 };
@@ -58,8 +61,10 @@ cudaError_t launch_ep_keys(const int* ids, int n, int world, int e_loc, int* key
 cudaError_t launch_ep_meta(const int* offsets, const int* sorted, const int* key, int n, int world, int e_loc,
                            int* counts, int* send_expert, cudaStream_t st);
 cudaError_t launch_fill_i32(int* p, int n, int v, cudaStream_t st);
+// sh_w: per-token shared weights (null: sh_scale for every token)
 cudaError_t launch_combine_ep(const void* ret, const int* inverse, const float* w, int T, int topk, int H,
-                              const float* sh, const int* sh_inv, float sh_scale, void* y, cudaStream_t st);
+                              const float* sh, const int* sh_inv, float sh_scale, const float* sh_w, void* y,
+                              cudaStream_t st);
 
 // ---- ep_p2p.cu: expert-parallel transport over NVLink peer memory
 constexpr int kEpMaxWorld = 64;

@@ -299,7 +299,7 @@ __device__ __forceinline__ uint32_t key_code(float v) {
 constexpr int kTopkSlots = 16;  // E <= 512
 template <int Q>  // slots per lane: E <= 32 * Q
 __device__ __forceinline__ void topk_token_q(const TopkArgs& a, int t, int lane) {
-  const float* lg = a.logits + (size_t)t * a.E;
+  const float* lg = a.logits + (size_t)t * (a.ld > 0 ? a.ld : a.E);
   float key[Q], val[Q];
   if (a.router == 0) {
     // keys = logits; probabilities exp(l - max) (their rounding only reaches
@@ -416,9 +416,15 @@ __device__ __forceinline__ void topk_token_q(const TopkArgs& a, int t, int lane)
     for (int h = 0; h < 2; ++h)
       if (lane + 32 * h < a.k) w[lane + 32 * h] = __fmul_rn((float)(sv[h] / ws), a.routed_scaling);
   }
-  if (lane == 0 && a.has_shared) {
-    ids[a.k] = a.E;
-    w[a.k] = a.shared_scale;
+  if (lane == 0 && (a.has_shared || a.shared_w)) {
+    // the shared expert's weight: constant, or the reference's float sigmoid of
+    // its gate row's logit (qwen3_6_moe_int4_model.cpp:29, :365-371)
+    const float sw = a.shared_gate ? 1.f / (1.f + expf(-lg[a.E])) : a.shared_scale;
+    if (a.has_shared) {
+      ids[a.k] = a.E;
+      w[a.k] = sw;
+    }
+    if (a.shared_w) a.shared_w[t] = sw;
   }
 }
 

@@ -325,7 +325,8 @@ struct llmoc_moe_layer {
   ExpertDev* table = nullptr; // device [n_exp]
   void* wmaps = nullptr;      // device TMA maps of the weights (tcgen05 path), or null
   std::vector<ExpertDev> htable;
-  uint16_t* router_w = nullptr;
+  uint16_t* router_w = nullptr;   // device [E (+1: the shared expert's gate row, when set)][H] bf16
+  int shared_gate = 0;            // router_w holds the shared gate row (llmoc_moe_layer_set_shared_gate)
   float* bias = nullptr;
   // stage timing (llmoc_moe_set_stage_timing): 7 events per timed call
   bool timing = false;
@@ -390,7 +391,7 @@ WsLayout ws_layout_g(const llmoc_moe_layer* L, int T, int kk, int n_perm, int ch
     return at;
   };
   w.max_work = (int)(std::min<size_t>((size_t)n_perm, n) + (n + chunk - 1) / chunk);
-  w.logits = logits ? take((size_t)T * L->d.n_experts * 4) : 0;
+  w.logits = logits ? take((size_t)T * (L->d.n_experts + L->shared_gate) * 4) : 0;
   w.ids = take(n * 4);
   w.weights = take(n * 4);
   w.offsets = take((size_t)(n_perm + 1) * 4);
@@ -630,7 +631,7 @@ llmoc_status run_route(const llmoc_moe_layer* L, const uint16_t* X, int T, const
   const int E = L->d.n_experts, H = L->d.hidden;
   float* logits = (float*)(ws + w.logits);
   if (se) se->mark(st);
-  if (!cuda_ok(launch_router_logits(X, false, L->router_w, T, E, H, logits, st), "router"))
+  if (!cuda_ok(launch_router_logits(X, false, L->router_w, T, E + L->shared_gate, H, logits, st), "router"))
     return LLMOC_ERR_CUDA;
   if (se) se->mark(st);
   TopkArgs ta{};
@@ -644,6 +645,8 @@ llmoc_status run_route(const llmoc_moe_layer* L, const uint16_t* X, int T, const
   ta.routed_scaling = L->d.routed_scaling;
   ta.shared_scale = L->d.shared_scale;
   ta.has_shared = L->d.has_shared;
+  ta.ld = E + L->shared_gate;
+  ta.shared_gate = L->shared_gate;
   ta.ids = (int*)(ws + w.ids);
   ta.weights = (float*)(ws + w.weights);
   count_launch(1);
@@ -755,7 +758,7 @@ llmoc_status run_ffn(const llmoc_moe_layer* L, const uint16_t* X, int R, int kk,
 // (owner rank, owner-local expert, token, slot); then the shared expert's run
 // over the T tokens.
 struct EpSrcLayout {
-  size_t logits, ids, weights, key, offsets, sorted, inverse, work, n_work, n_active, err;
+  size_t logits, ids, weights, shw, key, offsets, sorted, inverse, work, n_work, n_active, err;
   size_t sh = 0;     // shared-expert grouped run (ws_layout_g with kk = 1)
   WsLayout shl{};
   int sh_chunk = 8;
@@ -772,9 +775,10 @@ EpSrcLayout ep_src_layout(const llmoc_moe_layer* L, int T) {
     return at;
   };
   const int max_work = (int)(std::min<size_t>((size_t)E, n) + (n + 7) / 8);
-  w.logits = take((size_t)T * E * 4);
+  w.logits = take((size_t)T * (E + L->shared_gate) * 4);
   w.ids = take(n * 4);
   w.weights = take(n * 4);
+  w.shw = take((size_t)T * 4);  // per-token shared weights (shared gate)
   w.key = take(n * 4);
   w.offsets = take((size_t)(E + 1) * 4);
   w.sorted = take(n * 4);
@@ -1226,6 +1230,25 @@ llmoc_status llmoc_moe_forward_residual(const llmoc_moe_layer* L, const uint16_t
   return moe_forward(L, X, T, R, Y, workspace, workspace_bytes, stream);
 }
 
+llmoc_status llmoc_moe_layer_set_shared_gate(llmoc_moe_layer* L, const uint16_t* gate_row, int on_device) {
+  if (!L || !gate_row) return fails(LLMOC_ERR_INVALID, "bad arguments");
+  if (!L->d.has_shared) return fails(LLMOC_ERR_INVALID, "the layer has no shared expert");
+  DevGuard dg(L->device);
+  const size_t E = (size_t)L->d.n_experts, H = (size_t)L->d.hidden;
+  uint16_t* nw = nullptr;
+  if (!cuda_ok(cudaMalloc((void**)&nw, (E + 1) * H * 2), "router alloc")) return LLMOC_ERR_NO_MEMORY;
+  if (!cuda_ok(cudaMemcpy(nw, L->router_w, E * H * 2, cudaMemcpyDeviceToDevice), "router copy") ||
+      !cuda_ok(cudaMemcpy(nw + E * H, gate_row, H * 2, on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice),
+               "gate row")) {
+    cudaFree(nw);
+    return LLMOC_ERR_CUDA;
+  }
+  cudaFree(L->router_w);
+  L->router_w = nw;
+  L->shared_gate = 1;
+  return LLMOC_OK;
+}
+
 llmoc_status llmoc_moe_dequant(const llmoc_moe_layer* L, int expert, int proj, float* out,
                                void* stream) {
   if (!L || !out || expert < 0 || expert >= L->n_exp || proj < 0 || proj > 2)
@@ -1317,7 +1340,8 @@ llmoc_status llmoc_moe_ep_dispatch(const llmoc_moe_layer* L, const uint16_t* X, 
     return LLMOC_OK;
   }
   float* logits = (float*)(ws + w.logits);
-  if (!cuda_ok(launch_router_logits(X, false, L->router_w, T, E, H, logits, st), "router")) return LLMOC_ERR_CUDA;
+  if (!cuda_ok(launch_router_logits(X, false, L->router_w, T, E + L->shared_gate, H, logits, st), "router"))
+    return LLMOC_ERR_CUDA;
   TopkArgs ta{};
   ta.logits = logits;
   ta.bias = L->bias;
@@ -1329,6 +1353,9 @@ llmoc_status llmoc_moe_ep_dispatch(const llmoc_moe_layer* L, const uint16_t* X, 
   ta.routed_scaling = L->d.routed_scaling;
   ta.shared_scale = L->d.shared_scale;
   ta.has_shared = 0;
+  ta.ld = E + L->shared_gate;
+  ta.shared_gate = L->shared_gate;
+  if (L->shared_gate) ta.shared_w = (float*)(ws + w.shw);  // for the combine at this source
   ta.ids = (int*)(ws + w.ids);
   ta.weights = (float*)(ws + w.weights);
   int* key = (int*)(ws + w.key);
@@ -1414,7 +1441,8 @@ llmoc_status ep_combine_rows(const llmoc_moe_layer* L, int T, const uint16_t* re
     sh_inv = (const int*)(ws + w.sh + w.shl.inverse);
   }
   if (!cuda_ok(launch_combine_ep(ret_rows, (const int*)(ws + w.inverse), (const float*)(ws + w.weights), T,
-                                 L->d.topk, L->d.hidden, sh, sh_inv, L->d.shared_scale, Y, st),
+                                 L->d.topk, L->d.hidden, sh, sh_inv, L->d.shared_scale,
+                                 L->shared_gate ? (const float*)(ws + w.shw) : nullptr, Y, st),
                "combine"))
     return LLMOC_ERR_CUDA;
   count_launch(1);
@@ -1434,6 +1462,266 @@ llmoc_status llmoc_moe_ep_combine(const llmoc_moe_layer* L, const uint16_t* X, i
   llmoc_status rc = ep_shared(L, X, T, w, ws, st);
   if (rc != LLMOC_OK) return rc;
   return ep_combine_rows(L, T, ret_rows, Y, w, ws, st);
+}
+
+// ------------------------------------------------------- QLWC file loader
+// The reference's INT4 container (src/weights/qlwc_format.h, .cpp:40-160):
+// preface = magic "QLW1", u32 version, u64 catalog length, u64 FNV-1a 64 of
+// the catalog; catalog (little-endian) = u32 scheme, u32 group size, u32 block
+// alignment, u64 tensor count, then per tensor: string name (u32 length +
+// bytes), u32 kind, u64 rank, rank x u64 dims, and for a passthrough tensor
+// u32 dtype (1 bf16, 2 f16), u64 offset, u64 bytes; for an INT4 tensor u32
+// group size, u64 q offset/bytes, u64 scales offset/bytes, u64 zeros
+// offset/bytes.  Tensor names follow the reference's model loaders
+// (src/model/qwen3_6_moe_int4_model.cpp:201, src/model/moe_model.cpp:308-364).
+
+namespace {
+struct QTensor {
+  std::string name;
+  uint32_t kind = 0, dtype = 0, gs = 0;
+  std::vector<uint64_t> shape;
+  uint64_t off = 0, nbytes = 0, q_off = 0, q_n = 0, s_off = 0, s_n = 0, z_off = 0, z_n = 0;
+};
+struct QFile {
+  uint32_t scheme = 0, gs = 0;
+  std::vector<QTensor> tensors;
+  const QTensor* find(const std::string& n) const {
+    for (const auto& t : tensors)
+      if (t.name == n) return &t;
+    return nullptr;
+  }
+};
+
+bool qlwc_read_header(FILE* f, QFile* q) {
+  unsigned char pre[24];
+  if (fread(pre, 1, 24, f) != 24 || memcmp(pre, "QLW1", 4) != 0) return fails(LLMOC_ERR_INVALID, "not a QLWC v1 file"), false;
+  uint32_t ver;
+  uint64_t clen, crc;
+  memcpy(&ver, pre + 4, 4);
+  memcpy(&clen, pre + 8, 8);
+  memcpy(&crc, pre + 16, 8);
+  if (ver != 1 || clen > (1ull << 32)) return fails(LLMOC_ERR_INVALID, "QLWC version or catalog size"), false;
+  std::vector<unsigned char> cat(clen);
+  if (fread(cat.data(), 1, clen, f) != clen) return fails(LLMOC_ERR_INVALID, "QLWC catalog truncated"), false;
+  uint64_t h = 14695981039346656037ull;
+  for (unsigned char c : cat) h = (h ^ c) * 1099511628211ull;
+  if (h != crc) return fails(LLMOC_ERR_INVALID, "QLWC catalog checksum"), false;
+  size_t p = 0;
+  bool ok = true;
+  auto u32 = [&]() -> uint32_t {
+    uint32_t v = 0;
+    if (p + 4 > cat.size()) ok = false;
+    else memcpy(&v, &cat[p], 4);
+    p += 4;
+    return v;
+  };
+  auto u64 = [&]() -> uint64_t {
+    uint64_t v = 0;
+    if (p + 8 > cat.size()) ok = false;
+    else memcpy(&v, &cat[p], 8);
+    p += 8;
+    return v;
+  };
+  q->scheme = u32();
+  q->gs = u32();
+  u32();  // block alignment
+  const uint64_t n = u64();
+  for (uint64_t i = 0; ok && i < n; ++i) {
+    QTensor t;
+    const uint32_t len = u32();
+    if (!ok || p + len > cat.size()) {
+      ok = false;
+      break;
+    }
+    t.name.assign(reinterpret_cast<const char*>(&cat[p]), len);
+    p += len;
+    t.kind = u32();
+    const uint64_t rank = u64();
+    for (uint64_t r = 0; ok && r < rank && r < 8; ++r) t.shape.push_back(u64());
+    if (t.kind == 0) {
+      t.dtype = u32();
+      t.off = u64();
+      t.nbytes = u64();
+    } else {
+      t.gs = u32();
+      t.q_off = u64();
+      t.q_n = u64();
+      t.s_off = u64();
+      t.s_n = u64();
+      t.z_off = u64();
+      t.z_n = u64();
+    }
+    q->tensors.push_back(std::move(t));
+  }
+  if (!ok) return fails(LLMOC_ERR_INVALID, "QLWC catalog malformed"), false;
+  return true;
+}
+
+bool qlwc_read(FILE* f, uint64_t off, uint64_t n, void* dst) {
+  if (n == 0) return true;
+  if (fseeko(f, (off_t)off, SEEK_SET) != 0 || fread(dst, 1, n, f) != n)
+    return fails(LLMOC_ERR_INVALID, "QLWC payload truncated"), false;
+  return true;
+}
+
+struct QLayerNames {
+  std::string base, shared, gate, bias, shared_gate;
+};
+QLayerNames qlwc_names(const char* prefix, int layer, const QFile& q) {
+  QLayerNames n;
+  n.base = std::string(prefix ? prefix : "") + "layers." + std::to_string(layer) + ".mlp.";
+  n.gate = n.base + "gate.weight";
+  n.bias = n.base + "gate.e_score_correction_bias";
+  n.shared = q.find(n.base + "shared_expert.gate_proj.weight") ? n.base + "shared_expert."
+                                                                 : n.base + "shared_experts.";
+  n.shared_gate = n.base + "shared_expert_gate.weight";
+  return n;
+}
+
+// An INT4 tensor's payloads must be exactly its packed nibbles (M x K/2
+// bytes), M x K/gs fp16 scales and, for GPTQ, as many fp16 zeros.
+bool qlwc_int4_sizes_ok(const QTensor& t, const QFile& q) {
+  if (t.kind != 1 || t.shape.size() != 2) return false;
+  const uint64_t M = t.shape[0], K = t.shape[1], gs = t.gs ? t.gs : q.gs;
+  if (M == 0 || K == 0 || gs == 0 || M > (1u << 30) || K > (1u << 30)) return false;
+  const uint64_t ng = (K + gs - 1) / gs;
+  return t.q_n == M * ((K + 1) / 2) && t.s_n == M * ng * 2 &&
+         t.z_n == (q.scheme == LLMOC_SCHEME_GPTQ_ASYM ? M * ng * 2 : 0);
+}
+
+llmoc_status qlwc_info(const QFile& q, const QLayerNames& nm, llmoc_qlwc_layer_info* out) {
+  *out = llmoc_qlwc_layer_info{};
+  const QTensor* g0 = q.find(nm.base + "experts.0.gate_proj.weight");
+  const QTensor* d0 = q.find(nm.base + "experts.0.down_proj.weight");
+  if (!g0 || !d0 || g0->kind != 1 || d0->kind != 1 || g0->shape.size() != 2)
+    return fails(LLMOC_ERR_INVALID, "no INT4 experts for this layer in the QLWC file");
+  int E = 0;
+  while (q.find(nm.base + "experts." + std::to_string(E) + ".gate_proj.weight")) ++E;
+  for (int e = 0; e <= E; ++e) {  // e == E: the shared expert, if any
+    const std::string b = e < E ? nm.base + "experts." + std::to_string(e) + "." : nm.shared;
+    if (e == E && !q.find(b + "gate_proj.weight")) break;
+    for (const char* pn : {"gate_proj.weight", "up_proj.weight", "down_proj.weight"}) {
+      const QTensor* t = q.find(b + pn);
+      if (!t || !qlwc_int4_sizes_ok(*t, q)) return fails(LLMOC_ERR_INVALID, "QLWC tensor missing or malformed: " + b + pn);
+    }
+  }
+  out->n_experts = E;
+  out->inter = (int)g0->shape[0];
+  out->hidden = (int)g0->shape[1];
+  out->group_size = (int)(g0->gs ? g0->gs : q.gs);
+  out->scheme = (int)q.scheme;
+  out->has_shared = q.find(nm.shared + "gate_proj.weight") != nullptr;
+  out->has_shared_gate = q.find(nm.shared_gate) != nullptr;
+  out->has_bias = q.find(nm.bias) != nullptr;
+  const QTensor* r = q.find(nm.gate);
+  out->has_router = r && r->kind == 0 && r->dtype == 1;
+  return LLMOC_OK;
+}
+
+float qlwc_half_to_f32(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+}  // namespace
+
+llmoc_status llmoc_qlwc_describe(const char* path, const char* prefix, int layer, llmoc_qlwc_layer_info* out) {
+  if (!path || !out || layer < 0) return fails(LLMOC_ERR_INVALID, "bad arguments");
+  FILE* f = fopen(path, "rb");
+  if (!f) return fails(LLMOC_ERR_INVALID, "cannot open the QLWC file");
+  QFile q;
+  const bool ok = qlwc_read_header(f, &q);
+  fclose(f);
+  if (!ok) return LLMOC_ERR_INVALID;
+  return qlwc_info(q, qlwc_names(prefix, layer, q), out);
+}
+
+llmoc_status llmoc_moe_layer_create_qlwc(const char* path, const char* prefix, int layer,
+                                         const llmoc_moe_layer_desc* desc, int device, llmoc_moe_layer** out) {
+  if (!path || !desc || !out || layer < 0) return fails(LLMOC_ERR_INVALID, "bad arguments");
+  *out = nullptr;
+  FILE* f = fopen(path, "rb");
+  if (!f) return fails(LLMOC_ERR_INVALID, "cannot open the QLWC file");
+  struct Closer {
+    FILE* f;
+    ~Closer() { fclose(f); }
+  } closer{f};
+  QFile q;
+  if (!qlwc_read_header(f, &q)) return LLMOC_ERR_INVALID;
+  const QLayerNames nm = qlwc_names(prefix, layer, q);
+  llmoc_qlwc_layer_info info;
+  llmoc_status rc = qlwc_info(q, nm, &info);
+  if (rc != LLMOC_OK) return rc;
+  if (!info.has_router) return fails(LLMOC_ERR_INVALID, "router (mlp.gate.weight, bf16) missing");
+  if (desc->hidden != info.hidden || desc->inter != info.inter || desc->n_experts != info.n_experts ||
+      desc->group_size != info.group_size || desc->scheme != info.scheme || desc->has_shared != info.has_shared)
+    return fails(LLMOC_ERR_INVALID, "layer desc disagrees with the QLWC file");
+  const int E = info.n_experts, H = info.hidden;
+  // host copies of every tensor the layer needs; views point into them until the upload returns
+  std::vector<std::vector<uint8_t>> blobs;
+  blobs.reserve((size_t)3 * 3 * (E + 1) + 4);
+  auto load = [&](uint64_t off, uint64_t n) -> const uint8_t* {
+    blobs.emplace_back(n);
+    if (!qlwc_read(f, off, n, blobs.back().data())) return nullptr;
+    return blobs.back().data();
+  };
+  std::vector<llmoc_int4_view> views;
+  auto add_view = [&](const std::string& name, std::vector<llmoc_int4_view>& dst) -> bool {
+    const QTensor* t = q.find(name);
+    if (!t || t->kind != 1 || t->shape.size() != 2) return fails(LLMOC_ERR_INVALID, "missing INT4 tensor " + name), false;
+    llmoc_int4_view v{};
+    v.M = (int)t->shape[0];
+    v.K = (int)t->shape[1];
+    v.group_size = (int)(t->gs ? t->gs : q.gs);
+    if (!qlwc_int4_sizes_ok(*t, q)) return fails(LLMOC_ERR_INVALID, "QLWC payload sizes of " + name), false;
+    v.scheme = q.scheme;
+    v.awq_zp = q.scheme == LLMOC_SCHEME_AWQ_SYM ? 7 : 0;  // the reference's local AWQ zero point
+    v.qweight = load(t->q_off, t->q_n);
+    v.scales = (const uint16_t*)load(t->s_off, t->s_n);
+    v.zeros = t->z_n ? (const uint16_t*)load(t->z_off, t->z_n) : nullptr;
+    if (!v.qweight || !v.scales || (t->z_n && !v.zeros)) return false;
+    dst.push_back(v);
+    return true;
+  };
+  for (int e = 0; e < E; ++e)
+    for (const char* pn : {"gate_proj.weight", "up_proj.weight", "down_proj.weight"})
+      if (!add_view(nm.base + "experts." + std::to_string(e) + "." + pn, views)) return LLMOC_ERR_INVALID;
+  std::vector<llmoc_int4_view> shared;
+  if (info.has_shared)
+    for (const char* pn : {"gate_proj.weight", "up_proj.weight", "down_proj.weight"})
+      if (!add_view(nm.shared + pn, shared)) return LLMOC_ERR_INVALID;
+  const QTensor* rt = q.find(nm.gate);
+  if (rt->nbytes != (uint64_t)E * H * 2) return fails(LLMOC_ERR_INVALID, "router shape");
+  const uint16_t* router = (const uint16_t*)load(rt->off, rt->nbytes);
+  if (!router) return LLMOC_ERR_INVALID;
+  std::vector<float> bias;
+  if (info.has_bias) {  // selection bias (16-bit passthrough) -> fp32
+    const QTensor* bt = q.find(nm.bias);
+    if (bt->kind != 0 || bt->nbytes != (uint64_t)E * 2) return fails(LLMOC_ERR_INVALID, "bias shape");
+    const uint16_t* b = (const uint16_t*)load(bt->off, bt->nbytes);
+    if (!b) return LLMOC_ERR_INVALID;
+    bias.resize(E);
+    for (int e = 0; e < E; ++e) {
+      if (bt->dtype == 2) {
+        bias[e] = qlwc_half_to_f32(b[e]);
+      } else {
+        const uint32_t u = (uint32_t)b[e] << 16;
+        memcpy(&bias[e], &u, 4);
+      }
+    }
+  }
+  llmoc_moe_layer* L = nullptr;
+  rc = layer_create(desc, router, bias.empty() ? nullptr : bias.data(), views.data(),
+                    info.has_shared ? shared.data() : nullptr, device, false, &L);
+  if (rc != LLMOC_OK) return rc;
+  if (info.has_shared && info.has_shared_gate) {
+    const QTensor* gt = q.find(nm.shared_gate);
+    const uint16_t* g = (gt->kind == 0 && gt->dtype == 1 && gt->nbytes == (uint64_t)H * 2)
+                            ? (const uint16_t*)load(gt->off, gt->nbytes) : nullptr;
+    rc = g ? llmoc_moe_layer_set_shared_gate(L, g, 0) : fails(LLMOC_ERR_INVALID, "shared expert gate shape");
+    if (rc != LLMOC_OK) {
+      llmoc_moe_layer_destroy(L);
+      return rc;
+    }
+  }
+  *out = L;
+  return LLMOC_OK;
 }
 
 // ------------------------------------------- NVLink expert-parallel transport

@@ -48,6 +48,12 @@ class LayerDesc(C.Structure):
                 ("has_shared", C.c_int32), ("shared_scale", C.c_float)]
 
 
+class QlwcLayerInfo(C.Structure):
+    _fields_ = [("hidden", C.c_int32), ("inter", C.c_int32), ("n_experts", C.c_int32),
+                ("group_size", C.c_int32), ("scheme", C.c_int32), ("has_router", C.c_int32),
+                ("has_shared", C.c_int32), ("has_shared_gate", C.c_int32), ("has_bias", C.c_int32)]
+
+
 class RouteViews(C.Structure):
     _fields_ = [("logits", C.c_void_p), ("ids", C.c_void_p), ("weights", C.c_void_p),
                 ("offsets", C.c_void_p), ("sorted", C.c_void_p), ("inverse", C.c_void_p),
@@ -88,6 +94,9 @@ _SIGS = {
     "llmoc_expert_storage_bytes": (_sz, [_i, _i, _i, _i]),
     "llmoc_moe_workspace_bytes": (_sz, [_vp, _i]),
     "llmoc_moe_forward": (_i, [_vp, _vp, _i, _vp, _vp, _sz, _vp]),
+    "llmoc_moe_layer_set_shared_gate": (_i, [_vp, _vp, _i]),
+    "llmoc_qlwc_describe": (_i, [C.c_char_p, C.c_char_p, _i, C.POINTER(QlwcLayerInfo)]),
+    "llmoc_moe_layer_create_qlwc": (_i, [C.c_char_p, C.c_char_p, _i, C.POINTER(LayerDesc), _i, C.POINTER(_vp)]),
     "llmoc_moe_forward_residual": (_i, [_vp, _vp, _i, _vp, _vp, _vp, _sz, _vp]),
     "llmoc_moe_route_views": (_i, [_vp, _i, _vp, _sz, C.POINTER(RouteViews)]),
     "llmoc_moe_route": (_i, [_vp, _vp, _i, _vp, _sz, _vp]),
@@ -204,7 +213,23 @@ class MoeLayer:
         sh = None
         if layer.shared is not None:
             sh = [view_of(layer.shared.gate), view_of(layer.shared.up), view_of(layer.shared.down)]
-        return cls.create(desc, layer.router_w, layer.bias, views, sh, device)
+        dev = cls.create(desc, layer.router_w, layer.bias, views, sh, device)
+        if getattr(layer, "shared_gate_w", None) is not None:
+            dev.set_shared_gate(layer.shared_gate_w)
+        return dev
+
+    @classmethod
+    def from_qlwc(cls, path: str, prefix: str, layer: int, desc: "LayerDesc", device: int = 0) -> "MoeLayer":
+        """Layer `layer` of a QLWC file (llmoc_moe_layer_create_qlwc)."""
+        h = C.c_void_p()
+        check(lib.llmoc_moe_layer_create_qlwc(path.encode(), prefix.encode(), layer, C.byref(desc), device,
+                                              C.byref(h)), "llmoc_moe_layer_create_qlwc")
+        return cls(h.value, desc)
+
+    def set_shared_gate(self, gate_row, on_device: bool = False) -> None:
+        """Per-token shared-expert weight sigmoid(gate_row . x) (bf16 [hidden])."""
+        check(lib.llmoc_moe_layer_set_shared_gate(self.handle, ptr(gate_row), 1 if on_device else 0),
+              "llmoc_moe_layer_set_shared_gate")
 
     def close(self) -> None:
         if self.handle:
@@ -308,7 +333,10 @@ class EpLayerShard(MoeLayer):
         sh = None
         if layer.shared is not None:
             sh = [view_of(layer.shared.gate), view_of(layer.shared.up), view_of(layer.shared.down)]
-        return cls.create_ep(desc, layer.router_w, layer.bias, views, sh, rank, world, device)
+        dev = cls.create_ep(desc, layer.router_w, layer.bias, views, sh, rank, world, device)
+        if getattr(layer, "shared_gate_w", None) is not None:
+            dev.set_shared_gate(layer.shared_gate_w)
+        return dev
 
     @property
     def e_loc(self) -> int:
@@ -383,3 +411,9 @@ class EpTransport:
         if self.handle:
             lib.llmoc_ep_transport_destroy(self.handle)
             self.handle = None
+
+
+def qlwc_describe(path: str, prefix: str, layer: int) -> QlwcLayerInfo:
+    info = QlwcLayerInfo()
+    check(lib.llmoc_qlwc_describe(path.encode(), prefix.encode(), layer, C.byref(info)), "llmoc_qlwc_describe")
+    return info

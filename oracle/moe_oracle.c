@@ -436,6 +436,10 @@ typedef struct {
   const orc_expert* experts; /* [E] */
   const orc_expert* shared;  /* NULL or one expert with the same (I, H) */
   float shared_scale;
+  /* NULL, or the shared expert's gate row (bf16 [H]): the shared expert's
+   * weight is then per token, sigmoid(gate . x) with the router's dot order
+   * and the reference's float sigmoid (qwen3_6_moe_int4_model.cpp:29, :365-371) */
+  const uint16_t* shared_gate_w;
 } orc_layer;
 
 /* One expert's SwiGLU FFN on one token: d[H] = down(silu(gate x) * up x)
@@ -481,8 +485,14 @@ ORC_API void orc_moe_layer_forward(const orc_layer* L, const float* X, int T, fl
         for (int h = 0; h < H; ++h) y[h] = fmaf(w[j], d[h], y[h]);
       }
       if (L->shared) {
+        float ss = L->shared_scale;
+        if (L->shared_gate_w) {
+          float gl;
+          orc_gemm_bias_free(x, L->shared_gate_w, &gl, 1, H, 0);
+          ss = 1.f / (1.f + expf(-gl));
+        }
         orc_expert_ffn(L->shared, x, g, u, mid, d);
-        for (int h = 0; h < H; ++h) y[h] = fmaf(L->shared_scale, d[h], y[h]);
+        for (int h = 0; h < H; ++h) y[h] = fmaf(ss, d[h], y[h]);
       }
     }
     free(logits);

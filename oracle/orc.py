@@ -67,6 +67,7 @@ class LayerC(C.Structure):
         ("experts", C.POINTER(ExpertC)),
         ("shared", C.POINTER(ExpertC)),
         ("shared_scale", C.c_float),
+        ("shared_gate_w", C.c_void_p),
     ]
 
 
@@ -121,6 +122,7 @@ class MoeLayer:
     routed_scaling: float = 1.0
     shared: Optional[Expert] = None
     shared_scale: float = 1.0
+    shared_gate_w: Optional[np.ndarray] = None  # uint16 bf16 bits [H]: per-token sigmoid shared weight
     _keep: list = field(default_factory=list, repr=False)
 
     def c(self) -> LayerC:
@@ -139,6 +141,7 @@ class MoeLayer:
             C.cast(arr, C.POINTER(ExpertC)),
             sh,
             float(self.shared_scale),
+            self.shared_gate_w.ctypes.data if self.shared_gate_w is not None else None,
         )
 
 
@@ -349,7 +352,7 @@ def bits_to_f32(b: np.ndarray) -> np.ndarray:
 def make_layer(orc: Oracle, rng: np.random.Generator, H: int, I: int, E: int, topk: int, gs: int,
                router: int = ROUTER_SOFTMAX, routed_scaling: float = 1.0, shared: bool = False,
                shared_scale: float = 1.0, scheme: int = SCHEME_AWQ_SYM, wstd: float = 0.02,
-               n_real: Optional[int] = None) -> MoeLayer:
+               n_real: Optional[int] = None, shared_gate: bool = False) -> MoeLayer:
     """Seeded synthetic MoE layer: W ~ N(0, wstd^2) rounded to bf16, quantized
     per expert with quant_awq_sym semantics (bf16-valued scales) or GPTQ-asym.
     ``n_real`` < E makes only the first n_real experts distinct and re-uses
@@ -368,7 +371,8 @@ def make_layer(orc: Oracle, rng: np.random.Generator, H: int, I: int, E: int, to
     if router == ROUTER_SIGMOID_BIAS:
         bias = (rng.standard_normal(E, dtype=np.float32) * np.float32(0.1)).astype(np.float32)
     sh = Expert(q(I, H), q(I, H), q(H, I)) if shared else None
-    return MoeLayer(H, I, E, topk, rw, experts, router, bias, routed_scaling, sh, shared_scale)
+    sg = bf16_bits(rng.standard_normal(H, dtype=np.float32) * np.float32(0.05)) if shared and shared_gate else None
+    return MoeLayer(H, I, E, topk, rw, experts, router, bias, routed_scaling, sh, shared_scale, sg)
 
 
 def make_tokens(rng: np.random.Generator, T: int, H: int) -> np.ndarray:

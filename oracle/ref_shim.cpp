@@ -58,7 +58,11 @@ struct ref_layer {
   const ref_expert* experts;
   const ref_expert* shared;
   float shared_scale;
+  const uint16_t* shared_gate_w;  // null, or bf16 [H]: per-token scale sigmoid(gate . x)
 };
+
+// the reference's float sigmoid (qwen3_6_moe_int4_model.cpp:29)
+static float ref_sigmoid(float x) { return 1.f / (1.f + std::exp(-x)); }
 
 static qlwc::Int4View to_view(const ref_int4_view& v) {
   qlwc::Int4View W;
@@ -195,7 +199,13 @@ static void moe_token(const ref_layer& L, const float* x, float* down_acc, int* 
     hal::gemm_int4(x, to_view(L.shared->up), u.data());
     hal::silu_and_mul(g.data(), u.data(), mid.data(), I);
     hal::gemm_int4(mid.data(), to_view(L.shared->down), down.data());
-    for (int d = 0; d < H; ++d) down_acc[d] += L.shared_scale * down[static_cast<size_t>(d)];
+    float scale = L.shared_scale;
+    if (L.shared_gate_w) {  // qwen3_6_moe_int4_model.cpp:365-371
+      float gate_logit = 0.f;
+      hal::gemm_bias_free(x, L.shared_gate_w, &gate_logit, 1, H, hal::WDtype::kBF16, false);
+      scale = ref_sigmoid(gate_logit);
+    }
+    for (int d = 0; d < H; ++d) down_acc[d] += scale * down[static_cast<size_t>(d)];
   }
 }
 

@@ -15,7 +15,9 @@ Sources of truth, all from appolloqin/llm-on-cpu:
   in ``oracle/ref_shim.cpp`` from ``src/model/qwen3_6_moe_int4_model.cpp:184-232,377-404``,
   run single-threaded so the expert combine has one defined order;
 * the known-answer cases of ``tests/unit/test_int4_gemm.cpp:40-149`` and
-  ``tests/unit/test_gpu_quant_gemm.cpp:130-245`` (same patterns, same sizes).
+  ``tests/unit/test_gpu_quant_gemm.cpp:130-245`` (same patterns, same sizes);
+* ``write_qlwc`` of ``tools/quantize_int4.py`` (:183-260): a one-layer QLWC
+  file (``qlwc_cases.npz``) for the library's QLWC loader.
 
 Inputs that are large are not stored: they are regenerated from the seed by
 ``oracle/orc.py`` (whose quantizer is itself pinned here against the Python
@@ -166,6 +168,9 @@ LAYER_CASES = {
     "kimi_small_gs32": (13, dict(H=448, I=128, E=48, topk=8, gs=32, router=1,
                                  routed_scaling=2.827, shared=True), 4),
     "gptq_small": (14, dict(H=256, I=128, E=16, topk=4, gs=64, scheme=1, shared=True, shared_scale=0.5), 5),
+    # Qwen3.6-style shared expert with its per-token sigmoid gate (qwen3_6_moe_int4_model.cpp:365-371)
+    "gptq_shared_gate": (15, dict(H=256, I=128, E=16, topk=4, gs=64, scheme=1, shared=True,
+                                  shared_gate=True), 6),
 }
 
 
@@ -180,6 +185,8 @@ def layer_inputs(O: orc.Oracle, name: str):
         arrays.append(L.bias)
     if L.shared is not None:
         arrays += [L.shared.gate.q, L.shared.up.q, L.shared.down.q]
+    if L.shared_gate_w is not None:
+        arrays.append(L.shared_gate_w)
     return L, X, digest(*arrays)
 
 
@@ -190,6 +197,44 @@ def layer_cases(O: orc.Oracle, R: orc.Reference) -> dict:
         Y, ids, w, _ = R.moe_layer_forward(L, X)
         out[f"layer_{name}"] = dict(Y=Y, ids=ids, w=w, input_sha256=np.array(h))
     return out
+
+
+# One MoE layer as the reference's tools write it: GPTQ experts, a shared
+# expert with its per-token gate, bf16 router; layer index 3 under "model.".
+QLWC_CASE = dict(seed=21, layer=3, prefix="model.",
+                 kw=dict(H=256, I=64, E=8, topk=2, gs=64, scheme=1, shared=True, shared_gate=True))
+
+
+def qlwc_layer(O: orc.Oracle) -> orc.MoeLayer:
+    return orc.make_layer(O, np.random.default_rng(QLWC_CASE["seed"]), **QLWC_CASE["kw"])
+
+
+def qlwc_cases(O: orc.Oracle, qi) -> dict:
+    import tempfile
+    from pathlib import Path
+
+    L = qlwc_layer(O)
+    base = f"{QLWC_CASE['prefix']}layers.{QLWC_CASE['layer']}.mlp."
+    items = []
+
+    def int4(name, w):
+        # flat arrays, as the reference's own quantizer hands them to write_qlwc
+        items.append(dict(name=name, kind=1, shape=[w.M, w.K], q=w.q.tobytes(), scales=w.scales.reshape(-1),
+                          zeros=None if w.zeros is None else w.zeros.reshape(-1)))
+
+    for e, ex in enumerate(L.experts):
+        for pn, w in (("gate_proj", ex.gate), ("up_proj", ex.up), ("down_proj", ex.down)):
+            int4(f"{base}experts.{e}.{pn}.weight", w)
+    for pn, w in (("gate_proj", L.shared.gate), ("up_proj", L.shared.up), ("down_proj", L.shared.down)):
+        int4(f"{base}shared_expert.{pn}.weight", w)
+    items.append(dict(name=base + "gate.weight", kind=0, shape=[L.E, L.H], pass_dtype=1, data=L.router_w.tobytes()))
+    items.append(dict(name=base + "shared_expert_gate.weight", kind=0, shape=[1, L.H], pass_dtype=1,
+                      data=L.shared_gate_w.tobytes()))
+    with tempfile.TemporaryDirectory() as d:
+        path = Path(d) / "layer.qlwc"
+        qi.write_qlwc(path, 1, QLWC_CASE["kw"]["gs"], items)  # scheme 1 = GPTQ-asym
+        blob = np.frombuffer(path.read_bytes(), dtype=np.uint8).copy()
+    return {"qlwc_gptq_shared_gate": dict(file=blob, input_sha256=np.array(digest(L.router_w, L.shared_gate_w)))}
 
 
 def main() -> None:
@@ -203,7 +248,8 @@ def main() -> None:
     O = orc.Oracle()
     assert R.max_threads() == 1, "run with OMP_NUM_THREADS=1 so the combine order is defined"
     groups = {"unit_cases": unit_cases(R), "quant_cases": quant_cases(qi),
-              "router_cases": router_cases(R), "layer_cases": layer_cases(O, R)}
+              "router_cases": router_cases(R), "layer_cases": layer_cases(O, R),
+              "qlwc_cases": qlwc_cases(O, qi)}
     for gname, cases in groups.items():
         flat = {}
         for cname, d in cases.items():

@@ -82,6 +82,7 @@ class DevLayer:
         v = self.dev.route_views(T, self.ws, ws_bytes)
         base = self.ws.data_ptr()
         kk, E, n_exp = self.dev.kk, self.host.E, self.dev.n_exp
+        ld = E + (1 if getattr(self.host, "shared_gate_w", None) is not None else 0)  # + the shared gate's logit
 
         def grab(addr, n, dt):
             off = addr - base
@@ -89,7 +90,7 @@ class DevLayer:
             return self.ws[off:off + nbytes].cpu().numpy().view(dt).copy()
 
         return dict(
-            logits=grab(v.logits, T * E, np.float32).reshape(T, E),
+            logits=grab(v.logits, T * ld, np.float32).reshape(T, ld),
             ids=grab(v.ids, T * kk, np.int32).reshape(T, kk),
             weights=grab(v.weights, T * kk, np.float32).reshape(T, kk),
             offsets=grab(v.offsets, n_exp + 1, np.int32),

@@ -28,6 +28,7 @@ CFGS = {
     "glm_like_shared_sigmoid": dict(H=512, I=128, E=32, topk=8, gs=128, router=1, shared=True),
     "kimi_like_gs32": dict(H=448, I=128, E=48, topk=8, gs=32, router=1, routed_scaling=2.827, shared=True),
     "gptq_shared": dict(H=256, I=128, E=16, topk=4, gs=64, scheme=1, shared=True, shared_scale=0.75),
+    "shared_gate": dict(H=256, I=128, E=16, topk=4, gs=64, scheme=1, shared=True, shared_gate=True),
 }
 
 

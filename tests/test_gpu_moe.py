@@ -32,6 +32,8 @@ SMALL = {
                            shared=True),
     "gptq_shared": dict(H=256, I=128, E=16, topk=4, gs=64, scheme=1, shared=True, shared_scale=0.75),
     "odd_k_chunks": dict(H=288, I=96, E=12, topk=3, gs=32),
+    # Qwen3.6-style shared expert weighted per token by sigmoid(shared_expert_gate . x)
+    "shared_gate_gptq": dict(H=512, I=128, E=32, topk=8, gs=128, scheme=1, shared=True, shared_gate=True),
 }
 
 
@@ -80,7 +82,7 @@ def check_routing(oracle, dl, X, v, sample=None):
     sample = range(T) if sample is None else sample
     for t in sample:
         ref_logits = oracle.gemm_bias_free(X[t], h.router_w)
-        assert np.array_equal(v["logits"][t].view(np.uint32), ref_logits.view(np.uint32)), t
+        assert np.array_equal(v["logits"][t, :h.E].view(np.uint32), ref_logits.view(np.uint32)), t
         if h.router == orc.ROUTER_SOFTMAX:
             ids, w, _ = oracle.route_softmax(ref_logits, h.topk)
         else:
@@ -89,7 +91,13 @@ def check_routing(oracle, dl, X, v, sample=None):
         np.testing.assert_allclose(v["weights"][t, :h.topk], w, rtol=2e-6, atol=0)
         if h.shared is not None:
             assert v["ids"][t, h.topk] == h.E
-            assert v["weights"][t, h.topk] == np.float32(h.shared_scale)
+            if h.shared_gate_w is None:
+                assert v["weights"][t, h.topk] == np.float32(h.shared_scale)
+            else:  # the gate's logit is bitwise the reference's; the sigmoid within a few ulp
+                gl = oracle.gemm_bias_free(X[t], h.shared_gate_w[None, :])
+                assert np.array_equal(v["logits"][t, h.E:h.E + 1].view(np.uint32), gl.view(np.uint32)), t
+                want = np.float32(1.0) / (np.float32(1.0) + np.exp(-gl.astype(np.float32)))
+                np.testing.assert_allclose(v["weights"][t, h.topk], want[0], rtol=2e-6, atol=0)
     off, srt, inv = oracle.permute(v["ids"], dl.dev.n_exp)
     assert np.array_equal(v["offsets"], off)
     assert np.array_equal(v["sorted"], srt)
@@ -211,6 +219,42 @@ def test_forward_residual(oracle, T, in_place):
     err = np.abs(G.bf16_to_f32(Y) - (R + y2)).max()
     assert err <= 2.0 ** -6 * (np.abs(R).max() + np.abs(y2).max()), err
     dl.close()
+
+
+def test_layer_from_qlwc_file(oracle, tmp_path):
+    """A layer loaded by llmoc_moe_layer_create_qlwc from a file the
+    reference's own tools/quantize_int4.py wrote (GPTQ experts, shared expert
+    with its per-token gate): routing bit-exact and outputs within tolerance of
+    the oracle on the same weights."""
+    import make_golden as mg
+    import test_qlwc
+
+    path = test_qlwc.qlwc_file(tmp_path)
+    layer = mg.qlwc_layer(oracle)
+    kw = mg.QLWC_CASE["kw"]
+    desc = L.LayerDesc(kw["H"], kw["I"], kw["E"], kw["topk"], kw["gs"], L.SCHEME_GPTQ_ASYM, 0,
+                       L.ROUTER_SOFTMAX, 1.0, 1, 1.0)
+    dev = L.MoeLayer.from_qlwc(path, mg.QLWC_CASE["prefix"], mg.QLWC_CASE["layer"], desc, 0)
+    T = 24
+    X = orc.make_tokens(np.random.default_rng(5), T, kw["H"])
+    Xd = G.bf16_dev(X)
+    Y = torch.empty((T, kw["H"]), dtype=torch.bfloat16, device="cuda")
+    ws_bytes = dev.workspace_bytes(T)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+    dev.forward(Xd, T, Y, ws, ws_bytes, torch.cuda.current_stream())
+    torch.cuda.synchronize()
+    v = dev.route_views(T, ws, ws_bytes)
+    ids = ws[v.ids - ws.data_ptr(): v.ids - ws.data_ptr() + 4 * T * (kw["topk"] + 1)].cpu().numpy().view(np.int32)
+    Yref, ids_ref, _, _ = oracle.moe_layer_forward(layer, X)
+    assert np.array_equal(ids.reshape(T, -1)[:, :kw["topk"]], ids_ref)
+    mre, cos = G.quality(G.bf16_to_f32(Y), Yref)
+    assert mre <= G.MAX_REL and cos >= G.MIN_COS, (mre, cos)
+    # the desc must agree with the file
+    bad = L.LayerDesc(kw["H"], kw["I"], kw["E"] + 1, kw["topk"], kw["gs"], L.SCHEME_GPTQ_ASYM, 0,
+                      L.ROUTER_SOFTMAX, 1.0, 1, 1.0)
+    with pytest.raises(L.LlmocError):
+        L.MoeLayer.from_qlwc(path, mg.QLWC_CASE["prefix"], mg.QLWC_CASE["layer"], bad, 0)
+    dev.close()
 
 
 def test_zero_weights_give_zero_output(oracle):
