@@ -446,9 +446,14 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
 // next unit's work item, activation row and weight pointers are fetched when
 // the copies enter the current one, so they are in registers when needed.
 // Same arithmetic, per unit, as k_int4_mma with ks = 1.
+// A unit always carries two weight streams over the same activation rows: the
+// gate and up tiles of one 16-row tile (MODE_GATE_UP), or two adjacent 16-row
+// tiles of one projection (MODE_PLAIN_F32), so the activation copies, the
+// x-sum MMAs and the loop's bookkeeping are shared by 2 KB of weights a step.
 template <int MODE, int GSB, bool AWQ>
 __global__ void __launch_bounds__(kWarps * 32) k_int4_mma_p(GemmArgs a) {
-  constexpr int NP = MODE == MODE_GATE_UP ? 2 : 1;
+  constexpr int NP = 2;
+  constexpr bool PAIR = MODE != MODE_GATE_UP;
   constexpr int NG = GSB == 4 ? 1 : (GSB == 2 ? 2 : 4);  // groups per step
   using SG = WStage<NP, 1, AWQ>;
   extern __shared__ __align__(128) unsigned char wsm[];
@@ -461,7 +466,8 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma_p(GemmArgs a) {
     grid_dep_wait();
     grid_dep_release();
   }
-  const int Mt = (a.M + 15) >> 4;
+  const int Mt16 = (a.M + 15) >> 4;  // 16-row tiles
+  const int Mt = PAIR ? (Mt16 + 1) >> 1 : Mt16;  // row tiles (pairs) per work item
   const int nunits = *a.n_work * Mt;
   const int nsteps = a.K >> 7;
 
@@ -481,14 +487,13 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma_p(GemmArgs a) {
       prow = a.gather ? a.gather[pos] / a.kk : pos;
       const ExpertDev& ex = a.experts[pit.expert];
       const ProjDev& P0 = MODE == MODE_GATE_UP ? ex.gate : pick(ex, a.proj);
+      const ProjDev& P1 = MODE == MODE_GATE_UP ? ex.up : P0;
       pq[0] = P0.q;
       ps[0] = P0.s;
       pz[0] = P0.z;
-      if (NP == 2) {
-        pq[NP - 1] = ex.up.q;
-        ps[NP - 1] = ex.up.s;
-        pz[NP - 1] = ex.up.z;
-      }
+      pq[1] = P1.q;
+      ps[1] = P1.s;
+      pz[1] = P1.z;
     }
   };
 
@@ -504,9 +509,12 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma_p(GemmArgs a) {
     const int rt = pu % Mt;
 #pragma unroll
     for (int p = 0; p < NP; ++p) {
-      wsrc[p] = reinterpret_cast<const unsigned char*>(pq[p] + (size_t)rt * a.Kc * 32 + piece_slot(lane));
-      ssrc[p] = reinterpret_cast<const unsigned char*>(ps[p] + (size_t)rt * a.ng * 16);
-      zsrc[p] = AWQ ? nullptr : reinterpret_cast<const unsigned char*>(pz[p] + (size_t)rt * a.ng * 16);
+      // tile pair: the second tile of an odd count repeats the first (its
+      // results fall on rows >= M and are not stored)
+      const int tr = PAIR ? min(2 * rt + p, Mt16 - 1) : rt;
+      wsrc[p] = reinterpret_cast<const unsigned char*>(pq[p] + (size_t)tr * a.Kc * 32 + piece_slot(lane));
+      ssrc[p] = reinterpret_cast<const unsigned char*>(ps[p] + (size_t)tr * a.ng * 16);
+      zsrc[p] = AWQ ? nullptr : reinterpret_cast<const unsigned char*>(pz[p] + (size_t)tr * a.ng * 16);
     }
     bval = g < pit.nrows;
     bsrc = reinterpret_cast<const unsigned char*>(a.B) + ((size_t)prow * a.ldb + 8 * t) * 2;
@@ -652,21 +660,24 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma_p(GemmArgs a) {
 
     if (++cs < nsteps) continue;
     // unit done: C fragment (row g / g+8, col 2t / 2t+1) -> outputs
-    const int m0 = c_rt * 16 + g, m1 = m0 + 8;
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const int col = 2 * t + (r & 1);
-      const int m = (r < 2) ? m0 : m1;
-      if (col < c_nrows && m < a.M) {
-        const size_t o = (size_t)(c_row0 + col) * a.ldo + m;
-        float v = acc[0][r];
-        if (!isfinite(v)) v = 0.f;  // non-finite -> 0, as every reference GEMV does
-        if (MODE == MODE_GATE_UP) {
-          float uu = acc[NP - 1][r];
-          if (!isfinite(uu)) uu = 0.f;
-          reinterpret_cast<__nv_bfloat16*>(a.out)[o] = __float2bfloat16_rn(silu_mul(v, uu));
-        } else {
-          reinterpret_cast<float*>(a.out)[o] = v;
+    for (int p = 0; p < (PAIR ? 2 : 1); ++p) {
+      const int m0 = (PAIR ? 2 * c_rt + p : c_rt) * 16 + g, m1 = m0 + 8;
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int col = 2 * t + (r & 1);
+        const int m = (r < 2) ? m0 : m1;
+        if (col < c_nrows && m < a.M) {
+          const size_t o = (size_t)(c_row0 + col) * a.ldo + m;
+          float v = acc[p][r];
+          if (!isfinite(v)) v = 0.f;  // non-finite -> 0, as every reference GEMV does
+          if (MODE == MODE_GATE_UP) {
+            float uu = acc[1][r];
+            if (!isfinite(uu)) uu = 0.f;
+            reinterpret_cast<__nv_bfloat16*>(a.out)[o] = __float2bfloat16_rn(silu_mul(v, uu));
+          } else {
+            reinterpret_cast<float*>(a.out)[o] = v;
+          }
         }
       }
     }
@@ -701,7 +712,7 @@ static void launch_mma_k(const GemmArgs& a, dim3 grid, int ks, cudaStream_t st) 
 // Persistent grid: as many 4-warp CTAs as fit on the SMs at once.
 template <int MODE, int GSB, bool AWQ>
 static int mma_p_grid() {
-  constexpr int NP = MODE == MODE_GATE_UP ? 2 : 1;
+  constexpr int NP = 2;  // two weight streams per unit in both modes
   const size_t smem = (size_t)kWarps * kStagesW * WStage<NP, 1, AWQ>::kBytes;
   static int grid = 0;  // per template instance (one device per process in practice)
   if (!grid) {
@@ -717,7 +728,7 @@ static int mma_p_grid() {
 
 template <int MODE, int GSB, bool AWQ>
 static void launch_mma_pk(const GemmArgs& a, cudaStream_t st) {
-  constexpr int NP = MODE == MODE_GATE_UP ? 2 : 1;
+  constexpr int NP = 2;
   const size_t smem = (size_t)kWarps * kStagesW * WStage<NP, 1, AWQ>::kBytes;
   launch_pdl(k_int4_mma_p<MODE, GSB, AWQ>, dim3(mma_p_grid<MODE, GSB, AWQ>()), dim3(kWarps * 32), smem, st, a);
 }
