@@ -206,234 +206,242 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
     grid_dep_wait();
     grid_dep_release();
   }
-  if ((int)blockIdx.y >= *a.n_work) return;
+  // work items blockIdx.y, blockIdx.y + gridDim.y, ... (the grid is sized to
+  // the expected items, the loop covers the work list whatever its length)
   const int Mt = (a.M + 15) >> 4;
   const bool live = rt < Mt;
-  const WorkItem it = a.work[blockIdx.y];
-  const ExpertDev& ex = a.experts[it.expert];
-  const ProjDev* P[2];
-  P[0] = MODE == MODE_GATE_UP ? &ex.gate : &pick(ex, a.proj);
-  P[1] = &ex.up;
-  const int ntc = (it.nrows + 7) >> 3;
+  const int n_items = *a.n_work;
+  bool waited = MODE == MODE_GATE_UP;
+  for (int item = blockIdx.y; item < n_items; item += gridDim.y) {
+    const WorkItem it = a.work[item];
+    const ExpertDev& ex = a.experts[it.expert];
+    const ProjDev* P[2];
+    P[0] = MODE == MODE_GATE_UP ? &ex.gate : &pick(ex, a.proj);
+    P[1] = &ex.up;
+    const int ntc = (it.nrows + 7) >> 3;
 
-  const int nsteps = a.K >> 7;
-  const int per = (nsteps + ks - 1) / ks;
-  const int s0 = live ? min(nsteps, slice * per) : 0;
-  const int s1 = live ? min(nsteps, s0 + per) : 0;
-  const int nst = s1 - s0;
+    const int nsteps = a.K >> 7;
+    const int per = (nsteps + ks - 1) / ks;
+    const int s0 = live ? min(nsteps, slice * per) : 0;
+    const int s1 = live ? min(nsteps, s0 + per) : 0;
+    const int nst = s1 - s0;
 
-  // sources advanced one step per issue
-  const unsigned char* bsrc[NT];
-  bool bval[NT];
-#pragma unroll
-  for (int n = 0; n < NT; ++n) {
-    const int r = 8 * n + g;
-    bval[n] = r < it.nrows && n < ntc;
-    const int pos = it.row0 + (r < it.nrows ? r : 0);
-    const int row = a.gather ? a.gather[pos] / a.kk : pos;
-    bsrc[n] = reinterpret_cast<const unsigned char*>(a.B) + ((size_t)row * a.ldb + 8 * t + s0 * 128) * 2;
-  }
-  const int rtc = live ? rt : 0;
-  const unsigned char* wsrc[NP];
-  const unsigned char* ssrc[NP];
-  const unsigned char* zsrc[NP];
-#pragma unroll
-  for (int p = 0; p < NP; ++p) {
-    wsrc[p] = reinterpret_cast<const unsigned char*>(P[p]->q + ((size_t)rtc * a.Kc + 2 * s0) * 32 + piece_slot(lane));
-    ssrc[p] = reinterpret_cast<const unsigned char*>(P[p]->s + ((size_t)rtc * a.ng + (size_t)s0 * NG) * 16);
-    zsrc[p] = AWQ ? nullptr
-                  : reinterpret_cast<const unsigned char*>(P[p]->z + ((size_t)rtc * a.ng + (size_t)s0 * NG) * 16);
-  }
-  unsigned char* wbase = wsm + (size_t)warp * kStagesW * SG::kBytes;
-
-  // issue the copies of one step into a stage (every lane its own 16 B
-  // pieces): the weights (and scales, zeros), then the activations
-  auto issue_w = [&](int stage) {
-    unsigned char* sb = wbase + stage * SG::kBytes;
-#pragma unroll
-    for (int p = 0; p < NP; ++p) {
-      cp_async16(sb + p * 1024 + lane * 16, wsrc[p]);
-      cp_async16(sb + p * 1024 + 512 + lane * 16, wsrc[p] + 512);
-      wsrc[p] += 1024;
-      if (lane < NG * 2) cp_async16(sb + SG::kW + p * 128 + lane * 16, ssrc[p] + lane * 16);
-      if (!AWQ && lane < NG * 2) cp_async16(sb + SG::kW + SG::kS + p * 128 + lane * 16, zsrc[p] + lane * 16);
-      ssrc[p] += NG * 32;
-      if (!AWQ) zsrc[p] += NG * 32;
-    }
-  };
-  auto issue_b = [&](int stage) {
-    unsigned char* sb = wbase + stage * SG::kBytes;
+    // sources advanced one step per issue
+    const unsigned char* bsrc[NT];
+    bool bval[NT];
 #pragma unroll
     for (int n = 0; n < NT; ++n) {
-      if (bval[n]) {
-#pragma unroll
-        for (int b = 0; b < 4; ++b)
-          cp_async16(sb + SG::kW + SG::kS + SG::kZ + (n * 4 + b) * 512 + lane * 16, bsrc[n] + b * 64);
-      }
-      bsrc[n] += 256;
+      const int r = 8 * n + g;
+      bval[n] = r < it.nrows && n < ntc;
+      const int pos = it.row0 + (r < it.nrows ? r : 0);
+      const int row = a.gather ? a.gather[pos] / a.kk : pos;
+      bsrc[n] = reinterpret_cast<const unsigned char*>(a.B) + ((size_t)row * a.ldb + 8 * t + s0 * 128) * 2;
     }
-  };
-  auto issue = [&](int stage) {
-    issue_w(stage);
-    issue_b(stage);
-  };
-
-#pragma unroll
-  for (int d = 0; d < kStagesW - 1; ++d)
-    if (d < nst) issue_w(d);
-  if (MODE != MODE_GATE_UP) {
-    grid_dep_wait();
-    grid_dep_release();
-  }
-#pragma unroll
-  for (int d = 0; d < kStagesW - 1; ++d) {
-    if (d < nst) issue_b(d);
-    cp_async_commit();
-  }
-
-  const uint32_t ones[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};
-  const float bias = AWQ ? (float)(128 + a.zp) : 128.f;
-  // two partial accumulators per chain (k16 halves kt = 0 / 1) halve the
-  // dependent MMA chains; they are added at each group end
-  float acc[NP][NT][4], tmp[NP][NT][2][4], xs[NT][2][4];
-#pragma unroll
-  for (int p = 0; p < NP; ++p)
-#pragma unroll
-    for (int n = 0; n < NT; ++n)
-#pragma unroll
-      for (int r = 0; r < 4; ++r) acc[p][n][r] = tmp[p][n][0][r] = tmp[p][n][1][r] = 0.f;
-#pragma unroll
-  for (int n = 0; n < NT; ++n)
-#pragma unroll
-    for (int r = 0; r < 4; ++r) xs[n][0][r] = xs[n][1][r] = 0.f;
-
-  for (int i = 0; i < nst; ++i) {
-    if (i + kStagesW - 1 < nst) issue((i + kStagesW - 1) % kStagesW);
-    cp_async_commit();
-    cp_async_wait<kStagesW - 1>();
-    __syncwarp();  // the scales are copied by lanes 0..2*NG-1 and read by all
-    const unsigned char* sb = wbase + (i % kStagesW) * SG::kBytes;
-    uint4 wq[NP][2], bv[NT][4];
-    float sc[NP][NG][2], zz[NP][NG][2];
+    const int rtc = live ? rt : 0;
+    const unsigned char* wsrc[NP];
+    const unsigned char* ssrc[NP];
+    const unsigned char* zsrc[NP];
 #pragma unroll
     for (int p = 0; p < NP; ++p) {
-      wq[p][0] = *reinterpret_cast<const uint4*>(sb + p * 1024 + lane * 16);
-      wq[p][1] = *reinterpret_cast<const uint4*>(sb + p * 1024 + 512 + lane * 16);
-#pragma unroll
-      for (int q = 0; q < NG; ++q) {
-        const __half* sp = reinterpret_cast<const __half*>(sb + SG::kW + p * 128) + q * 16;
-        sc[p][q][0] = __half2float(sp[g]);
-        sc[p][q][1] = __half2float(sp[g + 8]);
-        if (!AWQ) {
-          const __half* zp = reinterpret_cast<const __half*>(sb + SG::kW + SG::kS + p * 128) + q * 16;
-          zz[p][q][0] = __half2float(zp[g]);
-          zz[p][q][1] = __half2float(zp[g + 8]);
-        }
-      }
+      wsrc[p] = reinterpret_cast<const unsigned char*>(P[p]->q + ((size_t)rtc * a.Kc + 2 * s0) * 32 + piece_slot(lane));
+      ssrc[p] = reinterpret_cast<const unsigned char*>(P[p]->s + ((size_t)rtc * a.ng + (size_t)s0 * NG) * 16);
+      zsrc[p] = AWQ ? nullptr
+                    : reinterpret_cast<const unsigned char*>(P[p]->z + ((size_t)rtc * a.ng + (size_t)s0 * NG) * 16);
     }
+    unsigned char* wbase = wsm + (size_t)warp * kStagesW * SG::kBytes;
+
+    // issue the copies of one step into a stage (every lane its own 16 B
+    // pieces): the weights (and scales, zeros), then the activations
+    auto issue_w = [&](int stage) {
+      unsigned char* sb = wbase + stage * SG::kBytes;
+#pragma unroll
+      for (int p = 0; p < NP; ++p) {
+        cp_async16(sb + p * 1024 + lane * 16, wsrc[p]);
+        cp_async16(sb + p * 1024 + 512 + lane * 16, wsrc[p] + 512);
+        wsrc[p] += 1024;
+        if (lane < NG * 2) cp_async16(sb + SG::kW + p * 128 + lane * 16, ssrc[p] + lane * 16);
+        if (!AWQ && lane < NG * 2) cp_async16(sb + SG::kW + SG::kS + p * 128 + lane * 16, zsrc[p] + lane * 16);
+        ssrc[p] += NG * 32;
+        if (!AWQ) zsrc[p] += NG * 32;
+      }
+    };
+    auto issue_b = [&](int stage) {
+      unsigned char* sb = wbase + stage * SG::kBytes;
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        if (bval[n]) {
+#pragma unroll
+          for (int b = 0; b < 4; ++b)
+            cp_async16(sb + SG::kW + SG::kS + SG::kZ + (n * 4 + b) * 512 + lane * 16, bsrc[n] + b * 64);
+        }
+        bsrc[n] += 256;
+      }
+    };
+    auto issue = [&](int stage) {
+      issue_w(stage);
+      issue_b(stage);
+    };
+
+#pragma unroll
+    for (int d = 0; d < kStagesW - 1; ++d)
+      if (d < nst) issue_w(d);
+    if (!waited) {
+      grid_dep_wait();
+      grid_dep_release();
+      waited = true;
+    }
+#pragma unroll
+    for (int d = 0; d < kStagesW - 1; ++d) {
+      if (d < nst) issue_b(d);
+      cp_async_commit();
+    }
+
+    const uint32_t ones[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};
+    const float bias = AWQ ? (float)(128 + a.zp) : 128.f;
+    // two partial accumulators per chain (k16 halves kt = 0 / 1) halve the
+    // dependent MMA chains; they are added at each group end
+    float acc[NP][NT][4], tmp[NP][NT][2][4], xs[NT][2][4];
+#pragma unroll
+    for (int p = 0; p < NP; ++p)
+#pragma unroll
+      for (int n = 0; n < NT; ++n)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) acc[p][n][r] = tmp[p][n][0][r] = tmp[p][n][1][r] = 0.f;
 #pragma unroll
     for (int n = 0; n < NT; ++n)
 #pragma unroll
-      for (int b = 0; b < 4; ++b)
-        bv[n][b] = bval[n] ? *reinterpret_cast<const uint4*>(sb + SG::kW + SG::kS + SG::kZ + (n * 4 + b) * 512 + lane * 16)
-                           : make_uint4(0, 0, 0, 0);
-    __syncwarp();  // every lane holds its operands before any lane refills this stage
+      for (int r = 0; r < 4; ++r) xs[n][0][r] = xs[n][1][r] = 0.f;
+
+    for (int i = 0; i < nst; ++i) {
+      if (i + kStagesW - 1 < nst) issue((i + kStagesW - 1) % kStagesW);
+      cp_async_commit();
+      cp_async_wait<kStagesW - 1>();
+      __syncwarp();  // the scales are copied by lanes 0..2*NG-1 and read by all
+      const unsigned char* sb = wbase + (i % kStagesW) * SG::kBytes;
+      uint4 wq[NP][2], bv[NT][4];
+      float sc[NP][NG][2], zz[NP][NG][2];
+#pragma unroll
+      for (int p = 0; p < NP; ++p) {
+        wq[p][0] = *reinterpret_cast<const uint4*>(sb + p * 1024 + lane * 16);
+        wq[p][1] = *reinterpret_cast<const uint4*>(sb + p * 1024 + 512 + lane * 16);
+#pragma unroll
+        for (int q = 0; q < NG; ++q) {
+          const __half* sp = reinterpret_cast<const __half*>(sb + SG::kW + p * 128) + q * 16;
+          sc[p][q][0] = __half2float(sp[g]);
+          sc[p][q][1] = __half2float(sp[g + 8]);
+          if (!AWQ) {
+            const __half* zp = reinterpret_cast<const __half*>(sb + SG::kW + SG::kS + p * 128) + q * 16;
+            zz[p][q][0] = __half2float(zp[g]);
+            zz[p][q][1] = __half2float(zp[g + 8]);
+          }
+        }
+      }
+#pragma unroll
+      for (int n = 0; n < NT; ++n)
+#pragma unroll
+        for (int b = 0; b < 4; ++b)
+          bv[n][b] = bval[n] ? *reinterpret_cast<const uint4*>(sb + SG::kW + SG::kS + SG::kZ + (n * 4 + b) * 512 + lane * 16)
+                             : make_uint4(0, 0, 0, 0);
+      __syncwarp();  // every lane holds its operands before any lane refills this stage
 
 #pragma unroll
-    for (int b = 0; b < 4; ++b) {  // 32-wide block b of the step
+      for (int b = 0; b < 4; ++b) {  // 32-wide block b of the step
 #pragma unroll
-      for (int kt = 0; kt < 2; ++kt) {
-#pragma unroll
-        for (int n = 0; n < NT; ++n)
-          if (NT == 1 || n < ntc)
-            mma_bf16(xs[n][kt], ones, kt ? bv[n][b].z : bv[n][b].x, kt ? bv[n][b].w : bv[n][b].y);
-#pragma unroll
-        for (int p = 0; p < NP; ++p) {
-          const uint4& q4 = wq[p][b >> 1];
-          const int wi = (b & 1) * 2 + kt;
-          const uint32_t wd = wi == 0 ? q4.x : wi == 1 ? q4.y : wi == 2 ? q4.z : q4.w;
-          uint32_t af[4];
-          raw_word(wd, af);
+        for (int kt = 0; kt < 2; ++kt) {
 #pragma unroll
           for (int n = 0; n < NT; ++n)
             if (NT == 1 || n < ntc)
-              mma_bf16(tmp[p][n][kt], af, kt ? bv[n][b].z : bv[n][b].x, kt ? bv[n][b].w : bv[n][b].y);
+              mma_bf16(xs[n][kt], ones, kt ? bv[n][b].z : bv[n][b].x, kt ? bv[n][b].w : bv[n][b].y);
+#pragma unroll
+          for (int p = 0; p < NP; ++p) {
+            const uint4& q4 = wq[p][b >> 1];
+            const int wi = (b & 1) * 2 + kt;
+            const uint32_t wd = wi == 0 ? q4.x : wi == 1 ? q4.y : wi == 2 ? q4.z : q4.w;
+            uint32_t af[4];
+            raw_word(wd, af);
+#pragma unroll
+            for (int n = 0; n < NT; ++n)
+              if (NT == 1 || n < ntc)
+                mma_bf16(tmp[p][n][kt], af, kt ? bv[n][b].z : bv[n][b].x, kt ? bv[n][b].w : bv[n][b].y);
+          }
+        }
+        if ((b + 1) % GSB == 0) {  // group end
+          const int q = b / GSB;
+#pragma unroll
+          for (int n = 0; n < NT; ++n)
+#pragma unroll
+            for (int r = 0; r < 4; ++r) xs[n][0][r] += xs[n][1][r];
+#pragma unroll
+          for (int p = 0; p < NP; ++p)
+#pragma unroll
+            for (int n = 0; n < NT; ++n)
+#pragma unroll
+              for (int r = 0; r < 4; ++r) {
+                const float pr = tmp[p][n][0][r] + tmp[p][n][1][r];
+                const float v = __fmaf_rn(-bias, xs[n][0][r], pr);  // sum x*(q - zp)
+                acc[p][n][r] = __fmaf_rn(v, sc[p][q][r >> 1], acc[p][n][r]);
+                if (!AWQ) acc[p][n][r] = __fmaf_rn(zz[p][q][r >> 1], xs[n][0][r], acc[p][n][r]);
+                tmp[p][n][0][r] = tmp[p][n][1][r] = 0.f;
+              }
+#pragma unroll
+          for (int n = 0; n < NT; ++n)
+#pragma unroll
+            for (int r = 0; r < 4; ++r) xs[n][0][r] = xs[n][1][r] = 0.f;
         }
       }
-      if ((b + 1) % GSB == 0) {  // group end
-        const int q = b / GSB;
+    }
+    cp_async_wait<0>();
+
+    if (ks > 1) {  // K-slice reduction in warp order, in each warp's drained stages
+      float* slot = reinterpret_cast<float*>(wbase);
+#pragma unroll
+      for (int p = 0; p < NP; ++p)
 #pragma unroll
         for (int n = 0; n < NT; ++n)
 #pragma unroll
-          for (int r = 0; r < 4; ++r) xs[n][0][r] += xs[n][1][r];
+          for (int r = 0; r < 4; ++r) slot[((p * NT + n) * 4 + r) * 32 + lane] = acc[p][n][r];
+      __syncthreads();
+      if (slice == 0) {
 #pragma unroll
         for (int p = 0; p < NP; ++p)
 #pragma unroll
           for (int n = 0; n < NT; ++n)
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
-              const float pr = tmp[p][n][0][r] + tmp[p][n][1][r];
-              const float v = __fmaf_rn(-bias, xs[n][0][r], pr);  // sum x*(q - zp)
-              acc[p][n][r] = __fmaf_rn(v, sc[p][q][r >> 1], acc[p][n][r]);
-              if (!AWQ) acc[p][n][r] = __fmaf_rn(zz[p][q][r >> 1], xs[n][0][r], acc[p][n][r]);
-              tmp[p][n][0][r] = tmp[p][n][1][r] = 0.f;
+              float v = acc[p][n][r];
+              for (int w = 1; w < ks; ++w) {
+                const float* o = reinterpret_cast<const float*>(wsm + (size_t)(warp + w) * kStagesW * SG::kBytes);
+                v += o[((p * NT + n) * 4 + r) * 32 + lane];
+              }
+              acc[p][n][r] = v;
             }
-#pragma unroll
-        for (int n = 0; n < NT; ++n)
-#pragma unroll
-          for (int r = 0; r < 4; ++r) xs[n][0][r] = xs[n][1][r] = 0.f;
       }
     }
-  }
-  cp_async_wait<0>();
-
-  if (ks > 1) {  // K-slice reduction in warp order, in each warp's drained stages
-    float* slot = reinterpret_cast<float*>(wbase);
+    if (live && slice == 0) {
+      // C fragment (row g / g+8, col 2t / 2t+1) of each N-tile
+      const int m0 = rt * 16 + g, m1 = m0 + 8;
 #pragma unroll
-    for (int p = 0; p < NP; ++p)
-#pragma unroll
-      for (int n = 0; n < NT; ++n)
-#pragma unroll
-        for (int r = 0; r < 4; ++r) slot[((p * NT + n) * 4 + r) * 32 + lane] = acc[p][n][r];
-    __syncthreads();
-    if (slice != 0) return;
-#pragma unroll
-    for (int p = 0; p < NP; ++p)
-#pragma unroll
-      for (int n = 0; n < NT; ++n)
+      for (int n = 0; n < NT; ++n) {
+        if (n >= ntc) continue;
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
-          float v = acc[p][n][r];
-          for (int w = 1; w < ks; ++w) {
-            const float* o = reinterpret_cast<const float*>(wsm + (size_t)(warp + w) * kStagesW * SG::kBytes);
-            v += o[((p * NT + n) * 4 + r) * 32 + lane];
+          const int col = 8 * n + 2 * t + (r & 1);
+          const int m = (r < 2) ? m0 : m1;
+          if (col >= it.nrows || m >= a.M) continue;
+          const size_t o = (size_t)(it.row0 + col) * a.ldo + m;
+          float v = acc[0][n][r];
+          if (!isfinite(v)) v = 0.f;  // non-finite -> 0, as every reference GEMV does
+          if (MODE == MODE_GATE_UP) {
+            float uu = acc[NP - 1][n][r];
+            if (!isfinite(uu)) uu = 0.f;
+            reinterpret_cast<__nv_bfloat16*>(a.out)[o] = __float2bfloat16_rn(silu_mul(v, uu));
+          } else {
+            reinterpret_cast<float*>(a.out)[o] = v;
           }
-          acc[p][n][r] = v;
         }
-  }
-  if (!live) return;
-
-  // C fragment (row g / g+8, col 2t / 2t+1) of each N-tile
-  const int m0 = rt * 16 + g, m1 = m0 + 8;
-#pragma unroll
-  for (int n = 0; n < NT; ++n) {
-    if (n >= ntc) continue;
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const int col = 8 * n + 2 * t + (r & 1);
-      const int m = (r < 2) ? m0 : m1;
-      if (col >= it.nrows || m >= a.M) continue;
-      const size_t o = (size_t)(it.row0 + col) * a.ldo + m;
-      float v = acc[0][n][r];
-      if (!isfinite(v)) v = 0.f;  // non-finite -> 0, as every reference GEMV does
-      if (MODE == MODE_GATE_UP) {
-        float uu = acc[NP - 1][n][r];
-        if (!isfinite(uu)) uu = 0.f;
-        reinterpret_cast<__nv_bfloat16*>(a.out)[o] = __float2bfloat16_rn(silu_mul(v, uu));
-      } else {
-        reinterpret_cast<float*>(a.out)[o] = v;
       }
     }
+    if (ks > 1) __syncthreads();  // the next item's copies reuse the reduction slots
   }
 }
 
@@ -1092,13 +1100,16 @@ cudaError_t launch_dequant(const ProjDev& P, int M, int K, int gs, int awq, int 
 }
 
 cudaError_t launch_gemm(int mode, int path, const GemmArgs& a, int max_work, int awq,
-                        int ntiles, cudaStream_t st, int n_groups) {
+                        int ntiles, cudaStream_t st, int n_groups, int grid_items) {
   if (max_work <= 0) return cudaSuccess;
   const int Mt = (a.M + 15) / 16;
   dim3 grid((Mt + 3) / 4, max_work);
   if (path == 0) {
+    // the K-split kernel walks the work list grid-stride: its grid covers the
+    // expected items, not the work list's capacity bound
+    const int gy = grid_items > 0 ? std::min(max_work, grid_items) : max_work;
     // K split: enough warps to cover the SMs when the expected work is small
-    const long units = (long)Mt * max_work;
+    const long units = (long)Mt * gy;
     const long units_est = (long)Mt * std::min(max_work, n_groups > 0 ? n_groups : max_work);
     const int nsteps = a.K / 128;
     const int ks = nsteps >= 8 && units < 148 * 16 ? 4 : (nsteps >= 8 ? 2 : 1);
@@ -1112,9 +1123,9 @@ cudaError_t launch_gemm(int mode, int path, const GemmArgs& a, int max_work, int
       else
         launch_mma_p<MODE_PLAIN_F32>(a, awq, st);
     } else if (mode == MODE_GATE_UP) {
-      launch_mma<MODE_GATE_UP>(a, max_work, ntiles, ks, awq, st);
+      launch_mma<MODE_GATE_UP>(a, gy, ntiles, ks, awq, st);
     } else {
-      launch_mma<MODE_PLAIN_F32>(a, max_work, ntiles, ks, awq, st);
+      launch_mma<MODE_PLAIN_F32>(a, gy, ntiles, ks, awq, st);
     }
   } else if (path == 1) {
     if (mode == MODE_GATE_UP)

@@ -118,9 +118,10 @@ cudaError_t launch_repack(const RepackArgs& a, cudaStream_t st);
 cudaError_t launch_dequant(const ProjDev& P, int M, int K, int gs, int awq, int zp, float* out,
                            cudaStream_t st);
 // path: 0 tensor-core (AWQ, bf16 B), 1 CUDA-core fp32 B, 2 CUDA-core bf16 B
-// n_groups: experts (groups) the rows can reach, for the decode kernel choice (0: unknown)
+// n_groups: experts (groups) the rows can reach, for the decode kernel choice (0: unknown);
+// grid_items: work items expected (0: max_work), the tensor-core K-split grid's height
 cudaError_t launch_gemm(int mode, int path, const GemmArgs& a, int max_work, int awq, int ntiles,
-                        cudaStream_t st, int n_groups = 0);
+                        cudaStream_t st, int n_groups = 0, int grid_items = 0);
 // int4_tma.cu: the same grouped GEMM fed by cp.async.bulk through a shared-
 // memory stage ring (decode-size items, K % 128 == 0, gs in {32, 64, 128}).
 cudaError_t launch_gemm_tma(int mode, const GemmArgs& a, int max_work, int awq, cudaStream_t st);

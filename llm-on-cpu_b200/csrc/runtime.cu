@@ -672,7 +672,7 @@ llmoc_status run_route(const llmoc_moe_layer* L, const uint16_t* X, int T, const
 // slots into Y (bf16; `weights` null = 1).
 llmoc_status run_ffn(const llmoc_moe_layer* L, const uint16_t* X, int R, int kk, int chunk, const WsLayout& w,
                      char* ws, uint16_t* Y, const float* weights, cudaStream_t st, StageEvents* se = nullptr,
-                     const uint16_t* residual = nullptr) {
+                     const uint16_t* residual = nullptr, int expect_pairs = 0) {
   const int H = L->d.hidden, I = L->d.inter;
   const bool awq = L->d.scheme == LLMOC_SCHEME_AWQ_SYM;
   // tensor cores when K of both GEMMs is a multiple of 128 and the group is
@@ -683,7 +683,10 @@ llmoc_status run_ffn(const llmoc_moe_layer* L, const uint16_t* X, int R, int kk,
   const bool umma = use_umma_c(L, chunk);
   if (tc && gemm_path_pref() == 2) path = 2;
   const int n_pairs = R * kk;
-  const int n_groups = std::min(n_pairs, L->n_exp);  // experts (groups) the pairs can reach
+  // rows expected to be occupied (padded receive slots: fewer than R * kk)
+  const int n_expect = expect_pairs > 0 ? std::min(expect_pairs, n_pairs) : n_pairs;
+  const int n_groups = std::min(n_expect, L->n_exp);  // experts (groups) the pairs can reach
+  const int grid_items = n_groups + (n_expect + chunk - 1) / chunk;  // work items expected
   if (umma) {
     if (!cuda_ok(launch_gather_rows(X, H, (const int*)(ws + w.sorted), kk, n_pairs,
                                     (const int*)(ws + w.offsets) + L->n_exp, ws + w.xs, st),
@@ -718,7 +721,8 @@ llmoc_status run_ffn(const llmoc_moe_layer* L, const uint16_t* X, int R, int kk,
   }
   if (!cuda_ok(umma ? launch_gemm_umma(MODE_GATE_UP, a, w.max_work, awq, n_pairs, st)
                : tma && path == 0 ? launch_gemm_tma(MODE_GATE_UP, a, w.max_work, awq, st)
-                                  : launch_gemm(MODE_GATE_UP, path, a, w.max_work, awq, ntiles, st, n_groups),
+                                  : launch_gemm(MODE_GATE_UP, path, a, w.max_work, awq, ntiles, st, n_groups,
+                                                grid_items),
                "gate/up"))
     return LLMOC_ERR_CUDA;
   if (se) se->mark(st);
@@ -736,7 +740,8 @@ llmoc_status run_ffn(const llmoc_moe_layer* L, const uint16_t* X, int R, int kk,
   b.ctr = (int*)(ws + w.err) + 2;
   if (!cuda_ok(umma ? launch_gemm_umma(MODE_PLAIN_F32, b, w.max_work, awq, n_pairs, st)
                : tma && path == 0 ? launch_gemm_tma(MODE_PLAIN_F32, b, w.max_work, awq, st)
-                                  : launch_gemm(MODE_PLAIN_F32, path, b, w.max_work, awq, ntiles, st, n_groups),
+                                  : launch_gemm(MODE_PLAIN_F32, path, b, w.max_work, awq, ntiles, st, n_groups,
+                                                grid_items),
                "down"))
     return LLMOC_ERR_CUDA;
   if (se) se->mark(st);
@@ -1406,7 +1411,7 @@ llmoc_status ep_experts(const llmoc_moe_layer* L, const uint16_t* rows, const in
   char* ws = (char*)workspace;
   llmoc_status rc = run_permute(expert, n, L->n_exp, chunk, w, ws, st);
   if (rc != LLMOC_OK) return rc;
-  return run_ffn(L, rows, n, 1, chunk, w, ws, out_rows, nullptr, st);
+  return run_ffn(L, rows, n, 1, chunk, w, ws, out_rows, nullptr, st, nullptr, nullptr, n_hint);
 }
 }  // namespace
 

@@ -160,6 +160,23 @@ def test_p2p_transport_two_ranks_one_gpu(oracle, name, T):
             assert torch.equal(outs[k][r], outs[0][r]), (name, T, r, k)
 
 
+def test_p2p_transport_skewed_to_one_owner(oracle):
+    """Every routed slot lands on rank 0's experts (a selection bias of -16 on
+    the odd ones): rank 0 serves twice the rows that its own tokens x topk
+    predict, so its K-split GEMMs walk more work items than their grid has
+    rows of CTAs; rank 1 serves no routed rows at all."""
+    layer = orc.make_layer(oracle, np.random.default_rng(11), **CFGS["glm_like_shared_sigmoid"])
+    layer.bias[1::2] -= np.float32(16.0)
+    Xh = [orc.make_tokens(np.random.default_rng(70 + r), 40, layer.H) for r in range(2)]
+    outs, errs = _p2p_emulated(layer, 2, [G.bf16_dev(X) for X in Xh], 2)
+    assert errs == [0, 0]
+    for r in range(2):
+        Yref, ids, _, _ = oracle.moe_layer_forward(layer, Xh[r])
+        assert np.all(ids % 2 == 0)
+        _check(outs[0][r], Yref, ("skew", r))
+        assert torch.equal(outs[1][r], outs[0][r])
+
+
 def test_p2p_transport_world_one(oracle):
     """world = 1: the transport loops back to the rank itself."""
     layer = orc.make_layer(oracle, np.random.default_rng(8), **CFGS["glm_like_shared_sigmoid"])
