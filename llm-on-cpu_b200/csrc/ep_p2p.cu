@@ -122,8 +122,8 @@ __global__ void __launch_bounds__(256) k_ep_push_dispatch(EpP2PLayout L, char* c
 }
 
 // Waits for every peer's flag of `kind` to reach seq (one thread per peer,
-// bounded).  Dispatch: then marks the receive slots past each source's count
-// as empty (expert id -1) for the permutation.
+// bounded).  The permutation that follows a dispatch wait reads only each
+// source's first meta.x slots, so the slots past a count are never read.
 __global__ void __launch_bounds__(256) k_ep_wait(EpP2PLayout L, char* base, int kind, uint32_t seq, int* err) {
   __shared__ int timed_out;
   if (threadIdx.x == 0) timed_out = 0;
@@ -140,17 +140,7 @@ __global__ void __launch_bounds__(256) k_ep_wait(EpP2PLayout L, char* base, int 
     }
   }
   __syncthreads();
-  if (timed_out) {
-    if (threadIdx.x == 0) atomicOr(err, 2);
-    return;
-  }
-  if (kind != 0) return;
-  const int parity = seq & 1;
-  for (int s = 0; s < L.world; ++s) {
-    const int n = min(max(meta_at(base, L, parity, s)->x, 0), L.cap);
-    int* ids = ids_at(base, L, parity, s);
-    for (int i = n + threadIdx.x; i < L.cap; i += blockDim.x) ids[i] = -1;
-  }
+  if (timed_out && threadIdx.x == 0) atomicOr(err, 2);
 }
 
 // Owner side: the down GEMM's fp32 output rows (in expert-sorted order;

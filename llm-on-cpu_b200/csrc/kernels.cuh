@@ -33,6 +33,13 @@ struct PermArgs {
   int* n_active;
   int* err;         // device error word + kGemmCounters unit counters, all cleared here for the kernels that follow
   int chunk;        // rows per work item (8, 16 or 32)
+  // segmented input (seg_len > 0): ids form n_seg segments of seg_len slots
+  // (n = n_seg * seg_len) of which the first seg_count[s * seg_stride]
+  // (clamped to [0, seg_len]) are occupied; only those are read, counted and
+  // placed (sorted / inverse), in slot order -- the NVLink transport's
+  // per-source receive regions
+  const int* seg_count;
+  int seg_stride, seg_len, n_seg;
 };
 
 constexpr int kGemmCounters = 2;  // err[1], err[2]: unit counters of the gate/up and down GEMMs

@@ -452,14 +452,34 @@ __global__ void __launch_bounds__(256) k_topk(TopkArgs a) {
 __device__ __forceinline__ void permute_block(const PermArgs& a, int* cnt) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int i = threadIdx.x; i < kPermWarps * a.n_exp; i += kPermThreads) cnt[i] = 0;
+  // Index space walked: 0..nv-1.  Plain input: the slots themselves.
+  // Segmented input: the occupied slots of each segment, segment after
+  // segment (slot order), v -> slot via the segments' exclusive offsets.
+  __shared__ int seg_off[kEpMaxWorld + 1];
+  const bool segd = a.seg_len > 0;
+  if (segd && threadIdx.x == 0) {
+    int o = 0;
+    for (int s = 0; s < a.n_seg; ++s) {
+      seg_off[s] = o;
+      o += min(max(a.seg_count[(size_t)s * a.seg_stride], 0), a.seg_len);
+    }
+    seg_off[a.n_seg] = o;
+  }
   __syncthreads();
+  const int nv = segd ? seg_off[a.n_seg] : a.n;
+  auto slot_of = [&](int v) {
+    if (!segd) return v;
+    int s = 0;
+    while (v >= seg_off[s + 1]) ++s;
+    return s * a.seg_len + (v - seg_off[s]);
+  };
 
-  const int per = (a.n + kPermWarps - 1) / kPermWarps;
-  const int lo = min(a.n, warp * per), hi = min(a.n, lo + per);
+  const int per = (nv + kPermWarps - 1) / kPermWarps;
+  const int lo = min(nv, warp * per), hi = min(nv, lo + per);
   // ids outside [0, n_exp) are empty slots (the padded receive layout of the
   // NVLink expert-parallel transport): not counted, not placed, inverse -1
-  for (int i = lo + lane; i < hi; i += 32) {
-    const int ex = a.ids[i];
+  for (int v = lo + lane; v < hi; v += 32) {
+    const int ex = a.ids[slot_of(v)];
     if ((unsigned)ex < (unsigned)a.n_exp) atomicAdd(&cnt[warp * a.n_exp + ex], 1);
   }
   __syncthreads();
@@ -537,10 +557,11 @@ __device__ __forceinline__ void permute_block(const PermArgs& a, int* cnt) {
 
   // placement: each warp walks its own range in order, 32 pairs at a time.
   for (int b = lo; b < hi; b += 32) {
-    const int i = b + lane;
-    const int ex = i < hi ? a.ids[i] : -1;
+    const int v = b + lane;
+    const int i = v < hi ? slot_of(v) : 0;
+    const int ex = v < hi ? a.ids[i] : -1;
     const bool ok = (unsigned)ex < (unsigned)a.n_exp;
-    if (i < hi && !ok) a.inverse[i] = -1;
+    if (v < hi && !ok) a.inverse[i] = -1;
     const unsigned act = __ballot_sync(0xffffffffu, ok);
     if (ok) {
       const unsigned peers = __match_any_sync(act, ex);

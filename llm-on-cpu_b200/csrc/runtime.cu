@@ -619,9 +619,21 @@ PermArgs perm_args(const int* ids, int n, int n_perm, int chunk, const WsLayout&
   return pa;
 }
 
+// Segments (seg_len > 0): ids are n_seg regions of seg_len slots, the first
+// seg_count[s * seg_stride] of each occupied (PermArgs).
+struct PermSegs {
+  const int* count = nullptr;
+  int stride = 0, len = 0, n = 0;
+};
+
 llmoc_status run_permute(const int* ids, int n, int n_perm, int chunk, const WsLayout& w, char* ws,
-                         cudaStream_t st) {
-  if (!cuda_ok(launch_permute(perm_args(ids, n, n_perm, chunk, w, ws), st), "permute")) return LLMOC_ERR_CUDA;
+                         cudaStream_t st, const PermSegs& segs = PermSegs{}) {
+  PermArgs pa = perm_args(ids, n, n_perm, chunk, w, ws);
+  pa.seg_count = segs.count;
+  pa.seg_stride = segs.stride;
+  pa.seg_len = segs.len;
+  pa.n_seg = segs.n;
+  if (!cuda_ok(launch_permute(pa, st), "permute")) return LLMOC_ERR_CUDA;
   count_launch(1);
   return LLMOC_OK;
 }
@@ -1402,14 +1414,15 @@ llmoc_status llmoc_moe_ep_dispatch(const llmoc_moe_layer* L, const uint16_t* X, 
 namespace {
 // n rows (expert ids < 0: empty slots), about n_hint of them occupied (sets the kernel regime)
 llmoc_status ep_experts(const llmoc_moe_layer* L, const uint16_t* rows, const int32_t* expert, int n, int n_hint,
-                        uint16_t* out_rows, void* workspace, size_t workspace_bytes, void* stream) {
+                        uint16_t* out_rows, void* workspace, size_t workspace_bytes, void* stream,
+                        const PermSegs& segs = PermSegs{}) {
   const int chunk = chunk_for_rows(n_hint, L->e_loc);
   const WsLayout w = ws_layout_g(L, n, 1, L->n_exp, chunk, false);
   if (!workspace || workspace_bytes < w.total) return fails(LLMOC_ERR_WORKSPACE, "workspace too small");
   DevGuard dg(L->device);
   cudaStream_t st = (cudaStream_t)stream;
   char* ws = (char*)workspace;
-  llmoc_status rc = run_permute(expert, n, L->n_exp, chunk, w, ws, st);
+  llmoc_status rc = run_permute(expert, n, L->n_exp, chunk, w, ws, st, segs);
   if (rc != LLMOC_OK) return rc;
   return run_ffn(L, rows, n, 1, chunk, w, ws, out_rows, nullptr, st, nullptr, nullptr, n_hint);
 }
@@ -1896,7 +1909,13 @@ llmoc_status llmoc_ep_p2p_serve(const llmoc_moe_layer* L, llmoc_ep_transport* tr
   // the grouped FFN over the padded slots, without the output-row pass: the
   // return push reads the down GEMM's fp32 rows through the inverse map
   const int n_hint = std::max(1, T * L->d.topk);
-  rc = ep_experts(L, rows, ids, slots, n_hint, nullptr, ws + w.own, ep_owner_bytes(L, slots), stream);
+  // the permutation reads only each source's occupied slots (its count in the meta)
+  PermSegs segs;
+  segs.count = (const int*)(tr->base + tr->lay.meta) + (size_t)parity * tr->world * 2;
+  segs.stride = 2;
+  segs.len = tr->lay.cap;
+  segs.n = tr->world;
+  rc = ep_experts(L, rows, ids, slots, n_hint, nullptr, ws + w.own, ep_owner_bytes(L, slots), stream, segs);
   if (rc != LLMOC_OK) return rc;
   const WsLayout wo = ws_layout_g(L, slots, 1, L->n_exp, chunk_for_rows(n_hint, L->e_loc), false);
   if (!cuda_ok(launch_ep_push_return(tr->lay, tr->peers_dev, tr->base, (const float*)(ws + w.own + wo.partial),
