@@ -104,6 +104,12 @@ LLMOC_API const char* llmoc_last_error(void);
 
 /* hal::cuda::try_gemm_int4 (cuda_backend.h:165; .cpp:2692): y[M] = W . x */
 LLMOC_API int llmoc_try_gemm_int4(const float* x, const llmoc_int4_view* W, float* y);
+/* hal::gemm_int4_argmax (int4_ops.h:13-19; .cpp:344-446): greedy decode over
+ * an INT4 lm_head, argmax_m of (W . x)[m] without returning the logits.  Row
+ * values as the reference sums them (within the GEMV tolerance); non-finite
+ * rows count as -1e30; equal maxima -> the smallest row.  index/value are the
+ * fields of hal::Int4ArgmaxResult.  1 = done, 0 = the caller runs its CPU path. */
+LLMOC_API int llmoc_try_gemm_int4_argmax(const float* x, const llmoc_int4_view* W, int32_t* index, float* value);
 /* hal::cuda::try_gemm_int4_batch (cuda_backend.h:166; .cpp:2858): Y[n,M] = X[n,K] . W^T */
 LLMOC_API int llmoc_try_gemm_int4_batch(const float* X, int n, const llmoc_int4_view* W, float* Y);
 /* hal::cuda::try_gemm_int4_multi (cuda_backend.h:172; .cpp:3048): 2..4 weights sharing x */

@@ -947,7 +947,7 @@ __global__ void __launch_bounds__(128) k_int4_cc(GemmArgs a, int awq) {
           if (!bv[j]) continue;
           const size_t o = (size_t)(it.row0 + r0 + j) * a.ldo + m;
           float v = acc[0][h][j];
-          if (!isfinite(v)) v = 0.f;
+          if (!isfinite(v) && !(MODE == MODE_PLAIN_F32 && a.keep_nonfinite)) v = 0.f;
           if (MODE == MODE_GATE_UP) {
             float u = acc[NP - 1][h][j];
             if (!isfinite(u)) u = 0.f;
@@ -1075,6 +1075,42 @@ __global__ void k_quant_awq_sym(const __nv_bfloat16* __restrict__ W, int M, int 
       qo[k / 2] = (uint8_t)((uint32_t)q0 | ((uint32_t)q1 << 4));
     }
   }
+}
+
+// ------------------------------------------------------------------ argmax
+
+// Key of row m: the value (non-finite -> -1e30, -0 -> +0) mapped to bits that
+// order as the floats do, above 0xFFFFFFFF - m, so the largest key is the
+// largest value and, among equal values, the smallest row.
+__device__ __forceinline__ unsigned long long argmax_key(float v, int m) {
+  if (!isfinite(v)) v = -1e30f;
+  if (v == 0.f) v = 0.f;
+  uint32_t b = __float_as_uint(v);
+  b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return ((unsigned long long)b << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)m);
+}
+
+__global__ void __launch_bounds__(256) k_argmax_rows(const float* __restrict__ y, int M,
+                                                     unsigned long long* key) {
+  unsigned long long best = 0;
+  for (int m = blockIdx.x * blockDim.x + threadIdx.x; m < M; m += gridDim.x * blockDim.x)
+    best = max(best, argmax_key(__ldg(y + m), m));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
+  __shared__ unsigned long long wbest[8];
+  if ((threadIdx.x & 31) == 0) wbest[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < 8; ++w) best = max(best, wbest[w]);
+    atomicMax(key, best);
+  }
+}
+
+cudaError_t launch_argmax_rows(const float* y, int M, unsigned long long* key, cudaStream_t st) {
+  cudaError_t e = cudaMemsetAsync(key, 0, sizeof(unsigned long long), st);
+  if (e != cudaSuccess || M <= 0) return e;
+  k_argmax_rows<<<std::min(148 * 4, (M + 255) / 256), 256, 0, st>>>(y, M, key);
+  return cudaGetLastError();
 }
 
 // -------------------------------------------------------------- launchers

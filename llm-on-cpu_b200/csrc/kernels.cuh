@@ -1,6 +1,8 @@
 // kernels.cuh — argument structs and launchers shared by the kernel files
 // (route.cu, int4_gemm.cu) and the host runtime (runtime.cu).
 #pragma once
+#include <cstring>
+
 #include "common.cuh"
 
 namespace llmoc {
@@ -119,7 +121,21 @@ struct GemmArgs {
   int* err;               // device error word: bit 0 = a bounded wait gave up (may be null)
   const void* wmaps;      // tcgen05 path: per-expert TMA maps of the weights (build_umma_weight_maps)
   int* ctr;               // persistent decode kernel: unit counter, zeroed by the permutation (or null)
+  int keep_nonfinite;     // cc kernel, PLAIN_F32: store non-finite sums as they are (argmax input)
 };
+
+// Argmax over y[M] (hal::gemm_int4_argmax semantics: non-finite -> -1e30,
+// the first of equal maxima): *key = max over rows of the key of (y[m], m),
+// the value's order-preserving bits above ~m; decode with argmax_decode.
+cudaError_t launch_argmax_rows(const float* y, int M, unsigned long long* key, cudaStream_t st);
+inline void argmax_decode(unsigned long long key, int32_t* index, float* value) {
+  const uint32_t b = (uint32_t)(key >> 32);
+  const uint32_t bits = (b & 0x80000000u) ? (b & 0x7FFFFFFFu) : ~b;
+  float v;
+  memcpy(&v, &bits, 4);
+  *value = v;
+  *index = (int32_t)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull));
+}
 
 cudaError_t launch_repack(const RepackArgs& a, cudaStream_t st);
 cudaError_t launch_dequant(const ProjDev& P, int M, int K, int gs, int awq, int zp, float* out,

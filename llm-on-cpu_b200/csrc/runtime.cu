@@ -260,20 +260,26 @@ struct Scratch {
 } g_scratch;
 
 // Dense Y[n,M] = X[n,K] . W^T through the CUDA-core fp32 kernel; X, Y host.
-int dense_gemm_host(const float* X, int n, const llmoc_int4_view* W, float* Y) {
-  if (!X || !Y || n <= 0) return fail("bad arguments");
+// With `am` (n = 1, Y unused): only the argmax of y comes back (index, value).
+struct ArgmaxOut {
+  int32_t* index;
+  float* value;
+};
+int dense_gemm_host(const float* X, int n, const llmoc_int4_view* W, float* Y, const ArgmaxOut* am = nullptr) {
+  if (!X || (!Y && !am) || n <= 0 || (am && n != 1)) return fail("bad arguments");
   Resident* r = ensure_resident(W);
   if (!r) return 0;
   const Geo& g = r->geo;
   const int nwork = (n + kChunkRows - 1) / kChunkRows;
   const size_t xb = align256((size_t)n * g.K * 4), yb = align256((size_t)n * g.M * 4);
   const size_t wb = align256((size_t)nwork * sizeof(WorkItem) + 16);
-  if (!g_scratch.ensure(xb + yb + wb)) return 0;
+  if (!g_scratch.ensure(xb + yb + wb + 256)) return 0;
   char* p = g_scratch.p;
   float* dX = (float*)p;
   float* dY = (float*)(p + xb);
   WorkItem* dW = (WorkItem*)(p + xb + yb);
   int* dN = (int*)(dW + nwork);
+  unsigned long long* dKey = (unsigned long long*)(p + xb + yb + wb);
   std::vector<WorkItem> work(nwork);
   for (int i = 0; i < nwork; ++i) work[i] = WorkItem{0, i * kChunkRows, std::min(kChunkRows, n - i * kChunkRows), 0};
   cudaStream_t st = g_stream;
@@ -298,10 +304,21 @@ int dense_gemm_host(const float* X, int n, const llmoc_int4_view* W, float* Y) {
   a.n_work = dN;
   a.out = dY;
   a.ldo = g.M;
+  a.keep_nonfinite = am ? 1 : 0;  // the argmax maps non-finite rows to -1e30, not 0
   if (!cuda_ok(launch_gemm(MODE_PLAIN_F32, 1, a, nwork, r->scheme == LLMOC_SCHEME_AWQ_SYM, 1, st),
                "gemm launch"))
     return 0;
   count_launch();
+  if (am) {
+    unsigned long long key = 0;
+    if (!cuda_ok(launch_argmax_rows(dY, g.M, dKey, st), "argmax launch") ||
+        !cuda_ok(cudaMemcpyAsync(&key, dKey, sizeof(key), cudaMemcpyDeviceToHost, st), "D2H argmax") ||
+        !cuda_ok(cudaStreamSynchronize(st), "gemm argmax"))
+      return 0;
+    count_launch();
+    argmax_decode(key, am->index, am->value);
+    return 1;
+  }
   if (!cuda_ok(cudaMemcpyAsync(Y, dY, (size_t)n * g.M * 4, cudaMemcpyDeviceToHost, st), "D2H y") ||
       !cuda_ok(cudaStreamSynchronize(st), "gemm"))
     return 0;
@@ -949,6 +966,13 @@ const char* llmoc_last_error(void) { return t_err.c_str(); }
 int llmoc_try_gemm_int4(const float* x, const llmoc_int4_view* W, float* y) {
   std::lock_guard<std::mutex> lk(g_mu);
   return dense_gemm_host(x, 1, W, y);
+}
+
+int llmoc_try_gemm_int4_argmax(const float* x, const llmoc_int4_view* W, int32_t* index, float* value) {
+  if (!x || !W || !index || !value || W->M <= 0) return fail("bad arguments");
+  std::lock_guard<std::mutex> lk(g_mu);
+  const ArgmaxOut am{index, value};
+  return dense_gemm_host(x, 1, W, nullptr, &am);
 }
 
 int llmoc_try_gemm_int4_batch(const float* X, int n, const llmoc_int4_view* W, float* Y) {

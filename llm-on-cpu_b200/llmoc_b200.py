@@ -76,6 +76,7 @@ _SIGS = {
     "llmoc_cuda_host_unregister": (_i, [_vp]),
     "llmoc_last_error": (C.c_char_p, []),
     "llmoc_try_gemm_int4": (_i, [_vp, C.POINTER(Int4View), _vp]),
+    "llmoc_try_gemm_int4_argmax": (_i, [_vp, C.POINTER(Int4View), C.POINTER(C.c_int32), C.POINTER(C.c_float)]),
     "llmoc_try_gemm_int4_batch": (_i, [_vp, _i, C.POINTER(Int4View), _vp]),
     "llmoc_try_gemm_int4_multi": (_i, [_vp, C.POINTER(C.POINTER(Int4View)), C.POINTER(_vp), _i]),
     "llmoc_try_gemm_int4_batch_multi": (_i, [_vp, _i, C.POINTER(C.POINTER(Int4View)),

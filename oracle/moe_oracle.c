@@ -243,6 +243,85 @@ ORC_API void orc_gemm_int4(const float* x, const orc_int4_view* W, float* y) {
   for (int m = 0; m < W->M; ++m) y[m] = orc_row(x, W, m, orc_is_single_row(W->M, m, 0));
 }
 
+/* Row value of hal::gemm_int4_argmax (int4_ops.cpp:344-381).  AWQ: per group
+ * dot_awq_noscale(x, q, zp) x scale accumulated in fp32 (:365-369); GPTQ: the
+ * scalar row gemm_row_scalar (:323-342), w = q * s + z in fp32 and the sum of
+ * x[k] * w in double.  awq_fma / w_fma / acc_fma: whether those multiply-adds
+ * are fused.  Against the compiled reference: the AWQ group sum is a multiply
+ * then an add (the fused form differed in 3 of 12 cases); for GPTQ the four
+ * forms gave the reference's result in all of 400 cases (the double sum hides
+ * the difference), and the unfused one is used. */
+static float orc_argmax_row(const float* x, const orc_int4_view* W, int m, int awq_fma, int w_fma, int acc_fma) {
+  const int K = W->K, gs = W->group_size, ng = orc_ng(W);
+  const size_t rb = (size_t)((K + 1) / 2);
+  const uint8_t* qrow = W->qweight + (size_t)m * rb;
+  if (W->scheme == ORC_SCHEME_AWQ_SYM) {
+    const float zp = (float)(W->awq_zp > 0 ? W->awq_zp : 7);
+    float acc = 0.f;
+    for (int g = 0; g < ng; ++g) {
+      const int k0 = g * gs;
+      const int k1 = (K < k0 + gs) ? K : k0 + gs;
+      const float s = orc_f16_to_f32(W->scales[(size_t)m * ng + g]);
+      const float p = orc_dot_awq_noscale(x, qrow, k0, k1, zp);
+      if (awq_fma) {
+        acc = fmaf(p, s, acc);
+      } else {
+        const float ps = p * s;
+        acc = acc + ps;
+      }
+    }
+    return acc;
+  }
+  double acc = 0.0;
+  for (int g = 0; g < ng; ++g) {
+    const int k0 = g * gs;
+    const int k1 = (K < k0 + gs) ? K : k0 + gs;
+    const float s = orc_f16_to_f32(W->scales[(size_t)m * ng + g]);
+    const float z = W->zeros ? orc_f16_to_f32(W->zeros[(size_t)m * ng + g]) : 0.f;
+    for (int k = k0; k < k1; ++k) {
+      const uint8_t b = qrow[k / 2];
+      const int qi = (k & 1) ? ((b >> 4) & 0xF) : (b & 0xF);
+      float w;
+      if (w_fma) {
+        w = fmaf((float)qi, s, z);
+      } else {
+        const float qs = (float)qi * s;
+        w = qs + z;
+      }
+      if (acc_fma) {
+        acc = fma((double)x[k], (double)w, acc);
+      } else {
+        const double xw = (double)x[k] * (double)w;
+        acc = acc + xw;
+      }
+    }
+  }
+  return (float)acc;
+}
+
+static void orc_argmax_v(const float* x, const orc_int4_view* W, int32_t* index, float* value, int awq_fma,
+                         int w_fma, int acc_fma) {
+  int32_t bi = 0;
+  float bv = -1e30f;
+  for (int m = 0; m < W->M; ++m) {
+    float v = orc_argmax_row(x, W, m, awq_fma, w_fma, acc_fma);
+    if (!isfinite(v)) v = -1e30f; /* :376 */
+    if (v > bv) {                 /* first maximum in row order (:424-431) */
+      bv = v;
+      bi = m;
+    }
+  }
+  *index = bi;
+  *value = bv;
+}
+
+/* hal::gemm_int4_argmax (int4_ops.cpp:344-446), the serial rule: the first
+ * maximum in row order (the reference's OpenMP branch for M >= 4096 breaks
+ * ties between threads by timing; with one thread it is this rule). */
+ORC_API void orc_gemm_int4_argmax(const float* x, const orc_int4_view* W, int32_t* index, float* value) {
+  orc_argmax_v(x, W, index, value, 0, 0, 0);
+}
+
 /* hal::gemm_int4_batch (int4_ops.cpp:621-638): Y[n,M] = X[n,K] . W^T.  The
  * token-tiled AVX2 kernels compute each (t, m) with the same chains as the
  * single-token kernel; only the row grouping differs (orc_is_single_row). */

@@ -163,6 +163,9 @@ class Oracle:
         self._gemm_int4 = g("gemm_int4")
         self._gemm_int4.argtypes = [_f32p, C.POINTER(Int4ViewC), _f32p]
         self._gemm_int4.restype = None
+        self._argmax = g("gemm_int4_argmax")
+        self._argmax.argtypes = [_f32p, C.POINTER(Int4ViewC), C.POINTER(C.c_int32), C.POINTER(C.c_float)]
+        self._argmax.restype = None
         self._gemm_int4_batch = g("gemm_int4_batch")
         self._gemm_int4_batch.argtypes = [_f32p, C.c_int, C.POINTER(Int4ViewC), _f32p]
         self._gemm_int4_batch.restype = None
@@ -215,6 +218,13 @@ class Oracle:
         v = W.view()
         self._gemm_int4(np.ascontiguousarray(x, np.float32), C.byref(v), y)
         return y
+
+    def gemm_int4_argmax(self, x: np.ndarray, W: Int4Weight):
+        """hal::gemm_int4_argmax: (index, value) of the largest row of W . x."""
+        i, v = C.c_int32(), C.c_float()
+        wv = W.view()
+        self._argmax(np.ascontiguousarray(x, np.float32), C.byref(wv), C.byref(i), C.byref(v))
+        return int(i.value), np.float32(v.value)
 
     def gemm_int4_batch(self, X: np.ndarray, W: Int4Weight) -> np.ndarray:
         X = np.ascontiguousarray(X, np.float32)

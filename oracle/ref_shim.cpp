@@ -83,6 +83,13 @@ __attribute__((visibility("default"))) void ref_gemm_int4(const float* x, const 
   hal::gemm_int4(x, to_view(*W), y);
 }
 
+__attribute__((visibility("default"))) void ref_gemm_int4_argmax(const float* x, const ref_int4_view* W,
+                                                                 int32_t* index, float* value) {
+  const hal::Int4ArgmaxResult r = hal::gemm_int4_argmax(x, to_view(*W));
+  *index = r.index;
+  *value = r.value;
+}
+
 __attribute__((visibility("default"))) void ref_gemm_int4_batch(const float* X, int n,
                                                                 const ref_int4_view* W, float* Y) {
   hal::gemm_int4_batch(X, n, to_view(*W), Y);

@@ -201,6 +201,56 @@ def layer_cases(O: orc.Oracle, R: orc.Reference) -> dict:
 
 # One MoE layer as the reference's tools write it: GPTQ experts, a shared
 # expert with its per-token gate, bf16 router; layer index 3 under "model.".
+# hal::gemm_int4_argmax (int4_ops.cpp:344-446) cases: weights drawn from
+# numpy seeds (rebuilt by the tests with argmax_weight), the reference's
+# (index, value) stored.  tie: rows 10 and 40 equal and largest; nan: a NaN in
+# x makes every row non-finite; large: M >= 4096 (the reference's OpenMP
+# branch, serial with one thread); neg: every row negative.
+ARGMAX_CASES = {
+    "awq": dict(seed=31, M=300, K=512, gs=128, scheme=2),
+    "gptq": dict(seed=32, M=200, K=256, gs=64, scheme=1),
+    "awq_tie": dict(seed=33, M=64, K=128, gs=64, scheme=2, tie=(10, 40)),
+    "awq_nan": dict(seed=34, M=48, K=128, gs=128, scheme=2, nan=True),
+    "awq_large": dict(seed=35, M=4099, K=64, gs=32, scheme=2),
+    "gptq_neg": dict(seed=36, M=96, K=128, gs=64, scheme=1, neg=True),
+}
+
+
+def argmax_weight(name: str):
+    """(x, Int4Weight) of an argmax case, from its seed alone."""
+    c = ARGMAX_CASES[name]
+    rng = np.random.default_rng(c["seed"])
+    M, K, gs = c["M"], c["K"], c["gs"]
+    ng = K // gs
+    q = rng.integers(0, 16, size=(M, K), dtype=np.uint8)
+    s = orc.bf16_round(rng.uniform(0.005, 0.02, size=(M, ng)).astype(np.float32))
+    x = rng.standard_normal(K).astype(np.float32)
+    if c.get("tie"):  # rows a and b equal, with q - 7 = 7 sign(x): the largest rows
+        a, b = c["tie"]
+        q[a] = np.where(x > 0, 14, 0).astype(np.uint8)
+        q[b], s[b] = q[a], s[a]
+    s16 = np.array([f32_to_f16bits_trunc(v) for v in s.reshape(-1)], np.uint16).reshape(M, ng)
+    z16 = None
+    if c["scheme"] == 1:
+        z = rng.uniform(0.0, 0.05, size=(M, ng)).astype(np.float32)
+        z16 = np.array([f32_to_f16bits_trunc(v) for v in z.reshape(-1)], np.uint16).reshape(M, ng)
+    if c.get("neg"):
+        x = -np.abs(x)
+    if c.get("nan"):
+        x[K // 3] = np.float32(np.nan)
+    W = orc.Int4Weight(pack(q), s16, z16, M, K, gs, c["scheme"], 7 if c["scheme"] == 2 else 0)
+    return x, W
+
+
+def argmax_cases(R: orc.Reference) -> dict:
+    out = {}
+    for name in ARGMAX_CASES:
+        x, W = argmax_weight(name)
+        i, v = R.gemm_int4_argmax(x, W)
+        out[name] = dict(index=np.int32(i), value=np.float32(v), x=x)
+    return out
+
+
 QLWC_CASE = dict(seed=21, layer=3, prefix="model.",
                  kw=dict(H=256, I=64, E=8, topk=2, gs=64, scheme=1, shared=True, shared_gate=True))
 
@@ -249,7 +299,7 @@ def main() -> None:
     assert R.max_threads() == 1, "run with OMP_NUM_THREADS=1 so the combine order is defined"
     groups = {"unit_cases": unit_cases(R), "quant_cases": quant_cases(qi),
               "router_cases": router_cases(R), "layer_cases": layer_cases(O, R),
-              "qlwc_cases": qlwc_cases(O, qi)}
+              "qlwc_cases": qlwc_cases(O, qi), "argmax_cases": argmax_cases(R)}
     for gname, cases in groups.items():
         flat = {}
         for cname, d in cases.items():

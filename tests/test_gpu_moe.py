@@ -342,6 +342,31 @@ def test_try_gemm_int4_reference_cases(case, fresh_cache):
     assert np.array_equal(dq.view(np.uint32), d["dq"].view(np.uint32))
 
 
+@pytest.mark.parametrize("case", ["awq", "gptq", "awq_tie", "awq_nan", "awq_large", "gptq_neg"])
+def test_try_gemm_int4_argmax(oracle, case, fresh_cache):
+    """llmoc_try_gemm_int4_argmax against the reference's hal::gemm_int4_argmax
+    (golden cases): equal largest rows -> the first; every row non-finite ->
+    (0, -1e30); otherwise the same row wherever the oracle's top two rows are
+    further apart than the GEMV tolerance, and the value within rel 1e-3 (the
+    reference GPU tests' bar)."""
+    import make_golden as mg
+
+    g = np.load(f"{mg.HERE}/argmax_cases.npz")
+    x, W = mg.argmax_weight(case)
+    want_i, want_v = int(g[f"{case}/index"]), np.float32(g[f"{case}/value"])
+    idx, val = C.c_int32(-1), C.c_float(0.0)
+    v = L.view_of(W)
+    assert L.lib.llmoc_try_gemm_int4_argmax(L.ptr(x), C.byref(v), C.byref(idx), C.byref(val)) == 1, L.last_error()
+    if case == "awq_nan":
+        assert (idx.value, val.value) == (0, np.float32(-1e30))
+        return
+    y = oracle.gemm_int4(x, W)
+    top = np.sort(y)[-2:]
+    if case == "awq_tie" or top[1] - top[0] > 1e-3 * (1 + abs(top[1])):
+        assert idx.value == want_i
+    assert abs(val.value - want_v) < 1e-3 * (1 + abs(want_v))
+
+
 @pytest.mark.parametrize("case", ["awq_batch", "gptq_batch"])
 def test_try_gemm_int4_batch_reference_cases(case, fresh_cache):
     d, W = unit_case(case)

@@ -52,6 +52,25 @@ def test_reference_unit_cases(oracle, case):
             assert np.all(np.abs(oracle.gemm_int4(d["X"][t], W) - Y[t]) < 1e-4 * (1 + np.abs(Y[t])))
 
 
+ARGMAX = ["awq", "gptq", "awq_tie", "awq_nan", "awq_large", "gptq_neg"]
+
+
+@pytest.mark.parametrize("case", ARGMAX)
+def test_argmax_cases(oracle, case):
+    """hal::gemm_int4_argmax (greedy lm_head): the oracle's (index, value)
+    equal the reference's bits on every case -- AWQ and GPTQ rows, equal
+    largest rows (the first wins), a NaN input (every row non-finite: value
+    -1e30, index 0), M >= 4096, all rows negative."""
+    import make_golden as mg
+
+    g = gold("argmax_cases")
+    x, W = mg.argmax_weight(case)
+    assert bits_equal(x, g[f"{case}/x"])
+    i, v = oracle.gemm_int4_argmax(x, W)
+    assert i == int(g[f"{case}/index"])
+    assert bits_equal(v, g[f"{case}/value"])
+
+
 @pytest.mark.parametrize("gs", [32, 128])
 def test_quantizers_match_reference_tool(oracle, gs):
     """quant_awq_sym / quant_gptq_asym of tools/quantize_int4.py, byte for byte."""
