@@ -370,6 +370,48 @@ LLMOC_API llmoc_status llmoc_ep_p2p_finish(const llmoc_moe_layer* shard, llmoc_e
                                            int T, uint16_t* Y, uint32_t seq, void* workspace,
                                            size_t workspace_bytes, void* stream);
 
+/* --------------------------------------------------- NVLink collectives */
+
+/* contracts::ICollective (src/contracts/collective.h:9-15) between the ranks
+ * of one box, one process (or one ranks' object) per GPU, over peer memory
+ * opened with CUDA IPC -- the implementation that exec/mesh_nccl.cpp:85-134
+ * leaves as stubs.  Every rank makes the same calls in the same order; each
+ * call is a step (numbered inside the object).  Operations (op):
+ *   LLMOC_COLL_ALLTOALL       send = world chunks of `bytes`; chunk d goes to
+ *                             rank d, which receives it as its chunk `rank`
+ *   LLMOC_COLL_ALLREDUCE_SUM  elementwise sum over ranks of a buffer of
+ *                             `bytes` (dtype fp32 or bf16; fp32 accumulation
+ *                             in rank order, so every rank gets the same bits)
+ *   LLMOC_COLL_BROADCAST      root's buffer of `bytes` to every rank
+ * bytes <= the max_bytes given at creation.  Asynchronous on `stream`; a wait
+ * that gives up (~1 s) sets bit 1 of llmoc_collective_error and the step's
+ * result is invalid.  start / finish split a step in two (the first pushes,
+ * the second waits and consumes) so that several ranks' objects can share
+ * one stream in one process; the op calls are start + finish. */
+enum { LLMOC_COLL_ALLTOALL = 0, LLMOC_COLL_ALLREDUCE_SUM = 1, LLMOC_COLL_BROADCAST = 2 };
+enum { LLMOC_DTYPE_F32 = 0, LLMOC_DTYPE_BF16 = 1 };
+typedef struct llmoc_collective llmoc_collective;
+/* Allocates this rank's buffer (2 x world x max_bytes of staging) and writes
+ * its IPC handle (llmoc_ep_ipc_handle_bytes() bytes; may be null for
+ * llmoc_collective_connect_local). */
+LLMOC_API llmoc_status llmoc_collective_create(int world, int rank, size_t max_bytes, int device,
+                                               llmoc_collective** out, void* ipc_handle);
+LLMOC_API llmoc_status llmoc_collective_connect(llmoc_collective* c, const void* handles);
+LLMOC_API llmoc_status llmoc_collective_connect_local(llmoc_collective* c, llmoc_collective* const* all);
+LLMOC_API void llmoc_collective_destroy(llmoc_collective* c);
+LLMOC_API int llmoc_collective_world_size(const llmoc_collective* c);
+LLMOC_API int llmoc_collective_error(llmoc_collective* c);
+LLMOC_API llmoc_status llmoc_collective_start(llmoc_collective* c, int op, const void* src, size_t bytes, int root,
+                                              void* stream);
+LLMOC_API llmoc_status llmoc_collective_finish(llmoc_collective* c, int op, void* dst, size_t bytes, int dtype,
+                                               int root, void* stream);
+LLMOC_API llmoc_status llmoc_collective_alltoall(llmoc_collective* c, const void* send, void* recv, size_t bytes,
+                                                 void* stream);
+LLMOC_API llmoc_status llmoc_collective_allreduce_sum(llmoc_collective* c, void* inout, size_t bytes, int dtype,
+                                                      void* stream);
+LLMOC_API llmoc_status llmoc_collective_broadcast(llmoc_collective* c, void* buf, size_t bytes, int root,
+                                                  void* stream);
+
 /* ------------------------------------------------------------ utilities */
 
 /* quant_awq_sym (tools/quantize_int4.py:150-166) on the device: W [M,K] bf16

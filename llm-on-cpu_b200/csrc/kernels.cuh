@@ -91,6 +91,18 @@ cudaError_t launch_ep_wait(const EpP2PLayout& L, char* base, int kind, uint32_t 
 cudaError_t launch_ep_push_return(const EpP2PLayout& L, char* const* peers, char* base, const float* partial,
                                   const int* inverse, int rank, uint32_t seq, int* ctr, cudaStream_t st);
 
+// ---- collective.cu: ICollective over NVLink peer memory (layout there)
+struct CollLayout {
+  int world;
+  size_t slot;  // bytes of one staging slot (the largest payload)
+  size_t flags, acks, stage, total;
+};
+cudaError_t launch_coll_wait(const CollLayout& L, char* base, int which, uint32_t target, int* err, cudaStream_t st);
+cudaError_t launch_coll_push(const CollLayout& L, char* const* peers, const void* src, size_t src_stride, size_t n,
+                             int rank, uint32_t seq, int* ctr, cudaStream_t st);
+cudaError_t launch_coll_consume(const CollLayout& L, char* base, char* const* peers, int op, void* dst, size_t n,
+                                int dtype, int root, int rank, uint32_t seq, int* ctr, cudaStream_t st);
+
 // ---- int4_gemm.cu
 struct RepackArgs {
   const uint8_t* q;      // QLWC [M, ceil(K/2)]

@@ -1977,3 +1977,188 @@ namespace llmoc {
 // Sets the text llmoc_last_error() returns on this thread.
 void set_last_error(const std::string& msg) { t_err = msg; }
 }  // namespace llmoc
+
+// ------------------------------------------------------ NVLink collectives
+
+struct llmoc_collective {
+  int world = 1, rank = 0, device = 0;
+  llmoc::CollLayout lay{};
+  uint32_t seq = 0;                // steps started
+  bool open_step = false;          // a start without its finish
+  char* base = nullptr;            // this rank's buffer (exported by CUDA IPC)
+  std::vector<char*> peer;         // every rank's buffer as seen from here
+  std::vector<bool> opened;
+  char** peers_dev = nullptr;
+  int* ctr = nullptr;              // device: CTA counters of the push and consume kernels
+  int* err = nullptr;              // device: bit 1 = a wait gave up
+  bool connected = false;
+};
+
+llmoc_status llmoc_collective_create(int world, int rank, size_t max_bytes, int device, llmoc_collective** out,
+                                     void* ipc_handle) {
+  if (!out || world < 1 || world > kEpMaxWorld || rank < 0 || rank >= world || max_bytes == 0 ||
+      max_bytes > ((size_t)1 << 34))
+    return fails(LLMOC_ERR_INVALID, "bad arguments");
+  *out = nullptr;
+  DevGuard dg(device);
+  auto* c = new llmoc_collective();
+  c->world = world;
+  c->rank = rank;
+  c->device = device;
+  CollLayout& l = c->lay;
+  l.world = world;
+  l.slot = align256(max_bytes);
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = o;
+    o += align256(bytes);
+    return at;
+  };
+  l.flags = take((size_t)world * 4);
+  l.acks = take((size_t)world * 4);
+  l.stage = take((size_t)2 * world * l.slot);
+  l.total = o;
+  bool ok = cuda_ok(cudaMalloc((void**)&c->base, l.total), "collective buffer") &&
+            cuda_ok(cudaMemset(c->base, 0, l.total), "collective memset") &&
+            cuda_ok(cudaMalloc((void**)&c->ctr, 64), "collective counters") &&
+            cuda_ok(cudaMemset(c->ctr, 0, 64), "collective memset") &&
+            cuda_ok(cudaMalloc((void**)&c->peers_dev, sizeof(char*) * world), "collective peers");
+  c->err = c->ctr + 8;
+  if (ok && ipc_handle) {
+    cudaIpcMemHandle_t h;
+    ok = cuda_ok(cudaIpcGetMemHandle(&h, c->base), "ipc handle");
+    if (ok) memcpy(ipc_handle, &h, sizeof(h));
+  }
+  c->peer.assign(world, nullptr);
+  c->opened.assign(world, false);
+  c->peer[rank] = c->base;
+  if (!ok) {
+    llmoc_collective_destroy(c);
+    return LLMOC_ERR_CUDA;
+  }
+  *out = c;
+  return LLMOC_OK;
+}
+
+namespace {
+llmoc_status coll_upload_peers(llmoc_collective* c) {
+  if (!cuda_ok(cudaMemcpy(c->peers_dev, c->peer.data(), sizeof(char*) * c->world, cudaMemcpyHostToDevice),
+               "collective peers"))
+    return LLMOC_ERR_CUDA;
+  c->connected = true;
+  return LLMOC_OK;
+}
+}  // namespace
+
+llmoc_status llmoc_collective_connect(llmoc_collective* c, const void* handles) {
+  if (!c || !handles) return fails(LLMOC_ERR_INVALID, "bad arguments");
+  DevGuard dg(c->device);
+  const char* hb = static_cast<const char*>(handles);
+  for (int r = 0; r < c->world; ++r) {
+    if (r == c->rank || c->opened[r]) continue;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, hb + (size_t)r * sizeof(h), sizeof(h));
+    void* p = nullptr;
+    if (!cuda_ok(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess), "ipc open")) return LLMOC_ERR_CUDA;
+    c->peer[r] = static_cast<char*>(p);
+    c->opened[r] = true;
+  }
+  return coll_upload_peers(c);
+}
+
+llmoc_status llmoc_collective_connect_local(llmoc_collective* c, llmoc_collective* const* all) {
+  if (!c || !all) return fails(LLMOC_ERR_INVALID, "bad arguments");
+  for (int r = 0; r < c->world; ++r) {
+    if (!all[r] || all[r]->world != c->world || all[r]->rank != r || all[r]->lay.total != c->lay.total)
+      return fails(LLMOC_ERR_INVALID, "collectives of one world, in rank order");
+    c->peer[r] = all[r]->base;
+  }
+  DevGuard dg(c->device);
+  return coll_upload_peers(c);
+}
+
+void llmoc_collective_destroy(llmoc_collective* c) {
+  if (!c) return;
+  DevGuard dg(c->device);
+  for (int r = 0; r < c->world; ++r)
+    if (c->opened[r]) cudaIpcCloseMemHandle(c->peer[r]);
+  if (c->base) cudaFree(c->base);
+  if (c->ctr) cudaFree(c->ctr);
+  if (c->peers_dev) cudaFree(c->peers_dev);
+  delete c;
+}
+
+int llmoc_collective_world_size(const llmoc_collective* c) { return c ? c->world : 0; }
+
+int llmoc_collective_error(llmoc_collective* c) {
+  if (!c) return -1;
+  DevGuard dg(c->device);
+  int v = 0;
+  if (!cuda_ok(cudaMemcpy(&v, c->err, 4, cudaMemcpyDeviceToHost), "error word")) return -1;
+  return v;
+}
+
+namespace {
+// whether (op, bytes, root, dtype) is a valid step for this collective
+bool coll_shape(const llmoc_collective* c, int op, size_t bytes, int root, int dtype) {
+  if (bytes == 0 || bytes > c->lay.slot) return false;
+  if (op == LLMOC_COLL_ALLREDUCE_SUM) return (dtype == LLMOC_DTYPE_F32 && bytes % 4 == 0) ||
+                                             (dtype == LLMOC_DTYPE_BF16 && bytes % 2 == 0);
+  if (op == LLMOC_COLL_BROADCAST) return root >= 0 && root < c->world;
+  return op == LLMOC_COLL_ALLTOALL;
+}
+}  // namespace
+
+llmoc_status llmoc_collective_start(llmoc_collective* c, int op, const void* src, size_t bytes, int root,
+                                    void* stream) {
+  // start sees no dtype: the looser (bf16) size rule here, the exact one in finish
+  if (!c || !src || c->open_step || !coll_shape(c, op, bytes, root, LLMOC_DTYPE_BF16))
+    return fails(LLMOC_ERR_INVALID, "bad arguments");
+  if (!c->connected) return fails(LLMOC_ERR_INVALID, "collective not connected");
+  DevGuard dg(c->device);
+  cudaStream_t st = (cudaStream_t)stream;
+  const uint32_t seq = c->seq + 1;
+  // staging parity seq & 1 was last used by step seq - 2: every rank must have consumed it
+  if (seq > 2 && !cuda_ok(launch_coll_wait(c->lay, c->base, 1, seq - 2, c->err, st), "collective wait acks"))
+    return LLMOC_ERR_CUDA;
+  const size_t n = op == LLMOC_COLL_BROADCAST && root != c->rank ? 0 : bytes;
+  const size_t stride = op == LLMOC_COLL_ALLTOALL ? bytes : 0;
+  if (!cuda_ok(launch_coll_push(c->lay, c->peers_dev, src, stride, n, c->rank, seq, c->ctr, st), "collective push"))
+    return LLMOC_ERR_CUDA;
+  count_launch(seq > 2 ? 2 : 1);
+  c->seq = seq;
+  c->open_step = true;
+  return LLMOC_OK;
+}
+
+llmoc_status llmoc_collective_finish(llmoc_collective* c, int op, void* dst, size_t bytes, int dtype, int root,
+                                     void* stream) {
+  if (!c || !dst || !c->open_step || !coll_shape(c, op, bytes, root, dtype))
+    return fails(LLMOC_ERR_INVALID, "bad arguments");
+  DevGuard dg(c->device);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (!cuda_ok(launch_coll_wait(c->lay, c->base, 0, c->seq, c->err, st), "collective wait flags") ||
+      !cuda_ok(launch_coll_consume(c->lay, c->base, c->peers_dev, op, dst, bytes, dtype, root, c->rank, c->seq,
+                                   c->ctr + 1, st),
+               "collective consume"))
+    return LLMOC_ERR_CUDA;
+  count_launch(2);
+  c->open_step = false;
+  return LLMOC_OK;
+}
+
+llmoc_status llmoc_collective_alltoall(llmoc_collective* c, const void* send, void* recv, size_t bytes,
+                                       void* stream) {
+  llmoc_status rc = llmoc_collective_start(c, LLMOC_COLL_ALLTOALL, send, bytes, 0, stream);
+  return rc != LLMOC_OK ? rc : llmoc_collective_finish(c, LLMOC_COLL_ALLTOALL, recv, bytes, 0, 0, stream);
+}
+
+llmoc_status llmoc_collective_allreduce_sum(llmoc_collective* c, void* inout, size_t bytes, int dtype, void* stream) {
+  llmoc_status rc = llmoc_collective_start(c, LLMOC_COLL_ALLREDUCE_SUM, inout, bytes, 0, stream);
+  return rc != LLMOC_OK ? rc : llmoc_collective_finish(c, LLMOC_COLL_ALLREDUCE_SUM, inout, bytes, dtype, 0, stream);
+}
+
+llmoc_status llmoc_collective_broadcast(llmoc_collective* c, void* buf, size_t bytes, int root, void* stream) {
+  llmoc_status rc = llmoc_collective_start(c, LLMOC_COLL_BROADCAST, buf, bytes, root, stream);
+  return rc != LLMOC_OK ? rc : llmoc_collective_finish(c, LLMOC_COLL_BROADCAST, buf, bytes, 0, root, stream);
+}

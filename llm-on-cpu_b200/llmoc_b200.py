@@ -77,6 +77,17 @@ _SIGS = {
     "llmoc_last_error": (C.c_char_p, []),
     "llmoc_try_gemm_int4": (_i, [_vp, C.POINTER(Int4View), _vp]),
     "llmoc_try_gemm_int4_argmax": (_i, [_vp, C.POINTER(Int4View), C.POINTER(C.c_int32), C.POINTER(C.c_float)]),
+    "llmoc_collective_create": (_i, [_i, _i, C.c_size_t, _i, C.POINTER(_vp), _vp]),
+    "llmoc_collective_connect": (_i, [_vp, _vp]),
+    "llmoc_collective_connect_local": (_i, [_vp, C.POINTER(_vp)]),
+    "llmoc_collective_destroy": (None, [_vp]),
+    "llmoc_collective_world_size": (_i, [_vp]),
+    "llmoc_collective_error": (_i, [_vp]),
+    "llmoc_collective_start": (_i, [_vp, _i, _vp, C.c_size_t, _i, _vp]),
+    "llmoc_collective_finish": (_i, [_vp, _i, _vp, C.c_size_t, _i, _i, _vp]),
+    "llmoc_collective_alltoall": (_i, [_vp, _vp, _vp, C.c_size_t, _vp]),
+    "llmoc_collective_allreduce_sum": (_i, [_vp, _vp, C.c_size_t, _i, _vp]),
+    "llmoc_collective_broadcast": (_i, [_vp, _vp, C.c_size_t, _i, _vp]),
     "llmoc_try_gemm_int4_batch": (_i, [_vp, _i, C.POINTER(Int4View), _vp]),
     "llmoc_try_gemm_int4_multi": (_i, [_vp, C.POINTER(C.POINTER(Int4View)), C.POINTER(_vp), _i]),
     "llmoc_try_gemm_int4_batch_multi": (_i, [_vp, _i, C.POINTER(C.POINTER(Int4View)),
@@ -411,6 +422,66 @@ class EpTransport:
     def close(self) -> None:
         if self.handle:
             lib.llmoc_ep_transport_destroy(self.handle)
+            self.handle = None
+
+
+class Collective:
+    """This rank's end of the NVLink collectives (llmoc_collective_*), the
+    contracts::ICollective operations between the GPUs of a box."""
+
+    ALLTOALL, ALLREDUCE_SUM, BROADCAST = 0, 1, 2
+    F32, BF16 = 0, 1
+
+    def __init__(self, world: int, rank: int, max_bytes: int, device: int = 0, export: bool = True):
+        self.world, self.rank = world, rank
+        h = C.c_void_p()
+        self.ipc = (C.c_char * int(lib.llmoc_ep_ipc_handle_bytes()))() if export else None
+        check(lib.llmoc_collective_create(world, rank, max_bytes, device, C.byref(h),
+                                          C.cast(self.ipc, C.c_void_p) if export else None),
+              "llmoc_collective_create")
+        self.handle = h.value
+
+    def connect(self, handles: bytes) -> None:
+        """handles: every rank's IPC handle, in rank order."""
+        buf = C.create_string_buffer(handles, len(handles))
+        check(lib.llmoc_collective_connect(self.handle, C.cast(buf, C.c_void_p)), "llmoc_collective_connect")
+
+    @staticmethod
+    def connect_local(colls) -> None:
+        """Every rank of the world in this process (tests)."""
+        arr = (C.c_void_p * len(colls))(*[c.handle for c in colls])
+        for c in colls:
+            check(lib.llmoc_collective_connect_local(c.handle, arr), "llmoc_collective_connect_local")
+
+    def world_size(self) -> int:
+        return int(lib.llmoc_collective_world_size(self.handle))
+
+    def error(self) -> int:
+        return int(lib.llmoc_collective_error(self.handle))
+
+    def start(self, op: int, src, nbytes: int, root: int = 0, stream=None) -> None:
+        check(lib.llmoc_collective_start(self.handle, op, ptr(src), nbytes, root, stream_ptr(stream)),
+              "llmoc_collective_start")
+
+    def finish(self, op: int, dst, nbytes: int, dtype: int = 0, root: int = 0, stream=None) -> None:
+        check(lib.llmoc_collective_finish(self.handle, op, ptr(dst), nbytes, dtype, root, stream_ptr(stream)),
+              "llmoc_collective_finish")
+
+    def alltoall(self, send, recv, chunk_bytes: int, stream=None) -> None:
+        check(lib.llmoc_collective_alltoall(self.handle, ptr(send), ptr(recv), chunk_bytes, stream_ptr(stream)),
+              "llmoc_collective_alltoall")
+
+    def allreduce_sum(self, inout, nbytes: int, dtype: int, stream=None) -> None:
+        check(lib.llmoc_collective_allreduce_sum(self.handle, ptr(inout), nbytes, dtype, stream_ptr(stream)),
+              "llmoc_collective_allreduce_sum")
+
+    def broadcast(self, buf, nbytes: int, root: int, stream=None) -> None:
+        check(lib.llmoc_collective_broadcast(self.handle, ptr(buf), nbytes, root, stream_ptr(stream)),
+              "llmoc_collective_broadcast")
+
+    def close(self) -> None:
+        if self.handle:
+            lib.llmoc_collective_destroy(self.handle)
             self.handle = None
 
 
