@@ -87,3 +87,80 @@ def test_int4_payload_sizes_checked(tmp_path):
     bad.write_bytes(bytes(raw))
     with pytest.raises(L.LlmocError):
         L.qlwc_describe(str(bad), "model.", 3)
+
+
+# --------------------------------------------------------------------------
+# A minimal QLWC v1 writer (the container of src/weights/qlwc_format.cpp:
+# preface "QLW1", u32 version, u64 catalog bytes, u64 FNV-1a 64 of the
+# catalog; catalog = u32 scheme, u32 group size, u32 alignment, u64 count,
+# then per tensor name, kind, rank, dims and its payload records).  Payload
+# bytes are zeros: describe reads the catalog only.
+
+def _qlwc_bytes(scheme, gs, tensors):
+    import struct
+
+    cat = bytearray(struct.pack("<IIIQ", scheme, gs, 64, len(tensors)))
+    off = 4096
+    for t in tensors:
+        name = t["name"].encode()
+        cat += struct.pack("<I", len(name)) + name + struct.pack("<IQ", t["kind"], len(t["shape"]))
+        cat += struct.pack(f"<{len(t['shape'])}Q", *t["shape"])
+        if t["kind"] == 0:
+            cat += struct.pack("<IQQ", t["dtype"], off, t["nbytes"])
+            off += t["nbytes"]
+        else:
+            cat += struct.pack("<I", gs)
+            for n in (t["q"], t["s"], t["z"]):
+                cat += struct.pack("<QQ", off, n)
+                off += n
+    pre = b"QLW1" + struct.pack("<IQQ", 1, len(cat), _fnv1a64(bytes(cat)))
+    body = pre + bytes(cat)
+    return body + bytes(max(0, off - len(body)))
+
+
+def _int4(name, M, K, gs, gptq=True, zeros=None):
+    ng = K // gs
+    z = (M * ng * 2 if gptq else 0) if zeros is None else zeros
+    return dict(name=name, kind=1, shape=[M, K], q=M * K // 2, s=M * ng * 2, z=z)
+
+
+def _layer(base, E, H, I, gs, gptq, shared=None, router=True, bias_dtype=None, zeros=None):
+    ts = []
+    for e in range(E):
+        for pn, (M, K) in (("gate_proj", (I, H)), ("up_proj", (I, H)), ("down_proj", (H, I))):
+            ts.append(_int4(f"{base}experts.{e}.{pn}.weight", M, K, gs, gptq, zeros))
+    if shared:
+        for pn, (M, K) in (("gate_proj", (I, H)), ("up_proj", (I, H)), ("down_proj", (H, I))):
+            ts.append(_int4(f"{base}{shared}{pn}.weight", M, K, gs, gptq))
+    if router:
+        ts.append(dict(name=base + "gate.weight", kind=0, shape=[E, H], dtype=1, nbytes=E * H * 2))
+    if bias_dtype:
+        ts.append(dict(name=base + "gate.e_score_correction_bias", kind=0, shape=[E], dtype=bias_dtype,
+                       nbytes=E * 2))
+    return ts
+
+
+def test_describe_glm_naming_awq_with_bias(tmp_path):
+    """GLM/DeepSeek-style names (shared_experts.), AWQ (no zeros), a 16-bit
+    selection bias, five experts."""
+    p = tmp_path / "glm.qlwc"
+    p.write_bytes(_qlwc_bytes(2, 64, _layer("model.layers.7.mlp.", 5, 256, 128, 64, False,
+                                              shared="shared_experts.", bias_dtype=2)))
+    info = L.qlwc_describe(str(p), "model.", 7)
+    assert (info.hidden, info.inter, info.n_experts, info.group_size, info.scheme) == (256, 128, 5, 64, 2)
+    assert (info.has_router, info.has_shared, info.has_shared_gate, info.has_bias) == (1, 1, 0, 1)
+
+
+def test_describe_without_router_and_bad_zeros(tmp_path):
+    p = tmp_path / "norouter.qlwc"
+    p.write_bytes(_qlwc_bytes(1, 64, _layer("model.layers.0.mlp.", 4, 128, 64, 64, True, router=False)))
+    info = L.qlwc_describe(str(p), "model.", 0)
+    assert (info.n_experts, info.has_router, info.has_shared, info.has_bias) == (4, 0, 0, 0)
+    p2 = tmp_path / "nozeros.qlwc"  # GPTQ experts without their fp16 zeros
+    p2.write_bytes(_qlwc_bytes(1, 64, _layer("model.layers.0.mlp.", 4, 128, 64, 64, True, zeros=0)))
+    with pytest.raises(L.LlmocError):
+        L.qlwc_describe(str(p2), "model.", 0)
+    p3 = tmp_path / "awqzeros.qlwc"  # AWQ experts with a zeros payload
+    p3.write_bytes(_qlwc_bytes(2, 64, _layer("model.layers.0.mlp.", 4, 128, 64, 64, False, zeros=128 * 2 * 2)))
+    with pytest.raises(L.LlmocError):
+        L.qlwc_describe(str(p3), "model.", 0)
