@@ -220,7 +220,9 @@ class P2PStep:
 
 
 def connect_p2p(transport, group=None) -> None:
-    """Exchange the ranks' IPC handles (one all-gather) and open the peers."""
+    """Exchange the ranks' IPC handles (one all-gather) and open the peers:
+    for an EpTransport or a Collective (anything with .ipc, .world and
+    .connect(handles in rank order))."""
     import llmoc_b200 as L
 
     nb = int(L.lib.llmoc_ep_ipc_handle_bytes())

@@ -84,3 +84,49 @@ def test_owner_map_is_the_references_kmod():
         for e in range(64):
             assert ep.owner_rank(e, world) == e % world
             assert ep.local_expert(e, world) * world + ep.owner_rank(e, world) == e
+
+
+class _FakeEnd:
+    """Stands in for an EpTransport / Collective: its IPC handle is the rank
+    number repeated; connect records what it was given."""
+
+    def __init__(self, rank, world, nb):
+        self.world, self.ipc, self.got = world, bytes([rank + 1]) * nb, None
+
+    def connect(self, handles):
+        self.got = handles
+
+
+def _connect_worker(rank, world, port, q):
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+        import llmoc_b200 as L
+
+        nb = int(L.lib.llmoc_ep_ipc_handle_bytes())
+        end = _FakeEnd(rank, world, nb)
+        ep.connect_p2p(end)
+        q.put((rank, end.got == b"".join(bytes([r + 1]) * nb for r in range(world)), nb))
+        dist.destroy_process_group()
+    except Exception as e:  # reported to the parent
+        q.put((rank, repr(e), None))
+
+
+def test_connect_exchanges_handles_in_rank_order():
+    """ep.connect_p2p over two gloo ranks: every rank's connect receives all
+    IPC handles, rank 0's first (the layout llmoc_ep_transport_connect and
+    llmoc_collective_connect read)."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_connect_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in ps:
+        p.start()
+    res = [q.get(timeout=180) for _ in range(world)]
+    for p in ps:
+        p.join(timeout=60)
+    for rank, ok, nb in res:
+        assert ok is True, (rank, ok)
+        assert nb == 64  # sizeof(cudaIpcMemHandle_t)
