@@ -401,8 +401,9 @@ def run_llmoc(args):
             except Exception as ex:  # the baseline is reported, not required
                 cpu = {"value": None, "unit": "tokens/s", "cores": None, "kind": "reference",
                        "sample": f"unavailable: {ex}"}
+        metric, config = line_identity(args, world)
         out = {
-            "metric": "INT4 MoE FFN tokens/s (decode, T=%d)" % T,
+            "metric": metric,
             "value": world_tokens / (r["ms"] * 1e-3),
             "unit": "tokens/s",
             "n_gpus": world,
@@ -414,11 +415,7 @@ def run_llmoc(args):
             "vs_baseline": None,
             "dtype": "int4 weights x bf16 activations, fp32 accumulate",
             "data": "synthetic (seeded device RNG; BASELINE shapes and distributions)",
-            "config": {"workload": f"{args.config} MoE layer (BASELINE config 2)" if args.config == "qwen3_30b_a3b"
-                       else f"{args.config} MoE layer", "tokens": T, "hidden": H, "experts": E,
-                       "topk": k, "inter": cfg["I"], "group_size": cfg["gs"],
-                       "parallelism": "replicas" if world > 1 else "single GPU",
-                       "l2": f"rotating {R} distinct layer copies (touched weights >= 3x the 126 MB L2)"},
+            "config": config,
             "e2e": {"value": world * T * args.steps / (ms_e2e * 1e-3), "unit": "tokens/s",
                     "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 2},
             "roofline": {"bound": "hbm", "kernel": "k_int4_mma<GATE_UP> (grouped gate/up + SiLU*mul)",
@@ -455,6 +452,54 @@ def zipf_targets(E, k, s):
         else:
             lo = c
     return np.minimum(1.0, lo * r ** -s)
+
+
+def sweep_tokens(args):
+    """Token counts a one-layer run measures (headline T = args.tokens)."""
+    return sorted({args.tokens} | ({int(x) for x in args.sweep.split(",") if x} if args.sweep else set()))
+
+
+def stack_tokens(args):
+    """Token counts the 48-layer stack measures (headline T = the largest)."""
+    return sorted({args.tokens if args.tokens <= 16 else 16} | ({1, 4, 16} if args.sweep else set()))
+
+
+def copies_for(cfg, Ts, world=1):
+    """Distinct layer copies the timed loop rotates so that the experts the
+    step touches (per rank: the world's tokens over its shard) are >= 3x L2."""
+    E, k = cfg["E"], cfg["topk"]
+    gu_b, dn_b = layer_bytes(cfg)
+    touched_min = min(expected_touched(E, k, world * T) / world for T in Ts) + (1 if cfg["shared"] else 0)
+    return int(max(2, min(24, np.ceil(3 * L2_BYTES / (touched_min * (gu_b + dn_b))))))
+
+
+def line_identity(args, world):
+    """(metric, config) of this run's bench line -- the library arm's and,
+    for the same configuration and N, the reference arm's."""
+    if args.config in STACKS:
+        st = STACKS[args.config]
+        cfg = CONFIGS[st["base"]]
+        T = max(stack_tokens(args))
+        tgt = zipf_targets(cfg["E"], cfg["topk"], st["zipf"])
+        tgt = tgt / tgt.sum()
+        return ("INT4 MoE 48-layer stack tokens/s (decode, T=%d)" % T,
+                {"workload": "qwen3_30b_a3b x 48 layers (BASELINE config 3)", "tokens": T, "layers": st["layers"],
+                 "zipf_s": st["zipf"], "l2": "48 distinct layers (15 GB of experts)",
+                 "zipf_target_share": {"top1": round(float(tgt[0]), 4), "top8": round(float(tgt[:8].sum()), 4),
+                                       "top32": round(float(tgt[:32].sum()), 4)}})
+    cfg = CONFIGS[args.config]
+    H, E, k, T = cfg["H"], cfg["E"], cfg["topk"], args.tokens
+    R = args.copies if args.copies > 0 else copies_for(cfg, sweep_tokens(args), world)
+    l2 = f"rotating {R} distinct layer copies (touched weights >= 3x the 126 MB L2)"
+    if world > 1:
+        return ("INT4 MoE FFN tokens/s (decode, T=%d per GPU)" % T,
+                {"workload": f"{args.config} MoE layer, expert-parallel", "tokens_per_gpu": T, "hidden": H,
+                 "experts": E, "experts_per_gpu": E // world, "topk": k, "inter": cfg["I"],
+                 "group_size": cfg["gs"], "parallelism": f"ep{world}", "l2": l2})
+    return ("INT4 MoE FFN tokens/s (decode, T=%d)" % T,
+            {"workload": f"{args.config} MoE layer (BASELINE config 2)" if args.config == "qwen3_30b_a3b"
+             else f"{args.config} MoE layer", "tokens": T, "hidden": H, "experts": E,
+             "topk": k, "inter": cfg["I"], "group_size": cfg["gs"], "parallelism": "single GPU", "l2": l2})
 
 
 def calibrate_boosts(E, k, sigma, target, seed, iters=80, n=16384):
@@ -606,17 +651,14 @@ def run_stack(args):
     r = results[T]
     per = r["ms"] / args.steps
     byts = r["touched"] * exp_b + NL * (E * H * 2 + 2 * T * H * 2)
-    tgt = target / target.sum()
+    metric, config = line_identity(args, 1)
     out = {
-        "metric": "INT4 MoE 48-layer stack tokens/s (decode, T=%d)" % T,
+        "metric": metric,
         "value": T * args.steps / (r["ms"] * 1e-3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
         "warmup": max(3, args.warmup), "ms_per_step": per, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "int4 weights x bf16 activations, fp32 accumulate",
         "data": "synthetic (seeded device RNG; BASELINE config 3 shapes, Zipf-skewed router)",
-        "config": {"workload": "qwen3_30b_a3b x 48 layers (BASELINE config 3)", "tokens": T, "layers": NL,
-                   "zipf_s": st["zipf"], "l2": "48 distinct layers (15 GB of experts)",
-                   "zipf_target_share": {"top1": round(float(tgt[0]), 4), "top8": round(float(tgt[:8].sum()), 4),
-                                         "top32": round(float(tgt[:32].sum()), 4)}},
+        "config": config,
         "e2e": {"value": T * args.steps / (ms_e2e * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2,
                 "d2h_bytes_per_step": T * H * 2},
         "roofline": {"bound": "hbm", "kernel": "whole 48-layer step", "achieved": byts / (per * 1e-3) / 1e9,
@@ -641,14 +683,18 @@ def run_reference(args):
     if not orc.ref_available():
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libllmoc_ref.so was not built"}))
         return None
-    cfg = CONFIGS[args.config]
+    # the library arm's metric and config for this configuration and N; a
+    # stack step is its layers' per-token CPU path one after another
+    metric, config = line_identity(args, world)
+    n_layers = STACKS[args.config]["layers"] if args.config in STACKS else 1
+    cfg = CONFIGS[STACKS[args.config]["base"]] if args.config in STACKS else CONFIGS[args.config]
     rng = np.random.default_rng(1234)
     O = orc.Oracle()
     layer = orc.make_layer(O, rng, H=cfg["H"], I=cfg["I"], E=cfg["E"], topk=cfg["topk"], gs=cfg["gs"],
                            router=cfg["router"], routed_scaling=cfg["scaling"], shared=cfg["shared"],
                            n_real=16)
     R = orc.Reference()
-    T = args.tokens
+    T = config.get("tokens", config.get("tokens_per_gpu"))
     X = orc.make_tokens(rng, T, cfg["H"])
     per_step = max(1, min(T, 8))  # bounded sample of each step's tokens
     for i in range(args.warmup):
@@ -657,15 +703,16 @@ def run_reference(args):
     for i in range(args.steps):
         R.moe_layer_forward(layer, X[(i * per_step) % T:][:per_step])
     dt = time.perf_counter() - t0
-    v = per_step * args.steps / dt
-    line = {"impl": "reference", "metric": "INT4 MoE FFN tokens/s (decode, T=%d)" % T, "value": v,
+    v = per_step * args.steps / dt / n_layers
+    line = {"impl": "reference", "metric": metric, "value": v,
             "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+            "ms_per_step": dt / args.steps * 1e3 * n_layers, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int4 weights x fp32 activations (AVX2 fp32)",
-            "data": "synthetic", "config": {"workload": f"{args.config} MoE layer", "tokens": T},
+            "data": "synthetic", "config": config,
             "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": R.max_threads(), "kind": "reference",
                              "sample": f"{per_step} of the {T} tokens per step through the reference's "
-                                       f"per-token moe_ffn_token CPU path"},
+                                       f"per-token moe_ffn_token CPU path"
+                                       + (f", one layer, rate / {n_layers} layers" if n_layers > 1 else "")},
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return line
@@ -803,8 +850,9 @@ def run_ep(args):
             sweep[str(t_)] = {"tokens_per_s": world * t_ * args.steps / (rr["ms"] * 1e-3), "ms_per_step": ps,
                               "phases_ms": {a: round(b, 5) for a, b in rr["phases"].items()}}
         a2a_bytes = T * k * H * 2 * 2 + T * k * 4  # rows out and back (bf16) + expert ids, per GPU
+        metric, config = line_identity(args, world)
         out = {
-            "metric": "INT4 MoE FFN tokens/s (decode, T=%d per GPU)" % T,
+            "metric": metric,
             "value": world * T * args.steps / (r["ms"] * 1e-3),
             "unit": "tokens/s",
             "n_gpus": world,
@@ -816,10 +864,7 @@ def run_ep(args):
             "vs_baseline": None,
             "dtype": "int4 weights x bf16 activations, fp32 accumulate",
             "data": "synthetic (seeded device RNG; BASELINE shapes and distributions)",
-            "config": {"workload": f"{args.config} MoE layer, expert-parallel", "tokens_per_gpu": T, "hidden": H,
-                       "experts": E, "experts_per_gpu": E // world, "topk": k, "inter": I,
-                       "group_size": cfg["gs"], "parallelism": f"ep{world}",
-                       "l2": f"rotating {R} distinct layer copies (touched weights >= 3x the 126 MB L2)"},
+            "config": config,
             "ep": {"phases_ms": ph, "a2a_bytes_per_gpu_per_step": a2a_bytes,
                    "a2a_GBps_per_gpu": a2a_bytes / (ph["a2a_ms"] * 1e-3) / 1e9 if ph["a2a_ms"] > 0 else None,
                    "transport": ("library NVLink transport: rows stored into the owners' receive buffers "
