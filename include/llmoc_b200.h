@@ -206,6 +206,10 @@ typedef struct llmoc_qlwc_layer_info {
 } llmoc_qlwc_layer_info;
 LLMOC_API llmoc_status llmoc_qlwc_describe(const char* path, const char* prefix, int layer,
                                            llmoc_qlwc_layer_info* out);
+/* The layer numbers n of the file's MoE layers (those holding an INT4
+ * "<prefix>layers.<n>.mlp.experts.0.gate_proj.weight"), ascending: writes up to
+ * max_layers of them and returns how many there are, or -1 (bad file). */
+LLMOC_API int llmoc_qlwc_moe_layers(const char* path, const char* prefix, int32_t* layers, int max_layers);
 /* desc gives what the file does not hold (topk, router kind, routed scaling,
  * shared scale) and must agree with it on the rest (llmoc_qlwc_describe). */
 LLMOC_API llmoc_status llmoc_moe_layer_create_qlwc(const char* path, const char* prefix, int layer,

@@ -1674,6 +1674,32 @@ llmoc_status llmoc_qlwc_describe(const char* path, const char* prefix, int layer
   return qlwc_info(q, qlwc_names(prefix, layer, q), out);
 }
 
+int llmoc_qlwc_moe_layers(const char* path, const char* prefix, int32_t* layers, int max_layers) {
+  if (!path || max_layers < 0 || (max_layers > 0 && !layers)) return fails(LLMOC_ERR_INVALID, "bad arguments"), -1;
+  FILE* f = fopen(path, "rb");
+  if (!f) return fails(LLMOC_ERR_INVALID, "cannot open the QLWC file"), -1;
+  QFile q;
+  const bool ok = qlwc_read_header(f, &q);
+  fclose(f);
+  if (!ok) return -1;
+  // layers with an INT4 expert 0: "<prefix>layers.<n>.mlp.experts.0.gate_proj.weight"
+  const std::string head = std::string(prefix ? prefix : "") + "layers.";
+  const std::string tail = ".mlp.experts.0.gate_proj.weight";
+  std::vector<int> found;
+  for (const auto& t : q.tensors) {
+    if (t.kind != 1 || t.name.size() <= head.size() + tail.size() || t.name.compare(0, head.size(), head) != 0 ||
+        t.name.compare(t.name.size() - tail.size(), tail.size(), tail) != 0)
+      continue;
+    const std::string mid = t.name.substr(head.size(), t.name.size() - head.size() - tail.size());
+    if (mid.empty() || mid.size() > 6 || mid.find_first_not_of("0123456789") != std::string::npos) continue;
+    found.push_back(std::stoi(mid));
+  }
+  std::sort(found.begin(), found.end());
+  found.erase(std::unique(found.begin(), found.end()), found.end());
+  for (int i = 0; i < (int)found.size() && i < max_layers; ++i) layers[i] = found[i];
+  return (int)found.size();
+}
+
 llmoc_status llmoc_moe_layer_create_qlwc(const char* path, const char* prefix, int layer,
                                          const llmoc_moe_layer_desc* desc, int device, llmoc_moe_layer** out) {
   if (!path || !desc || !out || layer < 0) return fails(LLMOC_ERR_INVALID, "bad arguments");

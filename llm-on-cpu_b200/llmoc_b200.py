@@ -108,6 +108,7 @@ _SIGS = {
     "llmoc_moe_forward": (_i, [_vp, _vp, _i, _vp, _vp, _sz, _vp]),
     "llmoc_moe_layer_set_shared_gate": (_i, [_vp, _vp, _i]),
     "llmoc_qlwc_describe": (_i, [C.c_char_p, C.c_char_p, _i, C.POINTER(QlwcLayerInfo)]),
+    "llmoc_qlwc_moe_layers": (_i, [C.c_char_p, C.c_char_p, C.POINTER(C.c_int32), _i]),
     "llmoc_moe_layer_create_qlwc": (_i, [C.c_char_p, C.c_char_p, _i, C.POINTER(LayerDesc), _i, C.POINTER(_vp)]),
     "llmoc_moe_forward_residual": (_i, [_vp, _vp, _i, _vp, _vp, _vp, _sz, _vp]),
     "llmoc_moe_route_views": (_i, [_vp, _i, _vp, _sz, C.POINTER(RouteViews)]),
@@ -483,6 +484,16 @@ class Collective:
         if self.handle:
             lib.llmoc_collective_destroy(self.handle)
             self.handle = None
+
+
+def qlwc_moe_layers(path: str, prefix: str) -> list:
+    """Layer numbers of the QLWC file's MoE layers, ascending."""
+    n = int(lib.llmoc_qlwc_moe_layers(path.encode(), prefix.encode(), None, 0))
+    if n < 0:
+        raise LlmocError("llmoc_qlwc_moe_layers: " + last_error())
+    arr = (C.c_int32 * max(1, n))()
+    lib.llmoc_qlwc_moe_layers(path.encode(), prefix.encode(), arr, n)
+    return list(arr[:n])
 
 
 def qlwc_describe(path: str, prefix: str, layer: int) -> QlwcLayerInfo:

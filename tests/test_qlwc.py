@@ -164,3 +164,22 @@ def test_describe_without_router_and_bad_zeros(tmp_path):
     p3.write_bytes(_qlwc_bytes(2, 64, _layer("model.layers.0.mlp.", 4, 128, 64, 64, False, zeros=128 * 2 * 2)))
     with pytest.raises(L.LlmocError):
         L.qlwc_describe(str(p3), "model.", 0)
+
+
+def test_moe_layer_listing(tmp_path):
+    """llmoc_qlwc_moe_layers: the reference-written file holds layer 3; a file
+    with MoE layers 0, 7 and 12 and a dense MLP layer 5 lists the three MoE
+    layers in order; a file that is not QLWC is an error."""
+    assert L.qlwc_moe_layers(qlwc_file(tmp_path), "model.") == [3]
+    ts = []
+    for n in (12, 0, 7):
+        ts += _layer(f"model.layers.{n}.mlp.", 2, 128, 64, 64, False)
+    ts.append(_int4("model.layers.5.mlp.gate_proj.weight", 64, 128, 64, False))  # a dense MLP
+    p = tmp_path / "three.qlwc"
+    p.write_bytes(_qlwc_bytes(2, 64, ts))
+    assert L.qlwc_moe_layers(str(p), "model.") == [0, 7, 12]
+    assert L.qlwc_moe_layers(str(p), "other.") == []
+    bad = tmp_path / "bad.qlwc"
+    bad.write_bytes(b"NOPE" + bytes(64))
+    with pytest.raises(L.LlmocError):
+        L.qlwc_moe_layers(str(bad), "model.")
