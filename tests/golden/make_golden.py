@@ -18,6 +18,9 @@ Sources of truth, all from appolloqin/llm-on-cpu:
   ``tests/unit/test_gpu_quant_gemm.cpp:130-245`` (same patterns, same sizes);
 * ``write_qlwc`` of ``tools/quantize_int4.py`` (:183-260): a one-layer QLWC
   file (``qlwc_cases.npz``) for the library's QLWC loader.
+* ``hal::gemm_int4_argmax`` (``src/hal/int4_ops.cpp:344-446``) through the
+  compiled reference: (index, value) of six cases whose weights come from
+  numpy seeds (``argmax_cases.npz``; ``argmax_weight`` rebuilds them).
 
 Inputs that are large are not stored: they are regenerated from the seed by
 ``oracle/orc.py`` (whose quantizer is itself pinned here against the Python
