@@ -5,7 +5,7 @@
  * Every entry point below names the reference interface it stands in for
  * (paths inside appolloqin/llm-on-cpu).  The plain structs are layout-
  * identical to the reference's C++ types, so the reference can pass its own
- * objects through a reinterpret_cast (see INTEGRATION.md).
+ * objects through a reinterpret_cast.
  *
  * Conventions
  *  - llmoc_try_* keep the reference's bool contract: 1 = done, 0 = not done
@@ -286,10 +286,18 @@ LLMOC_API llmoc_status llmoc_moe_stage_times(llmoc_moe_layer* layer, float* ms, 
  * before any stream capture on the device.  Returns LLMOC_ERR_WORKSPACE when
  * llmoc_moe_workspace_bytes(layer, T) exceeds the capacity.  All calls on a
  * device share the array: calls whose work overlaps on the GPU race and must
- * be serialized by the caller. */
+ * be serialized by the caller.  The cached address belongs to the device's
+ * context: after cudaDeviceReset it is stale, so a process that resets a
+ * device must not call this entry point again. */
 LLMOC_API llmoc_status llmoc_moe_forward_noalloc(const llmoc_moe_layer* layer, const uint16_t* X,
                                                  int T, uint16_t* Y, void* stream);
 LLMOC_API size_t llmoc_moe_noalloc_capacity(void);
+/* Synchronizes `stream`, then reads the device error word that the last
+ * llmoc_moe_forward_noalloc call of T tokens on the layer's device left in
+ * the static array (the caller has no workspace pointer to read it through):
+ * LLMOC_ERR_TIMEOUT when one of that forward's bounded device-side waits gave
+ * up (its outputs are then not valid), LLMOC_OK otherwise. */
+LLMOC_API llmoc_status llmoc_moe_noalloc_status(const llmoc_moe_layer* layer, int T, void* stream);
 
 /* ------------------------------------------------- expert parallelism (EP)
  * The reference gives only the contracts: expert e is owned by rank
@@ -364,6 +372,9 @@ LLMOC_API llmoc_status llmoc_ep_transport_connect_local(llmoc_ep_transport* tr, 
 LLMOC_API void llmoc_ep_transport_destroy(llmoc_ep_transport* tr);
 /* Reads (synchronously) the device error word: 0, or bit 1 when a wait gave up. */
 LLMOC_API int llmoc_ep_transport_error(llmoc_ep_transport* tr);
+/* SM clock cycles each of the transport's bounded waits spins before it gives
+ * up (default 2^31, about 1.1 s at 1.965 GHz); applies to later calls. */
+LLMOC_API llmoc_status llmoc_ep_transport_set_wait_cycles(llmoc_ep_transport* tr, long long cycles);
 LLMOC_API size_t llmoc_ep_p2p_workspace_bytes(const llmoc_moe_layer* shard, const llmoc_ep_transport* tr,
                                               int max_tokens);
 LLMOC_API llmoc_status llmoc_ep_p2p_send(const llmoc_moe_layer* shard, llmoc_ep_transport* tr, const uint16_t* X,
@@ -387,7 +398,8 @@ LLMOC_API llmoc_status llmoc_ep_p2p_finish(const llmoc_moe_layer* shard, llmoc_e
  *                             `bytes` (dtype fp32 or bf16; fp32 accumulation
  *                             in rank order, so every rank gets the same bits)
  *   LLMOC_COLL_BROADCAST      root's buffer of `bytes` to every rank
- * bytes <= the max_bytes given at creation.  Asynchronous on `stream`; a wait
+ * bytes <= the max_bytes given at creation; a finish must repeat its start's
+ * op, bytes and root (else LLMOC_ERR_INVALID).  Asynchronous on `stream`; a wait
  * that gives up (~1 s) sets bit 1 of llmoc_collective_error and the step's
  * result is invalid.  start / finish split a step in two (the first pushes,
  * the second waits and consumes) so that several ranks' objects can share
@@ -405,6 +417,8 @@ LLMOC_API llmoc_status llmoc_collective_connect_local(llmoc_collective* c, llmoc
 LLMOC_API void llmoc_collective_destroy(llmoc_collective* c);
 LLMOC_API int llmoc_collective_world_size(const llmoc_collective* c);
 LLMOC_API int llmoc_collective_error(llmoc_collective* c);
+/* SM clock cycles each bounded wait spins before it gives up (default 2^31). */
+LLMOC_API llmoc_status llmoc_collective_set_wait_cycles(llmoc_collective* c, long long cycles);
 LLMOC_API llmoc_status llmoc_collective_start(llmoc_collective* c, int op, const void* src, size_t bytes, int root,
                                               void* stream);
 LLMOC_API llmoc_status llmoc_collective_finish(llmoc_collective* c, int op, void* dst, size_t bytes, int dtype,

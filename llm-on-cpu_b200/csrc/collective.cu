@@ -20,14 +20,14 @@
 // every peer on every step, whatever the operation, so the waits are the
 // same for all of them.  Flags are written with st.release.sys after the
 // step's stores (system fence), read with ld.acquire.sys; a wait gives up
-// after ~2^31 SM clocks (~1 s), sets bit 1 of the error word and returns.
+// after its budget of SM clocks (default 2^31, ~1 s; set per collective),
+// sets bit 1 of the error word and returns.
 #include "kernels.cuh"
 
 namespace llmoc {
 
 namespace {
 
-constexpr long long kCollWaitCycles = 1ll << 31;
 constexpr int kCollCtas = 148;
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
@@ -79,7 +79,8 @@ __device__ __forceinline__ void grid_copy(char* dst, const char* src, size_t n, 
 
 // Waits until every rank's word of `which` (0 flags, 1 acks) has reached
 // `target` (one thread per rank, bounded).
-__global__ void __launch_bounds__(256) k_coll_wait(CollLayout L, char* base, int which, uint32_t target, int* err) {
+__global__ void __launch_bounds__(256) k_coll_wait(CollLayout L, char* base, int which, uint32_t target, int* err,
+                                                   long long budget) {
   __shared__ int timed_out;
   if (threadIdx.x == 0) timed_out = 0;
   __syncthreads();
@@ -87,7 +88,7 @@ __global__ void __launch_bounds__(256) k_coll_wait(CollLayout L, char* base, int
     const uint32_t* f = word_at(base, which ? L.acks : L.flags, threadIdx.x);
     const long long t0 = clock64();
     while ((int)(ld_acquire_sys(f) - target) < 0) {
-      if (clock64() - t0 > kCollWaitCycles) {
+      if (clock64() - t0 > budget) {
         timed_out = 1;
         break;
       }
@@ -144,8 +145,9 @@ __global__ void __launch_bounds__(256) k_coll_consume(CollLayout L, char* base, 
 
 // Plain stream-order launches: a wait kernel must never start before the
 // push or consume it follows.
-cudaError_t launch_coll_wait(const CollLayout& L, char* base, int which, uint32_t target, int* err, cudaStream_t st) {
-  k_coll_wait<<<1, 256, 0, st>>>(L, base, which, target, err);
+cudaError_t launch_coll_wait(const CollLayout& L, char* base, int which, uint32_t target, int* err, long long budget,
+                             cudaStream_t st) {
+  k_coll_wait<<<1, 256, 0, st>>>(L, base, which, target, err, budget);
   return cudaGetLastError();
 }
 cudaError_t launch_coll_push(const CollLayout& L, char* const* peers, const void* src, size_t src_stride, size_t n,

@@ -26,7 +26,8 @@
 //
 // Flags carry the step number (1, 2, ...): written with st.release.sys after
 // all the step's rows of that peer are in place, read with ld.acquire.sys.
-// A wait gives up after ~2^31 SM clocks (~1 s), sets bit 1 of the
+// A wait gives up after its budget of SM clocks (default 2^31, ~1 s; set per
+// transport), sets bit 1 of the
 // transport's error word and returns: outputs of that step are invalid, the
 // host checks the word, and no GPU is left waiting.
 #include "kernels.cuh"
@@ -34,8 +35,6 @@
 namespace llmoc {
 
 namespace {
-
-constexpr long long kP2PWaitCycles = 1ll << 31;
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -124,7 +123,8 @@ __global__ void __launch_bounds__(256) k_ep_push_dispatch(EpP2PLayout L, char* c
 // Waits for every peer's flag of `kind` to reach seq (one thread per peer,
 // bounded).  The permutation that follows a dispatch wait reads only each
 // source's first meta.x slots, so the slots past a count are never read.
-__global__ void __launch_bounds__(256) k_ep_wait(EpP2PLayout L, char* base, int kind, uint32_t seq, int* err) {
+__global__ void __launch_bounds__(256) k_ep_wait(EpP2PLayout L, char* base, int kind, uint32_t seq, int* err,
+                                                 long long budget) {
   __shared__ int timed_out;
   if (threadIdx.x == 0) timed_out = 0;
   __syncthreads();
@@ -132,7 +132,7 @@ __global__ void __launch_bounds__(256) k_ep_wait(EpP2PLayout L, char* base, int 
     const uint32_t* f = flag_at(base, L, kind, threadIdx.x);
     const long long t0 = clock64();
     while ((int)(ld_acquire_sys(f) - seq) < 0) {
-      if (clock64() - t0 > kP2PWaitCycles) {
+      if (clock64() - t0 > budget) {
         timed_out = 1;
         break;
       }
@@ -189,8 +189,9 @@ cudaError_t launch_ep_push_dispatch(const EpP2PLayout& L, char* const* peers, co
                                                    counts, rank, seq, ctr);
   return cudaGetLastError();
 }
-cudaError_t launch_ep_wait(const EpP2PLayout& L, char* base, int kind, uint32_t seq, int* err, cudaStream_t st) {
-  k_ep_wait<<<1, 256, 0, st>>>(L, base, kind, seq, err);
+cudaError_t launch_ep_wait(const EpP2PLayout& L, char* base, int kind, uint32_t seq, int* err, long long budget,
+                           cudaStream_t st) {
+  k_ep_wait<<<1, 256, 0, st>>>(L, base, kind, seq, err, budget);
   return cudaGetLastError();
 }
 cudaError_t launch_ep_push_return(const EpP2PLayout& L, char* const* peers, char* base, const float* partial,

@@ -779,15 +779,12 @@ static void launch_mma_gs(const GemmArgs& a, int max_work, int ks, cudaStream_t 
   }
 }
 
+// Items of at most 8 rows (one mma N tile): larger items take the tcgen05
+// kernel (int4_umma.cu) or the CUDA-core kernel.
 template <int MODE>
-static void launch_mma(const GemmArgs& a, int max_work, int ntiles, int ks, int awq, cudaStream_t st) {
-  if (awq) {
-    if (ntiles <= 1) launch_mma_gs<MODE, 1, true>(a, max_work, ks, st);
-    else launch_mma_gs<MODE, 4, true>(a, max_work, ks, st);
-  } else {
-    if (ntiles <= 1) launch_mma_gs<MODE, 1, false>(a, max_work, ks, st);
-    else launch_mma_gs<MODE, 4, false>(a, max_work, ks, st);
-  }
+static void launch_mma(const GemmArgs& a, int max_work, int ks, int awq, cudaStream_t st) {
+  if (awq) launch_mma_gs<MODE, 1, true>(a, max_work, ks, st);
+  else launch_mma_gs<MODE, 1, false>(a, max_work, ks, st);
 }
 
 // ------------------------------------------------------ CUDA-core fp32 GEMV
@@ -1158,10 +1155,12 @@ cudaError_t launch_gemm(int mode, int path, const GemmArgs& a, int max_work, int
         launch_mma_p<MODE_GATE_UP>(a, awq, st);
       else
         launch_mma_p<MODE_PLAIN_F32>(a, awq, st);
+    } else if (ntiles > 1) {
+      return cudaErrorInvalidValue;  // items above 8 rows: not this kernel's
     } else if (mode == MODE_GATE_UP) {
-      launch_mma<MODE_GATE_UP>(a, gy, ntiles, ks, awq, st);
+      launch_mma<MODE_GATE_UP>(a, gy, ks, awq, st);
     } else {
-      launch_mma<MODE_PLAIN_F32>(a, gy, ntiles, ks, awq, st);
+      launch_mma<MODE_PLAIN_F32>(a, gy, ks, awq, st);
     }
   } else if (path == 1) {
     if (mode == MODE_GATE_UP)

@@ -86,7 +86,10 @@ struct EpP2PLayout {
 cudaError_t launch_ep_push_dispatch(const EpP2PLayout& L, char* const* peers, const void* send_rows,
                                     const int* send_expert, const int* counts, int rank, uint32_t seq, int* ctr,
                                     cudaStream_t st);
-cudaError_t launch_ep_wait(const EpP2PLayout& L, char* base, int kind, uint32_t seq, int* err, cudaStream_t st);
+// budget: SM clock cycles after which a wait gives up (sets bit 1 of *err)
+constexpr long long kDefaultWaitCycles = 1ll << 31;  // ~1.1 s at 1.965 GHz
+cudaError_t launch_ep_wait(const EpP2PLayout& L, char* base, int kind, uint32_t seq, int* err, long long budget,
+                           cudaStream_t st);
 // partial: the owner's down output rows (fp32, expert-sorted), inverse: row of each receive slot
 cudaError_t launch_ep_push_return(const EpP2PLayout& L, char* const* peers, char* base, const float* partial,
                                   const int* inverse, int rank, uint32_t seq, int* ctr, cudaStream_t st);
@@ -97,7 +100,8 @@ struct CollLayout {
   size_t slot;  // bytes of one staging slot (the largest payload)
   size_t flags, acks, stage, total;
 };
-cudaError_t launch_coll_wait(const CollLayout& L, char* base, int which, uint32_t target, int* err, cudaStream_t st);
+cudaError_t launch_coll_wait(const CollLayout& L, char* base, int which, uint32_t target, int* err, long long budget,
+                             cudaStream_t st);
 cudaError_t launch_coll_push(const CollLayout& L, char* const* peers, const void* src, size_t src_stride, size_t n,
                              int rank, uint32_t seq, int* ctr, cudaStream_t st);
 cudaError_t launch_coll_consume(const CollLayout& L, char* base, char* const* peers, int op, void* dst, size_t n,
@@ -157,9 +161,6 @@ cudaError_t launch_dequant(const ProjDev& P, int M, int K, int gs, int awq, int 
 // grid_items: work items expected (0: max_work), the tensor-core K-split grid's height
 cudaError_t launch_gemm(int mode, int path, const GemmArgs& a, int max_work, int awq, int ntiles,
                         cudaStream_t st, int n_groups = 0, int grid_items = 0);
-// int4_tma.cu: the same grouped GEMM fed by cp.async.bulk through a shared-
-// memory stage ring (decode-size items, K % 128 == 0, gs in {32, 64, 128}).
-cudaError_t launch_gemm_tma(int mode, const GemmArgs& a, int max_work, int awq, cudaStream_t st);
 // int4_umma.cu: tcgen05.mma (TMEM accumulator) grouped GEMM for work items of
 // up to kUmmaRows rows (prefill-size groups); same K / group-size conditions.  B is
 // b_rows contiguous expert-sorted rows read by TMA (a.gather unused).

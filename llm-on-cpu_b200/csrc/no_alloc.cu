@@ -17,7 +17,16 @@
 // threads) race on it and must be serialized by the caller.  Everything the
 // forward reads from the scratch is written earlier in the same call (the
 // device error word is cleared there too), so stale contents of a previous
-// call do not matter.
+// call do not matter.  The cached address belongs to the device's current
+// context: after cudaDeviceReset every layer (and this address) is invalid,
+// so such a caller creates new layers and must not call this entry point
+// again in that process.
+//
+// The scratch also holds the forward's device error word, which the caller
+// cannot reach through a workspace pointer of its own:
+// llmoc_moe_noalloc_status reads it (after synchronizing the stream) and
+// reports LLMOC_ERR_TIMEOUT when a bounded device-side wait of the forward
+// gave up, i.e. when that forward's outputs are not valid.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -42,6 +51,43 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 std::mutex g_na_mu;
 void* g_na_ptr[kMaxDevices] = {};
 
+// The array's device address on `dev`, looked up once per device with that
+// device current.
+llmoc_status scratch_of(int dev, void** out) {
+  std::lock_guard<std::mutex> lk(g_na_mu);
+  if (g_na_ptr[dev]) {
+    *out = g_na_ptr[dev];
+    return LLMOC_OK;
+  }
+  int prev = 0;
+  cudaError_t e = cudaGetDevice(&prev);
+  if (e != cudaSuccess) {
+    llmoc::set_last_error(std::string("llmoc_moe_forward_noalloc: cudaGetDevice: ") + cudaGetErrorString(e));
+    cudaGetLastError();
+    return LLMOC_ERR_CUDA;
+  }
+  if (prev != dev && cudaSetDevice(dev) != cudaSuccess) {
+    llmoc::set_last_error("llmoc_moe_forward_noalloc: cannot select the layer's device");
+    cudaGetLastError();
+    return LLMOC_ERR_NO_DEVICE;
+  }
+  void* ptr = nullptr;
+  e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+  if (prev != dev && cudaSetDevice(prev) != cudaSuccess) {
+    llmoc::set_last_error("llmoc_moe_forward_noalloc: cannot restore the caller's device");
+    cudaGetLastError();
+    return LLMOC_ERR_CUDA;
+  }
+  if (e != cudaSuccess || !ptr) {
+    llmoc::set_last_error(std::string("llmoc_moe_forward_noalloc: cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+    cudaGetLastError();
+    return LLMOC_ERR_CUDA;
+  }
+  g_na_ptr[dev] = ptr;
+  *out = ptr;
+  return LLMOC_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -63,28 +109,35 @@ LLMOC_API llmoc_status llmoc_moe_forward_noalloc(const llmoc_moe_layer* layer, c
     return LLMOC_ERR_WORKSPACE;
   }
   void* ptr = nullptr;
-  {
-    std::lock_guard<std::mutex> lk(g_na_mu);
-    ptr = g_na_ptr[dev];
-    if (!ptr) {
-      int prev = 0;
-      if (cudaGetDevice(&prev) != cudaSuccess) return LLMOC_ERR_CUDA;
-      if (prev != dev && cudaSetDevice(dev) != cudaSuccess) {
-        llmoc::set_last_error("llmoc_moe_forward_noalloc: cannot select the layer's device");
-        return LLMOC_ERR_NO_DEVICE;
-      }
-      const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
-      if (prev != dev) cudaSetDevice(prev);
-      if (e != cudaSuccess || !ptr) {
-        llmoc::set_last_error(std::string("llmoc_moe_forward_noalloc: cudaGetSymbolAddress: ") +
-                              cudaGetErrorString(e));
-        cudaGetLastError();
-        return LLMOC_ERR_CUDA;
-      }
-      g_na_ptr[dev] = ptr;
-    }
-  }
+  const llmoc_status rc = scratch_of(dev, &ptr);
+  if (rc != LLMOC_OK) return rc;
   return llmoc_moe_forward(layer, X, T, Y, ptr, kNoAllocScratchBytes, stream);
+}
+
+LLMOC_API llmoc_status llmoc_moe_noalloc_status(const llmoc_moe_layer* layer, int T, void* stream) {
+  const int dev = llmoc::layer_device(layer);
+  if (dev < 0 || dev >= kMaxDevices || T < 0 || llmoc_moe_workspace_bytes(layer, T) > kNoAllocScratchBytes) {
+    llmoc::set_last_error("llmoc_moe_noalloc_status: bad layer or token count");
+    return LLMOC_ERR_INVALID;
+  }
+  void* ptr = nullptr;
+  llmoc_status rc = scratch_of(dev, &ptr);
+  if (rc != LLMOC_OK) return rc;
+  llmoc_route_views v{};
+  rc = llmoc_moe_route_views(layer, T, ptr, kNoAllocScratchBytes, &v);
+  if (rc != LLMOC_OK) return rc;
+  int word = 0;
+  cudaError_t e = cudaStreamSynchronize((cudaStream_t)stream);
+  if (e == cudaSuccess) e = cudaMemcpy(&word, v.error_flag, sizeof(word), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) {
+    llmoc::set_last_error(std::string("llmoc_moe_noalloc_status: ") + cudaGetErrorString(e));
+    return LLMOC_ERR_CUDA;
+  }
+  if (word != 0) {
+    llmoc::set_last_error("llmoc_moe_noalloc_status: a bounded device-side wait gave up; the outputs are not valid");
+    return LLMOC_ERR_TIMEOUT;
+  }
+  return LLMOC_OK;
 }
 
 }  // extern "C"

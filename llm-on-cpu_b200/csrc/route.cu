@@ -619,13 +619,9 @@ cudaError_t launch_router_logits(const void* X, bool x_is_f32, const uint16_t* W
                                  int H, float* logits, cudaStream_t st) {
   if (T <= 0) return cudaSuccess;
   // bf16 activations with H % 256 == 0 (every BASELINE shape): the tiled
-  // kernel, its tile chosen by T; LLMOC_ROUTER_PATH=lanes keeps the
-  // lane-group kernel below (same arithmetic) for comparison
-  static const bool lanes_only = [] {
-    const char* v = getenv("LLMOC_ROUTER_PATH");
-    return v && !strcmp(v, "lanes");
-  }();
-  if (!x_is_f32 && H % kRouterKC == 0 && !lanes_only) {
+  // kernel, its tile chosen by T; the lane-group kernel below (same
+  // arithmetic) otherwise
+  if (!x_is_f32 && H % kRouterKC == 0) {
     const auto* Xb = static_cast<const __nv_bfloat16*>(X);
     if (T <= 8) return launch_router_tiled<8, 1, 1, 8>(Xb, Wr, T, E, H, logits, st);    // 8 t x 8 e
     if (T < 128) return launch_router_tiled<8, 2, 1, 8>(Xb, Wr, T, E, H, logits, st);   // 8 t x 16 e

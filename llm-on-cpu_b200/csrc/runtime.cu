@@ -353,26 +353,11 @@ struct llmoc_moe_layer {
 
 namespace {
 
-// Grouped-GEMM implementation override for measurement (environment
-// LLMOC_GEMM_PATH = mma | tma | cuda_core).  Default (0): the register-fed
-// tensor-core kernel.  1 mma, 2 cuda-core, 3 the TMA-fed kernel for
-// decode-size items.
-int gemm_path_pref() {
-  static const int pref = [] {
-    const char* v = getenv("LLMOC_GEMM_PATH");
-    if (!v) return 0;
-    if (!strcmp(v, "mma")) return 1;
-    if (!strcmp(v, "cuda_core")) return 2;
-    if (!strcmp(v, "tma")) return 3;
-    return 0;
-  }();
-  return pref;
-}
-
 // Rows per work item: decode-size batches use one mma N tile (8 rows), so
 // that kernel variant has no per-tile branches; prefill-size batches use
-// kUmmaRows-row items for the tcgen05 kernel (32 when the mma path is forced).
-int chunk_rows(int T) { return T <= 128 ? 8 : (gemm_path_pref() == 1 ? kChunkRows : kUmmaRows); }
+// kUmmaRows-row items for the tcgen05 kernel (or the CUDA-core kernel, which
+// walks any item length, on shapes the tensor-core kernels do not take).
+int chunk_rows(int T) { return T <= 128 ? 8 : kUmmaRows; }
 
 struct WsLayout {
   size_t logits, ids, weights, offsets, sorted, inverse, work, n_work, n_active, err, mid, partial,
@@ -389,12 +374,11 @@ bool tc_shapes(const llmoc_moe_layer* L) {
 
 // Items hold at most `chunk` rows: 8 for decode-size groups (register-fed
 // tensor-core kernel), kUmmaRows for the tcgen05 kernel.
-int chunk_for_rows(int pairs, int groups) {
-  return pairs <= 8 * std::max(1, groups) + groups / 2 ? 8 : (gemm_path_pref() == 1 ? kChunkRows : kUmmaRows);
-}
-bool use_umma_c(const llmoc_moe_layer* L, int chunk) {
-  return tc_shapes(L) && L->wmaps && chunk == kUmmaRows && gemm_path_pref() != 2;
-}
+int chunk_for_rows(int pairs, int groups) { return pairs <= 8 * std::max(1, groups) + groups / 2 ? 8 : kUmmaRows; }
+// A layer with tensor-core shapes always holds its weight maps (creation
+// fails without them), so its kUmmaRows-row items always take the tcgen05
+// kernel: the register-fed kernel handles at most 8 rows per item.
+bool use_umma_c(const llmoc_moe_layer* L, int chunk) { return tc_shapes(L) && L->wmaps && chunk == kUmmaRows; }
 
 // Workspace of one grouped run over T rows with kk slots each, permuted over
 // n_perm groups; `logits` adds the router's [T, n_experts] logits.
@@ -552,12 +536,14 @@ llmoc_status layer_create(const llmoc_moe_layer_desc* d, const uint16_t* router_
     }
     if (tc_shapes(L)) {  // TMA maps of the resident weights for the tcgen05 prefill GEMMs
       std::vector<unsigned char> maps((size_t)n_exp * kMapsPerExpert * kTensorMapBytes);
-      if (build_umma_weight_maps(L->htable.data(), n_exp, I, H, d->group_size, z, maps.data())) {
-        if (cudaMalloc(&L->wmaps, maps.size()) != cudaSuccess ||
-            cudaMemcpy(L->wmaps, maps.data(), maps.size(), cudaMemcpyHostToDevice) != cudaSuccess) {
-          bail(LLMOC_ERR_NO_MEMORY, "weight tensor maps");
-          break;
-        }
+      if (!build_umma_weight_maps(L->htable.data(), n_exp, I, H, d->group_size, z, maps.data())) {
+        bail(LLMOC_ERR_CUDA, "cuTensorMapEncodeTiled refused a weight tensor map");
+        break;
+      }
+      if (cudaMalloc(&L->wmaps, maps.size()) != cudaSuccess ||
+          cudaMemcpy(L->wmaps, maps.data(), maps.size(), cudaMemcpyHostToDevice) != cudaSuccess) {
+        bail(LLMOC_ERR_NO_MEMORY, "weight tensor maps");
+        break;
       }
     }
   } while (false);
@@ -707,10 +693,8 @@ llmoc_status run_ffn(const llmoc_moe_layer* L, const uint16_t* X, int R, int kk,
   // tensor cores when K of both GEMMs is a multiple of 128 and the group is
   // 32/64/128 wide (every BASELINE shape); the CUDA-core kernel otherwise
   const bool tc = tc_shapes(L);
-  int path = tc ? 0 : 2;
-  const bool tma = tc && chunk == 8 && gemm_path_pref() == 3;
+  const int path = tc ? 0 : 2;
   const bool umma = use_umma_c(L, chunk);
-  if (tc && gemm_path_pref() == 2) path = 2;
   const int n_pairs = R * kk;
   // rows expected to be occupied (padded receive slots: fewer than R * kk)
   const int n_expect = expect_pairs > 0 ? std::min(expect_pairs, n_pairs) : n_pairs;
@@ -749,9 +733,7 @@ llmoc_status run_ffn(const llmoc_moe_layer* L, const uint16_t* X, int R, int kk,
     a.gather = nullptr;
   }
   if (!cuda_ok(umma ? launch_gemm_umma(MODE_GATE_UP, a, w.max_work, awq, n_pairs, st)
-               : tma && path == 0 ? launch_gemm_tma(MODE_GATE_UP, a, w.max_work, awq, st)
-                                  : launch_gemm(MODE_GATE_UP, path, a, w.max_work, awq, ntiles, st, n_groups,
-                                                grid_items),
+                    : launch_gemm(MODE_GATE_UP, path, a, w.max_work, awq, ntiles, st, n_groups, grid_items),
                "gate/up"))
     return LLMOC_ERR_CUDA;
   if (se) se->mark(st);
@@ -768,9 +750,7 @@ llmoc_status run_ffn(const llmoc_moe_layer* L, const uint16_t* X, int R, int kk,
   b.ldo = H;
   b.ctr = (int*)(ws + w.err) + 2;
   if (!cuda_ok(umma ? launch_gemm_umma(MODE_PLAIN_F32, b, w.max_work, awq, n_pairs, st)
-               : tma && path == 0 ? launch_gemm_tma(MODE_PLAIN_F32, b, w.max_work, awq, st)
-                                  : launch_gemm(MODE_PLAIN_F32, path, b, w.max_work, awq, ntiles, st, n_groups,
-                                                grid_items),
+                    : launch_gemm(MODE_PLAIN_F32, path, b, w.max_work, awq, ntiles, st, n_groups, grid_items),
                "down"))
     return LLMOC_ERR_CUDA;
   if (se) se->mark(st);
@@ -832,7 +812,7 @@ EpSrcLayout ep_src_layout(const llmoc_moe_layer* L, int T) {
 // owner-rank workspace for `rows` received rows (the larger of the two item sizes)
 size_t ep_owner_bytes(const llmoc_moe_layer* L, int rows) {
   return std::max(ws_layout_g(L, rows, 1, L->n_exp, 8, false).total,
-                  ws_layout_g(L, rows, 1, L->n_exp, gemm_path_pref() == 1 ? kChunkRows : kUmmaRows, false).total);
+                  ws_layout_g(L, rows, 1, L->n_exp, kUmmaRows, false).total);
 }
 
 // Workspace of one NVLink expert-parallel step on a rank: the source side
@@ -855,6 +835,7 @@ struct llmoc_ep_transport {
   char** peers_dev = nullptr;      // device copy of `peer`
   int* ctr = nullptr;              // device: CTA counters of the two push kernels
   int* err = nullptr;              // device: bit 1 = a wait gave up
+  long long wait_cycles = llmoc::kDefaultWaitCycles;  // budget of each bounded wait
   bool connected = false;
 };
 
@@ -1896,6 +1877,12 @@ void llmoc_ep_transport_destroy(llmoc_ep_transport* tr) {
   delete tr;
 }
 
+llmoc_status llmoc_ep_transport_set_wait_cycles(llmoc_ep_transport* tr, long long cycles) {
+  if (!tr || cycles <= 0) return fails(LLMOC_ERR_INVALID, "bad arguments");
+  tr->wait_cycles = cycles;
+  return LLMOC_OK;
+}
+
 int llmoc_ep_transport_error(llmoc_ep_transport* tr) {
   if (!tr) return -1;
   DevGuard dg(tr->device);
@@ -1950,7 +1937,7 @@ llmoc_status llmoc_ep_p2p_serve(const llmoc_moe_layer* L, llmoc_ep_transport* tr
   char* ws = (char*)workspace;
   cudaStream_t st = (cudaStream_t)stream;
   DevGuard dg(L->device);
-  if (!cuda_ok(launch_ep_wait(tr->lay, tr->base, 0, seq, tr->err, st), "ep wait")) return LLMOC_ERR_CUDA;
+  if (!cuda_ok(launch_ep_wait(tr->lay, tr->base, 0, seq, tr->err, tr->wait_cycles, st), "ep wait")) return LLMOC_ERR_CUDA;
   count_launch(1);
   const int parity = seq & 1, slots = tr->world * tr->lay.cap;
   const uint16_t* rows =
@@ -1984,7 +1971,7 @@ llmoc_status llmoc_ep_p2p_finish(const llmoc_moe_layer* L, llmoc_ep_transport* t
   const EpP2PWs w = ep_p2p_ws(L, tr, T);
   char* ws = (char*)workspace;
   DevGuard dg(L->device);
-  if (!cuda_ok(launch_ep_wait(tr->lay, tr->base, 1, seq, tr->err, (cudaStream_t)stream), "ep wait back"))
+  if (!cuda_ok(launch_ep_wait(tr->lay, tr->base, 1, seq, tr->err, tr->wait_cycles, (cudaStream_t)stream), "ep wait back"))
     return LLMOC_ERR_CUDA;
   count_launch(1);
   const uint16_t* ret = (const uint16_t*)(tr->base + tr->lay.ret_rows + (size_t)(seq & 1) * tr->lay.cap * tr->lay.row_bytes);
@@ -2011,12 +1998,15 @@ struct llmoc_collective {
   llmoc::CollLayout lay{};
   uint32_t seq = 0;                // steps started
   bool open_step = false;          // a start without its finish
+  int open_op = 0, open_root = 0;  // the open step's operation, root and size (its finish must match)
+  size_t open_bytes = 0;
   char* base = nullptr;            // this rank's buffer (exported by CUDA IPC)
   std::vector<char*> peer;         // every rank's buffer as seen from here
   std::vector<bool> opened;
   char** peers_dev = nullptr;
   int* ctr = nullptr;              // device: CTA counters of the push and consume kernels
   int* err = nullptr;              // device: bit 1 = a wait gave up
+  long long wait_cycles = llmoc::kDefaultWaitCycles;  // budget of each bounded wait
   bool connected = false;
 };
 
@@ -2116,6 +2106,12 @@ void llmoc_collective_destroy(llmoc_collective* c) {
 
 int llmoc_collective_world_size(const llmoc_collective* c) { return c ? c->world : 0; }
 
+llmoc_status llmoc_collective_set_wait_cycles(llmoc_collective* c, long long cycles) {
+  if (!c || cycles <= 0) return fails(LLMOC_ERR_INVALID, "bad arguments");
+  c->wait_cycles = cycles;
+  return LLMOC_OK;
+}
+
 int llmoc_collective_error(llmoc_collective* c) {
   if (!c) return -1;
   DevGuard dg(c->device);
@@ -2145,7 +2141,7 @@ llmoc_status llmoc_collective_start(llmoc_collective* c, int op, const void* src
   cudaStream_t st = (cudaStream_t)stream;
   const uint32_t seq = c->seq + 1;
   // staging parity seq & 1 was last used by step seq - 2: every rank must have consumed it
-  if (seq > 2 && !cuda_ok(launch_coll_wait(c->lay, c->base, 1, seq - 2, c->err, st), "collective wait acks"))
+  if (seq > 2 && !cuda_ok(launch_coll_wait(c->lay, c->base, 1, seq - 2, c->err, c->wait_cycles, st), "collective wait acks"))
     return LLMOC_ERR_CUDA;
   const size_t n = op == LLMOC_COLL_BROADCAST && root != c->rank ? 0 : bytes;
   const size_t stride = op == LLMOC_COLL_ALLTOALL ? bytes : 0;
@@ -2154,6 +2150,9 @@ llmoc_status llmoc_collective_start(llmoc_collective* c, int op, const void* src
   count_launch(seq > 2 ? 2 : 1);
   c->seq = seq;
   c->open_step = true;
+  c->open_op = op;
+  c->open_bytes = bytes;
+  c->open_root = op == LLMOC_COLL_BROADCAST ? root : 0;
   return LLMOC_OK;
 }
 
@@ -2161,9 +2160,12 @@ llmoc_status llmoc_collective_finish(llmoc_collective* c, int op, void* dst, siz
                                      void* stream) {
   if (!c || !dst || !c->open_step || !coll_shape(c, op, bytes, root, dtype))
     return fails(LLMOC_ERR_INVALID, "bad arguments");
+  // the finish consumes what its start staged: same operation, size and root
+  if (op != c->open_op || bytes != c->open_bytes || (op == LLMOC_COLL_BROADCAST && root != c->open_root))
+    return fails(LLMOC_ERR_INVALID, "collective finish does not match its start (operation, bytes or root)");
   DevGuard dg(c->device);
   cudaStream_t st = (cudaStream_t)stream;
-  if (!cuda_ok(launch_coll_wait(c->lay, c->base, 0, c->seq, c->err, st), "collective wait flags") ||
+  if (!cuda_ok(launch_coll_wait(c->lay, c->base, 0, c->seq, c->err, c->wait_cycles, st), "collective wait flags") ||
       !cuda_ok(launch_coll_consume(c->lay, c->base, c->peers_dev, op, dst, bytes, dtype, root, c->rank, c->seq,
                                    c->ctr + 1, st),
                "collective consume"))

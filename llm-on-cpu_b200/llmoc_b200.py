@@ -83,6 +83,7 @@ _SIGS = {
     "llmoc_collective_destroy": (None, [_vp]),
     "llmoc_collective_world_size": (_i, [_vp]),
     "llmoc_collective_error": (_i, [_vp]),
+    "llmoc_collective_set_wait_cycles": (_i, [_vp, C.c_longlong]),
     "llmoc_collective_start": (_i, [_vp, _i, _vp, C.c_size_t, _i, _vp]),
     "llmoc_collective_finish": (_i, [_vp, _i, _vp, C.c_size_t, _i, _i, _vp]),
     "llmoc_collective_alltoall": (_i, [_vp, _vp, _vp, C.c_size_t, _vp]),
@@ -119,6 +120,7 @@ _SIGS = {
     "llmoc_moe_set_stage_timing": (_i, [_vp, _i]),
     "llmoc_moe_forward_noalloc": (_i, [_vp, _vp, _i, _vp, _vp]),
     "llmoc_moe_noalloc_capacity": (_sz, []),
+    "llmoc_moe_noalloc_status": (_i, [_vp, _i, _vp]),
     "llmoc_moe_stage_times": (_i, [_vp, C.POINTER(C.c_float), C.POINTER(_i)]),
     "llmoc_moe_layer_create_ep": (_i, [C.POINTER(LayerDesc), _vp, _vp, C.POINTER(Int4View),
                                        C.POINTER(Int4View), _i, _i, _i, _i, C.POINTER(_vp)]),
@@ -133,6 +135,7 @@ _SIGS = {
     "llmoc_ep_transport_connect_local": (_i, [_vp, C.POINTER(_vp)]),
     "llmoc_ep_transport_destroy": (None, [_vp]),
     "llmoc_ep_transport_error": (_i, [_vp]),
+    "llmoc_ep_transport_set_wait_cycles": (_i, [_vp, C.c_longlong]),
     "llmoc_ep_p2p_workspace_bytes": (_sz, [_vp, _vp, _i]),
     "llmoc_ep_p2p_send": (_i, [_vp, _vp, _vp, _i, C.c_uint32, _vp, _sz, _vp]),
     "llmoc_ep_p2p_serve": (_i, [_vp, _vp, _i, C.c_uint32, _vp, _sz, _vp]),

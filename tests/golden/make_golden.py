@@ -292,7 +292,10 @@ def qlwc_cases(O: orc.Oracle, qi) -> dict:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("LLMOC_REFERENCE_TREE")
+                    or os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(HERE))), "reference"),
+                    help="the reference tree (default: $LLMOC_REFERENCE_TREE, else a 'reference' folder "
+                         "beside this repository)")
     args = ap.parse_args()
     sys.path.insert(0, os.path.join(args.ref, "tools"))
     import quantize_int4 as qi  # the reference's quantizer, imported unmodified

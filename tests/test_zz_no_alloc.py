@@ -35,6 +35,8 @@ def test_noalloc_forward_matches_workspace_forward(oracle):
         st = L.lib.llmoc_moe_forward_noalloc(dl.dev.handle, Xd.data_ptr(), T, Y.data_ptr(),
                                              stream.cuda_stream)
         assert st == 0, L.last_error()
+        # the forward's device error word lives in the static array: read through the status query
+        assert L.lib.llmoc_moe_noalloc_status(dl.dev.handle, T, stream.cuda_stream) == 0, L.last_error()
         torch.cuda.synchronize()
         mre, cos = G.quality(G.bf16_to_f32(Y), G.bf16_to_f32(Y_ref))
         assert mre <= G.MAX_REL and cos >= G.MIN_COS, (T, mre, cos)
@@ -56,4 +58,5 @@ def test_noalloc_refuses_sizes_beyond_capacity(oracle):
     Y = torch.empty((T, layer.H), dtype=torch.bfloat16, device="cuda")
     st = L.lib.llmoc_moe_forward_noalloc(dev.handle, X.data_ptr(), T, Y.data_ptr(), None)
     assert st == 7 and "static scratch" in L.last_error()
+    assert L.lib.llmoc_moe_noalloc_status(dev.handle, T, None) == 1  # no such forward fits
     dev.close()
