@@ -64,6 +64,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl"],
                     help="multi-GPU: the library's NVLink peer-store transport, or NCCL all-to-alls")
+    ap.add_argument("--no-targets", action="store_true",
+                    help="skip the north-star target workloads (Kimi-K2 x4, GLM-4.5-Air prefill) of the N=1 line")
     ap.add_argument("--copies", type=int, default=0,
                     help="distinct layer copies to rotate (0 = enough to defeat L2); small values "
                          "make ncu captures cheap")
@@ -139,6 +141,15 @@ def measured_peak():
         d = json.load(open(p))
         return float(d["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
+
+
+def measured_tensor_peak():
+    """Dense bf16 TFLOP/s: (burst, sustained, kind)."""
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["bf16_tflops"]), float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "measured"
+    return 1590.0, 1400.0, "fallback"
 
 
 def ncu_traffic(config: str, T: int):
@@ -374,6 +385,15 @@ def run_llmoc(args):
         e2e_step(i, T)
     ms_e2e = timed(T, args.steps, e2e_step)
 
+    targets = None
+    if world == 1 and not args.no_targets and args.config == "qwen3_30b_a3b":
+        for lay in layers:
+            lay.close()
+        layers = []
+        del ws, Xpool
+        torch.cuda.empty_cache()
+        targets = run_targets(torch, L, args.steps, args.warmup)
+
     out = None
     if rank == 0:
         world_tokens = world * T * args.steps
@@ -431,12 +451,126 @@ def run_llmoc(args):
             "clocks": clk,
             "gpu_launches": int(launches),
         }
+        if targets is not None:
+            out["targets"] = targets
         print(json.dumps(out), flush=True)
     for lay in layers:
         lay.close()
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+    return out
+
+
+# The north-star targets measured beside the headline (one GPU): BASELINE
+# config 5 (four Kimi-K2 layers: decode T = 1, 64 against the HBM roofline,
+# prefill T = 8192 against the tensor roofline) and config 4's prefill
+# (GLM-4.5-Air, T = 4096).  A step runs the target's layers in sequence with
+# the residual add fused (llmoc_moe_forward_residual, in place); every layer
+# is distinct and larger than L2.
+TARGETS = {
+    "kimi_k2_x4": dict(cfg="kimi_k2", layers=4, Ts=(1, 64, 8192), config="BASELINE config 5 (1 GPU)"),
+    "glm45_air": dict(cfg="glm45_air", layers=2, Ts=(4096,), config="BASELINE config 4 (prefill)"),
+}
+
+
+def run_targets(torch, L, steps, warmup):
+    """Per target and T: step time, touched experts, per-stage times (CUDA
+    events around each stage, a separate pass), and the two GEMMs' roofline
+    fractions from their algorithmic bytes (decode) or FLOPs (prefill)."""
+    hbm, _ = measured_peak()
+    tf_burst, tf_sust, tf_kind = measured_tensor_peak()
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    out = {}
+    for name, tg in TARGETS.items():
+        cfg = CONFIGS[tg["cfg"]]
+        H, I, E, k = cfg["H"], cfg["I"], cfg["E"], cfg["topk"]
+        kk = k + (1 if cfg["shared"] else 0)
+        gu_b, dn_b = layer_bytes(cfg)
+        layers, _ = build_layers(torch, L, cfg, tg["layers"], seed=2468)
+        Tmax = max(tg["Ts"])
+        ws_bytes = layers[0].workspace_bytes(Tmax)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+        g = torch.Generator(device="cuda").manual_seed(13)
+        X0 = torch.randn((Tmax, H), generator=g, device="cuda").to(torch.bfloat16)
+        X = torch.empty_like(X0)
+        res = {}
+        for T in tg["Ts"]:
+            K = max(2, min(steps, 10 if T < 1024 else 4))
+
+            def step():
+                for lay in layers:
+                    lay.forward_residual(X, T, X, X, ws, ws_bytes, sp)
+
+            X.copy_(X0)
+            for _ in range(max(3, warmup)):
+                step()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            for _ in range(K):
+                step()
+            b.record(stream)
+            torch.cuda.synchronize()
+            ms = a.elapsed_time(b) / K
+            # per-stage times (serialised by the events) and touched experts per layer
+            for lay in layers:
+                lay.set_stage_timing(True)
+            X.copy_(X0)
+            touched = []
+            for _ in range(K):
+                for lay in layers:
+                    lay.forward_residual(X, T, X, X, ws, ws_bytes, sp)
+                    vw = lay.route_views(T, ws, ws_bytes)
+                    off = ws[vw.offsets - ws.data_ptr(): vw.offsets - ws.data_ptr() + 4 * (E + 1)]
+                    touched.append(int(np.count_nonzero(np.diff(off.cpu().numpy().view(np.int32)))))
+            torch.cuda.synchronize()
+            stage = {s_: 0.0 for s_ in L.MoeLayer.STAGES}
+            calls = 0
+            for lay in layers:
+                st_, n_ = lay.stage_times()
+                for s_, v in st_.items():
+                    stage[s_] += v
+                calls += n_
+                lay.set_stage_timing(False)
+            stage = {s_: v / max(calls, 1) for s_, v in stage.items()}  # per layer forward
+            tch = float(np.mean(touched)) + (1 if cfg["shared"] else 0)  # experts streamed per layer
+            r = {"ms_per_step": ms, "tokens_per_s": T / (ms * 1e-3), "layers_per_step": len(layers),
+                 "touched_experts_per_layer": tch, "stage_ms_per_layer": {s_: round(v, 5) for s_, v in stage.items()}}
+            if T <= 128:  # decode: bytes (weights of the touched experts + activations) per GEMM launch
+                gu_bytes = tch * gu_b + T * H * 2 + T * kk * I * 2
+                dn_bytes = tch * dn_b + T * kk * (I * 2 + H * 4)
+                layer_bytes_ = tch * (gu_b + dn_b) + E * H * 2 + 2 * T * H * 2
+                r["gate_up"] = {"alg_bytes": gu_bytes, "ms": stage["gate_up"],
+                                "GBps": gu_bytes / (stage["gate_up"] * 1e-3) / 1e9,
+                                "hbm_frac": gu_bytes / (stage["gate_up"] * 1e-3) / 1e9 / hbm}
+                r["down"] = {"alg_bytes": dn_bytes, "ms": stage["down"],
+                             "GBps": dn_bytes / (stage["down"] * 1e-3) / 1e9,
+                             "hbm_frac": dn_bytes / (stage["down"] * 1e-3) / 1e9 / hbm}
+                r["layer"] = {"alg_bytes": layer_bytes_, "ms": ms / len(layers),
+                              "hbm_frac": layer_bytes_ / (ms / len(layers) * 1e-3) / 1e9 / hbm}
+                r["peak"] = {"hbm_GBps": hbm}
+            else:  # prefill: FLOPs per GEMM launch (routed + shared rows)
+                gu_fl = 2.0 * T * kk * 2 * I * H
+                dn_fl = 2.0 * T * kk * I * H
+                r["gate_up"] = {"flops": gu_fl, "ms": stage["gate_up"],
+                                "TFLOPs": gu_fl / (stage["gate_up"] * 1e-3) / 1e12,
+                                "tensor_frac_burst": gu_fl / (stage["gate_up"] * 1e-3) / 1e12 / tf_burst,
+                                "tensor_frac_sustained": gu_fl / (stage["gate_up"] * 1e-3) / 1e12 / tf_sust}
+                r["down"] = {"flops": dn_fl, "ms": stage["down"],
+                             "TFLOPs": dn_fl / (stage["down"] * 1e-3) / 1e12,
+                             "tensor_frac_burst": dn_fl / (stage["down"] * 1e-3) / 1e12 / tf_burst}
+                r["layer"] = {"flops": 3.0 * gu_fl / 2 + 2.0 * T * E * H, "ms": ms / len(layers),
+                              "TFLOPs": (3.0 * gu_fl / 2 + 2.0 * T * E * H) / (ms / len(layers) * 1e-3) / 1e12}
+                r["peak"] = {"bf16_tflops_burst": tf_burst, "bf16_tflops_sustained": tf_sust, "kind": tf_kind}
+            res[f"T{T}"] = r
+        out[name] = {"config": tg["config"], "workload": f"{tg['cfg']} x {tg['layers']} distinct layers",
+                     "results": res}
+        for lay in layers:
+            lay.close()
+        del ws, X, X0
+        torch.cuda.empty_cache()
     return out
 
 
@@ -672,6 +806,47 @@ def run_stack(args):
     return out
 
 
+def reference_layer(O, cfg, X, rng, weight_budget=2.5e9):
+    """A layer for the reference arm with every expert distinct: the router
+    (and selection bias) first, then the tokens of X are taken in order while
+    the experts they route to stay within `weight_budget` weights, and only
+    those experts (and the shared one) are drawn and quantized -- the CPU path
+    reads no other.  Returns (layer, token indices of that pool)."""
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import orc
+
+    H, I, E, k, gs = cfg["H"], cfg["I"], cfg["E"], cfg["topk"], cfg["gs"]
+    rw = orc.bf16_bits(rng.standard_normal((E, H), dtype=np.float32) * np.float32(0.02))
+    bias = (rng.standard_normal(E, dtype=np.float32) * np.float32(0.1)) if cfg["router"] == 1 else None
+    tiny = orc.Int4Weight(np.zeros((16, 16), np.uint8), np.zeros((16, 1), np.uint16), None, 16, 32, 32)
+    stub = orc.Expert(tiny, tiny, tiny)
+    probe = orc.MoeLayer(H, I, E, k, rw, [stub] * E, cfg["router"], bias, cfg["scaling"], None, 1.0)
+    _, ids, _ = O.moe_route(probe, X)
+    max_e = max(k + 1, int(weight_budget // (3 * I * H)))
+    need, pool = set(), []
+    for t in range(X.shape[0]):
+        s = need | set(ids[t].tolist())
+        if len(s) > max_e and pool:
+            break
+        need, pool = s, pool + [t]
+
+    def q(M, K, g):
+        W = orc.bf16_round(g.standard_normal((M, K), dtype=np.float32) * np.float32(0.02))
+        return O.quant_awq_sym(W, gs, bf16_scale=True)
+
+    made = {}
+    for e in sorted(need):
+        g = np.random.default_rng(10_000 + e)
+        made[e] = orc.Expert(q(I, H, g), q(I, H, g), q(H, I, g))
+    filler = made[min(need)]
+    experts = [made.get(e, filler) for e in range(E)]
+    sh = None
+    if cfg["shared"]:
+        g = np.random.default_rng(9_999)
+        sh = orc.Expert(q(I, H, g), q(I, H, g), q(H, I, g))
+    return orc.MoeLayer(H, I, E, k, rw, experts, cfg["router"], bias, cfg["scaling"], sh, 1.0), pool
+
+
 def run_reference(args):
     """The reference's own CPU implementation of the path on the host cores."""
     rank, world, _ = dist_env()
@@ -690,18 +865,17 @@ def run_reference(args):
     cfg = CONFIGS[STACKS[args.config]["base"]] if args.config in STACKS else CONFIGS[args.config]
     rng = np.random.default_rng(1234)
     O = orc.Oracle()
-    layer = orc.make_layer(O, rng, H=cfg["H"], I=cfg["I"], E=cfg["E"], topk=cfg["topk"], gs=cfg["gs"],
-                           router=cfg["router"], routed_scaling=cfg["scaling"], shared=cfg["shared"],
-                           n_real=16)
     R = orc.Reference()
     T = config.get("tokens", config.get("tokens_per_gpu"))
     X = orc.make_tokens(rng, T, cfg["H"])
-    per_step = max(1, min(T, 8))  # bounded sample of each step's tokens
+    layer, pool = reference_layer(O, cfg, X, rng)
+    Xp = X[pool]
+    per_step = max(1, min(len(pool), 8))  # bounded sample of each step's tokens
     for i in range(args.warmup):
-        R.moe_layer_forward(layer, X[:per_step])
+        R.moe_layer_forward(layer, Xp[:per_step])
     t0 = time.perf_counter()
     for i in range(args.steps):
-        R.moe_layer_forward(layer, X[(i * per_step) % T:][:per_step])
+        R.moe_layer_forward(layer, Xp[(i * per_step) % len(pool):][:per_step])
     dt = time.perf_counter() - t0
     v = per_step * args.steps / dt / n_layers
     line = {"impl": "reference", "metric": metric, "value": v,
@@ -710,7 +884,8 @@ def run_reference(args):
             "vs_baseline": None, "dtype": "int4 weights x fp32 activations (AVX2 fp32)",
             "data": "synthetic", "config": config,
             "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": R.max_threads(), "kind": "reference",
-                             "sample": f"{per_step} of the {T} tokens per step through the reference's "
+                             "sample": f"{per_step} tokens per step, cycling over {len(pool)} of the {T} "
+                                       f"tokens (every expert they route to distinct) through the reference's "
                                        f"per-token moe_ffn_token CPU path"
                                        + (f", one layer, rate / {n_layers} layers" if n_layers > 1 else "")},
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}

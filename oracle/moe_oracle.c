@@ -582,6 +582,24 @@ ORC_API void orc_moe_layer_forward(const orc_layer* L, const float* X, int T, fl
   }
 }
 
+/* The routing part of orc_moe_layer_forward for every token (router GEMV in
+ * the reference's order, then its softmax or the sigmoid + bias selection):
+ * logits[T,E], ids/weights[T,topk].  Tokens run in parallel (checker for
+ * large batches; no expert weights are read). */
+ORC_API void orc_moe_route(const orc_layer* L, const float* X, int T, float* logits, int* ids,
+                           float* weights) {
+  const int H = L->H, E = L->E, K = L->topk;
+#pragma omp parallel for schedule(dynamic, 16)
+  for (int t = 0; t < T; ++t) {
+    float* lg = logits + (size_t)t * E;
+    orc_gemm_bias_free(X + (size_t)t * H, L->router_w, lg, E, H, 0);
+    if (L->router == ORC_ROUTER_SOFTMAX)
+      orc_route_softmax(lg, E, K, ids + (size_t)t * K, weights + (size_t)t * K, NULL);
+    else
+      orc_route_sigmoid_bias(lg, L->bias, E, K, L->routed_scaling, ids + (size_t)t * K, weights + (size_t)t * K);
+  }
+}
+
 /* Expert FFN with the routing given (the contract of hal::cuda::try_moe_ffn_int4,
  * src/hal/cuda_backend.cpp:5217-5317): y = sum_j w_j * ffn_j(x) in the given
  * order, experts with |w| < 1e-12 skipped, then the shared expert. */

@@ -197,6 +197,9 @@ class Oracle:
             self._qgptq = L.orc_quant_gptq_asym
             self._qgptq.argtypes = [_f32p, C.c_int, C.c_int, C.c_int, _u8p, _u16p, _u16p]
             self._qgptq.restype = None
+            self._route_all = L.orc_moe_route
+            self._route_all.argtypes = [C.POINTER(LayerC), _f32p, C.c_int, _f32p, _i32p, _f32p]
+            self._route_all.restype = None
             self._routed = L.orc_moe_ffn_routed
             self._routed.argtypes = [_f32p, C.c_int, C.c_int, C.POINTER(ExpertC), _f32p, C.c_int,
                                      C.c_void_p, C.c_float, _f32p]
@@ -270,6 +273,19 @@ class Oracle:
         return Y, ids, w, None
 
     # --- oracle-only helpers --------------------------------------------
+    def moe_route(self, layer: MoeLayer, X: np.ndarray):
+        """Router logits [T,E], ids and weights [T,topk] of every token (the
+        routing of moe_layer_forward; tokens in parallel, no expert reads)."""
+        X = np.ascontiguousarray(X, np.float32)
+        T = X.shape[0]
+        logits = np.empty((T, layer.E), np.float32)
+        ids = np.empty((T, layer.topk), np.int32)
+        w = np.empty((T, layer.topk), np.float32)
+        lc = layer.c()
+        self._route_all(C.byref(lc), X, T, logits, ids, w)
+        return logits, ids, w
+
+
     def route_softmax(self, logits: np.ndarray, k: int):
         E = logits.size
         ids = np.empty(k, np.int32)

@@ -102,3 +102,106 @@ class DevLayer:
 
     def close(self):
         self.dev.close()
+
+
+# ------------------------------------------------ full-size layers in HBM
+
+class DeviceBuiltLayer:
+    """A full-size layer whose experts are all distinct, drawn and quantized
+    on the device (torch RNG, then llmoc_quantize_awq_sym: quant_awq_sym
+    semantics with bf16-valued scales, the same quantizer the CPU tests pin to
+    the reference's) and uploaded with llmoc_moe_layer_create_device.  The
+    QLWC tensors stay on the device, so the oracle can be handed any expert's
+    exact bytes (host_layer) without building every expert on the CPU."""
+
+    def __init__(self, H, I, E, topk, gs, router=0, routed_scaling=1.0, shared=False, seed=0,
+                 rw_add=None):
+        t = torch()
+        self.H, self.I, self.E, self.topk, self.gs = H, I, E, topk, gs
+        self.router, self.routed_scaling, self.has_shared = router, routed_scaling, shared
+        n_exp = E + (1 if shared else 0)
+        g = t.Generator(device="cuda")
+        g.manual_seed(seed)
+        self.raw = {}
+        for name, (M, K) in (("gate", (I, H)), ("up", (I, H)), ("down", (H, I))):
+            q = t.empty((n_exp * M, K // 2), dtype=t.uint8, device="cuda")
+            s = t.empty((n_exp * M, K // gs), dtype=t.int16, device="cuda")
+            per = max(1, int(2 ** 27 // (M * K)))
+            for e0 in range(0, n_exp, per):
+                e1 = min(n_exp, e0 + per)
+                W = (t.randn(((e1 - e0) * M, K), generator=g, device="cuda") * 0.02).to(t.bfloat16)
+                L.quantize_awq_sym(W, (e1 - e0) * M, K, gs, True, q[e0 * M:e1 * M], s[e0 * M:e1 * M])
+                del W
+            self.raw[name] = (q, s, M, K)
+        rw = t.randn((E, H), generator=g, device="cuda") * 0.02
+        if rw_add is not None:
+            rw = rw + rw_add
+        self.router_w = rw.to(t.bfloat16)
+        self.bias = (t.randn((E,), generator=g, device="cuda") * 0.1).float() if router == 1 else None
+        views = []
+        for e in range(n_exp):
+            for name in ("gate", "up", "down"):
+                q, s, M, K = self.raw[name]
+                views.append(L.view(q.data_ptr() + e * M * (K // 2), s.data_ptr() + e * M * (K // gs) * 2,
+                                    None, M, K, gs))
+        desc = L.LayerDesc(H, I, E, topk, gs, L.SCHEME_AWQ_SYM, 7, router, routed_scaling, 1 if shared else 0, 1.0)
+        t.cuda.synchronize()
+        self.dev = L.MoeLayer.create(desc, self.router_w, self.bias, views[:3 * E],
+                                     views[3 * E:] if shared else None, device=0, on_device=True)
+        self.router_bits = self.router_w.view(t.int16).cpu().numpy().view(np.uint16).copy()
+        self.bias_host = self.bias.cpu().numpy().copy() if self.bias is not None else None
+        self._cache = {}
+
+    def expert(self, e: int) -> orc.Expert:
+        """Expert e's QLWC bytes, copied to the host (e == E: the shared expert)."""
+        if e not in self._cache:
+            ws = []
+            for name in ("gate", "up", "down"):
+                q, s, M, K = self.raw[name]
+                ws.append(orc.Int4Weight(q[e * M:(e + 1) * M].cpu().numpy(),
+                                         s[e * M:(e + 1) * M].cpu().numpy().view(np.uint16),
+                                         None, M, K, self.gs, orc.SCHEME_AWQ_SYM, 7))
+            self._cache[e] = orc.Expert(*ws)
+        return self._cache[e]
+
+    def host_layer(self, needed) -> orc.MoeLayer:
+        """The layer as the oracle sees it, with the experts in `needed` (and the
+        shared one) holding their real bytes; the others stand in with the
+        first needed expert's (a token routed to one of them would not match)."""
+        needed = sorted(set(int(e) for e in needed))
+        filler = self.expert(needed[0])
+        experts = [self.expert(e) if e in set(needed) else filler for e in range(self.E)]
+        return orc.MoeLayer(self.H, self.I, self.E, self.topk, self.router_bits, experts, self.router,
+                            self.bias_host, self.routed_scaling,
+                            self.expert(self.E) if self.has_shared else None, 1.0)
+
+    def route_layer(self) -> orc.MoeLayer:
+        """The router part only (for oracle.moe_route: no expert is read)."""
+        e0 = self.expert(0)
+        return orc.MoeLayer(self.H, self.I, self.E, self.topk, self.router_bits, [e0] * self.E, self.router,
+                            self.bias_host, self.routed_scaling, None, 1.0)
+
+    def close(self):
+        self.dev.close()
+        self.raw = {}
+        self._cache = {}
+
+
+def cover_sample(ids: np.ndarray, n_spread: int = 64) -> np.ndarray:
+    """Tokens to check against the oracle: n_spread spread evenly over the
+    batch, plus a greedy cover so that every expert the batch routes to has at
+    least one of its rows among them (every expert group is checked)."""
+    T = ids.shape[0]
+    chosen = set(np.unique(np.linspace(0, T - 1, min(T, n_spread)).astype(int)).tolist())
+    covered = set(ids[sorted(chosen)].reshape(-1).tolist())
+    need = set(ids.reshape(-1).tolist()) - covered
+    first = {}
+    for t in range(T):
+        for e in ids[t]:
+            first.setdefault(int(e), t)
+    while need:
+        e = min(need)
+        t = first[e]
+        chosen.add(t)
+        need -= set(ids[t].tolist())
+    return np.array(sorted(chosen))

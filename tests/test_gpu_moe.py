@@ -270,36 +270,124 @@ def test_zero_weights_give_zero_output(oracle):
 
 FULL = {
     # Qwen3-30B-A3B layer
-    "qwen3_30b_a3b": dict(H=2048, I=768, E=128, topk=8, gs=128, n_real=16),
+    "qwen3_30b_a3b": dict(H=2048, I=768, E=128, topk=8, gs=128),
     # GLM-4.5-Air layer (sigmoid + bias, shared expert)
-    "glm45_air": dict(H=4096, I=1408, E=128, topk=8, gs=128, router=1, shared=True, n_real=8),
+    "glm45_air": dict(H=4096, I=1408, E=128, topk=8, gs=128, router=1, shared=True),
     # Kimi-K2 layer (gs 32, 384 experts, scaling 2.827, shared)
-    "kimi_k2": dict(H=7168, I=2048, E=384, topk=8, gs=32, router=1, routed_scaling=2.827,
-                    shared=True, n_real=4),
+    "kimi_k2": dict(H=7168, I=2048, E=384, topk=8, gs=32, router=1, routed_scaling=2.827, shared=True),
 }
+
+
+def _check_full(oracle, dl, X, Xd, T):
+    """Routing of every token against the oracle (logits bitwise, ids exact,
+    weights within 2e-6), the permutation against the canonical order, and the
+    outputs of >= 64 tokens that cover every expert group the batch uses."""
+    Y = torch.empty((T, dl.H), dtype=torch.bfloat16, device="cuda")
+    ws_bytes = dl.dev.workspace_bytes(T)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+    dl.dev.forward(Xd, T, Y, ws, ws_bytes, torch.cuda.current_stream())
+    torch.cuda.synchronize()
+    v = dl.dev.route_views(T, ws, ws_bytes)
+    base = ws.data_ptr()
+
+    def grab(addr, n, dt):
+        return ws[addr - base: addr - base + 4 * n].cpu().numpy().view(dt).copy()
+
+    kk, n_exp = dl.dev.kk, dl.dev.n_exp
+    assert int(grab(v.error_flag, 1, np.int32)[0]) == 0
+    logits = grab(v.logits, T * dl.E, np.float32).reshape(T, dl.E)
+    ids = grab(v.ids, T * kk, np.int32).reshape(T, kk)
+    w = grab(v.weights, T * kk, np.float32).reshape(T, kk)
+    ref_logits, ref_ids, ref_w = oracle.moe_route(dl.route_layer(), X)
+    assert np.array_equal(logits.view(np.uint32), ref_logits.view(np.uint32))
+    assert np.array_equal(ids[:, :dl.topk], ref_ids)
+    np.testing.assert_allclose(w[:, :dl.topk], ref_w, rtol=2e-6, atol=0)
+    if dl.has_shared:
+        assert np.all(ids[:, dl.topk] == dl.E)
+    off, srt, inv = oracle.permute(ids, n_exp)
+    assert np.array_equal(grab(v.offsets, n_exp + 1, np.int32), off)
+    assert np.array_equal(grab(v.sorted, T * kk, np.int32), srt)
+    assert np.array_equal(grab(v.inverse, T * kk, np.int32), inv)
+    sample = G.cover_sample(ids[:, :dl.topk])
+    assert len(sample) >= min(T, 64)
+    assert set(ids[sample, :dl.topk].reshape(-1)) == set(ids[:, :dl.topk].reshape(-1))
+    layer = dl.host_layer(ids[sample, :dl.topk].reshape(-1))
+    Yref, ids_s, _, _ = oracle.moe_layer_forward(layer, X[sample])
+    assert np.array_equal(ids_s, ref_ids[sample])
+    got = G.bf16_to_f32(Y[torch.as_tensor(sample, device="cuda")])
+    mre, cos = G.quality(got, Yref)
+    assert mre <= G.MAX_REL and cos >= G.MIN_COS, (mre, cos)
+    for i in range(len(sample)):  # every sampled token on its own, too
+        mre_t, cos_t = G.quality(got[i], Yref[i])
+        assert mre_t <= 2 * G.MAX_REL and cos_t >= 0.999, (int(sample[i]), mre_t, cos_t)
+    return ids
 
 
 @pytest.mark.parametrize("name,T", [("qwen3_30b_a3b", 1), ("qwen3_30b_a3b", 8), ("qwen3_30b_a3b", 64),
                                     ("qwen3_30b_a3b", 512), ("glm45_air", 64), ("glm45_air", 1024),
-                                    ("kimi_k2", 64), ("kimi_k2", 1024)])
+                                    ("glm45_air", 4096), ("kimi_k2", 1), ("kimi_k2", 64),
+                                    ("kimi_k2", 1024), ("kimi_k2", 8192)])
 def test_full_size_layer(oracle, name, T):
-    """Full BASELINE shapes: routing bit-exact for every token; outputs checked
-    against the oracle on a sample of tokens (each token's output depends on
-    that token alone)."""
-    rng = np.random.default_rng(100 + T)
-    layer = orc.make_layer(oracle, rng, **FULL[name])
-    X = orc.make_tokens(rng, T, layer.H)
-    dl = G.DevLayer(layer, T)
-    Y, ws_bytes = dl.forward(X)
-    v = dl.views(T, ws_bytes)
-    assert v["error_flag"] == 0
-    sample = np.unique(np.linspace(0, T - 1, min(T, 8)).astype(int))
-    check_routing(oracle, dl, X, v, sample)
-    Yref, ids, _, _ = oracle.moe_layer_forward(layer, X[sample])
-    assert np.array_equal(v["ids"][sample, :layer.topk], ids)
-    mre, cos = G.quality(G.bf16_to_f32(Y[torch.as_tensor(sample, device="cuda")]), Yref)
-    assert mre <= G.MAX_REL and cos >= G.MIN_COS, (mre, cos)
+    """The BASELINE shapes and token counts the bench times, every expert
+    distinct (no expert shares another's bytes, so an indexing slip in the
+    expert table, the repacked arena or the work list cannot pass): routing
+    bit-exact for every token, outputs on a sample covering every expert group
+    (each token's output depends on that token alone)."""
+    dl = G.DeviceBuiltLayer(**FULL[name], seed=100 + T)
+    g = torch.Generator(device="cuda").manual_seed(7 + T)
+    Xd = torch.randn((T, dl.H), generator=g, device="cuda").to(torch.bfloat16)
+    X = G.bf16_to_f32(Xd)
+    _check_full(oracle, dl, X, Xd, T)
     dl.close()
+
+
+def test_zipf_skewed_residual_stack(oracle):
+    """Four distinct Qwen3-30B-A3B-shape layers with router rows pushed towards
+    a Zipf(1.1) popularity (BASELINE config 3's skew: a few hot experts with
+    long groups, many cold or empty ones), run as a decoder stack through
+    llmoc_moe_forward_residual in place (h += moe(h)), T = 16.  Each layer's
+    output is checked against its input plus the oracle's layer output on that
+    same input (read back from the device), and the routing against the
+    oracle's, so an error in any layer of the stack shows up where it is.
+    The routed part is checked on its own (the plain forward of the same input
+    against the oracle), then the residual forward against input + that output
+    (one bf16 rounding of an fp32 sum apart)."""
+    E, H, T, n_layers = 128, 2048, 16, 4
+    g = torch.Generator(device="cuda").manual_seed(11)
+    v = torch.randn(H, generator=g, device="cuda")
+    v = v / v.norm()
+    ranks = torch.arange(1, E + 1, device="cuda", dtype=torch.float32)
+    boost = 0.2 * ranks ** -1.1  # a logit boost of ~3.2 for the hottest expert along 16 v
+    layers = [G.DeviceBuiltLayer(**FULL["qwen3_30b_a3b"], seed=500 + l,
+                                 rw_add=boost[torch.randperm(E, generator=g, device="cuda")][:, None] * v[None, :])
+              for l in range(n_layers)]
+    h = (torch.randn((T, H), generator=g, device="cuda") + 16.0 * v).to(torch.bfloat16)
+    ws_bytes = layers[0].dev.workspace_bytes(T)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+    top_share = []
+    stream = torch.cuda.current_stream()
+    for dl in layers:
+        x_in = G.bf16_to_f32(h)
+        Y = torch.empty_like(h)
+        dl.dev.forward(h, T, Y, ws, ws_bytes, stream)
+        torch.cuda.synchronize()
+        rv = dl.dev.route_views(T, ws, ws_bytes)
+        ids = ws[rv.ids - ws.data_ptr(): rv.ids - ws.data_ptr() + 4 * T * 8].cpu().numpy().view(np.int32)
+        ids = ids.reshape(T, 8).copy()
+        _, ref_ids, _ = oracle.moe_route(dl.route_layer(), x_in)
+        assert np.array_equal(ids, ref_ids)
+        top_share.append(np.bincount(ids.reshape(-1), minlength=E).max() / T)
+        Yref, _, _, _ = oracle.moe_layer_forward(dl.host_layer(ids.reshape(-1)), x_in)
+        y = G.bf16_to_f32(Y)
+        mre, cos = G.quality(y, Yref)
+        assert mre <= G.MAX_REL and cos >= G.MIN_COS, (mre, cos)
+        dl.dev.forward_residual(h, T, h, h, ws, ws_bytes, stream)  # h += moe(h), in place
+        torch.cuda.synchronize()
+        err = np.abs(G.bf16_to_f32(h) - (x_in + y)).max()
+        assert err <= 2.0 ** -6 * (np.abs(x_in).max() + np.abs(y).max()), err
+    assert max(top_share) >= 0.5, top_share  # skewed: some expert takes at least half of the tokens
+    for dl in layers:
+        dl.close()
 
 
 # ------------------------------------------- the reference's host-fp32 API
@@ -389,11 +477,31 @@ def test_try_gemm_int4_config1_shapes(oracle, M, K, gs, n, scheme, fresh_cache):
     assert L.lib.llmoc_try_gemm_int4_batch(L.ptr(X), n, C.byref(v), L.ptr(Y)) == 1, L.last_error()
     ref = oracle.gemm_int4_batch(X, W)
     assert np.all(np.abs(Y - ref) < 1e-3 * (1 + np.abs(ref)))
-    ys = [np.empty(M, np.float32) for _ in range(2)]
-    Ws = (C.POINTER(L.Int4View) * 2)(C.pointer(v), C.pointer(v))
-    yp = (C.c_void_p * 2)(*[L.ptr(a) for a in ys])
-    assert L.lib.llmoc_try_gemm_int4_multi(L.ptr(X[0]), Ws, yp, 2) == 1
-    assert np.array_equal(ys[0], Y[0]) and np.array_equal(ys[1], Y[0])
+
+
+@pytest.mark.parametrize("n", [2, 3, 4])
+def test_try_gemm_int4_multi_distinct_weights(oracle, n, fresh_cache):
+    """try_gemm_int4_multi (cuda_backend.cpp:3048-3112: up to 4 GEMVs sharing
+    x) with n different weights of different M: each ys[i] against the oracle
+    GEMV of its own W_i, and bitwise equal to the single-weight call on it, so
+    a swap or mix-up of the weights cannot pass."""
+    rng = np.random.default_rng(40 + n)
+    K = 2048
+    Ms = [768, 1536, 256, 2048][:n]
+    Wts = [oracle.quant_awq_sym(orc.bf16_round(rng.standard_normal((M, K), dtype=np.float32) * np.float32(0.02)),
+                                128, True) for M in Ms]
+    x = rng.standard_normal(K, dtype=np.float32)
+    vs = [L.view_of(w) for w in Wts]
+    ys = [np.full(M, np.nan, np.float32) for M in Ms]
+    Ws = (C.POINTER(L.Int4View) * n)(*[C.pointer(v) for v in vs])
+    yp = (C.c_void_p * n)(*[L.ptr(a) for a in ys])
+    assert L.lib.llmoc_try_gemm_int4_multi(L.ptr(x), Ws, yp, n) == 1, L.last_error()
+    for i in range(n):
+        ref = oracle.gemm_int4(x, Wts[i])
+        assert np.all(np.abs(ys[i] - ref) < 1e-3 * (1 + np.abs(ref))), i
+        one = np.empty(Ms[i], np.float32)
+        assert L.lib.llmoc_try_gemm_int4(L.ptr(x), C.byref(vs[i]), L.ptr(one)) == 1
+        assert np.array_equal(ys[i], one), i
 
 
 @pytest.mark.parametrize("shared", [False, True])
