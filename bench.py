@@ -466,8 +466,9 @@ def run_llmoc(args):
 # config 5 (four Kimi-K2 layers: decode T = 1, 64 against the HBM roofline,
 # prefill T = 8192 against the tensor roofline) and config 4's prefill
 # (GLM-4.5-Air, T = 4096).  A step runs the target's layers in sequence with
-# the residual add fused (llmoc_moe_forward_residual, in place); every layer
-# is distinct and larger than L2.
+# the residual add fused (llmoc_moe_forward_residual, in place), starting each
+# step from the same input rows (a T x H copy inside the step); every layer is
+# distinct and larger than L2.
 TARGETS = {
     "kimi_k2_x4": dict(cfg="kimi_k2", layers=4, Ts=(1, 64, 8192), config="BASELINE config 5 (1 GPU)"),
     "glm45_air": dict(cfg="glm45_air", layers=2, Ts=(4096,), config="BASELINE config 4 (prefill)"),
@@ -499,11 +500,11 @@ def run_targets(torch, L, steps, warmup):
         for T in tg["Ts"]:
             K = max(2, min(steps, 10 if T < 1024 else 4))
 
-            def step():
+            def step():  # the layers in sequence on the residual stream, from the same input every step
+                X[:T].copy_(X0[:T])
                 for lay in layers:
                     lay.forward_residual(X, T, X, X, ws, ws_bytes, sp)
 
-            X.copy_(X0)
             for _ in range(max(3, warmup)):
                 step()
             torch.cuda.synchronize()
@@ -517,9 +518,9 @@ def run_targets(torch, L, steps, warmup):
             # per-stage times (serialised by the events) and touched experts per layer
             for lay in layers:
                 lay.set_stage_timing(True)
-            X.copy_(X0)
             touched = []
             for _ in range(K):
+                X[:T].copy_(X0[:T])
                 for lay in layers:
                     lay.forward_residual(X, T, X, X, ws, ws_bytes, sp)
                     vw = lay.route_views(T, ws, ws_bytes)

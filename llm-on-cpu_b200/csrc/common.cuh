@@ -64,6 +64,81 @@ __device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) {
 __device__ __forceinline__ float to_f32(float v) { return v; }
 __device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
 
+// fp16 activation row for the decode gate/up GEMM, by one warp (all 32 lanes
+// call it): x = src (row r of the activations, bf16, H % 128 == 0; global
+// memory read through the non-coherent path when GNC, else any generic
+// address, e.g. a copy in shared memory) -> Xh[r] = x * 2^-e rounded to fp16,
+// with e = (largest finite exponent of the row) - 141, so the row's largest
+// finite |x| lands in [2^14, 2^15) and every scaling is exact (e >= -100; an
+// all-zero row keeps e = 0); xsum[r][H/gs] = fp32 sums of each group of the
+// fp16 values (each lane's 8 values in order, then a fixed xor-shuffle tree
+// over the group's lanes); xscale[r] = 2^e.  A lane holds up to P 16-byte
+// pieces of the row in registers, all requested at once; rows longer than
+// 32 x P pieces are read twice.
+__device__ __forceinline__ uint32_t bf16x2_max_exp(uint32_t w, uint32_t m) {
+  const uint32_t e0 = (w >> 7) & 0xFFu, e1 = (w >> 23) & 0xFFu;
+  if (e0 != 0xFFu) m = max(m, e0);  // non-finite values pick no scale
+  if (e1 != 0xFFu) m = max(m, e1);
+  return m;
+}
+template <int P, bool GNC>
+__device__ __forceinline__ void prep_xh_row(const uint4* __restrict__ src, int r, int H, int gs, uint4* __restrict__ Xh,
+                                            float* __restrict__ xsum, float* __restrict__ xscale, int lane) {
+  constexpr int kPrepPieces = P;
+  const int n8 = H / 8, ng = H / gs, lpg = gs / 8;  // 16-byte pieces, groups, lanes per group
+  uint4* dst = Xh + (size_t)r * n8;
+  const bool fits = n8 <= 32 * kPrepPieces;
+  uint4 v[kPrepPieces];
+  uint32_t mexp = 0;  // largest finite bf16 exponent field
+  for (int b0 = 0; b0 < n8; b0 += 32 * kPrepPieces) {
+#pragma unroll
+    for (int j = 0; j < kPrepPieces; ++j) {
+      const int i = b0 + lane + 32 * j;
+      v[j] = i < n8 ? (GNC ? __ldg(src + i) : src[i]) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int j = 0; j < kPrepPieces; ++j) {
+      mexp = bf16x2_max_exp(v[j].x, mexp);
+      mexp = bf16x2_max_exp(v[j].y, mexp);
+      mexp = bf16x2_max_exp(v[j].z, mexp);
+      mexp = bf16x2_max_exp(v[j].w, mexp);
+    }
+  }
+  mexp = __reduce_max_sync(0xffffffffu, mexp);
+  const int e = mexp == 0 ? 0 : max(-100, (int)mexp - 141);
+  const float down = __int_as_float((127 - e) << 23);  // 2^-e (-113 <= -e <= 100)
+  for (int b0 = 0; b0 < n8; b0 += 32 * kPrepPieces) {
+    if (!fits) {
+#pragma unroll
+      for (int j = 0; j < kPrepPieces; ++j) {
+        const int i = b0 + lane + 32 * j;
+        v[j] = i < n8 ? (GNC ? __ldg(src + i) : src[i]) : make_uint4(0, 0, 0, 0);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kPrepPieces; ++j) {
+      const int i = b0 + lane + 32 * j;
+      if (b0 + 32 * j >= n8) break;  // uniform over the warp
+      const uint32_t wd[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+      uint32_t o[4];
+      float s = 0.f;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const __half2 h2 = __floats2half2_rn(__uint_as_float(wd[q] << 16) * down,
+                                             __uint_as_float(wd[q] & 0xFFFF0000u) * down);
+        const float2 f2 = __half22float2(h2);
+        s += f2.x;
+        s += f2.y;
+        o[q] = *reinterpret_cast<const uint32_t*>(&h2);
+      }
+      if (i < n8) dst[i] = make_uint4(o[0], o[1], o[2], o[3]);
+      for (int off = 1; off < lpg; off <<= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+      if (i < n8 && lane % lpg == 0) xsum[(size_t)r * ng + (i * 8) / gs] = s;
+    }
+  }
+  if (lane == 0) xscale[r] = __int_as_float((127 + e) << 23);  // 2^e
+}
+
 __device__ __forceinline__ uint32_t lanemask_lt() {
   uint32_t m;
   asm volatile("mov.u32 %0, %%lanemask_lt;" : "=r"(m));

@@ -124,6 +124,23 @@ __device__ __forceinline__ void mma_bf16(float d[4], const uint32_t a[4], uint32
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// fp16 forms of the two MMAs (the decode gate/up GEMM's fp16 activation path)
+__device__ __forceinline__ void mma_f16_z(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+  const float z = 0.f;
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%10,%10,%10,%10};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(z));
+}
+__device__ __forceinline__ void mma_f16(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
 __device__ __forceinline__ uint4 ldg_nc(const uint4* p) {
   uint4 v;
   asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
@@ -143,6 +160,18 @@ __device__ __forceinline__ void raw_word(uint32_t w, uint32_t a[4]) {
   a[1] = lop3_and_or(w >> 4, 0x000F000Fu, 0x43004300u);
   a[2] = lop3_and_or(w >> 8, 0x000F000Fu, 0x43004300u);
   a[3] = lop3_and_or(w >> 12, 0x000F000Fu, 0x43004300u);
+}
+// The same word -> four A registers as fp16 pairs with one shift: an fp16
+// mantissa has room for a nibble at bits 0-3 (1024 + q) and one at bits 4-7
+// (1024 + 16 q), so registers 0 and 2 (row g) hold 1024 + q and registers 1
+// and 3 (row g + 8) hold 1024 + 16 q.  After the MMA, row g's sum is
+// P = 1024 sum(x) + sum(q x) and row g+8's is 1024 sum(x) + 16 sum(q x).
+__device__ __forceinline__ void raw_word_f16(uint32_t w, uint32_t a[4]) {
+  const uint32_t w8 = w >> 8;
+  a[0] = lop3_and_or(w, 0x000F000Fu, 0x64006400u);
+  a[1] = lop3_and_or(w, 0x00F000F0u, 0x64006400u);
+  a[2] = lop3_and_or(w8, 0x000F000Fu, 0x64006400u);
+  a[3] = lop3_and_or(w8, 0x00F000F0u, 0x64006400u);
 }
 
 // Grouped INT4 GEMM on the tensor cores.  A warp owns one 16-row tile (both
@@ -164,13 +193,14 @@ __device__ __forceinline__ void raw_word(uint32_t w, uint32_t a[4]) {
 // grid.x = ceil(Mt * ks / 4), grid.y = work-list bound.
 constexpr int kStagesW = 3;
 
-template <int NP, int NT, bool AWQ>
+template <int NP, int NT, bool AWQ, bool XH = false>
 struct WStage {  // bytes of one stage of one warp
   static constexpr int kW = NP * 1024;         // 2 chunks x 512 B per projection
   static constexpr int kS = NP * 128;          // scales of the step's groups (<= 4 x 32 B)
   static constexpr int kZ = AWQ ? 0 : NP * 128;  // zeros (GPTQ)
   static constexpr int kB = NT * 4 * 512;      // 4 blocks x 16 B per lane per N-tile
-  static constexpr int kBytes = kW + kS + kZ + kB;
+  static constexpr int kX = XH ? 128 : 0;      // fp16 path: the 8 columns' group sums (16 B each)
+  static constexpr int kBytes = kW + kS + kZ + kB + kX;
   // the K-slice reduction reuses the warp's own stages once they are drained
   static_assert(kStagesW * kBytes >= NP * NT * 4 * 32 * 4, "reduction slot");
 };
@@ -186,12 +216,28 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
+// 4 * NG bytes (4, 8 or 16; source aligned to that size) through L1
+template <int NG>
+__device__ __forceinline__ void cp_async_small(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], %2;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+               "l"(src), "n"(4 * NG)
+               : "memory");
+}
 
-template <int MODE, int NT, int GSB, bool AWQ>
+// Correction of one fp32 group partial P of the fp16 path into sum x (q - zp)
+// (AWQ; bias = zp) or sum x q (GPTQ; bias = 0): rows g (hi = 0) hold
+// 1024 sum x + sum q x, rows g + 8 (hi = 1) 1024 sum x + 16 sum q x.
+__device__ __forceinline__ float f16_group(float P, float xs, int hi, float bias) {
+  return hi ? __fmaf_rn(-(64.f + bias), xs, P * 0.0625f) : __fmaf_rn(-(1024.f + bias), xs, P);
+}
+
+// XH: the fp16 activation path of k_int4_mma_p (gate/up only, NT = 1).
+template <int MODE, int NT, int GSB, bool AWQ, bool XH>
 __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
   constexpr int NP = MODE == MODE_GATE_UP ? 2 : 1;
   constexpr int NG = GSB == 4 ? 1 : (GSB == 2 ? 2 : 4);  // groups per step
-  using SG = WStage<NP, NT, AWQ>;
+  static_assert(!XH || (MODE == MODE_GATE_UP && NT == 1), "fp16 activations: gate/up, 8-row items");
+  using SG = WStage<NP, NT, AWQ, XH>;
   extern __shared__ __align__(128) unsigned char wsm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
@@ -237,6 +283,20 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
       const int row = a.gather ? a.gather[pos] / a.kk : pos;
       bsrc[n] = reinterpret_cast<const unsigned char*>(a.B) + ((size_t)row * a.ldb + 8 * t + s0 * 128) * 2;
     }
+    // XH: lanes < 8 copy column `lane`'s group sums with each step; the row
+    // scales of columns 2t, 2t + 1 are read now and used by the epilogue
+    const float* xsrc = nullptr;
+    const bool xval = XH && lane < 8 && lane < it.nrows;
+    float bs[2] = {1.f, 1.f};
+    if constexpr (XH) {
+      const int px = it.row0 + ((lane & 7) < it.nrows ? (lane & 7) : 0);
+      xsrc = a.bsum + (size_t)(a.gather ? a.gather[px] / a.kk : px) * a.ng + (size_t)s0 * NG;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int c = 2 * t + h, pc = it.row0 + (c < it.nrows ? c : 0);
+        bs[h] = a.bscale[a.gather ? a.gather[pc] / a.kk : pc];
+      }
+    }
     const int rtc = live ? rt : 0;
     const unsigned char* wsrc[NP];
     const unsigned char* ssrc[NP];
@@ -276,6 +336,10 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
         }
         bsrc[n] += 256;
       }
+      if constexpr (XH) {
+        if (xval) cp_async_small<NG>(sb + SG::kW + SG::kS + SG::kZ + SG::kB + lane * 16, xsrc);
+        xsrc += NG;
+      }
     };
     auto issue = [&](int stage) {
       issue_w(stage);
@@ -298,6 +362,7 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
 
     const uint32_t ones[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};
     const float bias = AWQ ? (float)(128 + a.zp) : 128.f;
+    const float zbias = AWQ ? (float)a.zp : 0.f;
     // two partial accumulators per chain (k16 halves kt = 0 / 1) halve the
     // dependent MMA chains; they are added at each group end
     float acc[NP][NT][4], tmp[NP][NT][2][4], xs[NT][2][4];
@@ -348,24 +413,44 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
       for (int b = 0; b < 4; ++b) {  // 32-wide block b of the step
 #pragma unroll
         for (int kt = 0; kt < 2; ++kt) {
+          if constexpr (!XH) {
 #pragma unroll
-          for (int n = 0; n < NT; ++n)
-            if (NT == 1 || n < ntc)
-              mma_bf16(xs[n][kt], ones, kt ? bv[n][b].z : bv[n][b].x, kt ? bv[n][b].w : bv[n][b].y);
+            for (int n = 0; n < NT; ++n)
+              if (NT == 1 || n < ntc)
+                mma_bf16(xs[n][kt], ones, kt ? bv[n][b].z : bv[n][b].x, kt ? bv[n][b].w : bv[n][b].y);
+          }
 #pragma unroll
           for (int p = 0; p < NP; ++p) {
             const uint4& q4 = wq[p][b >> 1];
             const int wi = (b & 1) * 2 + kt;
             const uint32_t wd = wi == 0 ? q4.x : wi == 1 ? q4.y : wi == 2 ? q4.z : q4.w;
             uint32_t af[4];
-            raw_word(wd, af);
+            if constexpr (XH) {
+              raw_word_f16(wd, af);
+              mma_f16(tmp[p][0][kt], af, kt ? bv[0][b].z : bv[0][b].x, kt ? bv[0][b].w : bv[0][b].y);
+            } else {
+              raw_word(wd, af);
 #pragma unroll
-            for (int n = 0; n < NT; ++n)
-              if (NT == 1 || n < ntc)
-                mma_bf16(tmp[p][n][kt], af, kt ? bv[n][b].z : bv[n][b].x, kt ? bv[n][b].w : bv[n][b].y);
+              for (int n = 0; n < NT; ++n)
+                if (NT == 1 || n < ntc)
+                  mma_bf16(tmp[p][n][kt], af, kt ? bv[n][b].z : bv[n][b].x, kt ? bv[n][b].w : bv[n][b].y);
+            }
           }
         }
-        if ((b + 1) % GSB == 0) {  // group end
+        if (XH && (b + 1) % GSB == 0) {  // group end, fp16 path
+          const int q = b / GSB;
+          const float* xg = reinterpret_cast<const float*>(sb + SG::kW + SG::kS + SG::kZ + SG::kB);
+          const float xc[2] = {xg[(2 * t) * 4 + q], xg[(2 * t + 1) * 4 + q]};
+#pragma unroll
+          for (int p = 0; p < NP; ++p)
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+              const float v = f16_group(tmp[p][0][0][r] + tmp[p][0][1][r], xc[r & 1], r >> 1, zbias);
+              acc[p][0][r] = __fmaf_rn(v, sc[p][q][r >> 1], acc[p][0][r]);
+              if (!AWQ) acc[p][0][r] = __fmaf_rn(zz[p][q][r >> 1], xc[r & 1], acc[p][0][r]);
+              tmp[p][0][0][r] = tmp[p][0][1][r] = 0.f;
+            }
+        } else if ((b + 1) % GSB == 0) {  // group end
           const int q = b / GSB;
 #pragma unroll
           for (int n = 0; n < NT; ++n)
@@ -430,9 +515,11 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
           if (col >= it.nrows || m >= a.M) continue;
           const size_t o = (size_t)(it.row0 + col) * a.ldo + m;
           float v = acc[0][n][r];
+          if constexpr (XH) v *= bs[r & 1];  // undo the row's 2^-e
           if (!isfinite(v)) v = 0.f;  // non-finite -> 0, as every reference GEMV does
           if (MODE == MODE_GATE_UP) {
             float uu = acc[NP - 1][n][r];
+            if constexpr (XH) uu *= bs[r & 1];
             if (!isfinite(uu)) uu = 0.f;
             reinterpret_cast<__nv_bfloat16*>(a.out)[o] = __float2bfloat16_rn(silu_mul(v, uu));
           } else {
@@ -458,12 +545,17 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
 // gate and up tiles of one 16-row tile (MODE_GATE_UP), or two adjacent 16-row
 // tiles of one projection (MODE_PLAIN_F32), so the activation copies, the
 // x-sum MMAs and the loop's bookkeeping are shared by 2 KB of weights a step.
-template <int MODE, int GSB, bool AWQ>
+// XH (gate/up only): fp16 activations scaled per row (launch_prep_xh), fp16
+// weights from raw_word_f16, the group sums of the activations copied in with
+// each step instead of the all-ones MMA, and the row scales applied before
+// the SiLU*mul epilogue.
+template <int MODE, int GSB, bool AWQ, bool XH>
 __global__ void __launch_bounds__(kWarps * 32) k_int4_mma_p(GemmArgs a) {
   constexpr int NP = 2;
   constexpr bool PAIR = MODE != MODE_GATE_UP;
   constexpr int NG = GSB == 4 ? 1 : (GSB == 2 ? 2 : 4);  // groups per step
-  using SG = WStage<NP, 1, AWQ>;
+  static_assert(!XH || MODE == MODE_GATE_UP, "fp16 activations: gate/up only");
+  using SG = WStage<NP, 1, AWQ, XH>;
   extern __shared__ __align__(128) unsigned char wsm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
@@ -481,6 +573,8 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma_p(GemmArgs a) {
 
   // the next unit the copies will enter
   int pu = 0, prow = 0;
+  int pxrow = 0;                 // XH: the row of column lane & 7 (its group sums)
+  float pbs0 = 1.f, pbs1 = 1.f;  // XH: the row scales of columns 2t, 2t + 1
   WorkItem pit{};
   const uint4* pq[NP];
   const __half* ps[NP];
@@ -493,6 +587,14 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma_p(GemmArgs a) {
       pit = a.work[pu / Mt];
       const int pos = pit.row0 + (g < pit.nrows ? g : 0);
       prow = a.gather ? a.gather[pos] / a.kk : pos;
+      if constexpr (XH) {
+        const int cx = lane & 7, c0 = 2 * t, c1 = 2 * t + 1;
+        const int px = pit.row0 + (cx < pit.nrows ? cx : 0);
+        const int p0 = pit.row0 + (c0 < pit.nrows ? c0 : 0), p1 = pit.row0 + (c1 < pit.nrows ? c1 : 0);
+        pxrow = a.gather ? a.gather[px] / a.kk : px;
+        pbs0 = a.bscale[a.gather ? a.gather[p0] / a.kk : p0];
+        pbs1 = a.bscale[a.gather ? a.gather[p1] / a.kk : p1];
+      }
       const ExpertDev& ex = a.experts[pit.expert];
       const ProjDev& P0 = MODE == MODE_GATE_UP ? ex.gate : pick(ex, a.proj);
       const ProjDev& P1 = MODE == MODE_GATE_UP ? ex.up : P0;
@@ -510,9 +612,11 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma_p(GemmArgs a) {
   const unsigned char* ssrc[NP];
   const unsigned char* zsrc[NP];
   const unsigned char* bsrc = nullptr;
-  bool bval = false;
+  const float* xsrc = nullptr;  // XH, lanes < 8: the group sums of column `lane`
+  bool bval = false, xval = false;
   int is = 0, entered = 0;
   int n_row0 = 0, n_nrows = 0, n_rt = 0;  // the unit last entered
+  float n_bs0 = 1.f, n_bs1 = 1.f;
   auto enter = [&]() {
     const int rt = pu % Mt;
 #pragma unroll
@@ -526,6 +630,12 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma_p(GemmArgs a) {
     }
     bval = g < pit.nrows;
     bsrc = reinterpret_cast<const unsigned char*>(a.B) + ((size_t)prow * a.ldb + 8 * t) * 2;
+    if constexpr (XH) {
+      xval = lane < 8 && lane < pit.nrows;
+      xsrc = a.bsum + (size_t)pxrow * a.ng;
+      n_bs0 = pbs0;
+      n_bs1 = pbs1;
+    }
     n_row0 = pit.row0;
     n_nrows = pit.nrows;
     n_rt = rt;
@@ -553,6 +663,10 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma_p(GemmArgs a) {
         cp_async16(sb + SG::kW + SG::kS + SG::kZ + b * 512 + lane * 16, bsrc + b * 64);
     }
     bsrc += 256;
+    if constexpr (XH) {
+      if (xval) cp_async_small<NG>(sb + SG::kW + SG::kS + SG::kZ + SG::kB + lane * 16, xsrc);
+      xsrc += NG;
+    }
   };
   bool copying = true;
   // one step of copies; enters the prefetched unit when the current one is done
@@ -590,6 +704,7 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma_p(GemmArgs a) {
 
   const uint32_t ones[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};
   const float bias = AWQ ? (float)(128 + a.zp) : 128.f;
+  const float zbias = AWQ ? (float)a.zp : 0.f;  // XH: the zero point removed at group ends
   float acc[NP][4], tmp[NP][2][4], xs[2][4];  // tmp, xs: a group's partial sums (started fresh)
 #pragma unroll
   for (int p = 0; p < NP; ++p)
@@ -597,6 +712,7 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma_p(GemmArgs a) {
     for (int r = 0; r < 4; ++r) acc[p][r] = 0.f;
 
   int c_row0 = n_row0, c_nrows = n_nrows, c_rt = n_rt, done = 0, cs = 0;
+  float c_bs0 = n_bs0, c_bs1 = n_bs1;
   for (int i = 0;; ++i) {
     issue_step((i + kStagesW - 1) % kStagesW);
     cp_async_commit();
@@ -633,36 +749,60 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma_p(GemmArgs a) {
       const bool fresh = b % GSB == 0;  // first block of a group: new partial sums
 #pragma unroll
       for (int kt = 0; kt < 2; ++kt) {
-        if (fresh)
-          mma_bf16_z(xs[kt], ones, kt ? bv[b].z : bv[b].x, kt ? bv[b].w : bv[b].y);
-        else
-          mma_bf16(xs[kt], ones, kt ? bv[b].z : bv[b].x, kt ? bv[b].w : bv[b].y);
+        if constexpr (!XH) {
+          if (fresh)
+            mma_bf16_z(xs[kt], ones, kt ? bv[b].z : bv[b].x, kt ? bv[b].w : bv[b].y);
+          else
+            mma_bf16(xs[kt], ones, kt ? bv[b].z : bv[b].x, kt ? bv[b].w : bv[b].y);
+        }
 #pragma unroll
         for (int p = 0; p < NP; ++p) {
           const uint4& q4 = wq[p][b >> 1];
           const int wi = (b & 1) * 2 + kt;
           const uint32_t wd = wi == 0 ? q4.x : wi == 1 ? q4.y : wi == 2 ? q4.z : q4.w;
           uint32_t af[4];
-          raw_word(wd, af);
-          if (fresh)
-            mma_bf16_z(tmp[p][kt], af, kt ? bv[b].z : bv[b].x, kt ? bv[b].w : bv[b].y);
-          else
-            mma_bf16(tmp[p][kt], af, kt ? bv[b].z : bv[b].x, kt ? bv[b].w : bv[b].y);
+          if constexpr (XH) {
+            raw_word_f16(wd, af);
+            if (fresh)
+              mma_f16_z(tmp[p][kt], af, kt ? bv[b].z : bv[b].x, kt ? bv[b].w : bv[b].y);
+            else
+              mma_f16(tmp[p][kt], af, kt ? bv[b].z : bv[b].x, kt ? bv[b].w : bv[b].y);
+          } else {
+            raw_word(wd, af);
+            if (fresh)
+              mma_bf16_z(tmp[p][kt], af, kt ? bv[b].z : bv[b].x, kt ? bv[b].w : bv[b].y);
+            else
+              mma_bf16(tmp[p][kt], af, kt ? bv[b].z : bv[b].x, kt ? bv[b].w : bv[b].y);
+          }
         }
       }
       if ((b + 1) % GSB == 0) {  // group end
         const int q = b / GSB;
+        if constexpr (XH) {
+          // the group sums of columns 2t and 2t+1 (copied with the step)
+          const float* xg = reinterpret_cast<const float*>(sb + SG::kW + SG::kS + SG::kZ + SG::kB);
+          const float xc[2] = {xg[(2 * t) * 4 + q], xg[(2 * t + 1) * 4 + q]};
 #pragma unroll
-        for (int r = 0; r < 4; ++r) xs[0][r] += xs[1][r];
+          for (int p = 0; p < NP; ++p)
 #pragma unroll
-        for (int p = 0; p < NP; ++p)
+            for (int r = 0; r < 4; ++r) {
+              const float v = f16_group(tmp[p][0][r] + tmp[p][1][r], xc[r & 1], r >> 1, zbias);
+              acc[p][r] = __fmaf_rn(v, sc[p][q][r >> 1], acc[p][r]);
+              if (!AWQ) acc[p][r] = __fmaf_rn(zz[p][q][r >> 1], xc[r & 1], acc[p][r]);
+            }
+        } else {
 #pragma unroll
-          for (int r = 0; r < 4; ++r) {
-            const float pr = tmp[p][0][r] + tmp[p][1][r];
-            const float v = __fmaf_rn(-bias, xs[0][r], pr);  // sum x*(q - zp)
-            acc[p][r] = __fmaf_rn(v, sc[p][q][r >> 1], acc[p][r]);
-            if (!AWQ) acc[p][r] = __fmaf_rn(zz[p][q][r >> 1], xs[0][r], acc[p][r]);
-          }
+          for (int r = 0; r < 4; ++r) xs[0][r] += xs[1][r];
+#pragma unroll
+          for (int p = 0; p < NP; ++p)
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+              const float pr = tmp[p][0][r] + tmp[p][1][r];
+              const float v = __fmaf_rn(-bias, xs[0][r], pr);  // sum x*(q - zp)
+              acc[p][r] = __fmaf_rn(v, sc[p][q][r >> 1], acc[p][r]);
+              if (!AWQ) acc[p][r] = __fmaf_rn(zz[p][q][r >> 1], xs[0][r], acc[p][r]);
+            }
+        }
       }
     }
 
@@ -678,9 +818,11 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma_p(GemmArgs a) {
         if (col < c_nrows && m < a.M) {
           const size_t o = (size_t)(c_row0 + col) * a.ldo + m;
           float v = acc[p][r];
+          if constexpr (XH) v *= (r & 1) ? c_bs1 : c_bs0;  // undo the row's 2^-e
           if (!isfinite(v)) v = 0.f;  // non-finite -> 0, as every reference GEMV does
           if (MODE == MODE_GATE_UP) {
             float uu = acc[1][r];
+            if constexpr (XH) uu *= (r & 1) ? c_bs1 : c_bs0;
             if (!isfinite(uu)) uu = 0.f;
             reinterpret_cast<__nv_bfloat16*>(a.out)[o] = __float2bfloat16_rn(silu_mul(v, uu));
           } else {
@@ -700,91 +842,100 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma_p(GemmArgs a) {
     c_row0 = n_row0;
     c_nrows = n_nrows;
     c_rt = n_rt;
+    c_bs0 = n_bs0;
+    c_bs1 = n_bs1;
   }
   cp_async_wait<0>();
 }
 
-template <int MODE, int NT, int GSB, bool AWQ>
+template <int MODE, int NT, int GSB, bool AWQ, bool XH>
 static void launch_mma_k(const GemmArgs& a, dim3 grid, int ks, cudaStream_t st) {
   constexpr int NP = MODE == MODE_GATE_UP ? 2 : 1;
-  const size_t smem = (size_t)kWarps * kStagesW * WStage<NP, NT, AWQ>::kBytes;
+  const size_t smem = (size_t)kWarps * kStagesW * WStage<NP, NT, AWQ, XH>::kBytes;
   static bool attr = false;  // per template instance
   if (!attr) {
-    cudaFuncSetAttribute(k_int4_mma<MODE, NT, GSB, AWQ>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(k_int4_mma<MODE, NT, GSB, AWQ, XH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem);
     attr = true;
   }
-  launch_pdl(k_int4_mma<MODE, NT, GSB, AWQ>, grid, dim3(kWarps * 32), smem, st, a, ks);
+  launch_pdl(k_int4_mma<MODE, NT, GSB, AWQ, XH>, grid, dim3(kWarps * 32), smem, st, a, ks);
 }
 
 // Persistent grid: as many 4-warp CTAs as fit on the SMs at once.
-template <int MODE, int GSB, bool AWQ>
+template <int MODE, int GSB, bool AWQ, bool XH>
 static int mma_p_grid() {
   constexpr int NP = 2;  // two weight streams per unit in both modes
-  const size_t smem = (size_t)kWarps * kStagesW * WStage<NP, 1, AWQ>::kBytes;
+  const size_t smem = (size_t)kWarps * kStagesW * WStage<NP, 1, AWQ, XH>::kBytes;
   static int grid = 0;  // per template instance (one device per process in practice)
   if (!grid) {
-    cudaFuncSetAttribute(k_int4_mma_p<MODE, GSB, AWQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(k_int4_mma_p<MODE, GSB, AWQ, XH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     int per_sm = 0, dev = 0, sms = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_int4_mma_p<MODE, GSB, AWQ>, kWarps * 32, smem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_int4_mma_p<MODE, GSB, AWQ, XH>, kWarps * 32, smem);
     grid = std::max(1, per_sm) * std::max(1, sms);
   }
   return grid;
 }
 
-template <int MODE, int GSB, bool AWQ>
+template <int MODE, int GSB, bool AWQ, bool XH>
 static void launch_mma_pk(const GemmArgs& a, cudaStream_t st) {
   constexpr int NP = 2;
-  const size_t smem = (size_t)kWarps * kStagesW * WStage<NP, 1, AWQ>::kBytes;
-  launch_pdl(k_int4_mma_p<MODE, GSB, AWQ>, dim3(mma_p_grid<MODE, GSB, AWQ>()), dim3(kWarps * 32), smem, st, a);
+  const size_t smem = (size_t)kWarps * kStagesW * WStage<NP, 1, AWQ, XH>::kBytes;
+  launch_pdl(k_int4_mma_p<MODE, GSB, AWQ, XH>, dim3(mma_p_grid<MODE, GSB, AWQ, XH>()), dim3(kWarps * 32), smem, st,
+             a);
 }
 
-template <int MODE, bool AWQ>
+template <int MODE, bool AWQ, bool XH>
 static int mma_p_grid_gs(int gs) {
-  return gs == 32 ? mma_p_grid<MODE, 1, AWQ>() : (gs == 64 ? mma_p_grid<MODE, 2, AWQ>() : mma_p_grid<MODE, 4, AWQ>());
+  return gs == 32 ? mma_p_grid<MODE, 1, AWQ, XH>()
+                  : (gs == 64 ? mma_p_grid<MODE, 2, AWQ, XH>() : mma_p_grid<MODE, 4, AWQ, XH>());
 }
-static long mma_p_resident_warps(bool gate_up, int gs, int awq) {
-  const int grid = gate_up ? (awq ? mma_p_grid_gs<MODE_GATE_UP, true>(gs) : mma_p_grid_gs<MODE_GATE_UP, false>(gs))
-                           : (awq ? mma_p_grid_gs<MODE_PLAIN_F32, true>(gs) : mma_p_grid_gs<MODE_PLAIN_F32, false>(gs));
+static long mma_p_resident_warps(bool gate_up, int gs, int awq, bool xh) {
+  int grid;
+  if (gate_up && xh)
+    grid = awq ? mma_p_grid_gs<MODE_GATE_UP, true, true>(gs) : mma_p_grid_gs<MODE_GATE_UP, false, true>(gs);
+  else if (gate_up)
+    grid = awq ? mma_p_grid_gs<MODE_GATE_UP, true, false>(gs) : mma_p_grid_gs<MODE_GATE_UP, false, false>(gs);
+  else
+    grid = awq ? mma_p_grid_gs<MODE_PLAIN_F32, true, false>(gs) : mma_p_grid_gs<MODE_PLAIN_F32, false, false>(gs);
   return (long)grid * kWarps;
 }
 
-template <int MODE>
+template <int MODE, bool XH>
 static void launch_mma_p(const GemmArgs& a, int awq, cudaStream_t st) {
   if (awq) {
     switch (a.gs) {
-      case 32: launch_mma_pk<MODE, 1, true>(a, st); break;
-      case 64: launch_mma_pk<MODE, 2, true>(a, st); break;
-      default: launch_mma_pk<MODE, 4, true>(a, st); break;
+      case 32: launch_mma_pk<MODE, 1, true, XH>(a, st); break;
+      case 64: launch_mma_pk<MODE, 2, true, XH>(a, st); break;
+      default: launch_mma_pk<MODE, 4, true, XH>(a, st); break;
     }
   } else {
     switch (a.gs) {
-      case 32: launch_mma_pk<MODE, 1, false>(a, st); break;
-      case 64: launch_mma_pk<MODE, 2, false>(a, st); break;
-      default: launch_mma_pk<MODE, 4, false>(a, st); break;
+      case 32: launch_mma_pk<MODE, 1, false, XH>(a, st); break;
+      case 64: launch_mma_pk<MODE, 2, false, XH>(a, st); break;
+      default: launch_mma_pk<MODE, 4, false, XH>(a, st); break;
     }
   }
 }
 
-template <int MODE, int NT, bool AWQ>
+template <int MODE, int NT, bool AWQ, bool XH>
 static void launch_mma_gs(const GemmArgs& a, int max_work, int ks, cudaStream_t st) {
   const int Mt = (a.M + 15) / 16;
   const dim3 grid((Mt * ks + kWarps - 1) / kWarps, max_work);
   switch (a.gs) {
-    case 32: launch_mma_k<MODE, NT, 1, AWQ>(a, grid, ks, st); break;
-    case 64: launch_mma_k<MODE, NT, 2, AWQ>(a, grid, ks, st); break;
-    default: launch_mma_k<MODE, NT, 4, AWQ>(a, grid, ks, st); break;
+    case 32: launch_mma_k<MODE, NT, 1, AWQ, XH>(a, grid, ks, st); break;
+    case 64: launch_mma_k<MODE, NT, 2, AWQ, XH>(a, grid, ks, st); break;
+    default: launch_mma_k<MODE, NT, 4, AWQ, XH>(a, grid, ks, st); break;
   }
 }
 
 // Items of at most 8 rows (one mma N tile): larger items take the tcgen05
 // kernel (int4_umma.cu) or the CUDA-core kernel.
-template <int MODE>
+template <int MODE, bool XH>
 static void launch_mma(const GemmArgs& a, int max_work, int ks, int awq, cudaStream_t st) {
-  if (awq) launch_mma_gs<MODE, 1, true>(a, max_work, ks, st);
-  else launch_mma_gs<MODE, 1, false>(a, max_work, ks, st);
+  if (awq) launch_mma_gs<MODE, 1, true, XH>(a, max_work, ks, st);
+  else launch_mma_gs<MODE, 1, false, XH>(a, max_work, ks, st);
 }
 
 // ------------------------------------------------------ CUDA-core fp32 GEMV
@@ -1045,6 +1196,34 @@ __global__ void __launch_bounds__(256) k_combine(const float* __restrict__ d, co
   }
 }
 
+// ------------------------------------------- fp16 activation rows (decode)
+
+// One warp per row (launch_prep_xh): prep_xh_row (common.cuh) on row w, or on
+// row rows_of[w] for w < *n_valid.
+__global__ void __launch_bounds__(256) k_prep_xh(const uint4* __restrict__ X, int R, int H, int gs,
+                                                 const int* __restrict__ rows_of, const int* __restrict__ n_valid,
+                                                 uint4* __restrict__ Xh, float* __restrict__ xsum,
+                                                 float* __restrict__ xscale) {
+  grid_dep_wait();
+  grid_dep_release();
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (w >= R) return;
+  int r = w;
+  if (rows_of) {
+    if (w >= *n_valid) return;
+    r = rows_of[w];
+  }
+  prep_xh_row<16, true>(X + (size_t)r * (H / 8), r, H, gs, Xh, xsum, xscale, lane);
+}
+
+cudaError_t launch_prep_xh(const void* X, int R, int H, int gs, const int* rows_of, const int* n_valid, void* Xh,
+                           float* xsum, float* xscale, cudaStream_t st) {
+  if (R <= 0) return cudaSuccess;
+  if (H % 128 || (gs != 32 && gs != 64 && gs != 128)) return cudaErrorInvalidValue;
+  return launch_pdl(k_prep_xh, dim3((R + 7) / 8), dim3(256), 0, st, reinterpret_cast<const uint4*>(X), R, H, gs,
+                    rows_of, n_valid, reinterpret_cast<uint4*>(Xh), xsum, xscale);
+}
+
 // ---------------------------------------------------------------- quantize
 
 // quant_awq_sym: scale = max(absmax / 7, 1e-8); optionally rounded to bf16;
@@ -1149,18 +1328,24 @@ cudaError_t launch_gemm(int mode, int path, const GemmArgs& a, int max_work, int
     // decode-size items: the persistent kernel when the expected units (items ~
     // min(max_work, distinct experts) x row tiles) keep 1.5x its resident warps
     // busy; below that the K-split launch has more warps in flight
+    // the fp16 activation path: gate/up with launch_prep_xh's rows and sums
+    const bool xh = mode == MODE_GATE_UP && a.bsum != nullptr;
     if (ntiles <= 1 && a.ctr && nsteps >= kStagesW - 1 &&
-        2L * units_est >= 3L * mma_p_resident_warps(mode == MODE_GATE_UP, a.gs, awq)) {
-      if (mode == MODE_GATE_UP)
-        launch_mma_p<MODE_GATE_UP>(a, awq, st);
+        2L * units_est >= 3L * mma_p_resident_warps(mode == MODE_GATE_UP, a.gs, awq, xh)) {
+      if (xh)
+        launch_mma_p<MODE_GATE_UP, true>(a, awq, st);
+      else if (mode == MODE_GATE_UP)
+        launch_mma_p<MODE_GATE_UP, false>(a, awq, st);
       else
-        launch_mma_p<MODE_PLAIN_F32>(a, awq, st);
+        launch_mma_p<MODE_PLAIN_F32, false>(a, awq, st);
     } else if (ntiles > 1) {
       return cudaErrorInvalidValue;  // items above 8 rows: not this kernel's
+    } else if (xh) {
+      launch_mma<MODE_GATE_UP, true>(a, gy, ks, awq, st);
     } else if (mode == MODE_GATE_UP) {
-      launch_mma<MODE_GATE_UP>(a, gy, ks, awq, st);
+      launch_mma<MODE_GATE_UP, false>(a, gy, ks, awq, st);
     } else {
-      launch_mma<MODE_PLAIN_F32>(a, gy, ks, awq, st);
+      launch_mma<MODE_PLAIN_F32, false>(a, gy, ks, awq, st);
     }
   } else if (path == 1) {
     if (mode == MODE_GATE_UP)

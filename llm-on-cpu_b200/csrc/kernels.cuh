@@ -21,6 +21,13 @@ struct TopkArgs {
   float* shared_w = nullptr;  // [T] per-token shared weights (expert-parallel source; may be null)
   int* ids;              // [T,kk]
   float* weights;        // [T,kk]
+  // the token's fp16 row for the decode gate/up GEMM, made by the same warp
+  // (prep_xh_row; xh null: none)
+  const void* x = nullptr;  // bf16 [T][H]
+  int H = 0, gs = 0;
+  void* xh = nullptr;
+  float* xsum = nullptr;
+  float* xscale = nullptr;
 };
 
 struct PermArgs {
@@ -49,8 +56,17 @@ constexpr int kPermThreads = 1024;
 constexpr int kPermWarps = kPermThreads / 32;
 constexpr int kMaxExpPerm = 512;  // experts (incl. shared) the permutation CTA handles
 
+// The decode gate/up GEMM's fp16 rows (prep_xh_row) of the router's tokens,
+// made by the decode router (T <= kRouterSmallMaxT) from its copy of them.
+struct XhOut {
+  void* xh = nullptr;  // null: none
+  float* xsum = nullptr;
+  float* xscale = nullptr;
+  int gs = 0;
+};
+constexpr int kRouterSmallMaxT = 8;
 cudaError_t launch_router_logits(const void* X, bool x_is_f32, const uint16_t* Wr, int T, int E,
-                                 int H, float* logits, cudaStream_t st);
+                                 int H, float* logits, cudaStream_t st, const XhOut& xo = XhOut{});
 cudaError_t launch_topk(const TopkArgs& a, cudaStream_t st);
 cudaError_t launch_permute(const PermArgs& a, cudaStream_t st);
 // top-k and permutation in one CTA (decode-size T; pa.ids must be ta.ids, or,
@@ -138,7 +154,21 @@ struct GemmArgs {
   const void* wmaps;      // tcgen05 path: per-expert TMA maps of the weights (build_umma_weight_maps)
   int* ctr;               // persistent decode kernel: unit counter, zeroed by the permutation (or null)
   int keep_nonfinite;     // cc kernel, PLAIN_F32: store non-finite sums as they are (argmax input)
+  // fp16 activation form of the decode gate/up GEMM (bsum != null): B holds
+  // the rows as fp16 scaled by 2^-e per row, bsum [row][ng] the per-group sums
+  // of those fp16 values, bscale [row] = 2^e (launch_prep_xh)
+  const float* bsum = nullptr;
+  const float* bscale = nullptr;
 };
+
+// fp16 activation rows for the decode gate/up GEMM.  Row r (r < R, or, with
+// rows_of, row rows_of[p] for p < min(R, *n_valid)) of X (bf16 [.][H]):
+// Xh = x * 2^-e rounded to fp16, e chosen so the row's largest |x| lands in
+// [2^14, 2^15) (exact for every value within 2^28 of the largest; e = 0 for an
+// all-zero or non-finite row), xsum [.][H/gs] the fp32 sums of each group of
+// Xh (a fixed order), xscale = 2^e.  H % 128 == 0, gs in {32, 64, 128}.
+cudaError_t launch_prep_xh(const void* X, int R, int H, int gs, const int* rows_of, const int* n_valid, void* Xh,
+                           float* xsum, float* xscale, cudaStream_t st);
 
 // Argmax over y[M] (hal::gemm_int4_argmax semantics: non-finite -> -1e30,
 // the first of equal maxima): *key = max over rows of the key of (y[m], m),

@@ -166,17 +166,80 @@ struct RouterTile {
       (size_t)4 * (2 * kStage > kOut * 33 ? 2 * kStage : kOut * 33);  // stages, reused for the fold
 };
 
+// With xo.xh, the CTAs of the first expert tile also make their tokens' fp16
+// rows for the decode gate/up GEMM (prep_xh_row's format): each warp first
+// reads its token rows' largest exponent, then converts every staged chunk.
 template <int TT, int EE, int WT, int WE>
 __global__ void __launch_bounds__(RouterTile<TT, EE, WT, WE>::kThreads, 1)
     k_router_tiled(const __nv_bfloat16* __restrict__ X, const uint16_t* __restrict__ Wr, int T, int E, int H,
-                   float* __restrict__ logits) {
+                   float* __restrict__ logits, XhOut xo) {
   using RT = RouterTile<TT, EE, WT, WE>;
+  constexpr int kWarpsR = RT::kThreads / 32;
+  constexpr int kXRowsPerWarp = (RT::kRowsX + kWarpsR - 1) / kWarpsR;
   extern __shared__ float rsm[];
   grid_dep_wait();
   grid_dep_release();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tg = warp % WT, eg = warp / WT;
   const int t0 = blockIdx.y * RT::kRowsX, e0 = blockIdx.x * RT::kRowsW;
+  // fp16 rows: warp w owns token rows w, w + kWarpsR, ... of the tile
+  const bool xh = xo.xh != nullptr && blockIdx.x == 0;
+  float xdown[kXRowsPerWarp];
+  if (xh) {
+#pragma unroll
+    for (int j = 0; j < kXRowsPerWarp; ++j) {
+      const int row = warp + j * kWarpsR, t = t0 + row;
+      uint32_t mexp = 0;
+      if (row < RT::kRowsX && t < T) {
+        const uint4* src = reinterpret_cast<const uint4*>(X + (size_t)t * H);
+        for (int i0 = 0; i0 < H / 8; i0 += 8 * 32) {
+          uint4 v[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const int i = i0 + lane + 32 * q;
+            v[q] = i < H / 8 ? __ldg(src + i) : make_uint4(0, 0, 0, 0);
+          }
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            mexp = bf16x2_max_exp(v[q].x, mexp);
+            mexp = bf16x2_max_exp(v[q].y, mexp);
+            mexp = bf16x2_max_exp(v[q].z, mexp);
+            mexp = bf16x2_max_exp(v[q].w, mexp);
+          }
+        }
+      }
+      mexp = __reduce_max_sync(0xffffffffu, mexp);
+      const int e = mexp == 0 ? 0 : max(-100, (int)mexp - 141);
+      xdown[j] = __int_as_float((127 - e) << 23);
+      if (lane == 0 && row < RT::kRowsX && t < T) xo.xscale[t] = __int_as_float((127 + e) << 23);
+    }
+  }
+  // convert a parked stage's token rows (fp32 copies of the bf16 values): lane
+  // L takes 8 consecutive values of each of the warp's rows
+  auto emit_xh = [&](int s, int kc) {
+#pragma unroll
+    for (int j = 0; j < kXRowsPerWarp; ++j) {
+      const int row = warp + j * kWarpsR, t = t0 + row;
+      if (row >= RT::kRowsX) continue;  // uniform over the warp
+      const float* xs = rsm + (size_t)s * RT::kStage + (size_t)row * kRouterKC + 8 * lane;
+      uint32_t o[4];
+      float sum = 0.f;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const __half2 h2 = __floats2half2_rn(xs[2 * q] * xdown[j], xs[2 * q + 1] * xdown[j]);
+        const float2 f2 = __half22float2(h2);
+        sum += f2.x;
+        sum += f2.y;
+        o[q] = *reinterpret_cast<const uint32_t*>(&h2);
+      }
+      const int lpg = xo.gs / 8;
+      for (int off = 1; off < lpg; off <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+      if (t < T) {
+        reinterpret_cast<uint4*>(xo.xh)[((size_t)t * H + kc + 8 * lane) / 8] = make_uint4(o[0], o[1], o[2], o[3]);
+        if (lane % lpg == 0) xo.xsum[(size_t)t * (H / xo.gs) + (kc + 8 * lane) / xo.gs] = sum;
+      }
+    }
+  };
 
   // staging piece q: row q / 32 (X rows first, then W_r rows), k offset 8 (q % 32)
   const uint4* src[RT::kPer];
@@ -224,6 +287,7 @@ __global__ void __launch_bounds__(RouterTile<TT, EE, WT, WE>::kThreads, 1)
   for (int c = 0; c < nk; ++c) {
     const int s = c & 1;
     if (c + 1 < nk) fetch((c + 1) * kRouterKC);
+    if (xh) emit_xh(s, c * kRouterKC);
     const float* xs = rsm + (size_t)s * RT::kStage + (tg * TT) * kRouterKC + lane;
     const float* ws = rsm + (size_t)s * RT::kStage + (RT::kRowsX + eg * EE) * kRouterKC + lane;
 #pragma unroll 2
@@ -268,9 +332,93 @@ __global__ void __launch_bounds__(RouterTile<TT, EE, WT, WE>::kThreads, 1)
   }
 }
 
+// ------------------------------------------- router GEMV, decode (T <= 8)
+//
+// Decode batches read the whole router matrix for a handful of tokens, so the
+// work is one pass over W_r spread over as many SMs as possible.  A CTA takes
+// EPC expert rows and every token: it copies those rows and the T token rows
+// (bf16) into shared memory with one 16-byte load per thread and piece, then
+// each (token, expert) dot is one warp whose lane c runs the reference's FMA
+// chain c (k = c mod 32, ascending; fp32 of the bf16 values), and the chains
+// are folded with shuffles in the reference's tree order:
+// a[i] = (c[i]+c[8+i]) + (c[16+i]+c[24+i]); b[i] = a[i] + a[4+i];
+// r = (b0+b1) + (b2+b3).  Requires H % 256 == 0 (no unfused tail).
+constexpr int kRouterSmallThreads = 256;
+// With xo.xh, CTA t < T also makes token t's fp16 row from its shared copy.
+template <int EPC>
+__global__ void __launch_bounds__(kRouterSmallThreads) k_router_small(const __nv_bfloat16* __restrict__ X,
+                                                                      const uint16_t* __restrict__ Wr, int T,
+                                                                      int E, int H, float* __restrict__ logits,
+                                                                      XhOut xo) {
+  extern __shared__ __align__(16) uint16_t rsm16[];  // [EPC + T][H] bf16
+  grid_dep_wait();
+  grid_dep_release();
+  const int e0 = blockIdx.x * EPC;
+  const int nw = min(EPC, E - e0);
+  const int n8 = H / 8;
+  // W_r rows e0 .. e0 + nw - 1, then the T token rows: eight 16-byte pieces
+  // per thread requested at once
+  const int total = (nw + T) * n8;
+  for (int q0 = 0; q0 < total; q0 += 8 * kRouterSmallThreads) {
+    uint4 v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int q = q0 + threadIdx.x + j * kRouterSmallThreads;
+      if (q < total) {
+        const int row = q / n8, c = q % n8;
+        const uint16_t* src = row < nw ? Wr + (size_t)(e0 + row) * H
+                                       : reinterpret_cast<const uint16_t*>(X) + (size_t)(row - nw) * H;
+        v[j] = __ldg(reinterpret_cast<const uint4*>(src) + c);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int q = q0 + threadIdx.x + j * kRouterSmallThreads;
+      if (q < total) reinterpret_cast<uint4*>(rsm16)[q] = v[j];
+    }
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int pr = warp; pr < nw * T; pr += kRouterSmallThreads / 32) {
+    const int e = pr % nw, t = pr / nw;
+    const uint16_t* wrow = rsm16 + (size_t)e * H;
+    const uint16_t* xrow = rsm16 + (size_t)(nw + t) * H;
+    float c = 0.f;
+    for (int k = lane; k < H; k += 32) c = __fmaf_rn(bf16_bits_to_f32(xrow[k]), bf16_bits_to_f32(wrow[k]), c);
+    const float c8 = __shfl_down_sync(0xffffffffu, c, 8), c16 = __shfl_down_sync(0xffffffffu, c, 16),
+                c24 = __shfl_down_sync(0xffffffffu, c, 24);
+    const float av = (c + c8) + (c16 + c24);                       // a[lane], lanes 0..7
+    const float bv = av + __shfl_down_sync(0xffffffffu, av, 4);    // b[lane], lanes 0..3
+    const float b1 = __shfl_down_sync(0xffffffffu, bv, 1), b2 = __shfl_down_sync(0xffffffffu, bv, 2),
+                b3 = __shfl_down_sync(0xffffffffu, bv, 3);
+    if (lane == 0) {
+      const float r = (bv + b1) + (b2 + b3);
+      logits[(size_t)t * E + e0 + e] = isfinite(r) ? r : 0.f;
+    }
+  }
+  if (xo.xh && (int)blockIdx.x < T && warp == kRouterSmallThreads / 32 - 1)
+    prep_xh_row<4, false>(reinterpret_cast<const uint4*>(rsm16 + (size_t)(nw + blockIdx.x) * H), blockIdx.x, H,
+                          xo.gs, static_cast<uint4*>(xo.xh), xo.xsum, xo.xscale, lane);
+}
+
+template <int EPC>
+static cudaError_t launch_router_small(const __nv_bfloat16* X, const uint16_t* Wr, int T, int E, int H, float* logits,
+                                       cudaStream_t st, const XhOut& xo) {
+  const size_t smem = (size_t)(EPC + T) * H * 2;
+  if (smem > 227 * 1024) return cudaErrorInvalidValue;
+  if (smem > 48 * 1024) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(k_router_small<EPC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  if ((E + EPC - 1) / EPC < T && xo.xh) return cudaErrorInvalidValue;  // a CTA per token row
+  return launch_pdl(k_router_small<EPC>, dim3((E + EPC - 1) / EPC), dim3(kRouterSmallThreads), smem, st, X, Wr, T,
+                    E, H, logits, xo);
+}
+
 template <int TT, int EE, int WT, int WE>
 static cudaError_t launch_router_tiled(const __nv_bfloat16* X, const uint16_t* Wr, int T, int E, int H,
-                                       float* logits, cudaStream_t st) {
+                                       float* logits, cudaStream_t st, const XhOut& xo = XhOut{}) {
   using RT = RouterTile<TT, EE, WT, WE>;
   static bool attr = false;
   if (!attr) {
@@ -279,7 +427,8 @@ static cudaError_t launch_router_tiled(const __nv_bfloat16* X, const uint16_t* W
     attr = true;
   }
   const dim3 grid((E + RT::kRowsW - 1) / RT::kRowsW, (T + RT::kRowsX - 1) / RT::kRowsX);
-  return launch_pdl(k_router_tiled<TT, EE, WT, WE>, grid, dim3(RT::kThreads), RT::kSmem, st, X, Wr, T, E, H, logits);
+  return launch_pdl(k_router_tiled<TT, EE, WT, WE>, grid, dim3(RT::kThreads), RT::kSmem, st, X, Wr, T, E, H, logits,
+                    xo);
 }
 
 // --------------------------------------------------------------- top-k
@@ -435,6 +584,7 @@ __device__ __forceinline__ void topk_token(const TopkArgs& a, int t, int lane) {
   else topk_token_q<16>(a, t, lane);
 }
 
+
 // One warp per token.
 __global__ void __launch_bounds__(256) k_topk(TopkArgs a) {
   grid_dep_wait();
@@ -443,6 +593,9 @@ __global__ void __launch_bounds__(256) k_topk(TopkArgs a) {
   const int t = blockIdx.x * 8 + warp;
   if (t >= a.T) return;
   topk_token(a, t, lane);
+  if (a.xh)
+    prep_xh_row<16, true>(static_cast<const uint4*>(a.x) + (size_t)t * (a.H / 8), t, a.H, a.gs,
+                          static_cast<uint4*>(a.xh), a.xsum, a.xscale, lane);
 }
 
 // ----------------------------------------------------------- permutation
@@ -611,20 +764,28 @@ __global__ void __launch_bounds__(kPermThreads) k_topk_permute(TopkArgs ta, Perm
       ea.counts[r] = pa.offsets[(r + 1) * ea.e_loc] - pa.offsets[r * ea.e_loc];
     for (int q = threadIdx.x; q < pa.n; q += kPermThreads) ea.send_expert[q] = ea.key[pa.sorted[q]] % ea.e_loc;
   }
+  // the decode gate/up GEMM's fp16 rows (after the permutation, whose
+  // registers are dead by now)
+  if (ta.xh)
+    for (int t = warp; t < ta.T; t += kPermWarps)
+      prep_xh_row<4, true>(static_cast<const uint4*>(ta.x) + (size_t)t * (ta.H / 8), t, ta.H, ta.gs,
+                           static_cast<uint4*>(ta.xh), ta.xsum, ta.xscale, lane);
 }
 
 // ---------------------------------------------------------------- launch
 
 cudaError_t launch_router_logits(const void* X, bool x_is_f32, const uint16_t* Wr, int T, int E,
-                                 int H, float* logits, cudaStream_t st) {
+                                 int H, float* logits, cudaStream_t st, const XhOut& xo) {
   if (T <= 0) return cudaSuccess;
   // bf16 activations with H % 256 == 0 (every BASELINE shape): the tiled
   // kernel, its tile chosen by T; the lane-group kernel below (same
   // arithmetic) otherwise
   if (!x_is_f32 && H % kRouterKC == 0) {
     const auto* Xb = static_cast<const __nv_bfloat16*>(X);
-    if (T <= 8) return launch_router_tiled<8, 1, 1, 8>(Xb, Wr, T, E, H, logits, st);    // 8 t x 8 e
-    if (T < 128) return launch_router_tiled<8, 2, 1, 8>(Xb, Wr, T, E, H, logits, st);   // 8 t x 16 e
+    // decode: one or two expert rows per CTA (>= 128 CTAs for the BASELINE layers' E >= 128)
+    if (T <= kRouterSmallMaxT) return E >= 256 ? launch_router_small<2>(Xb, Wr, T, E, H, logits, st, xo)
+                                               : launch_router_small<1>(Xb, Wr, T, E, H, logits, st, xo);
+    if (T < 128) return launch_router_tiled<8, 2, 1, 8>(Xb, Wr, T, E, H, logits, st, xo);  // 8 t x 16 e
     return launch_router_tiled<8, 16, 4, 2>(Xb, Wr, T, E, H, logits, st);               // 32 t x 32 e
   }
   const int threads = 256;

@@ -361,7 +361,7 @@ int chunk_rows(int T) { return T <= 128 ? 8 : kUmmaRows; }
 
 struct WsLayout {
   size_t logits, ids, weights, offsets, sorted, inverse, work, n_work, n_active, err, mid, partial,
-      xs, total;
+      xs, xh, xsum, xscale, total;
   int max_work;
 };
 
@@ -405,6 +405,11 @@ WsLayout ws_layout_g(const llmoc_moe_layer* L, int T, int kk, int n_perm, int ch
   w.mid = take(n * L->d.inter * 2);
   w.partial = take(n * L->d.hidden * 4);
   w.xs = use_umma_c(L, chunk) ? take(n * L->d.hidden * 2) : 0;  // rows in expert-sorted order
+  if (tc_shapes(L) && !use_umma_c(L, chunk)) {  // decode gate/up: fp16 rows, group sums, row scales
+    w.xh = take((size_t)T * L->d.hidden * 2);
+    w.xsum = take((size_t)T * (L->d.hidden / L->d.group_size) * 4);
+    w.xscale = take((size_t)T * 4);
+  }
   w.total = o;
   return w;
 }
@@ -646,7 +651,17 @@ llmoc_status run_route(const llmoc_moe_layer* L, const uint16_t* X, int T, const
   const int E = L->d.n_experts, H = L->d.hidden;
   float* logits = (float*)(ws + w.logits);
   if (se) se->mark(st);
-  if (!cuda_ok(launch_router_logits(X, false, L->router_w, T, E + L->shared_gate, H, logits, st), "router"))
+  // the decode gate/up GEMM's fp16 rows: made by the router (its copy of the
+  // tokens; the bf16 kernels, H % 256 == 0, T < 128) or else by the top-k warps
+  const bool xh_router = w.xh && T < 128 && H % 256 == 0;
+  XhOut xo{};
+  if (xh_router) {
+    xo.xh = ws + w.xh;
+    xo.xsum = (float*)(ws + w.xsum);
+    xo.xscale = (float*)(ws + w.xscale);
+    xo.gs = L->d.group_size;
+  }
+  if (!cuda_ok(launch_router_logits(X, false, L->router_w, T, E + L->shared_gate, H, logits, st, xo), "router"))
     return LLMOC_ERR_CUDA;
   if (se) se->mark(st);
   TopkArgs ta{};
@@ -664,6 +679,14 @@ llmoc_status run_route(const llmoc_moe_layer* L, const uint16_t* X, int T, const
   ta.shared_gate = L->shared_gate;
   ta.ids = (int*)(ws + w.ids);
   ta.weights = (float*)(ws + w.weights);
+  if (w.xh && !xh_router) {  // decode-size forward: the top-k warps make the gate/up GEMM's fp16 rows
+    ta.x = X;
+    ta.H = H;
+    ta.gs = L->d.group_size;
+    ta.xh = ws + w.xh;
+    ta.xsum = (float*)(ws + w.xsum);
+    ta.xscale = (float*)(ws + w.xscale);
+  }
   count_launch(1);
   if (T <= kFusedRouteMaxT && L->n_exp <= kMaxExpPerm) {  // one CTA: top-k + permutation
     const PermArgs pa = perm_args(ta.ids, T * L->kk, L->n_exp, chunk_rows(T), w, ws);
@@ -687,7 +710,7 @@ llmoc_status run_route(const llmoc_moe_layer* L, const uint16_t* X, int T, const
 // slots into Y (bf16; `weights` null = 1).
 llmoc_status run_ffn(const llmoc_moe_layer* L, const uint16_t* X, int R, int kk, int chunk, const WsLayout& w,
                      char* ws, uint16_t* Y, const float* weights, cudaStream_t st, StageEvents* se = nullptr,
-                     const uint16_t* residual = nullptr, int expect_pairs = 0) {
+                     const uint16_t* residual = nullptr, int expect_pairs = 0, bool xh_ready = false) {
   const int H = L->d.hidden, I = L->d.inter;
   const bool awq = L->d.scheme == LLMOC_SCHEME_AWQ_SYM;
   // tensor cores when K of both GEMMs is a multiple of 128 and the group is
@@ -731,6 +754,22 @@ llmoc_status run_ffn(const llmoc_moe_layer* L, const uint16_t* X, int R, int kk,
   if (umma) {  // B = the gathered rows, read by TMA
     a.B = ws + w.xs;
     a.gather = nullptr;
+  } else if (path == 0) {
+    // decode gate/up on fp16 rows: each row scaled by a power of two, rounded to
+    // fp16, with its per-group sums -- made by the top-k warps of this forward
+    // (xh_ready), else here (kk == 1: only the rows the permutation placed,
+    // e.g. an expert-parallel owner's occupied receive slots)
+    if (!xh_ready) {
+      if (!cuda_ok(launch_prep_xh(X, R, H, L->d.group_size, kk == 1 ? (const int*)(ws + w.sorted) : nullptr,
+                                  (const int*)(ws + w.offsets) + L->n_exp, ws + w.xh, (float*)(ws + w.xsum),
+                                  (float*)(ws + w.xscale), st),
+                   "fp16 rows"))
+        return LLMOC_ERR_CUDA;
+      count_launch(1);
+    }
+    a.B = ws + w.xh;
+    a.bsum = (const float*)(ws + w.xsum);
+    a.bscale = (const float*)(ws + w.xscale);
   }
   if (!cuda_ok(umma ? launch_gemm_umma(MODE_GATE_UP, a, w.max_work, awq, n_pairs, st)
                     : launch_gemm(MODE_GATE_UP, path, a, w.max_work, awq, ntiles, st, n_groups, grid_items),
@@ -738,6 +777,8 @@ llmoc_status run_ffn(const llmoc_moe_layer* L, const uint16_t* X, int R, int kk,
     return LLMOC_ERR_CUDA;
   if (se) se->mark(st);
   GemmArgs b = a;
+  b.bsum = nullptr;  // the down GEMM reads mid (bf16) through its all-ones MMA
+  b.bscale = nullptr;
   b.proj = 2;
   b.M = H;
   b.K = I;
@@ -1234,7 +1275,8 @@ llmoc_status moe_forward(const llmoc_moe_layer* L, const uint16_t* X, int T, con
   StageEvents se(L);
   llmoc_status rc = run_route(L, X, T, w, ws, st, &se);
   if (rc != LLMOC_OK) return rc;
-  rc = run_ffn(L, X, T, L->kk, chunk_rows(T), w, ws, Y, (const float*)(ws + w.weights), st, &se, R);
+  rc = run_ffn(L, X, T, L->kk, chunk_rows(T), w, ws, Y, (const float*)(ws + w.weights), st, &se, R, 0,
+               w.xh != 0);
   if (rc != LLMOC_OK) return rc;
   se.commit();
   return LLMOC_OK;
