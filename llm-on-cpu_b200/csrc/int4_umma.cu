@@ -13,17 +13,18 @@
 // lane) and writes its bf16 values with tcgen05.st, so the only shared-memory
 // operand of the MMA is the activation tile (B).
 //
-// Issue cost sets the shape.  One thread issues the MMAs, and an M = 128, K =
-// 16 MMA of N = 128 columns runs for only ~64 SM cycles, about what a barrier
-// wait plus a commit cost the issuing thread.  So an item holds up to 256
-// tokens (N = 256: ~128 cycles per MMA), and each 64-wide K block costs one
-// wait and one commit: the A slot and the B slot of a block form one STAGE
-// with one "full" barrier (the four dequantising warps and the B loader arrive
-// on it) and one "empty" barrier (the MMA commit).
+// Issue cost sets the shape.  One thread issues the MMAs.  Measured on B200:
+// an M = 128, K = 16 MMA costs the issuing thread about 100 SM cycles whatever
+// its N (only N = 256, ~128 cycles of math, keeps the tensor pipe busy), and
+// an mbarrier wait about 190.  So an item holds up to 256 tokens, and the K
+// blocks go in pairs: the A slots and B slots of two 64-wide blocks share one
+// "full" barrier (the four dequantising warps and the B loader arrive on it
+// for each block) and one "empty" barrier (the MMA commit), one wait per
+// eight MMAs.
 //
 //   TMEM (512 columns x 128 lanes, fp32 words)
 //     [0,256)             accumulator (N <= 256 columns), single-buffered
-//     [256 + 32 s, +32)   A slot of stage s (s < kStages): 128 rows x 64 k, bf16 pairs
+//     [256 + 32 s, +32)   A slot s (s < kStages): 128 rows x 64 k, bf16 pairs
 //
 //   shared memory: the B slots (kStages x 256 token rows x 128 B, 128-byte
 //   swizzled K-major, one 64-wide K block each) and a weight ring (kWS slots of
@@ -42,11 +43,11 @@
 //                rows, which are contiguous: the down GEMM reads the
 //                expert-sorted gate/up output, and the gate/up GEMM a copy of
 //                the tokens gathered into expert-sorted order (k_gather_rows).
-//   warps 5..12  dequantisers: two per TMEM lane quadrant, alternating blocks;
+//   dequantisers: kDeqPerQuad per TMEM lane quadrant, taking blocks in turn;
 //                thread = one weight row: 16 words -> 64 bf16 w = (q - zp) * s
 //                (or q * s + z), one tcgen05.st.32x32b.x32 per block.  A
 //                weight slot is released as soon as its words are in registers.
-//   warps 13..20 epilogue, two per lane quadrant (half of the columns each):
+//   epilogue:    kEpiPerQuad per lane quadrant (a share of the columns each):
 //                tcgen05.ld the accumulator, SiLU*mul (gate/up, bf16 out) or
 //                fp32 (down), store to the expert-sorted rows.
 //
@@ -62,18 +63,32 @@ namespace llmoc {
 
 namespace {
 
-constexpr int kStages = 5;                 // stage ring: A slot (TMEM) + B slot (smem) per K block
-constexpr int kDeqWarps = 8;
-constexpr int kEpiWarps = 8;
+// Stage ring: an A slot (TMEM) and a B slot (smem) per K block; the blocks go
+// in pairs through one full and one empty barrier, so the MMA issuer waits
+// once per 128 k (an mbarrier wait costs the issuing thread about as much as
+// two of its MMAs).
+// Pair pr (blocks 2 pr, 2 pr + 1) uses barriers full/empty[pr % kPairBars]:
+// the slots of pair pr were last read by pair pr - kStages / 2, whose empty
+// barrier a slot writer waits for; with twice as many barriers as slot pairs
+// a barrier is reused only every 4 pairs, so a parity wait can never be two
+// phases stale (the weight ring keeps the dequantisers within 12 blocks of
+// one another).
+constexpr int kStages = 4;
+constexpr int kPairBars = kStages;
+static_assert(kStages % 2 == 0, "stage pairs");
+constexpr int kDeqPerQuad = 3;             // dequantising warps per TMEM lane quadrant
+constexpr int kEpiPerQuad = 2;             // epilogue warps per TMEM lane quadrant
+constexpr int kDeqWarps = 4 * kDeqPerQuad;
+constexpr int kEpiWarps = 4 * kEpiPerQuad;
 // Warp roles.  TMA copies are latency-bound (~2.5k cycles from L2 whatever
 // their size), so each instruction carries a large box and the rings are deep.
 constexpr int kWLoaders = 2;               // warps 1, 2: weight slots u % 2
 constexpr int kBLoaders = 2;               // warps 3, 4: B blocks j % 2
 constexpr int kWLoader0 = 1;
 constexpr int kBLoader0 = kWLoader0 + kWLoaders;          // 3
-constexpr int kDeq0 = kBLoader0 + kBLoaders;              // 5: warps 5..12 (lane quadrants 1,2,3,0 twice)
-constexpr int kEpi0 = kDeq0 + kDeqWarps;                  // 13: warps 13..20
-constexpr int kWarps = kEpi0 + kEpiWarps;                 // 21
+constexpr int kDeq0 = kBLoader0 + kBLoaders;              // 5: the dequantisers (lane quadrants 1,2,3,0, ...)
+constexpr int kEpi0 = kDeq0 + kDeqWarps;                  // then the epilogue warps
+constexpr int kWarps = kEpi0 + kEpiWarps;
 constexpr int kUThreads = kWarps * 32;                    // 672
 constexpr int kTmemCols = 512;
 constexpr int kAccCol = 0;                 // N <= 256 columns
@@ -107,6 +122,9 @@ __device__ __forceinline__ void mb_init(uint64_t* b, uint32_t c) {
 }
 __device__ __forceinline__ void mb_arrive(uint64_t* b) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
+}
+__device__ __forceinline__ void mb_arrive_n(uint64_t* b, uint32_t n) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(n) : "memory");
 }
 __device__ __forceinline__ bool mb_try(uint64_t* b, uint32_t par) {
   uint32_t ok;
@@ -291,7 +309,13 @@ __device__ __forceinline__ uint32_t bf16x2_of(float f) {
   const uint16_t u = *reinterpret_cast<const uint16_t*>(&h);
   return (uint32_t)u * 0x10001u;
 }
-__device__ __forceinline__ float silu_mul(float g, float u) { return (g / (1.f + expf(-g))) * u; }
+// SiLU(g) * u with the fast exponential and division (the epilogue of a
+// 256-column tile computes 32K of them while the single accumulator waits;
+// both approximations are a few ulp, far below the bf16 output's rounding)
+__device__ __forceinline__ float silu_mul(float g, float u) {
+  const float e = __expf(-g);
+  return g < -80.f ? 0.f : __fdividef(g, 1.f + e) * u;
+}
 
 // Sub-tile st (16 rows) of a tile: which projection and which 16-row tile.
 //   GATE_UP: st = 2q + gu  -> (gu ? up : gate), rows 64 mt + 16 q
@@ -322,7 +346,7 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a, const __
   constexpr int kWSlot = WRing<AWQ>::kSlot;
   extern __shared__ __align__(1024) unsigned char usm[];
   __shared__ __align__(8) uint64_t fullW[kWS], emptyW[kWS];
-  __shared__ __align__(8) uint64_t full[kStages], empty[kStages];
+  __shared__ __align__(8) uint64_t full[kPairBars], empty[kPairBars];
   __shared__ __align__(8) uint64_t accFull, accEmpty, done;
   __shared__ uint32_t tmem_base;
   __shared__ volatile int abort_flag;
@@ -346,10 +370,10 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a, const __
   if (threadIdx.x == 0) {
     for (int s = 0; s < kWS; ++s) {
       mb_init(&fullW[s], 1);           // weight loader's expect_tx (+ the bulk copies' bytes)
-      mb_init(&emptyW[s], kDeqWarps);  // every dequantising warp, after its last block of the slot
+      mb_init(&emptyW[s], 4 * kSlotBlocks);  // one arrival per (lane quadrant, block) of the slot
     }
-    for (int s = 0; s < kStages; ++s) {
-      mb_init(&full[s], 5);   // 4 dequantising warps (one per lane quadrant) + the B loader's expect_tx
+    for (int s = 0; s < kPairBars; ++s) {
+      mb_init(&full[s], 10);  // per block: 4 dequantising warps (one per lane quadrant) + the B loader's expect_tx
       mb_init(&empty[s], 1);  // MMA commit
     }
     mb_init(&accFull, 1);
@@ -377,7 +401,7 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a, const __
     // once the epilogue has drained tile i - 1 (the loaders and dequantisers
     // keep filling the stage ring meanwhile).
     if (lane == 0) {
-      uint32_t s = 0, ph = 0;
+      uint32_t j = 0;  // block counter (stage ring)
       const uint64_t dB0 = smem_desc(su32(ringB));
       int nrows = a.work[blockIdx.x / nmt].nrows;
       uint32_t i = 0;
@@ -389,15 +413,17 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a, const __
           break;
         }
         tc_fence_after();
-        for (int kb = 0; kb < nb; ++kb) {
-          if (!mb_wait(&full[s], ph, &abort_flag)) {
+        for (int kb = 0; kb < nb; kb += 2, j += 2) {  // nb is even (K % 128 == 0)
+          const uint32_t pr = j >> 1, p = pr % kPairBars;
+          if (!mb_wait(&full[p], (pr / kPairBars) & 1, &abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          umma_ts_k64(tmem + kAccCol, tmem + kACol + 32 * s, dB0 + ((s * kBSlot) >> 4), idesc, kb != 0);
-          umma_commit(&empty[s]);
-          if (++s == kStages) s = 0, ph ^= 1;
+          const uint32_t s0 = j % kStages, s1 = (j + 1) % kStages;
+          umma_ts_k64(tmem + kAccCol, tmem + kACol + 32 * s0, dB0 + ((s0 * kBSlot) >> 4), idesc, kb != 0);
+          umma_ts_k64(tmem + kAccCol, tmem + kACol + 32 * s1, dB0 + ((s1 * kBSlot) >> 4), idesc, 1);
+          umma_commit(&empty[p]);
         }
         if (ok) umma_commit(&accFull);
         nrows = nxt;
@@ -463,14 +489,15 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a, const __
       const uint32_t bytes = (32u << kind) * 128u;
       for (int kb = 0; kb < nb; ++kb, ++j) {
         if (j % kBLoaders != (uint32_t)(warp - kBLoader0)) continue;
-        const uint32_t s = j % kStages;
-        if (j >= (uint32_t)kStages && !mb_wait(&empty[s], ((j / kStages) - 1) & 1, &abort_flag)) {
+        const uint32_t s = j % kStages, pr = j >> 1, p = pr % kPairBars, po = pr - kStages / 2;
+        // slot s was last read by pair po
+        if (j >= (uint32_t)kStages && !mb_wait(&empty[po % kPairBars], (po / kPairBars) & 1, &abort_flag)) {
           ok = false;
           break;
         }
         if (lane == 0) {
-          mb_expect(&full[s], bytes);
-          tma_load_2d(su32(ringB + s * kBSlot), &tmB.m[kind], kb * 64, it.row0, &full[s]);
+          mb_expect(&full[p], bytes);
+          tma_load_2d(su32(ringB + s * kBSlot), &tmB.m[kind], kb * 64, it.row0, &full[p]);
         }
         __syncwarp();
       }
@@ -486,7 +513,7 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a, const __
   } else if (warp >= kDeq0 && warp < kDeq0 + kDeqWarps) {
     // ------------------------------- dequantisers -------------------------------
     const int quad = warp & 3;                  // TMEM lanes 32 quad .. +31
-    const int h = (warp - kDeq0) >> 2;          // blocks kb with kb % 2 == h
+    const int h = (warp - kDeq0) >> 2;          // blocks kb with kb % kDeqPerQuad == h
     const int r16 = lane & 15, g = r16 & 7, hi = r16 >> 3;
     // this thread's row: box op and tile within the box
     const int op = MODE == MODE_GATE_UP ? (lane >> 4) : 0;
@@ -502,9 +529,10 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a, const __
     const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16) + kACol;
     uint32_t j = 0;  // block counter (stage ring)
     for (uint32_t ti = 0; ti < my_tiles && ok; ++ti) {
-      for (int kb = h; kb < nb; kb += 2) {
+      for (int kb = h; kb < nb; kb += kDeqPerQuad) {
         const uint32_t jb = j + kb;
         const uint32_t u = ti * nsl + kb / kSlotBlocks, sw = u % kWS, sa = jb % kStages;
+        const uint32_t pra = jb >> 1, pa = pra % kPairBars, poa = pra - kStages / 2;
         const int c = kb % kSlotBlocks;
         if (!mb_wait(&fullW[sw], (u / kWS) & 1, &abort_flag)) {
           ok = false;
@@ -551,10 +579,14 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a, const __
             r[col + 1] = p1;
           }
         }
-        // the slot's words are in registers: release it after this warp's last block in it
+        // the block's words are in registers: one arrival for it on the slot (the
+        // last block of a partial slot also arrives for the slot's missing blocks)
         __syncwarp();
-        if (lane == 0 && (c + 2 >= kSlotBlocks || kb + 2 >= nb)) mb_arrive(&emptyW[sw]);
-        if (jb >= (uint32_t)kStages && !mb_wait(&empty[sa], ((jb / kStages) - 1) & 1, &abort_flag)) {
+        if (lane == 0) {
+          const int in_slot = min(kSlotBlocks, nb - (kb - c));
+          mb_arrive_n(&emptyW[sw], c == in_slot - 1 ? 1 + kSlotBlocks - in_slot : 1);
+        }
+        if (jb >= (uint32_t)kStages && !mb_wait(&empty[poa % kPairBars], (poa / kPairBars) & 1, &abort_flag)) {
           ok = false;
           break;
         }
@@ -562,15 +594,16 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a, const __
         tmem_st32(tl + 32 * sa, r);
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mb_arrive(&full[sa]);
+        if (lane == 0) mb_arrive(&full[pa]);
       }
       j += nb;
     }
   } else {
     // --------------------------------- epilogue ---------------------------------
-    // two warps per TMEM lane quadrant, each draining half of the N columns
+    // kEpiPerQuad warps per TMEM lane quadrant, each draining its share of the N columns
     const int quad = warp & 3;
-    const int half = (warp - kEpi0) >> 2;
+    const int part = (warp - kEpi0) >> 2;
+    constexpr int kCols = 256 / kEpiPerQuad;
     const uint32_t tq = tmem + ((uint32_t)(quad * 32) << 16) + kAccCol;
     uint32_t i = 0;
     for (int tile = blockIdx.x; tile < ntiles && ok; tile += G, ++i) {
@@ -582,7 +615,7 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a, const __
       }
       tc_fence_after();
       const int N = (it.nrows + 15) & ~15;
-      const int cbeg = half * 128, cend = min(N, cbeg + 128);
+      const int cbeg = part * kCols, cend = min(N, cbeg + kCols);
       for (int c0 = cbeg; c0 < cend; c0 += 16) {
         float v[16];
         tmem_ld16(tq + c0, v);
