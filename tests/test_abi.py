@@ -2,6 +2,7 @@
 header declares, and its host-side logic (argument checks, byte geometry,
 error reporting) behaves without touching a GPU."""
 import ctypes as C
+import os
 import subprocess
 
 import numpy as np
@@ -19,13 +20,33 @@ def test_exports_match_header():
     assert {s for s in exported if s.startswith("llmoc_")} == set(declared)
 
 
-def test_struct_layouts_match_reference_types():
-    """sizeof/offsetof of the reference's qlwc::Int4View and hal::cuda::MoeExpertInt4
-    on x86-64 (g++ over src/weights/qlwc_store.h, src/hal/cuda_backend.h):
-    Int4View 56 bytes, M at 32, scheme at 44, awq_zp at 48; MoeExpertInt4 32, weight at 24."""
-    assert C.sizeof(L.Int4View) == 56
-    assert (L.Int4View.M.offset, L.Int4View.scheme.offset, L.Int4View.awq_zp.offset) == (32, 44, 48)
-    assert C.sizeof(L.MoeExpertInt4) == 32 and L.MoeExpertInt4.weight.offset == 24
+def test_ctypes_structs_match_the_c_header(tmp_path):
+    """The binding's structs and include/llmoc_b200.h, both read by compilers
+    (the header's layouts against the reference's own types are pinned by
+    tests/test_boundary.py)."""
+    src = tmp_path / "h.c"
+    src.write_text("""
+#include <stddef.h>
+#include <stdio.h>
+#include "llmoc_b200.h"
+int main(void) {
+  printf("%zu %zu %zu %zu %zu %zu %zu %zu %zu %zu\\n", sizeof(llmoc_int4_view), offsetof(llmoc_int4_view, qweight),
+         offsetof(llmoc_int4_view, scales), offsetof(llmoc_int4_view, zeros), offsetof(llmoc_int4_view, scales_f32),
+         offsetof(llmoc_int4_view, M), offsetof(llmoc_int4_view, K), offsetof(llmoc_int4_view, group_size),
+         offsetof(llmoc_int4_view, scheme), offsetof(llmoc_int4_view, awq_zp));
+  printf("%zu %zu %zu %zu %zu\\n", sizeof(llmoc_moe_expert_int4), offsetof(llmoc_moe_expert_int4, gate),
+         offsetof(llmoc_moe_expert_int4, up), offsetof(llmoc_moe_expert_int4, down),
+         offsetof(llmoc_moe_expert_int4, weight));
+  return 0;
+}
+""")
+    exe = tmp_path / "h"
+    subprocess.check_call(["gcc", f"-I{os.path.dirname(L.HEADER)}", str(src), "-o", str(exe)])
+    view, moe = [list(map(int, ln.split())) for ln in subprocess.check_output([str(exe)]).decode().splitlines()]
+    V, E = L.Int4View, L.MoeExpertInt4
+    assert view == [C.sizeof(V), V.qweight.offset, V.scales.offset, V.zeros.offset, V.scales_f32.offset,
+                    V.M.offset, V.K.offset, V.group_size.offset, V.scheme.offset, V.awq_zp.offset]
+    assert moe == [C.sizeof(E), E.gate.offset, E.up.offset, E.down.offset, E.weight.offset]
 
 
 @pytest.mark.parametrize("H,I,gs,z,expect", [
