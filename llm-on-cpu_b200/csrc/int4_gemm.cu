@@ -328,7 +328,7 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
     auto issue_b = [&](int stage) {
       unsigned char* sb = wbase + stage * SG::kBytes;
 #pragma unroll
-      for (int n = 0; n < NT; ++n) {
+      for (int n = 0; n < NT; ++n) {  // a lane past the item's rows copies nothing (stale bytes are never stored)
         if (bval[n]) {
 #pragma unroll
           for (int b = 0; b < 4; ++b)
@@ -405,8 +405,7 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
       for (int n = 0; n < NT; ++n)
 #pragma unroll
         for (int b = 0; b < 4; ++b)
-          bv[n][b] = bval[n] ? *reinterpret_cast<const uint4*>(sb + SG::kW + SG::kS + SG::kZ + (n * 4 + b) * 512 + lane * 16)
-                             : make_uint4(0, 0, 0, 0);
+          bv[n][b] = *reinterpret_cast<const uint4*>(sb + SG::kW + SG::kS + SG::kZ + (n * 4 + b) * 512 + lane * 16);
       __syncwarp();  // every lane holds its operands before any lane refills this stage
 
 #pragma unroll
@@ -655,12 +654,14 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma_p(GemmArgs a) {
       if (!AWQ) zsrc[p] += NG * 32;
     }
   };
+  // a lane past the item's rows copies nothing; its stage bytes are stale
+  // and reach only MMA columns that are never stored, so the reads take no
+  // predicate
   auto issue_b = [&](int stage) {
     unsigned char* sb = wbase + stage * SG::kBytes;
     if (bval) {
 #pragma unroll
-      for (int b = 0; b < 4; ++b)
-        cp_async16(sb + SG::kW + SG::kS + SG::kZ + b * 512 + lane * 16, bsrc + b * 64);
+      for (int b = 0; b < 4; ++b) cp_async16(sb + SG::kW + SG::kS + SG::kZ + b * 512 + lane * 16, bsrc + b * 64);
     }
     bsrc += 256;
     if constexpr (XH) {
@@ -713,12 +714,15 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma_p(GemmArgs a) {
 
   int c_row0 = n_row0, c_nrows = n_nrows, c_rt = n_rt, done = 0, cs = 0;
   float c_bs0 = n_bs0, c_bs1 = n_bs1;
-  for (int i = 0;; ++i) {
-    issue_step((i + kStagesW - 1) % kStagesW);
+  int st_rd = 0, st_wr = kStagesW - 1;  // ring positions read and filled this step
+  for (;;) {
+    issue_step(st_wr);
+    st_wr = st_wr == kStagesW - 1 ? 0 : st_wr + 1;
     cp_async_commit();
     cp_async_wait<kStagesW - 1>();
     __syncwarp();  // the scales are copied by lanes 0..2*NG-1 and read by all
-    const unsigned char* sb = wbase + (i % kStagesW) * SG::kBytes;
+    const unsigned char* sb = wbase + st_rd * SG::kBytes;
+    st_rd = st_rd == kStagesW - 1 ? 0 : st_rd + 1;
     uint4 wq[NP][2], bv[4];
     float sc[NP][NG][2], zz[NP][NG][2];
 #pragma unroll
@@ -737,11 +741,8 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma_p(GemmArgs a) {
         }
       }
     }
-    const bool cval = g < c_nrows;
 #pragma unroll
-    for (int b = 0; b < 4; ++b)
-      bv[b] = cval ? *reinterpret_cast<const uint4*>(sb + SG::kW + SG::kS + SG::kZ + b * 512 + lane * 16)
-                   : make_uint4(0, 0, 0, 0);
+    for (int b = 0; b < 4; ++b) bv[b] = *reinterpret_cast<const uint4*>(sb + SG::kW + SG::kS + SG::kZ + b * 512 + lane * 16);
     __syncwarp();  // every lane holds its operands before any lane refills this stage
 
 #pragma unroll
