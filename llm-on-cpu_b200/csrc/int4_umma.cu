@@ -1,8 +1,9 @@
 // int4_umma.cu — grouped INT4 GEMM on the 5th-generation tensor cores
-// (tcgen05.mma) for prefill-size work items.
+// (tcgen05.mma) for work items of tens to hundreds of rows.
 //
 // One CTA per SM, persistent over a list of tiles.  A tile is 128 weight rows
-// of one expert against one work item (up to 256 of that expert's tokens):
+// of one expert against one work item (up to NMAX = 64 or 256 of that
+// expert's tokens):
 //     D[m, n] = sum_k W[m, k] * X[n, k]
 // MODE_GATE_UP tiles hold 64 gate rows and the same 64 up rows (interleaved
 // by 16 so a gate row and its up row sit 16 TMEM lanes apart and meet with one
@@ -13,32 +14,37 @@
 // lane) and writes its bf16 values with tcgen05.st, so the only shared-memory
 // operand of the MMA is the activation tile (B).
 //
-// Issue cost sets the shape.  One thread issues the MMAs.  Measured on B200:
-// an M = 128, K = 16 MMA costs the issuing thread about 100 SM cycles whatever
-// its N (only N = 256, ~128 cycles of math, keeps the tensor pipe busy), and
-// an mbarrier wait about 190.  So an item holds up to 256 tokens, and the K
-// blocks go in pairs: the A slots and B slots of two 64-wide blocks share one
-// "full" barrier (the four dequantising warps and the B loader arrive on it
-// for each block) and one "empty" barrier (the MMA commit), one wait per
-// eight MMAs.
+// Issue cost sets the shape.  Measured on B200: an M = 128, K = 16 MMA costs
+// the issuing thread about 100 SM cycles whatever its N (only N = 256, ~128
+// cycles of math, keeps the tensor pipe busy from one thread), and an
+// mbarrier wait about 190; MMAs issued by threads of different warps overlap
+// (two issuing warps of N = 128 MMAs doubled the SM's rate, four of N = 64
+// reached 1.4 PFLOP/s).  So the K blocks go in pairs (the A slots and B slots
+// of two 64-wide blocks share one "full" barrier, on which the four
+// dequantising warps and the B loader arrive for each block, and one "empty"
+// barrier, the MMA commit: one wait per eight MMAs), and a tile's pairs are
+// dealt round-robin to up to kIssuers issuing warps, each summing into its
+// own accumulator, as many as fit in TMEM next to the A slots.
 //
-//   TMEM (512 columns x 128 lanes, fp32 words)
-//     [0,256)             accumulator (N <= 256 columns), single-buffered
-//     [256 + 32 s, +32)   A slot s (s < kStages): 128 rows x 64 k, bf16 pairs
+//   TMEM (512 columns x 128 lanes, fp32 words), NMAX 256 / NMAX 64
+//     [0, 384) / [0, 256)        accumulators: nis of N columns, single-buffered
+//     [384 + 32 s) / [256 + 32 s) A slot s (s < kStages = 4 / 8): 128 rows x 64 k,
+//                                 bf16 pairs
 //
-//   shared memory: the B slots (kStages x 256 token rows x 128 B, 128-byte
+//   shared memory: the B slots (kStages x NMAX token rows x 128 B, 128-byte
 //   swizzled K-major, one 64-wide K block each) and a weight ring (kWS slots of
 //   kSlotBlocks K blocks: raw INT4 words + group scales (+ GPTQ zeros)).
 //
-//   warp 0       TMEM alloc; lane 0 issues tcgen05.mma (A from TMEM, B from
-//                smem), commits each stage and, per tile, the accumulator.
-//   warps 1..2   weight loaders (alternate slot uses): one instruction per
+//   warps 0..3   lane 0 issues tcgen05.mma (A from TMEM, B from smem) for its
+//                pairs of each tile, commits each pair and, per tile, its
+//                accumulator; warp 0 holds the TMEM allocation.
+//   warps 4..5   weight loaders (alternate slot uses): one instruction per
 //                slot whose lanes issue the 3-D TMA boxes of the raw words
 //                (fragment-order 512-byte chunks, whose piece order makes the
 //                row-per-thread reads below bank-conflict free), the scales
 //                and the zeros, from per-expert tensor maps built at layer
 //                creation.
-//   warps 3..4   activation loaders (alternate blocks): one TMA 2-D box (64 bf16
+//   warps 6..7   activation loaders (alternate blocks): one TMA 2-D box (64 bf16
 //                x 32/64/128/256 token rows, 128-byte swizzle) of the item's
 //                rows, which are contiguous: the down GEMM reads the
 //                expert-sorted gate/up output, and the gate/up GEMM a copy of
@@ -48,8 +54,9 @@
 //                (or q * s + z), one tcgen05.st.32x32b.x32 per block.  A
 //                weight slot is released as soon as its words are in registers.
 //   epilogue:    kEpiPerQuad per lane quadrant (a share of the columns each):
-//                tcgen05.ld the accumulator, SiLU*mul (gate/up, bf16 out) or
-//                fp32 (down), store to the expert-sorted rows.
+//                tcgen05.ld the tile's partial accumulators and add them in
+//                issuer order, SiLU*mul (gate/up, bf16 out) or fp32 (down),
+//                store to the expert-sorted rows.
 //
 // Every wait is bounded (about 2^31 SM clocks, ~1 s); a wait that gives up
 // sets a CTA-wide abort flag, bit 0 of *err, and every role drains and exits.
@@ -69,32 +76,45 @@ namespace {
 // two of its MMAs).
 // Pair pr (blocks 2 pr, 2 pr + 1) uses barriers full/empty[pr % kPairBars]:
 // the slots of pair pr were last read by pair pr - kStages / 2, whose empty
-// barrier a slot writer waits for; with twice as many barriers as slot pairs
-// a barrier is reused only every 4 pairs, so a parity wait can never be two
-// phases stale (the weight ring keeps the dequantisers within 12 blocks of
-// one another).
-constexpr int kStages = 4;
-constexpr int kPairBars = kStages;
-static_assert(kStages % 2 == 0, "stage pairs");
+// barrier a slot writer waits for.  With twice as many barriers as slot pairs
+// a barrier is reused only every kStages pairs, and pair pr + kStages / 2
+// cannot fill before pair pr is consumed (it rewrites pr's slots), so no
+// parity wait can be two phases stale, whichever issuer consumes a pair.  The
+// same reuse bounds the issuers' overlap to kStages / 2 pairs in flight.
+//
+// Two geometries (NMAX, the most rows an item holds):
+//   NMAX 256  4 stages of 32 KB B slots; A slots in TMEM columns [384, 512),
+//             accumulators below them;
+//   NMAX 64   8 stages of 8 KB B slots; A slots in [256, 512), accumulators in
+//             [0, 256).  Four slot pairs in flight let four issuers overlap.
+template <int NMAX>
+struct UCfg {
+  static_assert(NMAX == 64 || NMAX == 256, "item geometries");
+  static constexpr int kStages = NMAX == 64 ? 8 : 4;
+  static constexpr int kPairBars = kStages;
+  static constexpr int kBSlot = NMAX * 128;                 // NMAX token rows x 64 bf16
+  static constexpr int kACol = 512 - 32 * kStages;          // A slot s at kACol + 32 s
+  static constexpr int kAccCols = kACol;                    // accumulators in [0, kACol)
+  static constexpr int kBoxKinds = NMAX == 64 ? 2 : 4;      // B boxes of 32 << kind rows
+  static_assert(kStages % 2 == 0 && kAccCols >= NMAX, "stage pairs, one accumulator");
+};
 constexpr int kDeqPerQuad = 3;             // dequantising warps per TMEM lane quadrant
 constexpr int kEpiPerQuad = 2;             // epilogue warps per TMEM lane quadrant
 constexpr int kDeqWarps = 4 * kDeqPerQuad;
 constexpr int kEpiWarps = 4 * kEpiPerQuad;
 // Warp roles.  TMA copies are latency-bound (~2.5k cycles from L2 whatever
 // their size), so each instruction carries a large box and the rings are deep.
-constexpr int kWLoaders = 2;               // warps 1, 2: weight slots u % 2
-constexpr int kBLoaders = 2;               // warps 3, 4: B blocks j % 2
-constexpr int kWLoader0 = 1;
-constexpr int kBLoader0 = kWLoader0 + kWLoaders;          // 3
-constexpr int kDeq0 = kBLoader0 + kBLoaders;              // 5: the dequantisers (lane quadrants 1,2,3,0, ...)
+constexpr int kIssuers = 4;                // warps 0..3: lane 0 issues MMAs (warp 0 holds TMEM)
+constexpr int kWLoaders = 2;               // warps 4, 5: weight slots u % 2
+constexpr int kBLoaders = 2;               // warps 6, 7: B blocks j % 2
+constexpr int kWLoader0 = kIssuers;
+constexpr int kBLoader0 = kWLoader0 + kWLoaders;          // 6
+constexpr int kDeq0 = kBLoader0 + kBLoaders;              // 8: the dequantisers (lane quadrants 0,1,2,3, ...)
 constexpr int kEpi0 = kDeq0 + kDeqWarps;                  // then the epilogue warps
 constexpr int kWarps = kEpi0 + kEpiWarps;
-constexpr int kUThreads = kWarps * 32;                    // 672
+constexpr int kUThreads = kWarps * 32;                    // 896
 constexpr int kTmemCols = 512;
-constexpr int kAccCol = 0;                 // N <= 256 columns
-constexpr int kACol = 256;                 // + 32 * stage
-constexpr int kBSlot = kUmmaRows * 128;    // <= 256 token rows x 64 bf16 (32 KB)
-constexpr int kBBoxKinds = 4;              // B boxes of 32, 64, 128, 256 rows
+constexpr int kBBoxKinds = 4;              // B tensor maps of 32, 64, 128, 256 rows
 // A weight slot holds kSlotBlocks 64-wide K blocks of the tile's 128 rows:
 //   raw words  [op][tile][block][512 B]  (2 ops x 4 tiles for gate/up, 1 x 8 for down)
 //   scales     [op][tile][group][32 B]   (groups of the slot's 256 k), then zeros (GPTQ)
@@ -108,10 +128,12 @@ template <bool AWQ>
 struct WRing {
   static constexpr int kSlot = kWRaw + kWSc * (AWQ ? 1 : 2);  // 18 / 20 KB
   static constexpr int kDepth = 3;                              // 12 blocks in flight
-  static constexpr int kSmem = kStages * kBSlot + kDepth * kSlot + 1024;  // + alignment slack
 };
-static_assert(kACol + 32 * kStages <= kTmemCols, "TMEM columns");
-static_assert(WRing<false>::kSmem <= 227 * 1024, "shared memory");
+template <bool AWQ, int NMAX>
+constexpr int umma_smem() {  // B ring + weight ring + alignment slack
+  return UCfg<NMAX>::kStages * UCfg<NMAX>::kBSlot + WRing<AWQ>::kDepth * WRing<AWQ>::kSlot + 1024;
+}
+static_assert(umma_smem<false, 256>() <= 227 * 1024 && umma_smem<false, 64>() <= 227 * 1024, "shared memory");
 constexpr long long kWaitCycles = 1ll << 31;
 
 __device__ __forceinline__ uint32_t su32(const void* p) {
@@ -330,6 +352,19 @@ __device__ __forceinline__ int sub_rt(int mt, int st) {
   return MODE == MODE_GATE_UP ? mt * 4 + (st >> 1) : mt * 8 + st;
 }
 
+// Issuers of a tile of N accumulator columns and np K-block pairs: the most,
+// up to kIssuers and np, whose accumulators (each at a multiple of 32 columns,
+// `stride` apart) all fit below the A slots.  Issuer i takes the tile's pairs
+// i, i + nis, ... into the accumulator at column i * stride; the epilogue adds
+// the nis partial sums in issuer order.
+template <int NMAX>
+__device__ __forceinline__ int tile_issuers(int N, int np, int* stride) {
+  int nis = min(kIssuers, np);
+  while (nis > 1 && ((UCfg<NMAX>::kAccCols / nis) & ~31) < N) --nis;
+  *stride = (UCfg<NMAX>::kAccCols / nis) & ~31;
+  return nis;
+}
+
 }  // namespace
 
 // B operand tensor maps: boxes of 64 bf16 x {32, 64, 128, 256} token rows
@@ -338,8 +373,10 @@ struct BMaps {
   CUtensorMap m[kBBoxKinds];
 };
 
-template <int MODE, int GSB, bool AWQ>
+template <int MODE, int GSB, bool AWQ, int NMAX>
 __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a, const __grid_constant__ BMaps tmB) {
+  using C = UCfg<NMAX>;
+  constexpr int kStages = C::kStages, kPairBars = C::kPairBars, kBSlot = C::kBSlot, kACol = C::kACol;
   constexpr int NG = GSB == 1 ? 2 : 1;  // scale groups per 64-wide block
   constexpr int kRowsTile = MODE == MODE_GATE_UP ? 64 : 128;
   constexpr int kWS = WRing<AWQ>::kDepth;
@@ -347,7 +384,7 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a, const __
   extern __shared__ __align__(1024) unsigned char usm[];
   __shared__ __align__(8) uint64_t fullW[kWS], emptyW[kWS];
   __shared__ __align__(8) uint64_t full[kPairBars], empty[kPairBars];
-  __shared__ __align__(8) uint64_t accFull, accEmpty, done;
+  __shared__ __align__(8) uint64_t accFull, accEmpty, done[kIssuers];
   __shared__ uint32_t tmem_base;
   __shared__ volatile int abort_flag;
 
@@ -376,9 +413,9 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a, const __
       mb_init(&full[s], 10);  // per block: 4 dequantising warps (one per lane quadrant) + the B loader's expect_tx
       mb_init(&empty[s], 1);  // MMA commit
     }
-    mb_init(&accFull, 1);
+    mb_init(&accFull, kIssuers);  // every issuer, each tile (a commit, or an arrival if it has no pairs)
     mb_init(&accEmpty, kEpiWarps);
-    mb_init(&done, 1);
+    for (int i = 0; i < kIssuers; ++i) mb_init(&done[i], 1);
     abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -393,45 +430,60 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a, const __
   const uint32_t tmem = tmem_base;
   bool ok = true;
 
-  if (warp == 0) {
-    // ------------------------------- MMA issuer -------------------------------
-    // Per 64-wide K block: one wait (A slot dequantised and B box landed), four
-    // M = 128 MMAs of N = the item's rows rounded up to 16 (<= 256), one commit
-    // that frees the stage.  The accumulator is single-buffered: tile i starts
-    // once the epilogue has drained tile i - 1 (the loaders and dequantisers
-    // keep filling the stage ring meanwhile).
+  if (warp < kIssuers) {
+    // ------------------------------- MMA issuers -------------------------------
+    // Per pair of 64-wide K blocks: one wait (both A slots dequantised, both B
+    // boxes landed), eight M = 128 MMAs of N = the item's rows rounded up to 16,
+    // one commit that frees the pair's slots.  An MMA costs its issuing thread
+    // about 100 cycles whatever its N, but issuers in different warps run
+    // concurrently, so a tile's pairs are dealt round-robin to `nis` issuers
+    // (tile_issuers), each summing into its own accumulator: small-N tiles are
+    // issued up to four times faster.  The accumulators are single-buffered:
+    // tile i starts once the epilogue has drained tile i - 1 (the loaders and
+    // dequantisers keep filling the stage ring meanwhile).
     if (lane == 0) {
-      uint32_t j = 0;  // block counter (stage ring)
+      const int me = warp;
+      const int np = nb >> 1;
+      uint32_t j = 0;  // block counter (stage ring), over all of this CTA's tiles
       const uint64_t dB0 = smem_desc(su32(ringB));
       int nrows = a.work[blockIdx.x / nmt].nrows;
       uint32_t i = 0;
-      for (int tile = blockIdx.x; tile < ntiles && ok; tile += G, ++i) {
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += G, ++i, j += nb) {
         const int nxt = tile + G < ntiles ? a.work[(tile + G) / nmt].nrows : 0;  // prefetch
-        const uint32_t idesc = instr_desc(128, (nrows + 15) & ~15);
+        const int N = min(NMAX, (nrows + 15) & ~15);  // items hold at most NMAX rows (the permutation's chunk)
+        int stride;
+        const int nis = tile_issuers<NMAX>(N, np, &stride);
+        const uint32_t idesc = instr_desc(128, N);
+        const uint32_t dacc = tmem + (uint32_t)(me * stride);
         if (i >= 1 && !mb_wait(&accEmpty, (i - 1) & 1, &abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        for (int kb = 0; kb < nb; kb += 2, j += 2) {  // nb is even (K % 128 == 0)
-          const uint32_t pr = j >> 1, p = pr % kPairBars;
+        if (me >= nis) {  // no pairs of this tile: its MMAs of earlier tiles completed before accEmpty
+          mb_arrive(&accFull);
+          nrows = nxt;
+          continue;
+        }
+        for (int pt = me; pt < np; pt += nis) {
+          const uint32_t jj = j + 2 * pt, pr = jj >> 1, p = pr % kPairBars;
           if (!mb_wait(&full[p], (pr / kPairBars) & 1, &abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t s0 = j % kStages, s1 = (j + 1) % kStages;
-          umma_ts_k64(tmem + kAccCol, tmem + kACol + 32 * s0, dB0 + ((s0 * kBSlot) >> 4), idesc, kb != 0);
-          umma_ts_k64(tmem + kAccCol, tmem + kACol + 32 * s1, dB0 + ((s1 * kBSlot) >> 4), idesc, 1);
+          const uint32_t s0 = jj % kStages, s1 = (jj + 1) % kStages;
+          umma_ts_k64(dacc, tmem + kACol + 32 * s0, dB0 + ((s0 * kBSlot) >> 4), idesc, pt != me);
+          umma_ts_k64(dacc, tmem + kACol + 32 * s1, dB0 + ((s1 * kBSlot) >> 4), idesc, 1);
           umma_commit(&empty[p]);
         }
         if (ok) umma_commit(&accFull);
         nrows = nxt;
       }
-      // every MMA issued above has completed once `done` fires
-      umma_commit(&done);
+      // every MMA this thread issued has completed once its `done` fires
+      umma_commit(&done[me]);
       const long long t0 = clock64();
-      while (!mb_try(&done, 0))
+      while (!mb_try(&done[me], 0))
         if (clock64() - t0 > kWaitCycles) {
           ok = false;
           break;
@@ -485,7 +537,7 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a, const __
     WorkItem it = a.work[blockIdx.x / nmt];
     for (int tile = blockIdx.x; tile < ntiles && ok; tile += G) {
       const WorkItem nit = tile + G < ntiles ? a.work[(tile + G) / nmt] : it;  // prefetch
-      const int kind = it.nrows <= 32 ? 0 : (it.nrows <= 64 ? 1 : (it.nrows <= 128 ? 2 : 3));
+      const int kind = min(C::kBoxKinds - 1, it.nrows <= 32 ? 0 : (it.nrows <= 64 ? 1 : (it.nrows <= 128 ? 2 : 3)));
       const uint32_t bytes = (32u << kind) * 128u;
       for (int kb = 0; kb < nb; ++kb, ++j) {
         if (j % kBLoaders != (uint32_t)(warp - kBLoader0)) continue;
@@ -600,11 +652,13 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a, const __
     }
   } else {
     // --------------------------------- epilogue ---------------------------------
-    // kEpiPerQuad warps per TMEM lane quadrant, each draining its share of the N columns
+    // kEpiPerQuad warps per TMEM lane quadrant, each draining its share of the
+    // N columns; a column's value is the sum of the tile's nis partial
+    // accumulators, added in issuer order
     const int quad = warp & 3;
     const int part = (warp - kEpi0) >> 2;
-    constexpr int kCols = 256 / kEpiPerQuad;
-    const uint32_t tq = tmem + ((uint32_t)(quad * 32) << 16) + kAccCol;
+    const int np = nb >> 1;
+    const uint32_t tq = tmem + ((uint32_t)(quad * 32) << 16);
     uint32_t i = 0;
     for (int tile = blockIdx.x; tile < ntiles && ok; tile += G, ++i) {
       const WorkItem it = a.work[tile / nmt];  // loads while the accumulator fills
@@ -614,11 +668,20 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a, const __
         break;
       }
       tc_fence_after();
-      const int N = (it.nrows + 15) & ~15;
-      const int cbeg = part * kCols, cend = min(N, cbeg + kCols);
+      const int N = min(NMAX, (it.nrows + 15) & ~15);
+      int stride;
+      const int nis = tile_issuers<NMAX>(N, np, &stride);
+      const int share = ((N >> 4) + kEpiPerQuad - 1) / kEpiPerQuad * 16;
+      const int cbeg = part * share, cend = min(N, cbeg + share);
       for (int c0 = cbeg; c0 < cend; c0 += 16) {
         float v[16];
         tmem_ld16(tq + c0, v);
+        for (int q = 1; q < nis; ++q) {
+          float w[16];
+          tmem_ld16(tq + (uint32_t)(q * stride + c0), w);
+#pragma unroll
+          for (int c = 0; c < 16; ++c) v[c] += w[c];
+        }
         if (MODE == MODE_GATE_UP) {
           // lanes 0..15: gate rows, lanes 16..31: the same up rows; the pair
           // (c, c+1) is split: gate lane -> column c, up lane -> column c+1
@@ -771,40 +834,53 @@ int sm_count() {
 }
 }  // namespace
 
-template <int MODE, int GSB, bool AWQ>
+template <int MODE, int GSB, bool AWQ, int NMAX>
 static cudaError_t launch_u(const GemmArgs& a, int max_work, int b_rows, cudaStream_t st) {
   BMaps tmB;
-  for (int k = 0; k < kBBoxKinds; ++k)
+  memset(&tmB, 0, sizeof(tmB));
+  for (int k = 0; k < UCfg<NMAX>::kBoxKinds; ++k)
     if (!b_tensor_map(&tmB.m[k], a.B, a.K, b_rows, a.ldb, 32 << k)) return cudaErrorInvalidValue;
-  constexpr int smem = WRing<AWQ>::kSmem;
-  cudaError_t e = cudaFuncSetAttribute(k_int4_umma<MODE, GSB, AWQ>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return e;
+  constexpr int smem = umma_smem<AWQ, NMAX>();
+  static bool attr = false;  // per template instance
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(k_int4_umma<MODE, GSB, AWQ, NMAX>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
   const int nmt = a.M / (MODE == MODE_GATE_UP ? 64 : 128);
   const long long tiles = (long long)max_work * nmt;
   const int grid = (int)std::min<long long>(tiles, sm_count());
-  return launch_pdl(k_int4_umma<MODE, GSB, AWQ>, dim3(grid), dim3(kUThreads), (size_t)smem, st, a, tmB);
+  return launch_pdl(k_int4_umma<MODE, GSB, AWQ, NMAX>, dim3(grid), dim3(kUThreads), (size_t)smem, st, a, tmB);
 }
 
-template <int MODE, bool AWQ>
+template <int MODE, bool AWQ, int NMAX>
 static cudaError_t launch_u_gs(const GemmArgs& a, int max_work, int b_rows, cudaStream_t st) {
   switch (a.gs) {
-    case 32: return launch_u<MODE, 1, AWQ>(a, max_work, b_rows, st);
-    case 64: return launch_u<MODE, 2, AWQ>(a, max_work, b_rows, st);
-    default: return launch_u<MODE, 4, AWQ>(a, max_work, b_rows, st);
+    case 32: return launch_u<MODE, 1, AWQ, NMAX>(a, max_work, b_rows, st);
+    case 64: return launch_u<MODE, 2, AWQ, NMAX>(a, max_work, b_rows, st);
+    default: return launch_u<MODE, 4, AWQ, NMAX>(a, max_work, b_rows, st);
   }
 }
 
-// Requires M % 64 (gate/up) or M % 128 (down) == 0, K % 128 == 0, items of
-// at most kUmmaRows (256) rows, gs in {32, 64, 128}, and B = b_rows contiguous expert-
-// sorted rows (a.gather is not used).
-cudaError_t launch_gemm_umma(int mode, const GemmArgs& a, int max_work, int awq, int b_rows, cudaStream_t st) {
-  if (max_work <= 0) return cudaSuccess;
+template <int NMAX>
+static cudaError_t launch_u_n(int mode, const GemmArgs& a, int max_work, int awq, int b_rows, cudaStream_t st) {
   if (mode == MODE_GATE_UP)
-    return awq ? launch_u_gs<MODE_GATE_UP, true>(a, max_work, b_rows, st)
-               : launch_u_gs<MODE_GATE_UP, false>(a, max_work, b_rows, st);
-  return awq ? launch_u_gs<MODE_PLAIN_F32, true>(a, max_work, b_rows, st)
-             : launch_u_gs<MODE_PLAIN_F32, false>(a, max_work, b_rows, st);
+    return awq ? launch_u_gs<MODE_GATE_UP, true, NMAX>(a, max_work, b_rows, st)
+               : launch_u_gs<MODE_GATE_UP, false, NMAX>(a, max_work, b_rows, st);
+  return awq ? launch_u_gs<MODE_PLAIN_F32, true, NMAX>(a, max_work, b_rows, st)
+             : launch_u_gs<MODE_PLAIN_F32, false, NMAX>(a, max_work, b_rows, st);
+}
+
+// Requires M % 64 (gate/up) or M % 128 (down) == 0, K % 128 == 0, items of
+// at most item_rows rows (kUmmaSmallRows or kUmmaRows), gs in {32, 64, 128},
+// and B = b_rows contiguous expert-sorted rows (a.gather is not used).
+cudaError_t launch_gemm_umma(int mode, const GemmArgs& a, int max_work, int awq, int b_rows, int item_rows,
+                             cudaStream_t st) {
+  if (max_work <= 0) return cudaSuccess;
+  if (item_rows == kUmmaSmallRows) return launch_u_n<kUmmaSmallRows>(mode, a, max_work, awq, b_rows, st);
+  if (item_rows == kUmmaRows) return launch_u_n<kUmmaRows>(mode, a, max_work, awq, b_rows, st);
+  return cudaErrorInvalidValue;
 }
 
 }  // namespace llmoc

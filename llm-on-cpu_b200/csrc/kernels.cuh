@@ -192,10 +192,14 @@ cudaError_t launch_dequant(const ProjDev& P, int M, int K, int gs, int awq, int 
 cudaError_t launch_gemm(int mode, int path, const GemmArgs& a, int max_work, int awq, int ntiles,
                         cudaStream_t st, int n_groups = 0, int grid_items = 0);
 // int4_umma.cu: tcgen05.mma (TMEM accumulator) grouped GEMM for work items of
-// up to kUmmaRows rows (prefill-size groups); same K / group-size conditions.  B is
-// b_rows contiguous expert-sorted rows read by TMA (a.gather unused).
+// up to item_rows rows: kUmmaRows (prefill-size groups) or kUmmaSmallRows
+// (groups of tens of rows, up to four MMA issuers per tile); same K /
+// group-size conditions.  B is b_rows contiguous expert-sorted rows read by
+// TMA (a.gather unused).
 constexpr int kUmmaRows = 256;
-cudaError_t launch_gemm_umma(int mode, const GemmArgs& a, int max_work, int awq, int b_rows, cudaStream_t st);
+constexpr int kUmmaSmallRows = 64;
+cudaError_t launch_gemm_umma(int mode, const GemmArgs& a, int max_work, int awq, int b_rows, int item_rows,
+                             cudaStream_t st);
 // TMA tensor maps (128 bytes each) of every expert's repacked weights for the
 // tcgen05 kernel, kMapsPerExpert per expert: [part * 3 + proj], part 0 raw
 // words, 1 scales, 2 zeros (GPTQ); proj 0 gate, 1 up, 2 down.  Built once per

@@ -353,11 +353,23 @@ struct llmoc_moe_layer {
 
 namespace {
 
-// Rows per work item: decode-size batches use one mma N tile (8 rows), so
-// that kernel variant has no per-tile branches; prefill-size batches use
-// kUmmaRows-row items for the tcgen05 kernel (or the CUDA-core kernel, which
-// walks any item length, on shapes the tensor-core kernels do not take).
-int chunk_rows(int T) { return T <= 128 ? 8 : kUmmaRows; }
+// Rows per work item for `pairs` (row, expert) pairs over `groups` experts:
+// decode-size groups (about 8 pairs per expert or fewer) use one mma N tile (8
+// rows), so that kernel variant has no per-tile branches; groups of up to
+// kSmallAvg pairs on average use kUmmaSmallRows-row items (the tcgen05 kernel
+// with several MMA issuers per tile); larger ones kUmmaRows-row items (or, on
+// shapes the tensor-core kernels do not take, the CUDA-core kernel, which
+// walks any item length).
+constexpr long kSmallAvg = 40;
+int chunk_for_rows(long pairs, int groups) {
+  const long g = std::max(1, groups);
+  if (pairs <= 8 * g + g / 2) return 8;
+  return pairs <= kSmallAvg * g ? kUmmaSmallRows : kUmmaRows;
+}
+// A forward over T tokens: T <= 128 keeps the 8-row items (the decode GEMMs)
+int chunk_rows(const llmoc_moe_layer* L, int T) {
+  return T <= 128 ? 8 : ((long)T * L->kk <= kSmallAvg * L->n_exp ? kUmmaSmallRows : kUmmaRows);
+}
 
 struct WsLayout {
   size_t logits, ids, weights, offsets, sorted, inverse, work, n_work, n_active, err, mid, partial,
@@ -372,13 +384,12 @@ bool tc_shapes(const llmoc_moe_layer* L) {
   return L->d.hidden % 128 == 0 && L->d.inter % 128 == 0 && (gs == 32 || gs == 64 || gs == 128);
 }
 
-// Items hold at most `chunk` rows: 8 for decode-size groups (register-fed
-// tensor-core kernel), kUmmaRows for the tcgen05 kernel.
-int chunk_for_rows(int pairs, int groups) { return pairs <= 8 * std::max(1, groups) + groups / 2 ? 8 : kUmmaRows; }
 // A layer with tensor-core shapes always holds its weight maps (creation
-// fails without them), so its kUmmaRows-row items always take the tcgen05
-// kernel: the register-fed kernel handles at most 8 rows per item.
-bool use_umma_c(const llmoc_moe_layer* L, int chunk) { return tc_shapes(L) && L->wmaps && chunk == kUmmaRows; }
+// fails without them), so its kUmmaSmallRows- and kUmmaRows-row items always
+// take the tcgen05 kernel: the register-fed kernel handles at most 8 rows per item.
+bool use_umma_c(const llmoc_moe_layer* L, int chunk) {
+  return tc_shapes(L) && L->wmaps && (chunk == kUmmaRows || chunk == kUmmaSmallRows);
+}
 
 // Workspace of one grouped run over T rows with kk slots each, permuted over
 // n_perm groups; `logits` adds the router's [T, n_experts] logits.
@@ -415,7 +426,7 @@ WsLayout ws_layout_g(const llmoc_moe_layer* L, int T, int kk, int n_perm, int ch
 }
 
 WsLayout ws_layout(const llmoc_moe_layer* L, int T) {
-  return ws_layout_g(L, T, L->kk, L->n_exp, chunk_rows(T), true);
+  return ws_layout_g(L, T, L->kk, L->n_exp, chunk_rows(L, T), true);
 }
 
 llmoc_status validate_desc(const llmoc_moe_layer_desc* d) {
@@ -689,7 +700,7 @@ llmoc_status run_route(const llmoc_moe_layer* L, const uint16_t* X, int T, const
   }
   count_launch(1);
   if (T <= kFusedRouteMaxT && L->n_exp <= kMaxExpPerm) {  // one CTA: top-k + permutation
-    const PermArgs pa = perm_args(ta.ids, T * L->kk, L->n_exp, chunk_rows(T), w, ws);
+    const PermArgs pa = perm_args(ta.ids, T * L->kk, L->n_exp, chunk_rows(L, T), w, ws);
     if (!cuda_ok(launch_topk_permute(ta, pa, st), "topk+permute")) return LLMOC_ERR_CUDA;
     count_launch(1);
     if (se) se->mark(st);
@@ -699,7 +710,7 @@ llmoc_status run_route(const llmoc_moe_layer* L, const uint16_t* X, int T, const
   if (!cuda_ok(launch_topk(ta, st), "topk")) return LLMOC_ERR_CUDA;
   if (se) se->mark(st);
   count_launch(1);
-  llmoc_status rc = run_permute(ta.ids, T * L->kk, L->n_exp, chunk_rows(T), w, ws, st);
+  llmoc_status rc = run_permute(ta.ids, T * L->kk, L->n_exp, chunk_rows(L, T), w, ws, st);
   if (se) se->mark(st);
   return rc;
 }
@@ -771,7 +782,7 @@ llmoc_status run_ffn(const llmoc_moe_layer* L, const uint16_t* X, int R, int kk,
     a.bsum = (const float*)(ws + w.xsum);
     a.bscale = (const float*)(ws + w.xscale);
   }
-  if (!cuda_ok(umma ? launch_gemm_umma(MODE_GATE_UP, a, w.max_work, awq, n_pairs, st)
+  if (!cuda_ok(umma ? launch_gemm_umma(MODE_GATE_UP, a, w.max_work, awq, n_pairs, chunk, st)
                     : launch_gemm(MODE_GATE_UP, path, a, w.max_work, awq, ntiles, st, n_groups, grid_items),
                "gate/up"))
     return LLMOC_ERR_CUDA;
@@ -790,7 +801,7 @@ llmoc_status run_ffn(const llmoc_moe_layer* L, const uint16_t* X, int R, int kk,
   b.out = ws + w.partial;
   b.ldo = H;
   b.ctr = (int*)(ws + w.err) + 2;
-  if (!cuda_ok(umma ? launch_gemm_umma(MODE_PLAIN_F32, b, w.max_work, awq, n_pairs, st)
+  if (!cuda_ok(umma ? launch_gemm_umma(MODE_PLAIN_F32, b, w.max_work, awq, n_pairs, chunk, st)
                     : launch_gemm(MODE_PLAIN_F32, path, b, w.max_work, awq, ntiles, st, n_groups, grid_items),
                "down"))
     return LLMOC_ERR_CUDA;
@@ -852,8 +863,9 @@ EpSrcLayout ep_src_layout(const llmoc_moe_layer* L, int T) {
 }
 // owner-rank workspace for `rows` received rows (the larger of the two item sizes)
 size_t ep_owner_bytes(const llmoc_moe_layer* L, int rows) {
-  return std::max(ws_layout_g(L, rows, 1, L->n_exp, 8, false).total,
-                  ws_layout_g(L, rows, 1, L->n_exp, kUmmaRows, false).total);
+  size_t b = 0;
+  for (int chunk : {8, kUmmaSmallRows, kUmmaRows}) b = std::max(b, ws_layout_g(L, rows, 1, L->n_exp, chunk, false).total);
+  return b;
 }
 
 // Workspace of one NVLink expert-parallel step on a rank: the source side
@@ -1275,7 +1287,7 @@ llmoc_status moe_forward(const llmoc_moe_layer* L, const uint16_t* X, int T, con
   StageEvents se(L);
   llmoc_status rc = run_route(L, X, T, w, ws, st, &se);
   if (rc != LLMOC_OK) return rc;
-  rc = run_ffn(L, X, T, L->kk, chunk_rows(T), w, ws, Y, (const float*)(ws + w.weights), st, &se, R, 0,
+  rc = run_ffn(L, X, T, L->kk, chunk_rows(L, T), w, ws, Y, (const float*)(ws + w.weights), st, &se, R, 0,
                w.xh != 0);
   if (rc != LLMOC_OK) return rc;
   se.commit();
