@@ -21,7 +21,7 @@
 // (two issuing warps of N = 128 MMAs doubled the SM's rate, four of N = 64
 // reached 1.4 PFLOP/s).  So the K blocks go in pairs (the A slots and B slots
 // of two 64-wide blocks share one "full" barrier, on which the four
-// dequantising warps and the B loader arrive for each block, and one "empty"
+// dequantising warps arrive once per pair and the B loaders once per block, and one "empty"
 // barrier, the MMA commit: one wait per eight MMAs), and a tile's pairs are
 // dealt round-robin to up to kIssuers issuing warps, each summing into its
 // own accumulator, as many as fit in TMEM next to the A slots.
@@ -49,10 +49,11 @@
 //                rows, which are contiguous: the down GEMM reads the
 //                expert-sorted gate/up output, and the gate/up GEMM a copy of
 //                the tokens gathered into expert-sorted order (k_gather_rows).
-//   dequantisers: kDeqPerQuad per TMEM lane quadrant, taking blocks in turn;
-//                thread = one weight row: 16 words -> 64 bf16 w = (q - zp) * s
-//                (or q * s + z), one tcgen05.st.32x32b.x32 per block.  A
-//                weight slot is released as soon as its words are in registers.
+//   dequantisers: kDeqPerQuad per TMEM lane quadrant, taking block pairs in
+//                turn; thread = one weight row: 16 words -> 64 bf16 w = (q -
+//                zp) * s (or q * s + z), one tcgen05.st.32x32b.x32 per block.
+//                A pair's weight-slot share is released as soon as its words
+//                are in registers.
 //   epilogue:    kEpiPerQuad per lane quadrant (a share of the columns each):
 //                tcgen05.ld the tile's partial accumulators and add them in
 //                issuer order, SiLU*mul (gate/up, bf16 out) or fp32 (down),
@@ -98,10 +99,36 @@ struct UCfg {
   static constexpr int kBoxKinds = NMAX == 64 ? 2 : 4;      // B boxes of 32 << kind rows
   static_assert(kStages % 2 == 0 && kAccCols >= NMAX, "stage pairs, one accumulator");
 };
-constexpr int kDeqPerQuad = 3;             // dequantising warps per TMEM lane quadrant
-constexpr int kEpiPerQuad = 2;             // epilogue warps per TMEM lane quadrant
-constexpr int kDeqWarps = 4 * kDeqPerQuad;
-constexpr int kEpiWarps = 4 * kEpiPerQuad;
+// Dequantising and epilogue warps per TMEM lane quadrant (20 warps in all).
+//
+// Why every parity wait is sound (a wait for the phase of pair pr on a barrier
+// reused every R pairs passes early if the barrier has not yet completed the
+// phase of pr - R, so that phase must be known complete).  Pairs may be
+// consumed out of order, several issuers taking them; but both B loaders
+// handle EVERY pair in order, each waiting for pair q - S consumed (S =
+// kStages / 2 slot pairs) before loading pair q, so once any pair q is full,
+// every pair <= q - S has been consumed (and its weight slot has landed).
+// * A dequantising warp takes every kDeqPerQuad-th pair of a tile; before its
+//   pair pr it passed the A-slot wait of its previous pair pr - d (d <=
+//   kDeqPerQuad), so pair pr - d - S was full and every pair <= pr - d - 2S
+//   consumed.  Its A-slot wait (empty barrier of pair pr - S, reused every 2S
+//   pairs) needs pr - 3S: kDeqPerQuad <= S.  Its weight-slot wait (slot = pair,
+//   reused every kWS pairs) needs the slot of pr - kWS landed: kWS >=
+//   kDeqPerQuad + 2S.
+// * An issuer's previous wait on a full barrier was for its previous phase
+//   (tile_issuers: nis divides kPairBars); at a tile start every earlier pair
+//   has been consumed (accEmpty).
+// * Each loader warp handles every other slot (weights) or every pair (B), so
+//   its own previous wait covers the barrier's previous phase.
+template <int NMAX>
+struct URoles {
+  static constexpr int kDeqPerQuad = NMAX == 64 ? 4 : 2;
+  static constexpr int kEpiPerQuad = 5 - kDeqPerQuad;
+  static constexpr int kDeqWarps = 4 * kDeqPerQuad;
+  static constexpr int kEpiWarps = 4 * kEpiPerQuad;
+  static constexpr int S = UCfg<NMAX>::kStages / 2;
+  static_assert(kDeqPerQuad <= S, "dequantiser stride: at most S pairs");
+};
 // Warp roles.  TMA copies are latency-bound (~2.5k cycles from L2 whatever
 // their size), so each instruction carries a large box and the rings are deep.
 constexpr int kIssuers = 4;                // warps 0..3: lane 0 issues MMAs (warp 0 holds TMEM)
@@ -110,30 +137,42 @@ constexpr int kBLoaders = 2;               // warps 6, 7: B blocks j % 2
 constexpr int kWLoader0 = kIssuers;
 constexpr int kBLoader0 = kWLoader0 + kWLoaders;          // 6
 constexpr int kDeq0 = kBLoader0 + kBLoaders;              // 8: the dequantisers (lane quadrants 0,1,2,3, ...)
-constexpr int kEpi0 = kDeq0 + kDeqWarps;                  // then the epilogue warps
-constexpr int kWarps = kEpi0 + kEpiWarps;
+constexpr int kWarps = kDeq0 + 20;                        // then the epilogue warps (URoles)
 constexpr int kUThreads = kWarps * 32;                    // 896
 constexpr int kTmemCols = 512;
 constexpr int kBBoxKinds = 4;              // B tensor maps of 32, 64, 128, 256 rows
-// A weight slot holds kSlotBlocks 64-wide K blocks of the tile's 128 rows:
+// A weight slot holds one K-block pair (kSlotBlocks = 2 64-wide blocks) of the
+// tile's 128 rows, so slot u is pair u of the CTA's stage sequence (no tile
+// ends in a partial slot: K % 128 == 0):
 //   raw words  [op][tile][block][512 B]  (2 ops x 4 tiles for gate/up, 1 x 8 for down)
-//   scales     [op][tile][group][32 B]   (groups of the slot's 256 k), then zeros (GPTQ)
+//   scales     [op][tile][group][32 B]   (groups of the slot's 128 k), then zeros (GPTQ)
 // Each part arrives in ONE TMA box per op.
-constexpr int kSlotBlocks = 4;
-constexpr int kWRaw = 8 * kSlotBlocks * 512;              // 16 KB
-constexpr int kWSc = 8 * 8 * 32;                          // up to 8 groups per slot (gs 32)
+constexpr int kSlotBlocks = 2;
+constexpr int kWRaw = 8 * kSlotBlocks * 512;              // 8 KB
+constexpr int kWSc = 8 * (2 * kSlotBlocks) * 32;          // up to 2 kSlotBlocks groups per slot (gs 32)
 constexpr int kWOffS = kWRaw;
 constexpr int kWOffZ = kWRaw + kWSc;
-template <bool AWQ>
+// A weight slot's TMA boxes land ~3.5k SM cycles after they are issued and a
+// slot is reissued only once all four lane quadrants have dequantised it.  The
+// ring takes the shared memory the B ring leaves: 16 slots (pairs) beside the
+// 64 KB B ring of NMAX 64, 8 beside the 128 KB of NMAX 256 (powers of two: the
+// slot index is a mask), deep enough for the parity argument at URoles.
+template <bool AWQ, int NMAX>
 struct WRing {
-  static constexpr int kSlot = kWRaw + kWSc * (AWQ ? 1 : 2);  // 18 / 20 KB
-  static constexpr int kDepth = 3;                              // 12 blocks in flight
+  static constexpr int kSlot = kWRaw + kWSc * (AWQ ? 1 : 2);  // 9 / 10 KB
+  static constexpr int kDepth = NMAX == 64 ? 16 : 8;
 };
 template <bool AWQ, int NMAX>
 constexpr int umma_smem() {  // B ring + weight ring + alignment slack
-  return UCfg<NMAX>::kStages * UCfg<NMAX>::kBSlot + WRing<AWQ>::kDepth * WRing<AWQ>::kSlot + 1024;
+  return UCfg<NMAX>::kStages * UCfg<NMAX>::kBSlot + WRing<AWQ, NMAX>::kDepth * WRing<AWQ, NMAX>::kSlot + 1024;
 }
 static_assert(umma_smem<false, 256>() <= 227 * 1024 && umma_smem<false, 64>() <= 227 * 1024, "shared memory");
+static_assert((WRing<false, 64>::kDepth & (WRing<false, 64>::kDepth - 1)) == 0 &&
+                  (WRing<false, 256>::kDepth & (WRing<false, 256>::kDepth - 1)) == 0,
+              "weight ring depth: a power of two");
+static_assert(WRing<false, 64>::kDepth >= URoles<64>::kDeqPerQuad + 2 * URoles<64>::S &&
+                  WRing<false, 256>::kDepth >= URoles<256>::kDeqPerQuad + 2 * URoles<256>::S,
+              "weight ring depth: covers a dequantiser's parity argument");
 constexpr long long kWaitCycles = 1ll << 31;
 
 __device__ __forceinline__ uint32_t su32(const void* p) {
@@ -352,15 +391,18 @@ __device__ __forceinline__ int sub_rt(int mt, int st) {
   return MODE == MODE_GATE_UP ? mt * 4 + (st >> 1) : mt * 8 + st;
 }
 
-// Issuers of a tile of N accumulator columns and np K-block pairs: the most,
-// up to kIssuers and np, whose accumulators (each at a multiple of 32 columns,
-// `stride` apart) all fit below the A slots.  Issuer i takes the tile's pairs
-// i, i + nis, ... into the accumulator at column i * stride; the epilogue adds
-// the nis partial sums in issuer order.
+// Issuers of a tile of N accumulator columns and np K-block pairs: the most
+// of 4, 2, 1 (at most np) whose accumulators (each at a multiple of 32
+// columns, `stride` apart) all fit below the A slots.  Issuer i takes the
+// tile's pairs i, i + nis, ... into the accumulator at column i * stride; the
+// epilogue adds the nis partial sums in issuer order.  nis divides kPairBars,
+// so an issuer's previous wait on a full barrier was for that barrier's
+// previous phase and a parity wait cannot be two phases stale.
 template <int NMAX>
 __device__ __forceinline__ int tile_issuers(int N, int np, int* stride) {
-  int nis = min(kIssuers, np);
-  while (nis > 1 && ((UCfg<NMAX>::kAccCols / nis) & ~31) < N) --nis;
+  static_assert(UCfg<NMAX>::kPairBars % kIssuers == 0, "issuers divide the pair barriers");
+  int nis = kIssuers;
+  while (nis > 1 && (nis > np || ((UCfg<NMAX>::kAccCols / nis) & ~31) < N)) nis >>= 1;
   *stride = (UCfg<NMAX>::kAccCols / nis) & ~31;
   return nis;
 }
@@ -377,10 +419,13 @@ template <int MODE, int GSB, bool AWQ, int NMAX>
 __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a, const __grid_constant__ BMaps tmB) {
   using C = UCfg<NMAX>;
   constexpr int kStages = C::kStages, kPairBars = C::kPairBars, kBSlot = C::kBSlot, kACol = C::kACol;
+  constexpr int kDeqPerQuad = URoles<NMAX>::kDeqPerQuad, kEpiPerQuad = URoles<NMAX>::kEpiPerQuad;
+  constexpr int kDeqWarps = URoles<NMAX>::kDeqWarps, kEpiWarps = URoles<NMAX>::kEpiWarps;
+  constexpr int kEpi0 = kDeq0 + kDeqWarps;
   constexpr int NG = GSB == 1 ? 2 : 1;  // scale groups per 64-wide block
   constexpr int kRowsTile = MODE == MODE_GATE_UP ? 64 : 128;
-  constexpr int kWS = WRing<AWQ>::kDepth;
-  constexpr int kWSlot = WRing<AWQ>::kSlot;
+  constexpr int kWS = WRing<AWQ, NMAX>::kDepth;
+  constexpr int kWSlot = WRing<AWQ, NMAX>::kSlot;
   extern __shared__ __align__(1024) unsigned char usm[];
   __shared__ __align__(8) uint64_t fullW[kWS], emptyW[kWS];
   __shared__ __align__(8) uint64_t full[kPairBars], empty[kPairBars];
@@ -398,7 +443,7 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a, const __
   const int G = gridDim.x;
   const uint32_t my_tiles = (uint32_t)((ntiles - (int)blockIdx.x + G - 1) / G);
   const int nsl = (nb + kSlotBlocks - 1) / kSlotBlocks;  // weight-slot uses per tile
-  constexpr int kGps = 4 * 64 / (GSB * 32);                // scale groups per weight slot
+  constexpr int kGps = kSlotBlocks * 64 / (GSB * 32);      // scale groups per weight slot
   constexpr int kOps = MODE == MODE_GATE_UP ? 2 : 1;     // TMA boxes per part (gate, up)
   constexpr int kTilesOp = 8 / kOps;                     // 16-row tiles per box
   unsigned char* ringB = usm + ((1024 - (su32(usm) & 1023)) & 1023);  // 1024-aligned (SW128)
@@ -410,7 +455,7 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a, const __
       mb_init(&emptyW[s], 4 * kSlotBlocks);  // one arrival per (lane quadrant, block) of the slot
     }
     for (int s = 0; s < kPairBars; ++s) {
-      mb_init(&full[s], 10);  // per block: 4 dequantising warps (one per lane quadrant) + the B loader's expect_tx
+      mb_init(&full[s], 6);  // per pair: 4 dequantising warps (one per lane quadrant) + the B loaders' 2 expect_tx
       mb_init(&empty[s], 1);  // MMA commit
     }
     mb_init(&accFull, kIssuers);  // every issuer, each tile (a commit, or an arrival if it has no pairs)
@@ -565,7 +610,7 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a, const __
   } else if (warp >= kDeq0 && warp < kDeq0 + kDeqWarps) {
     // ------------------------------- dequantisers -------------------------------
     const int quad = warp & 3;                  // TMEM lanes 32 quad .. +31
-    const int h = (warp - kDeq0) >> 2;          // blocks kb with kb % kDeqPerQuad == h
+    const int h = (warp - kDeq0) >> 2;          // pairs pt with pt % kDeqPerQuad == h
     const int r16 = lane & 15, g = r16 & 7, hi = r16 >> 3;
     // this thread's row: box op and tile within the box
     const int op = MODE == MODE_GATE_UP ? (lane >> 4) : 0;
@@ -579,71 +624,78 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a, const __
     const float zpf = AWQ ? (float)(128 + a.zp) : 128.f;
     const uint32_t zp2 = bf16x2_of(zpf);
     const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16) + kACol;
-    uint32_t j = 0;  // block counter (stage ring)
+    const int np = nb >> 1;  // K-block pairs per tile (a pair never straddles a weight slot)
+    uint32_t j = 0;          // block counter (stage ring)
     for (uint32_t ti = 0; ti < my_tiles && ok; ++ti) {
-      for (int kb = h; kb < nb; kb += kDeqPerQuad) {
-        const uint32_t jb = j + kb;
-        const uint32_t u = ti * nsl + kb / kSlotBlocks, sw = u % kWS, sa = jb % kStages;
+      // the quadrant's warps take the tile's pairs in turn: one weight-slot wait,
+      // one A-slot wait and one arrival on the pair's full barrier per two blocks
+      for (int pt = h; pt < np; pt += kDeqPerQuad) {
+        const int kb0 = 2 * pt, c0 = kb0 % kSlotBlocks;
+        const uint32_t jb = j + kb0;
+        const uint32_t u = ti * nsl + kb0 / kSlotBlocks, sw = u % kWS;
         const uint32_t pra = jb >> 1, pa = pra % kPairBars, poa = pra - kStages / 2;
-        const int c = kb % kSlotBlocks;
         if (!mb_wait(&fullW[sw], (u / kWS) & 1, &abort_flag)) {
           ok = false;
           break;
         }
         const unsigned char* wsl = ringW + sw * kWSlot;
-        uint4 q4[4];
 #pragma unroll
-        for (int t = 0; t < 4; ++t) q4[t] = *reinterpret_cast<const uint4*>(wsl + qsrc[t] + c * 512);
-        // groups of this block within the slot: gs 128 -> c/2, gs 64 -> c, gs 32 -> 2c, 2c+1
-        const int gq = GSB == 4 ? (c >> 1) : (GSB == 2 ? c : 2 * c);
-        uint32_t sc[NG];  // AWQ: the scale as a bf16 pair
-        float sf[NG], zf[NG];  // GPTQ: scale and zero in fp32 (exact fp16 values)
+        for (int bi = 0; bi < 2; ++bi) {
+          const int c = c0 + bi;
+          uint4 q4[4];
 #pragma unroll
-        for (int q = 0; q < NG; ++q) {
-          const float s16 = __half2float(*reinterpret_cast<const __half*>(wsl + ssrc + (gq + q) * 32));
-          if (AWQ) {
-            sc[q] = bf16x2_of(s16);
-          } else {
-            sf[q] = s16;
-            zf[q] = __half2float(*reinterpret_cast<const __half*>(wsl + ssrc + (gq + q) * 32 + kWOffZ - kWOffS));
-          }
-        }
-        uint32_t r[32];
+          for (int t = 0; t < 4; ++t) q4[t] = *reinterpret_cast<const uint4*>(wsl + qsrc[t] + c * 512);
+          // groups of this block within the slot: gs 128 -> c/2, gs 64 -> c, gs 32 -> 2c, 2c+1
+          const int gq = GSB == 4 ? (c >> 1) : (GSB == 2 ? c : 2 * c);
+          uint32_t sc[NG];       // AWQ: the scale as a bf16 pair
+          float sf[NG], zf[NG];  // GPTQ: scale and zero in fp32 (exact fp16 values)
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const uint32_t wds[4] = {q4[t].x, q4[t].y, q4[t].z, q4[t].w};
-#pragma unroll
-          for (int wi = 0; wi < 4; ++wi) {
-            // word (kb2 = wi >> 1, kt = wi & 1) covers k = 32 kb2 + 8 t + 4 kt + {0..3}
-            const int kb2 = wi >> 1, kt = wi & 1, q = NG == 2 ? kb2 : 0;
-            const uint32_t v = wds[wi] >> shift;
-            uint32_t p0 = lop3_and_or(v, 0x000F000Fu, 0x43004300u);       // k+0, k+1
-            uint32_t p1 = lop3_and_or(v >> 8, 0x000F000Fu, 0x43004300u);  // k+2, k+3
-            if (AWQ) {  // (q - zp) * s: an exact integer times the scale, rounded once
-              p0 = h2mul(h2sub(p0, zp2), sc[q]);
-              p1 = h2mul(h2sub(p1, zp2), sc[q]);
-            } else {  // q * s + z in fp32 (q * s exact), rounded once to bf16
-              p0 = gptq_pair(p0, sf[q], zf[q]);
-              p1 = gptq_pair(p1, sf[q], zf[q]);
+          for (int q = 0; q < NG; ++q) {
+            const float s16 = __half2float(*reinterpret_cast<const __half*>(wsl + ssrc + (gq + q) * 32));
+            if (AWQ) {
+              sc[q] = bf16x2_of(s16);
+            } else {
+              sf[q] = s16;
+              zf[q] = __half2float(*reinterpret_cast<const __half*>(wsl + ssrc + (gq + q) * 32 + kWOffZ - kWOffS));
             }
-            const int col = kb2 * 16 + 4 * t + 2 * kt;  // TMEM column = k / 2
-            r[col] = p0;
-            r[col + 1] = p1;
           }
+          if (bi == 1) {  // both blocks' words are in registers: release this quadrant's share of the slot
+            __syncwarp();
+            if (lane == 0) mb_arrive_n(&emptyW[sw], kSlotBlocks);
+          }
+          uint32_t r[32];
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const uint32_t wds[4] = {q4[t].x, q4[t].y, q4[t].z, q4[t].w};
+#pragma unroll
+            for (int wi = 0; wi < 4; ++wi) {
+              // word (kb2 = wi >> 1, kt = wi & 1) covers k = 32 kb2 + 8 t + 4 kt + {0..3}
+              const int kb2 = wi >> 1, kt = wi & 1, q = NG == 2 ? kb2 : 0;
+              const uint32_t v = wds[wi] >> shift;
+              uint32_t p0 = lop3_and_or(v, 0x000F000Fu, 0x43004300u);       // k+0, k+1
+              uint32_t p1 = lop3_and_or(v >> 8, 0x000F000Fu, 0x43004300u);  // k+2, k+3
+              if (AWQ) {  // (q - zp) * s: an exact integer times the scale, rounded once
+                p0 = h2mul(h2sub(p0, zp2), sc[q]);
+                p1 = h2mul(h2sub(p1, zp2), sc[q]);
+              } else {  // q * s + z in fp32 (q * s exact), rounded once to bf16
+                p0 = gptq_pair(p0, sf[q], zf[q]);
+                p1 = gptq_pair(p1, sf[q], zf[q]);
+              }
+              const int col = kb2 * 16 + 4 * t + 2 * kt;  // TMEM column = k / 2
+              r[col] = p0;
+              r[col + 1] = p1;
+            }
+          }
+          if (bi == 0) {  // the pair's A slots were last read by pair poa
+            if (jb >= (uint32_t)kStages && !mb_wait(&empty[poa % kPairBars], (poa / kPairBars) & 1, &abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+          }
+          tmem_st32(tl + 32 * ((jb + bi) % kStages), r);
         }
-        // the block's words are in registers: one arrival for it on the slot (the
-        // last block of a partial slot also arrives for the slot's missing blocks)
-        __syncwarp();
-        if (lane == 0) {
-          const int in_slot = min(kSlotBlocks, nb - (kb - c));
-          mb_arrive_n(&emptyW[sw], c == in_slot - 1 ? 1 + kSlotBlocks - in_slot : 1);
-        }
-        if (jb >= (uint32_t)kStages && !mb_wait(&empty[poa % kPairBars], (poa / kPairBars) & 1, &abort_flag)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        tmem_st32(tl + 32 * sa, r);
+        if (!ok) break;
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mb_arrive(&full[pa]);
@@ -785,7 +837,7 @@ bool build_umma_weight_maps(const ExpertDev* h, int n_exp, int inter, int hidden
                             void* host_out) {
   static_assert(sizeof(CUtensorMap) == kTensorMapBytes, "tensor map size");
   const EncodeTiled enc = tensor_map_encoder();
-  if (!enc || gs <= 0 || 256 % gs) return false;
+  if (!enc || gs <= 0 || (kSlotBlocks * 64) % gs) return false;
   CUtensorMap* out = static_cast<CUtensorMap*>(host_out);
   memset(host_out, 0, (size_t)n_exp * kMapsPerExpert * sizeof(CUtensorMap));
   for (int e = 0; e < n_exp; ++e)
@@ -807,7 +859,7 @@ bool build_umma_weight_maps(const ExpertDev* h, int n_exp, int inter, int hidden
       for (int part = 1; part <= (gptq ? 2 : 1); ++part) {  // scales / zeros: {16 rows, group, tile}
         const cuuint64_t dims[3] = {16, ng, Mt};
         const cuuint64_t strides[2] = {32, ng * 32};
-        const cuuint32_t box[3] = {16, (cuuint32_t)(256 / gs), tiles};
+        const cuuint32_t box[3] = {16, (cuuint32_t)(kSlotBlocks * 64 / gs), tiles};
         const __half* base = part == 1 ? P.s : P.z;
         if (!base || enc(out + e * kMapsPerExpert + part * 3 + proj, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3,
                          const_cast<__half*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
