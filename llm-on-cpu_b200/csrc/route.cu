@@ -416,6 +416,18 @@ static cudaError_t launch_router_small(const __nv_bfloat16* X, const uint16_t* W
                     E, H, logits, xo);
 }
 
+static long router_sm_count() {
+  static long n[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (!n[dev]) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    n[dev] = v > 0 ? v : 148;
+  }
+  return n[dev];
+}
+
 template <int TT, int EE, int WT, int WE>
 static cudaError_t launch_router_tiled(const __nv_bfloat16* X, const uint16_t* Wr, int T, int E, int H,
                                        float* logits, cudaStream_t st, const XhOut& xo = XhOut{}) {
@@ -786,7 +798,15 @@ cudaError_t launch_router_logits(const void* X, bool x_is_f32, const uint16_t* W
     if (T <= kRouterSmallMaxT) return E >= 256 ? launch_router_small<2>(Xb, Wr, T, E, H, logits, st, xo)
                                                : launch_router_small<1>(Xb, Wr, T, E, H, logits, st, xo);
     if (T < 128) return launch_router_tiled<8, 2, 1, 8>(Xb, Wr, T, E, H, logits, st, xo);  // 8 t x 16 e
-    return launch_router_tiled<8, 16, 4, 2>(Xb, Wr, T, E, H, logits, st);               // 32 t x 32 e
+    // the largest tile whose grid still keeps the SMs busy: 32 x 32 (half a
+    // wave or more: at T = 1024, E = 128 its 128 CTAs beat 512 of 16 x 16),
+    // else 16 x 16 (one wave), else 8 x 16 (at T = 512, E = 128 the 32 x 32
+    // grid is 64 CTAs; 16 x 16 took it from 27 to 21 us)
+    const long sms = router_sm_count();
+    const auto ctas = [&](int rt, int re) { return (long)((T + rt - 1) / rt) * ((E + re - 1) / re); };
+    if (2 * ctas(32, 32) >= sms) return launch_router_tiled<8, 16, 4, 2>(Xb, Wr, T, E, H, logits, st);  // 32 t x 32 e
+    if (ctas(16, 16) >= sms) return launch_router_tiled<8, 4, 2, 4>(Xb, Wr, T, E, H, logits, st);       // 16 t x 16 e
+    return launch_router_tiled<8, 2, 1, 8>(Xb, Wr, T, E, H, logits, st);                                 // 8 t x 16 e
   }
   const int threads = 256;
   if (T <= 64) {

@@ -115,10 +115,12 @@ def test_routing_bit_exact(oracle, name, T):
     dl.close()
 
 
-@pytest.mark.parametrize("T", [3, 77, 150])
+@pytest.mark.parametrize("T", [3, 77, 150, 800, 2400])
 def test_router_tiles_bit_exact(oracle, T):
     """Router logits of every token bitwise equal to the reference's AVX2 order
-    on each tile shape of the tiled router (T <= 8, 8 < T < 128, T >= 128),
+    on each tile shape of the tiled router (T <= 8; 8 < T < 128; for T >= 128
+    8 x 16, 16 x 16 and 32 x 32 tiles as the grid grows: T = 150, 800, 2400 at
+    E = 40),
     with partial token and expert tiles (E = 40, T not a multiple of 32) and a
     non-finite activation (that token's logits become 0, as in the reference)."""
     rng = np.random.default_rng(40 + T)
