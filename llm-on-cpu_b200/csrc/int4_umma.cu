@@ -108,10 +108,10 @@ struct UCfg {
 // handle EVERY pair in order, each waiting for pair q - S consumed (S =
 // kStages / 2 slot pairs) before loading pair q, so once any pair q is full,
 // every pair <= q - S has been consumed (and its weight slot has landed).
-// * A dequantising warp takes every kDeqPerQuad-th pair of a tile; before its
-//   pair pr it passed the A-slot wait of its previous pair pr - d (d <=
-//   kDeqPerQuad), so pair pr - d - S was full and every pair <= pr - d - 2S
-//   consumed.  Its A-slot wait (empty barrier of pair pr - S, reused every 2S
+// * A dequantising warp takes every kDeqPerQuad-th pair of the CTA's pair
+//   sequence (counted over all its tiles); before its pair pr it passed the
+//   A-slot wait of its previous pair pr - d (d = kDeqPerQuad), so pair pr - d
+//   - S was full and every pair <= pr - d - 2S consumed.  Its A-slot wait (empty barrier of pair pr - S, reused every 2S
 //   pairs) needs pr - 3S: kDeqPerQuad <= S.  Its weight-slot wait (slot = pair,
 //   reused every kWS pairs) needs the slot of pr - kWS landed: kWS >=
 //   kDeqPerQuad + 2S.
@@ -627,9 +627,14 @@ __global__ void __launch_bounds__(kUThreads, 1) k_int4_umma(GemmArgs a, const __
     const int np = nb >> 1;  // K-block pairs per tile (a pair never straddles a weight slot)
     uint32_t j = 0;          // block counter (stage ring)
     for (uint32_t ti = 0; ti < my_tiles && ok; ++ti) {
-      // the quadrant's warps take the tile's pairs in turn: one weight-slot wait,
-      // one A-slot wait and one arrival on the pair's full barrier per two blocks
-      for (int pt = h; pt < np; pt += kDeqPerQuad) {
+      // the quadrant's warps take the pairs in turn by their index over all of
+      // the CTA's tiles, so a warp's successive pairs are exactly kDeqPerQuad
+      // apart across tile ends too (a per-tile restart would leave up to
+      // 2 kDeqPerQuad - 1 when np is not a multiple of it; URoles needs at most
+      // S): one weight-slot wait, one A-slot wait and one arrival on the
+      // pair's full barrier per two blocks
+      const int p0 = (int)((j >> 1) % kDeqPerQuad);
+      for (int pt = (h - p0 + kDeqPerQuad) % kDeqPerQuad; pt < np; pt += kDeqPerQuad) {
         const int kb0 = 2 * pt, c0 = kb0 % kSlotBlocks;
         const uint32_t jb = j + kb0;
         const uint32_t u = ti * nsl + kb0 / kSlotBlocks, sw = u % kWS;

@@ -326,7 +326,7 @@ def _check_full(oracle, dl, X, Xd, T):
 
 
 @pytest.mark.parametrize("name,T", [("qwen3_30b_a3b", 1), ("qwen3_30b_a3b", 8), ("qwen3_30b_a3b", 64),
-                                    ("qwen3_30b_a3b", 512), ("glm45_air", 64), ("glm45_air", 1024),
+                                    ("qwen3_30b_a3b", 512), ("glm45_air", 64), ("glm45_air", 512), ("glm45_air", 1024),
                                     ("glm45_air", 4096), ("kimi_k2", 1), ("kimi_k2", 64),
                                     ("kimi_k2", 1024), ("kimi_k2", 8192)])
 def test_full_size_layer(oracle, name, T):
