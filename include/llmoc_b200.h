@@ -338,6 +338,17 @@ LLMOC_API llmoc_status llmoc_moe_ep_experts(const llmoc_moe_layer* layer, const 
 LLMOC_API llmoc_status llmoc_moe_ep_combine(const llmoc_moe_layer* layer, const uint16_t* X, int T,
                                             const uint16_t* ret_rows, uint16_t* Y, void* workspace,
                                             size_t workspace_bytes, void* stream);
+/* Step 3 over a fixed-capacity receive layout, for an all-to-all whose split
+ * sizes the host never reads (equal splits of world x capacity slots, the
+ * transport ICollective::alltoall, src/contracts/collective.h:13, declares):
+ * slots whose owner-local expert id lies outside [0, experts of the shard)
+ * are empty -- not computed, their out_rows left as they were.  n_hint is
+ * the number of occupied slots expected (e.g. the T * topk pairs a source
+ * sends); it sizes the work items and the GEMM grids, not the result.  The
+ * workspace is llmoc_moe_ep_owner_workspace_bytes(layer, n). */
+LLMOC_API llmoc_status llmoc_moe_ep_experts_padded(const llmoc_moe_layer* layer, const uint16_t* rows,
+                                                   const int32_t* expert, int n, int n_hint, uint16_t* out_rows,
+                                                   void* workspace, size_t workspace_bytes, void* stream);
 
 /* -------------------------- expert-parallel transport over NVLink peer memory
  *

@@ -1494,6 +1494,18 @@ llmoc_status llmoc_moe_ep_experts(const llmoc_moe_layer* L, const uint16_t* rows
   return ep_experts(L, rows, expert, n, n, out_rows, workspace, workspace_bytes, stream);
 }
 
+llmoc_status llmoc_moe_ep_experts_padded(const llmoc_moe_layer* L, const uint16_t* rows, const int32_t* expert,
+                                         int n, int n_hint, uint16_t* out_rows, void* workspace,
+                                         size_t workspace_bytes, void* stream) {
+  if (!L || n < 0 || n_hint < 0 || (n > 0 && (!rows || !expert || !out_rows)))
+    return fails(LLMOC_ERR_INVALID, "bad arguments");
+  if (n == 0) return LLMOC_OK;
+  // empty slots (ids outside [0, n_exp)) are skipped by the permutation; the
+  // hint sizes the item regime and the GEMM grids by the occupied slots
+  return ep_experts(L, rows, expert, n, std::max(1, std::min(n, n_hint)), out_rows, workspace, workspace_bytes,
+                    stream);
+}
+
 namespace {
 // The shared expert over the source rank's own T tokens, into the source
 // workspace (no-op without a shared expert).

@@ -11,9 +11,14 @@ layer step:
 
     1. backend.dispatch   route, order the T*topk routed pairs by (owner,
                           owner-local expert, token, slot), gather their rows
-    2. all-to-all         per-peer pair counts, then rows + owner-local ids
-    3. backend.experts    grouped expert FFN over the received rows
-    4. all-to-all         expert outputs back to the source, in send order
+    2. all-to-all         rows + owner-local ids in fixed-capacity regions:
+                          region r of the send buffer holds the pairs for
+                          owner r, up to T*topk of them, the rest marked
+                          empty (id -1); equal splits, so the host never
+                          reads a count and nothing waits for it
+    3. backend.experts    grouped expert FFN over the received rows (empty
+                          slots skipped)
+    4. all-to-all         expert outputs back, region by region
     5. backend.combine    routed weights x returned rows (slot order) + shared
 
 `DeviceBackend` runs 1, 3 and 5 through the C ABI (llmoc_moe_ep_*); any
@@ -67,8 +72,35 @@ class _Marks:
             self.ev.append(e)
 
 
-def ep_forward(backend, X: torch.Tensor, T: int, group=None, times: Optional[EpTimes] = None) -> torch.Tensor:
-    """Y [T, H] (bf16) of this rank's T tokens; collective over `group`."""
+def pack_regions(send_rows: torch.Tensor, send_expert: torch.Tensor, send_counts: torch.Tensor, cap: int):
+    """The fixed-capacity send layout, on the device: the owner-ordered pairs
+    of `send_rows` / `send_expert` placed at region owner * cap + (rank among
+    the owner's pairs), every other slot marked empty (expert id -1).
+    Returns (rows, expert ids, dest) with dest[i] the slot of pair i."""
+    dev = send_rows.device
+    P, H = send_rows.shape
+    world = send_counts.numel()
+    counts = send_counts.to(torch.int64)
+    starts = torch.cumsum(counts, 0) - counts
+    owner = torch.repeat_interleave(torch.arange(world, device=dev), counts, output_size=P)
+    dest = owner * cap + (torch.arange(P, device=dev) - starts[owner])
+    pad_rows = torch.empty((world * cap, H), dtype=send_rows.dtype, device=dev)
+    pad_rows.index_copy_(0, dest, send_rows)
+    pad_expert = torch.full((world * cap,), -1, dtype=send_expert.dtype, device=dev)
+    pad_expert.index_copy_(0, dest, send_expert)
+    return pad_rows, pad_expert, dest
+
+
+def ep_forward(backend, X: torch.Tensor, T: int, group=None, times: Optional[EpTimes] = None,
+               max_tokens: Optional[int] = None) -> torch.Tensor:
+    """Y [T, H] (bf16) of this rank's T tokens; collective over `group`.
+
+    The step never synchronises with the host: each routed pair's place in the
+    send buffer (owner r's region r * cap, cap = max_tokens * topk, then its
+    rank among the pairs for r) is computed on the device from the per-owner
+    counts, and the all-to-alls move whole regions.  max_tokens bounds the T
+    of every rank in this step and must be the same on all of them (default:
+    T, when every rank passes the same T)."""
     H = X.shape[1]
     dev = X.device
     timed = times is not None and dev.type == "cuda"
@@ -76,28 +108,32 @@ def ep_forward(backend, X: torch.Tensor, T: int, group=None, times: Optional[EpT
     mk.mark()
     send_rows, send_expert, send_counts = backend.dispatch(X, T)
     mk.mark()
-    recv_counts = torch.empty_like(send_counts)
-    dist.all_to_all_single(recv_counts, send_counts, group=group)
-    counts = torch.stack([send_counts, recv_counts]).cpu()  # host split sizes
-    s_split = [int(v) for v in counts[0]]
-    r_split = [int(v) for v in counts[1]]
-    n_recv = sum(r_split)
-    recv_rows = torch.empty((n_recv, H), dtype=send_rows.dtype, device=dev)
-    recv_expert = torch.empty((n_recv,), dtype=send_expert.dtype, device=dev)
-    dist.all_to_all_single(recv_rows, send_rows, r_split, s_split, group=group)
-    dist.all_to_all_single(recv_expert, send_expert, r_split, s_split, group=group)
+    P = send_rows.shape[0]  # T * topk routed pairs, ordered by owner
+    world = send_counts.numel()
+    topk = P // T if T > 0 else 0
+    cap = (max_tokens if max_tokens is not None else T) * topk
+    if cap < P:
+        raise ValueError(f"T = {T} is above max_tokens = {max_tokens}")
+    pad_rows, pad_expert, dest = pack_regions(send_rows, send_expert, send_counts, cap)
+    recv_rows = torch.empty_like(pad_rows)
+    recv_expert = torch.empty_like(pad_expert)
+    dist.all_to_all_single(recv_rows, pad_rows, group=group)
+    dist.all_to_all_single(recv_expert, pad_expert, group=group)
     mk.mark()
-    out_rows = backend.experts(recv_rows, recv_expert, n_recv)
+    out_rows = backend.experts(recv_rows, recv_expert, world * cap, n_hint=P)
     mk.mark()
-    ret_rows = torch.empty_like(send_rows)
-    dist.all_to_all_single(ret_rows, out_rows, s_split, r_split, group=group)
+    ret_pad = torch.empty_like(out_rows)
+    dist.all_to_all_single(ret_pad, out_rows, group=group)
+    ret_rows = ret_pad.index_select(0, dest)
     mk.mark()
     Y = backend.combine(X, T, ret_rows)
     mk.mark()
     if times is not None:
-        times.sent_rows, times.recv_rows = sum(s_split), n_recv
         if timed:
             torch.cuda.current_stream().synchronize()
+        times.sent_rows = P
+        times.recv_rows = int((recv_expert >= 0).sum())  # the timing pass reads it; the step itself does not
+        if timed:
             e = mk.ev
             times.dispatch_ms = e[0].elapsed_time(e[1])
             times.a2a_ms = e[1].elapsed_time(e[2]) + e[3].elapsed_time(e[4])
@@ -144,14 +180,16 @@ class DeviceBackend:
         self.shard.dispatch(X, T, ws, wsb, rows, eid, cnt, self._stream())
         return rows, eid, cnt
 
-    def experts(self, rows, expert, n):
+    def experts(self, rows, expert, n, n_hint=None):
+        """n received rows; with n_hint, the fixed-capacity layout (empty slots
+        carry id -1, n_hint occupied slots expected)."""
         dev = rows.device
         out = self._buf(self._own, "out", (n, self.H), torch.bfloat16, dev)
         if n == 0:
             return out
         wsb = self.shard.owner_workspace_bytes(n)
         ws = self._buf(self._own, "ws", (wsb,), torch.uint8, dev)
-        self.shard.experts(rows, expert, n, out, ws, wsb, self._stream())
+        self.shard.experts(rows, expert, n, out, ws, wsb, self._stream(), n_hint=n_hint)
         return out
 
     def combine(self, X, T, ret_rows):

@@ -128,6 +128,7 @@ _SIGS = {
     "llmoc_moe_ep_owner_workspace_bytes": (_sz, [_vp, _i]),
     "llmoc_moe_ep_dispatch": (_i, [_vp, _vp, _i, _vp, _sz, _vp, _vp, _vp, _vp]),
     "llmoc_moe_ep_experts": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _sz, _vp]),
+    "llmoc_moe_ep_experts_padded": (_i, [_vp, _vp, _vp, _i, _i, _vp, _vp, _sz, _vp]),
     "llmoc_moe_ep_combine": (_i, [_vp, _vp, _i, _vp, _vp, _vp, _sz, _vp]),
     "llmoc_ep_ipc_handle_bytes": (_sz, []),
     "llmoc_ep_transport_create": (_i, [_i, _i, _i, _i, _i, _i, C.POINTER(_vp), _vp]),
@@ -368,9 +369,17 @@ class EpLayerShard(MoeLayer):
         check(lib.llmoc_moe_ep_dispatch(self.handle, ptr(X), T, ptr(ws), ws_bytes, ptr(send_rows), ptr(send_expert),
                                         ptr(send_counts), stream_ptr(stream)), "llmoc_moe_ep_dispatch")
 
-    def experts(self, rows, expert, n, out_rows, ws, ws_bytes, stream=None) -> None:
-        check(lib.llmoc_moe_ep_experts(self.handle, ptr(rows), ptr(expert), n, ptr(out_rows), ptr(ws), ws_bytes,
-                                       stream_ptr(stream)), "llmoc_moe_ep_experts")
+    def experts(self, rows, expert, n, out_rows, ws, ws_bytes, stream=None, n_hint=None) -> None:
+        """n rows of owner-local expert ids; with n_hint, the fixed-capacity
+        layout (ids outside the shard's experts are empty slots, n_hint the
+        occupied slots expected: llmoc_moe_ep_experts_padded)."""
+        if n_hint is None:
+            check(lib.llmoc_moe_ep_experts(self.handle, ptr(rows), ptr(expert), n, ptr(out_rows), ptr(ws),
+                                           ws_bytes, stream_ptr(stream)), "llmoc_moe_ep_experts")
+        else:
+            check(lib.llmoc_moe_ep_experts_padded(self.handle, ptr(rows), ptr(expert), n, n_hint, ptr(out_rows),
+                                                  ptr(ws), ws_bytes, stream_ptr(stream)),
+                  "llmoc_moe_ep_experts_padded")
 
     def combine(self, X, T, ret_rows, Y, ws, ws_bytes, stream=None) -> None:
         check(lib.llmoc_moe_ep_combine(self.handle, ptr(X), T, ptr(ret_rows), ptr(Y), ptr(ws), ws_bytes,

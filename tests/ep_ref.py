@@ -29,11 +29,13 @@ class OracleBackend:
         cnt = torch.from_numpy(np.bincount(key // self.e_loc, minlength=self.world).astype(np.int32))
         return rows.contiguous(), eid, cnt
 
-    def experts(self, rows: torch.Tensor, expert: torch.Tensor, n: int):
+    def experts(self, rows: torch.Tensor, expert: torch.Tensor, n: int, n_hint=None):
         L = self.layer
         out = np.zeros((n, L.H), np.float32)
         R = rows.float().numpy()
         for r in range(n):
+            if not 0 <= int(expert[r]) < self.e_loc:
+                continue  # an empty slot of the fixed-capacity layout
             e = int(expert[r]) * self.world + self.rank
             out[r] = self.o.moe_ffn_routed(R[r], L.H, L.I, [L.experts[e]], np.ones(1, np.float32), None, 0.0)
         return torch.from_numpy(orc.bf16_round(out)).to(torch.bfloat16)

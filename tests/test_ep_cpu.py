@@ -45,7 +45,8 @@ def _worker(rank, world, port, name, T, q):
         X = orc.make_tokens(np.random.default_rng(100 + rank), Tr, layer.H)
         Xt = torch.from_numpy(X).to(torch.bfloat16)
         times = ep.EpTimes()
-        Y = ep.ep_forward(OracleBackend(oracle, layer, rank, world), Xt, Tr, times=times)
+        Y = ep.ep_forward(OracleBackend(oracle, layer, rank, world), Xt, Tr, times=times,
+                          max_tokens=T + world - 1)  # the ragged counts' bound, the same on every rank
         Yref = oracle.moe_layer_forward(layer, X)[0]
         y, r = Y.float().numpy().reshape(-1).astype(np.float64), Yref.reshape(-1).astype(np.float64)
         mre = float(np.max(np.abs(y - r)) / np.max(np.abs(r)))

@@ -90,6 +90,48 @@ def test_two_shards_on_one_gpu(oracle, name, T):
         s.close()
 
 
+def _emulated_forward_padded(backends, Xs, max_tokens):
+    """ep_forward's fixed-capacity exchange for every rank in one process: the
+    regions packed on the device (ep.pack_regions), the all-to-alls as copies
+    of whole regions, the owners through llmoc_moe_ep_experts_padded."""
+    world = len(backends)
+    sends = [b.dispatch(X, X.shape[0]) for b, X in zip(backends, Xs)]
+    topk = sends[0][0].shape[0] // Xs[0].shape[0]
+    cap = max_tokens * topk
+    packed = [ep.pack_regions(r, e, c, cap) for r, e, c in sends]
+    outs = []
+    for r in range(world):  # owner r receives region r of every source, source order
+        rows = torch.cat([packed[s][0][r * cap:(r + 1) * cap] for s in range(world)]).contiguous()
+        eid = torch.cat([packed[s][1][r * cap:(r + 1) * cap] for s in range(world)]).contiguous()
+        outs.append(backends[r].experts(rows, eid, world * cap, n_hint=sends[r][0].shape[0]).clone())
+    Ys = []
+    for s in range(world):  # region s of every owner back to source s
+        ret = torch.cat([outs[r][s * cap:(s + 1) * cap] for r in range(world)])
+        Ys.append(backends[s].combine(Xs[s], Xs[s].shape[0], ret.index_select(0, packed[s][2]).contiguous()))
+    torch.cuda.synchronize()
+    return Ys
+
+
+@pytest.mark.parametrize("name", list(CFGS))
+@pytest.mark.parametrize("T", [5, 40])
+def test_fixed_capacity_exchange_matches(oracle, name, T):
+    """The host-free NCCL step's layout: every routed pair placed in its
+    owner's region on the device, empty slots (id -1) skipped by the owners.
+    Outputs equal the count-based exchange bit for bit (same expert groups,
+    same work items) and the oracle within the layer tolerance."""
+    layer = orc.make_layer(oracle, np.random.default_rng(3), **CFGS[name])
+    shards, bks = _backends(layer, 2)
+    Xh = [orc.make_tokens(np.random.default_rng(50 + r), T + 3 * r, layer.H) for r in range(2)]
+    Xd = [G.bf16_dev(X) for X in Xh]
+    Yp = _emulated_forward_padded(bks, Xd, T + 3)
+    Yc, _ = _emulated_forward(bks, Xd)
+    for r in range(2):
+        assert torch.equal(Yp[r], Yc[r]), (name, T, r)
+        _check(Yp[r], oracle.moe_layer_forward(layer, Xh[r])[0], (name, T, r))
+    for s in shards:
+        s.close()
+
+
 @pytest.mark.parametrize("name", ["qwen_like", "glm_like_shared_sigmoid"])
 def test_world_one_matches_plain_forward(oracle, name):
     layer = orc.make_layer(oracle, np.random.default_rng(4), **CFGS[name])
@@ -207,7 +249,7 @@ def _nccl_worker(rank, world, port, name, T, q):
         bk = ep.DeviceBackend(shard, layer.H, layer.topk)
         Xh = orc.make_tokens(np.random.default_rng(70 + rank), T + rank, layer.H)
         X = G.bf16_dev(Xh).to(f"cuda:{rank}")
-        Y = ep.ep_forward(bk, X, X.shape[0])
+        Y = ep.ep_forward(bk, X, X.shape[0], max_tokens=T + world - 1)  # ragged T, one bound on every rank
         torch.cuda.synchronize()
         mre, cos = G.quality(G.bf16_to_f32(Y), oracle.moe_layer_forward(layer, Xh)[0])
         q.put((rank, mre, cos))
