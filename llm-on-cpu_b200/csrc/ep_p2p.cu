@@ -85,12 +85,15 @@ __device__ __forceinline__ void copy_row(uint4* dst, const uint4* src, int n16, 
 
 // Source side: rows of send order q (grouped by owner: counts[d] rows for
 // owner d, owners ascending) go to owner d's receive slot q - off[d] of this
-// rank's region; then each owner's meta and flag.
+// rank's region; then each owner's meta and flag.  A row comes from
+// send_rows[q], or (sorted non-null) straight from the token's row
+// X[sorted[q] / kk], which spares the gathered copy and its launch.
 __global__ void __launch_bounds__(256) k_ep_push_dispatch(EpP2PLayout L, char* const* peers,
                                                           const uint4* __restrict__ send_rows,
                                                           const int* __restrict__ send_expert,
                                                           const int* __restrict__ counts, int rank, uint32_t seq,
-                                                          int* ctr) {
+                                                          int* ctr, const uint4* __restrict__ X,
+                                                          const int* __restrict__ sorted, int kk) {
   __shared__ int off[kEpMaxWorld + 1];
   if (threadIdx.x == 0) {
     int o = 0;
@@ -109,7 +112,8 @@ __global__ void __launch_bounds__(256) k_ep_push_dispatch(EpP2PLayout L, char* c
     while (q >= off[d + 1]) ++d;
     const int i = q - off[d];
     char* pb = peers[d];
-    copy_row(rows_at(pb, L, parity, rank) + (size_t)i * n16, send_rows + (size_t)q * n16, n16, lane);
+    const uint4* src = sorted ? X + (size_t)(sorted[q] / kk) * n16 : send_rows + (size_t)q * n16;
+    copy_row(rows_at(pb, L, parity, rank) + (size_t)i * n16, src, n16, lane);
     if (lane == 0) ids_at(pb, L, parity, rank)[i] = send_expert[q];
   }
   if (!last_cta(ctr)) return;
@@ -184,9 +188,10 @@ __global__ void __launch_bounds__(256) k_ep_push_return(EpP2PLayout L, char* con
 // early launch): a wait kernel must never start before the push it follows.
 cudaError_t launch_ep_push_dispatch(const EpP2PLayout& L, char* const* peers, const void* send_rows,
                                     const int* send_expert, const int* counts, int rank, uint32_t seq, int* ctr,
-                                    cudaStream_t st) {
+                                    cudaStream_t st, const void* X, const int* sorted, int kk) {
   k_ep_push_dispatch<<<kEpPushCtas, 256, 0, st>>>(L, peers, reinterpret_cast<const uint4*>(send_rows), send_expert,
-                                                   counts, rank, seq, ctr);
+                                                   counts, rank, seq, ctr, reinterpret_cast<const uint4*>(X), sorted,
+                                                   kk);
   return cudaGetLastError();
 }
 cudaError_t launch_ep_wait(const EpP2PLayout& L, char* base, int kind, uint32_t seq, int* err, long long budget,

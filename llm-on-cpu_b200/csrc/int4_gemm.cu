@@ -1369,7 +1369,8 @@ cudaError_t launch_gemm(int mode, int path, const GemmArgs& a, int max_work, int
 __global__ void k_combine_ep(const __nv_bfloat16* __restrict__ ret, const int* __restrict__ inverse,
                              const float* __restrict__ w, int T, int topk, int H, const float* __restrict__ sh,
                              const int* __restrict__ sh_inv, float sh_scale, const float* __restrict__ sh_w,
-                             __nv_bfloat16* __restrict__ y) {
+                             __nv_bfloat16* __restrict__ y, FlagWait fw) {
+  flag_wait_block(fw);  // every owner's return of this step has landed (bounded)
   const int t = blockIdx.y;
   const int h = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
   if (t >= T || h >= H) return;
@@ -1389,12 +1390,12 @@ __global__ void k_combine_ep(const __nv_bfloat16* __restrict__ ret, const int* _
 
 cudaError_t launch_combine_ep(const void* ret, const int* inverse, const float* w, int T, int topk, int H,
                               const float* sh, const int* sh_inv, float sh_scale, const float* sh_w, void* y,
-                              cudaStream_t st) {
+                              cudaStream_t st, const FlagWait& fw) {
   if (T <= 0) return cudaSuccess;
   const int threads = 128;
   dim3 grid(((H + 3) / 4 + threads - 1) / threads, T);
   k_combine_ep<<<grid, threads, 0, st>>>((const __nv_bfloat16*)ret, inverse, w, T, topk, H, sh, sh_inv, sh_scale,
-                                         sh_w, (__nv_bfloat16*)y);
+                                         sh_w, (__nv_bfloat16*)y, fw);
   return cudaGetLastError();
 }
 

@@ -21,6 +21,9 @@ struct TopkArgs {
   float* shared_w = nullptr;  // [T] per-token shared weights (expert-parallel source; may be null)
   int* ids;              // [T,kk]
   float* weights;        // [T,kk]
+  // expert parallelism: also each pair's owner key (e % world) * e_loc + e / world
+  int* ep_key = nullptr;  // [T,kk] (null: none)
+  int ep_world = 1, ep_e_loc = 1;
   // the token's fp16 row for the decode gate/up GEMM, made by the same warp
   // (prep_xh_row; xh null: none)
   const void* x = nullptr;  // bf16 [T][H]
@@ -29,6 +32,43 @@ struct TopkArgs {
   float* xsum = nullptr;
   float* xscale = nullptr;
 };
+
+// A bounded wait for peers' step flags, folded into the kernel that first
+// reads what they guard (the NVLink transport): threads 0..n-1 each poll
+// flags[i] with ld.acquire.sys until it reaches seq, giving up after `budget`
+// SM clocks (then bit 1 of *err is set and the kernel goes on).  Every thread
+// of the block calls flag_wait_block (it synchronises the block).
+struct FlagWait {
+  const uint32_t* flags = nullptr;  // null: no wait
+  int n = 0;
+  uint32_t seq = 0;
+  int* err = nullptr;
+  long long budget = 0;
+};
+#ifdef __CUDACC__
+__device__ __forceinline__ void flag_wait_block(const FlagWait& fw) {
+  if (!fw.flags) return;  // uniform over the block
+  __shared__ int fw_timed_out;
+  if (threadIdx.x == 0) fw_timed_out = 0;
+  __syncthreads();
+  if ((int)threadIdx.x < fw.n) {
+    const uint32_t* f = fw.flags + threadIdx.x;
+    const long long t0 = clock64();
+    for (;;) {
+      uint32_t v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+      if ((int)(v - fw.seq) >= 0) break;
+      if (clock64() - t0 > fw.budget) {
+        fw_timed_out = 1;
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  __syncthreads();
+  if (fw_timed_out && threadIdx.x == 0 && fw.err) atomicOr(fw.err, 2);
+}
+#endif
 
 struct PermArgs {
   const int* ids;   // [n] expert id per pair, n = T*kk, pair p = t*kk + j
@@ -49,6 +89,7 @@ struct PermArgs {
   // per-source receive regions
   const int* seg_count;
   int seg_stride, seg_len, n_seg;
+  FlagWait wait;    // the sources' dispatch flags, waited for before anything is read
 };
 
 constexpr int kGemmCounters = 2;  // err[1], err[2]: unit counters of the gate/up and down GEMMs
@@ -68,7 +109,11 @@ constexpr int kRouterSmallMaxT = 8;
 cudaError_t launch_router_logits(const void* X, bool x_is_f32, const uint16_t* Wr, int T, int E,
                                  int H, float* logits, cudaStream_t st, const XhOut& xo = XhOut{});
 cudaError_t launch_topk(const TopkArgs& a, cudaStream_t st);
+struct EpRouteArgs;
 cudaError_t launch_permute(const PermArgs& a, cudaStream_t st);
+// the same with the expert-parallel tail (per-owner counts, owner-local expert
+// of each pair in key order; pa.ids are the owner keys)
+cudaError_t launch_permute_ep(const PermArgs& a, const EpRouteArgs& ea, cudaStream_t st);
 // top-k and permutation in one CTA (decode-size T; pa.ids must be ta.ids, or,
 // for the expert-parallel dispatch, ea.key: the permutation then runs over the
 // owner keys, and the per-owner counts and owner-local experts are written)
@@ -81,15 +126,12 @@ struct EpRouteArgs {
 };
 cudaError_t launch_topk_permute(const TopkArgs& ta, const PermArgs& pa, cudaStream_t st,
                                 const EpRouteArgs& ea = EpRouteArgs{});
-// expert parallelism (owner of expert e = rank e % world, local id e / world)
-cudaError_t launch_ep_keys(const int* ids, int n, int world, int e_loc, int* key, cudaStream_t st);
-cudaError_t launch_ep_meta(const int* offsets, const int* sorted, const int* key, int n, int world, int e_loc,
-                           int* counts, int* send_expert, cudaStream_t st);
 cudaError_t launch_fill_i32(int* p, int n, int v, cudaStream_t st);
 // sh_w: per-token shared weights (null: sh_scale for every token)
+// fw: the owners' return flags, waited for before the returned rows are read
 cudaError_t launch_combine_ep(const void* ret, const int* inverse, const float* w, int T, int topk, int H,
                               const float* sh, const int* sh_inv, float sh_scale, const float* sh_w, void* y,
-                              cudaStream_t st);
+                              cudaStream_t st, const FlagWait& fw = FlagWait{});
 
 // ---- ep_p2p.cu: expert-parallel transport over NVLink peer memory
 constexpr int kEpMaxWorld = 64;
@@ -99,9 +141,12 @@ struct EpP2PLayout {
   int world, cap, row_bytes;  // row_bytes = hidden * 2
   size_t flags, meta, recv_ids, recv_rows, ret_rows, total;
 };
+// send_rows [q] = the q-th pair's row, or (sorted non-null) X[sorted[q] / kk]
+// read directly (no gathered copy)
 cudaError_t launch_ep_push_dispatch(const EpP2PLayout& L, char* const* peers, const void* send_rows,
                                     const int* send_expert, const int* counts, int rank, uint32_t seq, int* ctr,
-                                    cudaStream_t st);
+                                    cudaStream_t st, const void* X = nullptr, const int* sorted = nullptr,
+                                    int kk = 1);
 // budget: SM clock cycles after which a wait gives up (sets bit 1 of *err)
 constexpr long long kDefaultWaitCycles = 1ll << 31;  // ~1.1 s at 1.965 GHz
 cudaError_t launch_ep_wait(const EpP2PLayout& L, char* base, int kind, uint32_t seq, int* err, long long budget,

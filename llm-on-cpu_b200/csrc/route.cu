@@ -531,6 +531,7 @@ __device__ __forceinline__ void topk_token_q(const TopkArgs& a, int t, int lane)
     }
     if (j >= 32 && lane == (j & 31)) {  // k > 32: slots 32..63 go out now
       a.ids[(size_t)t * a.kk + j] = bi;
+      if (a.ep_key) a.ep_key[(size_t)t * a.kk + j] = (bi % a.ep_world) * a.ep_e_loc + bi / a.ep_world;
       a.weights[(size_t)t * a.kk + j] = v;  // finished below
     }
   }
@@ -544,7 +545,10 @@ __device__ __forceinline__ void topk_token_q(const TopkArgs& a, int t, int lane)
   sel[0] = my_val;
   sel[1] = lane + 32 < a.k ? w[lane + 32] : 0.f;
   __syncwarp();
-  if (lane < a.k) ids[lane] = my_id;
+  if (lane < a.k) {
+    ids[lane] = my_id;
+    if (a.ep_key) a.ep_key[(size_t)t * a.kk + lane] = (my_id % a.ep_world) * a.ep_e_loc + my_id / a.ep_world;
+  }
   if (a.router == 0) {
     double s = 0.0;
 #pragma unroll
@@ -615,6 +619,7 @@ __global__ void __launch_bounds__(256) k_topk(TopkArgs a) {
 // One CTA of kPermThreads threads.  cnt: kPermWarps x n_exp ints of shared
 // memory (counts, then running positions).
 __device__ __forceinline__ void permute_block(const PermArgs& a, int* cnt) {
+  flag_wait_block(a.wait);  // the transport's sources (their counts and rows) first
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int i = threadIdx.x; i < kPermWarps * a.n_exp; i += kPermThreads) cnt[i] = 0;
   // Index space walked: 0..nv-1.  Plain input: the slots themselves.
@@ -741,11 +746,17 @@ __device__ __forceinline__ void permute_block(const PermArgs& a, int* cnt) {
   }
 }
 
-__global__ void __launch_bounds__(kPermThreads) k_permute(PermArgs a) {
+__global__ void __launch_bounds__(kPermThreads) k_permute(PermArgs a, EpRouteArgs ea) {
   extern __shared__ int psm[];
   grid_dep_wait();
   grid_dep_release();
   permute_block(a, psm);
+  if (ea.key) {  // expert-parallel source: per-owner counts and owner-local experts in key order
+    __syncthreads();  // offsets and sorted complete
+    for (int r = threadIdx.x; r < ea.world; r += kPermThreads)
+      ea.counts[r] = a.offsets[(r + 1) * ea.e_loc] - a.offsets[r * ea.e_loc];
+    for (int q = threadIdx.x; q < a.n; q += kPermThreads) ea.send_expert[q] = ea.key[a.sorted[q]] % ea.e_loc;
+  }
 }
 
 // Decode-size batches: top-k of every token (warp w takes tokens w, w + 32,
@@ -753,8 +764,8 @@ __global__ void __launch_bounds__(kPermThreads) k_permute(PermArgs a) {
 // ids.  Shared memory: kPermWarps x n_exp ints (the permutation's counts).
 // Expert-parallel dispatch (ea.key != null): the permutation runs over the
 // owner keys (e % world) * e_loc + e / world of the ids, and the per-owner
-// counts and owner-local expert of each pair in key order follow (what
-// k_ep_keys and k_ep_meta do for larger T).
+// counts and owner-local expert of each pair in key order follow (for larger
+// T, k_topk writes the keys and k_permute adds the same tail).
 __global__ void __launch_bounds__(kPermThreads) k_topk_permute(TopkArgs ta, PermArgs pa, EpRouteArgs ea) {
   extern __shared__ int fsm[];
   grid_dep_wait();
@@ -850,13 +861,14 @@ cudaError_t launch_topk_permute(const TopkArgs& ta, const PermArgs& pa, cudaStre
   return launch_pdl(k_topk_permute, dim3(1), dim3(kPermThreads), smem, st, ta, pa, ea);
 }
 
-cudaError_t launch_permute(const PermArgs& a, cudaStream_t st) {
+cudaError_t launch_permute_ep(const PermArgs& a, const EpRouteArgs& ea, cudaStream_t st) {
   const size_t smem = (size_t)kPermWarps * a.n_exp * sizeof(int);
   cudaError_t e = cudaFuncSetAttribute(k_permute, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem);
   if (e != cudaSuccess) return e;
-  return launch_pdl(k_permute, dim3(1), dim3(kPermThreads), smem, st, a);
+  return launch_pdl(k_permute, dim3(1), dim3(kPermThreads), smem, st, a, ea);
 }
+cudaError_t launch_permute(const PermArgs& a, cudaStream_t st) { return launch_permute_ep(a, EpRouteArgs{}, st); }
 
 // ------------------------------------------------------ expert parallelism
 // Expert e is owned by rank e % world and is local expert e / world there (the
@@ -864,39 +876,10 @@ cudaError_t launch_permute(const PermArgs& a, cudaStream_t st) {
 // pairs by key = owner * e_loc + local id groups them by destination rank, in
 // the owner's local expert order.
 
-__global__ void k_ep_keys(const int* __restrict__ ids, int n, int world, int e_loc, int* __restrict__ key) {
-  for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < n; p += gridDim.x * blockDim.x) {
-    const int e = ids[p];
-    key[p] = (e % world) * e_loc + e / world;
-  }
-}
-
-// counts[r] = pairs sent to rank r; send_expert[q] = owner-local expert of the
-// q-th pair in key order
-__global__ void k_ep_meta(const int* __restrict__ offsets, const int* __restrict__ sorted,
-                          const int* __restrict__ key, int n, int world, int e_loc, int* __restrict__ counts,
-                          int* __restrict__ send_expert) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < world) counts[i] = offsets[(i + 1) * e_loc] - offsets[i * e_loc];
-  for (int q = i; q < n; q += gridDim.x * blockDim.x) send_expert[q] = key[sorted[q]] % e_loc;
-}
-
 __global__ void k_fill_i32(int* __restrict__ p, int n, int v) {
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) p[i] = v;
 }
 
-cudaError_t launch_ep_keys(const int* ids, int n, int world, int e_loc, int* key, cudaStream_t st) {
-  if (n <= 0) return cudaSuccess;
-  k_ep_keys<<<std::min((n + 255) / 256, 1184), 256, 0, st>>>(ids, n, world, e_loc, key);
-  return cudaGetLastError();
-}
-cudaError_t launch_ep_meta(const int* offsets, const int* sorted, const int* key, int n, int world, int e_loc,
-                           int* counts, int* send_expert, cudaStream_t st) {
-  const int m = std::max(n, world);
-  k_ep_meta<<<std::min((m + 255) / 256, 1184), 256, 0, st>>>(offsets, sorted, key, n, world, e_loc, counts,
-                                                            send_expert);
-  return cudaGetLastError();
-}
 cudaError_t launch_fill_i32(int* p, int n, int v, cudaStream_t st) {
   if (n <= 0) return cudaSuccess;
   k_fill_i32<<<std::min((n + 255) / 256, 1184), 256, 0, st>>>(p, n, v);

@@ -643,6 +643,7 @@ PermArgs perm_args(const int* ids, int n, int n_perm, int chunk, const WsLayout&
 struct PermSegs {
   const int* count = nullptr;
   int stride = 0, len = 0, n = 0;
+  FlagWait wait;  // the sources' flags, waited for by the permutation kernel itself
 };
 
 llmoc_status run_permute(const int* ids, int n, int n_perm, int chunk, const WsLayout& w, char* ws,
@@ -652,6 +653,7 @@ llmoc_status run_permute(const int* ids, int n, int n_perm, int chunk, const WsL
   pa.seg_stride = segs.stride;
   pa.seg_len = segs.len;
   pa.n_seg = segs.n;
+  pa.wait = segs.wait;
   if (!cuda_ok(launch_permute(pa, st), "permute")) return LLMOC_ERR_CUDA;
   count_launch(1);
   return LLMOC_OK;
@@ -1399,10 +1401,13 @@ size_t llmoc_moe_ep_owner_workspace_bytes(const llmoc_moe_layer* L, int max_rows
   return ep_owner_bytes(L, max_rows);
 }
 
-llmoc_status llmoc_moe_ep_dispatch(const llmoc_moe_layer* L, const uint16_t* X, int T, void* workspace,
-                                   size_t workspace_bytes, uint16_t* send_rows, int32_t* send_expert,
-                                   int32_t* send_counts, void* stream) {
-  if (!L || T < 0 || (T > 0 && (!X || !send_rows || !send_expert)) || !send_counts)
+namespace {
+// gather: write send_rows (the C entry point); the NVLink send passes false,
+// its push reads the tokens' rows through the sorted order instead
+llmoc_status ep_dispatch(const llmoc_moe_layer* L, const uint16_t* X, int T, void* workspace,
+                         size_t workspace_bytes, uint16_t* send_rows, int32_t* send_expert, int32_t* send_counts,
+                         void* stream, bool gather) {
+  if (!L || T < 0 || (T > 0 && (!X || (gather && !send_rows) || !send_expert)) || !send_counts)
     return fails(LLMOC_ERR_INVALID, "bad arguments");
   const EpSrcLayout w = ep_src_layout(L, T);
   if (!workspace || workspace_bytes < w.total) return fails(LLMOC_ERR_WORKSPACE, "workspace too small");
@@ -1456,18 +1461,32 @@ llmoc_status llmoc_moe_ep_dispatch(const llmoc_moe_layer* L, const uint16_t* X, 
     ea.send_expert = send_expert;
     if (!cuda_ok(launch_topk_permute(ta, pa, st, ea), "topk+permute")) return LLMOC_ERR_CUDA;
     count_launch(2);
-  } else {
-    if (!cuda_ok(launch_topk(ta, st), "topk") ||
-        !cuda_ok(launch_ep_keys(ta.ids, n, L->ep_world, L->e_loc, key, st), "ep keys") ||
-        !cuda_ok(launch_permute(pa, st), "permute") ||
-        !cuda_ok(launch_ep_meta(pa.offsets, pa.sorted, key, n, L->ep_world, L->e_loc, send_counts, send_expert, st),
-                 "ep meta"))
+  } else {  // top-k writing the owner keys too; the permutation with the per-owner tail
+    ta.ep_key = key;
+    ta.ep_world = L->ep_world;
+    ta.ep_e_loc = L->e_loc;
+    EpRouteArgs ea;
+    ea.world = L->ep_world;
+    ea.e_loc = L->e_loc;
+    ea.key = key;
+    ea.counts = send_counts;
+    ea.send_expert = send_expert;
+    if (!cuda_ok(launch_topk(ta, st), "topk") || !cuda_ok(launch_permute_ep(pa, ea, st), "permute"))
       return LLMOC_ERR_CUDA;
-    count_launch(5);
+    count_launch(3);
   }
-  if (!cuda_ok(launch_gather_rows(X, H, pa.sorted, k, n, nullptr, send_rows, st), "gather")) return LLMOC_ERR_CUDA;
-  count_launch(1);
+  if (gather) {
+    if (!cuda_ok(launch_gather_rows(X, H, pa.sorted, k, n, nullptr, send_rows, st), "gather")) return LLMOC_ERR_CUDA;
+    count_launch(1);
+  }
   return LLMOC_OK;
+}
+}  // namespace
+
+llmoc_status llmoc_moe_ep_dispatch(const llmoc_moe_layer* L, const uint16_t* X, int T, void* workspace,
+                                   size_t workspace_bytes, uint16_t* send_rows, int32_t* send_expert,
+                                   int32_t* send_counts, void* stream) {
+  return ep_dispatch(L, X, T, workspace, workspace_bytes, send_rows, send_expert, send_counts, stream, true);
 }
 
 namespace {
@@ -1522,7 +1541,7 @@ llmoc_status ep_shared(const llmoc_moe_layer* L, const uint16_t* X, int T, const
 }
 // Y = the routed weights x the returned rows (slot order) + the shared expert's rows.
 llmoc_status ep_combine_rows(const llmoc_moe_layer* L, int T, const uint16_t* ret_rows, uint16_t* Y,
-                             const EpSrcLayout& w, char* ws, cudaStream_t st) {
+                             const EpSrcLayout& w, char* ws, cudaStream_t st, const FlagWait& fw = FlagWait{}) {
   const float* sh = nullptr;
   const int* sh_inv = nullptr;
   if (L->d.has_shared) {
@@ -1531,7 +1550,7 @@ llmoc_status ep_combine_rows(const llmoc_moe_layer* L, int T, const uint16_t* re
   }
   if (!cuda_ok(launch_combine_ep(ret_rows, (const int*)(ws + w.inverse), (const float*)(ws + w.weights), T,
                                  L->d.topk, L->d.hidden, sh, sh_inv, L->d.shared_scale,
-                                 L->shared_gate ? (const float*)(ws + w.shw) : nullptr, Y, st),
+                                 L->shared_gate ? (const float*)(ws + w.shw) : nullptr, Y, st, fw),
                "combine"))
     return LLMOC_ERR_CUDA;
   count_launch(1);
@@ -1982,12 +2001,14 @@ llmoc_status llmoc_ep_p2p_send(const llmoc_moe_layer* L, llmoc_ep_transport* tr,
   if (T > 0 && !X) return fails(LLMOC_ERR_INVALID, "bad arguments");
   const EpP2PWs w = ep_p2p_ws(L, tr, T);
   char* ws = (char*)workspace;
-  rc = llmoc_moe_ep_dispatch(L, X, T, ws + w.src, w.sw.total, (uint16_t*)(ws + w.send_rows),
-                             (int32_t*)(ws + w.send_expert), (int32_t*)(ws + w.counts), stream);
+  rc = ep_dispatch(L, X, T, ws + w.src, w.sw.total, nullptr, (int32_t*)(ws + w.send_expert),
+                   (int32_t*)(ws + w.counts), stream, false);
   if (rc != LLMOC_OK) return rc;
   DevGuard dg(L->device);
-  if (!cuda_ok(launch_ep_push_dispatch(tr->lay, tr->peers_dev, ws + w.send_rows, (const int*)(ws + w.send_expert),
-                                       (const int*)(ws + w.counts), tr->rank, seq, tr->ctr, (cudaStream_t)stream),
+  // the push reads each routed pair's token row through the dispatch's sorted order
+  if (!cuda_ok(launch_ep_push_dispatch(tr->lay, tr->peers_dev, nullptr, (const int*)(ws + w.send_expert),
+                                       (const int*)(ws + w.counts), tr->rank, seq, tr->ctr, (cudaStream_t)stream, X,
+                                       (const int*)(ws + w.src + w.sw.sorted), L->d.topk),
                "ep push"))
     return LLMOC_ERR_CUDA;
   count_launch(1);
@@ -2003,8 +2024,6 @@ llmoc_status llmoc_ep_p2p_serve(const llmoc_moe_layer* L, llmoc_ep_transport* tr
   char* ws = (char*)workspace;
   cudaStream_t st = (cudaStream_t)stream;
   DevGuard dg(L->device);
-  if (!cuda_ok(launch_ep_wait(tr->lay, tr->base, 0, seq, tr->err, tr->wait_cycles, st), "ep wait")) return LLMOC_ERR_CUDA;
-  count_launch(1);
   const int parity = seq & 1, slots = tr->world * tr->lay.cap;
   const uint16_t* rows =
       (const uint16_t*)(tr->base + tr->lay.recv_rows + (size_t)parity * slots * tr->lay.row_bytes);
@@ -2018,6 +2037,12 @@ llmoc_status llmoc_ep_p2p_serve(const llmoc_moe_layer* L, llmoc_ep_transport* tr
   segs.stride = 2;
   segs.len = tr->lay.cap;
   segs.n = tr->world;
+  // the wait for every source's dispatch flag runs inside the permutation kernel
+  segs.wait.flags = (const uint32_t*)(tr->base + tr->lay.flags);
+  segs.wait.n = tr->world;
+  segs.wait.seq = seq;
+  segs.wait.err = tr->err;
+  segs.wait.budget = tr->wait_cycles;
   rc = ep_experts(L, rows, ids, slots, n_hint, nullptr, ws + w.own, ep_owner_bytes(L, slots), stream, segs);
   if (rc != LLMOC_OK) return rc;
   const WsLayout wo = ws_layout_g(L, slots, 1, L->n_exp, chunk_for_rows(n_hint, L->e_loc), false);
@@ -2037,12 +2062,22 @@ llmoc_status llmoc_ep_p2p_finish(const llmoc_moe_layer* L, llmoc_ep_transport* t
   const EpP2PWs w = ep_p2p_ws(L, tr, T);
   char* ws = (char*)workspace;
   DevGuard dg(L->device);
-  if (!cuda_ok(launch_ep_wait(tr->lay, tr->base, 1, seq, tr->err, tr->wait_cycles, (cudaStream_t)stream), "ep wait back"))
-    return LLMOC_ERR_CUDA;
-  count_launch(1);
   const uint16_t* ret = (const uint16_t*)(tr->base + tr->lay.ret_rows + (size_t)(seq & 1) * tr->lay.cap * tr->lay.row_bytes);
-  if (T == 0) return LLMOC_OK;
-  return ep_combine_rows(L, T, ret, Y, w.sw, ws + w.src, (cudaStream_t)stream);
+  // the wait for every owner's return flag runs inside the combine kernel
+  FlagWait fw;
+  fw.flags = (const uint32_t*)(tr->base + tr->lay.flags) + tr->world;  // kind 1: returns
+  fw.n = tr->world;
+  fw.seq = seq;
+  fw.err = tr->err;
+  fw.budget = tr->wait_cycles;
+  if (T == 0) {  // nothing to combine; the return flags are still waited for (the step's parity is reused)
+    if (!cuda_ok(launch_ep_wait(tr->lay, tr->base, 1, seq, tr->err, tr->wait_cycles, (cudaStream_t)stream),
+                 "ep wait back"))
+      return LLMOC_ERR_CUDA;
+    count_launch(1);
+    return LLMOC_OK;
+  }
+  return ep_combine_rows(L, T, ret, Y, w.sw, ws + w.src, (cudaStream_t)stream, fw);
 }
 
 }  // extern "C"

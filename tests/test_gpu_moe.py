@@ -115,17 +115,19 @@ def test_routing_bit_exact(oracle, name, T):
     dl.close()
 
 
-@pytest.mark.parametrize("T,E", [(3, 40), (77, 40), (20, 70), (150, 40), (800, 40), (2400, 40)])
-def test_router_tiles_bit_exact(oracle, T, E):
+@pytest.mark.parametrize("T,E,H", [(3, 40, 768), (77, 40, 768), (20, 70, 768), (77, 40, 1024), (150, 40, 768),
+                                   (800, 40, 768), (2400, 40, 768)])
+def test_router_tiles_bit_exact(oracle, T, E, H):
     """Router logits of every token bitwise equal to the reference's AVX2 order
     on each tile shape (T <= 8: one CTA per expert row; 8 < T < 128: 8 x 16
-    tiles, T = 77 and, with a partial expert tile, E = 70 at T = 20; T >= 128:
+    tiles, T = 77 and, with a partial expert tile, E = 70 at T = 20, and with
+    1024-wide K chunks at H = 1024; T >= 128:
     8 x 16, 16 x 16 and 32 x 32 tiles as the grid grows, T = 150, 800, 2400),
     with partial token and expert tiles (T not a multiple of 32) and a
     non-finite activation (that token's logits become 0, as in the reference)."""
     rng = np.random.default_rng(40 + T)
-    layer = orc.make_layer(oracle, rng, H=768, I=128, E=E, topk=4, gs=128)
-    X = orc.make_tokens(rng, T, 768)
+    layer = orc.make_layer(oracle, rng, H=H, I=128, E=E, topk=4, gs=128)
+    X = orc.make_tokens(rng, T, H)
     X[T // 2, 5] = np.inf
     dl = G.DevLayer(layer, T)
     _, ws_bytes = dl.forward(X)
