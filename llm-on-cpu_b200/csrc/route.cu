@@ -616,12 +616,17 @@ __global__ void __launch_bounds__(256) k_topk(TopkArgs a) {
 
 // ----------------------------------------------------------- permutation
 
-// One CTA of kPermThreads threads.  cnt: kPermWarps x n_exp ints of shared
-// memory (counts, then running positions).
+// One CTA of kPermThreads threads.  The pairs are counted and placed in NW
+// ranges, one per warp 0..NW-1 (NW <= kPermWarps: fewer ranges make the
+// per-expert loops and the counters NW long, which pays when there are few
+// pairs; the result is the same, pairs of an expert in ascending order).
+// cnt: NW x n_exp ints of shared memory (counts, then running positions).
+template <int NW>
 __device__ __forceinline__ void permute_block(const PermArgs& a, int* cnt) {
+  static_assert(NW >= 1 && NW <= kPermWarps, "counting ranges");
   flag_wait_block(a.wait);  // the transport's sources (their counts and rows) first
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int i = threadIdx.x; i < kPermWarps * a.n_exp; i += kPermThreads) cnt[i] = 0;
+  for (int i = threadIdx.x; i < NW * a.n_exp; i += kPermThreads) cnt[i] = 0;
   // Index space walked: 0..nv-1.  Plain input: the slots themselves.
   // Segmented input: the occupied slots of each segment, segment after
   // segment (slot order), v -> slot via the segments' exclusive offsets.
@@ -644,8 +649,8 @@ __device__ __forceinline__ void permute_block(const PermArgs& a, int* cnt) {
     return s * a.seg_len + (v - seg_off[s]);
   };
 
-  const int per = (nv + kPermWarps - 1) / kPermWarps;
-  const int lo = min(nv, warp * per), hi = min(nv, lo + per);
+  const int per = (nv + NW - 1) / NW;
+  const int lo = min(nv, warp * per), hi = min(nv, lo + per);  // empty for warps >= NW
   // ids outside [0, n_exp) are empty slots (the padded receive layout of the
   // NVLink expert-parallel transport): not counted, not placed, inverse -1
   for (int v = lo + lane; v < hi; v += 32) {
@@ -659,7 +664,7 @@ __device__ __forceinline__ void permute_block(const PermArgs& a, int* cnt) {
   const int e = threadIdx.x;
   int tot = 0;
   if (e < a.n_exp)
-    for (int w = 0; w < kPermWarps; ++w) tot += cnt[w * a.n_exp + e];
+    for (int w = 0; w < NW; ++w) tot += cnt[w * a.n_exp + e];
   const int chunks = (tot + a.chunk - 1) / a.chunk;
   // block exclusive scan of (tot, chunks, active) packed: do two scans
   int v1 = tot, v2 = chunks, v3 = tot > 0;
@@ -702,7 +707,7 @@ __device__ __forceinline__ void permute_block(const PermArgs& a, int* cnt) {
   if (e < a.n_exp) {
     a.offsets[e] = base1;
     int run = base1;
-    for (int w = 0; w < kPermWarps; ++w) {
+    for (int w = 0; w < NW; ++w) {
       const int c = cnt[w * a.n_exp + e];
       cnt[w * a.n_exp + e] = run;
       run += c;
@@ -750,7 +755,7 @@ __global__ void __launch_bounds__(kPermThreads) k_permute(PermArgs a, EpRouteArg
   extern __shared__ int psm[];
   grid_dep_wait();
   grid_dep_release();
-  permute_block(a, psm);
+  permute_block<kPermWarps>(a, psm);
   if (ea.key) {  // expert-parallel source: per-owner counts and owner-local experts in key order
     __syncthreads();  // offsets and sorted complete
     for (int r = threadIdx.x; r < ea.world; r += kPermThreads)
@@ -761,11 +766,13 @@ __global__ void __launch_bounds__(kPermThreads) k_permute(PermArgs a, EpRouteArg
 
 // Decode-size batches: top-k of every token (warp w takes tokens w, w + 32,
 // ...) and the permutation in one CTA, saving a launch and a pass over the
-// ids.  Shared memory: kPermWarps x n_exp ints (the permutation's counts).
+// ids.  Shared memory: kFusedPermRanges x n_exp ints (the permutation's
+// counts: at most kFusedRouteMaxT * 65 pairs, counted in 4 ranges).
 // Expert-parallel dispatch (ea.key != null): the permutation runs over the
 // owner keys (e % world) * e_loc + e / world of the ids, and the per-owner
 // counts and owner-local expert of each pair in key order follow (for larger
 // T, k_topk writes the keys and k_permute adds the same tail).
+constexpr int kFusedPermRanges = 4;
 __global__ void __launch_bounds__(kPermThreads) k_topk_permute(TopkArgs ta, PermArgs pa, EpRouteArgs ea) {
   extern __shared__ int fsm[];
   grid_dep_wait();
@@ -780,7 +787,7 @@ __global__ void __launch_bounds__(kPermThreads) k_topk_permute(TopkArgs ta, Perm
     }
     __syncthreads();
   }
-  permute_block(pa, fsm);
+  permute_block<kFusedPermRanges>(pa, fsm);
   if (ea.key) {
     __syncthreads();  // offsets and sorted complete
     for (int r = threadIdx.x; r < ea.world; r += kPermThreads)
@@ -855,7 +862,7 @@ cudaError_t launch_topk(const TopkArgs& a, cudaStream_t st) {
 
 cudaError_t launch_topk_permute(const TopkArgs& ta, const PermArgs& pa, cudaStream_t st, const EpRouteArgs& ea) {
   if (ta.E > 32 * kTopkSlots || ta.k > 64) return cudaErrorInvalidValue;
-  const size_t smem = (size_t)kPermWarps * pa.n_exp * sizeof(int);
+  const size_t smem = (size_t)kFusedPermRanges * pa.n_exp * sizeof(int);
   cudaError_t e = cudaFuncSetAttribute(k_topk_permute, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   return launch_pdl(k_topk_permute, dim3(1), dim3(kPermThreads), smem, st, ta, pa, ea);
