@@ -967,14 +967,19 @@ def run_ep(args):
             step(i, T)
         torch.cuda.synchronize()
         if T == args.tokens:
+            # ~1.5 s of back-to-back steps for the clock samples.  Every rank
+            # runs the same number of steps (a count agreed from one timed
+            # batch, max over ranks): a rank that ran ahead would wait on
+            # sequence flags its peers never raise until its budget ran out.
             clocks.start()
-            t_end = time.perf_counter() + 1.5
-            i = 0
-            while time.perf_counter() < t_end:
-                for _ in range(10):
-                    step(i, T)
-                    i += 1
-                torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            for i in range(10):
+                step(i, T)
+            torch.cuda.synchronize()
+            batches = int(np.ceil(1.5 / max(max_over_ranks(time.perf_counter() - t0), 1e-4)))
+            for i in range(10, 10 * batches):
+                step(i, T)
+            torch.cuda.synchronize()
             n0 = L.launch_count()
         ms = timed(T, args.steps, step)
         if T == args.tokens:

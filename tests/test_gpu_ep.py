@@ -202,6 +202,22 @@ def test_p2p_transport_two_ranks_one_gpu(oracle, name, T):
             assert torch.equal(outs[k][r], outs[0][r]), (name, T, r, k)
 
 
+@pytest.mark.parametrize("name", ["qwen_like", "glm_like_shared_sigmoid"])
+@pytest.mark.parametrize("T", [5, 40])
+def test_p2p_transport_four_ranks_one_gpu(oracle, name, T):
+    """world = 4 through the NVLink transport in one process (sends, then
+    serves, then finishes, one stream): T = 5 takes the one-CTA routing of the
+    dispatch, T = 40 the top-k kernel writing the owner keys and the
+    permutation with the per-owner tail."""
+    layer = orc.make_layer(oracle, np.random.default_rng(6), **CFGS[name])
+    Xh = [orc.make_tokens(np.random.default_rng(80 + r), T + r, layer.H) for r in range(4)]
+    outs, errs = _p2p_emulated(layer, 4, [G.bf16_dev(X) for X in Xh], 2)
+    assert errs == [0, 0, 0, 0]
+    for r in range(4):
+        _check(outs[0][r], oracle.moe_layer_forward(layer, Xh[r])[0], (name, T, r))
+        assert torch.equal(outs[1][r], outs[0][r]), (name, T, r)
+
+
 def test_p2p_transport_skewed_to_one_owner(oracle):
     """Every routed slot lands on rank 0's experts (a selection bias of -16 on
     the odd ones): rank 0 serves twice the rows that its own tokens x topk
