@@ -264,11 +264,20 @@ LLMOC_API llmoc_status llmoc_moe_route(const llmoc_moe_layer* layer, const uint1
 LLMOC_API llmoc_status llmoc_moe_dequant(const llmoc_moe_layer* layer, int expert, int proj, float* out,
                                void* stream);
 
+/* Budget, in SM clocks, of each grid-wide barrier wait inside the fused
+ * single-token forward (T = 1: the router, top-k, both GEMMs and the combine
+ * in one launch).  A wait that runs out sets bit 2 (value 4) of the
+ * workspace's error word (llmoc_route_views.error_flag) and the launch goes
+ * on, its outputs then invalid; the next forward starts clean.  Default 2^31
+ * (about a second).  No reference counterpart (its decode is host-driven). */
+LLMOC_API llmoc_status llmoc_moe_layer_set_wait_cycles(llmoc_moe_layer* layer, long long cycles);
+
 /* Per-stage CUDA-event timing of llmoc_moe_forward (the reference only keeps
  * wall-clock accumulators, src/hal/cuda_backend.cpp:285-288, :5347-5357).
  * While enabled, every forward records events around its six stages on its
  * stream: 0 router GEMV, 1 top-k, 2 permutation, 3 gate/up + SiLU*mul,
- * 4 down, 5 combine.  llmoc_moe_stage_times synchronizes on the recorded
+ * 4 down, 5 combine (a forward of one token runs as one launch, reported
+ * under stage 3).  llmoc_moe_stage_times synchronizes on the recorded
  * events, writes the summed milliseconds per stage into ms[6] and the number
  * of timed calls into *calls, and clears the record.  Disabling also clears. */
 LLMOC_API llmoc_status llmoc_moe_set_stage_timing(llmoc_moe_layer* layer, int enable);

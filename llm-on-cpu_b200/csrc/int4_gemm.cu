@@ -20,6 +20,7 @@
 #include <algorithm>
 
 #include "kernels.cuh"
+#include "route_dev.cuh"
 
 namespace llmoc {
 
@@ -211,6 +212,19 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
                "l"(src)
                : "memory");
 }
+// The same with an L2 cache policy (evict_first for weights streamed once per
+// forward: they leave the code, the router rows and the activations in L2).
+__device__ __forceinline__ void cp_async16_pol(void* dst, const void* src, unsigned long long pol) {
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+               "l"(src), "l"(pol)
+               : "memory");
+}
+__device__ __forceinline__ unsigned long long l2_evict_first() {
+  unsigned long long pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
@@ -232,17 +246,22 @@ __device__ __forceinline__ float f16_group(float P, float xs, int hi, float bias
 }
 
 // XH: the fp16 activation path of k_int4_mma_p (gate/up only, NT = 1).
+// One CTA's share of k_int4_mma: row-tile block bx (kWarps / ks tiles) of the
+// work items by, by + gy, ...; wsm = the CTA's kWarps stage rings.  Also the
+// GEMM phases of the fused single-token kernel (k_moe_decode1), which walks a
+// virtual grid of such blocks.
 template <int MODE, int NT, int GSB, bool AWQ, bool XH>
-__global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
+__device__ __forceinline__ void mma_kblock(const GemmArgs& a, int ks, int bx, int by, int gy,
+                                           unsigned char* wsm) {
   constexpr int NP = MODE == MODE_GATE_UP ? 2 : 1;
   constexpr int NG = GSB == 4 ? 1 : (GSB == 2 ? 2 : 4);  // groups per step
   static_assert(!XH || (MODE == MODE_GATE_UP && NT == 1), "fp16 activations: gate/up, 8-row items");
   using SG = WStage<NP, NT, AWQ, XH>;
-  extern __shared__ __align__(128) unsigned char wsm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int slice = warp % ks;
-  const int rt = blockIdx.x * (kWarps / ks) + warp / ks;
+  const int rt = bx * (kWarps / ks) + warp / ks;
+  const unsigned long long wpol = l2_evict_first();  // the weights: read once per forward
   // launched with programmatic dependent launch: gate/up waits for its
   // predecessor before reading the work list; the down GEMM (whose
   // predecessor, gate/up, only released it after waiting for the kernel that
@@ -252,13 +271,13 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
     grid_dep_wait();
     grid_dep_release();
   }
-  // work items blockIdx.y, blockIdx.y + gridDim.y, ... (the grid is sized to
+  // work items by, by + gy, ... (the grid is sized to
   // the expected items, the loop covers the work list whatever its length)
   const int Mt = (a.M + 15) >> 4;
   const bool live = rt < Mt;
   const int n_items = *a.n_work;
   bool waited = MODE == MODE_GATE_UP;
-  for (int item = blockIdx.y; item < n_items; item += gridDim.y) {
+  for (int item = by; item < n_items; item += gy) {
     const WorkItem it = a.work[item];
     const ExpertDev& ex = a.experts[it.expert];
     const ProjDev* P[2];
@@ -316,11 +335,11 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
       unsigned char* sb = wbase + stage * SG::kBytes;
 #pragma unroll
       for (int p = 0; p < NP; ++p) {
-        cp_async16(sb + p * 1024 + lane * 16, wsrc[p]);
-        cp_async16(sb + p * 1024 + 512 + lane * 16, wsrc[p] + 512);
+        cp_async16_pol(sb + p * 1024 + lane * 16, wsrc[p], wpol);
+        cp_async16_pol(sb + p * 1024 + 512 + lane * 16, wsrc[p] + 512, wpol);
         wsrc[p] += 1024;
-        if (lane < NG * 2) cp_async16(sb + SG::kW + p * 128 + lane * 16, ssrc[p] + lane * 16);
-        if (!AWQ && lane < NG * 2) cp_async16(sb + SG::kW + SG::kS + p * 128 + lane * 16, zsrc[p] + lane * 16);
+        if (lane < NG * 2) cp_async16_pol(sb + SG::kW + p * 128 + lane * 16, ssrc[p] + lane * 16, wpol);
+        if (!AWQ && lane < NG * 2) cp_async16_pol(sb + SG::kW + SG::kS + p * 128 + lane * 16, zsrc[p] + lane * 16, wpol);
         ssrc[p] += NG * 32;
         if (!AWQ) zsrc[p] += NG * 32;
       }
@@ -529,6 +548,12 @@ __global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
     }
     if (ks > 1) __syncthreads();  // the next item's copies reuse the reduction slots
   }
+}
+
+template <int MODE, int NT, int GSB, bool AWQ, bool XH>
+__global__ void __launch_bounds__(kWarps * 32) k_int4_mma(GemmArgs a, int ks) {
+  extern __shared__ __align__(128) unsigned char wsm[];
+  mma_kblock<MODE, NT, GSB, AWQ, XH>(a, ks, blockIdx.x, blockIdx.y, gridDim.y, wsm);
 }
 
 // Persistent form of k_int4_mma for decode-size items (NT = 1: at most 8 rows
@@ -1194,6 +1219,360 @@ __global__ void __launch_bounds__(256) k_combine(const float* __restrict__ d, co
           if (i < nh) ap[i] = __fadd_rn(__bfloat162float(res[o + i]), ap[i]);
       combine_store(y, o, ap, nh);
     }
+  }
+}
+
+// ------------------------------------------- fused single-token decode
+
+// Tag of barrier b of the launch with this epoch (splitmix64's finaliser over
+// epoch * 4 + b): neither an older launch's words nor the bytes of an
+// uninitialised workspace equal it except by a 2^-64 accident, so the barrier
+// words need no reset between launches.
+__device__ __forceinline__ unsigned long long decode1_tag(unsigned long long epoch, int b) {
+  unsigned long long x = epoch * 4ull + (unsigned long long)b + 0x9E3779B97F4A7C15ull;
+  x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+  x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+  return x ^ (x >> 31);
+}
+__device__ __forceinline__ void st_release_gpu_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_gpu_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Grid-wide barrier b of k_moe_decode1 (b = 0, 1, 2): an arrival counter at
+// a.bar[0] (its low 32 bits), zeroed by CTA 0 at the kernel's start, which
+// then publishes the launch's tag in a.bar[1]; a CTA checks that tag once
+// before its first arrival (so no arrival lands before the reset), then
+// every barrier is one release-add and a poll until the count reaches
+// (b + 1) * gridDim.x.  Each wait gives up after a.budget SM clocks: bit 2 of
+// *a.err is set and the kernel goes on (its outputs are then invalid), so a
+// launch never waits without end.  All threads of every CTA call it.
+__device__ __forceinline__ void decode1_barrier(const Decode1Args& a, int b) {
+  __syncthreads();  // the CTA's writes of this phase are issued
+  if (threadIdx.x == 0) {
+    bool timed_out = false;
+    unsigned int* ctr = reinterpret_cast<unsigned int*>(a.bar);
+    if (b == 0) {
+      const unsigned long long tag = decode1_tag(a.epoch, 0);
+      const long long t0 = clock64();
+      while (ld_acquire_gpu_u64(a.bar + 1) != tag) {
+        if (clock64() - t0 > a.budget) {
+          timed_out = true;
+          break;
+        }
+        __nanosleep(32);
+      }
+    }
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(ctr), "r"(1u) : "memory");
+    const unsigned int target = (unsigned int)(b + 1) * gridDim.x;
+    const long long t0 = clock64();
+    for (;;) {
+      unsigned int v;
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
+      if (v >= target) break;
+      if (clock64() - t0 > a.budget) {
+        timed_out = true;
+        break;
+      }
+      __nanosleep(32);
+    }
+    if (timed_out) atomicOr(a.err, 4);
+  }
+  __syncthreads();
+}
+
+// Bulk L2 prefetch of [p, p + bytes) (16-byte aligned, a multiple of 16),
+// evict_first like the copies that will read it.
+__device__ __forceinline__ void prefetch_l2(const void* p, unsigned int bytes, unsigned long long pol) {
+  asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(p), "r"(bytes), "l"(pol)
+               : "memory");
+}
+
+// The weights, scales (and zeros) one mma_kblock block (bx, expert) will
+// read, prefetched into L2 by the calling thread: its kWarps / ks row tiles
+// are consecutive, so each part of each projection is one contiguous range.
+template <int MODE>
+__device__ __forceinline__ void prefetch_kblock(const GemmArgs& a, int ks, int bx, int expert) {
+  const ExpertDev& ex = a.experts[expert];
+  const int tpb = kWarps / ks, Mt = (a.M + 15) >> 4;
+  const int r0 = bx * tpb, r1 = min(Mt, r0 + tpb);
+  if (r0 >= r1) return;
+  const unsigned long long pol = l2_evict_first();
+#pragma unroll
+  for (int p = 0; p < (MODE == MODE_GATE_UP ? 2 : 1); ++p) {
+    const ProjDev& P = MODE == MODE_GATE_UP ? (p ? ex.up : ex.gate) : pick(ex, a.proj);
+    prefetch_l2(P.q + (size_t)r0 * a.Kc * 32, (unsigned int)((r1 - r0) * a.Kc * 512), pol);
+    prefetch_l2(P.s + (size_t)r0 * a.ng * 16, (unsigned int)((r1 - r0) * a.ng * 32), pol);
+    if (P.z) prefetch_l2(P.z + (size_t)r0 * a.ng * 16, (unsigned int)((r1 - r0) * a.ng * 32), pol);
+  }
+}
+
+// One token through the whole layer in one cooperative launch (T = 1 decode:
+// the chain of separate kernels is bound by its launch boundaries, not its
+// bytes).  Phases, split by decode1_barrier:
+//   1. router rows r = blockIdx.x, + gridDim.x, ...: W_r row r and the token
+//      in shared memory, one warp's ordered FMA chains (router_dot_warp, the
+//      arithmetic of k_router_small); the sigmoid router's score of the row
+//      too (sigmoid_ref: its double arithmetic once per row, in parallel).
+//   2. every CTA: the token's top-k from the logits (topk_token, the same
+//      bits in every CTA) into shared memory; slot j becomes work item j (one
+//      row of expert ids[j]); CTA 0 writes the routing views (ids, weights,
+//      the canonical offsets / sorted / inverse of one token).
+//   3. gate/up + SiLU*mul: the blocks of k_int4_mma's grid (gx_gu x kk) dealt
+//      round-robin to the CTAs, each run by mma_kblock on the bf16 token row;
+//      each block's weights are prefetched into L2 one block ahead.
+//   4. down: the same over the gate/up rows (gx_dn x kk blocks); a CTA's
+//      first down block is prefetched before the barrier.
+//   5. combine: y = sum_j w_j * partial_j in slot order (k_combine's fmaf
+//      order), + the residual, to bf16.
+template <int GSB, bool AWQ>
+__global__ void __launch_bounds__(kWarps * 32) k_moe_decode1(Decode1Args a) {
+  extern __shared__ __align__(128) unsigned char wsm[];
+  __shared__ WorkItem s_work[kDecode1MaxSlots];
+  __shared__ int s_ids[kDecode1MaxSlots];
+  __shared__ float s_w[kDecode1MaxSlots];
+  __shared__ int s_nwork;
+  // slot j's expert (work item j names slot j), after the GEMM rings
+  ExpertDev* s_ex = reinterpret_cast<ExpertDev*>(wsm + a.ex_off);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int H = a.H, kk = a.ta.kk;
+  grid_dep_wait();  // the token row is the predecessor's output
+  grid_dep_release();
+  if (blockIdx.x == 0 && threadIdx.x == 0) {  // the barrier's counter, then the launch's tag
+    *a.err = 0;
+    *reinterpret_cast<unsigned int*>(a.bar) = 0;
+    __threadfence();
+    st_release_gpu_u64(a.bar + 1, decode1_tag(a.epoch, 0));
+  }
+
+  // 1. router rows (and the sigmoid router's scores)
+  {
+    const uint16_t* sw = reinterpret_cast<const uint16_t*>(wsm);
+    const uint16_t* sx = sw + H;
+    const int n8 = H / 8;
+    for (int r = blockIdx.x; r < a.rows; r += gridDim.x) {
+      for (int i = threadIdx.x; i < 2 * n8; i += blockDim.x) {
+        const uint4* src = i < n8 ? reinterpret_cast<const uint4*>(a.Wr + (size_t)r * H) + i
+                                  : reinterpret_cast<const uint4*>(a.X) + (i - n8);
+        reinterpret_cast<uint4*>(wsm)[i] = __ldg(src);
+      }
+      __syncthreads();
+      if (warp == 0) {
+        const float v = router_dot_warp(sw, sx, H, lane);
+        if (lane == 0) {
+          a.logits[r] = v;
+          if (a.sig && r < a.ta.E) a.sig[r] = sigmoid_ref(v);
+        }
+      }
+      __syncthreads();  // the staging is rewritten by the next row
+    }
+  }
+  decode1_barrier(a, 0);
+
+  // 2. top-k and the work list (every CTA), the routing views (CTA 0)
+  if (warp == 0) {
+    TopkArgs ta = a.ta;
+    ta.ids = s_ids;
+    ta.weights = s_w;
+    ta.ep_key = nullptr;
+    ta.shared_w = nullptr;
+    topk_token(ta, 0, lane);
+  }
+  __syncthreads();
+  if ((int)threadIdx.x < kk) {
+    const int j = threadIdx.x;
+    s_ex[j] = a.gu.experts[s_ids[j]];
+    WorkItem it;
+    it.expert = j;  // into s_ex
+    it.row0 = j;
+    it.nrows = 1;
+    it.pad = 0;
+    s_work[j] = it;
+  }
+  if (threadIdx.x == 0) s_nwork = kk;
+  __shared__ int s_active;
+  if (threadIdx.x == 0) s_active = 0;
+  __syncthreads();
+  if (blockIdx.x == 0) {
+    for (int j = threadIdx.x; j < kk; j += blockDim.x) {
+      const int e = s_ids[j];
+      int rank = 0;
+      bool first = true;
+      for (int i = 0; i < kk; ++i) {
+        rank += s_ids[i] < e || (s_ids[i] == e && i < j);
+        first = first && !(s_ids[i] == e && i < j);
+      }
+      a.ta.ids[j] = e;
+      a.ta.weights[j] = s_w[j];
+      a.sorted[rank] = j;
+      a.inverse[j] = rank;
+      if (first) atomicAdd(&s_active, 1);
+    }
+    for (int e = threadIdx.x; e <= a.n_exp; e += blockDim.x) {
+      int c = 0;
+      for (int i = 0; i < kk; ++i) c += s_ids[i] < e;
+      a.offsets[e] = c;
+    }
+  }
+  __syncthreads();
+  if (blockIdx.x == 0 && threadIdx.x == 0) *a.n_active = s_active;
+
+  // 3. gate/up + SiLU*mul
+  {
+    GemmArgs g = a.gu;
+    g.experts = s_ex;
+    g.work = s_work;
+    g.n_work = &s_nwork;
+    g.gather = nullptr;
+    g.ldb = 0;  // every slot reads the token's row
+    GemmArgs dpf = a.dn;  // the down phase's blocks, for prefetching
+    dpf.experts = s_ex;
+    const int nvb = a.gx_gu * kk, nvb_dn = a.gx_dn * kk;
+    // each block's weights go to L2 one block ahead of its ring of copies
+    if (threadIdx.x == 0 && (int)blockIdx.x < nvb)
+      prefetch_kblock<MODE_GATE_UP>(g, a.ks_gu, blockIdx.x % a.gx_gu, blockIdx.x / a.gx_gu);
+    // CTAs without a gate/up block fetch the down weights meanwhile (all of
+    // them, dealt over these CTAs)
+    if (threadIdx.x == 0 && (int)blockIdx.x >= nvb)
+      for (int vb = blockIdx.x - nvb; vb < nvb_dn; vb += gridDim.x - nvb)
+        prefetch_kblock<MODE_PLAIN_F32>(dpf, a.ks_dn, vb % a.gx_dn, vb / a.gx_dn);
+    for (int vb = blockIdx.x; vb < nvb; vb += gridDim.x) {
+      const int nx = vb + gridDim.x;
+      if (threadIdx.x == 0 && nx < nvb) prefetch_kblock<MODE_GATE_UP>(g, a.ks_gu, nx % a.gx_gu, nx / a.gx_gu);
+      mma_kblock<MODE_GATE_UP, 1, GSB, AWQ, false>(g, a.ks_gu, vb % a.gx_gu, vb / a.gx_gu, kk, wsm);
+    }
+    // else the CTA's first down block, while the others finish gate/up
+    if (threadIdx.x == 0 && nvb >= (int)gridDim.x && (int)blockIdx.x < nvb_dn)
+      prefetch_kblock<MODE_PLAIN_F32>(dpf, a.ks_dn, blockIdx.x % a.gx_dn, blockIdx.x / a.gx_dn);
+  }
+  decode1_barrier(a, 1);
+
+  // 4. down
+  {
+    GemmArgs d = a.dn;
+    d.experts = s_ex;
+    d.work = s_work;
+    d.n_work = &s_nwork;
+    d.gather = nullptr;  // B row = slot j (the gate/up output row)
+    d.kk = kk;
+    const int nvb = a.gx_dn * kk;
+    for (int vb = blockIdx.x; vb < nvb; vb += gridDim.x) {
+      const int nx = vb + gridDim.x;
+      if (threadIdx.x == 0 && nx < nvb) prefetch_kblock<MODE_PLAIN_F32>(d, a.ks_dn, nx % a.gx_dn, nx / a.gx_dn);
+      mma_kblock<MODE_PLAIN_F32, 1, GSB, AWQ, false>(d, a.ks_dn, vb % a.gx_dn, vb / a.gx_dn, kk, wsm);
+    }
+  }
+  decode1_barrier(a, 2);
+
+  // 5. combine (+ residual)
+  for (int h = (blockIdx.x * blockDim.x + threadIdx.x) * 4; h < H; h += gridDim.x * blockDim.x * 4) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j = 0; j < kk; ++j) {
+      const float wj = s_w[j];
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(a.partial + (size_t)j * H + h));
+      acc.x = __fmaf_rn(wj, v.x, acc.x);
+      acc.y = __fmaf_rn(wj, v.y, acc.y);
+      acc.z = __fmaf_rn(wj, v.z, acc.z);
+      acc.w = __fmaf_rn(wj, v.w, acc.w);
+    }
+    float ap[4] = {acc.x, acc.y, acc.z, acc.w};
+    if (a.R)  // read before written (R may alias Y)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) ap[i] = __fadd_rn(__bfloat162float(a.R[h + i]), ap[i]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) a.Y[h + i] = __float2bfloat16_rn(ap[i]);
+  }
+}
+
+template <int GSB, bool AWQ>
+static size_t decode1_smem_k() {
+  return std::max((size_t)kWarps * kStagesW * WStage<2, 1, AWQ, false>::kBytes,
+                  (size_t)kWarps * kStagesW * WStage<1, 1, AWQ, false>::kBytes);
+}
+
+// K split and virtual grid width of one GEMM phase: the split (1, 2 or 4 warps
+// per 16-row tile) with the fewest 128-wide K steps per warp over the rounds
+// of blocks the grid needs; ties keep the smaller split (no reduction).
+static void decode1_split(int M, int K, int kk, int grid, int* ks, int* gx) {
+  const int Mt = (M + 15) / 16, nsteps = K / 128;
+  long best = -1;
+  for (int c = 1; c <= kWarps; c *= 2) {
+    if (c > 1 && c > nsteps) break;
+    const int g = (Mt * c + kWarps - 1) / kWarps;
+    const long rounds = ((long)g * kk + grid - 1) / grid;
+    const long cost = rounds * ((nsteps + c - 1) / c);
+    if (best < 0 || cost < best) {
+      best = cost;
+      *ks = c;
+      *gx = g;
+    }
+  }
+}
+
+template <int GSB, bool AWQ>
+static cudaError_t launch_decode1_k(Decode1Args a, cudaStream_t st) {
+  // grid: every CTA resident at once (a cooperative launch), at most the
+  // barrier flags reserved in the workspace
+  static size_t smem = 0;
+  static int grid = 0;
+  static bool pdl = true;  // programmatic launch together with the cooperative attribute
+  a.ex_off = (int)((std::max(decode1_smem_k<GSB, AWQ>(), (size_t)a.H * 4) + 15) / 16 * 16);
+  const size_t need = (size_t)a.ex_off + (size_t)a.ta.kk * sizeof(ExpertDev);
+  if (need > 227 * 1024) return cudaErrorInvalidValue;
+  if (need != smem) {
+    cudaError_t e = cudaFuncSetAttribute(k_moe_decode1<GSB, AWQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)need);
+    if (e != cudaSuccess) return e;
+    int per_sm = 0, dev = 0, sms = 0;
+    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_moe_decode1<GSB, AWQ>, kWarps * 32, need);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) return cudaErrorInvalidConfiguration;
+    grid = std::min(per_sm * sms, kDecode1MaxCtas);
+    smem = need;
+  }
+  decode1_split(a.gu.M, a.gu.K, a.ta.kk, grid, &a.ks_gu, &a.gx_gu);
+  decode1_split(a.dn.M, a.dn.K, a.ta.kk, grid, &a.ks_dn, &a.gx_dn);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kWarps * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 2 : 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k_moe_decode1<GSB, AWQ>, a);
+  if (e != cudaSuccess && pdl) {  // the two attributes refused together: cooperative alone
+    (void)cudaGetLastError();
+    pdl = false;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, k_moe_decode1<GSB, AWQ>, a);
+  }
+  return e;
+}
+
+cudaError_t launch_decode1(Decode1Args a, int awq, cudaStream_t st) {
+  const int gs = a.gu.gs;
+  if (a.ta.kk > kDecode1MaxSlots || a.H % 256 != 0) return cudaErrorInvalidValue;
+  if (awq) {
+    switch (gs) {
+      case 32: return launch_decode1_k<1, true>(a, st);
+      case 64: return launch_decode1_k<2, true>(a, st);
+      default: return launch_decode1_k<4, true>(a, st);
+    }
+  }
+  switch (gs) {
+    case 32: return launch_decode1_k<1, false>(a, st);
+    case 64: return launch_decode1_k<2, false>(a, st);
+    default: return launch_decode1_k<4, false>(a, st);
   }
 }
 

@@ -19,6 +19,9 @@ struct TopkArgs {
   int has_shared;
   int shared_gate = 0;   // the shared expert's weight is sigmoid(logits[t][E]) per token
   float* shared_w = nullptr;  // [T] per-token shared weights (expert-parallel source; may be null)
+  // sigmoid router: the scores sigmoid_ref(logit), laid out as the logits,
+  // made where the logits were (null: computed from the logits here)
+  const float* sig = nullptr;
   int* ids;              // [T,kk]
   float* weights;        // [T,kk]
   // expert parallelism: also each pair's owner key (e % world) * e_loc + e / world
@@ -263,5 +266,38 @@ cudaError_t launch_combine(const float* d, const int* inverse, const float* w, i
                            void* y, int y_bf16, int skip_tiny, cudaStream_t st, const void* res = nullptr);
 cudaError_t launch_quant_awq_sym(const __nv_bfloat16* W, int M, int K, int gs, int bf16_scale,
                                  uint8_t* q, __half* sc, cudaStream_t st);
+
+// Fused single-token decode (k_moe_decode1, int4_gemm.cu): the router rows,
+// the top-k, gate/up + SiLU*mul, down and the weighted combine of one token in
+// one cooperative launch, with grid-wide barriers between the phases.  The
+// arithmetic of each phase is that of the separate kernels (router_dot_warp,
+// topk_token, mma_kblock, k_combine's ordered FMAs).
+constexpr int kDecode1MaxCtas = 2048;  // grid cap of the fused kernel
+constexpr int kDecode1MaxSlots = 65;   // topk <= 64, + the shared expert
+struct Decode1Args {
+  const __nv_bfloat16* X;  // [1][H]
+  const uint16_t* Wr;      // [rows][H] bf16 router rows (E routed, then the shared gate's)
+  int rows, H;
+  float* logits;           // [rows] the router's output
+  TopkArgs ta;             // T = 1 over logits; ids / weights: the routing views
+  float* sig;              // [rows] the sigmoid router's scores (ta.sig), or null
+  GemmArgs gu, dn;         // work, n_work and gather are set in the kernel (shared memory)
+  int ks_gu, gx_gu, ks_dn, gx_dn;  // K split and virtual grid width of each GEMM phase
+  int ex_off;              // byte offset of the slots' expert table in dynamic shared memory
+  const float* partial;    // dn.out
+  __nv_bfloat16* Y;
+  const __nv_bfloat16* R;  // residual (may alias Y) or null
+  int n_exp;               // routed + shared experts: offsets has n_exp + 1 entries
+  int* offsets;
+  int* sorted;
+  int* inverse;
+  int* n_active;
+  int* err;                // bit 2: a barrier wait gave up
+  unsigned long long* bar;  // [2]: the barrier's arrival counter (low 32 bits of [0]), the launch's tag
+  unsigned long long epoch;  // distinct per launch: barrier tags never match an older launch's words
+  long long budget;        // SM clocks per barrier wait
+};
+// Launches k_moe_decode1 (a.ks_* / a.gx_* are filled here from the grid).
+cudaError_t launch_decode1(Decode1Args a, int awq, cudaStream_t st);
 
 }  // namespace llmoc

@@ -29,6 +29,7 @@
 #include <algorithm>
 
 #include "kernels.cuh"
+#include "route_dev.cuh"
 
 namespace llmoc {
 
@@ -381,20 +382,8 @@ __global__ void __launch_bounds__(kRouterSmallThreads) k_router_small(const __nv
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int pr = warp; pr < nw * T; pr += kRouterSmallThreads / 32) {
     const int e = pr % nw, t = pr / nw;
-    const uint16_t* wrow = rsm16 + (size_t)e * H;
-    const uint16_t* xrow = rsm16 + (size_t)(nw + t) * H;
-    float c = 0.f;
-    for (int k = lane; k < H; k += 32) c = __fmaf_rn(bf16_bits_to_f32(xrow[k]), bf16_bits_to_f32(wrow[k]), c);
-    const float c8 = __shfl_down_sync(0xffffffffu, c, 8), c16 = __shfl_down_sync(0xffffffffu, c, 16),
-                c24 = __shfl_down_sync(0xffffffffu, c, 24);
-    const float av = (c + c8) + (c16 + c24);                       // a[lane], lanes 0..7
-    const float bv = av + __shfl_down_sync(0xffffffffu, av, 4);    // b[lane], lanes 0..3
-    const float b1 = __shfl_down_sync(0xffffffffu, bv, 1), b2 = __shfl_down_sync(0xffffffffu, bv, 2),
-                b3 = __shfl_down_sync(0xffffffffu, bv, 3);
-    if (lane == 0) {
-      const float r = (bv + b1) + (b2 + b3);
-      logits[(size_t)t * E + e0 + e] = isfinite(r) ? r : 0.f;
-    }
+    const float r = router_dot_warp(rsm16 + (size_t)e * H, rsm16 + (size_t)(nw + t) * H, H, lane);
+    if (lane == 0) logits[(size_t)t * E + e0 + e] = r;
   }
   if (xo.xh && (int)blockIdx.x < T && warp == kRouterSmallThreads / 32 - 1)
     prep_xh_row<4, false>(reinterpret_cast<const uint4*>(rsm16 + (size_t)(nw + blockIdx.x) * H), blockIdx.x, H,
@@ -446,159 +435,7 @@ static cudaError_t launch_router_tiled(const __nv_bfloat16* X, const uint16_t* W
 // --------------------------------------------------------------- top-k
 
 
-// Order-preserving map of a non-NaN float key to uint32 (larger key ->
-// larger code; -0 is folded into +0 first, so equal keys get equal codes).
-__device__ __forceinline__ uint32_t key_code(float v) {
-  const uint32_t u = __float_as_uint(v + 0.f);
-  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-
-// Top-k of one token by one warp (E <= 32 * kTopkSlots).  Lane l holds the
-// keys and values of experts l, l + 32, ... in registers; a round takes the
-// warp's largest key (smaller id on ties) with two warp reductions, and the
-// chosen ids and values stay in registers until the weights are written.
-constexpr int kTopkSlots = 16;  // E <= 512
-template <int Q>  // slots per lane: E <= 32 * Q
-__device__ __forceinline__ void topk_token_q(const TopkArgs& a, int t, int lane) {
-  const float* lg = a.logits + (size_t)t * (a.ld > 0 ? a.ld : a.E);
-  float key[Q], val[Q];
-  if (a.router == 0) {
-    // keys = logits; probabilities exp(l - max) (their rounding only reaches
-    // the weights, which are compared with a tolerance, never the ids)
-    float m = -INFINITY;
-#pragma unroll
-    for (int q = 0; q < Q; ++q) {
-      const int e = lane + 32 * q;
-      key[q] = e < a.E ? lg[e] : -INFINITY;
-      m = fmaxf(m, key[q]);
-    }
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 8));
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-#pragma unroll
-    for (int q = 0; q < Q; ++q) val[q] = lane + 32 * q < a.E ? expf(key[q] - m) : 0.f;
-  } else {
-    // s = sigmoid(l) in double rounded to fp32 (part of the selection key)
-#pragma unroll
-    for (int q = 0; q < Q; ++q) {
-      const int e = lane + 32 * q;
-      if (e < a.E) {
-        const float sg = (float)(1.0 / (1.0 + exp(-(double)lg[e])));
-        val[q] = sg;
-        const float kv = sg + a.bias[e];
-        key[q] = kv == kv ? kv : -FLT_MAX;  // a NaN bias must still leave a valid id
-      } else {
-        val[q] = 0.f;
-        key[q] = -INFINITY;
-      }
-    }
-  }
-
-  // k rounds of argmax over keys (ties -> smaller id); selected keys -> -inf.
-  // Padding slots (e >= E) hold -inf with ids above every real id, so a tie at
-  // -inf still resolves to a real expert.
-  int my_id = 0;
-  float my_val = 0.f;
-  for (int j = 0; j < a.k; ++j) {
-    uint32_t bc = key_code(key[0]);
-    int bq = 0;
-#pragma unroll
-    for (int q = 1; q < Q; ++q) {
-      const uint32_t c = key_code(key[q]);
-      if (c > bc) {
-        bc = c;
-        bq = q;
-      }
-    }
-    const uint32_t mc = __reduce_max_sync(0xffffffffu, bc);
-    const int bi = (int)__reduce_min_sync(0xffffffffu, bc == mc ? (uint32_t)(lane + 32 * bq) : 0x7fffffffu);
-    const int oq = bi >> 5, ol = bi & 31;
-    float v = 0.f;
-#pragma unroll
-    for (int q = 0; q < Q; ++q)
-      if (q == oq) {
-        v = val[q];
-        if (lane == ol) key[q] = -INFINITY;
-      }
-    v = __shfl_sync(0xffffffffu, v, ol);
-    if (lane == (j & 31)) {
-      if (j < 32) {
-        my_id = bi;
-        my_val = v;
-      }
-    }
-    if (j >= 32 && lane == (j & 31)) {  // k > 32: slots 32..63 go out now
-      a.ids[(size_t)t * a.kk + j] = bi;
-      if (a.ep_key) a.ep_key[(size_t)t * a.kk + j] = (bi % a.ep_world) * a.ep_e_loc + bi / a.ep_world;
-      a.weights[(size_t)t * a.kk + j] = v;  // finished below
-    }
-  }
-
-  // weights: lane l computes w[j] for j = l, l+32 (k <= 64); sums are warp
-  // reductions in double (the reference sums sequentially in double; the two
-  // agree except for double roundings far below fp32 resolution)
-  int* ids = a.ids + (size_t)t * a.kk;
-  float* w = a.weights + (size_t)t * a.kk;
-  float sel[2];
-  sel[0] = my_val;
-  sel[1] = lane + 32 < a.k ? w[lane + 32] : 0.f;
-  __syncwarp();
-  if (lane < a.k) {
-    ids[lane] = my_id;
-    if (a.ep_key) a.ep_key[(size_t)t * a.kk + lane] = (my_id % a.ep_world) * a.ep_e_loc + my_id / a.ep_world;
-  }
-  if (a.router == 0) {
-    double s = 0.0;
-#pragma unroll
-    for (int q = 0; q < Q; ++q) s += (double)val[q];
-    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    float p[2];
-    double ws = 0.0;
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int j = lane + 32 * h;
-      p[h] = j < a.k ? (float)((double)sel[h] / s) : 0.f;  // the reference's fp32 prob
-      ws += (double)p[h];
-    }
-    for (int o = 16; o; o >>= 1) ws += __shfl_xor_sync(0xffffffffu, ws, o);
-    if (ws < 1e-12) ws = 1.0;
-#pragma unroll
-    for (int h = 0; h < 2; ++h)
-      if (lane + 32 * h < a.k) w[lane + 32 * h] = (float)((double)p[h] / ws);
-  } else {
-    double sv[2], ws = 0.0;
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int j = lane + 32 * h;
-      sv[h] = j < a.k ? (double)sel[h] : 0.0;
-      ws += sv[h];
-    }
-    for (int o = 16; o; o >>= 1) ws += __shfl_xor_sync(0xffffffffu, ws, o);
-    if (ws < 1e-20) ws = 1.0;
-#pragma unroll
-    for (int h = 0; h < 2; ++h)
-      if (lane + 32 * h < a.k) w[lane + 32 * h] = __fmul_rn((float)(sv[h] / ws), a.routed_scaling);
-  }
-  if (lane == 0 && (a.has_shared || a.shared_w)) {
-    // the shared expert's weight: constant, or the reference's float sigmoid of
-    // its gate row's logit (qwen3_6_moe_int4_model.cpp:29, :365-371)
-    const float sw = a.shared_gate ? 1.f / (1.f + expf(-lg[a.E])) : a.shared_scale;
-    if (a.has_shared) {
-      ids[a.k] = a.E;
-      w[a.k] = sw;
-    }
-    if (a.shared_w) a.shared_w[t] = sw;
-  }
-}
-
-__device__ __forceinline__ void topk_token(const TopkArgs& a, int t, int lane) {
-  if (a.E <= 128) topk_token_q<4>(a, t, lane);
-  else if (a.E <= 256) topk_token_q<8>(a, t, lane);
-  else if (a.E <= 384) topk_token_q<12>(a, t, lane);
-  else topk_token_q<16>(a, t, lane);
-}
+// (key_code, topk_token_q and topk_token: route_dev.cuh)
 
 
 // One warp per token.

@@ -345,6 +345,7 @@ struct llmoc_moe_layer {
   uint16_t* router_w = nullptr;   // device [E (+1: the shared expert's gate row, when set)][H] bf16
   int shared_gate = 0;            // router_w holds the shared gate row (llmoc_moe_layer_set_shared_gate)
   float* bias = nullptr;
+  long long wait_cycles = llmoc::kDefaultWaitCycles;  // budget of the fused decode kernel's barrier waits
   // stage timing (llmoc_moe_set_stage_timing): 7 events per timed call
   bool timing = false;
   std::vector<cudaEvent_t> ev_pool;
@@ -373,7 +374,7 @@ int chunk_rows(const llmoc_moe_layer* L, int T) {
 
 struct WsLayout {
   size_t logits, ids, weights, offsets, sorted, inverse, work, n_work, n_active, err, mid, partial,
-      xs, xh, xsum, xscale, total;
+      xs, xh, xsum, xscale, bar, sig, total;
   int max_work;
 };
 
@@ -421,6 +422,9 @@ WsLayout ws_layout_g(const llmoc_moe_layer* L, int T, int kk, int n_perm, int ch
     w.xsum = take((size_t)T * (L->d.hidden / L->d.group_size) * 4);
     w.xscale = take((size_t)T * 4);
   }
+  // the fused single-token kernel's barrier words (a whole-layer forward of one token)
+  w.bar = logits && T == 1 ? take(16) : 0;
+  w.sig = logits && T == 1 ? take((size_t)(L->d.n_experts + L->shared_gate) * 4) : 0;  // sigmoid scores
   w.total = o;
   return w;
 }
@@ -817,6 +821,93 @@ llmoc_status run_ffn(const llmoc_moe_layer* L, const uint16_t* X, int R, int kk,
     count_launch(1);
   }
   if (se) se->mark(st);
+  return LLMOC_OK;
+}
+
+// The fused single-token kernel takes a whole-layer forward of one token when
+// the layer has the decode GEMMs' shapes (tc_shapes), the router's rows are a
+// multiple of 256 wide and the slots fit its work list.
+bool decode1_ok(const llmoc_moe_layer* L) {
+  return tc_shapes(L) && L->d.hidden % 256 == 0 && L->kk <= kDecode1MaxSlots && L->d.n_experts <= kMaxExperts;
+}
+
+// Distinct per launch of the fused kernel in this process (its barrier tags).
+std::atomic<unsigned long long> g_decode1_epoch{0};
+
+// One token through the layer in one launch (k_moe_decode1): the same
+// routing outputs in the workspace as run_route, the same rows in mid /
+// partial as run_ffn, y (+ the residual) as the combine.
+llmoc_status run_decode1(const llmoc_moe_layer* L, const uint16_t* X, const uint16_t* R, uint16_t* Y,
+                         const WsLayout& w, char* ws, cudaStream_t st, StageEvents* se) {
+  const int E = L->d.n_experts, H = L->d.hidden, I = L->d.inter;
+  Decode1Args a{};
+  a.X = (const __nv_bfloat16*)X;
+  a.Wr = L->router_w;
+  a.rows = E + L->shared_gate;
+  a.H = H;
+  a.logits = (float*)(ws + w.logits);
+  TopkArgs& ta = a.ta;
+  ta.logits = a.logits;
+  ta.bias = L->bias;
+  ta.T = 1;
+  ta.E = E;
+  ta.k = L->d.topk;
+  ta.kk = L->kk;
+  ta.ld = E + L->shared_gate;
+  ta.router = L->d.router;
+  ta.routed_scaling = L->d.routed_scaling;
+  ta.shared_scale = L->d.shared_scale;
+  ta.has_shared = L->d.has_shared;
+  ta.shared_gate = L->shared_gate;
+  ta.ids = (int*)(ws + w.ids);
+  ta.weights = (float*)(ws + w.weights);
+  a.sig = L->d.router == LLMOC_ROUTER_SIGMOID_BIAS ? (float*)(ws + w.sig) : nullptr;
+  ta.sig = a.sig;
+  GemmArgs& g = a.gu;
+  g.experts = L->table;
+  g.proj = 0;
+  g.M = I;
+  g.K = H;
+  g.Kc = L->gu.Kc;
+  g.gs = L->d.group_size;
+  g.ng = L->gu.ng;
+  g.zp = L->d.awq_zp;
+  g.B = X;  // the token's bf16 row (the kernel reads it for every slot)
+  g.ldb = H;
+  g.out = ws + w.mid;
+  g.ldo = I;
+  g.out_bf16 = 1;
+  g.err = (int*)(ws + w.err);
+  GemmArgs& d = a.dn;
+  d = g;
+  d.proj = 2;
+  d.M = H;
+  d.K = I;
+  d.Kc = L->dn.Kc;
+  d.ng = L->dn.ng;
+  d.B = ws + w.mid;
+  d.ldb = I;
+  d.out = ws + w.partial;
+  d.ldo = H;
+  a.partial = (const float*)(ws + w.partial);
+  a.Y = (__nv_bfloat16*)Y;
+  a.R = (const __nv_bfloat16*)R;
+  a.n_exp = L->n_exp;
+  a.offsets = (int*)(ws + w.offsets);
+  a.sorted = (int*)(ws + w.sorted);
+  a.inverse = (int*)(ws + w.inverse);
+  a.n_active = (int*)(ws + w.n_active);
+  a.err = (int*)(ws + w.err);
+  a.bar = (unsigned long long*)(ws + w.bar);
+  a.epoch = ++g_decode1_epoch;
+  a.budget = L->wait_cycles;
+  // stage timing: the whole launch is reported as the gate/up stage
+  for (int i = 0; i < 4; ++i)
+    if (se) se->mark(st);
+  if (!cuda_ok(launch_decode1(a, L->d.scheme == LLMOC_SCHEME_AWQ_SYM, st), "fused decode")) return LLMOC_ERR_CUDA;
+  count_launch(1);
+  for (int i = 0; i < 3; ++i)
+    if (se) se->mark(st);
   return LLMOC_OK;
 }
 
@@ -1287,6 +1378,11 @@ llmoc_status moe_forward(const llmoc_moe_layer* L, const uint16_t* X, int T, con
   cudaStream_t st = (cudaStream_t)stream;
   char* ws = (char*)workspace;
   StageEvents se(L);
+  if (T == 1 && decode1_ok(L)) {
+    const llmoc_status rc = run_decode1(L, X, R, Y, w, ws, st, &se);
+    if (rc == LLMOC_OK) se.commit();
+    return rc;
+  }
   llmoc_status rc = run_route(L, X, T, w, ws, st, &se);
   if (rc != LLMOC_OK) return rc;
   rc = run_ffn(L, X, T, L->kk, chunk_rows(L, T), w, ws, Y, (const float*)(ws + w.weights), st, &se, R, 0,
@@ -1352,6 +1448,12 @@ llmoc_status llmoc_quantize_awq_sym(const uint16_t* W, int M, int K, int group_s
                "quantize"))
     return LLMOC_ERR_CUDA;
   count_launch();
+  return LLMOC_OK;
+}
+
+llmoc_status llmoc_moe_layer_set_wait_cycles(llmoc_moe_layer* L, long long cycles) {
+  if (!L || cycles <= 0) return fails(LLMOC_ERR_INVALID, "bad arguments");
+  L->wait_cycles = cycles;
   return LLMOC_OK;
 }
 

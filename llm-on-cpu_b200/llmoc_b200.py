@@ -117,6 +117,7 @@ _SIGS = {
     "llmoc_moe_dequant": (_i, [_vp, _i, _i, _vp, _vp]),
     "llmoc_quantize_awq_sym": (_i, [_vp, _i, _i, _i, _i, _vp, _vp, _vp]),
     "llmoc_kernel_launch_count": (C.c_uint64, []),
+    "llmoc_moe_layer_set_wait_cycles": (_i, [_vp, C.c_longlong]),
     "llmoc_moe_set_stage_timing": (_i, [_vp, _i]),
     "llmoc_moe_forward_noalloc": (_i, [_vp, _vp, _i, _vp, _vp]),
     "llmoc_moe_noalloc_capacity": (_sz, []),
@@ -293,6 +294,10 @@ class MoeLayer:
         return v
 
     STAGES = ("router", "topk", "permute", "gate_up", "down", "combine")
+
+    def set_wait_cycles(self, cycles: int) -> None:
+        """Budget (SM clocks) of each barrier wait of the fused one-token forward."""
+        check(lib.llmoc_moe_layer_set_wait_cycles(self.handle, int(cycles)), "llmoc_moe_layer_set_wait_cycles")
 
     def set_stage_timing(self, enable: bool) -> None:
         check(lib.llmoc_moe_set_stage_timing(self.handle, int(enable)), "llmoc_moe_set_stage_timing")

@@ -157,6 +157,58 @@ def test_layer_matches_oracle(oracle, name, T):
     dl.close()
 
 
+def test_single_token_forward_on_a_stale_workspace(oracle):
+    """The fused one-token forward (one launch, grid-wide barriers whose words
+    live in the workspace, tagged per launch) on a workspace full of random
+    bytes, then again on what the previous launches left: every output
+    matches the oracle, the same token twice gives the same bits, and the
+    routing views are the canonical ones of one token."""
+    dl, rng = build(oracle, "glm_like_shared_sigmoid", 11, 1)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    dl.ws.copy_(torch.randint(0, 256, dl.ws.shape, generator=g, device="cuda", dtype=torch.int32).to(torch.uint8))
+    Xs = [orc.make_tokens(rng, 1, dl.host.H) for _ in range(3)]
+    outs = []
+    for X in Xs + [Xs[0]]:
+        Y, ws_bytes = dl.forward(X)
+        Yref, ids, w, _ = oracle.moe_layer_forward(dl.host, X)
+        v = dl.views(1, ws_bytes)
+        assert v["error_flag"] == 0
+        assert np.array_equal(v["ids"][:, :dl.host.topk], ids)
+        kk = dl.dev.kk
+        order = np.argsort(v["ids"][0], kind="stable")
+        assert np.array_equal(v["sorted"], order)
+        assert np.array_equal(v["inverse"][order], np.arange(kk))
+        assert np.array_equal(v["offsets"], np.searchsorted(np.sort(v["ids"][0]), np.arange(dl.dev.n_exp + 1)))
+        assert v["n_active"] == kk
+        mre, cos = G.quality(G.bf16_to_f32(Y), Yref)
+        assert mre <= G.MAX_REL and cos >= G.MIN_COS, (mre, cos)
+        outs.append(Y.clone())
+    assert torch.equal(outs[0], outs[3])
+    dl.close()
+
+
+def test_single_token_barrier_budget_runs_out(oracle):
+    """A barrier wait of the fused one-token kernel that runs out of its
+    budget (cut to one SM clock, so a CTA that arrives before the others gives
+    up): bit 2 of the error word is set, the launch ends, the device still
+    runs work, and with the default budget back the next forward is correct
+    and clean."""
+    dl, rng = build(oracle, "qwen_like", 12, 1)
+    X = orc.make_tokens(rng, 1, dl.host.H)
+    dl.dev.set_wait_cycles(1)
+    _, ws_bytes = dl.forward(X)
+    assert dl.views(1, ws_bytes)["error_flag"] & 4
+    a = torch.arange(1 << 20, device="cuda", dtype=torch.float32)
+    assert float(a.sum()) == float((1 << 20) * ((1 << 20) - 1) / 2)
+    dl.dev.set_wait_cycles(1 << 31)
+    Y, ws_bytes = dl.forward(X)
+    assert dl.views(1, ws_bytes)["error_flag"] == 0
+    Yref, _, _, _ = oracle.moe_layer_forward(dl.host, X)
+    mre, cos = G.quality(G.bf16_to_f32(Y), Yref)
+    assert mre <= G.MAX_REL and cos >= G.MIN_COS, (mre, cos)
+    dl.close()
+
+
 def test_zero_tokens_is_a_no_op(oracle):
     dl, _ = build(oracle, "qwen_like", 4, 4)
     assert L.lib.llmoc_moe_forward(dl.dev.handle, None, 0, None, None, 0, None) == 0
@@ -196,11 +248,12 @@ def test_skewed_routing_hot_expert(oracle, T):
     dl.close()
 
 
-@pytest.mark.parametrize("T,in_place", [(5, False), (5, True), (150, False), (150, True)])
+@pytest.mark.parametrize("T,in_place", [(1, False), (1, True), (5, False), (5, True), (150, False), (150, True)])
 def test_forward_residual(oracle, T, in_place):
     """Y = R + MoE(X) through llmoc_moe_forward_residual: separate R, and the
     in-place residual stream (R = Y = X, the decoder's h += moe(h)); decode and
-    prefill paths.  Compared with R + the oracle's fp32 layer output, and with
+    prefill paths, and the fused one-token kernel (T = 1).  Compared with R +
+    the oracle's fp32 layer output, and with
     the plain forward's output plus R."""
     rng = np.random.default_rng(30 + T)
     layer = orc.make_layer(oracle, rng, H=512, I=256, E=32, topk=8, gs=128)
@@ -328,7 +381,7 @@ def _check_full(oracle, dl, X, Xd, T):
 
 
 @pytest.mark.parametrize("name,T", [("qwen3_30b_a3b", 1), ("qwen3_30b_a3b", 8), ("qwen3_30b_a3b", 64),
-                                    ("qwen3_30b_a3b", 512), ("glm45_air", 64), ("glm45_air", 512), ("glm45_air", 1024),
+                                    ("qwen3_30b_a3b", 512), ("glm45_air", 1), ("glm45_air", 64), ("glm45_air", 512), ("glm45_air", 1024),
                                     ("glm45_air", 4096), ("kimi_k2", 1), ("kimi_k2", 64),
                                     ("kimi_k2", 1024), ("kimi_k2", 8192)])
 def test_full_size_layer(oracle, name, T):
