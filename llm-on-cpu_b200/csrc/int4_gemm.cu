@@ -1285,32 +1285,6 @@ __device__ __forceinline__ void decode1_barrier(const Decode1Args& a, int b) {
   __syncthreads();
 }
 
-// Bulk L2 prefetch of [p, p + bytes) (16-byte aligned, a multiple of 16),
-// evict_first like the copies that will read it.
-__device__ __forceinline__ void prefetch_l2(const void* p, unsigned int bytes, unsigned long long pol) {
-  asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(p), "r"(bytes), "l"(pol)
-               : "memory");
-}
-
-// The weights, scales (and zeros) one mma_kblock block (bx, expert) will
-// read, prefetched into L2 by the calling thread: its kWarps / ks row tiles
-// are consecutive, so each part of each projection is one contiguous range.
-template <int MODE>
-__device__ __forceinline__ void prefetch_kblock(const GemmArgs& a, int ks, int bx, int expert) {
-  const ExpertDev& ex = a.experts[expert];
-  const int tpb = kWarps / ks, Mt = (a.M + 15) >> 4;
-  const int r0 = bx * tpb, r1 = min(Mt, r0 + tpb);
-  if (r0 >= r1) return;
-  const unsigned long long pol = l2_evict_first();
-#pragma unroll
-  for (int p = 0; p < (MODE == MODE_GATE_UP ? 2 : 1); ++p) {
-    const ProjDev& P = MODE == MODE_GATE_UP ? (p ? ex.up : ex.gate) : pick(ex, a.proj);
-    prefetch_l2(P.q + (size_t)r0 * a.Kc * 32, (unsigned int)((r1 - r0) * a.Kc * 512), pol);
-    prefetch_l2(P.s + (size_t)r0 * a.ng * 16, (unsigned int)((r1 - r0) * a.ng * 32), pol);
-    if (P.z) prefetch_l2(P.z + (size_t)r0 * a.ng * 16, (unsigned int)((r1 - r0) * a.ng * 32), pol);
-  }
-}
-
 // One token through the whole layer in one cooperative launch (T = 1 decode:
 // the chain of separate kernels is bound by its launch boundaries, not its
 // bytes).  Phases, split by decode1_barrier:
@@ -1323,10 +1297,11 @@ __device__ __forceinline__ void prefetch_kblock(const GemmArgs& a, int ks, int b
 //      row of expert ids[j]); CTA 0 writes the routing views (ids, weights,
 //      the canonical offsets / sorted / inverse of one token).
 //   3. gate/up + SiLU*mul: the blocks of k_int4_mma's grid (gx_gu x kk) dealt
-//      round-robin to the CTAs, each run by mma_kblock on the bf16 token row;
-//      each block's weights are prefetched into L2 one block ahead.
-//   4. down: the same over the gate/up rows (gx_dn x kk blocks); a CTA's
-//      first down block is prefetched before the barrier.
+//      round-robin to the CTAs, each run by mma_kblock on the bf16 token row.
+//      (A bulk L2 prefetch of each block's weights one block ahead was
+//      measured: no gain at Qwen / GLM sizes, and at Kimi's 223 MB per token
+//      its ~100 MB in flight were evicted before use: 92 -> 105 us.)
+//   4. down: the same over the gate/up rows (gx_dn x kk blocks).
 //   5. combine: y = sum_j w_j * partial_j in slot order (k_combine's fmaf
 //      order), + the residual, to bf16.
 template <int GSB, bool AWQ>
@@ -1429,25 +1404,9 @@ __global__ void __launch_bounds__(kWarps * 32) k_moe_decode1(Decode1Args a) {
     g.n_work = &s_nwork;
     g.gather = nullptr;
     g.ldb = 0;  // every slot reads the token's row
-    GemmArgs dpf = a.dn;  // the down phase's blocks, for prefetching
-    dpf.experts = s_ex;
-    const int nvb = a.gx_gu * kk, nvb_dn = a.gx_dn * kk;
-    // each block's weights go to L2 one block ahead of its ring of copies
-    if (threadIdx.x == 0 && (int)blockIdx.x < nvb)
-      prefetch_kblock<MODE_GATE_UP>(g, a.ks_gu, blockIdx.x % a.gx_gu, blockIdx.x / a.gx_gu);
-    // CTAs without a gate/up block fetch the down weights meanwhile (all of
-    // them, dealt over these CTAs)
-    if (threadIdx.x == 0 && (int)blockIdx.x >= nvb)
-      for (int vb = blockIdx.x - nvb; vb < nvb_dn; vb += gridDim.x - nvb)
-        prefetch_kblock<MODE_PLAIN_F32>(dpf, a.ks_dn, vb % a.gx_dn, vb / a.gx_dn);
-    for (int vb = blockIdx.x; vb < nvb; vb += gridDim.x) {
-      const int nx = vb + gridDim.x;
-      if (threadIdx.x == 0 && nx < nvb) prefetch_kblock<MODE_GATE_UP>(g, a.ks_gu, nx % a.gx_gu, nx / a.gx_gu);
+    const int nvb = a.gx_gu * kk;
+    for (int vb = blockIdx.x; vb < nvb; vb += gridDim.x)
       mma_kblock<MODE_GATE_UP, 1, GSB, AWQ, false>(g, a.ks_gu, vb % a.gx_gu, vb / a.gx_gu, kk, wsm);
-    }
-    // else the CTA's first down block, while the others finish gate/up
-    if (threadIdx.x == 0 && nvb >= (int)gridDim.x && (int)blockIdx.x < nvb_dn)
-      prefetch_kblock<MODE_PLAIN_F32>(dpf, a.ks_dn, blockIdx.x % a.gx_dn, blockIdx.x / a.gx_dn);
   }
   decode1_barrier(a, 1);
 
@@ -1460,11 +1419,8 @@ __global__ void __launch_bounds__(kWarps * 32) k_moe_decode1(Decode1Args a) {
     d.gather = nullptr;  // B row = slot j (the gate/up output row)
     d.kk = kk;
     const int nvb = a.gx_dn * kk;
-    for (int vb = blockIdx.x; vb < nvb; vb += gridDim.x) {
-      const int nx = vb + gridDim.x;
-      if (threadIdx.x == 0 && nx < nvb) prefetch_kblock<MODE_PLAIN_F32>(d, a.ks_dn, nx % a.gx_dn, nx / a.gx_dn);
+    for (int vb = blockIdx.x; vb < nvb; vb += gridDim.x)
       mma_kblock<MODE_PLAIN_F32, 1, GSB, AWQ, false>(d, a.ks_dn, vb % a.gx_dn, vb / a.gx_dn, kk, wsm);
-    }
   }
   decode1_barrier(a, 2);
 
