@@ -194,16 +194,16 @@ __device__ __forceinline__ void raw_word_f16(uint32_t w, uint32_t a[4]) {
 // grid.x = ceil(Mt * ks / 4), grid.y = work-list bound.
 constexpr int kStagesW = 3;
 
-template <int NP, int NT, bool AWQ, bool XH = false>
-struct WStage {  // bytes of one stage of one warp
+template <int NP, int NT, bool AWQ, bool XH = false, bool ONE = false>
+struct WStage {  // bytes of one stage of one warp (ONE: the activations of one row only)
   static constexpr int kW = NP * 1024;         // 2 chunks x 512 B per projection
   static constexpr int kS = NP * 128;          // scales of the step's groups (<= 4 x 32 B)
   static constexpr int kZ = AWQ ? 0 : NP * 128;  // zeros (GPTQ)
-  static constexpr int kB = NT * 4 * 512;      // 4 blocks x 16 B per lane per N-tile
+  static constexpr int kB = ONE ? 4 * 64 : NT * 4 * 512;  // 4 blocks x 16 B per lane per N-tile (ONE: per t)
   static constexpr int kX = XH ? 128 : 0;      // fp16 path: the 8 columns' group sums (16 B each)
   static constexpr int kBytes = kW + kS + kZ + kB + kX;
   // the K-slice reduction reuses the warp's own stages once they are drained
-  static_assert(kStagesW * kBytes >= NP * NT * 4 * 32 * 4, "reduction slot");
+  static_assert(ONE || kStagesW * kBytes >= NP * NT * 4 * 32 * 4, "reduction slot");
 };
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
@@ -249,14 +249,17 @@ __device__ __forceinline__ float f16_group(float P, float xs, int hi, float bias
 // One CTA's share of k_int4_mma: row-tile block bx (kWarps / ks tiles) of the
 // work items by, by + gy, ...; wsm = the CTA's kWarps stage rings.  Also the
 // GEMM phases of the fused single-token kernel (k_moe_decode1), which walks a
-// virtual grid of such blocks.
-template <int MODE, int NT, int GSB, bool AWQ, bool XH>
+// virtual grid of such blocks.  ONECOL: items of one row, so only the C
+// fragment's column 2t (accumulators r = 0, 2; column 0 in lanes t = 0) is ever
+// stored and the group ends skip the others.
+template <int MODE, int NT, int GSB, bool AWQ, bool XH, bool ONECOL = false, int STG = kStagesW>
 __device__ __forceinline__ void mma_kblock(const GemmArgs& a, int ks, int bx, int by, int gy,
                                            unsigned char* wsm) {
   constexpr int NP = MODE == MODE_GATE_UP ? 2 : 1;
   constexpr int NG = GSB == 4 ? 1 : (GSB == 2 ? 2 : 4);  // groups per step
   static_assert(!XH || (MODE == MODE_GATE_UP && NT == 1), "fp16 activations: gate/up, 8-row items");
-  using SG = WStage<NP, NT, AWQ, XH>;
+  using SG = WStage<NP, NT, AWQ, XH, ONECOL>;
+  static_assert(STG >= 2 && STG * SG::kBytes >= NP * NT * 4 * 32 * 4, "stages: a reduction slot");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int slice = warp % ks;
@@ -327,7 +330,7 @@ __device__ __forceinline__ void mma_kblock(const GemmArgs& a, int ks, int bx, in
       zsrc[p] = AWQ ? nullptr
                     : reinterpret_cast<const unsigned char*>(P[p]->z + ((size_t)rtc * a.ng + (size_t)s0 * NG) * 16);
     }
-    unsigned char* wbase = wsm + (size_t)warp * kStagesW * SG::kBytes;
+    unsigned char* wbase = wsm + (size_t)warp * STG * SG::kBytes;
 
     // issue the copies of one step into a stage (every lane its own 16 B
     // pieces): the weights (and scales, zeros), then the activations
@@ -350,8 +353,9 @@ __device__ __forceinline__ void mma_kblock(const GemmArgs& a, int ks, int bx, in
       for (int n = 0; n < NT; ++n) {  // a lane past the item's rows copies nothing (stale bytes are never stored)
         if (bval[n]) {
 #pragma unroll
-          for (int b = 0; b < 4; ++b)
-            cp_async16(sb + SG::kW + SG::kS + SG::kZ + (n * 4 + b) * 512 + lane * 16, bsrc[n] + b * 64);
+          for (int b = 0; b < 4; ++b)  // ONECOL: lanes t = 0..3 of row g = 0, [b][t] slots
+            cp_async16(sb + SG::kW + SG::kS + SG::kZ + (ONECOL ? b * 64 + t * 16 : (n * 4 + b) * 512 + lane * 16),
+                       bsrc[n] + b * 64);
         }
         bsrc[n] += 256;
       }
@@ -366,7 +370,7 @@ __device__ __forceinline__ void mma_kblock(const GemmArgs& a, int ks, int bx, in
     };
 
 #pragma unroll
-    for (int d = 0; d < kStagesW - 1; ++d)
+    for (int d = 0; d < STG - 1; ++d)
       if (d < nst) issue_w(d);
     if (!waited) {
       grid_dep_wait();
@@ -374,7 +378,7 @@ __device__ __forceinline__ void mma_kblock(const GemmArgs& a, int ks, int bx, in
       waited = true;
     }
 #pragma unroll
-    for (int d = 0; d < kStagesW - 1; ++d) {
+    for (int d = 0; d < STG - 1; ++d) {
       if (d < nst) issue_b(d);
       cp_async_commit();
     }
@@ -397,11 +401,11 @@ __device__ __forceinline__ void mma_kblock(const GemmArgs& a, int ks, int bx, in
       for (int r = 0; r < 4; ++r) xs[n][0][r] = xs[n][1][r] = 0.f;
 
     for (int i = 0; i < nst; ++i) {
-      if (i + kStagesW - 1 < nst) issue((i + kStagesW - 1) % kStagesW);
+      if (i + STG - 1 < nst) issue((i + STG - 1) % STG);
       cp_async_commit();
-      cp_async_wait<kStagesW - 1>();
+      cp_async_wait<STG - 1>();
       __syncwarp();  // the scales are copied by lanes 0..2*NG-1 and read by all
-      const unsigned char* sb = wbase + (i % kStagesW) * SG::kBytes;
+      const unsigned char* sb = wbase + (i % STG) * SG::kBytes;
       uint4 wq[NP][2], bv[NT][4];
       float sc[NP][NG][2], zz[NP][NG][2];
 #pragma unroll
@@ -424,7 +428,8 @@ __device__ __forceinline__ void mma_kblock(const GemmArgs& a, int ks, int bx, in
       for (int n = 0; n < NT; ++n)
 #pragma unroll
         for (int b = 0; b < 4; ++b)
-          bv[n][b] = *reinterpret_cast<const uint4*>(sb + SG::kW + SG::kS + SG::kZ + (n * 4 + b) * 512 + lane * 16);
+          bv[n][b] = *reinterpret_cast<const uint4*>(
+              sb + SG::kW + SG::kS + SG::kZ + (ONECOL ? b * 64 + t * 16 : (n * 4 + b) * 512 + lane * 16));
       __syncwarp();  // every lane holds its operands before any lane refills this stage
 
 #pragma unroll
@@ -480,6 +485,10 @@ __device__ __forceinline__ void mma_kblock(const GemmArgs& a, int ks, int bx, in
             for (int n = 0; n < NT; ++n)
 #pragma unroll
               for (int r = 0; r < 4; ++r) {
+                if (ONECOL && (r & 1)) {  // a column no item row reaches
+                  tmp[p][n][0][r] = tmp[p][n][1][r] = 0.f;
+                  continue;
+                }
                 const float pr = tmp[p][n][0][r] + tmp[p][n][1][r];
                 const float v = __fmaf_rn(-bias, xs[n][0][r], pr);  // sum x*(q - zp)
                 acc[p][n][r] = __fmaf_rn(v, sc[p][q][r >> 1], acc[p][n][r]);
@@ -513,7 +522,7 @@ __device__ __forceinline__ void mma_kblock(const GemmArgs& a, int ks, int bx, in
             for (int r = 0; r < 4; ++r) {
               float v = acc[p][n][r];
               for (int w = 1; w < ks; ++w) {
-                const float* o = reinterpret_cast<const float*>(wsm + (size_t)(warp + w) * kStagesW * SG::kBytes);
+                const float* o = reinterpret_cast<const float*>(wsm + (size_t)(warp + w) * STG * SG::kBytes);
                 v += o[((p * NT + n) * 4 + r) * 32 + lane];
               }
               acc[p][n][r] = v;
@@ -1304,6 +1313,12 @@ __device__ __forceinline__ void decode1_barrier(const Decode1Args& a, int b) {
 //   4. down: the same over the gate/up rows (gx_dn x kk blocks).
 //   5. combine: y = sum_j w_j * partial_j in slot order (k_combine's fmaf
 //      order), + the residual, to bf16.
+// Ring depths of the GEMM phases (stages of the one-row layout: gate/up
+// 2.5 KB, down 1.4 KB per warp).  Measured on the three BASELINE layers, step
+// time with gate/up / down stages 3/3, 4/6, 5/8: Qwen 22.6 / 22.9 / 24.2 us,
+// GLM 39.0 / 39.9 / 41.3, Kimi 81.9 / 85.9 / 87.4 -- bytes in flight are not
+// what bounds these phases, and deeper rings cost registers.
+constexpr int kDecode1StagesGu = 3, kDecode1StagesDn = 3;
 template <int GSB, bool AWQ>
 __global__ void __launch_bounds__(kWarps * 32) k_moe_decode1(Decode1Args a) {
   extern __shared__ __align__(128) unsigned char wsm[];
@@ -1406,7 +1421,8 @@ __global__ void __launch_bounds__(kWarps * 32) k_moe_decode1(Decode1Args a) {
     g.ldb = 0;  // every slot reads the token's row
     const int nvb = a.gx_gu * kk;
     for (int vb = blockIdx.x; vb < nvb; vb += gridDim.x)
-      mma_kblock<MODE_GATE_UP, 1, GSB, AWQ, false>(g, a.ks_gu, vb % a.gx_gu, vb / a.gx_gu, kk, wsm);
+      mma_kblock<MODE_GATE_UP, 1, GSB, AWQ, false, true, kDecode1StagesGu>(g, a.ks_gu, vb % a.gx_gu, vb / a.gx_gu,
+                                                                         kk, wsm);
   }
   decode1_barrier(a, 1);
 
@@ -1420,7 +1436,8 @@ __global__ void __launch_bounds__(kWarps * 32) k_moe_decode1(Decode1Args a) {
     d.kk = kk;
     const int nvb = a.gx_dn * kk;
     for (int vb = blockIdx.x; vb < nvb; vb += gridDim.x)
-      mma_kblock<MODE_PLAIN_F32, 1, GSB, AWQ, false>(d, a.ks_dn, vb % a.gx_dn, vb / a.gx_dn, kk, wsm);
+      mma_kblock<MODE_PLAIN_F32, 1, GSB, AWQ, false, true, kDecode1StagesDn>(d, a.ks_dn, vb % a.gx_dn, vb / a.gx_dn,
+                                                                           kk, wsm);
   }
   decode1_barrier(a, 2);
 
@@ -1446,8 +1463,8 @@ __global__ void __launch_bounds__(kWarps * 32) k_moe_decode1(Decode1Args a) {
 
 template <int GSB, bool AWQ>
 static size_t decode1_smem_k() {
-  return std::max((size_t)kWarps * kStagesW * WStage<2, 1, AWQ, false>::kBytes,
-                  (size_t)kWarps * kStagesW * WStage<1, 1, AWQ, false>::kBytes);
+  return std::max((size_t)kWarps * kDecode1StagesGu * WStage<2, 1, AWQ, false, true>::kBytes,
+                  (size_t)kWarps * kDecode1StagesDn * WStage<1, 1, AWQ, false, true>::kBytes);
 }
 
 // K split and virtual grid width of one GEMM phase: the split (1, 2 or 4 warps
