@@ -187,6 +187,29 @@ def test_single_token_forward_on_a_stale_workspace(oracle):
     dl.close()
 
 
+@pytest.mark.parametrize("gs", [32, 64, 128])
+@pytest.mark.parametrize("scheme", [orc.SCHEME_AWQ_SYM, orc.SCHEME_GPTQ_ASYM])
+def test_single_token_every_group_size_and_scheme(oracle, gs, scheme):
+    """Every instance of the fused one-token kernel (group 32 / 64 / 128 x AWQ /
+    GPTQ; the GPTQ layers with the sigmoid+bias router and a shared expert):
+    ids bit-exact, output within the tolerance of the oracle."""
+    gptq = scheme == orc.SCHEME_GPTQ_ASYM
+    rng = np.random.default_rng(40 + gs + scheme)
+    layer = orc.make_layer(oracle, rng, H=512, I=256, E=32, topk=8, gs=gs, scheme=scheme,
+                           router=orc.ROUTER_SIGMOID_BIAS if gptq else orc.ROUTER_SOFTMAX, shared=gptq)
+    dl = G.DevLayer(layer, 1)
+    for _ in range(2):
+        X = orc.make_tokens(rng, 1, layer.H)
+        Y, ws_bytes = dl.forward(X)
+        Yref, ids, _, _ = oracle.moe_layer_forward(layer, X)
+        v = dl.views(1, ws_bytes)
+        assert v["error_flag"] == 0
+        assert np.array_equal(v["ids"][:, :layer.topk], ids)
+        mre, cos = G.quality(G.bf16_to_f32(Y), Yref)
+        assert mre <= G.MAX_REL and cos >= G.MIN_COS, (gs, scheme, mre, cos)
+    dl.close()
+
+
 def test_single_token_barrier_budget_runs_out(oracle):
     """A barrier wait of the fused one-token kernel that runs out of its
     budget (cut to one SM clock, so a CTA that arrives before the others gives
