@@ -1526,11 +1526,11 @@ static cudaError_t launch_decode1_k(Decode1Args a, cudaStream_t st) {
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 2 : 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, k_moe_decode1<GSB, AWQ>, a);
-  if (e != cudaSuccess && pdl) {  // the two attributes refused together: cooperative alone
+  if (e != cudaSuccess && pdl) {  // refused with both attributes: cooperative alone
     (void)cudaGetLastError();
-    pdl = false;
     cfg.numAttrs = 1;
     e = cudaLaunchKernelEx(&cfg, k_moe_decode1<GSB, AWQ>, a);
+    if (e == cudaSuccess) pdl = false;  // it was the pair of attributes
   }
   return e;
 }

@@ -904,7 +904,14 @@ llmoc_status run_decode1(const llmoc_moe_layer* L, const uint16_t* X, const uint
   // stage timing: the whole launch is reported as the gate/up stage
   for (int i = 0; i < 4; ++i)
     if (se) se->mark(st);
-  if (!cuda_ok(launch_decode1(a, L->d.scheme == LLMOC_SCHEME_AWQ_SYM, st), "fused decode")) return LLMOC_ERR_CUDA;
+  const cudaError_t e = launch_decode1(a, L->d.scheme == LLMOC_SCHEME_AWQ_SYM, st);
+  if (e == cudaErrorCooperativeLaunchTooLarge || e == cudaErrorNotSupported) {
+    // the grid cannot be resident at once here (e.g. a client limited to part
+    // of the GPU): nothing was launched, the caller runs the separate kernels
+    (void)cudaGetLastError();
+    return LLMOC_ERR_UNSUPPORTED;
+  }
+  if (!cuda_ok(e, "fused decode")) return LLMOC_ERR_CUDA;
   count_launch(1);
   for (int i = 0; i < 3; ++i)
     if (se) se->mark(st);
@@ -1380,8 +1387,11 @@ llmoc_status moe_forward(const llmoc_moe_layer* L, const uint16_t* X, int T, con
   StageEvents se(L);
   if (T == 1 && decode1_ok(L)) {
     const llmoc_status rc = run_decode1(L, X, R, Y, w, ws, st, &se);
-    if (rc == LLMOC_OK) se.commit();
-    return rc;
+    if (rc != LLMOC_ERR_UNSUPPORTED) {
+      if (rc == LLMOC_OK) se.commit();
+      return rc;
+    }
+    se.next = 0;  // the one-launch form was refused: the chain of separate kernels below
   }
   llmoc_status rc = run_route(L, X, T, w, ws, st, &se);
   if (rc != LLMOC_OK) return rc;
