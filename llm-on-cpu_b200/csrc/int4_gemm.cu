@@ -1253,9 +1253,11 @@ __device__ __forceinline__ unsigned long long ld_acquire_gpu_u64(const unsigned 
 }
 
 // Grid-wide barrier b of k_moe_decode1 (b = 0, 1, 2): an arrival counter at
-// a.bar[0] (its low 32 bits), zeroed by CTA 0 at the kernel's start, which
-// then publishes the launch's tag in a.bar[1]; a CTA checks that tag once
-// before its first arrival (so no arrival lands before the reset), then
+// a.bar[0] (its low 32 bits), zero when a launch starts (zeroed by the last
+// CTA of the previous launch past its last barrier, or by CTA 0 when the tag
+// in a.bar[1] is not this launch's, before it publishes it); a CTA checks
+// that tag once before its first arrival (so no arrival lands before a
+// reset), then
 // every barrier is one release-add and a poll until the count reaches
 // (b + 1) * gridDim.x.  Each wait gives up after a.budget SM clocks: bit 2 of
 // *a.err is set and the kernel goes on (its outputs are then invalid), so a
@@ -1335,11 +1337,19 @@ __global__ void __launch_bounds__(kWarps * 32, 4) k_moe_decode1(Decode1Args a) {
   const int H = a.H, kk = a.ta.kk;
   grid_dep_wait();  // the token row is the predecessor's output
   grid_dep_release();
-  if (blockIdx.x == 0 && threadIdx.x == 0) {  // the barrier's counter, then the launch's tag
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
     *a.err = 0;
-    *reinterpret_cast<unsigned int*>(a.bar) = 0;
-    __threadfence();
-    st_release_gpu_u64(a.bar + 1, decode1_tag(a.epoch, 0));
+    // a launch with a new tag (another epoch, or words this kernel did not
+    // write) zeroes the barrier's counters, then publishes the tag; a replay
+    // of the same launch (a captured graph: same epoch) finds its tag there
+    // and the counters already zeroed by the previous replay's last CTA
+    const unsigned long long tag = decode1_tag(a.epoch, 0);
+    if (ld_acquire_gpu_u64(a.bar + 1) != tag) {
+      *reinterpret_cast<unsigned int*>(a.bar) = 0;
+      *reinterpret_cast<unsigned int*>(a.bar + 2) = 0;
+      __threadfence();
+      st_release_gpu_u64(a.bar + 1, tag);
+    }
   }
 
   // 1. router rows (and the sigmoid router's scores)
@@ -1443,6 +1453,13 @@ __global__ void __launch_bounds__(kWarps * 32, 4) k_moe_decode1(Decode1Args a) {
                                                                            kk, wsm);
   }
   decode1_barrier(a, 2);
+  if (threadIdx.x == 0) {  // the last CTA past the last barrier zeroes the counters for the next launch
+    unsigned int* done = reinterpret_cast<unsigned int*>(a.bar + 2);
+    if (atomicAdd(done, 1u) == gridDim.x - 1) {
+      *reinterpret_cast<unsigned int*>(a.bar) = 0;
+      *done = 0;
+    }
+  }
 
   // 5. combine (+ residual)
   for (int h = (blockIdx.x * blockDim.x + threadIdx.x) * 4; h < H; h += gridDim.x * blockDim.x * 4) {

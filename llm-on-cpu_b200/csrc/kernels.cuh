@@ -293,7 +293,8 @@ struct Decode1Args {
   int* inverse;
   int* n_active;
   int* err;                // bit 2: a barrier wait gave up
-  unsigned long long* bar;  // [2]: the barrier's arrival counter (low 32 bits of [0]), the launch's tag
+  unsigned long long* bar;  // [3]: the barrier's arrival counter and the count of CTAs past the last barrier
+                           // (low 32 bits of [0] and [2]), the launch's tag [1]
   unsigned long long epoch;  // distinct per launch: barrier tags never match an older launch's words
   long long budget;        // SM clocks per barrier wait
 };

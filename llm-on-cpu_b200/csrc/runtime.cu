@@ -423,7 +423,7 @@ WsLayout ws_layout_g(const llmoc_moe_layer* L, int T, int kk, int n_perm, int ch
     w.xscale = take((size_t)T * 4);
   }
   // the fused single-token kernel's barrier words (a whole-layer forward of one token)
-  w.bar = logits && T == 1 ? take(16) : 0;
+  w.bar = logits && T == 1 ? take(24) : 0;
   w.sig = logits && T == 1 ? take((size_t)(L->d.n_experts + L->shared_gate) * 4) : 0;  // sigmoid scores
   w.total = o;
   return w;

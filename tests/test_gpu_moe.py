@@ -210,6 +210,33 @@ def test_single_token_every_group_size_and_scheme(oracle, gs, scheme):
     dl.close()
 
 
+def test_single_token_forward_replayed_from_a_cuda_graph(oracle):
+    """The fused one-token forward captured into a CUDA graph and replayed (the
+    launch's parameters, its epoch included, frozen): every replay correct and
+    clean -- each launch's last CTA leaves the barrier's counters at zero, so a
+    replay that finds its own tag in the workspace needs no reset."""
+    dl, rng = build(oracle, "qwen_like", 13, 1)
+    X = orc.make_tokens(rng, 1, dl.host.H)
+    Xd = G.bf16_dev(X)
+    Y = torch.empty((1, dl.host.H), dtype=torch.bfloat16, device="cuda")
+    ws_bytes = dl.dev.workspace_bytes(1)
+    dl.dev.forward(Xd, 1, Y, dl.ws, ws_bytes, torch.cuda.current_stream())  # first use outside the capture
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        dl.dev.forward(Xd, 1, Y, dl.ws, ws_bytes, torch.cuda.current_stream())
+    Yref, _, _, _ = oracle.moe_layer_forward(dl.host, X)
+    for _ in range(4):
+        Y.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        assert dl.views(1, ws_bytes)["error_flag"] == 0
+        mre, cos = G.quality(G.bf16_to_f32(Y), Yref)
+        assert mre <= G.MAX_REL and cos >= G.MIN_COS, (mre, cos)
+    del g
+    dl.close()
+
+
 def test_single_token_barrier_budget_runs_out(oracle):
     """A barrier wait of the fused one-token kernel that runs out of its
     budget (cut to one SM clock, so a CTA that arrives before the others gives
