@@ -18,6 +18,10 @@
 // is kept: the tensor core multiplies exact bf16 integers (q - zp) by bf16
 // activations, and the fp32 group partials are scaled on the accumulator.
 #include <algorithm>
+#include <atomic>
+#include <map>
+#include <mutex>
+#include <utility>
 
 #include "kernels.cuh"
 #include "route_dev.cuh"
@@ -1508,25 +1512,39 @@ static void decode1_split(int M, int K, int kk, int grid, int* ks, int* gx) {
 
 template <int GSB, bool AWQ>
 static cudaError_t launch_decode1_k(Decode1Args a, cudaStream_t st) {
-  // grid: every CTA resident at once (a cooperative launch), at most the
-  // barrier flags reserved in the workspace
-  static size_t smem = 0;
-  static int grid = 0;
-  static bool pdl = true;  // programmatic launch together with the cooperative attribute
+  // grid: every CTA resident at once (a cooperative launch).  The function's
+  // dynamic shared memory limit only grows and the grid is kept per (device,
+  // bytes), both under a lock and read into locals, so launches of layers
+  // with different needs from several host threads never pair one layer's
+  // grid or limit with another's bytes.
+  static std::mutex mu;
+  static std::map<int, size_t> limit;               // device -> attribute set so far
+  static std::map<std::pair<int, size_t>, int> grids;  // (device, bytes) -> resident grid
+  static std::atomic<bool> pdl{true};  // programmatic launch together with the cooperative attribute
   a.ex_off = (int)((std::max(decode1_smem_k<GSB, AWQ>(), (size_t)a.H * 4) + 15) / 16 * 16);
-  const size_t need = (size_t)a.ex_off + (size_t)a.ta.kk * sizeof(ExpertDev);
-  if (need > 227 * 1024) return cudaErrorInvalidValue;
-  if (need != smem) {
-    cudaError_t e = cudaFuncSetAttribute(k_moe_decode1<GSB, AWQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)need);
-    if (e != cudaSuccess) return e;
-    int per_sm = 0, dev = 0, sms = 0;
-    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
-    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_moe_decode1<GSB, AWQ>, kWarps * 32, need);
-    if (e != cudaSuccess) return e;
-    if (per_sm < 1) return cudaErrorInvalidConfiguration;
-    grid = std::min(per_sm * sms, kDecode1MaxCtas);
-    smem = need;
+  const size_t smem = (size_t)a.ex_off + (size_t)a.ta.kk * sizeof(ExpertDev);
+  if (smem > 227 * 1024) return cudaErrorInvalidValue;
+  int dev = 0, grid = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    size_t& lim = limit[dev];
+    if (smem > lim) {
+      e = cudaFuncSetAttribute(k_moe_decode1<GSB, AWQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return e;
+      lim = smem;
+    }
+    int& g = grids[{dev, smem}];
+    if (!g) {
+      int per_sm = 0, sms = 0;
+      if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_moe_decode1<GSB, AWQ>, kWarps * 32, smem);
+      if (e != cudaSuccess) return e;
+      if (per_sm < 1) return cudaErrorInvalidConfiguration;
+      g = std::min(per_sm * sms, kDecode1MaxCtas);
+    }
+    grid = g;
   }
   decode1_split(a.gu.M, a.gu.K, a.ta.kk, grid, &a.ks_gu, &a.gx_gu);
   decode1_split(a.dn.M, a.dn.K, a.ta.kk, grid, &a.ks_dn, &a.gx_dn);
@@ -1541,13 +1559,14 @@ static cudaError_t launch_decode1_k(Decode1Args a, cudaStream_t st) {
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 2 : 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, k_moe_decode1<GSB, AWQ>, a);
-  if (e != cudaSuccess && pdl) {  // refused with both attributes: cooperative alone
+  const bool with_pdl = pdl.load(std::memory_order_relaxed);
+  cfg.numAttrs = with_pdl ? 2 : 1;
+  e = cudaLaunchKernelEx(&cfg, k_moe_decode1<GSB, AWQ>, a);
+  if (e != cudaSuccess && with_pdl) {  // refused with both attributes: cooperative alone
     (void)cudaGetLastError();
     cfg.numAttrs = 1;
     e = cudaLaunchKernelEx(&cfg, k_moe_decode1<GSB, AWQ>, a);
-    if (e == cudaSuccess) pdl = false;  // it was the pair of attributes
+    if (e == cudaSuccess) pdl.store(false, std::memory_order_relaxed);  // it was the pair of attributes
   }
   return e;
 }
